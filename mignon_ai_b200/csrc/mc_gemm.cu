@@ -1,0 +1,365 @@
+// Isolated INT8 GEMMs on the 5th-generation tensor core (tcgen05 kind::i8).
+//
+// Two entry points share one structure (a 128-row M tile per CTA, K streamed through a ring of
+// shared-memory stages, accumulators in TMEM, an epilogue by four row-owning warps):
+//
+//  * gemm_i8_kernel: int8 activations A[M x K] and weights W[N x K], both loaded by TMA. The s32
+//    accumulators are exact; the epilogue writes them and/or y = acc * row_scale * col_scale + bias.
+//    This is the config-5 sweep (per-channel weight scales, per-row activation scales).
+//
+//  * gemm_f32a_kernel: float32 activations, the reference's INT8 product (MatVecInt8,
+//    internal/kernels/int8.go:31-41: y = (x . w) * scale + bias with x in float32). Each
+//    activation row is sliced into three int8 digit planes (mc_sm100.cuh: slice3) by the
+//    row-owning warps while the weights stream in by TMA; three MMAs per K step accumulate the
+//    planes into three exact s32 accumulators that the epilogue recombines.
+#include "mc_host.h"
+#include "mc_sm100.cuh"
+
+namespace mc {
+namespace gemm {
+
+constexpr int kBM = 128;   // rows per CTA (TMEM lanes)
+constexpr int kBK = 128;   // K bytes per stage (one 128-byte swizzle row)
+
+// ------------------------------------------------------------------------------------------------
+// int8 x int8
+// ------------------------------------------------------------------------------------------------
+constexpr int kI8BN = 256;
+constexpr int kI8Stages = 4;
+constexpr int kI8StageA = kBM * kBK;     // 16 KB
+constexpr int kI8StageB = kI8BN * kBK;   // 32 KB
+constexpr int kI8Smem = kI8Stages * (kI8StageA + kI8StageB) + 1024 + 256;
+
+struct I8Args {
+  int M, N, K;
+  const float* row_scale;  // [M] or null (1)
+  const float* col_scale;  // [N] or null (1)
+  const float* bias;       // [N] or null
+  int32_t* c_i32;          // [M x N] or null
+  float* y;                // [M x N] or null
+};
+
+__global__ void __launch_bounds__(192, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w, I8Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + kI8Stages * kI8StageA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + kI8Stages * kI8StageB);
+  uint64_t* empty = full + kI8Stages;
+  uint64_t* accfull = empty + kI8Stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accfull + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kI8BN;
+  const int ktiles = (args.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kI8Stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accfull, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // TMA producer.
+    prefetch_tensormap(&map_a);
+    prefetch_tensormap(&map_w);
+    for (int kt = 0; kt < ktiles; ++kt) {
+      const int s = kt % kI8Stages;
+      if (kt >= kI8Stages && !mbar_wait_or_abort(&empty[s], ((kt / kI8Stages) - 1) & 1, kErrWaitEmpty)) break;
+      mbar_arrive_expect_tx(&full[s], kI8StageA + kI8StageB);
+      tma_load_2d(sa + s * kI8StageA, &map_a, kt * kBK, m0, &full[s]);
+      tma_load_2d(sb + s * kI8StageB, &map_w, kt * kBK, n0, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer.
+    const uint32_t idesc = idesc_i8(kBM, kI8BN);
+    bool ok = true;
+    for (int kt = 0; kt < ktiles && ok; ++kt) {
+      const int s = kt % kI8Stages;
+      if (!mbar_wait_or_abort(&full[s], (kt / kI8Stages) & 1, kErrWaitFull)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint64_t da = smem_desc_sw128(sa + s * kI8StageA);
+      const uint64_t db = smem_desc_sw128(sb + s * kI8StageB);
+      const int ksteps = min(4, (args.K - kt * kBK + 31) / 32);
+      for (int kk = 0; kk < ksteps; ++kk)
+        mma_i8(tmem, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+      mma_commit(&empty[s]);
+    }
+    if (ok) mma_commit(accfull);
+  } else if (warp >= 2) {
+    // Epilogue: warp w reads TMEM lanes 32*(w%4)..+31, i.e. rows m0 + 32*(w%4) + lane.
+    const int quad = warp % 4;
+    const int row = m0 + quad * 32 + lane;
+    // TMEM loads are warp-collective: the whole warp takes the same branch.
+    if (__all_sync(0xffffffffu, mbar_wait_or_abort(accfull, 0, kErrWaitAcc))) {
+      tc_fence_after();
+      const float rs = (args.row_scale && row < args.M) ? args.row_scale[row] : 1.0f;
+      for (int c = 0; c < kI8BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem_addr(tmem, quad * 32, c), r);
+        tmem_wait_ld();
+        if (row >= args.M) continue;
+        const int n = n0 + c;
+        if (args.c_i32) {
+          int4* dst = reinterpret_cast<int4*>(args.c_i32 + (size_t)row * args.N + n);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            dst[j] = make_int4((int)r[4 * j], (int)r[4 * j + 1], (int)r[4 * j + 2], (int)r[4 * j + 3]);
+        }
+        if (args.y) {
+          float4* dst = reinterpret_cast<float4*>(args.y + (size_t)row * args.N + n);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int col = n + 4 * j + e;
+              float cs = args.col_scale ? args.col_scale[col] : 1.0f;
+              // Separately rounded multiplies and add (never contracted into an FMA).
+              float t = __fmul_rn((float)(int)r[4 * j + e], rs);
+              t = __fmul_rn(t, cs);
+              if (args.bias) t = __fadd_rn(t, args.bias[col]);
+              v[e] = t;
+            }
+            dst[j] = make_float4(v[0], v[1], v[2], v[3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
+// ------------------------------------------------------------------------------------------------
+// float32 activations (three digit planes) x int8 weights
+// ------------------------------------------------------------------------------------------------
+constexpr int kFBN = 128;
+constexpr int kFStages = 3;
+constexpr int kFTile = kBM * kBK;              // one 128 x 128 int8 tile
+constexpr int kFStage = 3 * kFTile + kFTile;   // three digit planes + the weight tile
+constexpr int kFSmem = kFStages * kFStage + 1024 + 256;
+
+struct F32Args {
+  int M, N, K;
+  const float* a;          // [M x K] float32
+  const float* row_max;    // [M] max |a_row|
+  float w_scale;           // per-tensor weight scale (MatVecInt8's scale)
+  const float* bias;       // [N] or null
+  float* y;                // [M x N]
+  int32_t* slices;         // [3 x M x N] or null: the exact per-plane accumulators
+};
+
+__global__ void row_absmax_kernel(const float* a, int M, int K, float* out) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= M) return;
+  float m = 0.f;
+  for (int k = lane; k < K; k += 32) m = fmaxf(m, fabsf(a[(size_t)row * K + k]));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) out[row] = m;
+}
+
+__global__ void __launch_bounds__(160, 1)
+    gemm_f32a_kernel(const __grid_constant__ CUtensorMap map_w, F32Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kFStages * kFStage);
+  uint64_t* empty = full + kFStages;
+  uint64_t* accfull = empty + kFStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accfull + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kFBN;
+  const int ktiles = (args.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kFStages; ++s) {
+      mbar_init(&full[s], 128 + 1);  // 128 slicing threads + the weight-tile expect_tx arrival
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accfull, 1);
+    fence_barrier_init();
+  }
+  if (warp == 4) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 4) {
+    // Producers: thread t slices row m0 + t of each K tile into the three digit planes.
+    const int t = threadIdx.x;
+    const int row = m0 + t;
+    const bool valid = row < args.M;
+    const float inv = valid ? row_inv_step(args.row_max[row]) : 0.f;
+    const float* arow = args.a + (size_t)(valid ? row : 0) * args.K;
+    bool ok = true;
+    for (int kt = 0; kt < ktiles; ++kt) {
+      const int s = kt % kFStages;
+      if (kt >= kFStages && !mbar_wait_or_abort(&empty[s], ((kt / kFStages) - 1) & 1, kErrWaitEmpty)) {
+        ok = false;
+        break;
+      }
+      uint8_t* st = smem + s * kFStage;
+      if (t == 0) {
+        mbar_arrive_expect_tx(&full[s], kFTile);
+        tma_load_2d(st + 3 * kFTile, &map_w, kt * kBK, n0, &full[s]);
+      }
+      const int k0 = kt * kBK;
+#pragma unroll 2
+      for (int c = 0; c < 8; ++c) {
+        uint32_t p1[4], p2[4], p3[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float x[4];
+          const int k = k0 + c * 16 + q * 4;
+          if (valid && k + 3 < args.K) {
+            float4 v = *reinterpret_cast<const float4*>(arow + k);
+            x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) x[e] = (valid && k + e < args.K) ? arow[k + e] : 0.f;
+          }
+          Digits3 d[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) d[e] = slice3(x[e], inv);
+          p1[q] = pack4(d[0].d1, d[1].d1, d[2].d1, d[3].d1);
+          p2[q] = pack4(d[0].d2, d[1].d2, d[2].d2, d[3].d2);
+          p3[q] = pack4(d[0].d3, d[1].d3, d[2].d3, d[3].d3);
+        }
+        const uint32_t off = sw128_offset(t, c);
+        *reinterpret_cast<uint4*>(st + off) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+        *reinterpret_cast<uint4*>(st + kFTile + off) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
+        *reinterpret_cast<uint4*>(st + 2 * kFTile + off) = make_uint4(p3[0], p3[1], p3[2], p3[3]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&full[s]);
+    }
+    // Epilogue (warp-uniform branch: TMEM loads are warp-collective).
+    if (__all_sync(0xffffffffu, ok && mbar_wait_or_abort(accfull, 0, kErrWaitAcc))) {
+      tc_fence_after();
+      const int quad = warp;  // warps 0..3 own TMEM lanes 32*warp..
+      const float step = valid ? row_step(args.row_max[row]) : 0.f;
+      for (int c = 0; c < kFBN; c += 32) {
+        uint32_t r1[32], r2[32], r3[32];
+        tmem_ld32(tmem_addr(tmem, quad * 32, c), r1);
+        tmem_ld32(tmem_addr(tmem, quad * 32, kFBN + c), r2);
+        tmem_ld32(tmem_addr(tmem, quad * 32, 2 * kFBN + c), r3);
+        tmem_wait_ld();
+        if (!valid) continue;
+        const int n = n0 + c;
+        float* yrow = args.y + (size_t)row * args.N + n;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float v[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const double acc = combine3((int)r1[j + e], (int)r2[j + e], (int)r3[j + e]);
+            const float dot = (float)(acc * (double)step);
+            // MatVecInt8: y = dot * scale, then y += bias, each rounded (int8.go:37-40).
+            float t2 = __fmul_rn(dot, args.w_scale);
+            if (args.bias) t2 = __fadd_rn(t2, args.bias[n + j + e]);
+            v[e] = t2;
+          }
+          *reinterpret_cast<float4*>(yrow + j) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+        if (args.slices) {
+          const size_t plane = (size_t)args.M * args.N;
+          int32_t* o = args.slices + (size_t)row * args.N + n;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            o[j] = (int)r1[j];
+            o[plane + j] = (int)r2[j];
+            o[2 * plane + j] = (int)r3[j];
+          }
+        }
+      }
+    }
+  } else if (warp == 4 && lane == 0) {
+    const uint32_t idesc = idesc_i8(kBM, kFBN);
+    bool ok = true;
+    for (int kt = 0; kt < ktiles && ok; ++kt) {
+      const int s = kt % kFStages;
+      if (!mbar_wait_or_abort(&full[s], (kt / kFStages) & 1, kErrWaitFull)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint8_t* st = smem + s * kFStage;
+      const uint64_t db = smem_desc_sw128(st + 3 * kFTile);
+      const int ksteps = min(4, (args.K - kt * kBK + 31) / 32);
+#pragma unroll
+      for (int p = 0; p < 3; ++p) {
+        const uint64_t da = smem_desc_sw128(st + p * kFTile);
+        for (int kk = 0; kk < ksteps; ++kk)
+          mma_i8(tmem + p * kFBN, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+      }
+      mma_commit(&empty[s]);
+    }
+    if (ok) mma_commit(accfull);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace gemm
+
+// ------------------------------------------------------------------------------------------------
+// Host launchers
+// ------------------------------------------------------------------------------------------------
+int gemm_i8_launch(const int8_t* a, const int8_t* w, int M, int N, int K, const float* row_scale,
+                   const float* col_scale, const float* bias, int32_t* c_i32, float* y, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || N % gemm::kI8BN != 0 || K % 16 != 0)
+    return set_error(kInvalidArgument, "gemm_i8: need M,N,K > 0, N % 256 == 0 and K % 16 == 0");
+  if (!c_i32 && !y) return set_error(kInvalidArgument, "gemm_i8: no output");
+  CUtensorMap ma, mw;
+  if (!make_tmap_i8(&ma, a, M, K, K, gemm::kBK, gemm::kBM)) return kCudaError;
+  if (!make_tmap_i8(&mw, w, N, K, K, gemm::kBK, gemm::kI8BN)) return kCudaError;
+  static bool attr = false;
+  if (!attr) {
+    MC_CUDA(cudaFuncSetAttribute(gemm::gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kI8Smem));
+    attr = true;
+  }
+  gemm::I8Args args{M, N, K, row_scale, col_scale, bias, c_i32, y};
+  dim3 grid(N / gemm::kI8BN, (M + gemm::kBM - 1) / gemm::kBM);
+  gemm::gemm_i8_kernel<<<grid, 192, gemm::kI8Smem, stream>>>(ma, mw, args);
+  MC_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+int gemm_f32a_launch(const float* a, const int8_t* w, int M, int N, int K, float w_scale, const float* bias,
+                     float* y, int32_t* slices, float* row_max_scratch, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || N % gemm::kFBN != 0 || K % 16 != 0)
+    return set_error(kInvalidArgument, "gemm_f32a: need M,N,K > 0, N % 128 == 0 and K % 16 == 0");
+  CUtensorMap mw;
+  if (!make_tmap_i8(&mw, w, N, K, K, gemm::kBK, gemm::kFBN)) return kCudaError;
+  static bool attr = false;
+  if (!attr) {
+    MC_CUDA(cudaFuncSetAttribute(gemm::gemm_f32a_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kFSmem));
+    attr = true;
+  }
+  gemm::row_absmax_kernel<<<(M + 7) / 8, 256, 0, stream>>>(a, M, K, row_max_scratch);
+  gemm::F32Args args{M, N, K, a, row_max_scratch, w_scale, bias, y, slices};
+  dim3 grid(N / gemm::kFBN, (M + gemm::kBM - 1) / gemm::kBM);
+  gemm::gemm_f32a_kernel<<<grid, 160, gemm::kFSmem, stream>>>(mw, args);
+  MC_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+}  // namespace mc

@@ -1,0 +1,44 @@
+// Host-side helpers of libmignoncuda: status/error reporting across the C-ABI and TMA tensor maps.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+namespace mc {
+
+// Sets the thread-local message returned by mc_last_error() and returns status.
+int set_error(int status, const std::string& msg);
+void clear_error();
+
+// Status codes of the C-ABI (mirrored in include/mignon_cuda.h).
+enum Status : int {
+  kOk = 0,
+  kInvalidArgument = 1,
+  kCudaError = 2,
+  kBadModel = 3,
+  kOutOfMemory = 4,
+  kDeviceTimeout = 5,
+  kUnsupported = 6,
+};
+
+// Checks a CUDA runtime call; on failure records the message and returns kCudaError.
+#define MC_CUDA(call)                                                                         \
+  do {                                                                                        \
+    cudaError_t e_ = (call);                                                                  \
+    if (e_ != cudaSuccess)                                                                    \
+      return ::mc::set_error(::mc::kCudaError, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+// Encodes a 2-D tiled tensor map over a row-major int8 matrix [rows x cols] (cols contiguous,
+// row pitch `pitch` bytes) with box {box_cols, box_rows} and the 128-byte swizzle. Returns false
+// (with the error recorded) if the driver rejects it.
+bool make_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch,
+                  uint32_t box_cols, uint32_t box_rows);
+
+// Reads and clears the device error word of the current device; non-zero codes become
+// kDeviceTimeout with a message.
+int check_device_error(cudaStream_t stream);
+
+}  // namespace mc
