@@ -59,6 +59,62 @@ int mc_gemm_f32a_dev(const float* x, const int8_t* w, int m, int n, int k, float
 int mc_gemm_i8(int device, const int8_t* a, const int8_t* w, int m, int n, int k, const float* row_scale,
                const float* col_scale, const float* bias, int32_t* c_i32, float* y);
 
+/* ---------------------------------------------------------------------------------------------
+ * Engine: models, session batches, prefill / append / generate.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct mc_ctx mc_ctx;
+typedef struct mc_model mc_model;
+typedef struct mc_batch mc_batch;
+
+typedef struct {
+  int n_devices;       /* 0: device 0 only */
+  const int* devices;  /* CUDA device ordinals; a batch's sessions are split evenly across them */
+} mc_options;
+
+/* Opens a context over one or more GPUs of this process. */
+int mc_open(const mc_options* opt, mc_ctx** out);
+int mc_close(mc_ctx* ctx);
+
+/* Parses an INT8 model file (binary mignon.model/1 or legacy JSON) and uploads a replica of the
+ * weights to every device of the context. Replaces quant.Decode (internal/quant/checkpoint.go:162)
+ * followed by quant.NewModel (model.go:91). Damaged files fail with MC_BAD_MODEL. */
+int mc_load_model(mc_ctx* ctx, const uint8_t* data, size_t n, mc_model** out);
+int mc_model_free(mc_model* model);
+
+/* out[10] = vocab, state, hidden, blocks, max_context, attn_heads, attn_window, total rule steps,
+ * norm ring length (longest dilation + 1), attention cache length. (quant.Model accessors,
+ * model.go:71-89, and the cache sizes of stream.go:39-47, attention.go:46-52.) */
+int mc_model_info(const mc_model* model, int32_t* out);
+
+/* Opens `count` sessions of one model: count x quant.(*Model).NewSession(context_size)
+ * (internal/quant/session.go:20-28; window = min(context_size, max_context), context_size <= 0
+ * meaning max_context). max_prompt bounds the prompts of later prefill/generate calls (<= 128);
+ * top_k (0..64) sizes the sampler. The sessions' state lives in device memory. */
+int mc_batch_open(mc_model* model, int count, int context_size, int max_prompt, int top_k, mc_batch** out);
+int mc_batch_close(mc_batch* batch);
+
+/* Session.Prefill for every session (session.go:30-39): session s restarts from
+ * tokens[s*stride .. s*stride+lens[s]) trimmed to its last `window` tokens. Writes, per session,
+ * the logits after the last token (if logits != NULL, [count x vocab] float32 — the reference
+ * returns them widened to float64), the greedy next token and its probability (argmaxProb,
+ * internal/generate/greedy.go:90-102). Sessions with lens[s] == 0 are left idle (nil logits). */
+int mc_prefill(mc_batch* batch, const int32_t* tokens, const int32_t* lens, int stride, float* logits, int32_t* next,
+               float* prob);
+
+/* Session.Append for every session (session.go:41-56, the streaming path appendPosition +
+ * headLogits): appends tokens[s] to session s and writes the logits after it, the greedy next
+ * token and its probability. */
+int mc_append(mc_batch* batch, const int32_t* tokens, float* logits, int32_t* next, float* prob);
+
+/* The decode loop of generate.greedyLoop (internal/generate/greedy.go:63-87) without stop tokens,
+ * or with temperature > 0 the sampled loop of sampleContinuation (generate/sample.go:196-247)
+ * with top-k = the batch's top_k, no repetition penalty, top-p 1: prefill each prompt, then
+ * n_new tokens per session, all steps on the device (one CUDA graph per step). Sampling draws
+ * its uniform from Philox4x32-10 keyed by (session0 + s, "SAMP") with counter = step.
+ * Writes out_tokens [count x n_new] and, if non-null, out_probs [count x n_new] (greedy only). */
+int mc_generate(mc_batch* batch, const int32_t* prompts, const int32_t* lens, int stride, int n_new, double temperature,
+                uint32_t session0, int32_t* out_tokens, float* out_probs);
+
 #ifdef __cplusplus
 }
 #endif

@@ -45,6 +45,16 @@ def _declare(L):
 EXTRA_SIGNATURES: dict = {}
 
 
+def register(signatures: dict):
+    """Adds C-ABI signatures; applies them at once if the library is already loaded."""
+    EXTRA_SIGNATURES.update(signatures)
+    if _lib is not None:
+        for name, argtypes in signatures.items():
+            f = getattr(_lib, name)
+            f.restype = ctypes.c_int
+            f.argtypes = argtypes
+
+
 def lib(build_if_missing: bool = True):
     """The loaded library; builds it first when the sources are newer (needs nvcc)."""
     global _lib

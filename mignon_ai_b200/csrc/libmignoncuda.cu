@@ -1,5 +1,10 @@
 // Single translation unit of libmignoncuda.so: every kernel and the C-ABI are compiled together so
-// device globals (the error word) need no separate device linking.
+// device globals (the error word) and shared device helpers need no separate device linking.
 #include "mc_host.cu"
 #include "mc_gemm.cu"
+#include "mc_modelfile.cu"
+#include "mc_block.cu"
+#include "mc_attn.cu"
+#include "mc_head.cu"
+#include "mc_engine_host.cu"
 #include "mc_api.cu"

@@ -1,8 +1,11 @@
 // C-ABI entry points of libmignoncuda (include/mignon_cuda.h).
+#include <algorithm>
 #include <cstring>
+#include <memory>
 #include <vector>
 
 #include "../../include/mignon_cuda.h"
+#include "mc_engine.cuh"
 #include "mc_host.h"
 
 namespace mc {
@@ -22,12 +25,324 @@ struct DevBuf {
 }  // namespace mc
 
 using namespace mc;
+using namespace mc::eng;
+
+struct mc_ctx {
+  std::vector<int> devices;
+};
+
+struct mc_model {
+  mc_ctx* ctx = nullptr;
+  HostModel host;
+  std::vector<std::unique_ptr<DevModel>> dev;  // one replica per device
+};
+
+struct mc_batch {
+  mc_model* model = nullptr;
+  int count = 0, window = 0, pmax = 0, topk = 0;
+  std::vector<int> first;                       // first session of each device shard
+  std::vector<std::unique_ptr<DevBatch>> shard;  // one per device
+};
+
+namespace {
+
+int shard_sizes(int count, int ndev, std::vector<int>& first) {
+  first.resize(ndev + 1);
+  for (int g = 0; g <= ndev; ++g) first[g] = (int)((long long)count * g / ndev);
+  return kOk;
+}
+
+int sync_all(mc_batch* b) {
+  int st = kOk;
+  for (auto& sh : b->shard) {
+    if (!sh || sh->S == 0) continue;
+    cudaSetDevice(sh->m->device);
+    int e = check_device_error(sh->stream);
+    if (e != kOk && st == kOk) st = e;
+  }
+  return st;
+}
+
+// Copies per-session host outputs back after a step that wrote column 0 of out_tok/out_prob.
+int copy_step_outputs(mc_batch* b, float* logits, int32_t* next, float* prob) {
+  for (size_t g = 0; g < b->shard.size(); ++g) {
+    DevBatch& sh = *b->shard[g];
+    if (sh.S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh.m->device));
+    const int s0 = b->first[g];
+    // column 0 of the [S x out_stride] output arrays
+    const size_t pitch = (size_t)sh.out_stride * 4;
+    if (next) MC_CUDA(cudaMemcpy2DAsync(next + s0, 4, sh.out_tok, pitch, 4, sh.S, cudaMemcpyDeviceToHost, sh.stream));
+    if (prob) MC_CUDA(cudaMemcpy2DAsync(prob + s0, 4, sh.out_prob, pitch, 4, sh.S, cudaMemcpyDeviceToHost, sh.stream));
+    if (logits)
+      MC_CUDA(cudaMemcpyAsync(logits + (size_t)s0 * sh.m->V, sh.logits, (size_t)sh.S * sh.m->V * 4, cudaMemcpyDeviceToHost,
+                              sh.stream));
+  }
+  return sync_all(b);
+}
+
+int ensure_step_outputs(DevBatch& sh, bool logits, int stride) {
+  int st;
+  if (sh.out_stride < stride) {
+    if ((st = sh.alloc(sh.out_tok, (size_t)sh.S * stride * 4)) || (st = sh.alloc(sh.out_prob, (size_t)sh.S * stride * 4)))
+      return st;
+    sh.out_stride = stride;
+  }
+  if (logits && !sh.logits && (st = sh.alloc(sh.logits, (size_t)sh.S * sh.m->V * 4))) return st;
+  return kOk;
+}
+
+// Uploads a prompt segment [count x stride] trimmed to each session's window into the shards'
+// token buffers; sets pos = 0 and seglen = trimmed length. Returns the longest trimmed length.
+int upload_prompts(mc_batch* b, const int32_t* tokens, const int32_t* lens, int stride, int* pmax_out) {
+  int pmax = 0;
+  for (int s = 0; s < b->count; ++s) {
+    if (lens[s] < 0 || lens[s] > stride) return set_error(kInvalidArgument, "prompt length outside [0, stride]");
+    pmax = std::max(pmax, std::min(lens[s], b->window));
+  }
+  if (pmax > b->pmax) return set_error(kInvalidArgument, "prompt longer than the batch's max_prompt");
+  *pmax_out = std::max(pmax, 1);
+  const int P = *pmax_out;
+  for (size_t g = 0; g < b->shard.size(); ++g) {
+    DevBatch& sh = *b->shard[g];
+    if (sh.S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh.m->device));
+    const int s0 = b->first[g];
+    std::vector<int32_t> tok((size_t)sh.S * P, 0), len(sh.S), rowmap(sh.S), zero(sh.S, 0);
+    const int spt = std::max(1, 128 / P);
+    for (int i = 0; i < sh.S; ++i) {
+      const int s = s0 + i;
+      const int n = std::max(0, std::min(lens[s], b->window));
+      const int32_t* src = tokens + (size_t)s * stride + (lens[s] - n);
+      std::copy(src, src + n, tok.begin() + (size_t)i * P);
+      len[i] = n;
+      rowmap[i] = (i / spt) * 128 + (i % spt) * P + std::max(n - 1, 0);
+    }
+    MC_CUDA(cudaMemcpyAsync(sh.tok, tok.data(), tok.size() * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.seglen, len.data(), sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.pos, zero.data(), sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.rowmap, rowmap.data(), sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    // The host vectors go out of scope: make the copies complete first.
+    MC_CUDA(cudaStreamSynchronize(sh.stream));
+  }
+  return kOk;
+}
+
+int run_graph_step(DevBatch& sh, int mode, double inv_temp, uint32_t session0, bool logits) {
+  DevBatch::GraphKey key;
+  key.mode = mode;
+  key.logits = (int)logits;
+  key.stride = sh.out_stride;
+  key.inv_t = inv_temp;
+  key.session0 = session0;
+  key.out_tok = sh.out_tok;
+  key.logits_buf = sh.logits;
+  if (!sh.graph || !(sh.graph_key == key)) {
+    if (sh.graph) {
+      cudaGraphExecDestroy(sh.graph);
+      sh.graph = nullptr;
+    }
+    cudaGraph_t gph;
+    MC_CUDA(cudaStreamBeginCapture(sh.stream, cudaStreamCaptureModeThreadLocal));
+    int st = enqueue_forward(sh, 1, mode, inv_temp, session0, logits, false);
+    cudaError_t e = cudaStreamEndCapture(sh.stream, &gph);
+    if (st != kOk) {
+      if (e == cudaSuccess) cudaGraphDestroy(gph);
+      return st;
+    }
+    if (e != cudaSuccess) return set_error(kCudaError, std::string("stream capture: ") + cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&sh.graph, gph, 0);
+    cudaGraphDestroy(gph);
+    if (e != cudaSuccess) return set_error(kCudaError, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    sh.graph_key = key;
+  }
+  MC_CUDA(cudaGraphLaunch(sh.graph, sh.stream));
+  return kOk;
+}
+
+}  // namespace
 
 extern "C" {
 
 const char* mc_last_error(void) { return last_error_cstr(); }
 
 int mc_version(void) { return 100; }
+
+int mc_open(const mc_options* opt, mc_ctx** out) {
+  clear_error();
+  if (!out) return set_error(kInvalidArgument, "mc_open: null output");
+  auto c = std::make_unique<mc_ctx>();
+  int ndev = 0;
+  MC_CUDA(cudaGetDeviceCount(&ndev));
+  if (opt && opt->n_devices > 0) {
+    if (!opt->devices) return set_error(kInvalidArgument, "mc_open: n_devices without a device list");
+    for (int i = 0; i < opt->n_devices; ++i) {
+      if (opt->devices[i] < 0 || opt->devices[i] >= ndev) return set_error(kInvalidArgument, "mc_open: no such device");
+      c->devices.push_back(opt->devices[i]);
+    }
+  } else {
+    if (ndev < 1) return set_error(kCudaError, "mc_open: no CUDA device");
+    c->devices.push_back(0);
+  }
+  *out = c.release();
+  return kOk;
+}
+
+int mc_close(mc_ctx* ctx) {
+  delete ctx;
+  return kOk;
+}
+
+int mc_load_model(mc_ctx* ctx, const uint8_t* data, size_t n, mc_model** out) {
+  clear_error();
+  if (!ctx || !data || !out) return set_error(kInvalidArgument, "mc_load_model: null argument");
+  auto m = std::make_unique<mc_model>();
+  m->ctx = ctx;
+  int st = parse_model_file(data, n, m->host);
+  if (st != kOk) return st;
+  for (int d : ctx->devices) {
+    std::unique_ptr<DevModel> dm;
+    if ((st = build_dev_model(m->host, d, dm)) != kOk) return st;
+    m->dev.push_back(std::move(dm));
+  }
+  *out = m.release();
+  return kOk;
+}
+
+int mc_model_free(mc_model* m) {
+  delete m;
+  return kOk;
+}
+
+int mc_model_info(const mc_model* m, int32_t* out) {
+  clear_error();
+  if (!m || !out) return set_error(kInvalidArgument, "mc_model_info: null argument");
+  const DevModel& d = *m->dev[0];
+  out[0] = d.V;
+  out[1] = d.D;
+  out[2] = d.H;
+  out[3] = (int32_t)d.blocks.size();
+  out[4] = d.max_context;
+  out[5] = d.heads;
+  out[6] = d.window;
+  out[7] = d.total_steps;
+  out[8] = d.ring;
+  out[9] = d.cache;
+  return kOk;
+}
+
+int mc_batch_open(mc_model* m, int count, int context_size, int max_prompt, int top_k, mc_batch** out) {
+  clear_error();
+  if (!m || !out || count <= 0) return set_error(kInvalidArgument, "mc_batch_open: bad arguments");
+  if (top_k < 0 || top_k > kMaxTopK) return set_error(kInvalidArgument, "mc_batch_open: top_k must be in [0, 64]");
+  auto b = std::make_unique<mc_batch>();
+  b->model = m;
+  b->count = count;
+  const DevModel& d0 = *m->dev[0];
+  b->window = d0.max_context;  // NewSession (session.go:20-28)
+  if (context_size > 0 && context_size < b->window) b->window = context_size;
+  b->pmax = std::min(std::max(1, max_prompt > 0 ? std::min(max_prompt, b->window) : b->window), 128);
+  b->topk = top_k;
+  const int ndev = (int)m->dev.size();
+  shard_sizes(count, ndev, b->first);
+  for (int g = 0; g < ndev; ++g) {
+    std::unique_ptr<DevBatch> sh;
+    const int S = b->first[g + 1] - b->first[g];
+    if (S == 0) {
+      b->shard.push_back(std::make_unique<DevBatch>());
+      b->shard.back()->m = m->dev[g].get();
+      continue;
+    }
+    int st = batch_create(m->dev[g].get(), S, b->window, b->pmax, top_k, sh);
+    if (st != kOk) return st;
+    if ((st = ensure_step_outputs(*sh, false, 1)) != kOk) return st;
+    b->shard.push_back(std::move(sh));
+  }
+  *out = b.release();
+  return kOk;
+}
+
+int mc_batch_close(mc_batch* b) {
+  delete b;
+  return kOk;
+}
+
+int mc_prefill(mc_batch* b, const int32_t* tokens, const int32_t* lens, int stride, float* logits, int32_t* next,
+               float* prob) {
+  clear_error();
+  if (!b || !tokens || !lens) return set_error(kInvalidArgument, "mc_prefill: null argument");
+  int P = 1;
+  int st = upload_prompts(b, tokens, lens, stride, &P);
+  if (st != kOk) return st;
+  for (auto& sh : b->shard) {
+    if (sh->S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh->m->device));
+    if ((st = ensure_step_outputs(*sh, logits != nullptr, 1)) != kOk) return st;
+    MC_CUDA(cudaMemsetAsync(sh->step, 0, 4, sh->stream));
+    if ((st = enqueue_forward(*sh, P, 0, 0.0, 0, logits != nullptr, true)) != kOk) return st;
+  }
+  return copy_step_outputs(b, logits, next, prob);
+}
+
+int mc_append(mc_batch* b, const int32_t* tokens, float* logits, int32_t* next, float* prob) {
+  clear_error();
+  if (!b || !tokens) return set_error(kInvalidArgument, "mc_append: null argument");
+  int st;
+  for (size_t g = 0; g < b->shard.size(); ++g) {
+    DevBatch& sh = *b->shard[g];
+    if (sh.S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh.m->device));
+    if ((st = ensure_step_outputs(sh, logits != nullptr, 1)) != kOk) return st;
+    MC_CUDA(cudaMemcpyAsync(sh.next_tok, tokens + b->first[g], sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemsetAsync(sh.step, 0, 4, sh.stream));
+    if ((st = run_graph_step(sh, 0, 0.0, 0, logits != nullptr)) != kOk) return st;
+  }
+  return copy_step_outputs(b, logits, next, prob);
+}
+
+int mc_generate(mc_batch* b, const int32_t* prompts, const int32_t* lens, int stride, int n_new, double temperature,
+                uint32_t session0, int32_t* out_tokens, float* out_probs) {
+  clear_error();
+  if (!b || !prompts || !lens || !out_tokens || n_new <= 0) return set_error(kInvalidArgument, "mc_generate: bad arguments");
+  const int mode = temperature > 0.001 ? 1 : 0;
+  if (mode == 1 && b->topk < 1)
+    return set_error(kUnsupported, "mc_generate: sampling needs a batch opened with top_k in [1, 64]");
+  const double inv_t = temperature > 0.001 ? 1.0 / temperature : 0.0;
+  int P = 1;
+  int st = upload_prompts(b, prompts, lens, stride, &P);
+  if (st != kOk) return st;
+  for (size_t g = 0; g < b->shard.size(); ++g) {
+    DevBatch& sh = *b->shard[g];
+    if (sh.S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh.m->device));
+    if ((st = ensure_step_outputs(sh, false, n_new)) != kOk) return st;
+    MC_CUDA(cudaMemsetAsync(sh.step, 0, 4, sh.stream));
+    const uint32_t s0 = session0 + (uint32_t)b->first[g];
+    if ((st = enqueue_forward(sh, P, mode, inv_t, s0, false, true)) != kOk) return st;
+    for (int t = 1; t < n_new; ++t)
+      if ((st = run_graph_step(sh, mode, inv_t, s0, false)) != kOk) return st;
+  }
+  for (size_t g = 0; g < b->shard.size(); ++g) {
+    DevBatch& sh = *b->shard[g];
+    if (sh.S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh.m->device));
+    // out columns are laid out with stride sh.out_stride >= n_new
+    std::vector<int32_t> t((size_t)sh.S * sh.out_stride);
+    std::vector<float> p((size_t)sh.S * sh.out_stride);
+    MC_CUDA(cudaMemcpyAsync(t.data(), sh.out_tok, t.size() * 4, cudaMemcpyDeviceToHost, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(p.data(), sh.out_prob, p.size() * 4, cudaMemcpyDeviceToHost, sh.stream));
+    if ((st = check_device_error(sh.stream)) != kOk) return st;
+    for (int i = 0; i < sh.S; ++i) {
+      const int s = b->first[g] + i;
+      std::copy(t.begin() + (size_t)i * sh.out_stride, t.begin() + (size_t)i * sh.out_stride + n_new,
+                out_tokens + (size_t)s * n_new);
+      if (out_probs)
+        std::copy(p.begin() + (size_t)i * sh.out_stride, p.begin() + (size_t)i * sh.out_stride + n_new,
+                  out_probs + (size_t)s * n_new);
+    }
+  }
+  return kOk;
+}
 
 int mc_gemm_i8_dev(const int8_t* a, const int8_t* w, int m, int n, int k, const float* row_scale,
                    const float* col_scale, const float* bias, int32_t* c_i32, float* y, void* stream) {

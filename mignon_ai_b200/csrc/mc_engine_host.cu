@@ -1,0 +1,517 @@
+// Host orchestration of the engine: the device replica of a model (pre-tiled weights), session
+// batches (state in HBM), and the launch sequences of prefill and decode.
+//
+// Decode step (one token for every session of a batch), all on one stream and captured once in a
+// CUDA graph:
+//   for each block b: block_kernel(b) [+ attn_decode_kernel(b)]
+//   block_kernel(final: last output projection + final RMSNorm)
+//   head_kernel (vocabulary split across CTAs) -> select_kernel -> bump_kernel
+// Prefill runs the same kernels layer-major over whole prompt segments (attn_prefill_kernel).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include "mc_engine.cuh"
+#include "mc_host.h"
+
+namespace mc {
+
+int parse_model_file(const uint8_t* data, size_t n, struct HostModel& m);
+
+namespace eng {
+
+// ------------------------------------------------------------------------------------------------
+// Weight tiling
+// ------------------------------------------------------------------------------------------------
+// Builds the pre-tiled image of W [rows x K] (row-major int8): chunk c, K tile kt, row r of the
+// tile = W row perm[c*128 + r] (-1: zero row), 128-byte swizzled.
+static std::vector<uint8_t> tile_weights(const int8_t* W, int K, const std::vector<int>& perm, int nchunks, int ktiles) {
+  std::vector<uint8_t> img((size_t)nchunks * ktiles * kTile, 0);
+  for (int c = 0; c < nchunks; ++c)
+    for (int kt = 0; kt < ktiles; ++kt) {
+      uint8_t* t = img.data() + ((size_t)c * ktiles + kt) * kTile;
+      for (int r = 0; r < 128; ++r) {
+        const int src = perm[(size_t)c * 128 + r];
+        if (src < 0) continue;
+        for (int k = 0; k < 128; ++k) {
+          const int kk = kt * 128 + k;
+          if (kk >= K) break;
+          const int chunk = k / 16;
+          const size_t off = (size_t)(r >> 3) * 1024 + (r & 7) * 128 + (size_t)((chunk ^ (r & 7)) << 4) + (k & 15);
+          t[off] = (uint8_t)W[(size_t)src * K + kk];
+        }
+      }
+    }
+  return img;
+}
+
+static std::vector<int> perm_identity(int rows, int nchunks) {
+  std::vector<int> p((size_t)nchunks * 128, -1);
+  for (int i = 0; i < rows; ++i) p[i] = i;
+  return p;
+}
+
+// Paired chunks: chunk c holds units [64c, 64c+64) of the first half (rows u) followed by the same
+// units of the second half (rows half + u): the GLU value/gate (W1) and highway delta/gate (W2)
+// pairs then meet in one 128-column accumulator.
+static std::vector<int> perm_paired(int half, int nchunks) {
+  std::vector<int> p((size_t)nchunks * 128, -1);
+  for (int c = 0; c < nchunks; ++c)
+    for (int j = 0; j < kHalfChunk; ++j) {
+      const int u = c * kHalfChunk + j;
+      if (u < half) {
+        p[(size_t)c * 128 + j] = u;
+        p[(size_t)c * 128 + kHalfChunk + j] = half + u;
+      }
+    }
+  return p;
+}
+
+struct DevGemm {
+  uint8_t* tiles = nullptr;
+  int K = 0, ktiles = 0, nchunks = 0;
+  float scale = 0;
+};
+
+struct DevBlock {
+  int steps = 0, attn_slot = -1;
+  std::vector<int> dil;
+  DevGemm w1, w2, wsel, qkv, out;
+  float *b1 = nullptr, *b2 = nullptr, *gamma = nullptr, *attn_norm = nullptr;
+};
+
+struct DevModel {
+  int device = 0;
+  int V = 0, D = 0, H = 0, max_context = 0, heads = 0, window = 0, cache = 0, ring = 0, total_steps = 0, n_attn = 0;
+  bool tied = true;
+  int8_t* embed = nullptr;
+  float embed_scale = 0;
+  DevGemm head;
+  float *head_b = nullptr, *final_gain = nullptr, *latch_base = nullptr;
+  std::vector<DevBlock> blocks;
+  std::vector<void*> allocs;
+  ~DevModel() {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    for (void* p : allocs) cudaFree(p);
+    cudaSetDevice(prev);
+  }
+  template <class T>
+  int upload(T*& dst, const void* src, size_t bytes) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, std::max<size_t>(bytes, 16)) != cudaSuccess)
+      return set_error(kOutOfMemory, "cudaMalloc failed for model weights");
+    allocs.push_back(p);
+    if (bytes) MC_CUDA(cudaMemcpy(p, src, bytes, cudaMemcpyHostToDevice));
+    dst = reinterpret_cast<T*>(p);
+    return kOk;
+  }
+  int upload_gemm(DevGemm& g, const int8_t* W, int rows, int K, float scale, int paired_half) {
+    g.K = K;
+    g.ktiles = (K + 127) / 128;
+    g.scale = scale;
+    std::vector<int> perm;
+    if (paired_half > 0) {
+      g.nchunks = (paired_half + kHalfChunk - 1) / kHalfChunk;
+      perm = perm_paired(paired_half, g.nchunks);
+    } else {
+      g.nchunks = (rows + 127) / 128;
+      perm = perm_identity(rows, g.nchunks);
+    }
+    auto img = tile_weights(W, K, perm, g.nchunks, g.ktiles);
+    return upload(g.tiles, img.data(), img.size());
+  }
+};
+
+// Latch base logits (ca/latch.go:11-25 over ca/layout.go:63-85).
+static void latch_base_logits(int D, std::vector<float>& out) {
+  out.resize(D);
+  const double minT = 1.5, maxT = 64.0;
+  for (int d = 0; d < D; ++d) {
+    double td = minT;
+    if (D > 1) td = minT * std::pow(std::pow(maxT / minT, 1.0 / (double)(D - 1)), (double)d);
+    const double lam = (double)(float)std::pow(2.0, -1.0 / td);
+    if (lam <= 0.0) out[d] = -15.0f;
+    else if (lam >= 1.0) out[d] = 15.0f;
+    else out[d] = (float)std::log(lam / (1.0 - lam));
+  }
+}
+
+static int step_dilation(int initial, int base, int step) {
+  int d = initial;
+  for (int s = 0; s < step && d < 32; ++s) d *= base;
+  return std::min(d, 32);
+}
+
+int build_dev_model(const HostModel& hm, int device, std::unique_ptr<DevModel>& out) {
+  auto m = std::make_unique<DevModel>();
+  m->device = device;
+  MC_CUDA(cudaSetDevice(device));
+  const int D = hm.state, H = hm.hidden, V = hm.vocab;
+  m->V = V;
+  m->D = D;
+  m->H = H;
+  m->tied = hm.tied;
+  m->max_context = hm.context_size < 64 ? 128 : hm.context_size;
+  m->heads = hm.attn_heads;
+  m->window = hm.attn_window;
+  m->cache = hm.attn_window > 0 ? hm.attn_window : m->max_context;
+  if (D > 384) return set_error(kUnsupported, "state_size > 384 is not supported by this build");
+  if (D % 4 != 0 || H % 4 != 0) return set_error(kUnsupported, "state_size and hidden_size must be multiples of 4");
+  int st;
+  if ((st = m->upload(m->embed, hm.embed.data.data(), hm.embed.data.size())) != kOk) return st;
+  m->embed_scale = hm.embed.scale;
+  const HostTensor& hw = hm.tied ? hm.embed : hm.head_w;
+  if ((st = m->upload_gemm(m->head, hw.data.data(), V, D, hw.scale, 0)) != kOk) return st;
+  if ((st = m->upload(m->head_b, hm.head_b.data(), hm.head_b.size() * 4)) != kOk) return st;
+  if ((int)hm.final_norm.size() == D) {
+    if ((st = m->upload(m->final_gain, hm.final_norm.data(), D * 4)) != kOk) return st;
+  }
+  std::vector<float> base;
+  latch_base_logits(D, base);
+  if ((st = m->upload(m->latch_base, base.data(), D * 4)) != kOk) return st;
+  int total = 0, longest = 0, nattn = 0;
+  for (const HostBlock& hb : hm.blocks) {
+    DevBlock b;
+    b.steps = hb.steps;
+    if (hb.steps > kMaxSteps) return set_error(kUnsupported, "more than 8 rule steps per block");
+    for (int s = 0; s < hb.steps; ++s) {
+      b.dil.push_back(step_dilation(hb.initial_dilation, hb.dilation_base, s));
+      longest = std::max(longest, b.dil.back());
+    }
+    total += hb.steps;
+    if ((st = m->upload_gemm(b.w1, hb.w1.data.data(), 2 * H, 3 * D, hb.w1.scale, H)) != kOk) return st;
+    if ((st = m->upload_gemm(b.w2, hb.w2.data.data(), 2 * D, H, hb.w2.scale, D)) != kOk) return st;
+    if ((st = m->upload_gemm(b.wsel, hb.wsel.data.data(), D, D, hb.wsel.scale, 0)) != kOk) return st;
+    if ((st = m->upload(b.b1, hb.b1.data(), hb.b1.size() * 4)) != kOk) return st;
+    if ((st = m->upload(b.b2, hb.b2.data(), hb.b2.size() * 4)) != kOk) return st;
+    if ((int)hb.gamma.size() == D && (st = m->upload(b.gamma, hb.gamma.data(), D * 4)) != kOk) return st;
+    if (hb.has_attn) {
+      if (m->heads <= 0 || D % m->heads != 0) return set_error(kBadModel, "attention blocks need attn_heads dividing state_size");
+      if (D / m->heads > 64) return set_error(kUnsupported, "attention head width above 64");
+      b.attn_slot = nattn++;
+      if ((st = m->upload_gemm(b.qkv, hb.qkv.data.data(), 3 * D, D, hb.qkv.scale, 0)) != kOk) return st;
+      if ((st = m->upload_gemm(b.out, hb.out.data.data(), D, D, hb.out.scale, 0)) != kOk) return st;
+      if ((st = m->upload(b.attn_norm, hb.attn_norm.data(), D * 4)) != kOk) return st;
+    }
+    m->blocks.push_back(std::move(b));
+  }
+  m->total_steps = total;
+  m->ring = longest + 1;
+  m->n_attn = nattn;
+  if (nattn > 0 && m->cache > 128) return set_error(kUnsupported, "attention caches above 128 positions");
+  out = std::move(m);
+  return kOk;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Session batches on one device
+// ------------------------------------------------------------------------------------------------
+struct DevBatch {
+  DevModel* m = nullptr;
+  int S = 0, window = 0, pmax = 0, nsplit = 1, topk = 0;
+  size_t rows = 0;  // scratch rows
+  cudaStream_t stream = nullptr;
+  std::vector<void*> allocs;
+  int32_t *pos = nullptr, *seglen = nullptr, *tok = nullptr, *next_tok = nullptr, *step = nullptr, *rowmap = nullptr,
+          *rowmap_id = nullptr, *target = nullptr;
+  float *norm_ring = nullptr, *latch = nullptr, *kv = nullptr;
+  float *cur = nullptr, *blockin = nullptr, *xbuf = nullptr, *hbuf = nullptr, *qbuf = nullptr, *att = nullptr,
+        *att_rowmax = nullptr, *fnorm = nullptr, *fnorm_rowmax = nullptr, *kvlin = nullptr, *logits = nullptr;
+  float4* part = nullptr;
+  float* topv = nullptr;
+  int32_t* topi = nullptr;
+  int32_t* out_tok = nullptr;
+  float* out_prob = nullptr;
+  double* out_logprob = nullptr;
+  int out_stride = 0;
+  cudaGraphExec_t graph = nullptr;
+  // Everything the captured decode step bakes in; a change forces a new capture.
+  struct GraphKey {
+    int mode = -1, logits = -1, stride = -1;
+    double inv_t = 0;
+    uint32_t session0 = 0;
+    const void* out_tok = nullptr;
+    const void* logits_buf = nullptr;
+    bool operator==(const GraphKey& o) const {
+      return mode == o.mode && logits == o.logits && stride == o.stride && inv_t == o.inv_t && session0 == o.session0 &&
+             out_tok == o.out_tok && logits_buf == o.logits_buf;
+    }
+  } graph_key;
+  ~DevBatch() {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(m ? m->device : prev);
+    if (graph) cudaGraphExecDestroy(graph);
+    for (void* p : allocs) cudaFree(p);
+    if (stream) cudaStreamDestroy(stream);
+    cudaSetDevice(prev);
+  }
+  template <class T>
+  int alloc(T*& p, size_t bytes) {
+    void* q = nullptr;
+    if (cudaMalloc(&q, std::max<size_t>(bytes, 16)) != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(kOutOfMemory, "cudaMalloc of " + std::to_string(bytes) + " bytes failed");
+    }
+    allocs.push_back(q);
+    p = reinterpret_cast<T*>(q);
+    return kOk;
+  }
+};
+
+static bool g_attr_done[64];
+static std::mutex g_attr_mu;
+
+static int ensure_attrs(int device) {
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  if (device < 64 && g_attr_done[device]) return kOk;
+  MC_CUDA(cudaFuncSetAttribute(block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
+  MC_CUDA(cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem));
+  MC_CUDA(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+  MC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+  if (device < 64) g_attr_done[device] = true;
+  return kOk;
+}
+
+int batch_create(DevModel* m, int S, int window, int pmax, int topk, std::unique_ptr<DevBatch>& out) {
+  MC_CUDA(cudaSetDevice(m->device));
+  int st = ensure_attrs(m->device);
+  if (st != kOk) return st;
+  auto b = std::make_unique<DevBatch>();
+  b->m = m;
+  b->S = S;
+  b->window = window;
+  b->pmax = std::max(1, std::min(pmax, 128));
+  b->topk = topk;
+  const int D = m->D, H = m->H;
+  const int spt_min = std::max(1, 128 / b->pmax);
+  const size_t tiles = std::max((size_t)(S + 127) / 128, (size_t)(S + spt_min - 1) / spt_min);
+  b->rows = tiles * 128;
+  // vocabulary splits: enough CTAs to cover the SMs
+  const int mtiles = (S + 127) / 128;
+  const int want = std::max(1, std::min({16, m->head.nchunks, (296 + mtiles - 1) / mtiles}));
+  const int cps = (m->head.nchunks + want - 1) / want;
+  b->nsplit = (m->head.nchunks + cps - 1) / cps;  // every split gets at least one chunk
+  MC_CUDA(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
+  const size_t R = b->rows;
+  if ((st = b->alloc(b->pos, S * 4)) || (st = b->alloc(b->seglen, S * 4)) || (st = b->alloc(b->tok, (size_t)S * b->pmax * 4)) ||
+      (st = b->alloc(b->next_tok, S * 4)) || (st = b->alloc(b->step, 4)) || (st = b->alloc(b->rowmap, S * 4)) ||
+      (st = b->alloc(b->rowmap_id, S * 4)) || (st = b->alloc(b->target, S * 4)))
+    return st;
+  if ((st = b->alloc(b->norm_ring, (size_t)S * m->total_steps * m->ring * D * 4)) ||
+      (st = b->alloc(b->latch, (size_t)S * m->total_steps * D * 4)) ||
+      (st = b->alloc(b->kv, (size_t)S * std::max(m->n_attn, 0) * 2 * m->cache * D * 4)))
+    return st;
+  if ((st = b->alloc(b->cur, R * D * 4)) || (st = b->alloc(b->blockin, R * D * 4)) || (st = b->alloc(b->xbuf, R * 3 * D * 4)) ||
+      (st = b->alloc(b->hbuf, R * H * 4)) || (st = b->alloc(b->qbuf, R * D * 4)) || (st = b->alloc(b->att, R * D * 4)) ||
+      (st = b->alloc(b->att_rowmax, R * 4)) || (st = b->alloc(b->fnorm, R * D * 4)) || (st = b->alloc(b->fnorm_rowmax, R * 4)))
+    return st;
+  if (m->n_attn > 0 && (st = b->alloc(b->kvlin, (size_t)S * b->pmax * 2 * D * 4))) return st;
+  if ((st = b->alloc(b->part, (size_t)S * b->nsplit * sizeof(float4)))) return st;
+  if (topk > 0 && ((st = b->alloc(b->topv, (size_t)S * b->nsplit * topk * 4)) ||
+                   (st = b->alloc(b->topi, (size_t)S * b->nsplit * topk * 4))))
+    return st;
+  MC_CUDA(cudaMemsetAsync(b->pos, 0, S * 4, b->stream));
+  MC_CUDA(cudaMemsetAsync(b->seglen, 0, S * 4, b->stream));
+  MC_CUDA(cudaMemsetAsync(b->step, 0, 4, b->stream));
+  MC_CUDA(cudaMemsetAsync(b->latch, 0, (size_t)S * m->total_steps * D * 4, b->stream));
+  std::vector<int32_t> id(S);
+  for (int i = 0; i < S; ++i) id[i] = i;
+  MC_CUDA(cudaMemcpyAsync(b->rowmap_id, id.data(), S * 4, cudaMemcpyHostToDevice, b->stream));
+  MC_CUDA(cudaStreamSynchronize(b->stream));
+  out = std::move(b);
+  return kOk;
+}
+
+static void fill_common(const DevBatch& b, BlockArgs& a, int P) {
+  const DevModel& m = *b.m;
+  memset(&a, 0, sizeof(a));
+  a.P = P;
+  a.spt = std::max(1, 128 / P);
+  a.n_sess = b.S;
+  a.n_tiles = (b.S + a.spt - 1) / a.spt;
+  a.pos0 = b.pos;
+  a.seglen = b.seglen;
+  a.tokens = P == 1 ? b.next_tok : b.tok;
+  a.D = m.D;
+  a.H = m.H;
+  a.V = m.V;
+  a.ring = m.ring;
+  a.total_steps = m.total_steps;
+  a.n_attn = m.n_attn;
+  a.cache = m.cache;
+  a.window = m.window;
+  a.embed = m.embed;
+  a.embed_scale = m.embed_scale;
+  a.latch_base = m.latch_base;
+  a.final_gain = m.final_gain;
+  a.norm_ring = b.norm_ring;
+  a.latch = b.latch;
+  a.kv = b.kv;
+  a.cur = b.cur;
+  a.blockin = b.blockin;
+  a.xbuf = b.xbuf;
+  a.hbuf = b.hbuf;
+  a.qbuf = b.qbuf;
+  a.att = b.att;
+  a.att_rowmax = b.att_rowmax;
+  a.fnorm = b.fnorm;
+  a.fnorm_rowmax = b.fnorm_rowmax;
+  a.kvlin = P > 1 ? b.kvlin : nullptr;
+}
+
+static GemmSpec spec(const DevGemm& g, int type, int step) {
+  GemmSpec s;
+  s.tiles = g.tiles;
+  s.K = g.K;
+  s.ktiles = g.ktiles;
+  s.nchunks = g.nchunks;
+  s.type = type;
+  s.step = step;
+  s.scale = g.scale;
+  return s;
+}
+
+static size_t attn_decode_smem(const DevModel& m, int nbuf) {
+  return (size_t)nbuf * 2 * m.cache * m.D * 4 + (size_t)m.D * 4 + (size_t)m.heads * m.cache * 4 + 32 * 4 + 16 + 128;
+}
+
+// Enqueues the whole forward pass of one segment (P rows per session; P = 1 is a decode step)
+// followed by the head and token selection.
+int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t session0, bool want_logits,
+                    bool advance_from_len) {
+  const DevModel& m = *b.m;
+  cudaStream_t s = b.stream;
+  const int nb = (int)m.blocks.size();
+  int bs = 0;
+  for (int bi = 0; bi <= nb; ++bi) {
+    BlockArgs a;
+    fill_common(b, a, P);
+    const bool final_k = bi == nb;
+    int g = 0;
+    if (bi > 0 && m.blocks[bi - 1].attn_slot >= 0) {
+      a.has_out = 1;
+      a.gemms[g++] = spec(m.blocks[bi - 1].out, kGOut, 0);
+    }
+    if (!final_k) {
+      const DevBlock& blk = m.blocks[bi];
+      a.block = bi;
+      a.embed_first = bi == 0;
+      a.residual = bi > 0;
+      a.nsteps = blk.steps;
+      a.bs0 = bs;
+      for (int st = 0; st < blk.steps; ++st) {
+        a.dil[st] = blk.dil[st];
+        a.gemms[g++] = spec(blk.wsel, kGWsel, st);
+        a.gemms[g++] = spec(blk.w1, kGW1, st);
+        a.gemms[g++] = spec(blk.w2, kGW2, st);
+      }
+      a.gamma = blk.gamma;
+      a.b1 = blk.b1;
+      a.b2 = blk.b2;
+      if (blk.attn_slot >= 0) {
+        a.has_attn = 1;
+        a.attn_slot = blk.attn_slot;
+        a.attn_norm = blk.attn_norm;
+        a.gemms[g++] = spec(blk.qkv, kGQkv, 0);
+      }
+      bs += blk.steps;
+    } else {
+      a.block = nb;
+      a.embed_first = nb == 0;
+      a.final_norm = 1;
+    }
+    a.ngemms = g;
+    block_kernel<<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a);
+    MC_CUDA(cudaGetLastError());
+    if (!final_k && m.blocks[bi].attn_slot >= 0) {
+      AttnArgs aa;
+      memset(&aa, 0, sizeof(aa));
+      aa.n_sess = b.S;
+      aa.D = m.D;
+      aa.heads = m.heads;
+      aa.dh = m.D / m.heads;
+      aa.cache = m.cache;
+      aa.window = m.window;
+      aa.n_attn = m.n_attn;
+      aa.attn_slot = m.blocks[bi].attn_slot;
+      aa.P = P;
+      aa.spt = a.spt;
+      aa.pos0 = b.pos;
+      aa.seglen = b.seglen;
+      aa.qbuf = b.qbuf;
+      aa.kv = b.kv;
+      aa.kvlin = b.kvlin;
+      aa.att = b.att;
+      aa.att_rowmax = b.att_rowmax;
+      aa.scale = (float)(1.0 / std::sqrt((double)aa.dh));
+      if (P == 1) {
+        const int nbuf = attn_decode_smem(m, 2) <= 200 * 1024 ? 2 : 1;
+        const int grid = std::min(b.S, 148 * (nbuf == 2 ? 1 : 1));
+        attn_decode_kernel<<<grid, kAttnThreads, attn_decode_smem(m, nbuf), s>>>(aa, nbuf);
+      } else {
+        const size_t smem = (size_t)P * 2 * m.D * 4 + 32 * 4 + 16 + 128;
+        if (smem > 220 * 1024) return set_error(kUnsupported, "prefill segment too long for the attention kernel");
+        attn_prefill_kernel<<<b.S, kAttnThreads, smem, s>>>(aa);
+      }
+      MC_CUDA(cudaGetLastError());
+    }
+  }
+  HeadArgs h;
+  memset(&h, 0, sizeof(h));
+  h.n_sess = b.S;
+  h.D = m.D;
+  h.V = m.V;
+  h.nsplit = b.nsplit;
+  h.nchunks = m.head.nchunks;
+  h.cps = (m.head.nchunks + b.nsplit - 1) / b.nsplit;
+  h.ktiles = m.head.ktiles;
+  h.rowmap = P == 1 ? b.rowmap_id : b.rowmap;
+  h.fnorm = b.fnorm;
+  h.fnorm_rowmax = b.fnorm_rowmax;
+  h.tiles = m.head.tiles;
+  h.scale = m.head.scale;
+  h.head_b = m.head_b;
+  h.topk = mode == 1 ? b.topk : 0;
+  h.target = mode == 2 ? b.target : nullptr;
+  h.logits_out = want_logits ? b.logits : nullptr;
+  h.part = b.part;
+  h.topv = b.topv;
+  h.topi = b.topi;
+  dim3 hg((b.S + 127) / 128, b.nsplit);
+  head_kernel<<<hg, kHeadThreads, kHeadSmem, s>>>(h);
+  MC_CUDA(cudaGetLastError());
+  SelectArgs sa;
+  memset(&sa, 0, sizeof(sa));
+  sa.n_sess = b.S;
+  sa.nsplit = b.nsplit;
+  sa.topk = b.topk;
+  sa.mode = mode;
+  sa.inv_temp = inv_temp;
+  sa.session0 = session0;
+  sa.part = b.part;
+  sa.topv = b.topv;
+  sa.topi = b.topi;
+  sa.step = b.step;
+  sa.out_stride = b.out_stride;
+  sa.next_tok = b.next_tok;
+  sa.out_tok = b.out_tok;
+  sa.out_prob = b.out_prob;
+  sa.out_logprob = b.out_logprob;
+  sa.pos = b.pos;
+  sa.seglen = b.seglen;
+  sa.advance_from_len = advance_from_len ? 1 : 0;
+  select_kernel<<<(b.S + 127) / 128, 128, 0, s>>>(sa);
+  MC_CUDA(cudaGetLastError());
+  bump_kernel<<<1, 1, 0, s>>>(b.step);
+  MC_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+}  // namespace eng
+}  // namespace mc

