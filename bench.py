@@ -1,0 +1,324 @@
+#!/usr/bin/env python
+"""Generated tokens/s of batched INT8 sessions on B200 (BASELINE.json metric, config 2).
+
+One step = one whole generation job on every GPU: 4096 sessions per GPU, each prefilled with a
+48-token prompt (uniform non-special ids, seed 2) and greedily decoded for 80 tokens (filling the
+128-token context) — 327,680 generated tokens per GPU per step. Sessions shard by index (weak
+scaling: each rank runs its own 4096 sessions, global session ids rank*4096 + i); there is no
+collective on the data path (one scalar all-reduce after timing takes the max over ranks).
+
+  value  device-resident prompts and outputs (mc_generate_dev), CUDA events on the batch stream
+  e2e    the public host API (mc_generate): pinned host prompts in, tokens/probs out, per step
+
+--impl reference times the CPU restatement of the reference engine (oracle/, the reference's own
+Go engine cannot be built here) on the host cores with all threads, on a bounded sample.
+"""
+import argparse
+import ctypes
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIG = 2
+SESSIONS = 4096
+PROMPT = 48
+NEW = 80
+PROMPT_SEED = 2
+METRIC = "generated tokens/s, batched INT8 sessions"
+UNIT = "tokens/s"
+
+
+def workload_config(n_gpus, sessions):
+    return {
+        "workload": "config2: INT8 Hybrid NCA d_model=128 hidden=256 4 blocks x 1 step, attn 4 heads window 64, "
+                    "vocab 2048, ctx 128; %d sessions per GPU, 48-token prompts (seed 2), greedy 80 tokens" % sessions,
+        "sessions_per_gpu": sessions, "prompt_tokens": PROMPT, "new_tokens": NEW, "model_seed": 0,
+        "parallelism": "sessions sharded by index, %d GPU(s), full weight replica per GPU" % n_gpus,
+        "l2": "no flush: per-GPU session state (KV rings 1.07 GB) is larger than the 126 MB L2",
+    }
+
+
+def prompts_for(rank, sessions):
+    from mignon_ai_b200 import synth
+    # rows of the Philox prompt stream are global session ids
+    allp = synth.prompts_uniform_fast((rank + 1) * sessions, PROMPT, synth.CONFIGS[CONFIG].vocab, PROMPT_SEED)
+    return np.ascontiguousarray(allp[rank * sessions:(rank + 1) * sessions])
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, indices):
+        self.indices = indices
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.p.wait(5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+        self.f.flush()
+        rows = []
+        with open(self.f.name) as fh:
+            for line in fh:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    idx = int(parts[0])
+                except ValueError:
+                    continue
+                if self.indices and idx not in self.indices:
+                    continue
+                rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clocks not sampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def run_cpu_reference(steps, warmup, sessions=None, label="reference"):
+    """The CPU restatement of the reference engine (oracle/) on all host threads, bounded sample."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle
+    from mignon_ai_b200 import synth
+    cores = os.cpu_count() or 1
+    n = sessions or max(64, 64 * cores)
+    data = synth.build_model_file(synth.CONFIGS[CONFIG])
+    om = pyoracle.Model(data)
+    prompts = prompts_for(0, n)
+    lens = np.full(n, PROMPT, np.int32)
+    for _ in range(max(0, warmup)):
+        om.generate_greedy(prompts[:cores], lens[:cores], 4, nthreads=cores)
+    times = []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        om.generate_greedy(prompts, lens, NEW, nthreads=cores)
+        times.append(time.perf_counter() - t0)
+    tps = n * NEW / float(np.mean(times))
+    sample = ("%d sessions x (48-token prompt + 80 greedy tokens) of the config-2 workload per step, "
+              "OpenMP over sessions, one engine state per session" % n)
+    return tps, cores, sample, float(np.mean(times))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--sessions", type=int, default=SESSIONS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        tps, cores, sample, sec = run_cpu_reference(args.steps, args.warmup)
+        line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1000.0, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32 activations x int8 weights (CPU)",
+                "data": "synthetic", "config": workload_config(args.gpus, args.sessions),
+                "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+                "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "note": "the reference is Go; no Go toolchain exists on these machines, so its CPU engine is "
+                        "timed as the C restatement in oracle/ (same algorithm and float32 operation order)"}
+        print(json.dumps(line))
+        return 0
+
+    import torch
+    from mignon_ai_b200 import _lib, quant, synth
+
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", local_rank)
+
+    S = args.sessions
+    data = synth.build_model_file(synth.CONFIGS[CONFIG])
+    ctx = quant.Context((local_rank,))
+    model = quant.Model.decode(data, ctx)
+    batch = model.new_batch(S, 0, PROMPT)
+    L = _lib.lib()
+    L.mc_generate_dev.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_double, ctypes.c_uint32] + \
+        [ctypes.c_void_p] * 2
+    L.mc_batch_stream.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]
+    L.mc_batch_error.argtypes = [ctypes.c_void_p]
+    L.mc_profile_step.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    sp = ctypes.c_void_p()
+    _lib.check(L.mc_batch_stream(batch._h, 0, ctypes.byref(sp)))
+    stream = torch.cuda.ExternalStream(sp.value, device=dev)
+
+    prompts = prompts_for(rank, S)
+    lens = np.full(S, PROMPT, np.int32)
+    d_prompts = torch.from_numpy(prompts).to(dev)
+    d_lens = torch.from_numpy(lens).to(dev)
+    d_tok = torch.zeros((S, NEW), dtype=torch.int32, device=dev)
+    d_prob = torch.zeros((S, NEW), dtype=torch.float32, device=dev)
+    session0 = rank * S
+
+    def job():
+        _lib.check(L.mc_generate_dev(batch._h, d_prompts.data_ptr(), d_lens.data_ptr(), PROMPT, PROMPT, NEW, 0.0,
+                                     session0, d_tok.data_ptr(), d_prob.data_ptr()))
+
+    for _ in range(args.warmup):
+        job()
+    _lib.check(L.mc_batch_error(batch._h))
+
+    clocks = ClockSampler([local_rank] if world == 1 else list(range(world))) if rank == 0 else None
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    if clocks:
+        clocks.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for _ in range(args.steps):
+        job()
+    t_end.record(stream)
+    _lib.check(L.mc_batch_error(batch._h))
+    torch.cuda.synchronize(dev)
+    ms = t_start.elapsed_time(t_end)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    tokens_per_step = S * NEW * world
+    value = tokens_per_step * args.steps / (ms / 1000.0)
+
+    # ---- e2e through the host API: pinned prompts in, tokens/probs out, every step ----
+    h_prompts = torch.from_numpy(prompts).pin_memory().numpy()
+    h_lens = torch.from_numpy(lens).pin_memory().numpy()
+    h_tok = torch.zeros((S, NEW), dtype=torch.int32).pin_memory().numpy()
+    h_prob = torch.zeros((S, NEW), dtype=torch.float32).pin_memory().numpy()
+    L.mc_generate.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 2 + [ctypes.c_double, ctypes.c_uint32] + \
+        [ctypes.c_void_p] * 2
+
+    def e2e_job():
+        _lib.check(L.mc_generate(batch._h, h_prompts.ctypes.data, h_lens.ctypes.data, PROMPT, NEW, 0.0, session0,
+                                 h_tok.ctypes.data, h_prob.ctypes.data))
+
+    e2e_job()
+    e_steps = max(1, min(args.steps, 3))
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e_steps):
+        e2e_job()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ems = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ems], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e_value = tokens_per_step * e_steps / (ems / 1000.0)
+    same = bool(np.array_equal(h_tok, d_tok.cpu().numpy()))
+
+    # ---- per-launch device times of one decode step (steady state: window full) ----
+    ms_arr = np.zeros(64, np.float32)
+    kinds = np.zeros(64, np.int32)
+    nl = ctypes.c_int()
+    _lib.check(L.mc_profile_step(batch._h, 64, ms_arr.ctypes.data, kinds.ctypes.data, ctypes.byref(nl)))
+    n = nl.value
+    per_kind = {}
+    for k, t in zip(kinds[:n], ms_arr[:n]):
+        per_kind.setdefault(int(k), []).append(float(t))
+    names = {0: "block_kernel", 1: "attn_decode_kernel", 2: "block_kernel(final)", 3: "head_kernel",
+             4: "select_kernel", 5: "bump_kernel"}
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    D, W, Hh = 128, 64, 4
+    span = min(PROMPT + NEW, W)
+    attn_bytes = S * (2 * span * D * 4 + 2 * D * 4 + 4)  # K and V windows read, q read, o written
+    attn_ms = float(np.mean(per_kind.get(1, [float("nan")])))
+    achieved = attn_bytes / (attn_ms / 1000.0) / 1e9
+    step_ms = sum(ms_arr[:n])
+    shares = {names.get(k, str(k)): round(sum(v) / step_ms, 4) for k, v in per_kind.items()}
+
+    launches_per_job = (1 + 2 * 4 + 1 + 3) + (NEW - 1) * (2 * 4 + 1 + 3)
+
+    out = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            tps, cores, sample, _ = run_cpu_reference(1, 0)
+            cpu = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+        out = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 weights x float32 activations (3 int8 digit planes, s32 accumulate)",
+            "data": "synthetic", "config": workload_config(world, S),
+            "clocks": clk,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(world * (prompts.nbytes + lens.nbytes)),
+                    "d2h_bytes_per_step": int(world * (h_tok.nbytes + h_prob.nbytes)), "matches_value_run": same},
+            "gpu_launches": int(launches_per_job * args.steps),
+            "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel", "achieved": achieved, "peak": hbm_peak,
+                         "unit": "GB/s", "frac": achieved / hbm_peak,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s",
+                         "traffic": None,
+                         "algorithmic_bytes_per_launch": attn_bytes, "avg_launch_ms": attn_ms},
+            "decode_step_profile": {"ms_total": float(step_ms), "share": shares,
+                                    "ms_per_kind": {names.get(k, str(k)): float(np.mean(v)) for k, v in per_kind.items()}},
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(out, default=lambda o: o.item() if hasattr(o, "item") else str(o)))
+    batch.close()
+    model.close()
+    ctx.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -115,6 +115,23 @@ int mc_append(mc_batch* batch, const int32_t* tokens, float* logits, int32_t* ne
 int mc_generate(mc_batch* batch, const int32_t* prompts, const int32_t* lens, int stride, int n_new, double temperature,
                 uint32_t session0, int32_t* out_tokens, float* out_probs);
 
+/* mc_generate with device-resident inputs and outputs on a single-device batch: enqueues the
+ * whole job on the batch's stream (mc_batch_stream) and returns without synchronizing.
+ * pmax >= every lens[s]. Check completion and device errors with mc_batch_error. */
+int mc_generate_dev(mc_batch* batch, const int32_t* d_prompts, const int32_t* d_lens, int stride, int pmax, int n_new,
+                    double temperature, uint32_t session0, int32_t* d_out_tokens, float* d_out_probs);
+
+/* The CUDA stream (cudaStream_t) the batch's work on device shard `shard` runs on. */
+int mc_batch_stream(mc_batch* batch, int shard, void** stream);
+
+/* Waits for the batch's work and reports a device-side error (MC_DEVICE_TIMEOUT) if any. */
+int mc_batch_error(mc_batch* batch);
+
+/* Runs one greedy decode step of a single-device batch launch by launch, timing each launch with
+ * CUDA events: ms[i] and kinds[i] (0 block, 1 attention, 2 final block, 3 head, 4 select,
+ * 5 step counter) for i < *n_launches <= max_launches. The step advances the sessions. */
+int mc_profile_step(mc_batch* batch, int max_launches, float* ms, int32_t* kinds, int* n_launches);
+
 #ifdef __cplusplus
 }
 #endif

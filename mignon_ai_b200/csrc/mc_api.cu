@@ -344,6 +344,71 @@ int mc_generate(mc_batch* b, const int32_t* prompts, const int32_t* lens, int st
   return kOk;
 }
 
+int mc_batch_stream(mc_batch* b, int shard, void** stream) {
+  clear_error();
+  if (!b || !stream || shard < 0 || shard >= (int)b->shard.size()) return set_error(kInvalidArgument, "mc_batch_stream: bad arguments");
+  *stream = (void*)b->shard[shard]->stream;
+  return kOk;
+}
+
+int mc_generate_dev(mc_batch* b, const int32_t* d_prompts, const int32_t* d_lens, int stride, int pmax, int n_new,
+                    double temperature, uint32_t session0, int32_t* d_out_tokens, float* d_out_probs) {
+  clear_error();
+  if (!b || !d_prompts || !d_lens || !d_out_tokens || n_new <= 0 || pmax <= 0)
+    return set_error(kInvalidArgument, "mc_generate_dev: bad arguments");
+  if (b->shard.size() != 1) return set_error(kUnsupported, "mc_generate_dev: single-device batches only");
+  DevBatch& sh = *b->shard[0];
+  const int P = std::min(pmax, b->window);
+  if (P > b->pmax) return set_error(kInvalidArgument, "mc_generate_dev: pmax above the batch's max_prompt");
+  const int mode = temperature > 0.001 ? 1 : 0;
+  if (mode == 1 && b->topk < 1) return set_error(kUnsupported, "mc_generate_dev: sampling needs top_k >= 1");
+  const double inv_t = mode ? 1.0 / temperature : 0.0;
+  MC_CUDA(cudaSetDevice(sh.m->device));
+  int st;
+  if ((st = ensure_step_outputs(sh, false, n_new)) != kOk) return st;
+  prepare_prompts_kernel<<<(sh.S + 127) / 128, 128, 0, sh.stream>>>(d_prompts, d_lens, stride, sh.S, P, b->window, sh.tok,
+                                                                      sh.seglen, sh.pos, sh.rowmap, sh.step);
+  MC_CUDA(cudaGetLastError());
+  if ((st = enqueue_forward(sh, P, mode, inv_t, session0, false, true)) != kOk) return st;
+  for (int t = 1; t < n_new; ++t)
+    if ((st = run_graph_step(sh, mode, inv_t, session0, false)) != kOk) return st;
+  MC_CUDA(cudaMemcpy2DAsync(d_out_tokens, (size_t)n_new * 4, sh.out_tok, (size_t)sh.out_stride * 4, (size_t)n_new * 4, sh.S,
+                            cudaMemcpyDeviceToDevice, sh.stream));
+  if (d_out_probs)
+    MC_CUDA(cudaMemcpy2DAsync(d_out_probs, (size_t)n_new * 4, sh.out_prob, (size_t)sh.out_stride * 4, (size_t)n_new * 4,
+                              sh.S, cudaMemcpyDeviceToDevice, sh.stream));
+  return kOk;
+}
+
+int mc_batch_error(mc_batch* b) {
+  clear_error();
+  if (!b) return set_error(kInvalidArgument, "mc_batch_error: null batch");
+  return sync_all(b);
+}
+
+int mc_profile_step(mc_batch* b, int max_launches, float* ms, int32_t* kinds, int* n_launches) {
+  clear_error();
+  if (!b || !ms || !kinds || !n_launches || b->shard.size() != 1)
+    return set_error(kInvalidArgument, "mc_profile_step: bad arguments (single-device batches only)");
+  DevBatch& sh = *b->shard[0];
+  MC_CUDA(cudaSetDevice(sh.m->device));
+  int st;
+  if ((st = ensure_step_outputs(sh, false, 1)) != kOk) return st;
+  MC_CUDA(cudaMemsetAsync(sh.step, 0, 4, sh.stream));
+  LaunchLog log;
+  if ((st = log.record(sh.stream, -1)) != kOk) return st;
+  if ((st = enqueue_forward(sh, 1, 0, 0.0, 0, false, false, &log)) != kOk) return st;
+  MC_CUDA(cudaStreamSynchronize(sh.stream));
+  if ((st = check_device_error(sh.stream)) != kOk) return st;
+  const int n = std::min((int)log.ev.size() - 1, max_launches);
+  for (int i = 0; i < n; ++i) {
+    MC_CUDA(cudaEventElapsedTime(&ms[i], log.ev[i], log.ev[i + 1]));
+    kinds[i] = log.kind[i + 1];
+  }
+  *n_launches = n;
+  return kOk;
+}
+
 int mc_gemm_i8_dev(const int8_t* a, const int8_t* w, int m, int n, int k, const float* row_scale,
                    const float* col_scale, const float* bias, int32_t* c_i32, float* y, void* stream) {
   clear_error();

@@ -381,10 +381,45 @@ static size_t attn_decode_smem(const DevModel& m, int nbuf) {
   return (size_t)nbuf * 2 * m.cache * m.D * 4 + (size_t)m.D * 4 + (size_t)m.heads * m.cache * 4 + 32 * 4 + 16 + 128;
 }
 
+// Launch profiler: when set, an event is recorded after every launch with the launch's kind
+// (0 block, 1 attention, 2 final block, 3 head, 4 select, 5 step counter).
+struct LaunchLog {
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> kind;
+  int record(cudaStream_t s, int k) {
+    cudaEvent_t e;
+    MC_CUDA(cudaEventCreate(&e));
+    MC_CUDA(cudaEventRecord(e, s));
+    ev.push_back(e);
+    kind.push_back(k);
+    return kOk;
+  }
+  ~LaunchLog() {
+    for (auto e : ev) cudaEventDestroy(e);
+  }
+};
+
+// Prepares a prefill from device-resident prompts: trims each prompt to the window, lays the
+// segment out [S][P], resets positions and computes the head's row map.
+__global__ void prepare_prompts_kernel(const int32_t* prompts, const int32_t* lens, int stride, int S, int P, int window,
+                                       int32_t* tok, int32_t* seglen, int32_t* pos, int32_t* rowmap, int32_t* step) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s == 0) *step = 0;
+  if (s >= S) return;
+  const int L = max(0, min(lens[s], stride));
+  const int n = min(min(L, window), P);
+  const int32_t* src = prompts + (size_t)s * stride + (L - n);
+  for (int i = 0; i < P; ++i) tok[(size_t)s * P + i] = i < n ? src[i] : 0;
+  seglen[s] = n;
+  pos[s] = 0;
+  const int spt = max(1, 128 / P);
+  rowmap[s] = (s / spt) * 128 + (s % spt) * P + max(n - 1, 0);
+}
+
 // Enqueues the whole forward pass of one segment (P rows per session; P = 1 is a decode step)
 // followed by the head and token selection.
 int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t session0, bool want_logits,
-                    bool advance_from_len) {
+                    bool advance_from_len, LaunchLog* log = nullptr) {
   const DevModel& m = *b.m;
   cudaStream_t s = b.stream;
   const int nb = (int)m.blocks.size();
@@ -429,6 +464,7 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
     a.ngemms = g;
     block_kernel<<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a);
     MC_CUDA(cudaGetLastError());
+    if (log) log->record(s, final_k ? 2 : 0);
     if (!final_k && m.blocks[bi].attn_slot >= 0) {
       AttnArgs aa;
       memset(&aa, 0, sizeof(aa));
@@ -460,6 +496,7 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
         attn_prefill_kernel<<<b.S, kAttnThreads, smem, s>>>(aa);
       }
       MC_CUDA(cudaGetLastError());
+      if (log) log->record(s, 1);
     }
   }
   HeadArgs h;
@@ -486,6 +523,7 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
   dim3 hg((b.S + 127) / 128, b.nsplit);
   head_kernel<<<hg, kHeadThreads, kHeadSmem, s>>>(h);
   MC_CUDA(cudaGetLastError());
+  if (log) log->record(s, 3);
   SelectArgs sa;
   memset(&sa, 0, sizeof(sa));
   sa.n_sess = b.S;
@@ -508,8 +546,10 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
   sa.advance_from_len = advance_from_len ? 1 : 0;
   select_kernel<<<(b.S + 127) / 128, 128, 0, s>>>(sa);
   MC_CUDA(cudaGetLastError());
+  if (log) log->record(s, 4);
   bump_kernel<<<1, 1, 0, s>>>(b.step);
   MC_CUDA(cudaGetLastError());
+  if (log) log->record(s, 5);
   return kOk;
 }
 
