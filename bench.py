@@ -136,6 +136,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--sessions", type=int, default=SESSIONS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quick", action="store_true",
+                    help="profiling case: one generation job, no timing, e2e, profile or CPU baseline")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -197,6 +199,15 @@ def main():
     def job():
         _lib.check(L.mc_generate_dev(batch._h, d_prompts.data_ptr(), d_lens.data_ptr(), PROMPT, PROMPT, NEW, 0.0,
                                      session0, d_tok.data_ptr(), d_prob.data_ptr()))
+
+    if args.quick:
+        job()
+        _lib.check(L.mc_batch_error(batch._h))
+        print(json.dumps({"quick": True, "sessions": S, "tokens": int(d_tok.sum().item())}))
+        batch.close()
+        model.close()
+        ctx.close()
+        return 0
 
     for _ in range(args.warmup):
         job()

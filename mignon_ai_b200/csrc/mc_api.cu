@@ -1,5 +1,7 @@
 // C-ABI entry points of libmignoncuda (include/mignon_cuda.h).
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <vector>
@@ -396,9 +398,28 @@ int mc_profile_step(mc_batch* b, int max_launches, float* ms, int32_t* kinds, in
   if ((st = ensure_step_outputs(sh, false, 1)) != kOk) return st;
   MC_CUDA(cudaMemsetAsync(sh.step, 0, 4, sh.stream));
   LaunchLog log;
+  // MC_TRACE=1: phase timestamps of CTA 0 of every block-kernel launch, printed to stderr.
+  const bool trace = getenv("MC_TRACE") != nullptr;
+  const int nb = (int)sh.m->blocks.size() + 1;
+  if (trace) {
+    MC_CUDA(cudaMalloc(&sh.trace, (size_t)64 * nb * 8));
+    MC_CUDA(cudaMemsetAsync(sh.trace, 0, (size_t)64 * nb * 8, sh.stream));
+  }
   if ((st = log.record(sh.stream, -1)) != kOk) return st;
   if ((st = enqueue_forward(sh, 1, 0, 0.0, 0, false, false, &log)) != kOk) return st;
   MC_CUDA(cudaStreamSynchronize(sh.stream));
+  if (trace) {
+    std::vector<unsigned long long> tr((size_t)64 * nb);
+    MC_CUDA(cudaMemcpy(tr.data(), sh.trace, tr.size() * 8, cudaMemcpyDeviceToHost));
+    cudaFree(sh.trace);
+    sh.trace = nullptr;
+    for (int b2 = 0; b2 < nb; ++b2) {
+      fprintf(stderr, "block launch %d phase ns:", b2);
+      for (int i = 1; i < 64 && tr[(size_t)64 * b2 + i]; ++i)
+        fprintf(stderr, " %llu", tr[(size_t)64 * b2 + i] - tr[(size_t)64 * b2 + i - 1]);
+      fprintf(stderr, "\n");
+    }
+  }
   if ((st = check_device_error(sh.stream)) != kOk) return st;
   const int n = std::min((int)log.ev.size() - 1, max_launches);
   for (int i = 0; i < n; ++i) {

@@ -46,112 +46,117 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return m;
 }
 
-// Decode: one row per session (P == 1). Dynamic smem: nbuf x (2 rings) + q + scores.
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnArgs a, int nbuf) {
-  extern __shared__ uint8_t smem_raw[];
-  float* sm = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  const int D = a.D, cache = a.cache;
-  const size_t ring_f = (size_t)cache * D;
-  float* kvbuf = sm;                          // nbuf x [2][cache][D]
-  float* sq = kvbuf + nbuf * 2 * ring_f;      // [D]
-  float* sc = sq + D;                         // [heads][cache]
-  float* red = sc + a.heads * cache;          // [32]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(red + 32);  // [2]
+// Decode: one warp per (session, head), P == 1. Lane i computes the scores of window positions
+// lo+i, lo+i+32, ... (keys read straight from the ring in HBM, 16-byte loads); the softmax runs on
+// warp shuffles; then the lanes own head dimensions and walk the window's values (coalesced rows).
+// max |o| of the row is max-accumulated into att_rowmax (zeroed by the block kernel).
+template <int DH>  // head width known at compile time (0: taken from the arguments)
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+  const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  const int s = gw / a.heads, h = gw - (gw / a.heads) * a.heads;
+  if (s >= a.n_sess || a.seglen[s] <= 0) return;
+  const int D = a.D, dh = DH > 0 ? DH : a.dh, cache = a.cache;
+  const int pos = a.pos0[s];
+  int ws = 0;
+  if (a.window > 0 && pos - a.window + 1 > 0) ws = pos - a.window + 1;
+  const int lo = max(ws, pos - cache + 1);
+  const int span = pos - lo + 1;  // <= cache <= 128
+  const int lo_slot = lo % cache;
+  const int grow = grow_of(a, s, 0);
+  const float* K = a.kv + ((size_t)s * a.n_attn + a.attn_slot) * 2 * (size_t)cache * D + h * dh;
+  const float* V = K + (size_t)cache * D;
+  const float* q = a.qbuf + (size_t)grow * D + h * dh;
 
-  if (threadIdx.x == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
-    fence_barrier_init();
+  float sc[4];
+  int slot[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = lane + 32 * k;
+    int sl = lo_slot + i;
+    if (sl >= cache) sl -= cache;
+    slot[k] = sl;
+    sc[k] = 0.f;
   }
-  __syncthreads();
-
-  auto issue = [&](int s, int buf) {
-    const int pos = a.pos0[s];
-    const int nslots = min(pos + 1, cache);
-    const uint32_t bytes = (uint32_t)(nslots * D * 4);
-    const float* src = a.kv + ((size_t)s * a.n_attn + a.attn_slot) * 2 * ring_f;
-    float* dst = kvbuf + (size_t)buf * 2 * ring_f;
-    mbar_arrive_expect_tx(&bar[buf], 2 * bytes);
-    bulk_load(dst, src, bytes, &bar[buf]);
-    bulk_load(dst + ring_f, src + ring_f, bytes, &bar[buf]);
-  };
-
-  uint32_t phase[2] = {0, 0};
-  int it = 0;
-  int s = blockIdx.x;
-  if (threadIdx.x == 0 && s < a.n_sess && a.seglen[s] > 0) issue(s, 0);
-  for (; s < a.n_sess; s += gridDim.x, ++it) {
-    const int buf = nbuf == 2 ? (it & 1) : 0;
-    const int next = s + gridDim.x;
-    const bool active = a.seglen[s] > 0;
-    // Single buffer: load this session now (the previous one is finished: the loop ends with a
-    // block-wide barrier). Double buffer: prefetch the next session into the other buffer.
-    if (nbuf == 1 && it > 0 && threadIdx.x == 0 && active) issue(s, 0);
-    if (nbuf == 2 && threadIdx.x == 0 && next < a.n_sess && a.seglen[next] > 0) issue(next, buf ^ 1);
-    if (!active) continue;
-    bool ok = mbar_wait_or_abort(&bar[buf], phase[buf], kErrWaitFull);
-    phase[buf] ^= 1;
-    const int pos = a.pos0[s];
-    int ws = 0;
-    if (a.window > 0 && pos - a.window + 1 > 0) ws = pos - a.window + 1;
-    const int lo = max(ws, pos - cache + 1);
-    const int span = pos - lo + 1;
-    const int grow = grow_of(a, s, 0);
-    const float* K = kvbuf + (size_t)buf * 2 * ring_f;
-    const float* V = K + ring_f;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) sq[d] = a.qbuf[(size_t)grow * D + d];
-    __syncthreads();
-    const int dh = a.dh;
-    if (ok) {
-      for (int item = threadIdx.x; item < a.heads * span; item += blockDim.x) {
-        const int h = item / span, i = item % span;
-        const int slot = (lo + i) % cache;
-        const float* k = K + (size_t)slot * D + h * dh;
-        const float* q = sq + h * dh;
-        float acc = 0.f;
-        for (int e = 0; e < dh; ++e) {
-          const int ee = (e + i) % dh;  // rotated start: lanes hit different banks
-          acc = __fmaf_rn(q[ee], k[ee], acc);
+  const bool vec = (dh % 4) == 0 && (D % 4) == 0;
+  if (vec) {
+#pragma unroll
+    for (int e = 0; e < dh; e += 4) {
+      const float4 q4 = *reinterpret_cast<const float4*>(q + e);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (lane + 32 * k < span) {
+          const float4 k4 = *reinterpret_cast<const float4*>(K + (size_t)slot[k] * D + e);
+          sc[k] = __fmaf_rn(q4.x, k4.x, sc[k]);
+          sc[k] = __fmaf_rn(q4.y, k4.y, sc[k]);
+          sc[k] = __fmaf_rn(q4.z, k4.z, sc[k]);
+          sc[k] = __fmaf_rn(q4.w, k4.w, sc[k]);
         }
-        sc[h * cache + i] = __fmul_rn(acc, a.scale);
       }
     }
-    __syncthreads();
-    // softmax per head: one warp per head
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int h = warp; h < a.heads; h += blockDim.x >> 5) {
-      float* row = sc + h * cache;
-      float m = -3.402823466e38f;
-      for (int i = lane; i < span; i += 32) m = fmaxf(m, row[i]);
+  } else {
+    for (int e = 0; e < dh; ++e) {
+      const float qe = q[e];
 #pragma unroll
-      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      float sum = 0.f;
-      for (int i = lane; i < span; i += 32) {
-        const float e = ref_vec_exp(__fsub_rn(row[i], m));
-        row[i] = e;
-        sum = __fadd_rn(sum, e);
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-      const float inv = __fdiv_rn(1.0f, sum);
-      for (int i = lane; i < span; i += 32) row[i] = __fmul_rn(row[i], inv);
+      for (int k = 0; k < 4; ++k)
+        if (lane + 32 * k < span) sc[k] = __fmaf_rn(qe, K[(size_t)slot[k] * D + e], sc[k]);
     }
-    __syncthreads();
-    float omax = 0.f;
-    for (int e = threadIdx.x; e < D; e += blockDim.x) {
-      const int h = e / dh;
-      const float* p = sc + h * cache;
-      float o = 0.f;
-      for (int i = 0; i < span; ++i) o = __fmaf_rn(p[i], V[(size_t)((lo + i) % cache) * D + e], o);
-      a.att[(size_t)grow * D + e] = o;
-      omax = fmaxf(omax, fabsf(o));
-    }
-    omax = block_max(omax, red);
-    if (threadIdx.x == 0) a.att_rowmax[grow] = omax;
-    __syncthreads();
   }
-  // Drain a prefetch that was issued for a session this CTA does not compute (none by design:
-  // prefetches target sessions of this CTA's own walk). Nothing to wait for here.
+  float m = -3.402823466e38f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (lane + 32 * k < span) {
+      sc[k] = __fmul_rn(sc[k], a.scale);
+      m = fmaxf(m, sc[k]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float sum = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (lane + 32 * k < span) {
+      sc[k] = ref_vec_exp(__fsub_rn(sc[k], m));
+      sum = __fadd_rn(sum, sc[k]);
+    } else {
+      sc[k] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+  const float inv = __fdiv_rn(1.0f, sum);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) sc[k] = __fmul_rn(sc[k], inv);
+
+  // o[e] for e = lane, lane + 32 (dh <= 64), walking the window in order
+  float o0 = 0.f, o1 = 0.f;
+  const bool has0 = lane < dh, has1 = lane + 32 < dh;
+  int sl = lo_slot;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int n = min(32, span - 32 * k);
+#pragma unroll 16
+    for (int jj = 0; jj < n; ++jj) {
+      const float p = __shfl_sync(0xffffffffu, sc[k], jj);
+      const float* v = V + (size_t)sl * D;
+      if (has0) o0 = __fmaf_rn(p, v[lane], o0);
+      if (has1) o1 = __fmaf_rn(p, v[lane + 32], o1);
+      if (++sl == cache) sl = 0;
+    }
+  }
+  float* out = a.att + (size_t)grow * D + h * dh;
+  float om = 0.f;
+  if (has0) {
+    out[lane] = o0;
+    om = fabsf(o0);
+  }
+  if (has1) {
+    out[lane + 32] = o1;
+    om = fmaxf(om, fabsf(o1));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) om = fmaxf(om, __shfl_xor_sync(0xffffffffu, om, o));
+  if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(a.att_rowmax + grow), __float_as_uint(om));
 }
 
 // Prefill: one CTA per session; the segment's keys and values (written by the block kernel to

@@ -16,64 +16,109 @@
 // the inter-block residual blockIn += cur; cur = blockIn (stream.go:158-163).
 //
 // Every product runs on the tensor core (tcgen05.mma kind::i8, TMEM accumulators): the
-// activation rows are sliced into three int8 digit planes in shared memory by the four row warps,
-// the pre-tiled weights stream in by TMA bulk copies (warp 5) through a 4-stage ring, and warp 4
-// issues the MMAs. The epilogues (dequantization, GLU, highway, latch gate) run in the row warps
-// straight from TMEM. Prefill tiles hold whole session segments, so the latch recurrence and the
-// left-neighbour lookups stay inside the CTA.
+// activation rows are sliced into three int8 digit planes in shared memory by sixteen row warps
+// (four threads per row, each a quarter of the K bytes), the pre-tiled weights stream in by TMA
+// bulk copies (the producer warp) through a 4-stage ring, and the MMA warp issues the MMAs. The
+// epilogues run in the row warps straight from TMEM, four threads per row splitting the columns;
+// each fetches its global operands before waiting for the accumulator.
+//
+// Decode rows (one position per session) update the latch, read the left neighbour from the
+// session's norm ring and write the ring inside the W_select epilogue, each thread on its own row.
+// Prefill tiles hold whole session segments; there the latch is a scan over the segment's rows
+// (channel-parallel) and left neighbours inside the segment are rows of the same tile.
 #include "mc_engine.cuh"
 
 namespace mc {
 namespace eng {
 
-constexpr int kBlockThreads = 192;
+constexpr int kRowThreads = 512;                 // four threads per row
+constexpr int kRowWarps = kRowThreads / 32;
+constexpr int kTPR = kRowThreads / kRows;          // threads per row
+constexpr int kBlockThreads = kRowThreads + 64;  // + MMA warp + weight producer warp
+constexpr int kMmaWarp = kRowWarps;
+constexpr int kProducerWarp = kRowWarps + 1;
 constexpr int kSmemA = kASlots * kASlot;        // 144 KB
 constexpr int kSmemB = kBStages * kTile;        // 64 KB
-constexpr int kBlockSmem = kSmemA + kSmemB + 1024 /*align*/ + 1024 /*barriers, row data*/;
+constexpr int kBlockSmem = kSmemA + kSmemB + 1024 /*align*/ + 16384 /*barriers, row data*/;
 
 struct Bars {
   uint64_t a_full[kASlots], a_empty[kASlots], b_full[kBStages], b_empty[kBStages], acc_full, acc_empty;
   uint32_t tmem;
-  uint32_t rowmax_ll[kRows];  // float bits of max |left|, |latch| per row
+  float rowmax_n[kRows];               // max |norm cell| per row
+  float rowmax_part[kTPR][kRows];       // per-thread partial maxima of an epilogue output
+  float rowmax_warp[kRowWarps][kRows]; // per-warp partial maxima of the prefill scan
+  int rvalid[kRows];                   // row holds a position of an active session
+  int rtok[kRows];                     // its token (clamped to the vocabulary)
+  int rsess[kRows];                    // its session
+  int rpos[kRows];                     // its position
+  float rowmax_a[kRows];               // max |A row| of the next GEMM (x, att)
+  float rowmax_h[kRows];               // max |hidden| per row
 };
+static_assert(sizeof(Bars) <= 16384, "barrier block");
 
-__device__ __forceinline__ void row_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void row_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
-// Slices K tile kt of one activation row into the three digit planes of an A slot.
-__device__ __forceinline__ void gen_tile(uint8_t* slot, int r, const float* rowp, int K, int kt, float inv, bool valid) {
-#pragma unroll 1
-  for (int ch = 0; ch < 8; ++ch) {
-    const int k = kt * 128 + ch * 16;
-    float x[16];
-    if (valid && k + 16 <= K && ((reinterpret_cast<uintptr_t>(rowp + k) & 15) == 0)) {
-      const float4* p = reinterpret_cast<const float4*>(rowp + k);
+// 16 consecutive floats p[n0 .. n0+16) with n < lim, zeros past lim.
+__device__ __forceinline__ void ld16(const float* __restrict__ p, int n0, int lim, float (&v)[16]) {
+  if (n0 + 16 <= lim && ((reinterpret_cast<uintptr_t>(p + n0) & 15) == 0)) {
+    const float4* q = reinterpret_cast<const float4*>(p + n0);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 v = p[q];
-        x[4 * q] = v.x; x[4 * q + 1] = v.y; x[4 * q + 2] = v.z; x[4 * q + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < 16; ++e) x[e] = (valid && k + e < K) ? rowp[k + e] : 0.f;
+    for (int i = 0; i < 4; ++i) {
+      const float4 t = q[i];
+      v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
     }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) v[e] = (n0 + e < lim) ? p[n0 + e] : 0.f;
+  }
+}
+
+__device__ __forceinline__ void st16(float* __restrict__ p, int n0, int lim, const float (&v)[16]) {
+  if (n0 + 16 <= lim && ((reinterpret_cast<uintptr_t>(p + n0) & 15) == 0)) {
+    float4* q = reinterpret_cast<float4*>(p + n0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+      if (n0 + e < lim) p[n0 + e] = v[e];
+  }
+}
+
+// Slices the 16-byte chunks [ch0, ch0 + NCH) of K tile kt of one activation row into the three
+// digit planes of an A slot (row r of the 128-row tile). All loads are issued before any slicing.
+template <int NCH>
+__device__ __forceinline__ void gen_tile(uint8_t* slot, int r, const float* __restrict__ rowp, int K, int kt, float inv,
+                                         bool valid, int ch0) {
+  float x[NCH][16];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    if (valid) ld16(rowp, kt * 128 + (ch0 + c) * 16, K, x[c]);
+    else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) x[c][e] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
     uint32_t p1[4], p2[4], p3[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      Digits3 d[4];
+      uint32_t u1[4], u2[4], u3[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) d[e] = slice3(x[4 * q + e], inv);
-      p1[q] = pack4(d[0].d1, d[1].d1, d[2].d1, d[3].d1);
-      p2[q] = pack4(d[0].d2, d[1].d2, d[2].d2, d[3].d2);
-      p3[q] = pack4(d[0].d3, d[1].d3, d[2].d3, d[3].d3);
+      for (int e = 0; e < 4; ++e) slice3_bits(x[c][4 * q + e], inv, u1[e], u2[e], u3[e]);
+      p1[q] = pack_low_bytes(u1[0], u1[1], u1[2], u1[3]);
+      p2[q] = pack_low_bytes(u2[0], u2[1], u2[2], u2[3]);
+      p3[q] = pack_low_bytes(u3[0], u3[1], u3[2], u3[3]);
     }
-    const uint32_t off = sw128_offset(r, ch);
+    const uint32_t off = sw128_offset(r, ch0 + c);
     *reinterpret_cast<uint4*>(slot + off) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
     *reinterpret_cast<uint4*>(slot + kTile + off) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
     *reinterpret_cast<uint4*>(slot + 2 * kTile + off) = make_uint4(p3[0], p3[1], p3[2], p3[3]);
   }
 }
 
-// Loads 16 columns of the three slice accumulators of this thread's row.
+// Loads 16 columns of the three slice accumulators of this thread's row (warp-collective).
 __device__ __forceinline__ void load_acc16(uint32_t tmem, int warp, int col, uint32_t (&a1)[16], uint32_t (&a2)[16],
                                           uint32_t (&a3)[16]) {
   const uint32_t base = tmem_addr(tmem, 32 * (warp & 3), col);
@@ -83,22 +128,84 @@ __device__ __forceinline__ void load_acc16(uint32_t tmem, int warp, int col, uin
   tmem_wait_ld();
 }
 
-// RMSNorm of one row (nn/rmsnorm.go:14-32): out = (x * (1/rms)) * gain. Returns max |out|.
-__device__ __forceinline__ float rmsnorm_row(const float* x, const float* gain, float* out, int D) {
-  float ss = 0.f;
-  for (int d = 0; d < D; ++d) ss = __fmaf_rn(x[d], x[d], ss);
-  const float ms = __fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f);
-  const float rms = (float)sqrt((double)ms);
-  const float inv = __fdiv_rn(1.0f, rms);
-  float m = 0.f;
-  for (int d = 0; d < D; ++d) {
-    const float v = gain ? __fmul_rn(__fmul_rn(x[d], inv), gain[d]) : x[d];
-    out[d] = v;
-    m = fmaxf(m, fabsf(v));
-  }
-  return m;
+// 8 columns of the three slice accumulators (warp-collective).
+__device__ __forceinline__ void load_acc8(uint32_t tmem, int warp, int col, uint32_t (&a1)[8], uint32_t (&a2)[8],
+                                         uint32_t (&a3)[8]) {
+  const uint32_t base = tmem_addr(tmem, 32 * (warp & 3), col);
+  tmem_ld8(base, a1);
+  tmem_ld8(base + kNC, a2);
+  tmem_ld8(base + 2 * kNC, a3);
+  tmem_wait_ld();
 }
 
+__device__ __forceinline__ void ld8(const float* __restrict__ p, int n0, int lim, float (&v)[8]) {
+  if (n0 + 8 <= lim && ((reinterpret_cast<uintptr_t>(p + n0) & 15) == 0)) {
+    const float4 t0 = reinterpret_cast<const float4*>(p + n0)[0], t1 = reinterpret_cast<const float4*>(p + n0)[1];
+    v[0] = t0.x; v[1] = t0.y; v[2] = t0.z; v[3] = t0.w; v[4] = t1.x; v[5] = t1.y; v[6] = t1.z; v[7] = t1.w;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = (n0 + e < lim) ? p[n0 + e] : 0.f;
+  }
+}
+
+__device__ __forceinline__ void st8(float* __restrict__ p, int n0, int lim, const float (&v)[8]) {
+  if (n0 + 8 <= lim && ((reinterpret_cast<uintptr_t>(p + n0) & 15) == 0)) {
+    reinterpret_cast<float4*>(p + n0)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p + n0)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (n0 + e < lim) p[n0 + e] = v[e];
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ void trace_point(const BlockArgs& a, int i) {
+  if (a.trace && blockIdx.x == 0 && threadIdx.x == 0 && i < 64) a.trace[i] = global_timer_ns();
+}
+
+// Writes the three digit planes of four consecutive activations (K indices e..e+3, e % 4 == 0)
+// of tile row r into the A slot holding K tile e / 128. One 32-bit store per plane; a warp
+// writing 128 consecutive K values of a row touches every bank once.
+__device__ __forceinline__ void put4(uint8_t* sA, int r, int e, float4 v, float inv) {
+  const int kt = e >> 7, k = e & 127;
+  uint8_t* tile = sA + (kt % kASlots) * kASlot;
+  const uint32_t off = sw128_offset(r, k >> 4) + (k & 15);
+  uint32_t a0, a1, a2, a3, b0, b1, b2, b3, c0, c1, c2, c3;
+  slice3_bits(v.x, inv, a0, b0, c0);
+  slice3_bits(v.y, inv, a1, b1, c1);
+  slice3_bits(v.z, inv, a2, b2, c2);
+  slice3_bits(v.w, inv, a3, b3, c3);
+  *reinterpret_cast<uint32_t*>(tile + off) = pack_low_bytes(a0, a1, a2, a3);
+  *reinterpret_cast<uint32_t*>(tile + kTile + off) = pack_low_bytes(b0, b1, b2, b3);
+  *reinterpret_cast<uint32_t*>(tile + 2 * kTile + off) = pack_low_bytes(c0, c1, c2, c3);
+}
+
+__device__ __forceinline__ float4 ld4_or0(const float* p, int e, int K, bool valid) {
+  if (!valid || e >= K) return make_float4(0.f, 0.f, 0.f, 0.f);
+  if (e + 4 <= K) return *reinterpret_cast<const float4*>(p + e);
+  float4 v = make_float4(p[e], 0.f, 0.f, 0.f);
+  if (e + 1 < K) v.y = p[e + 1];
+  if (e + 2 < K) v.z = p[e + 2];
+  return v;
+}
+
+__device__ __forceinline__ float max4(float4 v) { return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))); }
+
+constexpr int kRowsPerWarp = kRows / kRowWarps;  // 8
+
+template <int KF>  // float4 columns per lane per row: ceil(D / 128)
 __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_constant__ BlockArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -112,7 +219,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kASlots; ++i) {
-      mbar_init(&bars->a_full[i], 128);
+      mbar_init(&bars->a_full[i], kRowThreads);
       mbar_init(&bars->a_empty[i], 1);
     }
     for (int i = 0; i < kBStages; ++i) {
@@ -120,17 +227,16 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
       mbar_init(&bars->b_empty[i], 1);
     }
     mbar_init(&bars->acc_full, 1);
-    mbar_init(&bars->acc_empty, 128);
+    mbar_init(&bars->acc_empty, kRowThreads);
     fence_barrier_init();
   }
-  if (threadIdx.x < kRows) bars->rowmax_ll[threadIdx.x] = 0u;
-  if (warp == 4) tmem_alloc(&bars->tmem, 512);
+  if (warp == kMmaWarp) tmem_alloc(&bars->tmem, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem;
 
-  if (warp == 5) {
+  if (warp == kProducerWarp) {
     // ---------------- weight-tile producer (TMA bulk copies) ----------------
     if (lane == 0) {
       uint32_t bidx = 0;
@@ -149,7 +255,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
           }
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       uint32_t bidx = 0, chunk_idx = 0;
@@ -198,38 +304,79 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
       }
     }
   } else {
-    // ---------------- row warps: activations, epilogues, row/channel phases ----------------
-    const int r = threadIdx.x;  // row in tile (TMEM lane)
+    // ---------------- row warps ----------------
+    // Two views of the 128 rows: row-owner (thread t owns TMEM lane r = t % 128 and a quarter h of
+    // the columns; used by the accumulator epilogues) and warp-per-row (warp w owns rows w + 16u,
+    // lane l the float4 columns l + 32k; used by every phase that moves rows through memory).
+    const int t = threadIdx.x;
+    const int r = t & (kRows - 1);
+    const int h = t >> 7;
     const int grow = tile * kRows + r;
     const RowInfo ri = row_info(a, grow);
+    const bool decode = a.P == 1;
+    const int nf = D / 4;
     uint32_t afill[kASlots] = {0, 0, 0};
     uint32_t chunk_idx = 0;
     bool ok = true;
-    float rowmax_n = 0.f;   // max |norm cell| of this row (current step)
-    float rowmax_h = 0.f;   // max |hidden| of this row
+    int tp = 0;
+    trace_point(a, tp++);
+    if (h == 0) {
+      bars->rvalid[r] = ri.valid ? 1 : 0;
+      int tok = 0;
+      if (ri.valid && a.embed_first) {
+        tok = a.tokens[(size_t)ri.session * a.P + ri.t];
+        if (tok < 0 || tok >= a.V) tok = 0;
+      }
+      bars->rtok[r] = tok;
+      bars->rsess[r] = ri.session;
+      bars->rpos[r] = ri.pos;
+    }
+    row_bar();
 
-    // Runs GEMM g with activation rows src (row stride ld) whose max |.| is amax; the epilogue
-    // callback receives the chunk index.
-    auto run_gemm = [&](int g, const float* src, int ld, float amax, auto&& epilogue) {
+    auto acquire = [&](int slot) {
+      if (ok && afill[slot] >= 1 && !mbar_wait_or_abort(&bars->a_empty[slot], (afill[slot] - 1) & 1, kErrWaitEmpty))
+        ok = false;
+      afill[slot]++;
+    };
+    auto publish = [&](int slot) {
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->a_full[slot]);
+    };
+    // Warp-per-row slicing of K tile kt of the rows' fp32 source (coalesced loads, all of the
+    // warp's rows in flight together) with per-row maxima rmax (shared memory).
+    auto gen_rows = [&](int kt, const float* src, int ld, int K, const float* rmax) {
+      float4 v[kRowsPerWarp];
+      const int e = kt * 128 + 4 * lane;
+#pragma unroll
+      for (int u = 0; u < kRowsPerWarp; ++u) {
+        const int rr = warp + kRowWarps * u;
+        v[u] = ld4_or0(src + (size_t)(tile * kRows + rr) * ld, e, K, bars->rvalid[rr] != 0);
+      }
+#pragma unroll
+      for (int u = 0; u < kRowsPerWarp; ++u) {
+        const int rr = warp + kRowWarps * u;
+        put4(sA, rr, e, v[u], row_inv_step(rmax[rr]));
+      }
+    };
+    // Runs GEMM g. prefilled: its (resident) A tiles were already published by a fused phase;
+    // otherwise they are sliced from src with the row maxima rmax. The epilogue gets the chunk and
+    // this thread's row step and weight scale.
+    auto run_gemm = [&](int g, bool prefilled, const float* src, int ld, const float* rmax, auto&& epilogue) {
       const GemmSpec& G = a.gemms[g];
       const bool resident = G.ktiles <= kASlots;
-      const float inv = row_inv_step(amax);
-      const float step = row_step(amax);
-      const float* rowp = src + (size_t)grow * ld;
+      const float step = row_step(rmax[r]);
       for (int c = 0; c < G.nchunks; ++c) {
-        if (c == 0 || !resident) {
+        if (!prefilled && (c == 0 || !resident)) {
           for (int kt = 0; kt < G.ktiles; ++kt) {
             const int slot = kt % kASlots;
-            if (ok && afill[slot] >= 1 &&
-                !mbar_wait_or_abort(&bars->a_empty[slot], (afill[slot] - 1) & 1, kErrWaitEmpty))
-              ok = false;
-            afill[slot]++;
-            if (ok) gen_tile(sA + slot * kASlot, r, rowp, G.K, kt, inv, ri.valid);
-            fence_proxy_async_smem();
-            mbar_arrive(&bars->a_full[slot]);
+            acquire(slot);
+            if (ok) gen_rows(kt, src, ld, G.K, rmax);
+            publish(slot);
           }
         }
+        if (a.trace && a.trace_fine) trace_point(a, tp++);
         const bool got = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&bars->acc_full, chunk_idx & 1, kErrWaitAcc));
+        if (a.trace && a.trace_fine) trace_point(a, tp++);
         if (!got) ok = false;
         if (ok) {
           tc_fence_after();
@@ -238,230 +385,417 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
         tc_fence_before();
         mbar_arrive(&bars->acc_empty);
         ++chunk_idx;
+        if (a.trace && a.trace_fine) trace_point(a, tp++);
       }
+    };
+    // Warp-per-row RMSNorm (nn/rmsnorm.go:14-32) of cur, after the embedding (mode 1) or the
+    // inter-block residual (mode 2) when asked: writes out (fp32, row stride out_ld), max |out|
+    // per row (rmax, and rmax_g in global memory if given) and, if slice, the digit planes of the
+    // normed row into the A slots of a GEMM with K = D (acquired and published here).
+    auto norm_phase = [&](int mode, const float* gain, float* out, int out_ld, float* rmax, float* rmax_g, bool slice) {
+      const int kts = (D + 127) / 128;
+      if (slice)
+        for (int kt = 0; kt < kts; ++kt) acquire(kt % kASlots);
+#pragma unroll 2
+      for (int u = 0; u < kRowsPerWarp; ++u) {
+        const int rr = warp + kRowWarps * u;
+        const int gr = tile * kRows + rr;
+        const bool v = bars->rvalid[rr] != 0;
+        float4 x[KF];
+        float4* cur4 = reinterpret_cast<float4*>(a.cur + (size_t)gr * D);
+        float4* bin4 = reinterpret_cast<float4*>(a.blockin + (size_t)gr * D);
+        if (mode == 1) {
+          const char4* e4 = reinterpret_cast<const char4*>(a.embed + (size_t)bars->rtok[rr] * D);
+#pragma unroll
+          for (int k = 0; k < KF; ++k) {
+            const int f = lane + 32 * k;
+            float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (v && f < nf) {
+              const char4 q = e4[f];
+              y = make_float4(__fmul_rn((float)q.x, a.embed_scale), __fmul_rn((float)q.y, a.embed_scale),
+                              __fmul_rn((float)q.z, a.embed_scale), __fmul_rn((float)q.w, a.embed_scale));
+              cur4[f] = y;
+              bin4[f] = y;
+            }
+            x[k] = y;
+          }
+        } else if (mode == 2) {
+          float4 c4[KF], b4[KF];
+#pragma unroll
+          for (int k = 0; k < KF; ++k) {
+            const int f = lane + 32 * k;
+            const bool in = v && f < nf;
+            c4[k] = in ? cur4[f] : make_float4(0.f, 0.f, 0.f, 0.f);
+            b4[k] = in ? bin4[f] : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int k = 0; k < KF; ++k) {
+            const int f = lane + 32 * k;
+            float4 y = make_float4(__fadd_rn(b4[k].x, c4[k].x), __fadd_rn(b4[k].y, c4[k].y), __fadd_rn(b4[k].z, c4[k].z),
+                                   __fadd_rn(b4[k].w, c4[k].w));
+            if (v && f < nf) {
+              cur4[f] = y;
+              bin4[f] = y;
+            }
+            x[k] = y;
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < KF; ++k) {
+            const int f = lane + 32 * k;
+            x[k] = (v && f < nf) ? cur4[f] : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int k = 0; k < KF; ++k) {
+          ss = __fmaf_rn(x[k].x, x[k].x, ss);
+          ss = __fmaf_rn(x[k].y, x[k].y, ss);
+          ss = __fmaf_rn(x[k].z, x[k].z, ss);
+          ss = __fmaf_rn(x[k].w, x[k].w, ss);
+        }
+        ss = warp_sum(ss);
+        float inv = 1.f;
+        if (gain) inv = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f)));
+        float m = 0.f;
+        float4* o4 = reinterpret_cast<float4*>(out + (size_t)gr * out_ld);
+#pragma unroll
+        for (int k = 0; k < KF; ++k) {
+          const int f = lane + 32 * k;
+          if (f < nf && gain) {
+            const float4 gg = reinterpret_cast<const float4*>(gain)[f];
+            x[k].x = __fmul_rn(__fmul_rn(x[k].x, inv), gg.x);
+            x[k].y = __fmul_rn(__fmul_rn(x[k].y, inv), gg.y);
+            x[k].z = __fmul_rn(__fmul_rn(x[k].z, inv), gg.z);
+            x[k].w = __fmul_rn(__fmul_rn(x[k].w, inv), gg.w);
+          }
+          if (v && f < nf) o4[f] = x[k];
+          if (f < nf) m = fmaxf(m, max4(x[k]));
+        }
+        m = v ? warp_max(m) : 0.f;
+        if (lane == 0) {
+          rmax[rr] = m;
+          if (rmax_g) rmax_g[gr] = m;
+        }
+        if (slice) {
+          const float is = row_inv_step(m);
+#pragma unroll
+          for (int k = 0; k < KF; ++k) {
+            const int f = lane + 32 * k;
+            if (f < nf) put4(sA, rr, 4 * f, x[k], is);
+          }
+        }
+      }
+      if (slice)
+        for (int kt = 0; kt < kts; ++kt) publish(kt % kASlots);
+    };
+    // max over the four threads of a row (each ran the epilogue on its columns) into rmax
+    auto row_max_quad = [&](float mine, float* rmax) {
+      bars->rowmax_part[h][r] = mine;
+      row_bar();
+      if (h == 0)
+        rmax[r] = fmaxf(fmaxf(bars->rowmax_part[0][r], bars->rowmax_part[1][r]),
+                        fmaxf(bars->rowmax_part[2][r], bars->rowmax_part[3][r]));
+      row_bar();
     };
 
     int g = 0;
     // ---- output projection of the previous block's attention: cur += Out att s_out ----
     if (a.has_out) {
-      const float amax = a.att_rowmax[grow];
-      run_gemm(g++, a.att, D, amax, [&](int c, float step, float scale) {
-        for (int j0 = 0; j0 < kNC; j0 += 16) {
+      if (h == 0) bars->rowmax_a[r] = ri.valid ? a.att_rowmax[grow] : 0.f;
+      row_bar();
+      float* cur = a.cur + (size_t)grow * D;
+      run_gemm(g++, false, a.att, D, bars->rowmax_a, [&](int c, float step, float scale) {
+        for (int j0 = h * 32; j0 < h * 32 + 32; j0 += 16) {
+          const int n0 = c * kNC + j0;
+          const bool act = ri.valid && n0 < D;
+          float v[16];
+          if (act) ld16(cur, n0, D, v);
           uint32_t a1[16], a2[16], a3[16];
           load_acc16(tmem, warp, j0, a1, a2, a3);
-          if (!ri.valid) continue;
+          if (!act) continue;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int n = c * kNC + j0 + j;
-            if (n < D) {
-              float* p = a.cur + (size_t)grow * D + n;
-              *p = __fadd_rn(*p, dequant(a1[j], a2[j], a3[j], step, scale));
-            }
-          }
+          for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], dequant(a1[j], a2[j], a3[j], step, scale));
+          st16(cur, n0, D, v);
         }
       });
       row_bar();
-    }
-    // ---- embedding (first block) or inter-block residual ----
-    if (a.embed_first || a.residual) {
-      for (int rr = 0; rr < kRows; ++rr) {
-        const int gr = tile * kRows + rr;
-        const RowInfo rj = row_info(a, gr);
-        if (!rj.valid) continue;
-        float* cur = a.cur + (size_t)gr * D;
-        float* bin = a.blockin + (size_t)gr * D;
-        if (a.embed_first) {
-          int tok = a.tokens[(size_t)rj.session * a.P + rj.t];
-          if (tok < 0 || tok >= a.V) tok = 0;
-          const int8_t* e = a.embed + (size_t)tok * D;
-          for (int d = r; d < D; d += 128) {
-            const float v = __fmul_rn((float)e[d], a.embed_scale);
-            cur[d] = v;
-            bin[d] = v;
-          }
-        } else {
-          for (int d = r; d < D; d += 128) {
-            const float v = __fadd_rn(bin[d], cur[d]);
-            bin[d] = v;
-            cur[d] = v;
-          }
-        }
-      }
-      row_bar();
+      trace_point(a, tp++);
     }
 
     // ---- rule steps ----
     for (int s = 0; s < a.nsteps; ++s) {
       const int bs = a.bs0 + s;
       const int dil = a.dil[s];
-      float* xrow = a.xbuf + (size_t)grow * 3 * D;
-      // norm cell n -> xbuf[:, 0:D]
-      if (ri.valid) {
-        rowmax_n = rmsnorm_row(a.cur + (size_t)grow * D, a.gamma, xrow, D);
-      } else {
-        rowmax_n = 0.f;
-      }
-      bars->rowmax_ll[r] = 0u;
+      // norm cell n (after the embedding / residual on the first step), sliced for W_select
+      norm_phase(s == 0 ? (a.embed_first ? 1 : (a.residual ? 2 : 0)) : 0, a.gamma, a.xbuf, 3 * D, bars->rowmax_n,
+                 nullptr, true);
       row_bar();
-      // W_select: lambda -> xbuf[:, 2D:3D]
-      run_gemm(g++, a.xbuf, 3 * D, rowmax_n, [&](int c, float step, float scale) {
-        for (int j0 = 0; j0 < kNC; j0 += 16) {
+      trace_point(a, tp++);
+      // W_select epilogue: lambda = sigmoid(dot * s_sel + base) into the latch slot of xbuf
+      float* xrow = a.xbuf + (size_t)grow * 3 * D;
+      run_gemm(g++, true, nullptr, 0, bars->rowmax_n, [&](int c, float step, float scale) {
+        for (int j0 = h * 32; j0 < h * 32 + 32; j0 += 16) {
+          const int n0 = c * kNC + j0;
+          const bool act = ri.valid && n0 < D;
+          float base[16];
+          if (act) ld16(a.latch_base, n0, D, base);
           uint32_t a1[16], a2[16], a3[16];
           load_acc16(tmem, warp, j0, a1, a2, a3);
-          if (!ri.valid) continue;
+          if (!act) continue;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int n = c * kNC + j0 + j;
-            if (n < D) {
-              const float z = __fadd_rn(dequant(a1[j], a2[j], a3[j], step, scale), a.latch_base[n]);
-              xrow[2 * D + n] = sigmoid_clamped(z);
-            }
-          }
+          for (int j = 0; j < 16; ++j)
+            base[j] = sigmoid_clamped(__fadd_rn(dequant(a1[j], a2[j], a3[j], step, scale), base[j]));
+          st16(xrow + 2 * D, n0, D, base);
         }
       });
       row_bar();
-      // latch scan and left neighbours (channel-parallel over the rows of the tile)
-      for (int d = r; d < D; d += 128) {
-        for (int slot = 0; slot < a.spt; ++slot) {
-          const int sess = tile * a.spt + slot;
-          if (sess >= a.n_sess) break;
-          const int len = a.seglen[sess];
-          if (len <= 0) continue;
-          const int p0 = a.pos0[sess];
-          float* lstate = a.latch + ((size_t)sess * a.total_steps + bs) * D + d;
-          float l = (p0 == 0) ? 0.f : *lstate;
-          const float* ring = a.norm_ring + ((size_t)sess * a.total_steps + bs) * a.ring * D + d;
-          for (int t = 0; t < len; ++t) {
-            const int gr = tile * kRows + slot * a.P + t;
-            float* x = a.xbuf + (size_t)gr * 3 * D;
-            const float lam = x[2 * D + d];
-            const float nv = x[d];
-            l = __fadd_rn(__fmul_rn(lam, l), __fmul_rn(__fsub_rn(1.0f, lam), nv));
-            x[2 * D + d] = l;
-            float left = 0.f;
-            if (t >= dil) left = a.xbuf[(size_t)(gr - dil) * 3 * D + d];
-            else if (p0 + t - dil >= 0) left = ring[(size_t)((p0 + t - dil) % a.ring) * D];
-            x[D + d] = left;
-            const float m = fmaxf(fabsf(l), fabsf(left));
-            const unsigned wm = __reduce_max_sync(__activemask(), __float_as_uint(m));
-            if (lane == 0 || (d & 31) == 0) atomicMax(&bars->rowmax_ll[slot * a.P + t], wm);
+      trace_point(a, tp++);
+      const bool w1_resident = a.gemms[g].ktiles <= kASlots;
+      bool w1_prefilled = false;
+      if (decode) {
+        // ---- decode: latch update, left neighbour, ring write; one warp per row ----
+        const bool slice = w1_resident;
+        const int kts = a.gemms[g].ktiles;
+        if (slice)
+          for (int kt = 0; kt < kts; ++kt) acquire(kt % kASlots);
+#pragma unroll 2
+        for (int u = 0; u < kRowsPerWarp; ++u) {
+          const int rr = warp + kRowWarps * u;
+          const int gr = tile * kRows + rr;
+          const bool v = bars->rvalid[rr] != 0;
+          const int pos = bars->rpos[rr];
+          const size_t so = ((size_t)bars->rsess[rr] * a.total_steps + bs);
+          const float4* x4 = reinterpret_cast<const float4*>(a.xbuf + (size_t)gr * 3 * D);
+          float4* ls4 = reinterpret_cast<float4*>(a.latch + so * D);
+          float4* ring4 = reinterpret_cast<float4*>(a.norm_ring + so * a.ring * D);
+          const int lpos = pos - dil;
+          float4 nv[KF], lam[KF], lo[KF], lf[KF];
+#pragma unroll
+          for (int k = 0; k < KF; ++k) {
+            const int f = lane + 32 * k;
+            const bool in = v && f < nf;
+            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+            nv[k] = in ? x4[f] : z;
+            lam[k] = in ? x4[2 * nf + f] : z;
+            lo[k] = (in && pos > 0) ? ls4[f] : z;
+            lf[k] = (in && lpos >= 0) ? ring4[(size_t)(lpos % a.ring) * nf + f] : z;
           }
-          *lstate = l;
+          float m = 0.f;
+#pragma unroll
+          for (int k = 0; k < KF; ++k) {
+            const int f = lane + 32 * k;
+            float4 l;
+            l.x = __fadd_rn(__fmul_rn(lam[k].x, lo[k].x), __fmul_rn(__fsub_rn(1.0f, lam[k].x), nv[k].x));
+            l.y = __fadd_rn(__fmul_rn(lam[k].y, lo[k].y), __fmul_rn(__fsub_rn(1.0f, lam[k].y), nv[k].y));
+            l.z = __fadd_rn(__fmul_rn(lam[k].z, lo[k].z), __fmul_rn(__fsub_rn(1.0f, lam[k].z), nv[k].z));
+            l.w = __fadd_rn(__fmul_rn(lam[k].w, lo[k].w), __fmul_rn(__fsub_rn(1.0f, lam[k].w), nv[k].w));
+            lo[k] = l;
+            if (v && f < nf) {
+              ls4[f] = l;
+              ring4[(size_t)(pos % a.ring) * nf + f] = nv[k];
+              if (!slice) {
+                float4* xw = reinterpret_cast<float4*>(a.xbuf + (size_t)gr * 3 * D);
+                xw[nf + f] = lf[k];
+                xw[2 * nf + f] = l;
+              }
+            }
+            if (f < nf) m = fmaxf(m, fmaxf(max4(nv[k]), fmaxf(max4(l), max4(lf[k]))));
+          }
+          m = v ? warp_max(m) : 0.f;
+          if (lane == 0) bars->rowmax_a[rr] = m;
+          if (slice) {
+            const float is = row_inv_step(m);
+#pragma unroll
+            for (int k = 0; k < KF; ++k) {
+              const int f = lane + 32 * k;
+              if (f < nf) {
+                put4(sA, rr, 4 * f, nv[k], is);
+                put4(sA, rr, D + 4 * f, lf[k], is);
+                put4(sA, rr, 2 * D + 4 * f, lo[k], is);
+              }
+            }
+          }
         }
+        if (slice) {
+          for (int kt = 0; kt < kts; ++kt) publish(kt % kASlots);
+          w1_prefilled = true;
+        }
+        row_bar();
+      } else {
+        // ---- prefill: latch scan and left neighbours, channel-parallel over segment rows ----
+        for (int i = t; i < kRowWarps * kRows; i += kRowThreads) (&bars->rowmax_warp[0][0])[i] = 0.f;
+        row_bar();
+        for (int d = t; d < ((D + 31) & ~31); d += kRowThreads) {
+          const bool act = d < D;
+          for (int slot = 0; slot < a.spt; ++slot) {
+            const int sess = tile * a.spt + slot;
+            if (sess >= a.n_sess) break;
+            const int len = a.seglen[sess];
+            if (len <= 0) continue;
+            const int p0 = a.pos0[sess];
+            const size_t st_off = ((size_t)sess * a.total_steps + bs);
+            float l = (p0 == 0 || !act) ? 0.f : a.latch[st_off * D + d];
+            const float* rg = a.norm_ring + st_off * a.ring * D + d;
+            const int row0 = tile * kRows + slot * a.P;
+            for (int tt = 0; tt < len; ++tt) {
+              float* x = a.xbuf + (size_t)(row0 + tt) * 3 * D;
+              float nv = 0.f, left = 0.f;
+              if (act) {
+                const float lam = x[2 * D + d];
+                nv = x[d];
+                if (tt >= dil) left = a.xbuf[(size_t)(row0 + tt - dil) * 3 * D + d];
+                else if (p0 + tt - dil >= 0) left = rg[(size_t)((p0 + tt - dil) % a.ring) * D];
+                l = __fadd_rn(__fmul_rn(lam, l), __fmul_rn(__fsub_rn(1.0f, lam), nv));
+                x[2 * D + d] = l;
+                x[D + d] = left;
+              }
+              const float m = warp_max(act ? fmaxf(fabsf(nv), fmaxf(fabsf(l), fabsf(left))) : 0.f);
+              if (lane == 0) {
+                float* pm = &bars->rowmax_warp[warp][slot * a.P + tt];
+                *pm = fmaxf(*pm, m);
+              }
+            }
+            if (act) a.latch[st_off * D + d] = l;
+          }
+        }
+        row_bar();
+        for (int d = t; d < D; d += kRowThreads)
+          for (int slot = 0; slot < a.spt; ++slot) {
+            const int sess = tile * a.spt + slot;
+            if (sess >= a.n_sess) break;
+            const int len = a.seglen[sess];
+            const int p0 = a.pos0[sess];
+            float* rg = a.norm_ring + ((size_t)sess * a.total_steps + bs) * a.ring * D + d;
+            for (int tt = max(0, len - a.ring); tt < len; ++tt)
+              rg[(size_t)((p0 + tt) % a.ring) * D] = a.xbuf[(size_t)(tile * kRows + slot * a.P + tt) * 3 * D + d];
+          }
+        if (h == 0) {
+          float m = 0.f;
+          for (int w = 0; w < kRowWarps; ++w) m = fmaxf(m, bars->rowmax_warp[w][r]);
+          bars->rowmax_a[r] = m;
+        }
+        row_bar();
       }
-      row_bar();
-      // norm ring: the last `ring` positions of each segment
-      for (int d = r; d < D; d += 128)
-        for (int slot = 0; slot < a.spt; ++slot) {
-          const int sess = tile * a.spt + slot;
-          if (sess >= a.n_sess) break;
-          const int len = a.seglen[sess];
-          const int p0 = a.pos0[sess];
-          for (int t = max(0, len - a.ring); t < len; ++t) {
-            const int gr = tile * kRows + slot * a.P + t;
-            a.norm_ring[(((size_t)sess * a.total_steps + bs) * a.ring + (size_t)((p0 + t) % a.ring)) * D + d] =
-                a.xbuf[(size_t)gr * 3 * D + d];
+      trace_point(a, tp++);
+      // W1 + GLU -> hidden (fp32 rows in hbuf), per-thread max |hidden|
+      float hmax = 0.f;
+      float* hrow = a.hbuf + (size_t)grow * H;
+      run_gemm(g++, w1_prefilled, a.xbuf, 3 * D, bars->rowmax_a, [&](int c, float step, float scale) {
+        for (int j0 = h * 16; j0 < h * 16 + 16; j0 += 8) {  // this thread's 16 of the chunk's 64 hidden units
+          const int u0 = c * kHalfChunk + j0;
+          const bool act = ri.valid && u0 < H;
+          float bv[8], bg[8], hid[8];
+          if (act) {
+            ld8(a.b1, u0, H, bv);
+            ld8(a.b1 + H, u0, H, bg);
           }
-        }
-      // W1 + GLU -> hbuf
-      const float xmax = fmaxf(rowmax_n, __uint_as_float(bars->rowmax_ll[r]));
-      rowmax_h = 0.f;
-      run_gemm(g++, a.xbuf, 3 * D, xmax, [&](int c, float step, float scale) {
-        const int h0 = c * kHalfChunk;
-        for (int j0 = 0; j0 < kHalfChunk; j0 += 16) {
-          uint32_t v1[16], v2[16], v3[16], g1[16], g2[16], g3[16];
-          load_acc16(tmem, warp, j0, v1, v2, v3);
-          load_acc16(tmem, warp, kHalfChunk + j0, g1, g2, g3);
-          if (!ri.valid) continue;
+          uint32_t x1[8], x2[8], x3[8];
+          load_acc8(tmem, warp, j0, x1, x2, x3);  // value columns
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int h = h0 + j0 + j;
-            if (h < H) {
-              const float v = __fadd_rn(dequant(v1[j], v2[j], v3[j], step, scale), a.b1[h]);
-              const float gt = __fadd_rn(dequant(g1[j], g2[j], g3[j], step, scale), a.b1[H + h]);
-              const float hid = __fmul_rn(v, sigmoid_clamped(gt));
-              a.hbuf[(size_t)grow * H + h] = hid;
-              rowmax_h = fmaxf(rowmax_h, fabsf(hid));
+          for (int j = 0; j < 8; ++j) hid[j] = __fadd_rn(dequant(x1[j], x2[j], x3[j], step, scale), bv[j]);
+          load_acc8(tmem, warp, kHalfChunk + j0, x1, x2, x3);  // gate columns
+          if (act) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float gt = __fadd_rn(dequant(x1[j], x2[j], x3[j], step, scale), bg[j]);
+              hid[j] = __fmul_rn(hid[j], sigmoid_clamped(gt));
+              if (u0 + j < H) hmax = fmaxf(hmax, fabsf(hid[j]));
             }
+            st8(hrow, u0, H, hid);
           }
         }
       });
+      row_max_quad(hmax, bars->rowmax_h);
+      trace_point(a, tp++);
       // W2 + highway -> cur
-      run_gemm(g++, a.hbuf, H, rowmax_h, [&](int c, float step, float scale) {
-        const int d0 = c * kHalfChunk;
-        for (int j0 = 0; j0 < kHalfChunk; j0 += 16) {
-          uint32_t o1[16], o2[16], o3[16], q1[16], q2[16], q3[16];
-          load_acc16(tmem, warp, j0, o1, o2, o3);
-          load_acc16(tmem, warp, kHalfChunk + j0, q1, q2, q3);
-          if (!ri.valid) continue;
+      float* crow = a.cur + (size_t)grow * D;
+      run_gemm(g++, false, a.hbuf, H, bars->rowmax_h, [&](int c, float step, float scale) {
+        for (int j0 = h * 16; j0 < h * 16 + 16; j0 += 8) {  // this thread's 16 of the chunk's 64 state channels
+          const int d0 = c * kHalfChunk + j0;
+          const bool act = ri.valid && d0 < D;
+          float bd[8], bg[8], cv[8], od[8];
+          if (act) {
+            ld8(a.b2, d0, D, bd);
+            ld8(a.b2 + D, d0, D, bg);
+            ld8(crow, d0, D, cv);
+          }
+          uint32_t x1[8], x2[8], x3[8];
+          load_acc8(tmem, warp, j0, x1, x2, x3);  // delta columns
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int d = d0 + j0 + j;
-            if (d < D) {
-              const float od = __fadd_rn(dequant(o1[j], o2[j], o3[j], step, scale), a.b2[d]);
-              const float og = __fadd_rn(dequant(q1[j], q2[j], q3[j], step, scale), a.b2[D + d]);
+          for (int j = 0; j < 8; ++j) od[j] = __fadd_rn(dequant(x1[j], x2[j], x3[j], step, scale), bd[j]);
+          load_acc8(tmem, warp, kHalfChunk + j0, x1, x2, x3);  // gate columns
+          if (act) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float og = __fadd_rn(dequant(x1[j], x2[j], x3[j], step, scale), bg[j]);
               const float gate = sigmoid_clamped(og);
-              float* cp = a.cur + (size_t)grow * D + d;
-              *cp = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, gate), *cp), __fmul_rn(gate, od));
+              cv[j] = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, gate), cv[j]), __fmul_rn(gate, od[j]));
             }
+            st8(crow, d0, D, cv);
           }
         }
       });
       row_bar();
+      trace_point(a, tp++);
     }
 
-    // ---- attention sublayer: norm + QKV, keys/values into the ring ----
+    // ---- attention sublayer: norm (sliced for QKV) + QKV, keys/values into the ring ----
     if (a.has_attn) {
-      float* nrow = a.xbuf + (size_t)grow * 3 * D;
-      float amax = 0.f;
-      if (ri.valid) amax = rmsnorm_row(a.cur + (size_t)grow * D, a.attn_norm, nrow, D);
+      norm_phase(a.nsteps == 0 ? (a.embed_first ? 1 : (a.residual ? 2 : 0)) : 0, a.attn_norm, a.xbuf, 3 * D,
+                 bars->rowmax_n, nullptr, true);
+      if (h == 0 && ri.valid) a.att_rowmax[grow] = 0.f;  // the attention kernel max-accumulates it
       row_bar();
+      trace_point(a, tp++);
       float* kvs = a.kv + ((size_t)ri.session * a.n_attn + a.attn_slot) * 2 * (size_t)a.cache * D;
       const bool to_ring = ri.valid && ri.t >= ri.len - a.cache;
-      const int rslot = ri.pos % a.cache;
+      float* kring = kvs + (size_t)(ri.pos % a.cache) * D;
+      float* vring = kring + (size_t)a.cache * D;
       float* lin = a.kvlin ? a.kvlin + ((size_t)ri.session * a.P + ri.t) * 2 * D : nullptr;
-      run_gemm(g++, a.xbuf, 3 * D, amax, [&](int c, float step, float scale) {
-        for (int j0 = 0; j0 < kNC; j0 += 16) {
+      float* qrow = a.qbuf + (size_t)grow * D;
+      run_gemm(g++, true, nullptr, 0, bars->rowmax_n, [&](int c, float step, float scale) {
+        for (int j0 = h * 32; j0 < h * 32 + 32; j0 += 16) {
           uint32_t a1[16], a2[16], a3[16];
           load_acc16(tmem, warp, j0, a1, a2, a3);
-          if (!ri.valid) continue;
+          const int n0 = c * kNC + j0;
+          if (!ri.valid || n0 >= 3 * D) continue;
+          float v[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int n = c * kNC + j0 + j;
-            if (n >= 3 * D) continue;
-            const float v = dequant(a1[j], a2[j], a3[j], step, scale);
-            if (n < D) {
-              a.qbuf[(size_t)grow * D + n] = v;
-            } else {
-              const int which = n < 2 * D ? 0 : 1;
-              const int e = n - D - which * D;
-              if (to_ring) kvs[((size_t)which * a.cache + rslot) * D + e] = v;
-              if (lin) lin[which * D + e] = v;
+          for (int j = 0; j < 16; ++j) v[j] = dequant(a1[j], a2[j], a3[j], step, scale);
+          const int part = n0 / D;
+          if (n0 + 16 <= 3 * D && (n0 + 15) / D == part) {
+            const int e0 = n0 - part * D;
+            if (part == 0) st16(qrow, e0, D, v);
+            else {
+              if (to_ring) st16(part == 1 ? kring : vring, e0, D, v);
+              if (lin) st16(lin + (part - 1) * D, e0, D, v);
+            }
+          } else {
+            for (int j = 0; j < 16; ++j) {
+              const int n = n0 + j;
+              if (n >= 3 * D) break;
+              const int p = n / D, e = n - p * D;
+              if (p == 0) qrow[e] = v[j];
+              else {
+                if (to_ring) (p == 1 ? kring : vring)[e] = v[j];
+                if (lin) lin[(p - 1) * D + e] = v[j];
+              }
             }
           }
         }
       });
+      trace_point(a, tp++);
     }
 
     // ---- final RMSNorm (the head's input) ----
     if (a.final_norm) {
-      float m = 0.f;
-      if (ri.valid) {
-        if (a.final_gain) m = rmsnorm_row(a.cur + (size_t)grow * D, a.final_gain, a.fnorm + (size_t)grow * D, D);
-        else {
-          for (int d = 0; d < D; ++d) {
-            const float v = a.cur[(size_t)grow * D + d];
-            a.fnorm[(size_t)grow * D + d] = v;
-            m = fmaxf(m, fabsf(v));
-          }
-        }
-      }
-      a.fnorm_rowmax[grow] = m;
+      norm_phase(a.nsteps == 0 && !a.has_attn ? (a.embed_first ? 1 : (a.residual ? 2 : 0)) : 0, a.final_gain, a.fnorm,
+                 D, bars->rowmax_n, a.fnorm_rowmax, false);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) tmem_dealloc(tmem, 512);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
 }
 
 }  // namespace eng

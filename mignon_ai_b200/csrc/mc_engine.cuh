@@ -66,14 +66,23 @@ struct BlockArgs {
   float* fnorm;      // [rows][D] final-norm output (final kernel)
   float* fnorm_rowmax;
   float* kvlin;      // [S][P][2][D] keys and values of a prefill segment
+  unsigned long long* trace;  // optional phase timestamps of CTA 0 (null: off)
+  int trace_fine;             // also time every chunk of every GEMM
 };
 
-// sigmoidClamped (internal/quant/stream.go:128-136): exp in double, rounded to float32.
+// sigmoidClamped (internal/quant/stream.go:128-136): saturated beyond |x| > 15, else 1/(1+e^-x)
+// with float32 add and divide. The reference rounds a float64 exp to float32; CUDA's expf is
+// within 2 ulp of that, well inside the logit tolerance.
 __device__ __forceinline__ float sigmoid_clamped(float x) {
   if (x > 15.0f) return 1.0f;
   if (x < -15.0f) return 0.0f;
-  const float e = (float)exp(-(double)x);
-  return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+  return __frcp_rn(__fadd_rn(1.0f, expf(-x)));  // correctly rounded, as 1/x
+}
+
+// Three slice accumulators recombined in float32: a1 + (a2 + a3/254)/254 (two fused steps).
+__device__ __forceinline__ float combine3f(uint32_t a1, uint32_t a2, uint32_t a3) {
+  const float inv = 1.0f / 254.0f;
+  return __fmaf_rn(__fmaf_rn((float)(int)a3, inv, (float)(int)a2), inv, (float)(int)a1);
 }
 
 // One lane of the reference's vectorised exp (internal/kernels/vec_amd64.s:282-431, the
@@ -98,7 +107,7 @@ __device__ __forceinline__ float ref_vec_exp(float x) {
 // The slice-accumulator dot product of one output, scaled like MatVecInt8 (int8.go:37-40):
 // y = dot * scale (+ bias), each operation rounded.
 __device__ __forceinline__ float dequant(uint32_t a1, uint32_t a2, uint32_t a3, float step, float scale) {
-  const float dot = (float)(combine3((int)a1, (int)a2, (int)a3) * (double)step);
+  const float dot = __fmul_rn(combine3f(a1, a2, a3), step);
   return __fmul_rn(dot, scale);
 }
 

@@ -9,6 +9,7 @@
 // Prefill runs the same kernels layer-major over whole prompt segments (attn_prefill_kernel).
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -225,6 +226,7 @@ struct DevBatch {
   float4* part = nullptr;
   float* topv = nullptr;
   int32_t* topi = nullptr;
+  unsigned long long* trace = nullptr;  // phase timestamps of CTA 0 per block-kernel launch (debug)
   int32_t* out_tok = nullptr;
   float* out_prob = nullptr;
   double* out_logprob = nullptr;
@@ -270,9 +272,10 @@ static std::mutex g_attr_mu;
 static int ensure_attrs(int device) {
   std::lock_guard<std::mutex> lk(g_attr_mu);
   if (device < 64 && g_attr_done[device]) return kOk;
-  MC_CUDA(cudaFuncSetAttribute(block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
+  MC_CUDA(cudaFuncSetAttribute(block_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
+  MC_CUDA(cudaFuncSetAttribute(block_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
+  MC_CUDA(cudaFuncSetAttribute(block_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
   MC_CUDA(cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem));
-  MC_CUDA(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
   MC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
   if (device < 64) g_attr_done[device] = true;
   return kOk;
@@ -294,7 +297,8 @@ int batch_create(DevModel* m, int S, int window, int pmax, int topk, std::unique
   b->rows = tiles * 128;
   // vocabulary splits: enough CTAs to cover the SMs
   const int mtiles = (S + 127) / 128;
-  const int want = std::max(1, std::min({16, m->head.nchunks, (296 + mtiles - 1) / mtiles}));
+  // at most 16 chunks per CTA (the head kernel stages their biases in shared memory), at most 16 splits
+  const int want = std::max((m->head.nchunks + 15) / 16, std::min({16, m->head.nchunks, (296 + mtiles - 1) / mtiles}));
   const int cps = (m->head.nchunks + want - 1) / want;
   b->nsplit = (m->head.nchunks + cps - 1) / cps;  // every split gets at least one chunk
   MC_CUDA(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
@@ -312,9 +316,9 @@ int batch_create(DevModel* m, int S, int window, int pmax, int topk, std::unique
       (st = b->alloc(b->att_rowmax, R * 4)) || (st = b->alloc(b->fnorm, R * D * 4)) || (st = b->alloc(b->fnorm_rowmax, R * 4)))
     return st;
   if (m->n_attn > 0 && (st = b->alloc(b->kvlin, (size_t)S * b->pmax * 2 * D * 4))) return st;
-  if ((st = b->alloc(b->part, (size_t)S * b->nsplit * sizeof(float4)))) return st;
-  if (topk > 0 && ((st = b->alloc(b->topv, (size_t)S * b->nsplit * topk * 4)) ||
-                   (st = b->alloc(b->topi, (size_t)S * b->nsplit * topk * 4))))
+  if ((st = b->alloc(b->part, (size_t)S * b->nsplit * 4 * sizeof(float4)))) return st;
+  if (topk > 0 && ((st = b->alloc(b->topv, (size_t)S * b->nsplit * 4 * topk * 4)) ||
+                   (st = b->alloc(b->topi, (size_t)S * b->nsplit * 4 * topk * 4))))
     return st;
   MC_CUDA(cudaMemsetAsync(b->pos, 0, S * 4, b->stream));
   MC_CUDA(cudaMemsetAsync(b->seglen, 0, S * 4, b->stream));
@@ -377,9 +381,6 @@ static GemmSpec spec(const DevGemm& g, int type, int step) {
   return s;
 }
 
-static size_t attn_decode_smem(const DevModel& m, int nbuf) {
-  return (size_t)nbuf * 2 * m.cache * m.D * 4 + (size_t)m.D * 4 + (size_t)m.heads * m.cache * 4 + 32 * 4 + 16 + 128;
-}
 
 // Launch profiler: when set, an event is recorded after every launch with the launch's kind
 // (0 block, 1 attention, 2 final block, 3 head, 4 select, 5 step counter).
@@ -462,7 +463,13 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
       a.final_norm = 1;
     }
     a.ngemms = g;
-    block_kernel<<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a);
+    a.trace = b.trace ? b.trace + 64 * bi : nullptr;
+    a.trace_fine = getenv("MC_TRACE_FINE") != nullptr;
+    switch ((m.D + 127) / 128) {
+      case 1: block_kernel<1><<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
+      case 2: block_kernel<2><<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
+      default: block_kernel<3><<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
+    }
     MC_CUDA(cudaGetLastError());
     if (log) log->record(s, final_k ? 2 : 0);
     if (!final_k && m.blocks[bi].attn_slot >= 0) {
@@ -487,9 +494,14 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
       aa.att_rowmax = b.att_rowmax;
       aa.scale = (float)(1.0 / std::sqrt((double)aa.dh));
       if (P == 1) {
-        const int nbuf = attn_decode_smem(m, 2) <= 200 * 1024 ? 2 : 1;
-        const int grid = std::min(b.S, 148 * (nbuf == 2 ? 1 : 1));
-        attn_decode_kernel<<<grid, kAttnThreads, attn_decode_smem(m, nbuf), s>>>(aa, nbuf);
+        const long long warps = (long long)b.S * m.heads;
+        const int grid = (int)((warps * 32 + kAttnThreads - 1) / kAttnThreads);
+        switch (aa.dh) {
+          case 32: attn_decode_kernel<32><<<grid, kAttnThreads, 0, s>>>(aa); break;
+          case 48: attn_decode_kernel<48><<<grid, kAttnThreads, 0, s>>>(aa); break;
+          case 64: attn_decode_kernel<64><<<grid, kAttnThreads, 0, s>>>(aa); break;
+          default: attn_decode_kernel<0><<<grid, kAttnThreads, 0, s>>>(aa); break;
+        }
       } else {
         const size_t smem = (size_t)P * 2 * m.D * 4 + 32 * 4 + 16 + 128;
         if (smem > 220 * 1024) return set_error(kUnsupported, "prefill segment too long for the attention kernel");
@@ -527,7 +539,7 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
   SelectArgs sa;
   memset(&sa, 0, sizeof(sa));
   sa.n_sess = b.S;
-  sa.nsplit = b.nsplit;
+  sa.nsplit = b.nsplit * 4;  // partials per session: splits x column quarters
   sa.topk = b.topk;
   sa.mode = mode;
   sa.inv_temp = inv_temp;

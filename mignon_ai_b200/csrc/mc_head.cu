@@ -36,16 +36,27 @@ struct HeadArgs {
   int32_t* topi;
 };
 
-constexpr int kHeadThreads = 192;
+constexpr int kHeadRowThreads = 512;  // four threads per row, each a quarter of every chunk's columns
+constexpr int kHeadRowWarps = kHeadRowThreads / 32;
+constexpr int kHeadThreads = kHeadRowThreads + 64;
+constexpr int kHeadMmaWarp = kHeadRowWarps, kHeadProducerWarp = kHeadRowWarps + 1;
 constexpr int kHeadSmemA = kASlots * kASlot;
 constexpr int kHeadSmemB = kBStages * kTile;
-constexpr int kHeadSmem = kHeadSmemA + kHeadSmemB + 2048;
+constexpr int kHeadMaxBias = 16 * 128;  // biases of at most 16 chunks per CTA
+constexpr int kHeadSmem = kHeadSmemA + kHeadSmemB + 1024 + 12288;
 
 struct HeadBars {
   uint64_t a_full, b_full[kBStages], b_empty[kBStages], acc_full, acc_empty;
   uint32_t tmem;
+  int rrow[kRows];
+  int rvalid[kRows];
+  float rmax[kRows];
+  float bias[kHeadMaxBias];
 };
+static_assert(sizeof(HeadBars) <= 12288, "head barrier block");
 
+// Partials: per session, nsplit x 4 entries (split, column quarter), each (max, sum exp(l - max),
+// first argmax as int bits, target logit or 0); top-k lists likewise per (split, quarter).
 __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_constant__ HeadArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -57,22 +68,22 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
   const int c0 = split * a.cps, c1 = min(c0 + a.cps, a.nchunks);
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->a_full, 128);
+    mbar_init(&bars->a_full, kHeadRowThreads);
     for (int i = 0; i < kBStages; ++i) {
       mbar_init(&bars->b_full[i], 1);
       mbar_init(&bars->b_empty[i], 1);
     }
     mbar_init(&bars->acc_full, 1);
-    mbar_init(&bars->acc_empty, 128);
+    mbar_init(&bars->acc_empty, kHeadRowThreads);
     fence_barrier_init();
   }
-  if (warp == 4) tmem_alloc(&bars->tmem, 512);
+  if (warp == kHeadMmaWarp) tmem_alloc(&bars->tmem, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem;
 
-  if (warp == 5) {
+  if (warp == kHeadProducerWarp) {
     if (lane == 0) {
       uint32_t bidx = 0;
       for (int c = c0; c < c1; ++c)
@@ -85,7 +96,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         }
     producer_done:;
     }
-  } else if (warp == 4) {
+  } else if (warp == kHeadMmaWarp) {
     if (lane == 0) {
       const uint32_t idesc = idesc_i8(kRows, kNC);
       uint32_t bidx = 0;
@@ -116,29 +127,51 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
       }
     }
   } else {
-    const int r = threadIdx.x;
+    const int t = threadIdx.x;
+    const int r = t & (kRows - 1), h = t >> 7;
     const int s = mtile * kRows + r;
     const bool valid = s < a.n_sess;
-    const int grow = valid ? a.rowmap[s] : 0;
-    const float amax = valid ? a.fnorm_rowmax[grow] : 0.f;
-    const float inv = row_inv_step(amax), step = row_step(amax);
-    const float* rowp = a.fnorm + (size_t)grow * a.D;
+    if (h == 0) {
+      const int gr = valid ? a.rowmap[s] : 0;
+      bars->rrow[r] = gr;
+      bars->rvalid[r] = valid ? 1 : 0;
+      bars->rmax[r] = valid ? a.fnorm_rowmax[gr] : 0.f;
+    }
+    for (int i = t; i < (c1 - c0) * kNC && i < kHeadMaxBias; i += kHeadRowThreads) {
+      const int v = c0 * kNC + i;
+      bars->bias[i] = v < a.V ? a.head_b[v] : 0.f;
+    }
+    asm volatile("bar.sync 1, 512;" ::: "memory");
+    // operand: the final-normed rows, sliced warp-per-row (all rows of a warp in flight together)
     for (int kt = 0; kt < a.ktiles; ++kt) {
-      // gen_tile is defined in the block kernel's translation unit (same library TU).
-      gen_tile(sA + kt * kASlot, r, rowp, a.D, kt, inv, valid);
+      float4 v[kRows / kHeadRowWarps];
+      const int e = kt * 128 + 4 * lane;
+#pragma unroll
+      for (int u = 0; u < kRows / kHeadRowWarps; ++u) {
+        const int rr = warp + kHeadRowWarps * u;
+        v[u] = ld4_or0(a.fnorm + (size_t)bars->rrow[rr] * a.D, e, a.D, bars->rvalid[rr] != 0);
+      }
+#pragma unroll
+      for (int u = 0; u < kRows / kHeadRowWarps; ++u) {
+        const int rr = warp + kHeadRowWarps * u;
+        put4(sA, rr, e, v[u], row_inv_step(bars->rmax[rr]));
+      }
     }
     fence_proxy_async_smem();
     mbar_arrive(&bars->a_full);
 
+    const float step = row_step(bars->rmax[r]);
     float m = -INFINITY, sum = 0.f, lt = 0.f;
     int idx = 0;
     const int tgt = (valid && a.target) ? a.target[s] : -1;
+    const int pi = split * 4 + h;  // this thread's partial
+    const int npart = a.nsplit * 4;
     float* tv = nullptr;
     int32_t* ti = nullptr;
     float thresh = -INFINITY;
     if (valid && a.topk > 0) {
-      tv = a.topv + ((size_t)s * a.nsplit + split) * a.topk;
-      ti = a.topi + ((size_t)s * a.nsplit + split) * a.topk;
+      tv = a.topv + ((size_t)s * npart + pi) * a.topk;
+      ti = a.topi + ((size_t)s * npart + pi) * a.topk;
       for (int i = 0; i < a.topk; ++i) {
         tv[i] = -INFINITY;
         ti[i] = 0x7fffffff;
@@ -151,26 +184,38 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
       if (!got) ok = false;
       if (ok) {
         tc_fence_after();
-        for (int j0 = 0; j0 < kNC; j0 += 16) {
+        for (int j0 = h * 32; j0 < h * 32 + 32; j0 += 16) {
           uint32_t a1[16], a2[16], a3[16];
           load_acc16(tmem, warp, j0, a1, a2, a3);
           if (!valid) continue;
-#pragma unroll 4
-          for (int j = 0; j < 16; ++j) {
-            const int v = c * kNC + j0 + j;
-            if (v >= a.V) break;
-            const float l = __fadd_rn(dequant(a1[j], a2[j], a3[j], step, a.scale), a.head_b[v]);
-            if (a.logits_out) a.logits_out[(size_t)s * a.V + v] = l;
-            if (l > m) {
-              sum = __fmaf_rn(sum, expf(m - l), 1.0f);
-              m = l;
-              idx = v;
-            } else {
-              sum = __fadd_rn(sum, expf(l - m));
+          float l16[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            l16[j] = __fadd_rn(dequant(a1[j], a2[j], a3[j], step, a.scale), bars->bias[ci * kNC + j0 + j]);
+          const int v0 = c * kNC + j0;
+          if (a.logits_out) st16(a.logits_out + (size_t)s * a.V, v0, a.V, l16);
+          // chunk-local max first, then one rescale of the running sum
+          float cm = -INFINITY;
+          int ci2 = 0;
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (v0 + j < a.V && l16[j] > cm) {
+              cm = l16[j];
+              ci2 = v0 + j;
             }
-            if (v == tgt) lt = l;
-            if (tv && l > thresh) {
-              // insert into the descending list (ties keep the lower index first)
+          if (cm > m) {
+            sum = __fmul_rn(sum, expf(m - cm));
+            m = cm;
+            idx = ci2;
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (v0 + j < a.V) sum = __fadd_rn(sum, expf(l16[j] - m));
+          if (tgt >= v0 && tgt < v0 + 16) lt = l16[tgt - v0];
+          if (tv) {
+            for (int j = 0; j < 16; ++j) {
+              const float l = l16[j];
+              if (v0 + j >= a.V || !(l > thresh)) continue;
               int i = a.topk - 1;
               while (i > 0 && tv[i - 1] < l) {
                 tv[i] = tv[i - 1];
@@ -178,7 +223,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                 --i;
               }
               tv[i] = l;
-              ti[i] = v;
+              ti[i] = v0 + j;
               thresh = tv[a.topk - 1];
             }
           }
@@ -187,11 +232,11 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
       tc_fence_before();
       mbar_arrive(&bars->acc_empty);
     }
-    if (valid) a.part[(size_t)s * a.nsplit + split] = make_float4(m, sum, __int_as_float(idx), lt);
+    if (valid) a.part[(size_t)s * npart + pi] = make_float4(m, sum, __int_as_float(idx), lt);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) tmem_dealloc(tmem, 512);
+  if (warp == kHeadMmaWarp) tmem_dealloc(tmem, 512);
 }
 
 struct SelectArgs {
@@ -263,7 +308,7 @@ __global__ void select_kernel(const SelectArgs a) {
   int tok = idx;
   if (a.mode == 1 && a.topk > 1) {
     // Merge the split lists: repeatedly take the largest remaining (lowest index on ties).
-    int head[16];
+    int head[64];
     for (int k = 0; k < a.nsplit; ++k) head[k] = 0;
     float cv[kMaxTopK];
     int ci[kMaxTopK];

@@ -211,6 +211,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // TMEM address of (lane, column) relative to an allocation base.
@@ -252,6 +258,27 @@ __device__ __forceinline__ Digits3 slice3(float x, float inv_step) {
 }
 
 // The step of the first digit plane for a row whose largest magnitude is m, and its inverse.
+// slice3 with the digits left in the low byte of float bit patterns, ready to pack: adding
+// 1.5 * 2^23 to |v| < 2^22 rounds v to the nearest integer (ties to even, as rintf) and leaves it,
+// two's complement, in the low mantissa bits. Same digits as slice3.
+__device__ __forceinline__ void slice3_bits(float x, float inv, uint32_t& u1, uint32_t& u2, uint32_t& u3) {
+  const float M = 12582912.0f;
+  const float q = __fmul_rn(x, inv);
+  const float s1 = __fadd_rn(q, M);
+  const float t2 = __fmul_rn(__fsub_rn(q, __fsub_rn(s1, M)), kDigitBase);
+  const float s2 = __fadd_rn(t2, M);
+  const float t3 = __fmul_rn(__fsub_rn(t2, __fsub_rn(s2, M)), kDigitBase);
+  const float s3 = __fadd_rn(t3, M);
+  u1 = __float_as_uint(s1);
+  u2 = __float_as_uint(s2);
+  u3 = __float_as_uint(s3);
+}
+
+// Packs the low bytes of a, b, c, d into one word (a in the lowest byte).
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
 // Rows whose largest magnitude is below 1e-30 are treated as zero rows (their inverse step would
 // overflow float32).
 __device__ __forceinline__ float row_step(float m) { return m >= 1e-30f ? m * (1.0f / 127.0f) : 0.f; }
