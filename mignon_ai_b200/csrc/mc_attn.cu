@@ -7,9 +7,8 @@
 // The output o (and max |o| of each row, the scale of its digit slicing) feeds the block kernel
 // that applies the output projection.
 //
-// Decode is bound by reading the rings from HBM: each CTA walks its sessions, staging the
-// session's key and value rings into shared memory with TMA bulk copies (one per ring, the
-// slots [0, min(pos+1, cache)) are contiguous) while it computes on the previous session.
+// Decode is bound by reading the rings from HBM; each (session, head) warp streams its head's
+// contiguous key and value windows with many loads in flight.
 #include "mc_engine.cuh"
 
 namespace mc {
@@ -46,10 +45,12 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return m;
 }
 
-// Decode: one warp per (session, head), P == 1. Lane i computes the scores of window positions
-// lo+i, lo+i+32, ... (keys read straight from the ring in HBM, 16-byte loads); the softmax runs on
-// warp shuffles; then the lanes own head dimensions and walk the window's values (coalesced rows).
-// max |o| of the row is max-accumulated into att_rowmax (zeroed by the block kernel).
+// Decode: one warp per (session, head), P == 1. The rings are head-major ([K|V][head][slot][dh]),
+// so the warp streams two contiguous regions. Lane i computes the scores of window positions
+// lo+i, lo+i+32, ... (its key rows, 16-byte loads, all issued before the dot products); the
+// softmax runs on warp shuffles; then the lanes own head dimensions and walk the window's value
+// rows sixteen at a time (loads issued before the multiply-adds). max |o| of the row is
+// max-accumulated into att_rowmax (zeroed by the block kernel).
 template <int DH>  // head width known at compile time (0: taken from the arguments)
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
   const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
@@ -64,7 +65,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   const int span = pos - lo + 1;  // <= cache <= 128
   const int lo_slot = lo % cache;
   const int grow = grow_of(a, s, 0);
-  const float* K = a.kv + ((size_t)s * a.n_attn + a.attn_slot) * 2 * (size_t)cache * D + h * dh;
+  const float* K = a.kv + ((size_t)s * a.n_attn + a.attn_slot) * 2 * (size_t)cache * D + (size_t)h * cache * dh;
   const float* V = K + (size_t)cache * D;
   const float* q = a.qbuf + (size_t)grow * D + h * dh;
 
@@ -72,34 +73,40 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   int slot[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int i = lane + 32 * k;
-    int sl = lo_slot + i;
+    int sl = lo_slot + lane + 32 * k;
+    if (sl >= cache) sl -= cache;
     if (sl >= cache) sl -= cache;
     slot[k] = sl;
     sc[k] = 0.f;
   }
-  const bool vec = (dh % 4) == 0 && (D % 4) == 0;
-  if (vec) {
+  if constexpr (DH > 0) {
+    float4 q4[DH / 4];
 #pragma unroll
-    for (int e = 0; e < dh; e += 4) {
-      const float4 q4 = *reinterpret_cast<const float4*>(q + e);
+    for (int f = 0; f < DH / 4; ++f) q4[f] = reinterpret_cast<const float4*>(q)[f];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if (lane + 32 * k < span) {
-          const float4 k4 = *reinterpret_cast<const float4*>(K + (size_t)slot[k] * D + e);
-          sc[k] = __fmaf_rn(q4.x, k4.x, sc[k]);
-          sc[k] = __fmaf_rn(q4.y, k4.y, sc[k]);
-          sc[k] = __fmaf_rn(q4.z, k4.z, sc[k]);
-          sc[k] = __fmaf_rn(q4.w, k4.w, sc[k]);
-        }
+    for (int k = 0; k < 4; ++k) {
+      if (32 * k >= span) break;  // warp-uniform
+      const bool act = lane + 32 * k < span;
+      const float4* row = reinterpret_cast<const float4*>(K + (size_t)slot[k] * DH);
+      float4 k4[DH / 4];
+#pragma unroll
+      for (int f = 0; f < DH / 4; ++f) k4[f] = act ? row[f] : make_float4(0.f, 0.f, 0.f, 0.f);
+      float acc = 0.f;
+#pragma unroll
+      for (int f = 0; f < DH / 4; ++f) {
+        acc = __fmaf_rn(q4[f].x, k4[f].x, acc);
+        acc = __fmaf_rn(q4[f].y, k4[f].y, acc);
+        acc = __fmaf_rn(q4[f].z, k4[f].z, acc);
+        acc = __fmaf_rn(q4[f].w, k4[f].w, acc);
       }
+      sc[k] = acc;
     }
   } else {
     for (int e = 0; e < dh; ++e) {
       const float qe = q[e];
 #pragma unroll
       for (int k = 0; k < 4; ++k)
-        if (lane + 32 * k < span) sc[k] = __fmaf_rn(qe, K[(size_t)slot[k] * D + e], sc[k]);
+        if (lane + 32 * k < span) sc[k] = __fmaf_rn(qe, K[(size_t)slot[k] * dh + e], sc[k]);
     }
   }
   float m = -3.402823466e38f;
@@ -128,20 +135,34 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 #pragma unroll
   for (int k = 0; k < 4; ++k) sc[k] = __fmul_rn(sc[k], inv);
 
-  // o[e] for e = lane, lane + 32 (dh <= 64), walking the window in order
+  // o[e] for e = lane, lane + 32 (dh <= 64), the window in order, sixteen value rows at a time
   float o0 = 0.f, o1 = 0.f;
   const bool has0 = lane < dh, has1 = lane + 32 < dh;
-  int sl = lo_slot;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int n = min(32, span - 32 * k);
-#pragma unroll 16
-    for (int jj = 0; jj < n; ++jj) {
-      const float p = __shfl_sync(0xffffffffu, sc[k], jj);
-      const float* v = V + (size_t)sl * D;
-      if (has0) o0 = __fmaf_rn(p, v[lane], o0);
-      if (has1) o1 = __fmaf_rn(p, v[lane + 32], o1);
-      if (++sl == cache) sl = 0;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int j0 = 32 * k + 16 * half;
+      if (j0 >= span) break;  // warp-uniform
+      float v0[16], v1[16];
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        int sl = lo_slot + j0 + jj;
+        if (sl >= cache) sl -= cache;
+        if (sl >= cache) sl -= cache;
+        const bool in = j0 + jj < span;
+        const float* vr = V + (size_t)sl * dh;
+        v0[jj] = (in && has0) ? vr[lane] : 0.f;
+        v1[jj] = (in && has1) ? vr[lane + 32] : 0.f;
+      }
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        const float p = __shfl_sync(0xffffffffu, sc[k], 16 * half + jj);
+        if (j0 + jj < span) {
+          o0 = __fmaf_rn(p, v0[jj], o0);
+          o1 = __fmaf_rn(p, v1[jj], o1);
+        }
+      }
     }
   }
   float* out = a.att + (size_t)grow * D + h * dh;

@@ -747,12 +747,17 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
       if (h == 0 && ri.valid) a.att_rowmax[grow] = 0.f;  // the attention kernel max-accumulates it
       row_bar();
       trace_point(a, tp++);
+      // key/value rings, head-major: [K|V][head][slot][dh] (each head's window is contiguous)
       float* kvs = a.kv + ((size_t)ri.session * a.n_attn + a.attn_slot) * 2 * (size_t)a.cache * D;
       const bool to_ring = ri.valid && ri.t >= ri.len - a.cache;
-      float* kring = kvs + (size_t)(ri.pos % a.cache) * D;
-      float* vring = kring + (size_t)a.cache * D;
+      const int rslot = ri.pos % a.cache;
+      const int dh = a.dh;
       float* lin = a.kvlin ? a.kvlin + ((size_t)ri.session * a.P + ri.t) * 2 * D : nullptr;
       float* qrow = a.qbuf + (size_t)grow * D;
+      auto ring_at = [&](int which, int e) {  // element e (< D) of the key (0) or value (1)
+        const int hh = e / dh;
+        return kvs + (size_t)which * a.cache * D + ((size_t)hh * a.cache + rslot) * dh + (e - hh * dh);
+      };
       run_gemm(g++, true, nullptr, 0, bars->rowmax_n, [&](int c, float step, float scale) {
         for (int j0 = h * 32; j0 < h * 32 + 32; j0 += 16) {
           uint32_t a1[16], a2[16], a3[16];
@@ -763,11 +768,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = dequant(a1[j], a2[j], a3[j], step, scale);
           const int part = n0 / D;
-          if (n0 + 16 <= 3 * D && (n0 + 15) / D == part) {
-            const int e0 = n0 - part * D;
+          const int e0 = n0 - part * D;
+          if (n0 + 16 <= 3 * D && (n0 + 15) / D == part && (part == 0 || (e0 % dh) + 16 <= dh)) {
             if (part == 0) st16(qrow, e0, D, v);
             else {
-              if (to_ring) st16(part == 1 ? kring : vring, e0, D, v);
+              if (to_ring) st16(ring_at(part - 1, e0), 0, 16, v);
               if (lin) st16(lin + (part - 1) * D, e0, D, v);
             }
           } else {
@@ -777,7 +782,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
               const int p = n / D, e = n - p * D;
               if (p == 0) qrow[e] = v[j];
               else {
-                if (to_ring) (p == 1 ? kring : vring)[e] = v[j];
+                if (to_ring) *ring_at(p - 1, e) = v[j];
                 if (lin) lin[(p - 1) * D + e] = v[j];
               }
             }

@@ -40,7 +40,7 @@ struct BlockArgs {
   int block, nsteps, bs0, ring, total_steps;
   int dil[kMaxSteps];
   int embed_first, residual, has_out, has_attn, final_norm;
-  int attn_slot, n_attn, cache, window;
+  int attn_slot, n_attn, cache, window, dh;
   int ngemms;
   GemmSpec gemms[kMaxGemms];
   const int8_t* embed;

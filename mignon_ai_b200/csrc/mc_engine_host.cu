@@ -350,6 +350,7 @@ static void fill_common(const DevBatch& b, BlockArgs& a, int P) {
   a.n_attn = m.n_attn;
   a.cache = m.cache;
   a.window = m.window;
+  a.dh = m.heads > 0 ? m.D / m.heads : 0;
   a.embed = m.embed;
   a.embed_scale = m.embed_scale;
   a.latch_base = m.latch_base;
