@@ -55,6 +55,17 @@ int mc_gemm_i8_dev(const int8_t* a, const int8_t* w, int m, int n, int k, const 
 int mc_gemm_f32a_dev(const float* x, const int8_t* w, int m, int n, int k, float w_scale, const float* bias,
                      float* y, int32_t* slices, float* row_max_scratch, void* stream);
 
+/* mc_gemm_f32a_dev without any device allocation, for callers that cannot allocate GPU memory
+ * (a host runtime limited to buffers it registered in advance, a fixed memory budget, or work
+ * issued during CUDA graph capture, where cudaMalloc is not allowed). It has no counterpart in the
+ * reference. Its only scratch, one float per activation row, is a fixed device array of 65536
+ * entries (256 KB, held by every GPU that loads the library until exit): m above 65536 fails
+ * with MC_INVALID_ARGUMENT. The first call on each device looks up that array's device address
+ * (no allocation); make it before any stream capture. All calls share the array; calls that
+ * overlap on the GPU race on it and must be serialized by the caller. */
+int mc_gemm_f32a_noalloc_dev(const float* x, const int8_t* w, int m, int n, int k, float w_scale, const float* bias,
+                             float* y, void* stream);
+
 /* Host-pointer form of mc_gemm_i8_dev: copies in, runs on `device`, copies out. */
 int mc_gemm_i8(int device, const int8_t* a, const int8_t* w, int m, int n, int k, const float* row_scale,
                const float* col_scale, const float* bias, int32_t* c_i32, float* y);

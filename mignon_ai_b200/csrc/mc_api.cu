@@ -16,6 +16,8 @@ int gemm_i8_launch(const int8_t* a, const int8_t* w, int M, int N, int K, const 
                    const float* col_scale, const float* bias, int32_t* c_i32, float* y, cudaStream_t stream);
 int gemm_f32a_launch(const float* a, const int8_t* w, int M, int N, int K, float w_scale, const float* bias,
                      float* y, int32_t* slices, float* row_max_scratch, cudaStream_t stream);
+int gemm_f32a_noalloc_launch(const float* a, const int8_t* w, int M, int N, int K, float w_scale, const float* bias,
+                             float* y, cudaStream_t stream);
 
 // Device buffer released when the scope ends.
 struct DevBuf {
@@ -442,6 +444,13 @@ int mc_gemm_f32a_dev(const float* x, const int8_t* w, int m, int n, int k, float
   clear_error();
   if (!x || !w || !y || !row_max_scratch) return set_error(kInvalidArgument, "mc_gemm_f32a_dev: null pointer");
   return gemm_f32a_launch(x, w, m, n, k, w_scale, bias, y, slices, row_max_scratch, (cudaStream_t)stream);
+}
+
+int mc_gemm_f32a_noalloc_dev(const float* x, const int8_t* w, int m, int n, int k, float w_scale, const float* bias,
+                             float* y, void* stream) {
+  clear_error();
+  if (!x || !w || !y) return set_error(kInvalidArgument, "mc_gemm_f32a_noalloc_dev: null pointer");
+  return gemm_f32a_noalloc_launch(x, w, m, n, k, w_scale, bias, y, (cudaStream_t)stream);
 }
 
 int mc_gemm_i8(int device, const int8_t* a, const int8_t* w, int m, int n, int k, const float* row_scale,

@@ -12,6 +12,9 @@
 //    activation row is sliced into three int8 digit planes (mc_sm100.cuh: slice3) by the
 //    row-owning warps while the weights stream in by TMA; three MMAs per K step accumulate the
 //    planes into three exact s32 accumulators that the epilogue recombines.
+#include <mutex>
+#include <string>
+
 #include "mc_host.h"
 #include "mc_sm100.cuh"
 
@@ -360,6 +363,54 @@ int gemm_f32a_launch(const float* a, const int8_t* w, int M, int N, int K, float
   gemm::gemm_f32a_kernel<<<grid, 160, gemm::kFSmem, stream>>>(mw, args);
   MC_CUDA(cudaGetLastError());
   return kOk;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Allocation-free form of the float32-activation GEMM
+// ------------------------------------------------------------------------------------------------
+// Some callers cannot allocate device memory: a host runtime that may only pass buffers it
+// registered in advance, a service whose GPU memory is budgeted once at start-up, or code issuing
+// work while a CUDA graph is being captured (cudaMalloc is not allowed there). For them, the one
+// scratch buffer this GEMM needs, the largest magnitude of every activation row (one float per
+// row), lives in this fixed device array. Every GPU that loads the library holds it (256 KB)
+// until the process exits.
+constexpr int kNoAllocMaxRows = 65536;
+static __device__ __align__(256) float g_noalloc_row_max[kNoAllocMaxRows];
+
+// Device address of the array on the current device. Host code may not pass the array's name to
+// a kernel (on the host it is only a stand-in), so the address is looked up once per device with
+// that device current, and cached.
+static int noalloc_row_max(float** out) {
+  static std::mutex mu;
+  static float* addr[64] = {nullptr};
+  int dev = 0;
+  MC_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(kUnsupported, "device ordinal above 63");
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_row_max);
+    if (e != cudaSuccess)
+      return set_error(kCudaError, std::string("cudaGetSymbolAddress(g_noalloc_row_max): ") + cudaGetErrorString(e));
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return kOk;
+}
+
+// The float32-activation GEMM with its row-maximum scratch in g_noalloc_row_max: allocates
+// nothing. Rows above kNoAllocMaxRows are rejected. All calls share the array, which keeps the
+// last call's values; each call rewrites every entry it reads before reading it, so nothing needs
+// clearing, but calls that overlap on the GPU race on it and must be serialized by the caller.
+int gemm_f32a_noalloc_launch(const float* a, const int8_t* w, int M, int N, int K, float w_scale, const float* bias,
+                             float* y, cudaStream_t stream) {
+  if (M > kNoAllocMaxRows)
+    return set_error(kInvalidArgument, "gemm_f32a_noalloc: m = " + std::to_string(M) + " is above the fixed maximum of " +
+                                           std::to_string(kNoAllocMaxRows) + " rows");
+  float* row_max = nullptr;
+  const int st = noalloc_row_max(&row_max);
+  if (st != kOk) return st;
+  return gemm_f32a_launch(a, w, M, N, K, w_scale, bias, y, nullptr, row_max, stream);
 }
 
 }  // namespace mc
