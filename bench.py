@@ -34,6 +34,9 @@ PROMPT = 48
 NEW = 80
 PROMPT_SEED = 2
 METRIC = "generated tokens/s, batched INT8 sessions"
+# DRAM bytes (read + write) per session of one attn_decode_kernel launch, from an ncu capture of
+# the 1024-session case (58.63 MB / 1024); traffic grows with the session count.
+ATTN_DRAM_BYTES_PER_SESSION = 57256
 UNIT = "tokens/s"
 
 
@@ -52,6 +55,21 @@ def prompts_for(rank, sessions):
     # rows of the Philox prompt stream are global session ids
     allp = synth.prompts_uniform_fast((rank + 1) * sessions, PROMPT, synth.CONFIGS[CONFIG].vocab, PROMPT_SEED)
     return np.ascontiguousarray(allp[rank * sessions:(rank + 1) * sessions])
+
+
+def session_range(rank, sessions):
+    """Global session ids [first, end) of a rank: weak scaling, `sessions` per rank, by index."""
+    return rank * sessions, (rank + 1) * sessions
+
+
+def max_over_ranks(ms, dist, device):
+    """The slowest rank's time (every rank calls this, in the same order)."""
+    if dist is None:
+        return float(ms)
+    import torch
+    t = torch.tensor([float(ms)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 class ClockSampler:
@@ -194,7 +212,7 @@ def main():
     d_lens = torch.from_numpy(lens).to(dev)
     d_tok = torch.zeros((S, NEW), dtype=torch.int32, device=dev)
     d_prob = torch.zeros((S, NEW), dtype=torch.float32, device=dev)
-    session0 = rank * S
+    session0 = session_range(rank, S)[0]
 
     def job():
         _lib.check(L.mc_generate_dev(batch._h, d_prompts.data_ptr(), d_lens.data_ptr(), PROMPT, PROMPT, NEW, 0.0,
@@ -227,11 +245,8 @@ def main():
     t_end.record(stream)
     _lib.check(L.mc_batch_error(batch._h))
     torch.cuda.synchronize(dev)
-    ms = t_start.elapsed_time(t_end)
+    ms = max_over_ranks(t_start.elapsed_time(t_end), dist, dev)
     if dist:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
         dist.barrier()
     clk = clocks.stop() if clocks else None
     tokens_per_step = S * NEW * world
@@ -261,11 +276,7 @@ def main():
         e2e_job()
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    ems = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([ems], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ems = float(t.item())
+    ems = max_over_ranks(e0.elapsed_time(e1), dist, dev)
     e2e_value = tokens_per_step * e_steps / (ems / 1000.0)
     same = bool(np.array_equal(h_tok, d_tok.cpu().numpy()))
 
@@ -315,7 +326,9 @@ def main():
             "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel", "achieved": achieved, "peak": hbm_peak,
                          "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s",
-                         "traffic": None,
+                         "traffic": ATTN_DRAM_BYTES_PER_SESSION * S,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at 1024 "
+                                           "sessions, scaled by sessions (profiles/attn_decode_kernel_1024sessions.md)",
                          "algorithmic_bytes_per_launch": attn_bytes, "avg_launch_ms": attn_ms},
             "decode_step_profile": {"ms_total": float(step_ms), "share": shares,
                                     "ms_per_kind": {names.get(k, str(k)): float(np.mean(v)) for k, v in per_kind.items()}},
