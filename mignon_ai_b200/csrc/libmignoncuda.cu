@@ -4,6 +4,7 @@
 #include "mc_gemm.cu"
 #include "mc_modelfile.cu"
 #include "mc_block.cu"
+#include "mc_block_decode.cu"
 #include "mc_attn.cu"
 #include "mc_head.cu"
 #include "mc_engine_host.cu"

@@ -1,0 +1,604 @@
+// The decode block kernel: one CTA advances 32 sessions by one position through one CA block.
+//
+// The arithmetic is block_kernel's (mc_block.cu) for one position per session, operation for
+// operation, with the roles of the GEMM operands swapped. The weights are the MMA's M side (128
+// output channels per tile) and the sessions its N side (32 per CTA), so a batch of S sessions
+// spreads over S/32 CTAs (128 CTAs for 4096 sessions, against 32 CTAs of 128 rows). One M-tile's
+// three digit-plane accumulators take 3 x 32 TMEM columns, so four tiles are in flight while the
+// epilogue drains earlier ones. Each epilogue thread owns one output channel (TMEM lane) and
+// eight sessions (TMEM columns). The GLU value/gate (W1) and highway delta/gate (W2) halves come
+// from two consecutive M-tiles: their weight images hold 128 value rows, then the 128 matching
+// gate rows. The sessions' rows (cur, the norm cell, the latch gate, the hidden layer) stay in
+// shared memory for the whole block; only the session state (latch, norm ring, key/value ring)
+// and the rows handed to the next kernel go through global memory.
+//
+// Roles: 16 row warps (row phases: one warp per session row; epilogues: thread = channel), one
+// MMA warp (one elected thread issues tcgen05.mma), one producer warp (bulk copies of the
+// pre-tiled weight tiles through a 6-stage ring). All mbarrier waits are bounded.
+#include "mc_engine.cuh"
+
+namespace mc {
+namespace eng {
+
+constexpr int kDR = 32;                          // sessions per CTA (MMA N)
+constexpr int kDRowWarps = 16;
+constexpr int kDRowThreads = kDRowWarps * 32;
+constexpr int kDThreads = kDRowThreads + 64;     // + MMA warp + producer warp
+constexpr int kDMmaWarp = kDRowWarps;
+constexpr int kDProducerWarp = kDRowWarps + 1;
+constexpr int kDWStages = 6;                     // weight-tile ring (16 KB tiles)
+constexpr int kDSlots = 4;                       // TMEM accumulator slots
+constexpr int kDSlotCols = 128;                  // three planes of kDR columns each, padded
+constexpr int kDBTile = kDR * 128;               // one digit plane of one K tile of the sessions (4 KB)
+constexpr int kDRowsPerWarp = kDR / kDRowWarps;  // 2
+constexpr int kDCols = kDR / 4;                  // sessions per epilogue thread (8)
+
+struct DBars {
+  uint64_t w_full[kDWStages], w_empty[kDWStages], s_full[kDSlots], s_empty[kDSlots], b_full;
+  uint32_t tmem;
+  int valid[kDR], tok[kDR], pos[kDR];
+  float rstep[kDR];  // step of each session row of the current GEMM's activation planes
+};
+
+constexpr size_t kDecodeSmemMax = 227 * 1024;  // the per-block opt-in limit of sm_100
+
+// Dynamic shared memory of the decode kernel for state width D, hidden width H and kt K tiles of
+// activation planes (kt = ceil(max(3D, H) / 128)).
+inline size_t decode_smem_bytes(int D, int H, int kt) {
+  return 1024 + (size_t)kDWStages * kTile + (size_t)3 * kt * kDBTile + (size_t)4 * kDR * (2 * D + (D > H ? D : H)) +
+         sizeof(DBars);
+}
+
+__device__ __forceinline__ void row_bar_d() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+
+__device__ __forceinline__ float warp_sum_d(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max_d(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float max4_d(float4 v) {
+  return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+}
+
+// The three digit planes of four consecutive activations (K indices e..e+3, e % 4 == 0) of
+// session row r, written into the plane tiles of K tile e / 128 (one 32-bit store per plane).
+__device__ __forceinline__ void put_planes(uint8_t* sB, int KT, int r, int e, float4 v, float inv) {
+  uint8_t* tile = sB + (e >> 7) * kDBTile;
+  const int k = e & 127;
+  const uint32_t off = sw128_offset(r, k >> 4) + (k & 15);
+  uint32_t a0, a1, a2, a3, b0, b1, b2, b3, c0, c1, c2, c3;
+  slice3_bits(v.x, inv, a0, b0, c0);
+  slice3_bits(v.y, inv, a1, b1, c1);
+  slice3_bits(v.z, inv, a2, b2, c2);
+  slice3_bits(v.w, inv, a3, b3, c3);
+  *reinterpret_cast<uint32_t*>(tile + off) = pack_low_bytes(a0, a1, a2, a3);
+  *reinterpret_cast<uint32_t*>(tile + KT * kDBTile + off) = pack_low_bytes(b0, b1, b2, b3);
+  *reinterpret_cast<uint32_t*>(tile + 2 * KT * kDBTile + off) = pack_low_bytes(c0, c1, c2, c3);
+}
+
+template <int KF>  // float4 columns per lane of a state row: ceil(D / 128)
+__global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid_constant__ BlockArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int D = a.D, H = a.H, KT = a.dec_kt;
+  const int DH = D > H ? D : H;
+  uint8_t* sW = smem;
+  uint8_t* sB = sW + kDWStages * kTile;
+  float* sCur = reinterpret_cast<float*>(sB + 3 * KT * kDBTile);  // [kDR][D]
+  float* sNrm = sCur + kDR * D;                                    // [kDR][D] norm cell
+  float* sAux = sNrm + kDR * D;                                    // [kDR][D] latch gate, then [kDR][H] hidden
+  DBars* bars = reinterpret_cast<DBars*>(sAux + kDR * DH);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int s0 = blockIdx.x * kDR;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kDWStages; ++i) {
+      mbar_init(&bars->w_full[i], 1);
+      mbar_init(&bars->w_empty[i], 1);
+    }
+    for (int i = 0; i < kDSlots; ++i) {
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->s_empty[i], kDRowWarps);
+    }
+    mbar_init(&bars->b_full, kDRowThreads);
+    fence_barrier_init();
+  }
+  if (warp == kDMmaWarp) tmem_alloc(&bars->tmem, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem;
+
+  if (warp == kDProducerWarp) {
+    // ---------------- weight tiles, in the order the MMA warp consumes them ----------------
+    if (lane == 0) {
+      uint32_t widx = 0;
+      bool ok = true;
+      for (int g = 0; g < a.ngemms && ok; ++g) {
+        const GemmSpec& G = a.gemms[g];
+        for (int c = 0; c < G.nchunks && ok; ++c)
+          for (int kt = 0; kt < G.ktiles; ++kt, ++widx) {
+            const int st = widx % kDWStages;
+            if (widx >= kDWStages &&
+                !mbar_wait_or_abort(&bars->w_empty[st], ((widx / kDWStages) - 1) & 1, kErrWaitEmpty)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&bars->w_full[st], kTile);
+            bulk_load(sW + st * kTile, G.tiles + ((size_t)c * G.ktiles + kt) * kTile, kTile, &bars->w_full[st]);
+          }
+      }
+    }
+  } else if (warp == kDMmaWarp) {
+    // ---------------- MMA issuer: D[channel][session] += W[channel][k] * X[session][k] ----------------
+    if (lane == 0) {
+      uint32_t widx = 0, sidx = 0;
+      const uint32_t idesc = idesc_i8(128, kDR);
+      bool ok = true;
+      for (int g = 0; g < a.ngemms && ok; ++g) {
+        const GemmSpec& G = a.gemms[g];
+        if (!mbar_wait_or_abort(&bars->b_full, g & 1, kErrWaitFull)) break;
+        tc_fence_after();
+        for (int c = 0; c < G.nchunks && ok; ++c, ++sidx) {
+          const int slot = sidx % kDSlots;
+          if (sidx >= kDSlots &&
+              !mbar_wait_or_abort(&bars->s_empty[slot], ((sidx / kDSlots) - 1) & 1, kErrWaitAccFree)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int kt = 0; kt < G.ktiles; ++kt, ++widx) {
+            const int st = widx % kDWStages;
+            if (!mbar_wait_or_abort(&bars->w_full[st], (widx / kDWStages) & 1, kErrWaitFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t da = smem_desc_sw128(sW + st * kTile);
+            const int ksteps = min(4, (G.K - kt * 128 + 31) / 32);
+#pragma unroll
+            for (int p = 0; p < 3; ++p) {
+              const uint64_t db = smem_desc_sw128(sB + (p * KT + kt) * kDBTile);
+              for (int kk = 0; kk < ksteps; ++kk)
+                mma_i8(tmem + slot * kDSlotCols + p * kDR, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+            }
+            mma_commit(&bars->w_empty[st]);
+          }
+          if (!ok) break;
+          mma_commit(&bars->s_full[slot]);
+        }
+      }
+    }
+  } else {
+    // ---------------- row warps ----------------
+    const int t = threadIdx.x;
+    const int chl = 32 * (warp & 3) + lane;  // channel within an M-tile = TMEM lane
+    const int r0 = kDCols * (warp >> 2);      // first of this thread's epilogue sessions = TMEM column
+    const int nf = D / 4;
+    uint32_t sidx = 0;
+    bool ok = true;
+    if (t < kDR) {
+      const int s = s0 + t;
+      const bool v = s < a.n_sess && a.seglen[s] > 0;
+      bars->valid[t] = v ? 1 : 0;
+      bars->pos[t] = v ? a.pos0[s] : 0;
+      int tok = 0;
+      if (v && a.embed_first) {
+        tok = a.tokens[s];
+        if (tok < 0 || tok >= a.V) tok = 0;
+      }
+      bars->tok[t] = tok;
+    }
+    row_bar_d();
+
+    auto publish = [&]() {
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->b_full);
+      row_bar_d();
+    };
+    auto wait_slot = [&](int slot, uint32_t k) {
+      const bool got =
+          __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&bars->s_full[slot], (k / kDSlots) & 1, kErrWaitAcc));
+      if (!got) ok = false;
+      tc_fence_after();
+    };
+    auto release_slot = [&](int slot) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->s_empty[slot]);
+    };
+    auto acc8 = [&](int slot, uint32_t(&x1)[8], uint32_t(&x2)[8], uint32_t(&x3)[8]) {
+      const uint32_t base = tmem_addr(tmem, 32 * (warp & 3), slot * kDSlotCols + r0);
+      tmem_ld8(base, x1);
+      tmem_ld8(base + kDR, x2);
+      tmem_ld8(base + 2 * kDR, x3);
+      tmem_wait_ld();
+    };
+    auto load_steps = [&](float(&stp)[kDCols]) {
+#pragma unroll
+      for (int j = 0; j < kDCols; ++j) stp[j] = bars->rstep[r0 + j];
+    };
+    // The M-tiles of one GEMM, one accumulator each: fn(tile, steps, planes).
+    auto tiles1 = [&](const GemmSpec& G, auto&& fn) {
+      float stp[kDCols];
+      load_steps(stp);
+      for (int c = 0; c < G.nchunks; ++c, ++sidx) {
+        const int slot = sidx % kDSlots;
+        wait_slot(slot, sidx);
+        uint32_t x1[8], x2[8], x3[8];
+        acc8(slot, x1, x2, x3);
+        release_slot(slot);
+        fn(c, stp, x1, x2, x3);
+      }
+    };
+    // Pairs of M-tiles (value/delta tile, gate tile): fn(pair, steps, value planes, gate planes).
+    auto tiles2 = [&](const GemmSpec& G, auto&& fn) {
+      float stp[kDCols];
+      load_steps(stp);
+      for (int c = 0; c + 1 < G.nchunks; c += 2, sidx += 2) {
+        const int sv = sidx % kDSlots, sg = (sidx + 1) % kDSlots;
+        uint32_t v1[8], v2[8], v3[8], g1[8], g2[8], g3[8];
+        wait_slot(sv, sidx);
+        acc8(sv, v1, v2, v3);
+        wait_slot(sg, sidx + 1);
+        acc8(sg, g1, g2, g3);
+        release_slot(sv);
+        release_slot(sg);
+        fn(c / 2, stp, v1, v2, v3, g1, g2, g3);
+      }
+    };
+    // RMSNorm (nn/rmsnorm.go:14-32) of the cur rows with gain `gain` (null: identity, no norm).
+    // Writes the result to `out` (shared or global rows of stride D; null: none), max |y| of the
+    // row to rmax_g (global, if given), and if slice its digit planes as the next GEMM's input.
+    auto norm_rows = [&](const float* gain, float* out, bool out_global, float* rmax_g, bool slice) {
+#pragma unroll
+      for (int u = 0; u < kDRowsPerWarp; ++u) {
+        const int rr = warp + kDRowWarps * u;
+        const int s = s0 + rr;
+        const bool v = bars->valid[rr] != 0;
+        float4 x[KF];
+        const float4* c4 = reinterpret_cast<const float4*>(sCur + rr * D);
+#pragma unroll
+        for (int k = 0; k < KF; ++k) {
+          const int f = lane + 32 * k;
+          x[k] = (v && f < nf) ? c4[f] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int k = 0; k < KF; ++k) {
+          ss = __fmaf_rn(x[k].x, x[k].x, ss);
+          ss = __fmaf_rn(x[k].y, x[k].y, ss);
+          ss = __fmaf_rn(x[k].z, x[k].z, ss);
+          ss = __fmaf_rn(x[k].w, x[k].w, ss);
+        }
+        ss = warp_sum_d(ss);
+        float inv = 1.f;
+        if (gain) inv = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f)));
+        float m = 0.f;
+        float4* o4 = out ? reinterpret_cast<float4*>(out + (size_t)(out_global ? s : rr) * D) : nullptr;
+#pragma unroll
+        for (int k = 0; k < KF; ++k) {
+          const int f = lane + 32 * k;
+          if (f < nf && gain) {
+            const float4 gg = reinterpret_cast<const float4*>(gain)[f];
+            x[k].x = __fmul_rn(__fmul_rn(x[k].x, inv), gg.x);
+            x[k].y = __fmul_rn(__fmul_rn(x[k].y, inv), gg.y);
+            x[k].z = __fmul_rn(__fmul_rn(x[k].z, inv), gg.z);
+            x[k].w = __fmul_rn(__fmul_rn(x[k].w, inv), gg.w);
+          }
+          if (o4 && f < nf && (v || !out_global)) o4[f] = x[k];
+          if (f < nf) m = fmaxf(m, max4_d(x[k]));
+        }
+        m = v ? warp_max_d(m) : 0.f;
+        if (lane == 0) {
+          bars->rstep[rr] = row_step(m);
+          if (rmax_g && s < a.n_sess) rmax_g[s] = m;
+        }
+        if (slice) {
+          const float is = row_inv_step(m);
+#pragma unroll
+          for (int k = 0; k < KF; ++k) {
+            const int f = lane + 32 * k;
+            if (f < nf) put_planes(sB, KT, rr, 4 * f, x[k], is);
+          }
+        }
+      }
+    };
+
+    int gi = 0;
+    // ---- the sessions' cur rows: the token embedding (block 0) or the previous block's output ----
+#pragma unroll
+    for (int u = 0; u < kDRowsPerWarp; ++u) {
+      const int rr = warp + kDRowWarps * u;
+      const int s = s0 + rr;
+      const bool v = bars->valid[rr] != 0;
+      float4* c4 = reinterpret_cast<float4*>(sCur + rr * D);
+      const char4* e4 = reinterpret_cast<const char4*>(a.embed + (size_t)bars->tok[rr] * D);
+      const float4* g4 = reinterpret_cast<const float4*>(a.cur + (size_t)s * D);
+#pragma unroll
+      for (int k = 0; k < KF; ++k) {
+        const int f = lane + 32 * k;
+        if (f >= nf) continue;
+        float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (v) {
+          if (a.embed_first) {
+            const char4 q = e4[f];
+            y = make_float4(__fmul_rn((float)q.x, a.embed_scale), __fmul_rn((float)q.y, a.embed_scale),
+                            __fmul_rn((float)q.z, a.embed_scale), __fmul_rn((float)q.w, a.embed_scale));
+            reinterpret_cast<float4*>(a.blockin + (size_t)s * D)[f] = y;
+          } else {
+            y = g4[f];
+          }
+        }
+        c4[f] = y;
+      }
+    }
+
+    // ---- output projection of the previous block's attention: cur += Out att s_out ----
+    if (a.has_out) {
+#pragma unroll
+      for (int u = 0; u < kDRowsPerWarp; ++u) {
+        const int rr = warp + kDRowWarps * u;
+        const int s = s0 + rr;
+        const bool v = bars->valid[rr] != 0;
+        const float m = v ? a.att_rowmax[s] : 0.f;
+        const float is = row_inv_step(m);
+        if (lane == 0) bars->rstep[rr] = row_step(m);
+        const float4* a4 = reinterpret_cast<const float4*>(a.att + (size_t)s * D);
+#pragma unroll
+        for (int k = 0; k < KF; ++k) {
+          const int f = lane + 32 * k;
+          if (f < nf) put_planes(sB, KT, rr, 4 * f, v ? a4[f] : make_float4(0.f, 0.f, 0.f, 0.f), is);
+        }
+      }
+      publish();
+      tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[8], uint32_t(&x2)[8],
+                                uint32_t(&x3)[8]) {
+        const int n = c * 128 + chl;
+        if (n >= D) return;
+#pragma unroll
+        for (int j = 0; j < kDCols; ++j) {
+          const int rr = r0 + j;
+          if (!bars->valid[rr]) continue;
+          float* p = sCur + rr * D + n;
+          *p = __fadd_rn(*p, dequant(x1[j], x2[j], x3[j], stp[j], a.gemms[gi - 1].scale));
+        }
+      });
+      row_bar_d();
+    }
+
+    // ---- inter-block residual: blockIn += cur; cur = blockIn (stream.go:158-163) ----
+    if (a.residual && !a.embed_first) {
+#pragma unroll
+      for (int u = 0; u < kDRowsPerWarp; ++u) {
+        const int rr = warp + kDRowWarps * u;
+        const int s = s0 + rr;
+        if (!bars->valid[rr]) continue;
+        float4* c4 = reinterpret_cast<float4*>(sCur + rr * D);
+        float4* b4 = reinterpret_cast<float4*>(a.blockin + (size_t)s * D);
+#pragma unroll
+        for (int k = 0; k < KF; ++k) {
+          const int f = lane + 32 * k;
+          if (f >= nf) continue;
+          const float4 b = b4[f], c = c4[f];
+          const float4 y = make_float4(__fadd_rn(b.x, c.x), __fadd_rn(b.y, c.y), __fadd_rn(b.z, c.z), __fadd_rn(b.w, c.w));
+          c4[f] = y;
+          b4[f] = y;
+        }
+      }
+      row_bar_d();
+    }
+
+    // ---- rule steps ----
+    for (int st = 0; st < a.nsteps; ++st) {
+      const int bs = a.bs0 + st;
+      const int dil = a.dil[st];
+      // the session state this step reads (latch, left neighbour in the norm ring), fetched now
+      float4 lo[kDRowsPerWarp][KF], lf[kDRowsPerWarp][KF];
+#pragma unroll
+      for (int u = 0; u < kDRowsPerWarp; ++u) {
+        const int rr = warp + kDRowWarps * u;
+        const int s = s0 + rr;
+        const bool v = bars->valid[rr] != 0;
+        const int pos = bars->pos[rr];
+        const size_t so = (size_t)s * a.total_steps + bs;
+        const float4* ls4 = reinterpret_cast<const float4*>(a.latch + so * D);
+        const float4* ring4 = reinterpret_cast<const float4*>(a.norm_ring + so * a.ring * D);
+        const int lpos = pos - dil;
+#pragma unroll
+        for (int k = 0; k < KF; ++k) {
+          const int f = lane + 32 * k;
+          const bool in = v && f < nf;
+          const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+          lo[u][k] = (in && pos > 0) ? ls4[f] : z;
+          lf[u][k] = (in && lpos >= 0) ? ring4[(size_t)(lpos % a.ring) * nf + f] : z;
+        }
+      }
+      // norm cell n, kept in shared memory and sliced for W_select
+      norm_rows(a.gamma, sNrm, false, nullptr, true);
+      publish();
+      // lambda = sigmoid(W_select n s_sel + base), into the latch-gate rows
+      tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[8], uint32_t(&x2)[8],
+                                uint32_t(&x3)[8]) {
+        const int n = c * 128 + chl;
+        if (n >= D) return;
+        const float base = a.latch_base[n];
+        const float scale = a.gemms[gi - 1].scale;
+#pragma unroll
+        for (int j = 0; j < kDCols; ++j)
+          sAux[(r0 + j) * D + n] = sigmoid_clamped(__fadd_rn(dequant(x1[j], x2[j], x3[j], stp[j], scale), base));
+      });
+      row_bar_d();
+      // latch update, ring write, and x = [n | n(pos - dil) | latch] sliced for W1
+#pragma unroll
+      for (int u = 0; u < kDRowsPerWarp; ++u) {
+        const int rr = warp + kDRowWarps * u;
+        const int s = s0 + rr;
+        const bool v = bars->valid[rr] != 0;
+        const int pos = bars->pos[rr];
+        const size_t so = (size_t)s * a.total_steps + bs;
+        float4* ls4 = reinterpret_cast<float4*>(a.latch + so * D);
+        float4* ring4 = reinterpret_cast<float4*>(a.norm_ring + so * a.ring * D);
+        const float4* n4 = reinterpret_cast<const float4*>(sNrm + rr * D);
+        const float4* l4 = reinterpret_cast<const float4*>(sAux + rr * D);
+        float4 nv[KF], lv[KF];
+        float m = 0.f;
+#pragma unroll
+        for (int k = 0; k < KF; ++k) {
+          const int f = lane + 32 * k;
+          const bool in = v && f < nf;
+          const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+          nv[k] = in ? n4[f] : z;
+          const float4 lam = in ? l4[f] : z;
+          const float4 o = lo[u][k];
+          float4 l;
+          l.x = __fadd_rn(__fmul_rn(lam.x, o.x), __fmul_rn(__fsub_rn(1.0f, lam.x), nv[k].x));
+          l.y = __fadd_rn(__fmul_rn(lam.y, o.y), __fmul_rn(__fsub_rn(1.0f, lam.y), nv[k].y));
+          l.z = __fadd_rn(__fmul_rn(lam.z, o.z), __fmul_rn(__fsub_rn(1.0f, lam.z), nv[k].z));
+          l.w = __fadd_rn(__fmul_rn(lam.w, o.w), __fmul_rn(__fsub_rn(1.0f, lam.w), nv[k].w));
+          lv[k] = l;
+          if (in) {
+            ls4[f] = l;
+            ring4[(size_t)(pos % a.ring) * nf + f] = nv[k];
+          }
+          if (f < nf) m = fmaxf(m, fmaxf(max4_d(nv[k]), fmaxf(max4_d(l), max4_d(lf[u][k]))));
+        }
+        m = v ? warp_max_d(m) : 0.f;
+        if (lane == 0) bars->rstep[rr] = row_step(m);
+        const float is = row_inv_step(m);
+#pragma unroll
+        for (int k = 0; k < KF; ++k) {
+          const int f = lane + 32 * k;
+          if (f < nf) {
+            put_planes(sB, KT, rr, 4 * f, nv[k], is);
+            put_planes(sB, KT, rr, D + 4 * f, lf[u][k], is);
+            put_planes(sB, KT, rr, 2 * D + 4 * f, lv[k], is);
+          }
+        }
+      }
+      publish();
+      // hidden = (W1v x s1 + b1v) * sigmoid(W1g x s1 + b1g)   (applyRule layer 1, stream.go:212-220)
+      tiles2(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&v1)[8], uint32_t(&v2)[8],
+                                uint32_t(&v3)[8], uint32_t(&g1)[8], uint32_t(&g2)[8], uint32_t(&g3)[8]) {
+        const int hu = c * 128 + chl;
+        if (hu >= H) return;
+        const float bv = a.b1[hu], bg = a.b1[H + hu];
+        const float scale = a.gemms[gi - 1].scale;
+#pragma unroll
+        for (int j = 0; j < kDCols; ++j) {
+          const float hv = __fadd_rn(dequant(v1[j], v2[j], v3[j], stp[j], scale), bv);
+          const float gt = __fadd_rn(dequant(g1[j], g2[j], g3[j], stp[j], scale), bg);
+          sAux[(r0 + j) * H + hu] = __fmul_rn(hv, sigmoid_clamped(gt));
+        }
+      });
+      row_bar_d();
+      // the hidden rows sliced for W2 (max |hidden| of each row)
+      {
+        const int hf = H / 4;
+#pragma unroll
+        for (int u = 0; u < kDRowsPerWarp; ++u) {
+          const int rr = warp + kDRowWarps * u;
+          const bool v = bars->valid[rr] != 0;
+          const float4* h4 = reinterpret_cast<const float4*>(sAux + rr * H);
+          float m = 0.f;
+          for (int f = lane; f < hf; f += 32) m = fmaxf(m, max4_d(h4[f]));
+          m = v ? warp_max_d(m) : 0.f;
+          if (lane == 0) bars->rstep[rr] = row_step(m);
+          const float is = row_inv_step(m);
+          for (int f = lane; f < hf; f += 32) put_planes(sB, KT, rr, 4 * f, v ? h4[f] : make_float4(0.f, 0.f, 0.f, 0.f), is);
+        }
+      }
+      publish();
+      // o = W2 hidden s2 + b2; gate = sigmoid(o_gate); cur = (1 - gate) cur + gate o_delta (:222-229)
+      tiles2(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&v1)[8], uint32_t(&v2)[8],
+                                uint32_t(&v3)[8], uint32_t(&g1)[8], uint32_t(&g2)[8], uint32_t(&g3)[8]) {
+        const int d = c * 128 + chl;
+        if (d >= D) return;
+        const float bd = a.b2[d], bg = a.b2[D + d];
+        const float scale = a.gemms[gi - 1].scale;
+#pragma unroll
+        for (int j = 0; j < kDCols; ++j) {
+          const int rr = r0 + j;
+          if (!bars->valid[rr]) continue;
+          const float od = __fadd_rn(dequant(v1[j], v2[j], v3[j], stp[j], scale), bd);
+          const float og = __fadd_rn(dequant(g1[j], g2[j], g3[j], stp[j], scale), bg);
+          const float gate = sigmoid_clamped(og);
+          float* p = sCur + rr * D + d;
+          *p = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, gate), *p), __fmul_rn(gate, od));
+        }
+      });
+      row_bar_d();
+    }
+
+    // ---- attention sublayer: norm (sliced for QKV) + QKV, keys/values into the ring ----
+    if (a.has_attn) {
+      norm_rows(a.attn_norm, nullptr, false, nullptr, true);
+      if (lane == 0) {
+#pragma unroll
+        for (int u = 0; u < kDRowsPerWarp; ++u) {
+          const int rr = warp + kDRowWarps * u;
+          if (bars->valid[rr]) a.att_rowmax[s0 + rr] = 0.f;  // the attention kernel max-accumulates it
+        }
+      }
+      publish();
+      const int dh = a.dh;
+      tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[8], uint32_t(&x2)[8],
+                                uint32_t(&x3)[8]) {
+        const int n = c * 128 + chl;
+        if (n >= 3 * D) return;
+        const int part = n / D, e = n - part * D;
+        const int hh = part > 0 ? e / dh : 0;
+        const float scale = a.gemms[gi - 1].scale;
+#pragma unroll
+        for (int j = 0; j < kDCols; ++j) {
+          const int rr = r0 + j;
+          if (!bars->valid[rr]) continue;
+          const int s = s0 + rr;
+          const float y = dequant(x1[j], x2[j], x3[j], stp[j], scale);
+          if (part == 0) {
+            a.qbuf[(size_t)s * D + e] = y;
+          } else {
+            // key/value rings, head-major: [K|V][head][slot][dh]
+            float* kvs = a.kv + ((size_t)s * a.n_attn + a.attn_slot) * 2 * (size_t)a.cache * D;
+            const int rslot = bars->pos[rr] % a.cache;
+            kvs[(size_t)(part - 1) * a.cache * D + ((size_t)hh * a.cache + rslot) * dh + (e - hh * dh)] = y;
+          }
+        }
+      });
+    }
+
+    // ---- final RMSNorm (the head's input) ----
+    if (a.final_norm) norm_rows(a.final_gain, a.fnorm, true, a.fnorm_rowmax, false);
+
+    // ---- the block's output rows for the next kernel ----
+    if (!a.final_norm) {
+      row_bar_d();
+#pragma unroll
+      for (int u = 0; u < kDRowsPerWarp; ++u) {
+        const int rr = warp + kDRowWarps * u;
+        if (!bars->valid[rr]) continue;
+        const float4* c4 = reinterpret_cast<const float4*>(sCur + rr * D);
+        float4* g4 = reinterpret_cast<float4*>(a.cur + (size_t)(s0 + rr) * D);
+#pragma unroll
+        for (int k = 0; k < KF; ++k) {
+          const int f = lane + 32 * k;
+          if (f < nf) g4[f] = c4[f];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kDMmaWarp) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace eng
+}  // namespace mc

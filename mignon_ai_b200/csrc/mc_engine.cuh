@@ -68,6 +68,7 @@ struct BlockArgs {
   float* kvlin;      // [S][P][2][D] keys and values of a prefill segment
   unsigned long long* trace;  // optional phase timestamps of CTA 0 (null: off)
   int trace_fine;             // also time every chunk of every GEMM
+  int dec_kt;                 // decode kernel: K tiles of its activation-plane region
 };
 
 // sigmoidClamped (internal/quant/stream.go:128-136): saturated beyond |x| > 15, else 1/(1+e^-x)

@@ -71,6 +71,22 @@ static std::vector<int> perm_paired(int half, int nchunks) {
   return p;
 }
 
+// Split pairs (the decode kernel's layout): tile 2c holds units [128c, 128c+128) of the first half,
+// tile 2c+1 the same units of the second half, so a TMEM lane sees a value and its gate in two
+// consecutive accumulators.
+static std::vector<int> perm_split(int half, int npairs) {
+  std::vector<int> p((size_t)2 * npairs * 128, -1);
+  for (int c = 0; c < npairs; ++c)
+    for (int j = 0; j < 128; ++j) {
+      const int u = c * 128 + j;
+      if (u < half) {
+        p[(size_t)(2 * c) * 128 + j] = u;
+        p[(size_t)(2 * c + 1) * 128 + j] = half + u;
+      }
+    }
+  return p;
+}
+
 struct DevGemm {
   uint8_t* tiles = nullptr;
   int K = 0, ktiles = 0, nchunks = 0;
@@ -81,12 +97,16 @@ struct DevBlock {
   int steps = 0, attn_slot = -1;
   std::vector<int> dil;
   DevGemm w1, w2, wsel, qkv, out;
+  DevGemm w1d, w2d;  // W1 and W2 in split-pair tiles (decode kernel)
   float *b1 = nullptr, *b2 = nullptr, *gamma = nullptr, *attn_norm = nullptr;
 };
 
 struct DevModel {
   int device = 0;
   int V = 0, D = 0, H = 0, max_context = 0, heads = 0, window = 0, cache = 0, ring = 0, total_steps = 0, n_attn = 0;
+  int dec_kt = 0;         // decode kernel: K tiles of its activation planes
+  size_t dec_smem = 0;    // decode kernel: dynamic shared memory
+  bool dec_ok = false;    // the decode kernel fits this model (else decode uses block_kernel)
   bool tied = true;
   int8_t* embed = nullptr;
   float embed_scale = 0;
@@ -111,12 +131,15 @@ struct DevModel {
     dst = reinterpret_cast<T*>(p);
     return kOk;
   }
-  int upload_gemm(DevGemm& g, const int8_t* W, int rows, int K, float scale, int paired_half) {
+  int upload_gemm(DevGemm& g, const int8_t* W, int rows, int K, float scale, int paired_half, bool split = false) {
     g.K = K;
     g.ktiles = (K + 127) / 128;
     g.scale = scale;
     std::vector<int> perm;
-    if (paired_half > 0) {
+    if (split) {
+      g.nchunks = 2 * ((paired_half + 127) / 128);
+      perm = perm_split(paired_half, g.nchunks / 2);
+    } else if (paired_half > 0) {
       g.nchunks = (paired_half + kHalfChunk - 1) / kHalfChunk;
       perm = perm_paired(paired_half, g.nchunks);
     } else {
@@ -187,6 +210,8 @@ int build_dev_model(const HostModel& hm, int device, std::unique_ptr<DevModel>& 
     total += hb.steps;
     if ((st = m->upload_gemm(b.w1, hb.w1.data.data(), 2 * H, 3 * D, hb.w1.scale, H)) != kOk) return st;
     if ((st = m->upload_gemm(b.w2, hb.w2.data.data(), 2 * D, H, hb.w2.scale, D)) != kOk) return st;
+    if ((st = m->upload_gemm(b.w1d, hb.w1.data.data(), 2 * H, 3 * D, hb.w1.scale, H, true)) != kOk) return st;
+    if ((st = m->upload_gemm(b.w2d, hb.w2.data.data(), 2 * D, H, hb.w2.scale, D, true)) != kOk) return st;
     if ((st = m->upload_gemm(b.wsel, hb.wsel.data.data(), D, D, hb.wsel.scale, 0)) != kOk) return st;
     if ((st = m->upload(b.b1, hb.b1.data(), hb.b1.size() * 4)) != kOk) return st;
     if ((st = m->upload(b.b2, hb.b2.data(), hb.b2.size() * 4)) != kOk) return st;
@@ -204,6 +229,9 @@ int build_dev_model(const HostModel& hm, int device, std::unique_ptr<DevModel>& 
   m->total_steps = total;
   m->ring = longest + 1;
   m->n_attn = nattn;
+  m->dec_kt = (std::max(3 * D, H) + 127) / 128;
+  m->dec_smem = decode_smem_bytes(D, H, m->dec_kt);
+  m->dec_ok = m->dec_smem <= kDecodeSmemMax;
   if (nattn > 0 && m->cache > 128) return set_error(kUnsupported, "attention caches above 128 positions");
   out = std::move(m);
   return kOk;
@@ -215,6 +243,7 @@ int build_dev_model(const HostModel& hm, int device, std::unique_ptr<DevModel>& 
 struct DevBatch {
   DevModel* m = nullptr;
   int S = 0, window = 0, pmax = 0, nsplit = 1, topk = 0;
+  bool decode_kernel = true;  // decode steps use block_decode_kernel (MC_DECODE_KERNEL=block: block_kernel)
   size_t rows = 0;  // scratch rows
   cudaStream_t stream = nullptr;
   std::vector<void*> allocs;
@@ -275,6 +304,9 @@ static int ensure_attrs(int device) {
   MC_CUDA(cudaFuncSetAttribute(block_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
   MC_CUDA(cudaFuncSetAttribute(block_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
   MC_CUDA(cudaFuncSetAttribute(block_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
+  MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
+  MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
+  MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem));
   MC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
   if (device < 64) g_attr_done[device] = true;
@@ -291,6 +323,10 @@ int batch_create(DevModel* m, int S, int window, int pmax, int topk, std::unique
   b->window = window;
   b->pmax = std::max(1, std::min(pmax, 128));
   b->topk = topk;
+  {
+    const char* k = getenv("MC_DECODE_KERNEL");
+    b->decode_kernel = m->dec_ok && !(k && strcmp(k, "block") == 0);
+  }
   const int D = m->D, H = m->H;
   const int spt_min = std::max(1, 128 / b->pmax);
   const size_t tiles = std::max((size_t)(S + 127) / 128, (size_t)(S + spt_min - 1) / spt_min);
@@ -466,10 +502,25 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
     a.ngemms = g;
     a.trace = b.trace ? b.trace + 64 * bi : nullptr;
     a.trace_fine = getenv("MC_TRACE_FINE") != nullptr;
-    switch ((m.D + 127) / 128) {
-      case 1: block_kernel<1><<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
-      case 2: block_kernel<2><<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
-      default: block_kernel<3><<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
+    if (P == 1 && b.decode_kernel) {
+      // the decode kernel reads W1 and W2 in split-pair tiles
+      for (int i = 0; i < a.ngemms; ++i) {
+        if (a.gemms[i].type == kGW1) a.gemms[i] = spec(m.blocks[bi].w1d, kGW1, a.gemms[i].step);
+        if (a.gemms[i].type == kGW2) a.gemms[i] = spec(m.blocks[bi].w2d, kGW2, a.gemms[i].step);
+      }
+      a.dec_kt = m.dec_kt;
+      const int grid = (b.S + kDR - 1) / kDR;
+      switch ((m.D + 127) / 128) {
+        case 1: block_decode_kernel<1><<<grid, kDThreads, m.dec_smem, s>>>(a); break;
+        case 2: block_decode_kernel<2><<<grid, kDThreads, m.dec_smem, s>>>(a); break;
+        default: block_decode_kernel<3><<<grid, kDThreads, m.dec_smem, s>>>(a); break;
+      }
+    } else {
+      switch ((m.D + 127) / 128) {
+        case 1: block_kernel<1><<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
+        case 2: block_kernel<2><<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
+        default: block_kernel<3><<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
+      }
     }
     MC_CUDA(cudaGetLastError());
     if (log) log->record(s, final_k ? 2 : 0);

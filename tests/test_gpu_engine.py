@@ -166,6 +166,36 @@ def test_sampling_matches_oracle(oracle):
         assert t >= 0
 
 
+@pytest.mark.parametrize("cfg,vocab", [(2, None), (1, None)])
+def test_decode_kernel_matches_block_kernel_bitwise(monkeypatch, cfg, vocab):
+    """Decode steps run on block_decode_kernel (weights on the MMA's M side, 32 sessions per CTA);
+    block_kernel (128 session rows per CTA) computes the same float32 operations in the same
+    order, so the two give bit-identical logits, tokens and probabilities (MC_DECODE_KERNEL=block
+    selects block_kernel for a batch opened under it). Ragged and idle sessions included."""
+    spec = small_spec(cfg, vocab)
+    data = synth.build_model_file(spec)
+    gm = quant.Model.decode(data)
+    n = 200
+    prompts = synth.prompts_uniform_fast(n, 48, spec.vocab, seed=5)
+    lens = np.full(n, 48, np.int32)
+    lens[3] = 0
+    lens[50] = 7
+    lens[199] = 1
+    got = {}
+    for kern in ("decode", "block"):
+        if kern == "block":
+            monkeypatch.setenv("MC_DECODE_KERNEL", "block")
+        else:
+            monkeypatch.delenv("MC_DECODE_KERNEL", raising=False)
+        got[kern] = run_steps(gm, prompts, lens, 6)
+    monkeypatch.delenv("MC_DECODE_KERNEL", raising=False)
+    act = lens > 0
+    for i, name in enumerate(("tokens", "probs", "logits")):
+        a, b = got["decode"][i][act], got["block"][i][act]
+        assert np.array_equal(a, b), f"{name}: {np.sum(a != b)} entries differ"
+    gm.close()
+
+
 def test_model_file_errors():
     """Damaged files are rejected by the engine's own reader (binary_test.go:58-75)."""
     qm = synth.build_model_uniform(16, 8, 8, synth.build_block_configs(2, 3, 2), 0, 0, 16, seed=1)
