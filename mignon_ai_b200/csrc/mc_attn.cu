@@ -180,6 +180,207 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(a.att_rowmax + grow), __float_as_uint(om));
 }
 
+// Decode with the key/value windows staged in shared memory: a persistent CTA per SM takes a
+// contiguous range of (session, head) items and deals them to its warps round-robin. Each warp
+// owns `depth` shared-memory stages and their mbarriers: its lane 0 fetches the key ring and the
+// value ring of its next items (one contiguous block each in the head-major layout) with bulk
+// copies, so every stage has a single producer and a single consumer, which waits on each phase
+// of its own stages in order. While a warp computes one item its next one is in flight.
+//   scores  lane i scores window positions lo+i, lo+i+32, ... (its key rows, 16-byte columns
+//           read in a per-lane rotation: conflict-free), one independent sum per key;
+//   softmax the max shift, the reference's exp polynomial and one reciprocal, on warp shuffles;
+//   values  the probabilities go to a per-warp shared buffer; lanes own (row group, 16-byte
+//           column) pairs and accumulate float4 rows of their group, then the groups combine.
+constexpr int kAsMaxStages = 12;
+constexpr size_t kAsSmemBudget = 200 * 1024;  // stages; the launch limit is kAsSmemMax
+constexpr size_t kAsSmemMax = 227 * 1024;
+
+struct AttnStaging {
+  int warps = 0, depth = 0;
+  size_t smem = 0;
+};
+
+// Warps and stages per warp of the staged decode kernel (warps == 0: not usable; the bulk copies
+// need 16-byte multiples).
+inline AttnStaging attn_staging(int cache, int dh) {
+  AttnStaging st;
+  const size_t stage = (size_t)2 * cache * dh * 4;
+  // head widths with an instantiated kernel: the value phase's row groups (32 / (dh / 4)) must be a
+  // power of two
+  if ((stage / 2) % 16 != 0 || !(dh == 4 || dh == 8 || dh == 16 || dh == 32 || dh == 48 || dh == 64)) return st;
+  const size_t per_warp_extra = 128 * 4 + 2 * 8;
+  int total = (int)((kAsSmemBudget - 1024) / stage);
+  if (total > kAsMaxStages) total = kAsMaxStages;
+  if (total < 2) return st;
+  st.depth = total >= 8 ? 2 : 1;
+  st.warps = total / st.depth;
+  st.smem = 128 + (size_t)st.warps * st.depth * stage + (size_t)st.warps * per_warp_extra;
+  return st;
+}
+
+template <int DH>  // head width (a multiple of 4, at most 64)
+__global__ void __launch_bounds__(kAsMaxStages * 32) attn_decode_staged_kernel(const __grid_constant__ AttnArgs a,
+                                                                             int depth, int per_cta) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  constexpr int NF = DH / 4;                 // float4 columns of a head row
+  constexpr int G = 32 / NF;                 // row groups of the value phase
+  const int cache = a.cache, D = a.D, heads = a.heads;
+  const uint32_t head_bytes = (uint32_t)(cache * DH * 4);
+  const uint32_t stage_bytes = 2 * head_bytes;
+  const int nwarps = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* stages = sm + (size_t)warp * depth * stage_bytes;
+  float* pbuf = reinterpret_cast<float*>(sm + (size_t)nwarps * depth * stage_bytes) + warp * 128;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)nwarps * depth * stage_bytes + (size_t)nwarps * 512) +
+                   warp * depth;
+  const long long items = (long long)a.n_sess * heads;
+  const long long i0 = (long long)blockIdx.x * per_cta;
+  const long long n = min(items, i0 + per_cta) - i0;
+  const int nm = n > warp ? (int)((n - warp + nwarps - 1) / nwarps) : 0;  // this warp's items
+  if (lane == 0) {
+    for (int d = 0; d < depth; ++d) mbar_init(&full[d], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+
+  // lane 0: fetch the warp's m-th item into stage m % depth (an idle session: arrival only)
+  int issued = 0;
+  auto issue = [&](int m) {
+    if (m >= nm) return;
+    issued = m + 1;
+    const long long it = i0 + warp + (long long)nwarps * m;
+    const int s = (int)(it / heads), h = (int)(it - (long long)s * heads);
+    uint64_t* bar = &full[m % depth];
+    if (a.seglen[s] <= 0) {
+      mbar_arrive(bar);
+      return;
+    }
+    const float* Kh = a.kv + ((size_t)s * a.n_attn + a.attn_slot) * 2 * (size_t)cache * D + (size_t)h * cache * DH;
+    uint8_t* dst = stages + (size_t)(m % depth) * stage_bytes;
+    mbar_arrive_expect_tx(bar, stage_bytes);
+    bulk_load(dst, Kh, head_bytes, bar);
+    bulk_load(dst + head_bytes, Kh + (size_t)cache * D, head_bytes, bar);
+  };
+  if (lane == 0)
+    for (int m = 0; m < depth; ++m) issue(m);
+
+  bool healthy = true;  // false after a wait gave up: issue nothing more, drain what is in flight
+  for (int m = 0; m < nm; ++m) {
+    const long long it = i0 + warp + (long long)nwarps * m;
+    const int s = (int)(it / heads), h = (int)(it - (long long)s * heads);
+    const int st = m % depth;
+    const bool active = a.seglen[s] > 0;
+    const int pos = a.pos0[s];
+    int ws = 0;
+    if (a.window > 0 && pos - a.window + 1 > 0) ws = pos - a.window + 1;
+    const int lo = max(ws, pos - cache + 1);
+    const int span = pos - lo + 1;  // <= cache <= 128
+    const int lo_slot = lo % cache;
+    const int grow = grow_of(a, s, 0);
+    const float* q = a.qbuf + (size_t)grow * D + h * DH;
+    float4 qr[NF];  // q rotated like the key reads: qr[f] = q4[(f + lane) % NF]
+    if (active) {
+#pragma unroll
+      for (int f = 0; f < NF; ++f) qr[f] = reinterpret_cast<const float4*>(q)[(f + lane) % NF];
+    }
+    const bool got = __all_sync(0xffffffffu, healthy && mbar_wait_or_abort(&full[st], (m / depth) & 1, kErrWaitFull));
+    if (!got) healthy = false;
+    if (got && active) {
+      const float* Ks = reinterpret_cast<const float*>(stages + (size_t)st * stage_bytes);
+      const float* Vs = Ks + (size_t)cache * DH;
+      float sc[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = lane + 32 * u;
+        float acc = 0.f;
+        if (j < span) {
+          int sl = lo_slot + j;
+          if (sl >= cache) sl -= cache;
+          if (sl >= cache) sl -= cache;
+          const float4* row = reinterpret_cast<const float4*>(Ks + (size_t)sl * DH);
+#pragma unroll
+          for (int f = 0; f < NF; ++f) {
+            const float4 k4 = row[(f + lane) % NF];
+            acc = __fmaf_rn(qr[f].x, k4.x, acc);
+            acc = __fmaf_rn(qr[f].y, k4.y, acc);
+            acc = __fmaf_rn(qr[f].z, k4.z, acc);
+            acc = __fmaf_rn(qr[f].w, k4.w, acc);
+          }
+        }
+        sc[u] = acc;
+      }
+      float mx = -3.402823466e38f;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (lane + 32 * u < span) {
+          sc[u] = __fmul_rn(sc[u], a.scale);
+          mx = fmaxf(mx, sc[u]);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float sum = 0.f;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (lane + 32 * u < span) {
+          sc[u] = ref_vec_exp(__fsub_rn(sc[u], mx));
+          sum = __fadd_rn(sum, sc[u]);
+        } else {
+          sc[u] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+      const float inv = __fdiv_rn(1.0f, sum);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) pbuf[lane + 32 * u] = __fmul_rn(sc[u], inv);
+      __syncwarp();
+      // values: lane = (row group g, column c); rows j = g, g + G, ... of the window
+      const int c = lane % NF, g = lane / NF;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (g < G) {
+        int sl = lo_slot + g;
+        if (sl >= cache) sl -= cache;
+        const float4* V4 = reinterpret_cast<const float4*>(Vs);
+#pragma unroll 4
+        for (int j = g; j < span; j += G) {
+          const float p = pbuf[j];
+          const float4 v = V4[(size_t)sl * NF + c];
+          o.x = __fmaf_rn(p, v.x, o.x);
+          o.y = __fmaf_rn(p, v.y, o.y);
+          o.z = __fmaf_rn(p, v.z, o.z);
+          o.w = __fmaf_rn(p, v.w, o.w);
+          sl += G;
+          if (sl >= cache) sl -= cache;
+        }
+      }
+#pragma unroll
+      for (int off = (G / 2) * NF; off >= NF; off >>= 1) {
+        o.x = __fadd_rn(o.x, __shfl_down_sync(0xffffffffu, o.x, off));
+        o.y = __fadd_rn(o.y, __shfl_down_sync(0xffffffffu, o.y, off));
+        o.z = __fadd_rn(o.z, __shfl_down_sync(0xffffffffu, o.z, off));
+        o.w = __fadd_rn(o.w, __shfl_down_sync(0xffffffffu, o.w, off));
+      }
+      float om = 0.f;
+      if (lane < NF) {
+        reinterpret_cast<float4*>(a.att + (size_t)grow * D + h * DH)[lane] = o;
+        om = fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w)));
+      }
+#pragma unroll
+      for (int k = 16; k; k >>= 1) om = fmaxf(om, __shfl_xor_sync(0xffffffffu, om, k));
+      if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(a.att_rowmax + grow), __float_as_uint(om));
+    }
+    __syncwarp();
+    if (lane == 0 && healthy) issue(m + depth);  // refill the stage just read
+  }
+  // never leave with a copy still writing this warp's stages (bounded waits; only an aborted
+  // wait above can leave one)
+  if (lane == 0)
+    for (int m = issued > depth ? issued - depth : 0; m < issued; ++m)
+      mbar_wait(&full[m % depth], (m / depth) & 1, kErrWaitFull);
+}
+
 // Prefill: one CTA per session; the segment's keys and values (written by the block kernel to
 // kvlin) are staged into shared memory; one warp per (query, head) item.
 __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const __grid_constant__ AttnArgs a) {

@@ -244,6 +244,7 @@ struct DevBatch {
   DevModel* m = nullptr;
   int S = 0, window = 0, pmax = 0, nsplit = 1, topk = 0;
   bool decode_kernel = true;  // decode steps use block_decode_kernel (MC_DECODE_KERNEL=block: block_kernel)
+  int n_sm = 148;             // multiprocessors of the device (persistent grids)
   size_t rows = 0;  // scratch rows
   cudaStream_t stream = nullptr;
   std::vector<void*> allocs;
@@ -308,6 +309,12 @@ static int ensure_attrs(int device) {
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem));
+  MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
+  MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
+  MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
+  MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
+  MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<48>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
+  MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
   MC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
   if (device < 64) g_attr_done[device] = true;
   return kOk;
@@ -327,6 +334,7 @@ int batch_create(DevModel* m, int S, int window, int pmax, int topk, std::unique
     const char* k = getenv("MC_DECODE_KERNEL");
     b->decode_kernel = m->dec_ok && !(k && strcmp(k, "block") == 0);
   }
+  MC_CUDA(cudaDeviceGetAttribute(&b->n_sm, cudaDevAttrMultiProcessorCount, m->device));
   const int D = m->D, H = m->H;
   const int spt_min = std::max(1, 128 / b->pmax);
   const size_t tiles = std::max((size_t)(S + 127) / 128, (size_t)(S + spt_min - 1) / spt_min);
@@ -545,7 +553,22 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
       aa.att = b.att;
       aa.att_rowmax = b.att_rowmax;
       aa.scale = (float)(1.0 / std::sqrt((double)aa.dh));
-      if (P == 1) {
+      const AttnStaging stg = attn_staging(m.cache, aa.dh);
+      if (P == 1 && stg.warps > 0 && stg.smem <= kAsSmemMax) {
+        const long long items = (long long)b.S * m.heads;
+        int grid = (int)std::min<long long>(items, b.n_sm);
+        const int per_cta = (int)((items + grid - 1) / grid);
+        grid = (int)((items + per_cta - 1) / per_cta);
+        const int threads = stg.warps * 32;
+        switch (aa.dh) {
+          case 4: attn_decode_staged_kernel<4><<<grid, threads, stg.smem, s>>>(aa, stg.depth, per_cta); break;
+          case 8: attn_decode_staged_kernel<8><<<grid, threads, stg.smem, s>>>(aa, stg.depth, per_cta); break;
+          case 16: attn_decode_staged_kernel<16><<<grid, threads, stg.smem, s>>>(aa, stg.depth, per_cta); break;
+          case 32: attn_decode_staged_kernel<32><<<grid, threads, stg.smem, s>>>(aa, stg.depth, per_cta); break;
+          case 48: attn_decode_staged_kernel<48><<<grid, threads, stg.smem, s>>>(aa, stg.depth, per_cta); break;
+          default: attn_decode_staged_kernel<64><<<grid, threads, stg.smem, s>>>(aa, stg.depth, per_cta); break;
+        }
+      } else if (P == 1) {
         const long long warps = (long long)b.S * m.heads;
         const int grid = (int)((warps * 32 + kAttnThreads - 1) / kAttnThreads);
         switch (aa.dh) {
