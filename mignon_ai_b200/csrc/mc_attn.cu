@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   const int span = pos - lo + 1;  // <= cache <= 128
   const int lo_slot = lo % cache;
   const int grow = grow_of(a, s, 0);
-  const float* K = a.kv + ((size_t)s * a.n_attn + a.attn_slot) * 2 * (size_t)cache * D + (size_t)h * cache * dh;
+  const float* K = a.kv + ((size_t)a.attn_slot * a.n_sess + s) * 2 * (size_t)cache * D + (size_t)h * cache * dh;
   const float* V = K + (size_t)cache * D;
   const float* q = a.qbuf + (size_t)grow * D + h * dh;
 
@@ -180,96 +180,101 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(a.att_rowmax + grow), __float_as_uint(om));
 }
 
-// Decode with the key/value windows staged in shared memory: a persistent CTA per SM takes a
-// contiguous range of (session, head) items and deals them to its warps round-robin. Each warp
-// owns `depth` shared-memory stages and their mbarriers: its lane 0 fetches the key ring and the
-// value ring of its next items (one contiguous block each in the head-major layout) with bulk
-// copies, so every stage has a single producer and a single consumer, which waits on each phase
-// of its own stages in order. While a warp computes one item its next one is in flight.
+// Decode with the key/value windows staged in shared memory: a persistent grid (one CTA per SM)
+// deals the (session, head) items to its warps round-robin, CTA-major. Each warp
+// owns two shared-memory buffers, one for a key ring and one for a value ring (each one
+// contiguous block in the head-major layout), each with its own mbarrier. Lane 0 of the warp
+// fetches them with bulk copies: the keys of the next item as soon as this item's scores are
+// done, its values as soon as this item's values are done. So a copy is always in flight while
+// the warp computes, and every buffer has one producer and one consumer (the same warp), which
+// waits on its phases in order.
 //   scores  lane i scores window positions lo+i, lo+i+32, ... (its key rows, 16-byte columns
 //           read in a per-lane rotation: conflict-free), one independent sum per key;
 //   softmax the max shift, the reference's exp polynomial and one reciprocal, on warp shuffles;
 //   values  the probabilities go to a per-warp shared buffer; lanes own (row group, 16-byte
 //           column) pairs and accumulate float4 rows of their group, then the groups combine.
-constexpr int kAsMaxStages = 12;
-constexpr size_t kAsSmemBudget = 200 * 1024;  // stages; the launch limit is kAsSmemMax
+constexpr int kAsMaxWarps = 12;
+constexpr size_t kAsSmemBudget = 200 * 1024;  // key/value buffers; the launch limit is kAsSmemMax
 constexpr size_t kAsSmemMax = 227 * 1024;
 
 struct AttnStaging {
-  int warps = 0, depth = 0;
+  int warps = 0;
   size_t smem = 0;
 };
 
-// Warps and stages per warp of the staged decode kernel (warps == 0: not usable; the bulk copies
-// need 16-byte multiples).
+inline size_t attn_staged_smem(int cache, int dh, int warps) {
+  return 128 + (size_t)warps * (2 * (size_t)cache * dh * 4 + 128 * 4 + 2 * 8);
+}
+
+// Warps of the staged decode kernel (warps == 0: not usable; the bulk copies need 16-byte
+// multiples, and the value phase's row groups, 32 / (dh / 4), a power of two).
 inline AttnStaging attn_staging(int cache, int dh) {
   AttnStaging st;
-  const size_t stage = (size_t)2 * cache * dh * 4;
-  // head widths with an instantiated kernel: the value phase's row groups (32 / (dh / 4)) must be a
-  // power of two
-  if ((stage / 2) % 16 != 0 || !(dh == 4 || dh == 8 || dh == 16 || dh == 32 || dh == 48 || dh == 64)) return st;
-  const size_t per_warp_extra = 128 * 4 + 2 * 8;
-  int total = (int)((kAsSmemBudget - 1024) / stage);
-  if (total > kAsMaxStages) total = kAsMaxStages;
-  if (total < 2) return st;
-  st.depth = total >= 8 ? 2 : 1;
-  st.warps = total / st.depth;
-  st.smem = 128 + (size_t)st.warps * st.depth * stage + (size_t)st.warps * per_warp_extra;
+  const size_t ring = (size_t)cache * dh * 4;
+  if (ring % 16 != 0 || !(dh == 4 || dh == 8 || dh == 16 || dh == 32 || dh == 48 || dh == 64)) return st;
+  int w = (int)((kAsSmemBudget - 1024) / (2 * ring));
+  if (w > kAsMaxWarps) w = kAsMaxWarps;
+  if (w < 1) return st;
+  st.warps = w;
+  st.smem = attn_staged_smem(cache, dh, w);
   return st;
 }
 
 template <int DH>  // head width (a multiple of 4, at most 64)
-__global__ void __launch_bounds__(kAsMaxStages * 32) attn_decode_staged_kernel(const __grid_constant__ AttnArgs a,
-                                                                             int depth, int per_cta) {
+__global__ void __launch_bounds__(kAsMaxWarps * 32) attn_decode_staged_kernel(const __grid_constant__ AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  constexpr int NF = DH / 4;                 // float4 columns of a head row
-  constexpr int G = 32 / NF;                 // row groups of the value phase
+  constexpr int NF = DH / 4;  // float4 columns of a head row
+  constexpr int G = 32 / NF;  // row groups of the value phase
   const int cache = a.cache, D = a.D, heads = a.heads;
-  const uint32_t head_bytes = (uint32_t)(cache * DH * 4);
-  const uint32_t stage_bytes = 2 * head_bytes;
+  const uint32_t ring_bytes = (uint32_t)(cache * DH * 4);
   const int nwarps = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* stages = sm + (size_t)warp * depth * stage_bytes;
-  float* pbuf = reinterpret_cast<float*>(sm + (size_t)nwarps * depth * stage_bytes) + warp * 128;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)nwarps * depth * stage_bytes + (size_t)nwarps * 512) +
-                   warp * depth;
+  float* Ks = reinterpret_cast<float*>(sm + (size_t)warp * 2 * ring_bytes);
+  float* Vs = Ks + (size_t)cache * DH;
+  float* pbuf = reinterpret_cast<float*>(sm + (size_t)nwarps * 2 * ring_bytes) + warp * 128;
+  uint64_t* kfull = reinterpret_cast<uint64_t*>(sm + (size_t)nwarps * (2 * ring_bytes + 512)) + warp * 2;
+  uint64_t* vfull = kfull + 1;
+  // item m of this warp: base + stride * m (the whole grid walks the items in order, so the rings
+  // read at any moment form one contiguous region)
   const long long items = (long long)a.n_sess * heads;
-  const long long i0 = (long long)blockIdx.x * per_cta;
-  const long long n = min(items, i0 + per_cta) - i0;
-  const int nm = n > warp ? (int)((n - warp + nwarps - 1) / nwarps) : 0;  // this warp's items
+  const long long base = blockIdx.x + (long long)gridDim.x * warp;
+  const long long stride = (long long)gridDim.x * nwarps;
+  const int nm = base < items ? (int)((items - base + stride - 1) / stride) : 0;
   if (lane == 0) {
-    for (int d = 0; d < depth; ++d) mbar_init(&full[d], 1);
+    mbar_init(kfull, 1);
+    mbar_init(vfull, 1);
     fence_barrier_init();
   }
   __syncwarp();
 
-  // lane 0: fetch the warp's m-th item into stage m % depth (an idle session: arrival only)
-  int issued = 0;
-  auto issue = [&](int m) {
+  // lane 0: fetch the key (which 0) or value (1) ring of the warp's m-th item (an idle session:
+  // arrival only). issued[which] counts the copies, for the final drain.
+  int issued[2] = {0, 0};
+  auto issue = [&](int m, int which) {
     if (m >= nm) return;
-    issued = m + 1;
-    const long long it = i0 + warp + (long long)nwarps * m;
+    issued[which] = m + 1;
+    const long long it = base + stride * m;
     const int s = (int)(it / heads), h = (int)(it - (long long)s * heads);
-    uint64_t* bar = &full[m % depth];
+    uint64_t* bar = which ? vfull : kfull;
     if (a.seglen[s] <= 0) {
       mbar_arrive(bar);
       return;
     }
-    const float* Kh = a.kv + ((size_t)s * a.n_attn + a.attn_slot) * 2 * (size_t)cache * D + (size_t)h * cache * DH;
-    uint8_t* dst = stages + (size_t)(m % depth) * stage_bytes;
-    mbar_arrive_expect_tx(bar, stage_bytes);
-    bulk_load(dst, Kh, head_bytes, bar);
-    bulk_load(dst + head_bytes, Kh + (size_t)cache * D, head_bytes, bar);
+    const float* src = a.kv + ((size_t)a.attn_slot * a.n_sess + s) * 2 * (size_t)cache * D + (size_t)which * cache * D +
+                       (size_t)h * cache * DH;
+    mbar_arrive_expect_tx(bar, ring_bytes);
+    bulk_load(which ? Vs : Ks, src, ring_bytes, bar);
   };
-  if (lane == 0)
-    for (int m = 0; m < depth; ++m) issue(m);
+  if (lane == 0) {
+    issue(0, 0);
+    issue(0, 1);
+  }
 
   bool healthy = true;  // false after a wait gave up: issue nothing more, drain what is in flight
   for (int m = 0; m < nm; ++m) {
-    const long long it = i0 + warp + (long long)nwarps * m;
+    const long long it = base + stride * m;
     const int s = (int)(it / heads), h = (int)(it - (long long)s * heads);
-    const int st = m % depth;
     const bool active = a.seglen[s] > 0;
     const int pos = a.pos0[s];
     int ws = 0;
@@ -284,11 +289,10 @@ __global__ void __launch_bounds__(kAsMaxStages * 32) attn_decode_staged_kernel(c
 #pragma unroll
       for (int f = 0; f < NF; ++f) qr[f] = reinterpret_cast<const float4*>(q)[(f + lane) % NF];
     }
-    const bool got = __all_sync(0xffffffffu, healthy && mbar_wait_or_abort(&full[st], (m / depth) & 1, kErrWaitFull));
+    // ---- scores and softmax from the key ring ----
+    bool got = __all_sync(0xffffffffu, healthy && mbar_wait_or_abort(kfull, m & 1, kErrWaitFull));
     if (!got) healthy = false;
     if (got && active) {
-      const float* Ks = reinterpret_cast<const float*>(stages + (size_t)st * stage_bytes);
-      const float* Vs = Ks + (size_t)cache * DH;
       float sc[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -335,8 +339,14 @@ __global__ void __launch_bounds__(kAsMaxStages * 32) attn_decode_staged_kernel(c
       const float inv = __fdiv_rn(1.0f, sum);
 #pragma unroll
       for (int u = 0; u < 4; ++u) pbuf[lane + 32 * u] = __fmul_rn(sc[u], inv);
-      __syncwarp();
-      // values: lane = (row group g, column c); rows j = g, g + G, ... of the window
+    }
+    __syncwarp();
+    if (lane == 0 && healthy) issue(m + 1, 0);  // the key buffer is free: next item's keys
+    // ---- values from the value ring ----
+    got = __all_sync(0xffffffffu, healthy && mbar_wait_or_abort(vfull, m & 1, kErrWaitFull));
+    if (!got) healthy = false;
+    if (got && active) {
+      // lane = (row group g, column c); rows j = g, g + G, ... of the window
       const int c = lane % NF, g = lane / NF;
       float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
       if (g < G) {
@@ -372,13 +382,14 @@ __global__ void __launch_bounds__(kAsMaxStages * 32) attn_decode_staged_kernel(c
       if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(a.att_rowmax + grow), __float_as_uint(om));
     }
     __syncwarp();
-    if (lane == 0 && healthy) issue(m + depth);  // refill the stage just read
+    if (lane == 0 && healthy) issue(m + 1, 1);  // the value buffer is free: next item's values
   }
-  // never leave with a copy still writing this warp's stages (bounded waits; only an aborted
-  // wait above can leave one)
-  if (lane == 0)
-    for (int m = issued > depth ? issued - depth : 0; m < issued; ++m)
-      mbar_wait(&full[m % depth], (m / depth) & 1, kErrWaitFull);
+  // never leave with a copy still writing this warp's buffers (bounded waits; only an aborted wait
+  // above can leave one): the last copy into each buffer was its phase issued - 1
+  if (lane == 0) {
+    if (issued[0] > 0) mbar_wait(kfull, (issued[0] - 1) & 1, kErrWaitFull);
+    if (issued[1] > 0) mbar_wait(vfull, (issued[1] - 1) & 1, kErrWaitFull);
+  }
 }
 
 // Prefill: one CTA per session; the segment's keys and values (written by the block kernel to

@@ -748,7 +748,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
       row_bar();
       trace_point(a, tp++);
       // key/value rings, head-major: [K|V][head][slot][dh] (each head's window is contiguous)
-      float* kvs = a.kv + ((size_t)ri.session * a.n_attn + a.attn_slot) * 2 * (size_t)a.cache * D;
+      float* kvs = a.kv + ((size_t)a.attn_slot * a.n_sess + ri.session) * 2 * (size_t)a.cache * D;
       const bool to_ring = ri.valid && ri.t >= ri.len - a.cache;
       const int rslot = ri.pos % a.cache;
       const int dh = a.dh;

@@ -567,7 +567,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
             a.qbuf[(size_t)s * D + e] = y;
           } else {
             // key/value rings, head-major: [K|V][head][slot][dh]
-            float* kvs = a.kv + ((size_t)s * a.n_attn + a.attn_slot) * 2 * (size_t)a.cache * D;
+            float* kvs = a.kv + ((size_t)a.attn_slot * a.n_sess + s) * 2 * (size_t)a.cache * D;
             const int rslot = bars->pos[rr] % a.cache;
             kvs[(size_t)(part - 1) * a.cache * D + ((size_t)hh * a.cache + rslot) * dh + (e - hh * dh)] = y;
           }

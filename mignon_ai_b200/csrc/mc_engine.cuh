@@ -54,7 +54,7 @@ struct BlockArgs {
   // session state
   float* norm_ring;  // [S][total_steps][ring][D]
   float* latch;      // [S][total_steps][D]
-  float* kv;         // [S][n_attn][2][cache][D]
+  float* kv;         // [n_attn][S][K|V][head][slot][dh]
   // scratch, indexed by global row (tile * 128 + r)
   float* cur;        // [rows][D]
   float* blockin;    // [rows][D]

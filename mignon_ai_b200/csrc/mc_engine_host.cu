@@ -556,17 +556,15 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
       const AttnStaging stg = attn_staging(m.cache, aa.dh);
       if (P == 1 && stg.warps > 0 && stg.smem <= kAsSmemMax) {
         const long long items = (long long)b.S * m.heads;
-        int grid = (int)std::min<long long>(items, b.n_sm);
-        const int per_cta = (int)((items + grid - 1) / grid);
-        grid = (int)((items + per_cta - 1) / per_cta);
+        const int grid = (int)std::min<long long>((items + stg.warps - 1) / stg.warps, b.n_sm);
         const int threads = stg.warps * 32;
         switch (aa.dh) {
-          case 4: attn_decode_staged_kernel<4><<<grid, threads, stg.smem, s>>>(aa, stg.depth, per_cta); break;
-          case 8: attn_decode_staged_kernel<8><<<grid, threads, stg.smem, s>>>(aa, stg.depth, per_cta); break;
-          case 16: attn_decode_staged_kernel<16><<<grid, threads, stg.smem, s>>>(aa, stg.depth, per_cta); break;
-          case 32: attn_decode_staged_kernel<32><<<grid, threads, stg.smem, s>>>(aa, stg.depth, per_cta); break;
-          case 48: attn_decode_staged_kernel<48><<<grid, threads, stg.smem, s>>>(aa, stg.depth, per_cta); break;
-          default: attn_decode_staged_kernel<64><<<grid, threads, stg.smem, s>>>(aa, stg.depth, per_cta); break;
+          case 4: attn_decode_staged_kernel<4><<<grid, threads, stg.smem, s>>>(aa); break;
+          case 8: attn_decode_staged_kernel<8><<<grid, threads, stg.smem, s>>>(aa); break;
+          case 16: attn_decode_staged_kernel<16><<<grid, threads, stg.smem, s>>>(aa); break;
+          case 32: attn_decode_staged_kernel<32><<<grid, threads, stg.smem, s>>>(aa); break;
+          case 48: attn_decode_staged_kernel<48><<<grid, threads, stg.smem, s>>>(aa); break;
+          default: attn_decode_staged_kernel<64><<<grid, threads, stg.smem, s>>>(aa); break;
         }
       } else if (P == 1) {
         const long long warps = (long long)b.S * m.heads;
