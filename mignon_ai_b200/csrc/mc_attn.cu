@@ -264,7 +264,7 @@ __global__ void __launch_bounds__(kAsMaxWarps * 32) attn_decode_staged_kernel(co
     const float* src = a.kv + ((size_t)a.attn_slot * a.n_sess + s) * 2 * (size_t)cache * D + (size_t)which * cache * D +
                        (size_t)h * cache * DH;
     mbar_arrive_expect_tx(bar, ring_bytes);
-    bulk_load(which ? Vs : Ks, src, ring_bytes, bar);
+    bulk_load_hint(which ? Vs : Ks, src, ring_bytes, bar, l2_policy_evict_first());
   };
   if (lane == 0) {
     issue(0, 0);

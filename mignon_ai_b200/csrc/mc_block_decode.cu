@@ -133,7 +133,8 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
               break;
             }
             mbar_arrive_expect_tx(&bars->w_full[st], kTile);
-            bulk_load(sW + st * kTile, G.tiles + ((size_t)c * G.ktiles + kt) * kTile, kTile, &bars->w_full[st]);
+            bulk_load_hint(sW + st * kTile, G.tiles + ((size_t)c * G.ktiles + kt) * kTile, kTile, &bars->w_full[st],
+                           l2_policy_evict_last());
           }
       }
     }
@@ -164,11 +165,13 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
             tc_fence_after();
             const uint64_t da = smem_desc_sw128(sW + st * kTile);
             const int ksteps = min(4, (G.K - kt * 128 + 31) / 32);
+            // planes innermost: three independent accumulation chains in flight
+            for (int kk = 0; kk < ksteps; ++kk) {
 #pragma unroll
-            for (int p = 0; p < 3; ++p) {
-              const uint64_t db = smem_desc_sw128(sB + (p * KT + kt) * kDBTile);
-              for (int kk = 0; kk < ksteps; ++kk)
+              for (int p = 0; p < 3; ++p) {
+                const uint64_t db = smem_desc_sw128(sB + (p * KT + kt) * kDBTile);
                 mma_i8(tmem + slot * kDSlotCols + p * kDR, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+              }
             }
             mma_commit(&bars->w_empty[st]);
           }
@@ -185,6 +188,8 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
     const int nf = D / 4;
     uint32_t sidx = 0;
     bool ok = true;
+    int tp = 0;
+    trace_point(a, tp++);
     if (t < kDR) {
       const int s = s0 + t;
       const bool v = s < a.n_sess && a.seglen[s] > 0;
@@ -233,10 +238,12 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       for (int c = 0; c < G.nchunks; ++c, ++sidx) {
         const int slot = sidx % kDSlots;
         wait_slot(slot, sidx);
+        if (a.trace_fine) trace_point(a, tp++);
         uint32_t x1[8], x2[8], x3[8];
         acc8(slot, x1, x2, x3);
         release_slot(slot);
         fn(c, stp, x1, x2, x3);
+        if (a.trace_fine) trace_point(a, tp++);
       }
     };
     // Pairs of M-tiles (value/delta tile, gate tile): fn(pair, steps, value planes, gate planes).
@@ -249,10 +256,12 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
         wait_slot(sv, sidx);
         acc8(sv, v1, v2, v3);
         wait_slot(sg, sidx + 1);
+        if (a.trace_fine) trace_point(a, tp++);
         acc8(sg, g1, g2, g3);
         release_slot(sv);
         release_slot(sg);
         fn(c / 2, stp, v1, v2, v3, g1, g2, g3);
+        if (a.trace_fine) trace_point(a, tp++);
       }
     };
     // RMSNorm (nn/rmsnorm.go:14-32) of the cur rows with gain `gain` (null: identity, no norm).
@@ -342,6 +351,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       }
     }
 
+    trace_point(a, tp++);
     // ---- output projection of the previous block's attention: cur += Out att s_out ----
     if (a.has_out) {
 #pragma unroll
@@ -360,6 +370,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
         }
       }
       publish();
+      trace_point(a, tp++);
       tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[8], uint32_t(&x2)[8],
                                 uint32_t(&x3)[8]) {
         const int n = c * 128 + chl;
@@ -423,8 +434,10 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
         }
       }
       // norm cell n, kept in shared memory and sliced for W_select
+      trace_point(a, tp++);
       norm_rows(a.gamma, sNrm, false, nullptr, true);
       publish();
+      trace_point(a, tp++);
       // lambda = sigmoid(W_select n s_sel + base), into the latch-gate rows
       tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[8], uint32_t(&x2)[8],
                                 uint32_t(&x3)[8]) {
@@ -437,6 +450,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
           sAux[(r0 + j) * D + n] = sigmoid_clamped(__fadd_rn(dequant(x1[j], x2[j], x3[j], stp[j], scale), base));
       });
       row_bar_d();
+      trace_point(a, tp++);
       // latch update, ring write, and x = [n | n(pos - dil) | latch] sliced for W1
 #pragma unroll
       for (int u = 0; u < kDRowsPerWarp; ++u) {
@@ -485,6 +499,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
         }
       }
       publish();
+      trace_point(a, tp++);
       // hidden = (W1v x s1 + b1v) * sigmoid(W1g x s1 + b1g)   (applyRule layer 1, stream.go:212-220)
       tiles2(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&v1)[8], uint32_t(&v2)[8],
                                 uint32_t(&v3)[8], uint32_t(&g1)[8], uint32_t(&g2)[8], uint32_t(&g3)[8]) {
@@ -500,6 +515,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
         }
       });
       row_bar_d();
+      trace_point(a, tp++);
       // the hidden rows sliced for W2 (max |hidden| of each row)
       {
         const int hf = H / 4;
@@ -517,6 +533,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
         }
       }
       publish();
+      trace_point(a, tp++);
       // o = W2 hidden s2 + b2; gate = sigmoid(o_gate); cur = (1 - gate) cur + gate o_delta (:222-229)
       tiles2(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&v1)[8], uint32_t(&v2)[8],
                                 uint32_t(&v3)[8], uint32_t(&g1)[8], uint32_t(&g2)[8], uint32_t(&g3)[8]) {
@@ -549,6 +566,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
         }
       }
       publish();
+      trace_point(a, tp++);
       const int dh = a.dh;
       tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[8], uint32_t(&x2)[8],
                                 uint32_t(&x3)[8]) {
@@ -575,6 +593,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       });
     }
 
+    trace_point(a, tp++);
     // ---- final RMSNorm (the head's input) ----
     if (a.final_norm) norm_rows(a.final_gain, a.fnorm, true, a.fnorm_rowmax, false);
 
@@ -594,6 +613,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
         }
       }
     }
+    trace_point(a, tp++);
   }
   tc_fence_before();
   __syncthreads();
