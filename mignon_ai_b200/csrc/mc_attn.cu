@@ -392,8 +392,141 @@ __global__ void __launch_bounds__(kAsMaxWarps * 32) attn_decode_staged_kernel(co
   }
 }
 
-// Prefill: one CTA per session; the segment's keys and values (written by the block kernel to
-// kvlin) are staged into shared memory; one warp per (query, head) item.
+// Prefill: one CTA per session. The segment's keys and values (written by the block kernel to
+// kvlin, [t][K|V][D]) arrive in shared memory by one bulk copy; the warps take the (query, head)
+// items in turn. Per item: lane i scores keys lo+i, lo+i+32, ... (16-byte columns in a per-lane
+// rotation, q read as rotated 16-byte broadcasts), the softmax on warp shuffles, then lanes own
+// (row group, 16-byte column) pairs of the value rows as in the staged decode kernel. max |o| of
+// each row accumulates in shared memory across the heads.
+template <int DH>  // head width: 4, 8, 16, 32, 48 or 64 (32 / (DH / 4) row groups, a power of two)
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_prefill_fast_kernel(const __grid_constant__ AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  float* sm = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  constexpr int NF = DH / 4;
+  constexpr int G = 32 / NF;
+  const int s = blockIdx.x;
+  const int len = a.seglen[s];
+  if (len <= 0) return;
+  const int D = a.D, heads = a.heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float* kvs = sm;                                   // [len][2][D]
+  float* pbuf = kvs + (size_t)len * 2 * D + warp * 128;
+  unsigned int* rmax = reinterpret_cast<unsigned int*>(kvs + (size_t)len * 2 * D + nw * 128);  // [128]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(rmax + 128);
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i < 128; i += blockDim.x) rmax[i] = 0u;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t bytes = (uint32_t)(len * 2 * D * 4);
+    mbar_arrive_expect_tx(bar, bytes);
+    bulk_load(kvs, a.kvlin + (size_t)s * a.P * 2 * D, bytes, bar);
+  }
+  const bool ok = __all_sync(0xffffffffu, mbar_wait_or_abort(bar, 0, kErrWaitFull));
+  const int p0 = a.pos0[s];
+  if (ok) {
+    for (int item = warp; item < len * heads; item += nw) {
+      const int t = item / heads, h = item - (item / heads) * heads;
+      const int pos = p0 + t;
+      int ws = 0;
+      if (a.window > 0 && pos - a.window + 1 > 0) ws = pos - a.window + 1;
+      const int lo = max(max(ws, pos - a.cache + 1), p0) - p0;  // in-segment index of the first key
+      const int span = t - lo + 1;                               // <= 128
+      const int grow = grow_of(a, s, t);
+      const float4* q4 = reinterpret_cast<const float4*>(a.qbuf + (size_t)grow * D + h * DH);
+      float4 qr[NF];
+#pragma unroll
+      for (int f = 0; f < NF; ++f) qr[f] = q4[(f + lane) % NF];
+      float sc[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = lane + 32 * u;
+        float acc = 0.f;
+        if (j < span) {
+          const float4* row = reinterpret_cast<const float4*>(kvs + (size_t)(lo + j) * 2 * D + h * DH);
+#pragma unroll
+          for (int f = 0; f < NF; ++f) {
+            const float4 k4 = row[(f + lane) % NF];
+            acc = __fmaf_rn(qr[f].x, k4.x, acc);
+            acc = __fmaf_rn(qr[f].y, k4.y, acc);
+            acc = __fmaf_rn(qr[f].z, k4.z, acc);
+            acc = __fmaf_rn(qr[f].w, k4.w, acc);
+          }
+        }
+        sc[u] = acc;
+      }
+      float mx = -3.402823466e38f;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (lane + 32 * u < span) {
+          sc[u] = __fmul_rn(sc[u], a.scale);
+          mx = fmaxf(mx, sc[u]);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float sum = 0.f;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (lane + 32 * u < span) {
+          sc[u] = ref_vec_exp(__fsub_rn(sc[u], mx));
+          sum = __fadd_rn(sum, sc[u]);
+        } else {
+          sc[u] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+      const float inv = __fdiv_rn(1.0f, sum);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) pbuf[lane + 32 * u] = __fmul_rn(sc[u], inv);
+      __syncwarp();
+      const int c = lane % NF, g = lane / NF;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (g < G) {
+#pragma unroll 4
+        for (int j = g; j < span; j += G) {
+          const float p = pbuf[j];
+          const float4 v = reinterpret_cast<const float4*>(kvs + (size_t)(lo + j) * 2 * D + D + h * DH)[c];
+          o.x = __fmaf_rn(p, v.x, o.x);
+          o.y = __fmaf_rn(p, v.y, o.y);
+          o.z = __fmaf_rn(p, v.z, o.z);
+          o.w = __fmaf_rn(p, v.w, o.w);
+        }
+      }
+#pragma unroll
+      for (int off = (G / 2) * NF; off >= NF; off >>= 1) {
+        o.x = __fadd_rn(o.x, __shfl_down_sync(0xffffffffu, o.x, off));
+        o.y = __fadd_rn(o.y, __shfl_down_sync(0xffffffffu, o.y, off));
+        o.z = __fadd_rn(o.z, __shfl_down_sync(0xffffffffu, o.z, off));
+        o.w = __fadd_rn(o.w, __shfl_down_sync(0xffffffffu, o.w, off));
+      }
+      float om = 0.f;
+      if (lane < NF) {
+        reinterpret_cast<float4*>(a.att + (size_t)grow * D + h * DH)[lane] = o;
+        om = fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w)));
+      }
+#pragma unroll
+      for (int k = 16; k; k >>= 1) om = fmaxf(om, __shfl_xor_sync(0xffffffffu, om, k));
+      if (lane == 0) atomicMax(&rmax[t], __float_as_uint(om));
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < len; t += blockDim.x) a.att_rowmax[grow_of(a, s, t)] = __uint_as_float(rmax[t]);
+}
+
+inline bool attn_prefill_fast_ok(int dh) { return dh == 4 || dh == 8 || dh == 16 || dh == 32 || dh == 48 || dh == 64; }
+
+inline size_t attn_prefill_fast_smem(int P, int D) {
+  return 128 + (size_t)P * 2 * D * 4 + (size_t)(kAttnThreads / 32) * 128 * 4 + 128 * 4 + 16;
+}
+
+// Prefill (head widths without a fast kernel): one CTA per session; the segment's keys and values
+// (written by the block kernel to kvlin) are staged into shared memory; one warp per (query, head)
+// item.
 __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const __grid_constant__ AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   float* sm = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));

@@ -316,6 +316,12 @@ static int ensure_attrs(int device) {
   MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<48>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
   MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
   MC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+  MC_CUDA(cudaFuncSetAttribute(attn_prefill_fast_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+  MC_CUDA(cudaFuncSetAttribute(attn_prefill_fast_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+  MC_CUDA(cudaFuncSetAttribute(attn_prefill_fast_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+  MC_CUDA(cudaFuncSetAttribute(attn_prefill_fast_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+  MC_CUDA(cudaFuncSetAttribute(attn_prefill_fast_kernel<48>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+  MC_CUDA(cudaFuncSetAttribute(attn_prefill_fast_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
   if (device < 64) g_attr_done[device] = true;
   return kOk;
 }
@@ -574,6 +580,16 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
           case 48: attn_decode_kernel<48><<<grid, kAttnThreads, 0, s>>>(aa); break;
           case 64: attn_decode_kernel<64><<<grid, kAttnThreads, 0, s>>>(aa); break;
           default: attn_decode_kernel<0><<<grid, kAttnThreads, 0, s>>>(aa); break;
+        }
+      } else if (attn_prefill_fast_ok(aa.dh) && attn_prefill_fast_smem(P, m.D) <= 220 * 1024) {
+        const size_t smem = attn_prefill_fast_smem(P, m.D);
+        switch (aa.dh) {
+          case 4: attn_prefill_fast_kernel<4><<<b.S, kAttnThreads, smem, s>>>(aa); break;
+          case 8: attn_prefill_fast_kernel<8><<<b.S, kAttnThreads, smem, s>>>(aa); break;
+          case 16: attn_prefill_fast_kernel<16><<<b.S, kAttnThreads, smem, s>>>(aa); break;
+          case 32: attn_prefill_fast_kernel<32><<<b.S, kAttnThreads, smem, s>>>(aa); break;
+          case 48: attn_prefill_fast_kernel<48><<<b.S, kAttnThreads, smem, s>>>(aa); break;
+          default: attn_prefill_fast_kernel<64><<<b.S, kAttnThreads, smem, s>>>(aa); break;
         }
       } else {
         const size_t smem = (size_t)P * 2 * m.D * 4 + 32 * 4 + 16 + 128;
