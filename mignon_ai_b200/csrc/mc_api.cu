@@ -283,7 +283,27 @@ int mc_prefill(mc_batch* b, const int32_t* tokens, const int32_t* lens, int stri
     MC_CUDA(cudaSetDevice(sh->m->device));
     if ((st = ensure_step_outputs(*sh, logits != nullptr, 1)) != kOk) return st;
     MC_CUDA(cudaMemsetAsync(sh->step, 0, 4, sh->stream));
+    // MC_TRACE=1: phase timestamps of CTA 0 of every block-kernel launch, printed to stderr.
+    const bool trace = getenv("MC_TRACE") != nullptr;
+    const int nb = (int)sh->m->blocks.size() + 1;
+    if (trace) {
+      MC_CUDA(cudaMalloc(&sh->trace, (size_t)64 * nb * 8));
+      MC_CUDA(cudaMemsetAsync(sh->trace, 0, (size_t)64 * nb * 8, sh->stream));
+    }
     if ((st = enqueue_forward(*sh, P, 0, 0.0, 0, logits != nullptr, true)) != kOk) return st;
+    if (trace) {
+      std::vector<unsigned long long> tr((size_t)64 * nb);
+      MC_CUDA(cudaStreamSynchronize(sh->stream));
+      MC_CUDA(cudaMemcpy(tr.data(), sh->trace, tr.size() * 8, cudaMemcpyDeviceToHost));
+      cudaFree(sh->trace);
+      sh->trace = nullptr;
+      for (int b2 = 0; b2 < nb; ++b2) {
+        fprintf(stderr, "prefill block launch %d phase ns:", b2);
+        for (int i = 1; i < 64 && tr[(size_t)64 * b2 + i]; ++i)
+          fprintf(stderr, " %llu", tr[(size_t)64 * b2 + i] - tr[(size_t)64 * b2 + i - 1]);
+        fprintf(stderr, "\n");
+      }
+    }
   }
   return copy_step_outputs(b, logits, next, prob);
 }

@@ -623,57 +623,74 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
         }
         row_bar();
       } else {
-        // ---- prefill: latch scan and left neighbours, channel-parallel over segment rows ----
-        for (int i = t; i < kRowWarps * kRows; i += kRowThreads) (&bars->rowmax_warp[0][0])[i] = 0.f;
-        row_bar();
-        for (int d = t; d < ((D + 31) & ~31); d += kRowThreads) {
-          const bool act = d < D;
-          for (int slot = 0; slot < a.spt; ++slot) {
-            const int sess = tile * a.spt + slot;
-            if (sess >= a.n_sess) break;
-            const int len = a.seglen[sess];
-            if (len <= 0) continue;
-            const int p0 = a.pos0[sess];
-            const size_t st_off = ((size_t)sess * a.total_steps + bs);
-            float l = (p0 == 0 || !act) ? 0.f : a.latch[st_off * D + d];
-            const float* rg = a.norm_ring + st_off * a.ring * D + d;
-            const int row0 = tile * kRows + slot * a.P;
-            for (int tt = 0; tt < len; ++tt) {
-              float* x = a.xbuf + (size_t)(row0 + tt) * 3 * D;
-              float nv = 0.f, left = 0.f;
-              if (act) {
-                const float lam = x[2 * D + d];
-                nv = x[d];
-                if (tt >= dil) left = a.xbuf[(size_t)(row0 + tt - dil) * 3 * D + d];
-                else if (p0 + tt - dil >= 0) left = rg[(size_t)((p0 + tt - dil) % a.ring) * D];
-                l = __fadd_rn(__fmul_rn(lam, l), __fmul_rn(__fsub_rn(1.0f, lam), nv));
-                x[2 * D + d] = l;
-                x[D + d] = left;
-              }
-              const float m = warp_max(act ? fmaxf(fabsf(nv), fmaxf(fabsf(l), fabsf(left))) : 0.f);
-              if (lane == 0) {
-                float* pm = &bars->rowmax_warp[warp][slot * a.P + tt];
-                *pm = fmaxf(*pm, m);
+        // ---- prefill: latch scan, left neighbours, ring write and row maxima, in passes ----
+        // (1) the latch recurrence over the segment, one thread per (session slot, channel), with
+        //     lambda and n of 8 positions loaded ahead of each run of steps
+        for (int task = t; task < a.spt * D; task += kRowThreads) {
+          const int slot = task / D, d = task - slot * D;
+          const int sess = tile * a.spt + slot;
+          if (sess >= a.n_sess) continue;
+          const int len = a.seglen[sess];
+          if (len <= 0) continue;
+          const int p0 = a.pos0[sess];
+          const size_t st_off = ((size_t)sess * a.total_steps + bs);
+          float l = p0 == 0 ? 0.f : a.latch[st_off * D + d];
+          float* x0 = a.xbuf + (size_t)(tile * kRows + slot * a.P) * 3 * D + d;
+          for (int c0 = 0; c0 < len; c0 += 8) {
+            float lam[8], nv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const bool in = c0 + i < len;
+              lam[i] = in ? x0[(size_t)(c0 + i) * 3 * D + 2 * D] : 0.f;
+              nv[i] = in ? x0[(size_t)(c0 + i) * 3 * D] : 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              if (c0 + i < len) {
+                l = __fadd_rn(__fmul_rn(lam[i], l), __fmul_rn(__fsub_rn(1.0f, lam[i]), nv[i]));
+                x0[(size_t)(c0 + i) * 3 * D + 2 * D] = l;
               }
             }
-            if (act) a.latch[st_off * D + d] = l;
           }
+          a.latch[st_off * D + d] = l;
+        }
+        // (2) left neighbours n(pos - dil): from the segment, or from the ring before it
+        for (int idx = t; idx < kRows * D; idx += kRowThreads) {
+          const int rr = idx / D, d = idx - rr * D;
+          if (!bars->rvalid[rr]) continue;
+          const int slot = rr / a.P, tt = rr - slot * a.P;
+          const int sess = tile * a.spt + slot;
+          const int p0 = a.pos0[sess];
+          float* x = a.xbuf + (size_t)(tile * kRows + rr) * 3 * D;
+          float left = 0.f;
+          if (tt >= dil) left = a.xbuf[(size_t)(tile * kRows + rr - dil) * 3 * D + d];
+          else if (p0 + tt - dil >= 0)
+            left = a.norm_ring[((size_t)sess * a.total_steps + bs) * a.ring * D + (size_t)((p0 + tt - dil) % a.ring) * D + d];
+          x[D + d] = left;
         }
         row_bar();
-        for (int d = t; d < D; d += kRowThreads)
-          for (int slot = 0; slot < a.spt; ++slot) {
-            const int sess = tile * a.spt + slot;
-            if (sess >= a.n_sess) break;
-            const int len = a.seglen[sess];
-            const int p0 = a.pos0[sess];
-            float* rg = a.norm_ring + ((size_t)sess * a.total_steps + bs) * a.ring * D + d;
-            for (int tt = max(0, len - a.ring); tt < len; ++tt)
-              rg[(size_t)((p0 + tt) % a.ring) * D] = a.xbuf[(size_t)(tile * kRows + slot * a.P + tt) * 3 * D + d];
-          }
-        if (h == 0) {
+        // (3) the ring keeps the segment's last norm cells
+        for (int task = t; task < a.spt * D; task += kRowThreads) {
+          const int slot = task / D, d = task - slot * D;
+          const int sess = tile * a.spt + slot;
+          if (sess >= a.n_sess) continue;
+          const int len = a.seglen[sess];
+          const int p0 = a.pos0[sess];
+          float* rg = a.norm_ring + ((size_t)sess * a.total_steps + bs) * a.ring * D + d;
+          for (int tt = max(0, len - a.ring); tt < len; ++tt)
+            rg[(size_t)((p0 + tt) % a.ring) * D] = a.xbuf[(size_t)(tile * kRows + slot * a.P + tt) * 3 * D + d];
+        }
+        // (4) max |x| of each row, one warp per row
+#pragma unroll 2
+        for (int u = 0; u < kRowsPerWarp; ++u) {
+          const int rr = warp + kRowWarps * u;
           float m = 0.f;
-          for (int w = 0; w < kRowWarps; ++w) m = fmaxf(m, bars->rowmax_warp[w][r]);
-          bars->rowmax_a[r] = m;
+          if (bars->rvalid[rr]) {
+            const float* x = a.xbuf + (size_t)(tile * kRows + rr) * 3 * D;
+            for (int e = lane; e < 3 * D; e += 32) m = fmaxf(m, fabsf(x[e]));
+          }
+          m = warp_max(m);
+          if (lane == 0) bars->rowmax_a[rr] = m;
         }
         row_bar();
       }
