@@ -288,11 +288,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
             tc_fence_after();
             const uint64_t db = smem_desc_sw128(sB + st * kTile);
             const int ksteps = min(4, (G.K - kt * 128 + 31) / 32);
+            // planes innermost: three independent accumulation chains in flight
+            for (int kk = 0; kk < ksteps; ++kk) {
 #pragma unroll
-            for (int p = 0; p < 3; ++p) {
-              const uint64_t da = smem_desc_sw128(sA + slot * kASlot + p * kTile);
-              for (int kk = 0; kk < ksteps; ++kk)
+              for (int p = 0; p < 3; ++p) {
+                const uint64_t da = smem_desc_sw128(sA + slot * kASlot + p * kTile);
                 mma_i8(tmem + p * kNC, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+              }
             }
             mma_commit(&bars->b_empty[st]);
             if (!resident || c == G.nchunks - 1) mma_commit(&bars->a_empty[slot]);
