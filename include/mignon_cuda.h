@@ -117,6 +117,14 @@ int mc_prefill(mc_batch* batch, const int32_t* tokens, const int32_t* lens, int 
  * token and its probability. */
 int mc_append(mc_batch* batch, const int32_t* tokens, float* logits, int32_t* next, float* prob);
 
+/* Per-token log-probabilities of whole sequences (the scoring workload): session s restarts from
+ * seqs[s*stride .. s*stride+lens[s]) and out[s*(stride-1) + t] = log p(seqs[t+1] | seqs[0..t])
+ * for t < lens[s]-1 — logProb (internal/eval/suite.go:201-209) of the logits Call(prefix) gives
+ * (model.go:122-132), all prefixes in one prefill pass; other entries are 0. Requires
+ * lens[s] <= the sessions' window and the batch's max_prompt, and target ids inside the
+ * vocabulary. Afterwards the sessions continue as after mc_prefill of the same tokens. */
+int mc_score(mc_batch* batch, const int32_t* seqs, const int32_t* lens, int stride, double* out);
+
 /* The decode loop of generate.greedyLoop (internal/generate/greedy.go:63-87) without stop tokens,
  * or with temperature > 0 the sampled loop of sampleContinuation (generate/sample.go:196-247)
  * with top-k = the batch's top_k, no repetition penalty, top-p 1: prefill each prompt, then

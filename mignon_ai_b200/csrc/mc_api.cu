@@ -308,6 +308,62 @@ int mc_prefill(mc_batch* b, const int32_t* tokens, const int32_t* lens, int stri
   return copy_step_outputs(b, logits, next, prob);
 }
 
+int mc_score(mc_batch* b, const int32_t* seqs, const int32_t* lens, int stride, double* out) {
+  clear_error();
+  if (!b || !seqs || !lens || !out) return set_error(kInvalidArgument, "mc_score: null argument");
+  if (stride < 1) return set_error(kInvalidArgument, "mc_score: stride < 1");
+  const int V = b->model->dev[0]->V;
+  for (int s = 0; s < b->count; ++s) {
+    if (lens[s] < 0 || lens[s] > stride) return set_error(kInvalidArgument, "mc_score: length outside [0, stride]");
+    if (lens[s] > b->window)
+      return set_error(kInvalidArgument, "mc_score: sequence " + std::to_string(s) + " is longer than the session window");
+    for (int t = 1; t < lens[s]; ++t)
+      if (seqs[(size_t)s * stride + t] < 0 || seqs[(size_t)s * stride + t] >= V)
+        return set_error(kInvalidArgument, "mc_score: target token outside the vocabulary");
+  }
+  int P = 1;
+  int st = upload_prompts(b, seqs, lens, stride, &P);
+  if (st != kOk) return st;
+  const int cols = stride - 1;
+  std::fill(out, out + (size_t)b->count * cols, 0.0);
+  for (size_t g = 0; g < b->shard.size(); ++g) {
+    DevBatch& sh = *b->shard[g];
+    if (sh.S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh.m->device));
+    const int s0 = b->first[g];
+    const size_t rows = (size_t)sh.S * P;
+    if ((st = ensure_score_rows(sh, rows)) != kOk) return st;
+    // row r = i * P + t: the final-normed row of position t of session i, target token t + 1
+    const int spt = std::max(1, 128 / P);
+    std::vector<int32_t> rowmap(rows), target(rows, 0), valid(rows, 0), pos(sh.S), seglen(sh.S);
+    for (int i = 0; i < sh.S; ++i) {
+      const int n = lens[s0 + i];
+      for (int t = 0; t < P; ++t) {
+        const size_t r = (size_t)i * P + t;
+        rowmap[r] = (i / spt) * 128 + (i % spt) * P + t;
+        if (t + 1 < n) {
+          target[r] = seqs[(size_t)(s0 + i) * stride + t + 1];
+          valid[r] = 1;
+        }
+      }
+      pos[i] = n;  // afterwards the sessions continue as after mc_prefill of the same tokens
+      seglen[i] = n > 0 ? 1 : 0;
+    }
+    MC_CUDA(cudaMemcpyAsync(sh.sc_rowmap, rowmap.data(), rows * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.sc_target, target.data(), rows * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.sc_valid, valid.data(), rows * 4, cudaMemcpyHostToDevice, sh.stream));
+    if ((st = enqueue_score(sh, P, rows)) != kOk) return st;
+    std::vector<double> lp(rows);
+    MC_CUDA(cudaMemcpyAsync(lp.data(), sh.sc_logprob, rows * 8, cudaMemcpyDeviceToHost, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.pos, pos.data(), sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.seglen, seglen.data(), sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    if ((st = check_device_error(sh.stream)) != kOk) return st;  // synchronizes the stream
+    for (int i = 0; i < sh.S; ++i)
+      for (int t = 0; t + 1 < lens[s0 + i]; ++t) out[(size_t)(s0 + i) * cols + t] = lp[(size_t)i * P + t];
+  }
+  return kOk;
+}
+
 int mc_append(mc_batch* b, const int32_t* tokens, float* logits, int32_t* next, float* prob) {
   clear_error();
   if (!b || !tokens) return set_error(kInvalidArgument, "mc_append: null argument");

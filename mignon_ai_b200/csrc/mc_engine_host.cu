@@ -260,6 +260,12 @@ struct DevBatch {
   int32_t* out_tok = nullptr;
   float* out_prob = nullptr;
   double* out_logprob = nullptr;
+  // scoring (every row of a segment through the head): per-row scratch, grown on demand
+  size_t sc_rows = 0;
+  int sc_nsplit = 1;
+  int32_t *sc_rowmap = nullptr, *sc_target = nullptr, *sc_valid = nullptr, *sc_next = nullptr;
+  float4* sc_part = nullptr;
+  double* sc_logprob = nullptr;
   int out_stride = 0;
   cudaGraphExec_t graph = nullptr;
   // Everything the captured decode step bakes in; a change forces a new capture.
@@ -468,10 +474,9 @@ __global__ void prepare_prompts_kernel(const int32_t* prompts, const int32_t* le
   rowmap[s] = (s / spt) * 128 + (s % spt) * P + max(n - 1, 0);
 }
 
-// Enqueues the whole forward pass of one segment (P rows per session; P = 1 is a decode step)
-// followed by the head and token selection.
-int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t session0, bool want_logits,
-                    bool advance_from_len, LaunchLog* log = nullptr) {
+// Enqueues the blocks (and attention sublayers) of one segment: P rows per session, P = 1 a decode
+// step; ends with the final RMSNorm of every row.
+static int enqueue_layers(DevBatch& b, int P, LaunchLog* log) {
   const DevModel& m = *b.m;
   cudaStream_t s = b.stream;
   const int nb = (int)m.blocks.size();
@@ -600,6 +605,17 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
       if (log) log->record(s, 1);
     }
   }
+  return kOk;
+}
+
+// Enqueues the whole forward pass of one segment (P rows per session; P = 1 is a decode step)
+// followed by the head and token selection.
+int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t session0, bool want_logits,
+                    bool advance_from_len, LaunchLog* log = nullptr) {
+  const DevModel& m = *b.m;
+  cudaStream_t s = b.stream;
+  int st = enqueue_layers(b, P, log);
+  if (st != kOk) return st;
   HeadArgs h;
   memset(&h, 0, sizeof(h));
   h.n_sess = b.S;
@@ -651,6 +667,64 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
   bump_kernel<<<1, 1, 0, s>>>(b.step);
   MC_CUDA(cudaGetLastError());
   if (log) log->record(s, 5);
+  return kOk;
+}
+
+// Scoring rows: every row of the last segment goes through the head with the next token of its
+// sequence as target; select_kernel writes logProb (internal/eval/suite.go:201-209) per row.
+int ensure_score_rows(DevBatch& b, size_t rows) {
+  if (rows <= b.sc_rows) return kOk;
+  const DevModel& m = *b.m;
+  // at most 16 chunks per CTA (the head kernel stages their biases in shared memory)
+  b.sc_nsplit = std::max(1, (m.head.nchunks + 15) / 16);
+  int st;
+  if ((st = b.alloc(b.sc_rowmap, rows * 4)) || (st = b.alloc(b.sc_target, rows * 4)) ||
+      (st = b.alloc(b.sc_valid, rows * 4)) || (st = b.alloc(b.sc_next, rows * 4)) ||
+      (st = b.alloc(b.sc_part, rows * b.sc_nsplit * 4 * sizeof(float4))) || (st = b.alloc(b.sc_logprob, rows * 8)))
+    return st;
+  b.sc_rows = rows;
+  return kOk;
+}
+
+// The forward pass of a prompt segment (P rows per session) and the log-probability of every
+// row's target: sc_logprob[r] for the rows r with sc_valid[r] != 0.
+int enqueue_score(DevBatch& b, int P, size_t rows) {
+  const DevModel& m = *b.m;
+  cudaStream_t s = b.stream;
+  int st = enqueue_layers(b, P, nullptr);
+  if (st != kOk) return st;
+  HeadArgs h;
+  memset(&h, 0, sizeof(h));
+  h.n_sess = (int)rows;
+  h.D = m.D;
+  h.V = m.V;
+  h.nsplit = b.sc_nsplit;
+  h.nchunks = m.head.nchunks;
+  h.cps = (m.head.nchunks + b.sc_nsplit - 1) / b.sc_nsplit;
+  h.ktiles = m.head.ktiles;
+  h.rowmap = b.sc_rowmap;
+  h.fnorm = b.fnorm;
+  h.fnorm_rowmax = b.fnorm_rowmax;
+  h.tiles = m.head.tiles;
+  h.scale = m.head.scale;
+  h.head_b = m.head_b;
+  h.target = b.sc_target;
+  h.part = b.sc_part;
+  dim3 hg((unsigned)((rows + 127) / 128), b.sc_nsplit);
+  head_kernel<<<hg, kHeadThreads, kHeadSmem, s>>>(h);
+  MC_CUDA(cudaGetLastError());
+  SelectArgs sa;
+  memset(&sa, 0, sizeof(sa));
+  sa.n_sess = (int)rows;
+  sa.nsplit = b.sc_nsplit * 4;
+  sa.mode = 2;
+  sa.part = b.sc_part;
+  sa.out_stride = 1;
+  sa.next_tok = b.sc_next;
+  sa.out_logprob = b.sc_logprob;
+  sa.seglen = b.sc_valid;  // rows without a target are skipped
+  select_kernel<<<(unsigned)((rows + 127) / 128), 128, 0, s>>>(sa);
+  MC_CUDA(cudaGetLastError());
   return kOk;
 }
 

@@ -32,6 +32,7 @@ _lib.register({
     "mc_batch_open": [c_vp, _i, _i, _i, _i, ctypes.POINTER(c_vp)],
     "mc_batch_close": [c_vp],
     "mc_prefill": [c_vp, c_vp, c_vp, _i, c_vp, c_vp, c_vp],
+    "mc_score": [c_vp, c_vp, c_vp, _i, c_vp],
     "mc_append": [c_vp, c_vp, c_vp, c_vp, c_vp],
     "mc_generate": [c_vp, c_vp, c_vp, _i, _i, ctypes.c_double, ctypes.c_uint32, c_vp, c_vp],
 })
@@ -170,6 +171,17 @@ class SessionBatch:
         prob = np.zeros(self.count, np.float32)
         _lib.check(_lib.lib().mc_append(self._h, _lib.ptr(t), _lib.ptr(logits), _lib.ptr(nxt), _lib.ptr(prob)))
         return logits, nxt, prob
+
+    def score(self, seqs, lens=None):
+        """Per-token log-probabilities: out[s, t] = log p(seqs[s, t+1] | seqs[s, :t+1]) for
+        t < lens[s] - 1 (eval.logProb over every prefix, one prefill pass); other entries 0."""
+        q = np.ascontiguousarray(seqs, np.int32)
+        if q.ndim == 1:
+            q = q[None, :]
+        lens = np.full(self.count, q.shape[1], np.int32) if lens is None else np.ascontiguousarray(lens, np.int32)
+        out = np.zeros((self.count, max(q.shape[1] - 1, 0)), np.float64)
+        _lib.check(_lib.lib().mc_score(self._h, _lib.ptr(q), _lib.ptr(lens), q.shape[1], _lib.ptr(out)))
+        return out
 
     def generate(self, prompts, lens, n_new: int, temperature: float = 0.0, session0: int = 0):
         p = np.ascontiguousarray(prompts, np.int32)

@@ -166,6 +166,37 @@ def test_sampling_matches_oracle(oracle):
         assert t >= 0
 
 
+def test_score_matches_oracle(oracle):
+    """mc_score on config-4 shapes (D=192, 6 blocks x 2 rule steps, dilation up to 32, attention
+    4 x 48): the log-probability of every next token from one prefill pass, against the oracle's
+    logProb of Call(prefix) for every prefix (eval/suite.go:201-209). log p = l_t - logsumexp(l)
+    moves by at most 2 max|dlogit|, so the bar is 2e-3 * max|logit|. Ragged, one-token and empty
+    sequences included; afterwards the sessions continue like prefilled ones."""
+    spec = small_spec(4, vocab=512)
+    data = synth.build_model_file(spec)
+    om, gm = oracle.Model(data), quant.Model.decode(data)
+    n, L = 24, 64
+    seqs = synth.prompts_uniform_fast(n, L, spec.vocab, seed=4)
+    want = om.score(seqs)
+    lens = np.full(n, L, np.int32)
+    lens[5], lens[9], lens[11] = 1, 0, 30
+    b = gm.new_batch(n, 0, L)
+    got = b.score(seqs, lens)
+    scale = max(float(np.max(np.abs(om.call(seqs[s])))) for s in range(4))
+    for s in range(n):
+        k = max(int(lens[s]) - 1, 0)
+        err = float(np.max(np.abs(got[s, :k] - want[s, :k]), initial=0.0))
+        assert err <= 2e-3 * scale, f"sequence {s}: max |dlogprob| {err:.3g} > {2e-3 * scale:.3g}"
+        assert np.all(got[s, k:] == 0.0)
+    # continuation: session 0 appends one token as after a prefill of its sequence
+    tok = np.full(n, 7, np.int32)
+    logits, _, _ = b.append(tok, want_logits=True)
+    os_ = om.new_session(0)
+    os_.prefill(seqs[0])
+    check_logits(logits[0], os_.append(7), "append after score")
+    b.close()
+
+
 @pytest.mark.parametrize("cfg,vocab", [(2, None), (1, None)])
 def test_decode_kernel_matches_block_kernel_bitwise(monkeypatch, cfg, vocab):
     """Decode steps run on block_decode_kernel (weights on the MMA's M side, 32 sessions per CTA);
