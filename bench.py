@@ -34,9 +34,9 @@ PROMPT = 48
 NEW = 80
 PROMPT_SEED = 2
 METRIC = "generated tokens/s, batched INT8 sessions"
-# DRAM bytes (read + write) per session of one attn_decode_kernel launch, from an ncu capture of
-# the 1024-session case (58.63 MB / 1024); traffic grows with the session count.
-ATTN_DRAM_BYTES_PER_SESSION = 57256
+# DRAM bytes (read + write) of one attention launch per session, from an ncu capture of the
+# full 4096-session launch (273.4 MB / 4096, profiles/attn_decode_staged_kernel_config2.md).
+ATTN_DRAM_BYTES_PER_SESSION = 66739
 UNIT = "tokens/s"
 
 
@@ -128,7 +128,7 @@ def run_cpu_reference(steps, warmup, sessions=None, label="reference"):
     import pyoracle
     from mignon_ai_b200 import synth
     cores = os.cpu_count() or 1
-    n = sessions or max(64, 64 * cores)
+    n = sessions or max(640, 640 * cores)  # about 10 s of CPU work at ~5K tokens/s per core
     data = synth.build_model_file(synth.CONFIGS[CONFIG])
     om = pyoracle.Model(data)
     prompts = prompts_for(0, n)
@@ -289,7 +289,7 @@ def main():
     per_kind = {}
     for k, t in zip(kinds[:n], ms_arr[:n]):
         per_kind.setdefault(int(k), []).append(float(t))
-    names = {0: "block_kernel", 1: "attn_decode_kernel", 2: "block_kernel(final)", 3: "head_kernel",
+    names = {0: "block_decode_kernel", 1: "attn_decode_staged_kernel", 2: "block_decode_kernel(final)", 3: "head_kernel",
              4: "select_kernel", 5: "bump_kernel"}
     peaks = {}
     try:
@@ -323,12 +323,12 @@ def main():
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(world * (prompts.nbytes + lens.nbytes)),
                     "d2h_bytes_per_step": int(world * (h_tok.nbytes + h_prob.nbytes)), "matches_value_run": same},
             "gpu_launches": int(launches_per_job * args.steps),
-            "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel", "achieved": achieved, "peak": hbm_peak,
+            "roofline": {"bound": "hbm", "kernel": "attn_decode_staged_kernel", "achieved": achieved, "peak": hbm_peak,
                          "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s",
                          "traffic": ATTN_DRAM_BYTES_PER_SESSION * S,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at 1024 "
-                                           "sessions, scaled by sessions (profiles/attn_decode_kernel_1024sessions.md)",
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a full-size launch "
+                                           "(profiles/attn_decode_staged_kernel_config2.md)",
                          "algorithmic_bytes_per_launch": attn_bytes, "avg_launch_ms": attn_ms},
             "decode_step_profile": {"ms_total": float(step_ms), "share": shares,
                                     "ms_per_kind": {names.get(k, str(k)): float(np.mean(v)) for k, v in per_kind.items()}},
