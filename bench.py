@@ -322,7 +322,7 @@ def main():
             "clocks": clk,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(world * (prompts.nbytes + lens.nbytes)),
                     "d2h_bytes_per_step": int(world * (h_tok.nbytes + h_prob.nbytes)), "matches_value_run": same},
-            "gpu_launches": int(launches_per_job * args.steps),
+            "gpu_launches": int(launches_per_job * args.steps * world),  # all ranks
             "roofline": {"bound": "hbm", "kernel": "attn_decode_staged_kernel", "achieved": achieved, "peak": hbm_peak,
                          "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s",
