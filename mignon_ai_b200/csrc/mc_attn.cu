@@ -237,9 +237,9 @@ __global__ void __launch_bounds__(kAsMaxWarps * 32) attn_decode_staged_kernel(co
   uint64_t* vfull = kfull + 1;
   // item m of this warp: base + stride * m (the whole grid walks the items in order, so the rings
   // read at any moment form one contiguous region)
-  const long long items = (long long)a.n_sess * heads;
-  const long long base = blockIdx.x + (long long)gridDim.x * warp;
-  const long long stride = (long long)gridDim.x * nwarps;
+  const int items = a.n_sess * heads;  // < 2^31 (checked by the launcher)
+  const int base = blockIdx.x + gridDim.x * warp;
+  const int stride = gridDim.x * nwarps;
   const int nm = base < items ? (int)((items - base + stride - 1) / stride) : 0;
   if (lane == 0) {
     mbar_init(kfull, 1);
@@ -254,8 +254,8 @@ __global__ void __launch_bounds__(kAsMaxWarps * 32) attn_decode_staged_kernel(co
   auto issue = [&](int m, int which) {
     if (m >= nm) return;
     issued[which] = m + 1;
-    const long long it = base + stride * m;
-    const int s = (int)(it / heads), h = (int)(it - (long long)s * heads);
+    const int it = base + stride * m;
+    const int s = it / heads, h = it - s * heads;
     uint64_t* bar = which ? vfull : kfull;
     if (a.seglen[s] <= 0) {
       mbar_arrive(bar);
@@ -273,8 +273,8 @@ __global__ void __launch_bounds__(kAsMaxWarps * 32) attn_decode_staged_kernel(co
 
   bool healthy = true;  // false after a wait gave up: issue nothing more, drain what is in flight
   for (int m = 0; m < nm; ++m) {
-    const long long it = base + stride * m;
-    const int s = (int)(it / heads), h = (int)(it - (long long)s * heads);
+    const int it = base + stride * m;
+    const int s = it / heads, h = it - s * heads;
     const bool active = a.seglen[s] > 0;
     const int pos = a.pos0[s];
     int ws = 0;
@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(kAsMaxWarps * 32) attn_decode_staged_kernel(co
     const int lo = max(ws, pos - cache + 1);
     const int span = pos - lo + 1;  // <= cache <= 128
     const int lo_slot = lo % cache;
-    const int grow = grow_of(a, s, 0);
+    const int grow = s;  // decode: the q and output row of session s is row s
     const float* q = a.qbuf + (size_t)grow * D + h * DH;
     float4 qr[NF];  // q rotated like the key reads: qr[f] = q4[(f + lane) % NF]
     if (active) {

@@ -565,7 +565,7 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log) {
       aa.att_rowmax = b.att_rowmax;
       aa.scale = (float)(1.0 / std::sqrt((double)aa.dh));
       const AttnStaging stg = attn_staging(m.cache, aa.dh);
-      if (P == 1 && stg.warps > 0 && stg.smem <= kAsSmemMax) {
+      if (P == 1 && stg.warps > 0 && stg.smem <= kAsSmemMax && (long long)b.S * m.heads < (1LL << 31)) {
         const long long items = (long long)b.S * m.heads;
         const int grid = (int)std::min<long long>((items + stg.warps - 1) / stg.warps, b.n_sm);
         const int threads = stg.warps * 32;
