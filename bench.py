@@ -290,7 +290,7 @@ def main():
     for k, t in zip(kinds[:n], ms_arr[:n]):
         per_kind.setdefault(int(k), []).append(float(t))
     names = {0: "block_decode_kernel", 1: "attn_decode_staged_kernel", 2: "block_decode_kernel(final)", 3: "head_kernel",
-             4: "select_kernel", 5: "bump_kernel"}
+             4: "select_kernel"}
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -306,7 +306,8 @@ def main():
     step_ms = sum(ms_arr[:n])
     shares = {names.get(k, str(k)): round(sum(v) / step_ms, 4) for k, v in per_kind.items()}
 
-    launches_per_job = (1 + 2 * 4 + 1 + 3) + (NEW - 1) * (2 * 4 + 1 + 3)
+    # prefill: prompt preparation, 4 x (block + attention), final block, head, select; decode steps likewise
+    launches_per_job = (1 + 2 * 4 + 1 + 2) + (NEW - 1) * (2 * 4 + 1 + 2)
 
     out = None
     if rank == 0:

@@ -147,8 +147,8 @@ int mc_batch_stream(mc_batch* batch, int shard, void** stream);
 int mc_batch_error(mc_batch* batch);
 
 /* Runs one greedy decode step of a single-device batch launch by launch, timing each launch with
- * CUDA events: ms[i] and kinds[i] (0 block, 1 attention, 2 final block, 3 head, 4 select,
- * 5 step counter) for i < *n_launches <= max_launches. The step advances the sessions. */
+ * CUDA events: ms[i] and kinds[i] (0 block, 1 attention, 2 final block, 3 head, 4 select) for
+ * i < *n_launches <= max_launches. The step advances the sessions. */
 int mc_profile_step(mc_batch* batch, int max_launches, float* ms, int32_t* kinds, int* n_launches);
 
 #ifdef __cplusplus

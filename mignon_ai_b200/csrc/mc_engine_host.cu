@@ -5,7 +5,7 @@
 // CUDA graph:
 //   for each block b: block_kernel(b) [+ attn_decode_kernel(b)]
 //   block_kernel(final: last output projection + final RMSNorm)
-//   head_kernel (vocabulary split across CTAs) -> select_kernel -> bump_kernel
+//   head_kernel (vocabulary split across CTAs) -> select_kernel (also advances the step counter)
 // Prefill runs the same kernels layer-major over whole prompt segments (attn_prefill_kernel).
 #include <algorithm>
 #include <cmath>
@@ -248,6 +248,7 @@ struct DevBatch {
   size_t rows = 0;  // scratch rows
   cudaStream_t stream = nullptr;
   std::vector<void*> allocs;
+  int32_t* sel_done = nullptr;  // select_kernel's finished-block counter (zero between launches)
   int32_t *pos = nullptr, *seglen = nullptr, *tok = nullptr, *next_tok = nullptr, *step = nullptr, *rowmap = nullptr,
           *rowmap_id = nullptr, *target = nullptr;
   float *norm_ring = nullptr, *latch = nullptr, *kv = nullptr;
@@ -360,7 +361,7 @@ int batch_create(DevModel* m, int S, int window, int pmax, int topk, std::unique
   MC_CUDA(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
   const size_t R = b->rows;
   if ((st = b->alloc(b->pos, S * 4)) || (st = b->alloc(b->seglen, S * 4)) || (st = b->alloc(b->tok, (size_t)S * b->pmax * 4)) ||
-      (st = b->alloc(b->next_tok, S * 4)) || (st = b->alloc(b->step, 4)) || (st = b->alloc(b->rowmap, S * 4)) ||
+      (st = b->alloc(b->next_tok, S * 4)) || (st = b->alloc(b->step, 4)) || (st = b->alloc(b->sel_done, 4)) || (st = b->alloc(b->rowmap, S * 4)) ||
       (st = b->alloc(b->rowmap_id, S * 4)) || (st = b->alloc(b->target, S * 4)))
     return st;
   if ((st = b->alloc(b->norm_ring, (size_t)S * m->total_steps * m->ring * D * 4)) ||
@@ -379,6 +380,7 @@ int batch_create(DevModel* m, int S, int window, int pmax, int topk, std::unique
   MC_CUDA(cudaMemsetAsync(b->pos, 0, S * 4, b->stream));
   MC_CUDA(cudaMemsetAsync(b->seglen, 0, S * 4, b->stream));
   MC_CUDA(cudaMemsetAsync(b->step, 0, 4, b->stream));
+  MC_CUDA(cudaMemsetAsync(b->sel_done, 0, 4, b->stream));
   MC_CUDA(cudaMemsetAsync(b->latch, 0, (size_t)S * m->total_steps * D * 4, b->stream));
   std::vector<int32_t> id(S);
   for (int i = 0; i < S; ++i) id[i] = i;
@@ -661,12 +663,10 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
   sa.pos = b.pos;
   sa.seglen = b.seglen;
   sa.advance_from_len = advance_from_len ? 1 : 0;
-  select_kernel<<<(b.S + 127) / 128, 128, 0, s>>>(sa);
+  sa.done = b.sel_done;  // the last block advances the step counter
+  select_kernel<<<(b.S + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, s>>>(sa);
   MC_CUDA(cudaGetLastError());
   if (log) log->record(s, 4);
-  bump_kernel<<<1, 1, 0, s>>>(b.step);
-  MC_CUDA(cudaGetLastError());
-  if (log) log->record(s, 5);
   return kOk;
 }
 
@@ -723,7 +723,7 @@ int enqueue_score(DevBatch& b, int P, size_t rows) {
   sa.next_tok = b.sc_next;
   sa.out_logprob = b.sc_logprob;
   sa.seglen = b.sc_valid;  // rows without a target are skipped
-  select_kernel<<<(unsigned)((rows + 127) / 128), 128, 0, s>>>(sa);
+  select_kernel<<<(unsigned)((rows + kSelectWarps - 1) / kSelectWarps), kSelectWarps * 32, 0, s>>>(sa);
   MC_CUDA(cudaGetLastError());
   return kOk;
 }

@@ -246,7 +246,7 @@ struct SelectArgs {
   const float4* part;
   const float* topv;
   const int32_t* topi;
-  const int32_t* step;             // device step counter (output column, Philox counter)
+  int32_t* step;                   // device step counter (output column, Philox counter)
   int out_stride;                  // columns of the output arrays
   int32_t* next_tok;               // [S] input of the next decode step
   int32_t* out_tok;                // [S][out_stride] or null
@@ -255,6 +255,7 @@ struct SelectArgs {
   int32_t* pos;                    // [S] positions, advanced by `advance` (0 = no change)
   int32_t* seglen;                 // [S] set to 1 for the next decode step when advancing
   int advance_from_len;            // 1: pos = pos0 + seglen (after a prefill); 0: pos += 1
+  int32_t* done;                   // finished-block counter (zero between launches); null: no step bump
 };
 
 __device__ __forceinline__ void philox4x32_10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0,
@@ -284,82 +285,125 @@ __device__ __forceinline__ double sample_uniform(uint32_t session, uint32_t step
   return (double)(a * 67108864ull + b) * (1.0 / 9007199254740992.0);
 }
 
-__global__ void select_kernel(const SelectArgs a) {
-  const int s = blockIdx.x * blockDim.x + threadIdx.x;
-  if (s >= a.n_sess) return;
+// One warp per session; lane k holds partials k and k + 32 (at most 64 partials). The step
+// counter (output column and Philox counter) is read by every block before any work and advanced
+// by the last block to finish (a.done counts finished blocks), so no separate launch bumps it.
+constexpr int kSelectWarps = 4;
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
+
+__global__ void __launch_bounds__(kSelectWarps * 32) select_kernel(const SelectArgs a) {
+  __shared__ float cand_v[kSelectWarps][kMaxTopK];
+  __shared__ int cand_i[kSelectWarps][kMaxTopK];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int s = blockIdx.x * kSelectWarps + warp;
   const int step = a.step ? *a.step : 0;
-  if (a.seglen[s] <= 0) return;
-  float M = -INFINITY;
-  int idx = 0;
-  for (int k = 0; k < a.nsplit; ++k) {
-    const float4 p = a.part[(size_t)s * a.nsplit + k];
-    if (p.x > M) {
-      M = p.x;
-      idx = __float_as_int(p.z);
+  const int np = a.nsplit;  // partials per session (<= 64)
+  if (s < a.n_sess && a.seglen[s] > 0) {
+    const float4 none = make_float4(-INFINITY, 0.f, __int_as_float(0x7fffffff), 0.f);
+    const float4 p0 = lane < np ? a.part[(size_t)s * np + lane] : none;
+    const float4 p1 = lane + 32 < np ? a.part[(size_t)s * np + lane + 32] : none;
+    // max and its first index (argmaxProb, greedy.go:90-102: the lowest index among equal maxima)
+    float M = fmaxf(p0.x, p1.x);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    int idx = 0x7fffffff;
+    if (p0.x == M) idx = __float_as_int(p0.z);
+    if (p1.x == M) idx = min(idx, __float_as_int(p1.z));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) idx = min(idx, __shfl_xor_sync(0xffffffffu, idx, o));
+    // sum exp(l - max) over the vocabulary (in double, like the reference) and the target logit
+    double S = 0.0;
+    if (p0.x > -INFINITY) S += (double)p0.y * exp((double)p0.x - (double)M);
+    if (p1.x > -INFINITY) S += (double)p1.y * exp((double)p1.x - (double)M);
+    float lt = p0.w + p1.w;  // only the partial holding the target has a non-zero entry
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      S += __shfl_xor_sync(0xffffffffu, S, o);
+      lt += __shfl_xor_sync(0xffffffffu, lt, o);
     }
-  }
-  double S = 0.0;
-  float lt = 0.f;
-  for (int k = 0; k < a.nsplit; ++k) {
-    const float4 p = a.part[(size_t)s * a.nsplit + k];
-    S += (double)p.y * exp((double)p.x - (double)M);
-    lt += p.w;  // only the split holding the target has a non-zero entry... see below
-  }
-  int tok = idx;
-  if (a.mode == 1 && a.topk > 1) {
-    // Merge the split lists: repeatedly take the largest remaining (lowest index on ties).
-    int head[64];
-    for (int k = 0; k < a.nsplit; ++k) head[k] = 0;
-    float cv[kMaxTopK];
-    int ci[kMaxTopK];
-    for (int n = 0; n < a.topk; ++n) {
-      int bk = -1;
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-      for (int k = 0; k < a.nsplit; ++k) {
-        if (head[k] >= a.topk) continue;
-        const size_t o = ((size_t)s * a.nsplit + k) * a.topk + head[k];
-        const float v = a.topv[o];
-        const int i = a.topi[o];
-        if (v > bv || (v == bv && i < bi)) {
-          bv = v;
-          bi = i;
-          bk = k;
+    int tok = idx;
+    if (a.mode == 1 && a.topk > 1) {
+      // Merge the partials' top-k lists: repeatedly take the largest remaining value (lowest
+      // index on ties); lane k walks lists k and k + 32.
+      int h0 = 0, h1 = 0;
+      const size_t b0 = ((size_t)s * np + lane) * a.topk, b1 = ((size_t)s * np + lane + 32) * a.topk;
+      for (int n = 0; n < a.topk; ++n) {
+        float v0 = -INFINITY, v1 = -INFINITY;
+        int i0 = 0x7fffffff, i1 = 0x7fffffff;
+        if (lane < np && h0 < a.topk) {
+          v0 = a.topv[b0 + h0];
+          i0 = a.topi[b0 + h0];
+        }
+        if (lane + 32 < np && h1 < a.topk) {
+          v1 = a.topv[b1 + h1];
+          i1 = a.topi[b1 + h1];
+        }
+        const bool take1 = better(v1, i1, v0, i0);
+        float bv = take1 ? v1 : v0;
+        int bi = take1 ? i1 : i0;
+        int bl = lane * 2 + (take1 ? 1 : 0);  // which list of which lane
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+          if (better(ov, oi, bv, bi) || (ov == bv && oi == bi && ol < bl)) {
+            bv = ov;
+            bi = oi;
+            bl = ol;
+          }
+        }
+        if (lane == 0) {
+          cand_v[warp][n] = bv;
+          cand_i[warp][n] = bi;
+        }
+        if (bl == lane * 2) ++h0;
+        if (bl == lane * 2 + 1) ++h1;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        const double mx = (double)cand_v[warp][0] * a.inv_temp;
+        double sp = 0.0;
+        for (int n = 0; n < a.topk; ++n)
+          sp += (cand_v[warp][n] == -INFINITY) ? 0.0 : exp((double)cand_v[warp][n] * a.inv_temp - mx);
+        const double r = sample_uniform(a.session0 + (uint32_t)s, (uint32_t)step) * sp;
+        double cum = 0.0;
+        tok = cand_i[warp][a.topk - 1];
+        for (int n = 0; n < a.topk; ++n) {
+          cum += (cand_v[warp][n] == -INFINITY) ? 0.0 : exp((double)cand_v[warp][n] * a.inv_temp - mx);
+          if (r <= cum) {
+            tok = cand_i[warp][n];
+            break;
+          }
         }
       }
-      cv[n] = bv;
-      ci[n] = bi;
-      if (bk >= 0) head[bk]++;
     }
-    const double mx = (double)cv[0] * a.inv_temp;
-    double w[kMaxTopK], sp = 0.0;
-    for (int n = 0; n < a.topk; ++n) {
-      w[n] = (cv[n] == -INFINITY) ? 0.0 : exp((double)cv[n] * a.inv_temp - mx);
-      sp += w[n];
-    }
-    const double r = sample_uniform(a.session0 + (uint32_t)s, (uint32_t)step) * sp;
-    double cum = 0.0;
-    tok = ci[a.topk - 1];
-    for (int n = 0; n < a.topk; ++n) {
-      cum += w[n];
-      if (r <= cum) {
-        tok = ci[n];
-        break;
+    if (lane == 0) {
+      a.next_tok[s] = tok;
+      if (a.out_tok) a.out_tok[(size_t)s * a.out_stride + step] = tok;
+      if (a.out_prob) a.out_prob[(size_t)s * a.out_stride + step] = (float)(1.0 / S);
+      if (a.out_logprob) a.out_logprob[(size_t)s * a.out_stride + step] = (double)lt - (double)M - log(S);
+      if (a.pos) {
+        if (a.advance_from_len) a.pos[s] = a.pos[s] + a.seglen[s];
+        else a.pos[s] = a.pos[s] + 1;
+        a.seglen[s] = 1;
       }
     }
   }
-  a.next_tok[s] = tok;
-  if (a.out_tok) a.out_tok[(size_t)s * a.out_stride + step] = tok;
-  if (a.out_prob) a.out_prob[(size_t)s * a.out_stride + step] = (float)(1.0 / S);
-  if (a.out_logprob) a.out_logprob[(size_t)s * a.out_stride + step] = (double)lt - (double)M - log(S);
-  if (a.pos) {
-    if (a.advance_from_len) a.pos[s] = a.pos[s] + a.seglen[s];
-    else a.pos[s] = a.pos[s] + 1;
-    a.seglen[s] = 1;
+  if (a.done) {
+    // the last block to finish advances the step counter (every block has read it by then)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(a.done, 1) == (int)gridDim.x - 1) {
+        *a.step += 1;
+        *a.done = 0;
+        __threadfence();
+      }
+    }
   }
 }
-
-__global__ void bump_kernel(int32_t* step) { *step += 1; }
 
 }  // namespace eng
 }  // namespace mc

@@ -142,28 +142,41 @@ def test_ragged_prompts_and_idle_sessions(oracle):
     compare_streams(gt[mask], wt[mask], wl[mask])
 
 
+def _cdf_margin(logits, temperature, topk, u):
+    """Distance of the draw from the nearest bucket edge of the top-k CDF, relative to its total
+    (the truncated branch of SampleRawLogitsAdvanced, generate/sample.go:91-172, on these logits)."""
+    l = np.asarray(logits, np.float64)
+    order = np.lexsort((np.arange(l.size), -l))[:topk]  # value descending, index ascending
+    v = l[order] / temperature
+    cdf = np.cumsum(np.exp(v - v[0]))
+    return float(np.min(np.abs(cdf - u * cdf[-1])) / cdf[-1])
+
+
 def test_sampling_matches_oracle(oracle):
     """Config-3 shapes (D=384, streamed activation tiles), T=0.8, top-k 40, Philox per session:
-    sampled streams equal the oracle's (same draws), except after excused near-ties."""
+    the sampled streams equal the oracle's (the same draws). A stream may leave the oracle's only
+    at a step where the oracle's own draw falls within 5e-3 of a CDF bucket edge (the logits
+    agree to 1e-3 of their maximum, so only such draws can flip), and at most a quarter may."""
     spec = small_spec(3, vocab=1024)
     data = synth.build_model_file(spec)
     om, gm = oracle.Model(data), quant.Model.decode(data)
-    n = 16
+    n, steps, T, K = 16, 12, 0.8, 40
     lens = synth.prompt_lengths(n, 16, 64, seed=3)
     prompts = synth.prompts_uniform_fast(n, 64, spec.vocab, seed=3)
-    wt, wl = om.generate_sample(prompts, lens, 12, 0.8, 40, session0=0, logits=True)
-    b = gm.new_batch(n, 0, 64, top_k=40)
-    gt, _ = b.generate(prompts, lens, 12, temperature=0.8, session0=0)
+    wt, wl = om.generate_sample(prompts, lens, steps, T, K, session0=0, logits=True)
+    b = gm.new_batch(n, 0, 64, top_k=K)
+    gt, _ = b.generate(prompts, lens, steps, temperature=T, session0=0)
     b.close()
-    agree = np.mean(gt[:, 0] == wt[:, 0])
-    assert agree >= 0.9, agree
+    diverged = 0
     for s in range(n):
-        for t in range(12):
-            if gt[s, t] != wt[s, t]:
-                break
-        else:
+        diff = np.nonzero(gt[s] != wt[s])[0]
+        if diff.size == 0:
             continue
-        assert t >= 0
+        t = int(diff[0])
+        diverged += 1
+        m = _cdf_margin(wl[s, t], T, K, synth.sample_uniform(s, t))
+        assert m < 5e-3, f"session {s} step {t}: {gt[s, t]} != {wt[s, t]} with the draw {m:.3g} from a bucket edge"
+    assert diverged <= n // 4, diverged
 
 
 def test_score_matches_oracle(oracle):
