@@ -20,33 +20,28 @@
 namespace mc {
 namespace eng {
 
-constexpr int kDR = 32;                          // sessions per CTA (MMA N)
+constexpr int kDMaxR = 32;                       // sessions per CTA (MMA N): 32, or 16 for wide models
 constexpr int kDRowWarps = 16;
 constexpr int kDRowThreads = kDRowWarps * 32;
 constexpr int kDThreads = kDRowThreads + 64;     // + MMA warp + producer warp
 constexpr int kDMmaWarp = kDRowWarps;
 constexpr int kDProducerWarp = kDRowWarps + 1;
-constexpr int kDWStages = 6;                     // weight-tile ring (16 KB tiles)
+constexpr int kDMaxWStages = 6;                  // weight-tile ring (16 KB tiles): 6, or 3 for wide models
 constexpr int kDSlots = 4;                       // TMEM accumulator slots
-constexpr int kDSlotCols = 128;                  // three planes of kDR columns each, padded
-constexpr int kDBTile = kDR * 128;               // one digit plane of one K tile of the sessions (4 KB)
-constexpr int kDRowsPerWarp = kDR / kDRowWarps;  // 2
-constexpr int kDCols = kDR / 4;                  // sessions per epilogue thread (8)
 
 struct DBars {
-  uint64_t w_full[kDWStages], w_empty[kDWStages], s_full[kDSlots], s_empty[kDSlots], b_full;
+  uint64_t w_full[kDMaxWStages], w_empty[kDMaxWStages], s_full[kDSlots], s_empty[kDSlots], b_full;
   uint32_t tmem;
-  int valid[kDR], tok[kDR], pos[kDR];
-  float rstep[kDR];  // step of each session row of the current GEMM's activation planes
+  int valid[kDMaxR], tok[kDMaxR], pos[kDMaxR];
+  float rstep[kDMaxR];  // step of each session row of the current GEMM's activation planes
 };
 
 constexpr size_t kDecodeSmemMax = 227 * 1024;  // the per-block opt-in limit of sm_100
 
-// Dynamic shared memory of the decode kernel for state width D, hidden width H and kt K tiles of
-// activation planes (kt = ceil(max(3D, H) / 128)).
-inline size_t decode_smem_bytes(int D, int H, int kt) {
-  return 1024 + (size_t)kDWStages * kTile + (size_t)3 * kt * kDBTile + (size_t)4 * kDR * (2 * D + (D > H ? D : H)) +
-         sizeof(DBars);
+// Dynamic shared memory of the decode kernel for state width D, hidden width H, kt K tiles of
+// activation planes (kt = ceil(max(3D, H) / 128)), R sessions per CTA and ws weight stages.
+inline size_t decode_smem_bytes(int D, int H, int kt, int R, int ws) {
+  return 1024 + (size_t)ws * kTile + (size_t)3 * kt * R * 128 + (size_t)4 * R * (2 * D + (D > H ? D : H)) + sizeof(DBars);
 }
 
 __device__ __forceinline__ void row_bar_d() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
@@ -69,7 +64,9 @@ __device__ __forceinline__ float max4_d(float4 v) {
 
 // The three digit planes of four consecutive activations (K indices e..e+3, e % 4 == 0) of
 // session row r, written into the plane tiles of K tile e / 128 (one 32-bit store per plane).
+template <int R>
 __device__ __forceinline__ void put_planes(uint8_t* sB, int KT, int r, int e, float4 v, float inv) {
+  constexpr int kDBTile = R * 128;  // one digit plane of one K tile of the sessions
   uint8_t* tile = sB + (e >> 7) * kDBTile;
   const int k = e & 127;
   const uint32_t off = sw128_offset(r, k >> 4) + (k & 15);
@@ -83,8 +80,14 @@ __device__ __forceinline__ void put_planes(uint8_t* sB, int KT, int r, int e, fl
   *reinterpret_cast<uint32_t*>(tile + 2 * KT * kDBTile + off) = pack_low_bytes(c0, c1, c2, c3);
 }
 
-template <int KF>  // float4 columns per lane of a state row: ceil(D / 128)
+template <int KF, int R, int WS>  // float4 columns per state row lane (ceil(D / 128)), sessions per CTA, weight stages
 __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid_constant__ BlockArgs a) {
+  constexpr int kDR = R;
+  constexpr int kDWStages = WS;
+  constexpr int kDBTile = R * 128;               // one digit plane of one K tile of the sessions
+  constexpr int kDRowsPerWarp = R / kDRowWarps;  // session rows per row warp
+  constexpr int kDCols = R / 4;                  // sessions per epilogue thread
+  constexpr int kDSlotCols = R == 32 ? 128 : 64; // three planes of R columns, padded
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int D = a.D, H = a.H, KT = a.dec_kt;
@@ -220,11 +223,17 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->s_empty[slot]);
     };
-    auto acc8 = [&](int slot, uint32_t(&x1)[8], uint32_t(&x2)[8], uint32_t(&x3)[8]) {
+    auto acc8 = [&](int slot, uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols], uint32_t(&x3)[kDCols]) {
       const uint32_t base = tmem_addr(tmem, 32 * (warp & 3), slot * kDSlotCols + r0);
-      tmem_ld8(base, x1);
-      tmem_ld8(base + kDR, x2);
-      tmem_ld8(base + 2 * kDR, x3);
+      if constexpr (kDCols == 8) {
+        tmem_ld8(base, x1);
+        tmem_ld8(base + kDR, x2);
+        tmem_ld8(base + 2 * kDR, x3);
+      } else {
+        tmem_ld4(base, x1);
+        tmem_ld4(base + kDR, x2);
+        tmem_ld4(base + 2 * kDR, x3);
+      }
       tmem_wait_ld();
     };
     auto load_steps = [&](float(&stp)[kDCols]) {
@@ -239,7 +248,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
         const int slot = sidx % kDSlots;
         wait_slot(slot, sidx);
         if (a.trace_fine) trace_point(a, tp++);
-        uint32_t x1[8], x2[8], x3[8];
+        uint32_t x1[kDCols], x2[kDCols], x3[kDCols];
         acc8(slot, x1, x2, x3);
         release_slot(slot);
         fn(c, stp, x1, x2, x3);
@@ -252,7 +261,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       load_steps(stp);
       for (int c = 0; c + 1 < G.nchunks; c += 2, sidx += 2) {
         const int sv = sidx % kDSlots, sg = (sidx + 1) % kDSlots;
-        uint32_t v1[8], v2[8], v3[8], g1[8], g2[8], g3[8];
+        uint32_t v1[kDCols], v2[kDCols], v3[kDCols], g1[kDCols], g2[kDCols], g3[kDCols];
         wait_slot(sv, sidx);
         acc8(sv, v1, v2, v3);
         wait_slot(sg, sidx + 1);
@@ -316,7 +325,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
 #pragma unroll
           for (int k = 0; k < KF; ++k) {
             const int f = lane + 32 * k;
-            if (f < nf) put_planes(sB, KT, rr, 4 * f, x[k], is);
+            if (f < nf) put_planes<R>(sB, KT, rr, 4 * f, x[k], is);
           }
         }
       }
@@ -366,13 +375,13 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
 #pragma unroll
         for (int k = 0; k < KF; ++k) {
           const int f = lane + 32 * k;
-          if (f < nf) put_planes(sB, KT, rr, 4 * f, v ? a4[f] : make_float4(0.f, 0.f, 0.f, 0.f), is);
+          if (f < nf) put_planes<R>(sB, KT, rr, 4 * f, v ? a4[f] : make_float4(0.f, 0.f, 0.f, 0.f), is);
         }
       }
       publish();
       trace_point(a, tp++);
-      tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[8], uint32_t(&x2)[8],
-                                uint32_t(&x3)[8]) {
+      tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols],
+                                uint32_t(&x3)[kDCols]) {
         const int n = c * 128 + chl;
         if (n >= D) return;
 #pragma unroll
@@ -439,8 +448,8 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       publish();
       trace_point(a, tp++);
       // lambda = sigmoid(W_select n s_sel + base), into the latch-gate rows
-      tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[8], uint32_t(&x2)[8],
-                                uint32_t(&x3)[8]) {
+      tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols],
+                                uint32_t(&x3)[kDCols]) {
         const int n = c * 128 + chl;
         if (n >= D) return;
         const float base = a.latch_base[n];
@@ -492,17 +501,17 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
         for (int k = 0; k < KF; ++k) {
           const int f = lane + 32 * k;
           if (f < nf) {
-            put_planes(sB, KT, rr, 4 * f, nv[k], is);
-            put_planes(sB, KT, rr, D + 4 * f, lf[u][k], is);
-            put_planes(sB, KT, rr, 2 * D + 4 * f, lv[k], is);
+            put_planes<R>(sB, KT, rr, 4 * f, nv[k], is);
+            put_planes<R>(sB, KT, rr, D + 4 * f, lf[u][k], is);
+            put_planes<R>(sB, KT, rr, 2 * D + 4 * f, lv[k], is);
           }
         }
       }
       publish();
       trace_point(a, tp++);
       // hidden = (W1v x s1 + b1v) * sigmoid(W1g x s1 + b1g)   (applyRule layer 1, stream.go:212-220)
-      tiles2(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&v1)[8], uint32_t(&v2)[8],
-                                uint32_t(&v3)[8], uint32_t(&g1)[8], uint32_t(&g2)[8], uint32_t(&g3)[8]) {
+      tiles2(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&v1)[kDCols], uint32_t(&v2)[kDCols],
+                                uint32_t(&v3)[kDCols], uint32_t(&g1)[kDCols], uint32_t(&g2)[kDCols], uint32_t(&g3)[kDCols]) {
         const int hu = c * 128 + chl;
         if (hu >= H) return;
         const float bv = a.b1[hu], bg = a.b1[H + hu];
@@ -529,14 +538,14 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
           m = v ? warp_max_d(m) : 0.f;
           if (lane == 0) bars->rstep[rr] = row_step(m);
           const float is = row_inv_step(m);
-          for (int f = lane; f < hf; f += 32) put_planes(sB, KT, rr, 4 * f, v ? h4[f] : make_float4(0.f, 0.f, 0.f, 0.f), is);
+          for (int f = lane; f < hf; f += 32) put_planes<R>(sB, KT, rr, 4 * f, v ? h4[f] : make_float4(0.f, 0.f, 0.f, 0.f), is);
         }
       }
       publish();
       trace_point(a, tp++);
       // o = W2 hidden s2 + b2; gate = sigmoid(o_gate); cur = (1 - gate) cur + gate o_delta (:222-229)
-      tiles2(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&v1)[8], uint32_t(&v2)[8],
-                                uint32_t(&v3)[8], uint32_t(&g1)[8], uint32_t(&g2)[8], uint32_t(&g3)[8]) {
+      tiles2(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&v1)[kDCols], uint32_t(&v2)[kDCols],
+                                uint32_t(&v3)[kDCols], uint32_t(&g1)[kDCols], uint32_t(&g2)[kDCols], uint32_t(&g3)[kDCols]) {
         const int d = c * 128 + chl;
         if (d >= D) return;
         const float bd = a.b2[d], bg = a.b2[D + d];
@@ -568,8 +577,8 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       publish();
       trace_point(a, tp++);
       const int dh = a.dh;
-      tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[8], uint32_t(&x2)[8],
-                                uint32_t(&x3)[8]) {
+      tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols],
+                                uint32_t(&x3)[kDCols]) {
         const int n = c * 128 + chl;
         if (n >= 3 * D) return;
         const int part = n / D, e = n - part * D;

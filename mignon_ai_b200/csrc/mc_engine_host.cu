@@ -105,6 +105,7 @@ struct DevModel {
   int device = 0;
   int V = 0, D = 0, H = 0, max_context = 0, heads = 0, window = 0, cache = 0, ring = 0, total_steps = 0, n_attn = 0;
   int dec_kt = 0;         // decode kernel: K tiles of its activation planes
+  int dec_r = 32;         // decode kernel: sessions per CTA (32, or 16 for wide models)
   size_t dec_smem = 0;    // decode kernel: dynamic shared memory
   bool dec_ok = false;    // the decode kernel fits this model (else decode uses block_kernel)
   bool tied = true;
@@ -230,7 +231,13 @@ int build_dev_model(const HostModel& hm, int device, std::unique_ptr<DevModel>& 
   m->ring = longest + 1;
   m->n_attn = nattn;
   m->dec_kt = (std::max(3 * D, H) + 127) / 128;
-  m->dec_smem = decode_smem_bytes(D, H, m->dec_kt);
+  // 32 sessions per CTA with a 6-stage weight ring, or (wide models) 16 with 3 stages
+  m->dec_r = 32;
+  m->dec_smem = decode_smem_bytes(D, H, m->dec_kt, 32, 6);
+  if (m->dec_smem > kDecodeSmemMax) {
+    m->dec_r = 16;
+    m->dec_smem = decode_smem_bytes(D, H, m->dec_kt, 16, 3);
+  }
   m->dec_ok = m->dec_smem <= kDecodeSmemMax;
   if (nattn > 0 && m->cache > 128) return set_error(kUnsupported, "attention caches above 128 positions");
   out = std::move(m);
@@ -312,9 +319,12 @@ static int ensure_attrs(int device) {
   MC_CUDA(cudaFuncSetAttribute(block_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
   MC_CUDA(cudaFuncSetAttribute(block_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
   MC_CUDA(cudaFuncSetAttribute(block_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
-  MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
-  MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
-  MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
+  MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<1, 32, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
+  MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<2, 32, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
+  MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<3, 32, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
+  MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<1, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
+  MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<2, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
+  MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<3, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem));
   MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
   MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
@@ -530,11 +540,16 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log) {
         if (a.gemms[i].type == kGW2) a.gemms[i] = spec(m.blocks[bi].w2d, kGW2, a.gemms[i].step);
       }
       a.dec_kt = m.dec_kt;
-      const int grid = (b.S + kDR - 1) / kDR;
-      switch ((m.D + 127) / 128) {
-        case 1: block_decode_kernel<1><<<grid, kDThreads, m.dec_smem, s>>>(a); break;
-        case 2: block_decode_kernel<2><<<grid, kDThreads, m.dec_smem, s>>>(a); break;
-        default: block_decode_kernel<3><<<grid, kDThreads, m.dec_smem, s>>>(a); break;
+      const int grid = (b.S + m.dec_r - 1) / m.dec_r;
+      const int kf = (m.D + 127) / 128;
+      if (m.dec_r == 32) {
+        if (kf == 1) block_decode_kernel<1, 32, 6><<<grid, kDThreads, m.dec_smem, s>>>(a);
+        else if (kf == 2) block_decode_kernel<2, 32, 6><<<grid, kDThreads, m.dec_smem, s>>>(a);
+        else block_decode_kernel<3, 32, 6><<<grid, kDThreads, m.dec_smem, s>>>(a);
+      } else {
+        if (kf == 1) block_decode_kernel<1, 16, 3><<<grid, kDThreads, m.dec_smem, s>>>(a);
+        else if (kf == 2) block_decode_kernel<2, 16, 3><<<grid, kDThreads, m.dec_smem, s>>>(a);
+        else block_decode_kernel<3, 16, 3><<<grid, kDThreads, m.dec_smem, s>>>(a);
       }
     } else {
       switch ((m.D + 127) / 128) {

@@ -210,7 +210,7 @@ def test_score_matches_oracle(oracle):
     b.close()
 
 
-@pytest.mark.parametrize("cfg,vocab", [(2, None), (1, None)])
+@pytest.mark.parametrize("cfg,vocab", [(2, None), (1, None), (3, 1024), (4, 512)])
 def test_decode_kernel_matches_block_kernel_bitwise(monkeypatch, cfg, vocab):
     """Decode steps run on block_decode_kernel (weights on the MMA's M side, 32 sessions per CTA);
     block_kernel (128 session rows per CTA) computes the same float32 operations in the same
