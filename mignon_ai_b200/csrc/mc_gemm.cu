@@ -31,7 +31,10 @@ constexpr int kI8BN = 256;
 constexpr int kI8Stages = 4;
 constexpr int kI8StageA = kBM * kBK;     // 16 KB
 constexpr int kI8StageB = kI8BN * kBK;   // 32 KB
-constexpr int kI8Smem = kI8Stages * (kI8StageA + kI8StageB) + 1024 + 256;
+constexpr int kI8EpiWarps = 8;
+constexpr int kI8StageStride = 20;  // words per row of an epilogue warp's 32 x 16 staging tile (padded)
+constexpr int kI8Staging = kI8EpiWarps * 32 * kI8StageStride * 4;
+constexpr int kI8Smem = kI8Stages * (kI8StageA + kI8StageB) + kI8Staging + 1024 + 256;  // ring, staging, barriers
 
 struct I8Args {
   int M, N, K;
@@ -42,109 +45,156 @@ struct I8Args {
   float* y;                // [M x N] or null
 };
 
-__global__ void __launch_bounds__(192, 1)
+// Persistent: one CTA per SM walks the 128 x 256 output tiles (N-tiles fastest, so neighbouring
+// CTAs share the A tile in L2). Warp 0 issues the TMA loads through a 4-stage ring, warp 1 the
+// MMAs into one of two TMEM accumulators (2 x 256 columns), and eight epilogue warps drain the
+// other accumulator (warp w: TMEM lanes 32*(w%4), columns 128*((w-2)/4)) while the next tile's
+// MMAs run, so output stores overlap the tensor core.
+constexpr int kI8Threads = 64 + 32 * kI8EpiWarps;
+
+__global__ void __launch_bounds__(kI8Threads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w, I8Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
   uint8_t* sb = smem + kI8Stages * kI8StageA;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + kI8Stages * kI8StageB);
+  uint32_t* stg = reinterpret_cast<uint32_t*>(sb + kI8Stages * kI8StageB);  // [warp][32][kI8StageStride]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + kI8Stages * kI8StageB + kI8Staging);
   uint64_t* empty = full + kI8Stages;
-  uint64_t* accfull = empty + kI8Stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accfull + 1);
+  uint64_t* acc_full = empty + kI8Stages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kI8BN;
   const int ktiles = (args.K + kBK - 1) / kBK;
+  const int ntn = args.N / kI8BN, ntm = (args.M + kBM - 1) / kBM;
+  const int ntiles = ntn * ntm;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kI8Stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accfull, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kI8EpiWarps);
+    }
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 256);
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // TMA producer.
-    prefetch_tensormap(&map_a);
-    prefetch_tensormap(&map_w);
-    for (int kt = 0; kt < ktiles; ++kt) {
-      const int s = kt % kI8Stages;
-      if (kt >= kI8Stages && !mbar_wait_or_abort(&empty[s], ((kt / kI8Stages) - 1) & 1, kErrWaitEmpty)) break;
-      mbar_arrive_expect_tx(&full[s], kI8StageA + kI8StageB);
-      tma_load_2d(sa + s * kI8StageA, &map_a, kt * kBK, m0, &full[s]);
-      tma_load_2d(sb + s * kI8StageB, &map_w, kt * kBK, n0, &full[s]);
-    }
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer.
-    const uint32_t idesc = idesc_i8(kBM, kI8BN);
-    bool ok = true;
-    for (int kt = 0; kt < ktiles && ok; ++kt) {
-      const int s = kt % kI8Stages;
-      if (!mbar_wait_or_abort(&full[s], (kt / kI8Stages) & 1, kErrWaitFull)) {
-        ok = false;
-        break;
+  if (warp == 0) {
+    // TMA producer: every tile's K tiles through the ring
+    if (lane == 0) {
+      prefetch_tensormap(&map_a);
+      prefetch_tensormap(&map_w);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const int m0 = (t / ntn) * kBM, n0 = (t % ntn) * kI8BN;
+        for (int kt = 0; kt < ktiles; ++kt, ++it) {
+          const int s = it % kI8Stages;
+          if (it >= kI8Stages && !mbar_wait_or_abort(&empty[s], ((it / kI8Stages) - 1) & 1, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], kI8StageA + kI8StageB);
+          tma_load_2d(sa + s * kI8StageA, &map_a, kt * kBK, m0, &full[s]);
+          tma_load_2d(sb + s * kI8StageB, &map_w, kt * kBK, n0, &full[s]);
+        }
       }
-      tc_fence_after();
-      const uint64_t da = smem_desc_sw128(sa + s * kI8StageA);
-      const uint64_t db = smem_desc_sw128(sb + s * kI8StageB);
-      const int ksteps = min(4, (args.K - kt * kBK + 31) / 32);
-      for (int kk = 0; kk < ksteps; ++kk)
-        mma_i8(tmem, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
-      mma_commit(&empty[s]);
     }
-    if (ok) mma_commit(accfull);
-  } else if (warp >= 2) {
-    // Epilogue: warp w reads TMEM lanes 32*(w%4)..+31, i.e. rows m0 + 32*(w%4) + lane.
-    const int quad = warp % 4;
-    const int row = m0 + quad * 32 + lane;
-    // TMEM loads are warp-collective: the whole warp takes the same branch.
-    if (__all_sync(0xffffffffu, mbar_wait_or_abort(accfull, 0, kErrWaitAcc))) {
+  } else if (warp == 1) {
+    // MMA issuer: tile i accumulates into TMEM buffer i % 2 once the epilogue has drained it
+    if (lane == 0) {
+      const uint32_t idesc = idesc_i8(kBM, kI8BN);
+      uint32_t it = 0, i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !mbar_wait_or_abort(&acc_empty[b], ((i / 2) - 1) & 1, kErrWaitAccFree)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + b * kI8BN;
+        for (int kt = 0; kt < ktiles; ++kt, ++it) {
+          const int s = it % kI8Stages;
+          if (!mbar_wait_or_abort(&full[s], (it / kI8Stages) & 1, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_sw128(sa + s * kI8StageA);
+          const uint64_t db = smem_desc_sw128(sb + s * kI8StageB);
+          const int ksteps = min(4, (args.K - kt * kBK + 31) / 32);
+          for (int kk = 0; kk < ksteps; ++kk)
+            mma_i8(acc, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&empty[s]);
+        }
+        if (ok) mma_commit(&acc_full[b]);
+      }
+    }
+  } else {
+    // Epilogue warps: warp w reads TMEM lanes 32*(w%4)..+31 (rows) and columns 128*((w-2)/4)..+127
+    const int quad = warp % 4, half = (warp - 2) / 4;
+    uint32_t i = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+      const int b = i & 1;
+      const int m0 = (t / ntn) * kBM, n0 = (t % ntn) * kI8BN;
+      const int row = m0 + quad * 32 + lane;
+      // TMEM loads are warp-collective: the whole warp takes the same branch.
+      if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&acc_full[b], (i / 2) & 1, kErrWaitAcc))) break;
       tc_fence_after();
       const float rs = (args.row_scale && row < args.M) ? args.row_scale[row] : 1.0f;
-      for (int c = 0; c < kI8BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem_addr(tmem, quad * 32, c), r);
-        tmem_wait_ld();
-        if (row >= args.M) continue;
-        const int n = n0 + c;
-        if (args.c_i32) {
-          int4* dst = reinterpret_cast<int4*>(args.c_i32 + (size_t)row * args.N + n);
+      uint32_t* st = stg + (size_t)(warp - 2) * 32 * kI8StageStride;
+      // 16 columns at a time: thread = row into the staging tile (conflict-free), then the warp
+      // stores 8 rows x 64 contiguous bytes per instruction
+      for (int pass = 0; pass < 2; ++pass) {
+        int32_t* out = pass == 0 ? args.c_i32 : reinterpret_cast<int32_t*>(args.y);
+        if (!out) continue;
+        for (int c = half * 128; c < half * 128 + 128; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(tmem_addr(tmem, quad * 32, b * kI8BN + c), r);
+          tmem_wait_ld();
+          const int n = n0 + c;
+          if (pass == 1) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            dst[j] = make_int4((int)r[4 * j], (int)r[4 * j + 1], (int)r[4 * j + 2], (int)r[4 * j + 3]);
-        }
-        if (args.y) {
-          float4* dst = reinterpret_cast<float4*>(args.y + (size_t)row * args.N + n);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float v[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int col = n + 4 * j + e;
-              float cs = args.col_scale ? args.col_scale[col] : 1.0f;
+            for (int e = 0; e < 16; ++e) {
+              const float cs = args.col_scale ? args.col_scale[n + e] : 1.0f;
               // Separately rounded multiplies and add (never contracted into an FMA).
-              float t = __fmul_rn((float)(int)r[4 * j + e], rs);
-              t = __fmul_rn(t, cs);
-              if (args.bias) t = __fadd_rn(t, args.bias[col]);
-              v[e] = t;
+              float tv = __fmul_rn((float)(int)r[e], rs);
+              tv = __fmul_rn(tv, cs);
+              if (args.bias) tv = __fadd_rn(tv, args.bias[n + e]);
+              r[e] = __float_as_uint(tv);
             }
-            dst[j] = make_float4(v[0], v[1], v[2], v[3]);
           }
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(st + lane * kI8StageStride + 4 * j) =
+                make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int piece = lane + 32 * i;  // 32 rows x 4 pieces of 16 bytes
+            const int rr = piece >> 2, ch = piece & 3;
+            const int grow = m0 + quad * 32 + rr;
+            const uint4 v = *reinterpret_cast<const uint4*>(st + rr * kI8StageStride + 4 * ch);
+            if (grow < args.M) *reinterpret_cast<uint4*>(out + (size_t)grow * args.N + n + 4 * ch) = v;
+          }
+          __syncwarp();
         }
       }
+      // the accumulator is read: the MMA warp may reuse it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, 256);
+  if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -340,8 +390,14 @@ int gemm_i8_launch(const int8_t* a, const int8_t* w, int M, int N, int K, const 
     attr = true;
   }
   gemm::I8Args args{M, N, K, row_scale, col_scale, bias, c_i32, y};
-  dim3 grid(N / gemm::kI8BN, (M + gemm::kBM - 1) / gemm::kBM);
-  gemm::gemm_i8_kernel<<<grid, 192, gemm::kI8Smem, stream>>>(ma, mw, args);
+  static int n_sm = 0;
+  if (!n_sm) {
+    int dev = 0;
+    MC_CUDA(cudaGetDevice(&dev));
+    MC_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+  }
+  const int tiles = (N / gemm::kI8BN) * ((M + gemm::kBM - 1) / gemm::kBM);
+  gemm::gemm_i8_kernel<<<std::min(tiles, n_sm), gemm::kI8Threads, gemm::kI8Smem, stream>>>(ma, mw, args);
   MC_CUDA(cudaGetLastError());
   return kOk;
 }
