@@ -218,6 +218,66 @@ def run_gemm_sweep(args):
     return 0
 
 
+SCORE_SEQS = 16384
+SCORE_LEN = 128
+
+
+def run_score(args):
+    """Config 4: 16384 sequences of 128 uniform token ids (seed 4) scored in one pass through the
+    public host API (mc_score: sequences in from host memory, per-token log-probabilities out),
+    timed with CUDA events around the whole call; the CPU restatement scores a sample beside it."""
+    import torch
+    from mignon_ai_b200 import quant, synth
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle
+    spec = synth.CONFIGS[4]
+    n = SCORE_SEQS if args.sessions == SESSIONS else args.sessions
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    data = synth.build_model_file(spec)
+    ctx = quant.Context((0,))
+    model = quant.Model.decode(data, ctx)
+    seqs = synth.prompts_uniform_fast(n, SCORE_LEN, spec.vocab, seed=4)
+    lens = np.full(n, SCORE_LEN, np.int32)
+    batch = model.new_batch(n, 0, SCORE_LEN)
+    for _ in range(max(1, args.warmup)):
+        out = batch.score(seqs, lens)
+    steps = max(1, args.steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record()
+    for _ in range(steps):
+        out = batch.score(seqs, lens)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    tokens = n * (SCORE_LEN - 1)
+    value = tokens / (ms / 1000.0)
+    # CPU restatement on a sample, all host threads
+    cores = os.cpu_count() or 1
+    k = max(cores, 32)
+    om = pyoracle.Model(data)
+    t0 = time.perf_counter()
+    want = om.score(seqs[:k], nthreads=cores)
+    cpu_s = time.perf_counter() - t0
+    err = float(np.max(np.abs(out[:k] - want)))
+    line = {"metric": "scored tokens/s (config-4 per-token log-probabilities)", "value": value, "unit": "tokens/s",
+            "n_gpus": 1, "steps": steps, "warmup": max(1, args.warmup), "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "none", "vs_baseline": None, "dtype": "int8 weights x float32 activations (3 int8 digit planes)",
+            "data": "synthetic",
+            "config": {"workload": "config4: D=192 H=512 6 blocks x 2 steps, attn 4 heads window 64, vocab 2048; "
+                                   "%d sequences x %d tokens (seed 4), every next-token log-probability" % (n, SCORE_LEN),
+                       "timing": "the host API call (sequences in, log-probabilities out) per step"},
+            "cpu_baseline": {"value": k * (SCORE_LEN - 1) / cpu_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": "%d sequences of the workload" % k},
+            "max_abs_dlogprob_vs_cpu": err}
+    print(json.dumps(line))
+    batch.close()
+    model.close()
+    ctx.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -228,11 +288,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true",
                     help="profiling case: one generation job, no timing, e2e, profile or CPU baseline")
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemm"],
-                    help="decode: the config-2 generation job (the headline); gemm: the config-5 INT8 GEMM sweep")
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemm", "score"],
+                    help="decode: the config-2 generation job (the headline); gemm: the config-5 INT8 GEMM "
+                         "sweep; score: the config-4 scoring pass")
     args = ap.parse_args()
     if args.workload == "gemm":
         return run_gemm_sweep(args)
+    if args.workload == "score":
+        return run_score(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
