@@ -241,11 +241,15 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       for (int j = 0; j < kDCols; ++j) stp[j] = bars->rstep[r0 + j];
     };
     // The M-tiles of one GEMM, one accumulator each: fn(tile, steps, planes).
-    auto tiles1 = [&](const GemmSpec& G, auto&& fn) {
+    // pre(tile) returns the tile's per-channel vectors (biases), loaded before the accumulator
+    // wait so that their latency overlaps it; the epilogue reads them from pv.
+    float2 pv = make_float2(0.f, 0.f);
+    auto tiles1 = [&](const GemmSpec& G, auto&& pre, auto&& fn) {
       float stp[kDCols];
       load_steps(stp);
       for (int c = 0; c < G.nchunks; ++c, ++sidx) {
         const int slot = sidx % kDSlots;
+        pv = pre(c);
         wait_slot(slot, sidx);
         if (a.trace_fine) trace_point(a, tp++);
         uint32_t x1[kDCols], x2[kDCols], x3[kDCols];
@@ -256,12 +260,13 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       }
     };
     // Pairs of M-tiles (value/delta tile, gate tile): fn(pair, steps, value planes, gate planes).
-    auto tiles2 = [&](const GemmSpec& G, auto&& fn) {
+    auto tiles2 = [&](const GemmSpec& G, auto&& pre, auto&& fn) {
       float stp[kDCols];
       load_steps(stp);
       for (int c = 0; c + 1 < G.nchunks; c += 2, sidx += 2) {
         const int sv = sidx % kDSlots, sg = (sidx + 1) % kDSlots;
         uint32_t v1[kDCols], v2[kDCols], v3[kDCols], g1[kDCols], g2[kDCols], g3[kDCols];
+        pv = pre(c / 2);
         wait_slot(sv, sidx);
         acc8(sv, v1, v2, v3);
         wait_slot(sg, sidx + 1);
@@ -282,12 +287,13 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
         const int rr = warp + kDRowWarps * u;
         const int s = s0 + rr;
         const bool v = bars->valid[rr] != 0;
-        float4 x[KF];
+        float4 x[KF], gg[KF];
         const float4* c4 = reinterpret_cast<const float4*>(sCur + rr * D);
 #pragma unroll
         for (int k = 0; k < KF; ++k) {
           const int f = lane + 32 * k;
           x[k] = (v && f < nf) ? c4[f] : make_float4(0.f, 0.f, 0.f, 0.f);
+          gg[k] = (gain && f < nf) ? reinterpret_cast<const float4*>(gain)[f] : make_float4(1.f, 1.f, 1.f, 1.f);
         }
         float ss = 0.f;
 #pragma unroll
@@ -306,11 +312,10 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
         for (int k = 0; k < KF; ++k) {
           const int f = lane + 32 * k;
           if (f < nf && gain) {
-            const float4 gg = reinterpret_cast<const float4*>(gain)[f];
-            x[k].x = __fmul_rn(__fmul_rn(x[k].x, inv), gg.x);
-            x[k].y = __fmul_rn(__fmul_rn(x[k].y, inv), gg.y);
-            x[k].z = __fmul_rn(__fmul_rn(x[k].z, inv), gg.z);
-            x[k].w = __fmul_rn(__fmul_rn(x[k].w, inv), gg.w);
+            x[k].x = __fmul_rn(__fmul_rn(x[k].x, inv), gg[k].x);
+            x[k].y = __fmul_rn(__fmul_rn(x[k].y, inv), gg[k].y);
+            x[k].z = __fmul_rn(__fmul_rn(x[k].z, inv), gg[k].z);
+            x[k].w = __fmul_rn(__fmul_rn(x[k].w, inv), gg[k].w);
           }
           if (o4 && f < nf && (v || !out_global)) o4[f] = x[k];
           if (f < nf) m = fmaxf(m, max4_d(x[k]));
@@ -380,7 +385,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       }
       publish();
       trace_point(a, tp++);
-      tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols],
+      tiles1(a.gemms[gi++], [](int) { return make_float2(0.f, 0.f); }, [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols],
                                 uint32_t(&x3)[kDCols]) {
         const int n = c * 128 + chl;
         if (n >= D) return;
@@ -448,11 +453,13 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       publish();
       trace_point(a, tp++);
       // lambda = sigmoid(W_select n s_sel + base), into the latch-gate rows
-      tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols],
-                                uint32_t(&x3)[kDCols]) {
+      tiles1(a.gemms[gi++], [&](int c) {
+        const int n = c * 128 + chl;
+        return make_float2(n < D ? a.latch_base[n] : 0.f, 0.f);
+      }, [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols], uint32_t(&x3)[kDCols]) {
         const int n = c * 128 + chl;
         if (n >= D) return;
-        const float base = a.latch_base[n];
+        const float base = pv.x;
         const float scale = a.gemms[gi - 1].scale;
 #pragma unroll
         for (int j = 0; j < kDCols; ++j)
@@ -510,11 +517,14 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       publish();
       trace_point(a, tp++);
       // hidden = (W1v x s1 + b1v) * sigmoid(W1g x s1 + b1g)   (applyRule layer 1, stream.go:212-220)
-      tiles2(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&v1)[kDCols], uint32_t(&v2)[kDCols],
-                                uint32_t(&v3)[kDCols], uint32_t(&g1)[kDCols], uint32_t(&g2)[kDCols], uint32_t(&g3)[kDCols]) {
+      tiles2(a.gemms[gi++], [&](int c) {
+        const int hu = c * 128 + chl;
+        return hu < H ? make_float2(a.b1[hu], a.b1[H + hu]) : make_float2(0.f, 0.f);
+      }, [&](int c, const float(&stp)[kDCols], uint32_t(&v1)[kDCols], uint32_t(&v2)[kDCols], uint32_t(&v3)[kDCols],
+             uint32_t(&g1)[kDCols], uint32_t(&g2)[kDCols], uint32_t(&g3)[kDCols]) {
         const int hu = c * 128 + chl;
         if (hu >= H) return;
-        const float bv = a.b1[hu], bg = a.b1[H + hu];
+        const float bv = pv.x, bg = pv.y;
         const float scale = a.gemms[gi - 1].scale;
 #pragma unroll
         for (int j = 0; j < kDCols; ++j) {
@@ -544,11 +554,14 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       publish();
       trace_point(a, tp++);
       // o = W2 hidden s2 + b2; gate = sigmoid(o_gate); cur = (1 - gate) cur + gate o_delta (:222-229)
-      tiles2(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&v1)[kDCols], uint32_t(&v2)[kDCols],
-                                uint32_t(&v3)[kDCols], uint32_t(&g1)[kDCols], uint32_t(&g2)[kDCols], uint32_t(&g3)[kDCols]) {
+      tiles2(a.gemms[gi++], [&](int c) {
+        const int d = c * 128 + chl;
+        return d < D ? make_float2(a.b2[d], a.b2[D + d]) : make_float2(0.f, 0.f);
+      }, [&](int c, const float(&stp)[kDCols], uint32_t(&v1)[kDCols], uint32_t(&v2)[kDCols], uint32_t(&v3)[kDCols],
+             uint32_t(&g1)[kDCols], uint32_t(&g2)[kDCols], uint32_t(&g3)[kDCols]) {
         const int d = c * 128 + chl;
         if (d >= D) return;
-        const float bd = a.b2[d], bg = a.b2[D + d];
+        const float bd = pv.x, bg = pv.y;
         const float scale = a.gemms[gi - 1].scale;
 #pragma unroll
         for (int j = 0; j < kDCols; ++j) {
@@ -577,7 +590,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
       publish();
       trace_point(a, tp++);
       const int dh = a.dh;
-      tiles1(a.gemms[gi++], [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols],
+      tiles1(a.gemms[gi++], [](int) { return make_float2(0.f, 0.f); }, [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols],
                                 uint32_t(&x3)[kDCols]) {
         const int n = c * 128 + chl;
         if (n >= 3 * D) return;
