@@ -445,8 +445,9 @@ def main():
     step_ms = sum(ms_arr[:n])
     shares = {names.get(k, str(k)): round(sum(v) / step_ms, 4) for k, v in per_kind.items()}
 
-    # prefill: prompt preparation, 4 x (block + attention), final block, head, select; decode steps likewise
-    launches_per_job = (1 + 2 * 4 + 1 + 2) + (NEW - 1) * (2 * 4 + 1 + 2)
+    # prefill: prompt preparation, 4 x (block + attention), final block, head, select; decode steps:
+    # 4 x (block + attention) and the final block with the greedy head fused in
+    launches_per_job = (1 + 2 * 4 + 1 + 2) + (NEW - 1) * (2 * 4 + 1)
 
     out = None
     if rank == 0:

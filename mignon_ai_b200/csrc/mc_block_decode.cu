@@ -34,6 +34,9 @@ struct DBars {
   uint32_t tmem;
   int valid[kDMaxR], tok[kDMaxR], pos[kDMaxR];
   float rstep[kDMaxR];  // step of each session row of the current GEMM's activation planes
+  // fused head: per quadrant warp, each session's running (max, sum of exp, first argmax)
+  float red_m[4][kDMaxR], red_s[4][kDMaxR];
+  int red_i[4][kDMaxR];
 };
 
 constexpr size_t kDecodeSmemMax = 227 * 1024;  // the per-block opt-in limit of sm_100
@@ -617,7 +620,87 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
 
     trace_point(a, tp++);
     // ---- final RMSNorm (the head's input) ----
-    if (a.final_norm) norm_rows(a.final_gain, a.fnorm, true, a.fnorm_rowmax, false);
+    if (a.final_norm && !a.fuse_head) norm_rows(a.final_gain, a.fnorm, true, a.fnorm_rowmax, false);
+
+    // ---- fused greedy head: logits = E c s_e + head_b (headLogits, stream.go:233-248), then
+    // argmaxProb (generate/greedy.go:90-102): first index of the max, probability 1 / sum exp(l - max)
+    if (a.final_norm && a.fuse_head) {
+      norm_rows(a.final_gain, nullptr, false, nullptr, true);
+      publish();
+      const int step = *a.step;  // read before this CTA's arrival below, so before any increment
+      float hm[kDCols], hs[kDCols];
+      int hi[kDCols];
+#pragma unroll
+      for (int j = 0; j < kDCols; ++j) {
+        hm[j] = -INFINITY;
+        hs[j] = 0.f;
+        hi[j] = 0x7fffffff;
+      }
+      tiles1(a.gemms[gi++], [&](int c) {
+        const int v = c * 128 + chl;
+        return make_float2(v < a.V ? a.head_b[v] : 0.f, 0.f);
+      }, [&](int c, const float(&stp)[kDCols], uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols], uint32_t(&x3)[kDCols]) {
+        const int v = c * 128 + chl;
+        if (v >= a.V) return;
+        const float scale = a.gemms[gi - 1].scale;
+#pragma unroll
+        for (int j = 0; j < kDCols; ++j) {
+          const float l = __fadd_rn(dequant(x1[j], x2[j], x3[j], stp[j], scale), pv.x);
+          if (l > hm[j]) {  // channels arrive in increasing order: ties keep the first index
+            hs[j] = __fmul_rn(hs[j], expf(hm[j] - l));
+            hm[j] = l;
+            hi[j] = v;
+          }
+          hs[j] = __fadd_rn(hs[j], expf(l - hm[j]));
+        }
+      });
+      // combine over the 32 channels of the warp, then over the four quadrant warps
+      auto combine = [](float& m, float& sm, int& i, float m2, float s2, int i2) {
+        const float M = fmaxf(m, m2);
+        if (M == -INFINITY) return;
+        const float sa = m == -INFINITY ? 0.f : __fmul_rn(sm, expf(m - M));
+        const float sb = m2 == -INFINITY ? 0.f : __fmul_rn(s2, expf(m2 - M));
+        i = (m == M && m2 == M) ? min(i, i2) : (m == M ? i : i2);
+        m = M;
+        sm = __fadd_rn(sa, sb);
+      };
+#pragma unroll
+      for (int j = 0; j < kDCols; ++j) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+          const float m2 = __shfl_xor_sync(0xffffffffu, hm[j], o);
+          const float s2 = __shfl_xor_sync(0xffffffffu, hs[j], o);
+          const int i2 = __shfl_xor_sync(0xffffffffu, hi[j], o);
+          combine(hm[j], hs[j], hi[j], m2, s2, i2);
+        }
+        if (lane == 0) {
+          bars->red_m[warp & 3][r0 + j] = hm[j];
+          bars->red_s[warp & 3][r0 + j] = hs[j];
+          bars->red_i[warp & 3][r0 + j] = hi[j];
+        }
+      }
+      row_bar_d();
+      if (t < kDR && bars->valid[t]) {
+        float m = bars->red_m[0][t], sm = bars->red_s[0][t];
+        int i = bars->red_i[0][t];
+        for (int q = 1; q < 4; ++q) combine(m, sm, i, bars->red_m[q][t], bars->red_s[q][t], bars->red_i[q][t]);
+        const int s = s0 + t;
+        a.next_tok[s] = i;
+        if (a.out_tok) a.out_tok[(size_t)s * a.out_stride + step] = i;
+        if (a.out_prob) a.out_prob[(size_t)s * a.out_stride + step] = __fdiv_rn(1.0f, sm);
+        a.pos_w[s] = bars->pos[t] + 1;
+      }
+      // the last CTA to finish advances the step counter (every CTA has read it by then)
+      row_bar_d();
+      if (t == 0) {
+        __threadfence();
+        if (atomicAdd(a.done, 1) == (int)gridDim.x - 1) {
+          *a.step += 1;
+          *a.done = 0;
+          __threadfence();
+        }
+      }
+    }
 
     // ---- the block's output rows for the next kernel ----
     if (!a.final_norm) {

@@ -69,6 +69,18 @@ struct BlockArgs {
   unsigned long long* trace;  // optional phase timestamps of CTA 0 (null: off)
   int trace_fine;             // also time every chunk of every GEMM
   int dec_kt;                 // decode kernel: K tiles of its activation-plane region
+  // decode kernel, final launch with the greedy head fused in (fuse_head): the last GEMM is the
+  // tied head; each session's first argmax and probability (argmaxProb) are written as
+  // select_kernel would, and the last CTA to finish advances the step counter.
+  int fuse_head;
+  const float* head_b;  // [V]
+  int32_t* next_tok;    // [S]
+  int32_t* out_tok;     // [S][out_stride] or null
+  float* out_prob;      // [S][out_stride] or null
+  int out_stride;
+  int32_t* pos_w;       // [S] positions, advanced by one
+  int32_t* step;        // device step counter (output column)
+  int32_t* done;        // finished-CTA counter (zero between launches)
 };
 
 // sigmoidClamped (internal/quant/stream.go:128-136): saturated beyond |x| > 15, else 1/(1+e^-x)

@@ -488,7 +488,7 @@ __global__ void prepare_prompts_kernel(const int32_t* prompts, const int32_t* le
 
 // Enqueues the blocks (and attention sublayers) of one segment: P rows per session, P = 1 a decode
 // step; ends with the final RMSNorm of every row.
-static int enqueue_layers(DevBatch& b, int P, LaunchLog* log) {
+static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = false) {
   const DevModel& m = *b.m;
   cudaStream_t s = b.stream;
   const int nb = (int)m.blocks.size();
@@ -529,6 +529,19 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log) {
       a.block = nb;
       a.embed_first = nb == 0;
       a.final_norm = 1;
+      if (fuse_head) {
+        // the greedy head and selection run inside the final decode launch
+        a.fuse_head = 1;
+        a.gemms[g++] = spec(m.head, kGHead, 0);
+        a.head_b = m.head_b;
+        a.next_tok = b.next_tok;
+        a.out_tok = b.out_tok;
+        a.out_prob = b.out_prob;
+        a.out_stride = b.out_stride;
+        a.pos_w = b.pos;
+        a.step = b.step;
+        a.done = b.sel_done;
+      }
     }
     a.ngemms = g;
     a.trace = b.trace ? b.trace + 64 * bi : nullptr;
@@ -631,8 +644,12 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
                     bool advance_from_len, LaunchLog* log = nullptr) {
   const DevModel& m = *b.m;
   cudaStream_t s = b.stream;
-  int st = enqueue_layers(b, P, log);
+  // greedy decode steps without logits: the head and the selection are fused into the final
+  // decode launch
+  const bool fuse = P == 1 && b.decode_kernel && mode == 0 && !want_logits && !getenv("MC_NO_FUSED_HEAD");
+  int st = enqueue_layers(b, P, log, fuse);
   if (st != kOk) return st;
+  if (fuse) return kOk;
   HeadArgs h;
   memset(&h, 0, sizeof(h));
   h.n_sess = b.S;

@@ -240,6 +240,33 @@ def test_decode_kernel_matches_block_kernel_bitwise(monkeypatch, cfg, vocab):
     gm.close()
 
 
+def test_fused_head_matches_head_kernel(monkeypatch):
+    """Greedy decode steps without logits run the head and the selection inside the final decode
+    launch. The separate head_kernel + select_kernel path (MC_NO_FUSED_HEAD, read when a step is
+    enqueued) computes the same logits, so the tokens are identical (first index of the maximum)
+    and the probabilities agree to float rounding of the sum of exponentials."""
+    spec = small_spec(2)
+    gm = quant.Model.decode(synth.build_model_file(spec))
+    n = 300
+    prompts = synth.prompts_uniform_fast(n, 48, spec.vocab, seed=9)
+    lens = synth.prompt_lengths(n, 1, 48, seed=9)
+    lens[17] = 0
+    got = {}
+    for fused in (True, False):
+        if fused:
+            monkeypatch.delenv("MC_NO_FUSED_HEAD", raising=False)
+        else:
+            monkeypatch.setenv("MC_NO_FUSED_HEAD", "1")
+        b = gm.new_batch(n, 0, 48)
+        got[fused] = b.generate(prompts, lens, 24)
+        b.close()
+    monkeypatch.delenv("MC_NO_FUSED_HEAD", raising=False)
+    act = lens > 0
+    assert np.array_equal(got[True][0][act], got[False][0][act])
+    assert np.allclose(got[True][1][act], got[False][1][act], rtol=1e-5, atol=0)
+    gm.close()
+
+
 def test_model_file_errors():
     """Damaged files are rejected by the engine's own reader (binary_test.go:58-75)."""
     qm = synth.build_model_uniform(16, 8, 8, synth.build_block_configs(2, 3, 2), 0, 0, 16, seed=1)
