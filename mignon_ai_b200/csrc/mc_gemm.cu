@@ -32,8 +32,7 @@ constexpr int kI8Stages = 4;
 constexpr int kI8StageA = kBM * kBK;     // 16 KB
 constexpr int kI8StageB = kI8BN * kBK;   // 32 KB
 constexpr int kI8EpiWarps = 8;
-constexpr int kI8StageStride = 20;  // words per row of an epilogue warp's 32 x 16 staging tile (padded)
-constexpr int kI8Staging = kI8EpiWarps * 32 * kI8StageStride * 4;
+constexpr int kI8Staging = kI8EpiWarps * 32 * 128;  // per epilogue warp: 32 rows x 128 bytes, 16-byte chunks swizzled
 constexpr int kI8Smem = kI8Stages * (kI8StageA + kI8StageB) + kI8Staging + 1024 + 256;  // ring, staging, barriers
 
 struct I8Args {
@@ -58,7 +57,7 @@ __global__ void __launch_bounds__(kI8Threads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
   uint8_t* sb = smem + kI8Stages * kI8StageA;
-  uint32_t* stg = reinterpret_cast<uint32_t*>(sb + kI8Stages * kI8StageB);  // [warp][32][kI8StageStride]
+  uint32_t* stg = reinterpret_cast<uint32_t*>(sb + kI8Stages * kI8StageB);  // [warp][32 rows][32 words]
   uint64_t* full = reinterpret_cast<uint64_t*>(sb + kI8Stages * kI8StageB + kI8Staging);
   uint64_t* empty = full + kI8Stages;
   uint64_t* acc_full = empty + kI8Stages;  // [2]
@@ -148,20 +147,21 @@ __global__ void __launch_bounds__(kI8Threads, 1)
       if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&acc_full[b], (i / 2) & 1, kErrWaitAcc))) break;
       tc_fence_after();
       const float rs = (args.row_scale && row < args.M) ? args.row_scale[row] : 1.0f;
-      uint32_t* st = stg + (size_t)(warp - 2) * 32 * kI8StageStride;
-      // 16 columns at a time: thread = row into the staging tile (conflict-free), then the warp
-      // stores 8 rows x 64 contiguous bytes per instruction
+      uint32_t* st = stg + (size_t)(warp - 2) * 32 * 32;
+      // 32 columns at a time: thread = row writes its 128-byte row into the staging tile with the
+      // 16-byte chunks XOR-swizzled by row (conflict-free), then 8 lanes per row store whole
+      // 128-byte lines (4 rows per instruction)
       for (int pass = 0; pass < 2; ++pass) {
         int32_t* out = pass == 0 ? args.c_i32 : reinterpret_cast<int32_t*>(args.y);
         if (!out) continue;
-        for (int c = half * 128; c < half * 128 + 128; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(tmem_addr(tmem, quad * 32, b * kI8BN + c), r);
+        for (int c = half * 128; c < half * 128 + 128; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem_addr(tmem, quad * 32, b * kI8BN + c), r);
           tmem_wait_ld();
           const int n = n0 + c;
           if (pass == 1) {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
+            for (int e = 0; e < 32; ++e) {
               const float cs = args.col_scale ? args.col_scale[n + e] : 1.0f;
               // Separately rounded multiplies and add (never contracted into an FMA).
               float tv = __fmul_rn((float)(int)r[e], rs);
@@ -171,16 +171,16 @@ __global__ void __launch_bounds__(kI8Threads, 1)
             }
           }
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            *reinterpret_cast<uint4*>(st + lane * kI8StageStride + 4 * j) =
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(st + lane * 32 + 4 * (j ^ (lane & 7))) =
                 make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
           __syncwarp();
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int piece = lane + 32 * i;  // 32 rows x 4 pieces of 16 bytes
-            const int rr = piece >> 2, ch = piece & 3;
+          for (int i = 0; i < 8; ++i) {
+            const int piece = lane + 32 * i;  // 32 rows x 8 chunks of 16 bytes
+            const int rr = piece >> 3, ch = piece & 7;
             const int grow = m0 + quad * 32 + rr;
-            const uint4 v = *reinterpret_cast<const uint4*>(st + rr * kI8StageStride + 4 * ch);
+            const uint4 v = *reinterpret_cast<const uint4*>(st + rr * 32 + 4 * (ch ^ (rr & 7)));
             if (grow < args.M) *reinterpret_cast<uint4*>(out + (size_t)grow * args.N + n + 4 * ch) = v;
           }
           __syncwarp();
