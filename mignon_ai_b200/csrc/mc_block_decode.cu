@@ -4,8 +4,9 @@
 // operation, with the roles of the GEMM operands swapped. The weights are the MMA's M side (128
 // output channels per tile) and the sessions its N side (32 per CTA), so a batch of S sessions
 // spreads over S/32 CTAs (128 CTAs for 4096 sessions, against 32 CTAs of 128 rows). One M-tile's
-// three digit-plane accumulators take 3 x 32 TMEM columns, so four tiles are in flight while the
-// epilogue drains earlier ones. Each epilogue thread owns one output channel (TMEM lane) and
+// three digit planes of each K tile are stacked along N (plane p's rows follow plane p-1's), so one
+// MMA of N = 3 x 32 computes all three plane accumulators: 3 x 32 TMEM columns per M-tile, four
+// tiles in flight while the epilogue drains earlier ones. Each epilogue thread owns one output channel (TMEM lane) and
 // eight sessions (TMEM columns). The GLU value/gate (W1) and highway delta/gate (W2) halves come
 // from two consecutive M-tiles: their weight images hold 128 value rows, then the 128 matching
 // gate rows. The sessions' rows (cur, the norm cell, the latch gate, the hidden layer) stay in
@@ -66,11 +67,13 @@ __device__ __forceinline__ float max4_d(float4 v) {
 }
 
 // The three digit planes of four consecutive activations (K indices e..e+3, e % 4 == 0) of
-// session row r, written into the plane tiles of K tile e / 128 (one 32-bit store per plane).
+// session row r, written into K tile e / 128 (one 32-bit store per plane). A K tile holds the
+// planes stacked as one 3R-row operand: row p * R + r is plane p of session row r (R is a
+// multiple of 8, so the 128-byte swizzle of row r is the same in every plane).
 template <int R>
-__device__ __forceinline__ void put_planes(uint8_t* sB, int KT, int r, int e, float4 v, float inv) {
+__device__ __forceinline__ void put_planes(uint8_t* sB, int r, int e, float4 v, float inv) {
   constexpr int kDBTile = R * 128;  // one digit plane of one K tile of the sessions
-  uint8_t* tile = sB + (e >> 7) * kDBTile;
+  uint8_t* tile = sB + (e >> 7) * 3 * kDBTile;
   const int k = e & 127;
   const uint32_t off = sw128_offset(r, k >> 4) + (k & 15);
   uint32_t a0, a1, a2, a3, b0, b1, b2, b3, c0, c1, c2, c3;
@@ -79,8 +82,8 @@ __device__ __forceinline__ void put_planes(uint8_t* sB, int KT, int r, int e, fl
   slice3_bits(v.z, inv, a2, b2, c2);
   slice3_bits(v.w, inv, a3, b3, c3);
   *reinterpret_cast<uint32_t*>(tile + off) = pack_low_bytes(a0, a1, a2, a3);
-  *reinterpret_cast<uint32_t*>(tile + KT * kDBTile + off) = pack_low_bytes(b0, b1, b2, b3);
-  *reinterpret_cast<uint32_t*>(tile + 2 * KT * kDBTile + off) = pack_low_bytes(c0, c1, c2, c3);
+  *reinterpret_cast<uint32_t*>(tile + kDBTile + off) = pack_low_bytes(b0, b1, b2, b3);
+  *reinterpret_cast<uint32_t*>(tile + 2 * kDBTile + off) = pack_low_bytes(c0, c1, c2, c3);
 }
 
 template <int KF, int R, int WS>  // float4 columns per state row lane (ceil(D / 128)), sessions per CTA, weight stages
@@ -148,7 +151,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
     // ---------------- MMA issuer: D[channel][session] += W[channel][k] * X[session][k] ----------------
     if (lane == 0) {
       uint32_t widx = 0, sidx = 0;
-      const uint32_t idesc = idesc_i8(128, kDR);
+      const uint32_t idesc = idesc_i8(128, 3 * kDR);  // the three planes stacked along N
       bool ok = true;
       for (int g = 0; g < a.ngemms && ok; ++g) {
         const GemmSpec& G = a.gemms[g];
@@ -170,15 +173,10 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
             }
             tc_fence_after();
             const uint64_t da = smem_desc_sw128(sW + st * kTile);
+            const uint64_t db = smem_desc_sw128(sB + kt * 3 * kDBTile);
             const int ksteps = min(4, (G.K - kt * 128 + 31) / 32);
-            // planes innermost: three independent accumulation chains in flight
-            for (int kk = 0; kk < ksteps; ++kk) {
-#pragma unroll
-              for (int p = 0; p < 3; ++p) {
-                const uint64_t db = smem_desc_sw128(sB + (p * KT + kt) * kDBTile);
-                mma_i8(tmem + slot * kDSlotCols + p * kDR, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
-              }
-            }
+            for (int kk = 0; kk < ksteps; ++kk)
+              mma_i8(tmem + slot * kDSlotCols, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
             mma_commit(&bars->w_empty[st]);
           }
           if (!ok) break;
@@ -333,7 +331,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
 #pragma unroll
           for (int k = 0; k < KF; ++k) {
             const int f = lane + 32 * k;
-            if (f < nf) put_planes<R>(sB, KT, rr, 4 * f, x[k], is);
+            if (f < nf) put_planes<R>(sB, rr, 4 * f, x[k], is);
           }
         }
       }
@@ -383,7 +381,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
 #pragma unroll
         for (int k = 0; k < KF; ++k) {
           const int f = lane + 32 * k;
-          if (f < nf) put_planes<R>(sB, KT, rr, 4 * f, v ? a4[f] : make_float4(0.f, 0.f, 0.f, 0.f), is);
+          if (f < nf) put_planes<R>(sB, rr, 4 * f, v ? a4[f] : make_float4(0.f, 0.f, 0.f, 0.f), is);
         }
       }
       publish();
@@ -511,9 +509,9 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
         for (int k = 0; k < KF; ++k) {
           const int f = lane + 32 * k;
           if (f < nf) {
-            put_planes<R>(sB, KT, rr, 4 * f, nv[k], is);
-            put_planes<R>(sB, KT, rr, D + 4 * f, lf[u][k], is);
-            put_planes<R>(sB, KT, rr, 2 * D + 4 * f, lv[k], is);
+            put_planes<R>(sB, rr, 4 * f, nv[k], is);
+            put_planes<R>(sB, rr, D + 4 * f, lf[u][k], is);
+            put_planes<R>(sB, rr, 2 * D + 4 * f, lv[k], is);
           }
         }
       }
@@ -551,7 +549,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
           m = v ? warp_max_d(m) : 0.f;
           if (lane == 0) bars->rstep[rr] = row_step(m);
           const float is = row_inv_step(m);
-          for (int f = lane; f < hf; f += 32) put_planes<R>(sB, KT, rr, 4 * f, v ? h4[f] : make_float4(0.f, 0.f, 0.f, 0.f), is);
+          for (int f = lane; f < hf; f += 32) put_planes<R>(sB, rr, 4 * f, v ? h4[f] : make_float4(0.f, 0.f, 0.f, 0.f), is);
         }
       }
       publish();

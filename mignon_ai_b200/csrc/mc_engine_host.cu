@@ -555,15 +555,10 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
       a.dec_kt = m.dec_kt;
       const int grid = (b.S + m.dec_r - 1) / m.dec_r;
       const int kf = (m.D + 127) / 128;
-      if (m.dec_r == 32) {
-        if (kf == 1) block_decode_kernel<1, 32, 6><<<grid, kDThreads, m.dec_smem, s>>>(a);
-        else if (kf == 2) block_decode_kernel<2, 32, 6><<<grid, kDThreads, m.dec_smem, s>>>(a);
-        else block_decode_kernel<3, 32, 6><<<grid, kDThreads, m.dec_smem, s>>>(a);
-      } else {
-        if (kf == 1) block_decode_kernel<1, 16, 3><<<grid, kDThreads, m.dec_smem, s>>>(a);
-        else if (kf == 2) block_decode_kernel<2, 16, 3><<<grid, kDThreads, m.dec_smem, s>>>(a);
-        else block_decode_kernel<3, 16, 3><<<grid, kDThreads, m.dec_smem, s>>>(a);
-      }
+      void (*kern)(BlockArgs);
+      if (m.dec_r == 32) kern = kf == 1 ? block_decode_kernel<1, 32, 6> : kf == 2 ? block_decode_kernel<2, 32, 6> : block_decode_kernel<3, 32, 6>;
+      else kern = kf == 1 ? block_decode_kernel<1, 16, 3> : kf == 2 ? block_decode_kernel<2, 16, 3> : block_decode_kernel<3, 16, 3>;
+      kern<<<grid, kDThreads, m.dec_smem, s>>>(a);
     } else {
       switch ((m.D + 127) / 128) {
         case 1: block_kernel<1><<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
@@ -599,14 +594,16 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
         const long long items = (long long)b.S * m.heads;
         const int grid = (int)std::min<long long>((items + stg.warps - 1) / stg.warps, b.n_sm);
         const int threads = stg.warps * 32;
+        void (*kern)(AttnArgs);
         switch (aa.dh) {
-          case 4: attn_decode_staged_kernel<4><<<grid, threads, stg.smem, s>>>(aa); break;
-          case 8: attn_decode_staged_kernel<8><<<grid, threads, stg.smem, s>>>(aa); break;
-          case 16: attn_decode_staged_kernel<16><<<grid, threads, stg.smem, s>>>(aa); break;
-          case 32: attn_decode_staged_kernel<32><<<grid, threads, stg.smem, s>>>(aa); break;
-          case 48: attn_decode_staged_kernel<48><<<grid, threads, stg.smem, s>>>(aa); break;
-          default: attn_decode_staged_kernel<64><<<grid, threads, stg.smem, s>>>(aa); break;
+          case 4: kern = attn_decode_staged_kernel<4>; break;
+          case 8: kern = attn_decode_staged_kernel<8>; break;
+          case 16: kern = attn_decode_staged_kernel<16>; break;
+          case 32: kern = attn_decode_staged_kernel<32>; break;
+          case 48: kern = attn_decode_staged_kernel<48>; break;
+          default: kern = attn_decode_staged_kernel<64>; break;
         }
+        kern<<<grid, threads, stg.smem, s>>>(aa);
       } else if (P == 1) {
         const long long warps = (long long)b.S * m.heads;
         const int grid = (int)((warps * 32 + kAttnThreads - 1) / kAttnThreads);
