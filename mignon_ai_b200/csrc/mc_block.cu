@@ -656,6 +656,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
           }
           a.latch[st_off * D + d] = l;
         }
+        if (a.trace && a.trace_fine) trace_point(a, tp++);
         // (2) left neighbours n(pos - dil): from the segment, or from the ring before it
         for (int idx = t; idx < kRows * D; idx += kRowThreads) {
           const int rr = idx / D, d = idx - rr * D;
@@ -671,6 +672,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
           x[D + d] = left;
         }
         row_bar();
+        if (a.trace && a.trace_fine) trace_point(a, tp++);
         // (3) the ring keeps the segment's last norm cells
         for (int task = t; task < a.spt * D; task += kRowThreads) {
           const int slot = task / D, d = task - slot * D;
@@ -682,6 +684,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
           for (int tt = max(0, len - a.ring); tt < len; ++tt)
             rg[(size_t)((p0 + tt) % a.ring) * D] = a.xbuf[(size_t)(tile * kRows + slot * a.P + tt) * 3 * D + d];
         }
+        if (a.trace && a.trace_fine) trace_point(a, tp++);
         // (4) max |x| of each row, one warp per row
 #pragma unroll 2
         for (int u = 0; u < kRowsPerWarp; ++u) {

@@ -1,13 +1,15 @@
-// The decode block kernel: one CTA advances 32 sessions by one position through one CA block.
+// The decode block kernel: one CTA advances R sessions (16 or 32) by one position through one CA
+// block.
 //
 // The arithmetic is block_kernel's (mc_block.cu) for one position per session, operation for
 // operation, with the roles of the GEMM operands swapped. The weights are the MMA's M side (128
-// output channels per tile) and the sessions its N side (32 per CTA), so a batch of S sessions
-// spreads over S/32 CTAs (128 CTAs for 4096 sessions, against 32 CTAs of 128 rows). One M-tile's
-// three digit planes of each K tile are stacked along N (plane p's rows follow plane p-1's), so one
-// MMA of N = 3 x 32 computes all three plane accumulators: 3 x 32 TMEM columns per M-tile, four
-// tiles in flight while the epilogue drains earlier ones. Each epilogue thread owns one output channel (TMEM lane) and
-// eight sessions (TMEM columns). The GLU value/gate (W1) and highway delta/gate (W2) halves come
+// output channels per tile) and the sessions its N side (R per CTA), so a batch of S sessions
+// spreads over S/R CTAs (at state width 128: 256 CTAs of 16 sessions for 4096 sessions, two per
+// multiprocessor, against 32 CTAs of 128 rows). The three digit planes of each K tile are
+// stacked along N (plane p's rows follow plane p-1's), so one MMA of N = 3R computes all three
+// plane accumulators: 3R TMEM columns per M-tile, four tiles in flight while the epilogue drains
+// earlier ones. Each epilogue thread owns one output channel (TMEM lane) and
+// R/4 sessions (TMEM columns). The GLU value/gate (W1) and highway delta/gate (W2) halves come
 // from two consecutive M-tiles: their weight images hold 128 value rows, then the 128 matching
 // gate rows. The sessions' rows (cur, the norm cell, the latch gate, the hidden layer) stay in
 // shared memory for the whole block; only the session state (latch, norm ring, key/value ring)
@@ -15,7 +17,8 @@
 //
 // Roles: 16 row warps (row phases: one warp per session row; epilogues: thread = channel), one
 // MMA warp (one elected thread issues tcgen05.mma), one producer warp (bulk copies of the
-// pre-tiled weight tiles through a 6-stage ring). All mbarrier waits are bounded.
+// pre-tiled weight tiles through a 6-stage ring, 3 stages at R = 16). All mbarrier waits are
+// bounded.
 #include "mc_engine.cuh"
 
 namespace mc {
@@ -41,6 +44,7 @@ struct DBars {
 };
 
 constexpr size_t kDecodeSmemMax = 227 * 1024;  // the per-block opt-in limit of sm_100
+constexpr size_t kSmemPerSm = 228 * 1024;      // shared memory of one sm_100 multiprocessor (1 KB reserved per CTA)
 
 // Dynamic shared memory of the decode kernel for state width D, hidden width H, kt K tiles of
 // activation planes (kt = ceil(max(3D, H) / 128)), R sessions per CTA and ws weight stages.
@@ -86,14 +90,20 @@ __device__ __forceinline__ void put_planes(uint8_t* sB, int r, int e, float4 v, 
   *reinterpret_cast<uint32_t*>(tile + 2 * kDBTile + off) = pack_low_bytes(c0, c1, c2, c3);
 }
 
+// CTAs of the decode kernel resident on one multiprocessor: two for 16 sessions per CTA at state
+// widths up to 128 (each then holds half of the TMEM and at most 56 registers per thread), so the
+// latency chains of two CTAs interleave; one otherwise.
+__host__ __device__ constexpr int decode_ctas_per_sm(int kf, int r) { return (r == 16 && kf == 1) ? 2 : 1; }
+
 template <int KF, int R, int WS>  // float4 columns per state row lane (ceil(D / 128)), sessions per CTA, weight stages
-__global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid_constant__ BlockArgs a) {
+__global__ void __launch_bounds__(kDThreads, decode_ctas_per_sm(KF, R)) block_decode_kernel(const __grid_constant__ BlockArgs a) {
   constexpr int kDR = R;
   constexpr int kDWStages = WS;
   constexpr int kDBTile = R * 128;               // one digit plane of one K tile of the sessions
   constexpr int kDRowsPerWarp = R / kDRowWarps;  // session rows per row warp
   constexpr int kDCols = R / 4;                  // sessions per epilogue thread
   constexpr int kDSlotCols = R == 32 ? 128 : 64; // three planes of R columns, padded
+  constexpr uint32_t kDTmemCols = kDSlots * kDSlotCols;  // 512 or 256 (a power of two >= 32)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int D = a.D, H = a.H, KT = a.dec_kt;
@@ -120,7 +130,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
     mbar_init(&bars->b_full, kDRowThreads);
     fence_barrier_init();
   }
-  if (warp == kDMmaWarp) tmem_alloc(&bars->tmem, 512);
+  if (warp == kDMmaWarp) tmem_alloc(&bars->tmem, kDTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -720,7 +730,7 @@ __global__ void __launch_bounds__(kDThreads, 1) block_decode_kernel(const __grid
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kDMmaWarp) tmem_dealloc(tmem, 512);
+  if (warp == kDMmaWarp) tmem_dealloc(tmem, kDTmemCols);
 }
 
 }  // namespace eng

@@ -105,7 +105,7 @@ struct DevModel {
   int device = 0;
   int V = 0, D = 0, H = 0, max_context = 0, heads = 0, window = 0, cache = 0, ring = 0, total_steps = 0, n_attn = 0;
   int dec_kt = 0;         // decode kernel: K tiles of its activation planes
-  int dec_r = 32;         // decode kernel: sessions per CTA (32, or 16 for wide models)
+  int dec_r = 32;         // decode kernel: sessions per CTA (16 or 32)
   size_t dec_smem = 0;    // decode kernel: dynamic shared memory
   bool dec_ok = false;    // the decode kernel fits this model (else decode uses block_kernel)
   bool tied = true;
@@ -231,13 +231,15 @@ int build_dev_model(const HostModel& hm, int device, std::unique_ptr<DevModel>& 
   m->ring = longest + 1;
   m->n_attn = nattn;
   m->dec_kt = (std::max(3 * D, H) + 127) / 128;
-  // 32 sessions per CTA with a 6-stage weight ring, or (wide models) 16 with 3 stages
-  m->dec_r = 32;
-  m->dec_smem = decode_smem_bytes(D, H, m->dec_kt, 32, 6);
-  if (m->dec_smem > kDecodeSmemMax) {
-    m->dec_r = 16;
-    m->dec_smem = decode_smem_bytes(D, H, m->dec_kt, 16, 3);
-  }
+  // Sessions per CTA: 16 with a 3-stage weight ring where two such CTAs share a multiprocessor
+  // (state width <= 128: their latency chains interleave), else 32 with a 6-stage ring, else
+  // (wide models) 16 with 3 stages, one CTA per multiprocessor. MC_DECODE_R=16 / 32 forces one.
+  const size_t smem16 = decode_smem_bytes(D, H, m->dec_kt, 16, 3), smem32 = decode_smem_bytes(D, H, m->dec_kt, 32, 6);
+  const bool pair16 = decode_ctas_per_sm((D + 127) / 128, 16) == 2 && 2 * (smem16 + 1024) <= kSmemPerSm;
+  const char* rsel = getenv("MC_DECODE_R");
+  const int want = rsel ? atoi(rsel) : 0;
+  m->dec_r = (want == 16 || (want != 32 && pair16) || smem32 > kDecodeSmemMax) ? 16 : 32;
+  m->dec_smem = m->dec_r == 16 ? smem16 : smem32;
   m->dec_ok = m->dec_smem <= kDecodeSmemMax;
   if (nattn > 0 && m->cache > 128) return set_error(kUnsupported, "attention caches above 128 positions");
   out = std::move(m);
@@ -323,6 +325,9 @@ static int ensure_attrs(int device) {
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<2, 32, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<3, 32, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<1, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
+  // two CTAs of this instance share a multiprocessor: ask for the largest shared-memory carveout
+  MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<1, 16, 3>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               (int)cudaSharedmemCarveoutMaxShared));
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<2, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<3, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem));
@@ -339,6 +344,9 @@ static int ensure_attrs(int device) {
   MC_CUDA(cudaFuncSetAttribute(attn_prefill_fast_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
   MC_CUDA(cudaFuncSetAttribute(attn_prefill_fast_kernel<48>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
   MC_CUDA(cudaFuncSetAttribute(attn_prefill_fast_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+  // several prefill CTAs (a few tens of KB each) share a multiprocessor
+  MC_CUDA(cudaFuncSetAttribute(attn_prefill_fast_kernel<32>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               (int)cudaSharedmemCarveoutMaxShared));
   if (device < 64) g_attr_done[device] = true;
   return kOk;
 }

@@ -210,15 +210,22 @@ def test_score_matches_oracle(oracle):
     b.close()
 
 
-@pytest.mark.parametrize("cfg,vocab", [(2, None), (1, None), (3, 1024), (4, 512)])
-def test_decode_kernel_matches_block_kernel_bitwise(monkeypatch, cfg, vocab):
+@pytest.mark.parametrize("cfg,vocab,dec_r", [(2, None, None), (1, None, None), (3, 1024, None), (4, 512, None),
+                                             (2, None, "32")])
+def test_decode_kernel_matches_block_kernel_bitwise(monkeypatch, cfg, vocab, dec_r):
     """Decode steps run on block_decode_kernel (weights on the MMA's M side, 32 sessions per CTA);
     block_kernel (128 session rows per CTA) computes the same float32 operations in the same
     order, so the two give bit-identical logits, tokens and probabilities (MC_DECODE_KERNEL=block
-    selects block_kernel for a batch opened under it). Ragged and idle sessions included."""
+    selects block_kernel for a batch opened under it). Ragged and idle sessions included.
+    Configs 1 and 2 run the 16-sessions-per-CTA instance (two CTAs per multiprocessor at state
+    width 128), configs 3 and 4 the wide one; dec_r "32": the model is loaded under
+    MC_DECODE_R=32, the 32-sessions-per-CTA instance."""
     spec = small_spec(cfg, vocab)
     data = synth.build_model_file(spec)
+    if dec_r:
+        monkeypatch.setenv("MC_DECODE_R", dec_r)
     gm = quant.Model.decode(data)
+    monkeypatch.delenv("MC_DECODE_R", raising=False)
     n = 200
     prompts = synth.prompts_uniform_fast(n, 48, spec.vocab, seed=5)
     lens = np.full(n, 48, np.int32)
