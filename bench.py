@@ -73,7 +73,7 @@ def max_over_ranks(ms, dist, device):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms during the timed region."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -84,11 +84,23 @@ class ClockSampler:
         self.p = None
 
     def start(self):
+        """Starts the sampler and waits (at most 5 s) for its first line, so that the samples
+        taken while the timed region runs are the ones that follow; those earlier are dropped."""
+        self.skip = 0
         try:
             self.p = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                       "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 5.0 and self.p.poll() is None:
+            with open(self.f.name) as fh:
+                n = sum(1 for line in fh if line.endswith("\n"))
+            if n > 0:
+                self.skip = n
+                break
+            time.sleep(0.02)
 
     def stop(self):
         if self.p:
@@ -100,7 +112,9 @@ class ClockSampler:
         self.f.flush()
         rows = []
         with open(self.f.name) as fh:
-            for line in fh:
+            for i, line in enumerate(fh):
+                if i < self.skip:
+                    continue
                 parts = [x.strip() for x in line.split(",")]
                 if len(parts) < 9:
                     continue

@@ -90,6 +90,11 @@ __device__ __forceinline__ void put_planes(uint8_t* sB, int r, int e, float4 v, 
   *reinterpret_cast<uint32_t*>(tile + 2 * kDBTile + off) = pack_low_bytes(c0, c1, c2, c3);
 }
 
+// M-tiles whose MMAs the decode kernel interleaves: the value/gate pairs of W1 and W2 (their
+// epilogue needs both tiles at once: two independent accumulation chains in flight finish the pair
+// sooner than one chain after the other); single tiles otherwise.
+__device__ __forceinline__ int decode_mma_group(const GemmSpec& G) { return (G.type == kGW1 || G.type == kGW2) ? 2 : 1; }
+
 // CTAs of the decode kernel resident on one multiprocessor: two for 16 sessions per CTA at state
 // widths up to 128 (each then holds half of the TMEM and at most 56 registers per thread), so the
 // latency chains of two CTAs interleave; one otherwise.
@@ -143,18 +148,20 @@ __global__ void __launch_bounds__(kDThreads, decode_ctas_per_sm(KF, R)) block_de
       bool ok = true;
       for (int g = 0; g < a.ngemms && ok; ++g) {
         const GemmSpec& G = a.gemms[g];
-        for (int c = 0; c < G.nchunks && ok; ++c)
-          for (int kt = 0; kt < G.ktiles; ++kt, ++widx) {
-            const int st = widx % kDWStages;
-            if (widx >= kDWStages &&
-                !mbar_wait_or_abort(&bars->w_empty[st], ((widx / kDWStages) - 1) & 1, kErrWaitEmpty)) {
-              ok = false;
-              break;
+        const int gs = decode_mma_group(G);
+        for (int c0 = 0; c0 < G.nchunks && ok; c0 += gs)
+          for (int kt = 0; kt < G.ktiles && ok; ++kt)
+            for (int c = c0; c < c0 + gs && c < G.nchunks; ++c, ++widx) {
+              const int st = widx % kDWStages;
+              if (widx >= kDWStages &&
+                  !mbar_wait_or_abort(&bars->w_empty[st], ((widx / kDWStages) - 1) & 1, kErrWaitEmpty)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(&bars->w_full[st], kTile);
+              bulk_load_hint(sW + st * kTile, G.tiles + ((size_t)c * G.ktiles + kt) * kTile, kTile, &bars->w_full[st],
+                             l2_policy_evict_last());
             }
-            mbar_arrive_expect_tx(&bars->w_full[st], kTile);
-            bulk_load_hint(sW + st * kTile, G.tiles + ((size_t)c * G.ktiles + kt) * kTile, kTile, &bars->w_full[st],
-                           l2_policy_evict_last());
-          }
       }
     }
   } else if (warp == kDMmaWarp) {
@@ -167,30 +174,38 @@ __global__ void __launch_bounds__(kDThreads, decode_ctas_per_sm(KF, R)) block_de
         const GemmSpec& G = a.gemms[g];
         if (!mbar_wait_or_abort(&bars->b_full, g & 1, kErrWaitFull)) break;
         tc_fence_after();
-        for (int c = 0; c < G.nchunks && ok; ++c, ++sidx) {
-          const int slot = sidx % kDSlots;
-          if (sidx >= kDSlots &&
-              !mbar_wait_or_abort(&bars->s_empty[slot], ((sidx / kDSlots) - 1) & 1, kErrWaitAccFree)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          for (int kt = 0; kt < G.ktiles; ++kt, ++widx) {
-            const int st = widx % kDWStages;
-            if (!mbar_wait_or_abort(&bars->w_full[st], (widx / kDWStages) & 1, kErrWaitFull)) {
+        // gs M-tiles at a time (a value/gate pair: two independent accumulation chains, their
+        // MMAs alternating K step by K step), each in its own TMEM slot
+        const int gs = decode_mma_group(G);
+        for (int c0 = 0; c0 < G.nchunks && ok; c0 += gs) {
+          const int n = min(gs, G.nchunks - c0);
+          for (int q = 0; q < n && ok; ++q) {
+            const uint32_t si = sidx + q;
+            if (si >= kDSlots && !mbar_wait_or_abort(&bars->s_empty[si % kDSlots], ((si / kDSlots) - 1) & 1, kErrWaitAccFree))
               ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint64_t da = smem_desc_sw128(sW + st * kTile);
-            const uint64_t db = smem_desc_sw128(sB + kt * 3 * kDBTile);
-            const int ksteps = min(4, (G.K - kt * 128 + 31) / 32);
-            for (int kk = 0; kk < ksteps; ++kk)
-              mma_i8(tmem + slot * kDSlotCols, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
-            mma_commit(&bars->w_empty[st]);
           }
           if (!ok) break;
-          mma_commit(&bars->s_full[slot]);
+          tc_fence_after();
+          for (int kt = 0; kt < G.ktiles && ok; ++kt) {
+            const uint64_t db = smem_desc_sw128(sB + kt * 3 * kDBTile);
+            const int ksteps = min(4, (G.K - kt * 128 + 31) / 32);
+            for (int q = 0; q < n; ++q, ++widx) {
+              const int st = widx % kDWStages;
+              if (!mbar_wait_or_abort(&bars->w_full[st], (widx / kDWStages) & 1, kErrWaitFull)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint64_t da = smem_desc_sw128(sW + st * kTile);
+              const uint32_t dt = tmem + ((sidx + q) % kDSlots) * kDSlotCols;
+              for (int kk = 0; kk < ksteps; ++kk)
+                mma_i8(dt, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+              mma_commit(&bars->w_empty[st]);
+            }
+          }
+          if (!ok) break;
+          for (int q = 0; q < n; ++q) mma_commit(&bars->s_full[(sidx + q) % kDSlots]);
+          sidx += n;
         }
       }
     }
