@@ -657,45 +657,99 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
           a.latch[st_off * D + d] = l;
         }
         if (a.trace && a.trace_fine) trace_point(a, tp++);
-        // (2) left neighbours n(pos - dil): from the segment, or from the ring before it
-        for (int idx = t; idx < kRows * D; idx += kRowThreads) {
-          const int rr = idx / D, d = idx - rr * D;
-          if (!bars->rvalid[rr]) continue;
-          const int slot = rr / a.P, tt = rr - slot * a.P;
-          const int sess = tile * a.spt + slot;
-          const int p0 = a.pos0[sess];
-          float* x = a.xbuf + (size_t)(tile * kRows + rr) * 3 * D;
-          float left = 0.f;
-          if (tt >= dil) left = a.xbuf[(size_t)(tile * kRows + rr - dil) * 3 * D + d];
-          else if (p0 + tt - dil >= 0)
-            left = a.norm_ring[((size_t)sess * a.total_steps + bs) * a.ring * D + (size_t)((p0 + tt - dil) % a.ring) * D + d];
-          x[D + d] = left;
-        }
-        row_bar();
-        if (a.trace && a.trace_fine) trace_point(a, tp++);
-        // (3) the ring keeps the segment's last norm cells
-        for (int task = t; task < a.spt * D; task += kRowThreads) {
-          const int slot = task / D, d = task - slot * D;
-          const int sess = tile * a.spt + slot;
-          if (sess >= a.n_sess) continue;
-          const int len = a.seglen[sess];
-          const int p0 = a.pos0[sess];
-          float* rg = a.norm_ring + ((size_t)sess * a.total_steps + bs) * a.ring * D + d;
-          for (int tt = max(0, len - a.ring); tt < len; ++tt)
-            rg[(size_t)((p0 + tt) % a.ring) * D] = a.xbuf[(size_t)(tile * kRows + slot * a.P + tt) * 3 * D + d];
-        }
-        if (a.trace && a.trace_fine) trace_point(a, tp++);
-        // (4) max |x| of each row, one warp per row
+        if (w1_resident) {
+          // (2) one warp per row: the left neighbour n(pos - dil) (from the segment, or from the
+          //     ring before it), max |x| over x = [n | left | latch], and x sliced straight into
+          //     W1's A slots (no fp32 copy of x goes back to memory). x = one float4 per lane.
+          row_bar();  // the latch scan's rows
+          const int kts = a.gemms[g].ktiles;
+          for (int kt = 0; kt < kts; ++kt) acquire(kt % kASlots);
 #pragma unroll 2
-        for (int u = 0; u < kRowsPerWarp; ++u) {
-          const int rr = warp + kRowWarps * u;
-          float m = 0.f;
-          if (bars->rvalid[rr]) {
-            const float* x = a.xbuf + (size_t)(tile * kRows + rr) * 3 * D;
-            for (int e = lane; e < 3 * D; e += 32) m = fmaxf(m, fabsf(x[e]));
+          for (int u = 0; u < kRowsPerWarp; ++u) {
+            const int rr = warp + kRowWarps * u;
+            const bool v = bars->rvalid[rr] != 0;
+            const int tt = rr - (rr / a.P) * a.P;
+            const int sess = bars->rsess[rr], lpos = bars->rpos[rr] - dil;
+            const bool in = v && lane < nf;
+            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4* x4 = reinterpret_cast<const float4*>(a.xbuf + (size_t)(tile * kRows + rr) * 3 * D);
+            float4 nv = z, lt = z, lf = z;
+            if (in) {
+              nv = x4[lane];
+              lt = x4[2 * nf + lane];
+              if (tt >= dil)
+                lf = reinterpret_cast<const float4*>(a.xbuf + (size_t)(tile * kRows + rr - dil) * 3 * D)[lane];
+              else if (lpos >= 0)
+                lf = reinterpret_cast<const float4*>(a.norm_ring + ((size_t)sess * a.total_steps + bs) * a.ring * D +
+                                                     (size_t)(lpos % a.ring) * D)[lane];
+            }
+            float m = fmaxf(max4(nv), fmaxf(max4(lf), max4(lt)));
+            m = v ? warp_max(m) : 0.f;
+            if (lane == 0) bars->rowmax_a[rr] = m;
+            const float is = row_inv_step(m);
+            if (lane < nf) {
+              put4(sA, rr, 4 * lane, nv, is);
+              put4(sA, rr, D + 4 * lane, lf, is);
+              put4(sA, rr, 2 * D + 4 * lane, lt, is);
+            }
           }
-          m = warp_max(m);
-          if (lane == 0) bars->rowmax_a[rr] = m;
+          for (int kt = 0; kt < kts; ++kt) publish(kt % kASlots);
+          w1_prefilled = true;
+          row_bar();  // row maxima; the ring reads above come before the ring writes below
+          if (a.trace && a.trace_fine) trace_point(a, tp++);
+          // (3) the ring keeps the segment's last norm cells
+          for (int task = t; task < a.spt * D; task += kRowThreads) {
+            const int slot = task / D, d = task - slot * D;
+            const int sess = tile * a.spt + slot;
+            if (sess >= a.n_sess) continue;
+            const int len = a.seglen[sess];
+            const int p0 = a.pos0[sess];
+            float* rg = a.norm_ring + ((size_t)sess * a.total_steps + bs) * a.ring * D + d;
+            for (int tt = max(0, len - a.ring); tt < len; ++tt)
+              rg[(size_t)((p0 + tt) % a.ring) * D] = a.xbuf[(size_t)(tile * kRows + slot * a.P + tt) * 3 * D + d];
+          }
+          if (a.trace && a.trace_fine) trace_point(a, tp++);
+        } else {
+          // (2) left neighbours n(pos - dil): from the segment, or from the ring before it
+          for (int idx = t; idx < kRows * D; idx += kRowThreads) {
+            const int rr = idx / D, d = idx - rr * D;
+            if (!bars->rvalid[rr]) continue;
+            const int slot = rr / a.P, tt = rr - slot * a.P;
+            const int sess = tile * a.spt + slot;
+            const int p0 = a.pos0[sess];
+            float* x = a.xbuf + (size_t)(tile * kRows + rr) * 3 * D;
+            float left = 0.f;
+            if (tt >= dil) left = a.xbuf[(size_t)(tile * kRows + rr - dil) * 3 * D + d];
+            else if (p0 + tt - dil >= 0)
+              left = a.norm_ring[((size_t)sess * a.total_steps + bs) * a.ring * D + (size_t)((p0 + tt - dil) % a.ring) * D + d];
+            x[D + d] = left;
+          }
+          row_bar();
+          if (a.trace && a.trace_fine) trace_point(a, tp++);
+          // (3) the ring keeps the segment's last norm cells
+          for (int task = t; task < a.spt * D; task += kRowThreads) {
+            const int slot = task / D, d = task - slot * D;
+            const int sess = tile * a.spt + slot;
+            if (sess >= a.n_sess) continue;
+            const int len = a.seglen[sess];
+            const int p0 = a.pos0[sess];
+            float* rg = a.norm_ring + ((size_t)sess * a.total_steps + bs) * a.ring * D + d;
+            for (int tt = max(0, len - a.ring); tt < len; ++tt)
+              rg[(size_t)((p0 + tt) % a.ring) * D] = a.xbuf[(size_t)(tile * kRows + slot * a.P + tt) * 3 * D + d];
+          }
+          if (a.trace && a.trace_fine) trace_point(a, tp++);
+          // (4) max |x| of each row, one warp per row
+#pragma unroll 2
+          for (int u = 0; u < kRowsPerWarp; ++u) {
+            const int rr = warp + kRowWarps * u;
+            float m = 0.f;
+            if (bars->rvalid[rr]) {
+              const float* x = a.xbuf + (size_t)(tile * kRows + rr) * 3 * D;
+              for (int e = lane; e < 3 * D; e += 32) m = fmaxf(m, fabsf(x[e]));
+            }
+            m = warp_max(m);
+            if (lane == 0) bars->rowmax_a[rr] = m;
+          }
         }
         row_bar();
       }
