@@ -128,13 +128,18 @@ __device__ __forceinline__ void load_acc16(uint32_t tmem, int warp, int col, uin
   tmem_wait_ld();
 }
 
-// 8 columns of the three slice accumulators (warp-collective).
-__device__ __forceinline__ void load_acc8(uint32_t tmem, int warp, int col, uint32_t (&a1)[8], uint32_t (&a2)[8],
-                                         uint32_t (&a3)[8]) {
-  const uint32_t base = tmem_addr(tmem, 32 * (warp & 3), col);
-  tmem_ld8(base, a1);
-  tmem_ld8(base + kNC, a2);
-  tmem_ld8(base + 2 * kNC, a3);
+// 8 columns of the three slice accumulators at two column offsets (a value tile and its gate
+// tile): all six loads in flight before one wait (warp-collective).
+__device__ __forceinline__ void load_acc8x2(uint32_t tmem, int warp, int col_a, int col_b, uint32_t (&a1)[8],
+                                           uint32_t (&a2)[8], uint32_t (&a3)[8], uint32_t (&b1)[8], uint32_t (&b2)[8],
+                                           uint32_t (&b3)[8]) {
+  const uint32_t ba = tmem_addr(tmem, 32 * (warp & 3), col_a), bb = tmem_addr(tmem, 32 * (warp & 3), col_b);
+  tmem_ld8(ba, a1);
+  tmem_ld8(ba + kNC, a2);
+  tmem_ld8(ba + 2 * kNC, a3);
+  tmem_ld8(bb, b1);
+  tmem_ld8(bb + kNC, b2);
+  tmem_ld8(bb + 2 * kNC, b3);
   tmem_wait_ld();
 }
 
@@ -766,15 +771,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
             ld8(a.b1, u0, H, bv);
             ld8(a.b1 + H, u0, H, bg);
           }
-          uint32_t x1[8], x2[8], x3[8];
-          load_acc8(tmem, warp, j0, x1, x2, x3);  // value columns
+          uint32_t x1[8], x2[8], x3[8], y1[8], y2[8], y3[8];
+          load_acc8x2(tmem, warp, j0, kHalfChunk + j0, x1, x2, x3, y1, y2, y3);  // value and gate columns
 #pragma unroll
           for (int j = 0; j < 8; ++j) hid[j] = __fadd_rn(dequant(x1[j], x2[j], x3[j], step, scale), bv[j]);
-          load_acc8(tmem, warp, kHalfChunk + j0, x1, x2, x3);  // gate columns
           if (act) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              const float gt = __fadd_rn(dequant(x1[j], x2[j], x3[j], step, scale), bg[j]);
+              const float gt = __fadd_rn(dequant(y1[j], y2[j], y3[j], step, scale), bg[j]);
               hid[j] = __fmul_rn(hid[j], sigmoid_clamped(gt));
               if (u0 + j < H) hmax = fmaxf(hmax, fabsf(hid[j]));
             }
@@ -796,15 +800,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
             ld8(a.b2 + D, d0, D, bg);
             ld8(crow, d0, D, cv);
           }
-          uint32_t x1[8], x2[8], x3[8];
-          load_acc8(tmem, warp, j0, x1, x2, x3);  // delta columns
+          uint32_t x1[8], x2[8], x3[8], y1[8], y2[8], y3[8];
+          load_acc8x2(tmem, warp, j0, kHalfChunk + j0, x1, x2, x3, y1, y2, y3);  // delta and gate columns
 #pragma unroll
           for (int j = 0; j < 8; ++j) od[j] = __fadd_rn(dequant(x1[j], x2[j], x3[j], step, scale), bd[j]);
-          load_acc8(tmem, warp, kHalfChunk + j0, x1, x2, x3);  // gate columns
           if (act) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              const float og = __fadd_rn(dequant(x1[j], x2[j], x3[j], step, scale), bg[j]);
+              const float og = __fadd_rn(dequant(y1[j], y2[j], y3[j], step, scale), bg[j]);
               const float gate = sigmoid_clamped(og);
               cv[j] = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, gate), cv[j]), __fmul_rn(gate, od[j]));
             }

@@ -249,7 +249,8 @@ __global__ void __launch_bounds__(kDThreads, decode_ctas_per_sm(KF, R)) block_de
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->s_empty[slot]);
     };
-    auto acc8 = [&](int slot, uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols], uint32_t(&x3)[kDCols]) {
+    // this thread's three plane accumulators of a slot: loads issued (acc_issue), then waited for
+    auto acc_issue = [&](int slot, uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols], uint32_t(&x3)[kDCols]) {
       const uint32_t base = tmem_addr(tmem, 32 * (warp & 3), slot * kDSlotCols + r0);
       if constexpr (kDCols == 8) {
         tmem_ld8(base, x1);
@@ -260,6 +261,9 @@ __global__ void __launch_bounds__(kDThreads, decode_ctas_per_sm(KF, R)) block_de
         tmem_ld4(base + kDR, x2);
         tmem_ld4(base + 2 * kDR, x3);
       }
+    };
+    auto acc8 = [&](int slot, uint32_t(&x1)[kDCols], uint32_t(&x2)[kDCols], uint32_t(&x3)[kDCols]) {
+      acc_issue(slot, x1, x2, x3);
       tmem_wait_ld();
     };
     auto load_steps = [&](float(&stp)[kDCols]) {
@@ -294,10 +298,11 @@ __global__ void __launch_bounds__(kDThreads, decode_ctas_per_sm(KF, R)) block_de
         uint32_t v1[kDCols], v2[kDCols], v3[kDCols], g1[kDCols], g2[kDCols], g3[kDCols];
         pv = pre(c / 2);
         wait_slot(sv, sidx);
-        acc8(sv, v1, v2, v3);
-        wait_slot(sg, sidx + 1);
+        wait_slot(sg, sidx + 1);  // the pair's MMAs complete together
         if (a.trace_fine) trace_point(a, tp++);
-        acc8(sg, g1, g2, g3);
+        acc_issue(sv, v1, v2, v3);
+        acc_issue(sg, g1, g2, g3);
+        tmem_wait_ld();
         release_slot(sv);
         release_slot(sg);
         fn(c / 2, stp, v1, v2, v3, g1, g2, g3);
