@@ -164,6 +164,15 @@ int run_graph_step(DevBatch& sh, int mode, double inv_temp, uint32_t session0, b
   return kOk;
 }
 
+// The n_new - 1 decode steps after a prefill: one captured step graph per step.
+int run_decode_steps(DevBatch& sh, int n_new, int mode, double inv_temp, uint32_t session0) {
+  for (int t = 1; t < n_new; ++t) {
+    const int st = run_graph_step(sh, mode, inv_temp, session0, false);
+    if (st != kOk) return st;
+  }
+  return kOk;
+}
+
 }  // namespace
 
 extern "C" {
@@ -399,8 +408,7 @@ int mc_generate(mc_batch* b, const int32_t* prompts, const int32_t* lens, int st
     MC_CUDA(cudaMemsetAsync(sh.step, 0, 4, sh.stream));
     const uint32_t s0 = session0 + (uint32_t)b->first[g];
     if ((st = enqueue_forward(sh, P, mode, inv_t, s0, false, true)) != kOk) return st;
-    for (int t = 1; t < n_new; ++t)
-      if ((st = run_graph_step(sh, mode, inv_t, s0, false)) != kOk) return st;
+    if ((st = run_decode_steps(sh, n_new, mode, inv_t, s0)) != kOk) return st;
   }
   for (size_t g = 0; g < b->shard.size(); ++g) {
     DevBatch& sh = *b->shard[g];
@@ -450,8 +458,7 @@ int mc_generate_dev(mc_batch* b, const int32_t* d_prompts, const int32_t* d_lens
                                                                       sh.seglen, sh.pos, sh.rowmap, sh.step);
   MC_CUDA(cudaGetLastError());
   if ((st = enqueue_forward(sh, P, mode, inv_t, session0, false, true)) != kOk) return st;
-  for (int t = 1; t < n_new; ++t)
-    if ((st = run_graph_step(sh, mode, inv_t, session0, false)) != kOk) return st;
+  if ((st = run_decode_steps(sh, n_new, mode, inv_t, session0)) != kOk) return st;
   MC_CUDA(cudaMemcpy2DAsync(d_out_tokens, (size_t)n_new * 4, sh.out_tok, (size_t)sh.out_stride * 4, (size_t)n_new * 4, sh.S,
                             cudaMemcpyDeviceToDevice, sh.stream));
   if (d_out_probs)

@@ -180,6 +180,127 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(a.att_rowmax + grow), __float_as_uint(om));
 }
 
+// One decode item (session, head) of the staged attention, shared by the staged kernel and the
+// persistent decode loop. The window of a session at position pos: the first ring slot and the
+// number of keys (at most the cache length, 128).
+struct AttnWindow {
+  int lo_slot, span;
+};
+
+__device__ __forceinline__ AttnWindow attn_window(int pos, int window, int cache) {
+  int ws = 0;
+  if (window > 0 && pos - window + 1 > 0) ws = pos - window + 1;
+  const int lo = max(ws, pos - cache + 1);
+  AttnWindow w;
+  w.span = pos - lo + 1;
+  w.lo_slot = lo % cache;
+  return w;
+}
+
+// q rotated like the key reads: qr[f] = q4[(f + lane) % NF] (loaded ahead of the key wait).
+template <int DH>
+__device__ __forceinline__ void attn_load_q(const float* q, float4 (&qr)[DH / 4], int lane) {
+#pragma unroll
+  for (int f = 0; f < DH / 4; ++f) qr[f] = reinterpret_cast<const float4*>(q)[(f + lane) % (DH / 4)];
+}
+
+// Scores of the window's keys (lane i: keys lo+i, lo+i+32, ...; 16-byte columns in a per-lane
+// rotation), the max shift, the reference's exp polynomial and one reciprocal: the softmax
+// weights of the window's positions into pbuf[0..128).
+template <int DH>
+__device__ __forceinline__ void attn_scores(const float4 (&qr)[DH / 4], const float* Ks, AttnWindow w, int cache,
+                                            float scale, float* pbuf, int lane) {
+  constexpr int NF = DH / 4;
+  float sc[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int j = lane + 32 * u;
+    float acc = 0.f;
+    if (j < w.span) {
+      int sl = w.lo_slot + j;
+      if (sl >= cache) sl -= cache;
+      if (sl >= cache) sl -= cache;
+      const float4* row = reinterpret_cast<const float4*>(Ks + (size_t)sl * DH);
+#pragma unroll
+      for (int f = 0; f < NF; ++f) {
+        const float4 k4 = row[(f + lane) % NF];
+        acc = __fmaf_rn(qr[f].x, k4.x, acc);
+        acc = __fmaf_rn(qr[f].y, k4.y, acc);
+        acc = __fmaf_rn(qr[f].z, k4.z, acc);
+        acc = __fmaf_rn(qr[f].w, k4.w, acc);
+      }
+    }
+    sc[u] = acc;
+  }
+  float mx = -3.402823466e38f;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    if (lane + 32 * u < w.span) {
+      sc[u] = __fmul_rn(sc[u], scale);
+      mx = fmaxf(mx, sc[u]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    if (lane + 32 * u < w.span) {
+      sc[u] = ref_vec_exp(__fsub_rn(sc[u], mx));
+      sum = __fadd_rn(sum, sc[u]);
+    } else {
+      sc[u] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+  const float inv = __fdiv_rn(1.0f, sum);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) pbuf[lane + 32 * u] = __fmul_rn(sc[u], inv);
+}
+
+// The weighted sum of the window's values (lanes own (row group, 16-byte column) pairs; the groups
+// combine on shuffles) into out[0..DH), and max |out| into *rowmax (atomic max of the float bits).
+template <int DH>
+__device__ __forceinline__ void attn_values(const float* Vs, const float* pbuf, AttnWindow w, int cache, float* out,
+                                            float* rowmax, int lane) {
+  constexpr int NF = DH / 4;  // float4 columns of a head row
+  constexpr int G = 32 / NF;  // row groups
+  const int c = lane % NF, g = lane / NF;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (g < G) {
+    int sl = w.lo_slot + g;
+    if (sl >= cache) sl -= cache;
+    const float4* V4 = reinterpret_cast<const float4*>(Vs);
+#pragma unroll 4
+    for (int j = g; j < w.span; j += G) {
+      const float p = pbuf[j];
+      const float4 v = V4[(size_t)sl * NF + c];
+      o.x = __fmaf_rn(p, v.x, o.x);
+      o.y = __fmaf_rn(p, v.y, o.y);
+      o.z = __fmaf_rn(p, v.z, o.z);
+      o.w = __fmaf_rn(p, v.w, o.w);
+      sl += G;
+      if (sl >= cache) sl -= cache;
+    }
+  }
+#pragma unroll
+  for (int off = (G / 2) * NF; off >= NF; off >>= 1) {
+    o.x = __fadd_rn(o.x, __shfl_down_sync(0xffffffffu, o.x, off));
+    o.y = __fadd_rn(o.y, __shfl_down_sync(0xffffffffu, o.y, off));
+    o.z = __fadd_rn(o.z, __shfl_down_sync(0xffffffffu, o.z, off));
+    o.w = __fadd_rn(o.w, __shfl_down_sync(0xffffffffu, o.w, off));
+  }
+  float om = 0.f;
+  if (lane < NF) {
+    reinterpret_cast<float4*>(out)[lane] = o;
+    om = fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w)));
+  }
+#pragma unroll
+  for (int k = 16; k; k >>= 1) om = fmaxf(om, __shfl_xor_sync(0xffffffffu, om, k));
+  if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(rowmax), __float_as_uint(om));
+}
+
 // Decode with the key/value windows staged in shared memory: a persistent grid (one CTA per SM)
 // deals the (session, head) items to its warps round-robin, CTA-major. Each warp
 // owns two shared-memory buffers, one for a key ring and one for a value ring (each one
@@ -225,7 +346,6 @@ __global__ void __launch_bounds__(kAsMaxWarps * 32) attn_decode_staged_kernel(co
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   constexpr int NF = DH / 4;  // float4 columns of a head row
-  constexpr int G = 32 / NF;  // row groups of the value phase
   const int cache = a.cache, D = a.D, heads = a.heads;
   const uint32_t ring_bytes = (uint32_t)(cache * DH * 4);
   const int nwarps = blockDim.x >> 5;
@@ -276,111 +396,20 @@ __global__ void __launch_bounds__(kAsMaxWarps * 32) attn_decode_staged_kernel(co
     const int it = base + stride * m;
     const int s = it / heads, h = it - s * heads;
     const bool active = a.seglen[s] > 0;
-    const int pos = a.pos0[s];
-    int ws = 0;
-    if (a.window > 0 && pos - a.window + 1 > 0) ws = pos - a.window + 1;
-    const int lo = max(ws, pos - cache + 1);
-    const int span = pos - lo + 1;  // <= cache <= 128
-    const int lo_slot = lo % cache;
+    const AttnWindow w = attn_window(a.pos0[s], a.window, cache);
     const int grow = s;  // decode: the q and output row of session s is row s
-    const float* q = a.qbuf + (size_t)grow * D + h * DH;
-    float4 qr[NF];  // q rotated like the key reads: qr[f] = q4[(f + lane) % NF]
-    if (active) {
-#pragma unroll
-      for (int f = 0; f < NF; ++f) qr[f] = reinterpret_cast<const float4*>(q)[(f + lane) % NF];
-    }
+    float4 qr[NF];
+    if (active) attn_load_q<DH>(a.qbuf + (size_t)grow * D + h * DH, qr, lane);
     // ---- scores and softmax from the key ring ----
     bool got = __all_sync(0xffffffffu, healthy && mbar_wait_or_abort(kfull, m & 1, kErrWaitFull));
     if (!got) healthy = false;
-    if (got && active) {
-      float sc[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = lane + 32 * u;
-        float acc = 0.f;
-        if (j < span) {
-          int sl = lo_slot + j;
-          if (sl >= cache) sl -= cache;
-          if (sl >= cache) sl -= cache;
-          const float4* row = reinterpret_cast<const float4*>(Ks + (size_t)sl * DH);
-#pragma unroll
-          for (int f = 0; f < NF; ++f) {
-            const float4 k4 = row[(f + lane) % NF];
-            acc = __fmaf_rn(qr[f].x, k4.x, acc);
-            acc = __fmaf_rn(qr[f].y, k4.y, acc);
-            acc = __fmaf_rn(qr[f].z, k4.z, acc);
-            acc = __fmaf_rn(qr[f].w, k4.w, acc);
-          }
-        }
-        sc[u] = acc;
-      }
-      float mx = -3.402823466e38f;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (lane + 32 * u < span) {
-          sc[u] = __fmul_rn(sc[u], a.scale);
-          mx = fmaxf(mx, sc[u]);
-        }
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      float sum = 0.f;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (lane + 32 * u < span) {
-          sc[u] = ref_vec_exp(__fsub_rn(sc[u], mx));
-          sum = __fadd_rn(sum, sc[u]);
-        } else {
-          sc[u] = 0.f;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-      const float inv = __fdiv_rn(1.0f, sum);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) pbuf[lane + 32 * u] = __fmul_rn(sc[u], inv);
-    }
+    if (got && active) attn_scores<DH>(qr, Ks, w, cache, a.scale, pbuf, lane);
     __syncwarp();
     if (lane == 0 && healthy) issue(m + 1, 0);  // the key buffer is free: next item's keys
     // ---- values from the value ring ----
     got = __all_sync(0xffffffffu, healthy && mbar_wait_or_abort(vfull, m & 1, kErrWaitFull));
     if (!got) healthy = false;
-    if (got && active) {
-      // lane = (row group g, column c); rows j = g, g + G, ... of the window
-      const int c = lane % NF, g = lane / NF;
-      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (g < G) {
-        int sl = lo_slot + g;
-        if (sl >= cache) sl -= cache;
-        const float4* V4 = reinterpret_cast<const float4*>(Vs);
-#pragma unroll 4
-        for (int j = g; j < span; j += G) {
-          const float p = pbuf[j];
-          const float4 v = V4[(size_t)sl * NF + c];
-          o.x = __fmaf_rn(p, v.x, o.x);
-          o.y = __fmaf_rn(p, v.y, o.y);
-          o.z = __fmaf_rn(p, v.z, o.z);
-          o.w = __fmaf_rn(p, v.w, o.w);
-          sl += G;
-          if (sl >= cache) sl -= cache;
-        }
-      }
-#pragma unroll
-      for (int off = (G / 2) * NF; off >= NF; off >>= 1) {
-        o.x = __fadd_rn(o.x, __shfl_down_sync(0xffffffffu, o.x, off));
-        o.y = __fadd_rn(o.y, __shfl_down_sync(0xffffffffu, o.y, off));
-        o.z = __fadd_rn(o.z, __shfl_down_sync(0xffffffffu, o.z, off));
-        o.w = __fadd_rn(o.w, __shfl_down_sync(0xffffffffu, o.w, off));
-      }
-      float om = 0.f;
-      if (lane < NF) {
-        reinterpret_cast<float4*>(a.att + (size_t)grow * D + h * DH)[lane] = o;
-        om = fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w)));
-      }
-#pragma unroll
-      for (int k = 16; k; k >>= 1) om = fmaxf(om, __shfl_xor_sync(0xffffffffu, om, k));
-      if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(a.att_rowmax + grow), __float_as_uint(om));
-    }
+    if (got && active) attn_values<DH>(Vs, pbuf, w, cache, a.att + (size_t)grow * D + h * DH, a.att_rowmax + grow, lane);
     __syncwarp();
     if (lane == 0 && healthy) issue(m + 1, 1);  // the value buffer is free: next item's values
   }

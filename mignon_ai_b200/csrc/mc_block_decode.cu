@@ -100,31 +100,45 @@ __device__ __forceinline__ int decode_mma_group(const GemmSpec& G) { return (G.t
 // latency chains of two CTAs interleave; one otherwise.
 __host__ __device__ constexpr int decode_ctas_per_sm(int kf, int r) { return (r == 16 && kf == 1) ? 2 : 1; }
 
-template <int KF, int R, int WS>  // float4 columns per state row lane (ceil(D / 128)), sessions per CTA, weight stages
-__global__ void __launch_bounds__(kDThreads, decode_ctas_per_sm(KF, R)) block_decode_kernel(const __grid_constant__ BlockArgs a) {
-  constexpr int kDR = R;
-  constexpr int kDWStages = WS;
-  constexpr int kDBTile = R * 128;               // one digit plane of one K tile of the sessions
-  constexpr int kDRowsPerWarp = R / kDRowWarps;  // session rows per row warp
-  constexpr int kDCols = R / 4;                  // sessions per epilogue thread
-  constexpr int kDSlotCols = R == 32 ? 128 : 64; // three planes of R columns, padded
-  constexpr uint32_t kDTmemCols = kDSlots * kDSlotCols;  // 512 or 256 (a power of two >= 32)
-  extern __shared__ uint8_t smem_raw[];
+// Shared memory of a decode CTA: the weight ring, the sessions' activation planes, the norm and
+// auxiliary rows, the cur rows, then the barriers.
+struct DecodeLayout {
+  uint8_t* sW;   // [WS][128 x 128] weight tiles
+  uint8_t* sB;   // [KT][3 planes][R rows x 128] activation planes, stacked along N
+  float* sNrm;   // [R][D] norm cell
+  float* sAux;   // [R][max(D, H)] latch gate, then hidden
+  float* sCur;   // [R][D] the block's state rows
+  DBars* bars;
+};
+
+template <int R, int WS>
+__device__ __forceinline__ DecodeLayout decode_layout(uint8_t* smem_raw, int D, int H, int KT) {
+  DecodeLayout L;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int D = a.D, H = a.H, KT = a.dec_kt;
   const int DH = D > H ? D : H;
-  uint8_t* sW = smem;
-  uint8_t* sB = sW + kDWStages * kTile;
-  float* sCur = reinterpret_cast<float*>(sB + 3 * KT * kDBTile);  // [kDR][D]
-  float* sNrm = sCur + kDR * D;                                    // [kDR][D] norm cell
-  float* sAux = sNrm + kDR * D;                                    // [kDR][D] latch gate, then [kDR][H] hidden
-  DBars* bars = reinterpret_cast<DBars*>(sAux + kDR * DH);
+  L.sW = smem;
+  L.sB = L.sW + WS * kTile;
+  L.sNrm = reinterpret_cast<float*>(L.sB + 3 * KT * R * 128);
+  L.sAux = L.sNrm + R * D;
+  L.sCur = L.sAux + R * DH;
+  L.bars = reinterpret_cast<DBars*>(L.sCur + R * D);
+  return L;
+}
 
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int s0 = blockIdx.x * kDR;
+// One thread's running state through a block: ring and slot counters, the GEMMs whose planes
+// were published, trace points, and whether every wait so far succeeded (after a wait gave up,
+// the thread skips all further waits, so a failure costs one wait limit).
+struct DecodeRun {
+  uint32_t widx = 0, sidx = 0, gidx = 0;
+  int tp = 0;
+  bool ok = true;
+};
 
+template <int KF, int R, int WS>
+__device__ __forceinline__ void decode_init(const DecodeLayout& L) {
+  DBars* bars = L.bars;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kDWStages; ++i) {
+    for (int i = 0; i < WS; ++i) {
       mbar_init(&bars->w_full[i], 1);
       mbar_init(&bars->w_empty[i], 1);
     }
@@ -135,17 +149,36 @@ __global__ void __launch_bounds__(kDThreads, decode_ctas_per_sm(KF, R)) block_de
     mbar_init(&bars->b_full, kDRowThreads);
     fence_barrier_init();
   }
-  if (warp == kDMmaWarp) tmem_alloc(&bars->tmem, kDTmemCols);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = bars->tmem;
+}
+
+// One CA block for the CTA's R sessions, every role (weight producer, MMA issuer, row warps)
+// with its running state.
+template <int KF, int R, int WS>
+__device__ __forceinline__ void decode_block(const BlockArgs& a, const DecodeLayout& L, uint32_t tmem, DecodeRun& run) {
+  constexpr int kDR = R;
+  constexpr int kDWStages = WS;
+  constexpr int kDBTile = R * 128;               // one digit plane of one K tile of the sessions
+  constexpr int kDRowsPerWarp = R / kDRowWarps;  // session rows per row warp
+  constexpr int kDCols = R / 4;                  // sessions per epilogue thread
+  constexpr int kDSlotCols = R == 32 ? 128 : 64; // three planes of R columns, padded
+  const int D = a.D, H = a.H;
+  uint8_t* sW = L.sW;
+  uint8_t* sB = L.sB;
+  float* sCur = L.sCur;
+  float* sNrm = L.sNrm;
+  float* sAux = L.sAux;
+  DBars* bars = L.bars;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int s0 = blockIdx.x * kDR;
+  // the row warps run on after a failed wait (skipping every wait and epilogue) so that they all
+  // meet at each of their named barriers
+  if (!run.ok && warp >= kDRowWarps) return;
 
   if (warp == kDProducerWarp) {
     // ---------------- weight tiles, in the order the MMA warp consumes them ----------------
     if (lane == 0) {
-      uint32_t widx = 0;
-      bool ok = true;
+      uint32_t& widx = run.widx;
+      bool& ok = run.ok;
       for (int g = 0; g < a.ngemms && ok; ++g) {
         const GemmSpec& G = a.gemms[g];
         const int gs = decode_mma_group(G);
@@ -167,12 +200,16 @@ __global__ void __launch_bounds__(kDThreads, decode_ctas_per_sm(KF, R)) block_de
   } else if (warp == kDMmaWarp) {
     // ---------------- MMA issuer: D[channel][session] += W[channel][k] * X[session][k] ----------------
     if (lane == 0) {
-      uint32_t widx = 0, sidx = 0;
+      uint32_t& widx = run.widx;
+      uint32_t& sidx = run.sidx;
       const uint32_t idesc = idesc_i8(128, 3 * kDR);  // the three planes stacked along N
-      bool ok = true;
+      bool& ok = run.ok;
       for (int g = 0; g < a.ngemms && ok; ++g) {
         const GemmSpec& G = a.gemms[g];
-        if (!mbar_wait_or_abort(&bars->b_full, g & 1, kErrWaitFull)) break;
+        if (!mbar_wait_or_abort(&bars->b_full, (run.gidx++) & 1, kErrWaitFull)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         // gs M-tiles at a time (a value/gate pair: two independent accumulation chains, their
         // MMAs alternating K step by K step), each in its own TMEM slot
@@ -215,9 +252,9 @@ __global__ void __launch_bounds__(kDThreads, decode_ctas_per_sm(KF, R)) block_de
     const int chl = 32 * (warp & 3) + lane;  // channel within an M-tile = TMEM lane
     const int r0 = kDCols * (warp >> 2);      // first of this thread's epilogue sessions = TMEM column
     const int nf = D / 4;
-    uint32_t sidx = 0;
-    bool ok = true;
-    int tp = 0;
+    uint32_t& sidx = run.sidx;
+    bool& ok = run.ok;
+    int& tp = run.tp;
     trace_point(a, tp++);
     if (t < kDR) {
       const int s = s0 + t;
@@ -748,6 +785,22 @@ __global__ void __launch_bounds__(kDThreads, decode_ctas_per_sm(KF, R)) block_de
     }
     trace_point(a, tp++);
   }
+}
+
+template <int KF, int R, int WS>  // float4 columns per state row lane (ceil(D / 128)), sessions per CTA, weight stages
+__global__ void __launch_bounds__(kDThreads, decode_ctas_per_sm(KF, R)) block_decode_kernel(const __grid_constant__ BlockArgs a) {
+  constexpr uint32_t kDTmemCols = kDSlots * (R == 32 ? 128 : 64);  // 512 or 256 (a power of two >= 32)
+  extern __shared__ uint8_t smem_raw[];
+  const DecodeLayout L = decode_layout<R, WS>(smem_raw, a.D, a.H, a.dec_kt);
+  const int warp = threadIdx.x / 32;
+  decode_init<KF, R, WS>(L);
+  if (warp == kDMmaWarp) tmem_alloc(&L.bars->tmem, kDTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = L.bars->tmem;
+  DecodeRun run;
+  decode_block<KF, R, WS>(a, L, tmem, run);
   tc_fence_before();
   __syncthreads();
   if (warp == kDMmaWarp) tmem_dealloc(tmem, kDTmemCols);

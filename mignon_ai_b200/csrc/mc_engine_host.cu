@@ -494,6 +494,72 @@ __global__ void prepare_prompts_kernel(const int32_t* prompts, const int32_t* le
   rowmap[s] = (s / spt) * 128 + (s % spt) * P + max(n - 1, 0);
 }
 
+// The arguments of launch bi of one forward (the CA blocks, then bi = blocks: the final one) for
+// P rows per session; *bs: rule steps of the blocks before bi (advanced past block bi).
+static void build_block_args(const DevBatch& b, int P, int bi, bool fuse_head, int* bs, BlockArgs& a) {
+  const DevModel& m = *b.m;
+  const int nb = (int)m.blocks.size();
+  fill_common(b, a, P);
+  const bool final_k = bi == nb;
+  int g = 0;
+  if (bi > 0 && m.blocks[bi - 1].attn_slot >= 0) {
+    a.has_out = 1;
+    a.gemms[g++] = spec(m.blocks[bi - 1].out, kGOut, 0);
+  }
+  if (!final_k) {
+    const DevBlock& blk = m.blocks[bi];
+    a.block = bi;
+    a.embed_first = bi == 0;
+    a.residual = bi > 0;
+    a.nsteps = blk.steps;
+    a.bs0 = *bs;
+    for (int st = 0; st < blk.steps; ++st) {
+      a.dil[st] = blk.dil[st];
+      a.gemms[g++] = spec(blk.wsel, kGWsel, st);
+      a.gemms[g++] = spec(blk.w1, kGW1, st);
+      a.gemms[g++] = spec(blk.w2, kGW2, st);
+    }
+    a.gamma = blk.gamma;
+    a.b1 = blk.b1;
+    a.b2 = blk.b2;
+    if (blk.attn_slot >= 0) {
+      a.has_attn = 1;
+      a.attn_slot = blk.attn_slot;
+      a.attn_norm = blk.attn_norm;
+      a.gemms[g++] = spec(blk.qkv, kGQkv, 0);
+    }
+    *bs += blk.steps;
+  } else {
+    a.block = nb;
+    a.embed_first = nb == 0;
+    a.final_norm = 1;
+    if (fuse_head) {
+      // the greedy head and selection run inside the final decode launch
+      a.fuse_head = 1;
+      a.gemms[g++] = spec(m.head, kGHead, 0);
+      a.head_b = m.head_b;
+      a.next_tok = b.next_tok;
+      a.out_tok = b.out_tok;
+      a.out_prob = b.out_prob;
+      a.out_stride = b.out_stride;
+      a.pos_w = b.pos;
+      a.step = b.step;
+      a.done = b.sel_done;
+    }
+  }
+  a.ngemms = g;
+  a.trace = b.trace ? b.trace + 64 * bi : nullptr;
+  a.trace_fine = getenv("MC_TRACE_FINE") != nullptr;
+  if (P == 1 && b.decode_kernel) {
+    // the decode kernel reads W1 and W2 in split-pair tiles
+    for (int i = 0; i < a.ngemms; ++i) {
+      if (a.gemms[i].type == kGW1) a.gemms[i] = spec(m.blocks[bi].w1d, kGW1, a.gemms[i].step);
+      if (a.gemms[i].type == kGW2) a.gemms[i] = spec(m.blocks[bi].w2d, kGW2, a.gemms[i].step);
+    }
+    a.dec_kt = m.dec_kt;
+  }
+}
+
 // Enqueues the blocks (and attention sublayers) of one segment: P rows per session, P = 1 a decode
 // step; ends with the final RMSNorm of every row.
 static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = false) {
@@ -503,64 +569,9 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
   int bs = 0;
   for (int bi = 0; bi <= nb; ++bi) {
     BlockArgs a;
-    fill_common(b, a, P);
+    build_block_args(b, P, bi, fuse_head, &bs, a);
     const bool final_k = bi == nb;
-    int g = 0;
-    if (bi > 0 && m.blocks[bi - 1].attn_slot >= 0) {
-      a.has_out = 1;
-      a.gemms[g++] = spec(m.blocks[bi - 1].out, kGOut, 0);
-    }
-    if (!final_k) {
-      const DevBlock& blk = m.blocks[bi];
-      a.block = bi;
-      a.embed_first = bi == 0;
-      a.residual = bi > 0;
-      a.nsteps = blk.steps;
-      a.bs0 = bs;
-      for (int st = 0; st < blk.steps; ++st) {
-        a.dil[st] = blk.dil[st];
-        a.gemms[g++] = spec(blk.wsel, kGWsel, st);
-        a.gemms[g++] = spec(blk.w1, kGW1, st);
-        a.gemms[g++] = spec(blk.w2, kGW2, st);
-      }
-      a.gamma = blk.gamma;
-      a.b1 = blk.b1;
-      a.b2 = blk.b2;
-      if (blk.attn_slot >= 0) {
-        a.has_attn = 1;
-        a.attn_slot = blk.attn_slot;
-        a.attn_norm = blk.attn_norm;
-        a.gemms[g++] = spec(blk.qkv, kGQkv, 0);
-      }
-      bs += blk.steps;
-    } else {
-      a.block = nb;
-      a.embed_first = nb == 0;
-      a.final_norm = 1;
-      if (fuse_head) {
-        // the greedy head and selection run inside the final decode launch
-        a.fuse_head = 1;
-        a.gemms[g++] = spec(m.head, kGHead, 0);
-        a.head_b = m.head_b;
-        a.next_tok = b.next_tok;
-        a.out_tok = b.out_tok;
-        a.out_prob = b.out_prob;
-        a.out_stride = b.out_stride;
-        a.pos_w = b.pos;
-        a.step = b.step;
-        a.done = b.sel_done;
-      }
-    }
-    a.ngemms = g;
-    a.trace = b.trace ? b.trace + 64 * bi : nullptr;
-    a.trace_fine = getenv("MC_TRACE_FINE") != nullptr;
     if (P == 1 && b.decode_kernel) {
-      // the decode kernel reads W1 and W2 in split-pair tiles
-      for (int i = 0; i < a.ngemms; ++i) {
-        if (a.gemms[i].type == kGW1) a.gemms[i] = spec(m.blocks[bi].w1d, kGW1, a.gemms[i].step);
-        if (a.gemms[i].type == kGW2) a.gemms[i] = spec(m.blocks[bi].w2d, kGW2, a.gemms[i].step);
-      }
-      a.dec_kt = m.dec_kt;
       const int grid = (b.S + m.dec_r - 1) / m.dec_r;
       const int kf = (m.D + 127) / 128;
       void (*kern)(BlockArgs);
@@ -643,8 +654,6 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
   return kOk;
 }
 
-// Enqueues the whole forward pass of one segment (P rows per session; P = 1 is a decode step)
-// followed by the head and token selection.
 int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t session0, bool want_logits,
                     bool advance_from_len, LaunchLog* log = nullptr) {
   const DevModel& m = *b.m;
