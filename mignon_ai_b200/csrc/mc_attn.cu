@@ -428,7 +428,9 @@ __global__ void __launch_bounds__(kAsMaxWarps * 32) attn_decode_staged_kernel(co
 // (row group, 16-byte column) pairs of the value rows as in the staged decode kernel. max |o| of
 // each row accumulates in shared memory across the heads.
 template <int DH>  // head width: 4, 8, 16, 32, 48 or 64 (32 / (DH / 4) row groups, a power of two)
-__global__ void __launch_bounds__(kAttnThreads, 4) attn_prefill_fast_kernel(const __grid_constant__ AttnArgs a) {
+// Four CTAs per SM (64 registers) for head widths up to 32, whose segments are short enough to fit
+// four in shared memory; two for wider heads (their rotated q rows need the registers).
+__global__ void __launch_bounds__(kAttnThreads, DH <= 32 ? 4 : 2) attn_prefill_fast_kernel(const __grid_constant__ AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   float* sm = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   constexpr int NF = DH / 4;
