@@ -203,6 +203,7 @@ __device__ __forceinline__ void decode_block(const BlockArgs& a, const DecodeLay
       uint32_t& widx = run.widx;
       uint32_t& sidx = run.sidx;
       const uint32_t idesc = idesc_i8(128, 3 * kDR);  // the three planes stacked along N
+      const uint64_t desc_w0 = smem_desc_sw128(sW), desc_b0 = smem_desc_sw128(sB);
       bool& ok = run.ok;
       for (int g = 0; g < a.ngemms && ok; ++g) {
         const GemmSpec& G = a.gemms[g];
@@ -223,21 +224,36 @@ __device__ __forceinline__ void decode_block(const BlockArgs& a, const DecodeLay
           }
           if (!ok) break;
           tc_fence_after();
+          // descriptors advance by their encoded start address (bytes / 16): a weight stage is
+          // kTile bytes, a K tile of the planes 3 * kDBTile
+          const uint32_t dt0 = tmem + (sidx % kDSlots) * kDSlotCols;
+          const uint32_t dt1 = tmem + ((sidx + 1) % kDSlots) * kDSlotCols;
+          uint32_t st = widx % kDWStages, ph = (widx / kDWStages) & 1;
           for (int kt = 0; kt < G.ktiles && ok; ++kt) {
-            const uint64_t db = smem_desc_sw128(sB + kt * 3 * kDBTile);
+            const uint64_t db = desc_b0 + (uint64_t)(kt * (3 * kDBTile >> 4));
             const int ksteps = min(4, (G.K - kt * 128 + 31) / 32);
             for (int q = 0; q < n; ++q, ++widx) {
-              const int st = widx % kDWStages;
-              if (!mbar_wait_or_abort(&bars->w_full[st], (widx / kDWStages) & 1, kErrWaitFull)) {
+              if (!mbar_wait_or_abort(&bars->w_full[st], ph, kErrWaitFull)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              const uint64_t da = smem_desc_sw128(sW + st * kTile);
-              const uint32_t dt = tmem + ((sidx + q) % kDSlots) * kDSlotCols;
-              for (int kk = 0; kk < ksteps; ++kk)
-                mma_i8(dt, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+              const uint64_t da = desc_w0 + (uint64_t)(st * (kTile >> 4));
+              const uint32_t dt = q == 0 ? dt0 : dt1;
+              if (ksteps == 4) {
+                mma_i8(dt, da, db, idesc, kt > 0 ? 1u : 0u);
+                mma_i8(dt, da + 2, db + 2, idesc, 1u);
+                mma_i8(dt, da + 4, db + 4, idesc, 1u);
+                mma_i8(dt, da + 6, db + 6, idesc, 1u);
+              } else {
+                for (int kk = 0; kk < ksteps; ++kk)
+                  mma_i8(dt, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+              }
               mma_commit(&bars->w_empty[st]);
+              if (++st == kDWStages) {
+                st = 0;
+                ph ^= 1;
+              }
             }
           }
           if (!ok) break;
