@@ -200,14 +200,15 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
   return d;
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread. No memory clobber: the operands are
+// ordered by the (volatile, clobbering) mbarrier waits and fences around it, and volatile asm
+// statements keep their order.
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 // Arrives on the mbarrier once all previously issued MMAs of this thread have completed.
