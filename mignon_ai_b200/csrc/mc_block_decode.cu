@@ -179,21 +179,26 @@ __device__ __forceinline__ void decode_block(const BlockArgs& a, const DecodeLay
     if (lane == 0) {
       uint32_t& widx = run.widx;
       bool& ok = run.ok;
+      const uint64_t policy = l2_policy_evict_last();
+      uint32_t st = widx % kDWStages, ph = (widx / kDWStages) & 1;  // stage, and the parity of its fill
       for (int g = 0; g < a.ngemms && ok; ++g) {
         const GemmSpec& G = a.gemms[g];
         const int gs = decode_mma_group(G);
         for (int c0 = 0; c0 < G.nchunks && ok; c0 += gs)
           for (int kt = 0; kt < G.ktiles && ok; ++kt)
             for (int c = c0; c < c0 + gs && c < G.nchunks; ++c, ++widx) {
-              const int st = widx % kDWStages;
-              if (widx >= kDWStages &&
-                  !mbar_wait_or_abort(&bars->w_empty[st], ((widx / kDWStages) - 1) & 1, kErrWaitEmpty)) {
+              // the stage's previous fill (parity ph ^ 1) has been consumed
+              if (widx >= kDWStages && !mbar_wait_or_abort(&bars->w_empty[st], ph ^ 1, kErrWaitEmpty)) {
                 ok = false;
                 break;
               }
               mbar_arrive_expect_tx(&bars->w_full[st], kTile);
               bulk_load_hint(sW + st * kTile, G.tiles + ((size_t)c * G.ktiles + kt) * kTile, kTile, &bars->w_full[st],
-                             l2_policy_evict_last());
+                             policy);
+              if (++st == kDWStages) {
+                st = 0;
+                ph ^= 1;
+              }
             }
       }
     }
