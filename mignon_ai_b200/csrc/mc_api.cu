@@ -112,22 +112,39 @@ int upload_prompts(mc_batch* b, const int32_t* tokens, const int32_t* lens, int 
     if (sh.S == 0) continue;
     MC_CUDA(cudaSetDevice(sh.m->device));
     const int s0 = b->first[g];
-    std::vector<int32_t> tok((size_t)sh.S * P, 0), len(sh.S), rowmap(sh.S), zero(sh.S, 0);
+    // pinned staging [tokens S*P | lengths S | zeros S | row map S], reused once the previous
+    // upload's copies are done
+    const size_t need = (size_t)sh.S * P + 3 * (size_t)sh.S;
+    if (sh.h_stage_done) MC_CUDA(cudaEventSynchronize(sh.h_stage_done));
+    else MC_CUDA(cudaEventCreateWithFlags(&sh.h_stage_done, cudaEventDisableTiming));
+    if (sh.h_stage_n < need) {
+      if (sh.h_stage) MC_CUDA(cudaFreeHost(sh.h_stage));
+      sh.h_stage = nullptr;
+      sh.h_stage_n = 0;
+      MC_CUDA(cudaHostAlloc(&sh.h_stage, need * 4, cudaHostAllocDefault));
+      sh.h_stage_n = need;
+    }
+    int32_t* tok = sh.h_stage;
+    int32_t* len = tok + (size_t)sh.S * P;
+    int32_t* zero = len + sh.S;
+    int32_t* rowmap = zero + sh.S;
     const int spt = std::max(1, 128 / P);
     for (int i = 0; i < sh.S; ++i) {
       const int s = s0 + i;
       const int n = std::max(0, std::min(lens[s], b->window));
       const int32_t* src = tokens + (size_t)s * stride + (lens[s] - n);
-      std::copy(src, src + n, tok.begin() + (size_t)i * P);
+      int32_t* dst = tok + (size_t)i * P;
+      std::copy(src, src + n, dst);
+      std::fill(dst + n, dst + P, 0);
       len[i] = n;
+      zero[i] = 0;
       rowmap[i] = (i / spt) * 128 + (i % spt) * P + std::max(n - 1, 0);
     }
-    MC_CUDA(cudaMemcpyAsync(sh.tok, tok.data(), tok.size() * 4, cudaMemcpyHostToDevice, sh.stream));
-    MC_CUDA(cudaMemcpyAsync(sh.seglen, len.data(), sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
-    MC_CUDA(cudaMemcpyAsync(sh.pos, zero.data(), sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
-    MC_CUDA(cudaMemcpyAsync(sh.rowmap, rowmap.data(), sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
-    // The host vectors go out of scope: make the copies complete first.
-    MC_CUDA(cudaStreamSynchronize(sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.tok, tok, (size_t)sh.S * P * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.seglen, len, sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.pos, zero, sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.rowmap, rowmap, sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaEventRecord(sh.h_stage_done, sh.stream));
   }
   return kOk;
 }
@@ -414,20 +431,20 @@ int mc_generate(mc_batch* b, const int32_t* prompts, const int32_t* lens, int st
     DevBatch& sh = *b->shard[g];
     if (sh.S == 0) continue;
     MC_CUDA(cudaSetDevice(sh.m->device));
-    // out columns are laid out with stride sh.out_stride >= n_new
-    std::vector<int32_t> t((size_t)sh.S * sh.out_stride);
-    std::vector<float> p((size_t)sh.S * sh.out_stride);
-    MC_CUDA(cudaMemcpyAsync(t.data(), sh.out_tok, t.size() * 4, cudaMemcpyDeviceToHost, sh.stream));
-    MC_CUDA(cudaMemcpyAsync(p.data(), sh.out_prob, p.size() * 4, cudaMemcpyDeviceToHost, sh.stream));
+    // out columns are laid out with stride sh.out_stride >= n_new: the first n_new of each
+    // session's row go straight to the caller's rows of this shard's sessions
+    const size_t row0 = (size_t)b->first[g] * n_new;
+    MC_CUDA(cudaMemcpy2DAsync(out_tokens + row0, (size_t)n_new * 4, sh.out_tok, (size_t)sh.out_stride * 4,
+                              (size_t)n_new * 4, sh.S, cudaMemcpyDeviceToHost, sh.stream));
+    if (out_probs)
+      MC_CUDA(cudaMemcpy2DAsync(out_probs + row0, (size_t)n_new * 4, sh.out_prob, (size_t)sh.out_stride * 4,
+                                (size_t)n_new * 4, sh.S, cudaMemcpyDeviceToHost, sh.stream));
+  }
+  for (size_t g = 0; g < b->shard.size(); ++g) {
+    DevBatch& sh = *b->shard[g];
+    if (sh.S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh.m->device));
     if ((st = check_device_error(sh.stream)) != kOk) return st;
-    for (int i = 0; i < sh.S; ++i) {
-      const int s = b->first[g] + i;
-      std::copy(t.begin() + (size_t)i * sh.out_stride, t.begin() + (size_t)i * sh.out_stride + n_new,
-                out_tokens + (size_t)s * n_new);
-      if (out_probs)
-        std::copy(p.begin() + (size_t)i * sh.out_stride, p.begin() + (size_t)i * sh.out_stride + n_new,
-                  out_probs + (size_t)s * n_new);
-    }
   }
   return kOk;
 }

@@ -278,6 +278,11 @@ struct DevBatch {
   double* sc_logprob = nullptr;
   int out_stride = 0;
   cudaGraphExec_t graph = nullptr;
+  // pinned host staging of uploaded prompt segments (tokens, lengths, zero positions, row map),
+  // and an event recorded after the copies out of it: the next upload waits for it
+  int32_t* h_stage = nullptr;
+  size_t h_stage_n = 0;
+  cudaEvent_t h_stage_done = nullptr;
   // Everything the captured decode step bakes in; a change forces a new capture.
   struct GraphKey {
     int mode = -1, logits = -1, stride = -1;
@@ -295,6 +300,8 @@ struct DevBatch {
     cudaGetDevice(&prev);
     cudaSetDevice(m ? m->device : prev);
     if (graph) cudaGraphExecDestroy(graph);
+    if (h_stage_done) cudaEventSynchronize(h_stage_done), cudaEventDestroy(h_stage_done);
+    if (h_stage) cudaFreeHost(h_stage);
     for (void* p : allocs) cudaFree(p);
     if (stream) cudaStreamDestroy(stream);
     cudaSetDevice(prev);
