@@ -266,6 +266,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
       uint32_t bidx = 0, chunk_idx = 0;
       uint32_t afill[kASlots] = {0, 0, 0};
       const uint32_t idesc = idesc_i8(kRows, kNC);
+      const uint64_t desc_a0 = smem_desc_sw128(sA), desc_b0 = smem_desc_sw128(sB);
       bool ok = true;
       for (int g = 0; g < a.ngemms && ok; ++g) {
         const GemmSpec& G = a.gemms[g];
@@ -291,15 +292,16 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
               break;
             }
             tc_fence_after();
-            const uint64_t db = smem_desc_sw128(sB + st * kTile);
+            // descriptors advance by their encoded start address (bytes / 16)
+            const uint64_t db = desc_b0 + (uint64_t)(st * (kTile >> 4));
+            const uint64_t da = desc_a0 + (uint64_t)(slot * (kASlot >> 4));
             const int ksteps = min(4, (G.K - kt * 128 + 31) / 32);
             // planes innermost: three independent accumulation chains in flight
             for (int kk = 0; kk < ksteps; ++kk) {
+              const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
 #pragma unroll
-              for (int p = 0; p < 3; ++p) {
-                const uint64_t da = smem_desc_sw128(sA + slot * kASlot + p * kTile);
-                mma_i8(tmem + p * kNC, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
-              }
+              for (int p = 0; p < 3; ++p)
+                mma_i8(tmem + p * kNC, da + (uint64_t)(p * (kTile >> 4)) + 2 * kk, db + 2 * kk, idesc, acc);
             }
             mma_commit(&bars->b_empty[st]);
             if (!resident || c == G.nchunks - 1) mma_commit(&bars->a_empty[slot]);
