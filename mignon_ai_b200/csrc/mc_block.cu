@@ -42,7 +42,7 @@ constexpr int kSmemB = kBStages * kTile;        // 64 KB
 constexpr int kBlockSmem = kSmemA + kSmemB + 1024 /*align*/ + 16384 /*barriers, row data*/;
 
 struct Bars {
-  uint64_t a_full[kASlots], a_empty[kASlots], b_full[kBStages], b_empty[kBStages], acc_full, acc_empty;
+  uint64_t a_full[kASlots], a_empty[kASlots], a_tma[kASlots], b_full[kBStages], b_empty[kBStages], acc_full, acc_empty;
   uint32_t tmem;
   float rowmax_n[kRows];               // max |norm cell| per row
   float rowmax_part[kTPR][kRows];       // per-thread partial maxima of an epilogue output
@@ -197,6 +197,35 @@ __device__ __forceinline__ void put4(uint8_t* sA, int r, int e, float4 v, float 
   *reinterpret_cast<uint32_t*>(tile + 2 * kTile + off) = pack_low_bytes(c0, c1, c2, c3);
 }
 
+// put4 that also writes the same three words at the same offsets of a global copy of the A
+// slots' contents (gA: K tile 0 of the copy; K tile kt at gA + kt * kASlot).
+__device__ __forceinline__ void put4_2(uint8_t* sA, uint8_t* gA, int r, int e, float4 v, float inv) {
+  const int kt = e >> 7, k = e & 127;
+  uint8_t* tile = sA + (kt % kASlots) * kASlot;
+  uint8_t* gtile = gA + (size_t)kt * kASlot;
+  const uint32_t off = sw128_offset(r, k >> 4) + (k & 15);
+  uint32_t a0, a1, a2, a3, b0, b1, b2, b3, c0, c1, c2, c3;
+  slice3_bits(v.x, inv, a0, b0, c0);
+  slice3_bits(v.y, inv, a1, b1, c1);
+  slice3_bits(v.z, inv, a2, b2, c2);
+  slice3_bits(v.w, inv, a3, b3, c3);
+  const uint32_t p1 = pack_low_bytes(a0, a1, a2, a3), p2 = pack_low_bytes(b0, b1, b2, b3), p3 = pack_low_bytes(c0, c1, c2, c3);
+  *reinterpret_cast<uint32_t*>(tile + off) = p1;
+  *reinterpret_cast<uint32_t*>(tile + kTile + off) = p2;
+  *reinterpret_cast<uint32_t*>(tile + 2 * kTile + off) = p3;
+  *reinterpret_cast<uint32_t*>(gtile + off) = p1;
+  *reinterpret_cast<uint32_t*>(gtile + kTile + off) = p2;
+  *reinterpret_cast<uint32_t*>(gtile + 2 * kTile + off) = p3;
+}
+
+// How the A slots are filled for chunk c of GEMM G: 0 not at all (a resident GEMM's later chunks),
+// 1 by the row warps (sliced, published on a_full), 2 by the producer from the per-SM cache
+// (bulk copies completing on a_tma).
+__device__ __forceinline__ int a_fill_kind(const GemmSpec& G, int c, bool cache) {
+  if (G.ktiles <= kASlots) return c == 0 ? 1 : 0;
+  return (c > 0 && cache) ? 2 : 1;
+}
+
 __device__ __forceinline__ float4 ld4_or0(const float* p, int e, int K, bool valid) {
   if (!valid || e >= K) return make_float4(0.f, 0.f, 0.f, 0.f);
   if (e + 4 <= K) return *reinterpret_cast<const float4*>(p + e);
@@ -210,7 +239,7 @@ __device__ __forceinline__ float max4(float4 v) { return fmaxf(fmaxf(fabsf(v.x),
 
 constexpr int kRowsPerWarp = kRows / kRowWarps;  // 8
 
-template <int KF>  // float4 columns per lane per row: ceil(D / 128)
+template <int KF, bool CACHE>  // float4 columns per lane per row: ceil(D / 128); whether the plane cache is in use
 __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_constant__ BlockArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -221,11 +250,22 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int tile = blockIdx.x;
   const int D = a.D, H = a.H;
+  // this SM's plane cache (one block-kernel CTA per SM at a time: its shared memory)
+  uint8_t* acache = nullptr;
+  {
+    uint32_t id;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(id));
+    if (a.a_cache && (int)id < a.a_cache_sms) acache = a.a_cache + (size_t)id * a.a_cache_kt * kASlot;
+  }
+  // the cache serves GEMM G when it holds all of G's K tiles (instances without CACHE compile none
+  // of its code)
+  auto use_cache = [&](const GemmSpec& G) { return CACHE && acache != nullptr && G.ktiles <= a.a_cache_kt; };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kASlots; ++i) {
       mbar_init(&bars->a_full[i], kRowThreads);
       mbar_init(&bars->a_empty[i], 1);
+      mbar_init(&bars->a_tma[i], 1);
     }
     for (int i = 0; i < kBStages; ++i) {
       mbar_init(&bars->b_full[i], 1);
@@ -245,11 +285,33 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
     // ---------------- weight-tile producer (TMA bulk copies) ----------------
     if (lane == 0) {
       uint32_t bidx = 0;
+      // fills of each A slot so far (by anyone) and by the row warps, in the consumption order
+      uint32_t fills[kASlots] = {0, 0, 0}, rfills[kASlots] = {0, 0, 0};
       bool ok = true;
       for (int g = 0; g < a.ngemms && ok; ++g) {
         const GemmSpec& G = a.gemms[g];
-        for (int c = 0; c < G.nchunks && ok; ++c)
+        const bool cache = use_cache(G);
+        for (int c = 0; c < G.nchunks && ok; ++c) {
+          const int kind = a_fill_kind(G, c, cache);
+          if (kind == 2 && c == 1) {
+            // the first chunk's row fills wrote every K tile to the cache: acquire their writes
+            for (int sl = 0; sl < kASlots && ok; ++sl)
+              if (rfills[sl] > 0 && !mbar_wait_or_abort(&bars->a_full[sl], (rfills[sl] - 1) & 1, kErrWaitFull)) ok = false;
+          }
           for (int kt = 0; kt < G.ktiles && ok; ++kt, ++bidx) {
+            const int slot = kt % kASlots;
+            if (kind == 1) {
+              ++fills[slot];
+              ++rfills[slot];
+            } else if (kind == 2) {
+              if (fills[slot] >= 1 && !mbar_wait_or_abort(&bars->a_empty[slot], (fills[slot] - 1) & 1, kErrWaitEmpty)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(&bars->a_tma[slot], kASlot);
+              bulk_load(sA + slot * kASlot, acache + (size_t)kt * kASlot, kASlot, &bars->a_tma[slot]);
+              ++fills[slot];
+            }
             const int st = bidx % kBStages;
             if (bidx >= kBStages && !mbar_wait_or_abort(&bars->b_empty[st], ((bidx / kBStages) - 1) & 1, kErrWaitEmpty)) {
               ok = false;
@@ -258,33 +320,42 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
             mbar_arrive_expect_tx(&bars->b_full[st], kTile);
             bulk_load(sB + st * kTile, G.tiles + ((size_t)c * G.ktiles + kt) * kTile, kTile, &bars->b_full[st]);
           }
+        }
       }
     }
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       uint32_t bidx = 0, chunk_idx = 0;
-      uint32_t afill[kASlots] = {0, 0, 0};
+      uint32_t afill[kASlots] = {0, 0, 0}, tfill[kASlots] = {0, 0, 0};  // row fills, cache fills consumed
       const uint32_t idesc = idesc_i8(kRows, kNC);
       const uint64_t desc_a0 = smem_desc_sw128(sA), desc_b0 = smem_desc_sw128(sB);
       bool ok = true;
       for (int g = 0; g < a.ngemms && ok; ++g) {
         const GemmSpec& G = a.gemms[g];
         const bool resident = G.ktiles <= kASlots;
+        const bool cache = use_cache(G);
         for (int c = 0; c < G.nchunks && ok; ++c) {
           if (chunk_idx > 0 && !mbar_wait_or_abort(&bars->acc_empty, (chunk_idx - 1) & 1, kErrWaitAccFree)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const int kind = a_fill_kind(G, c, cache);
           for (int kt = 0; kt < G.ktiles; ++kt, ++bidx) {
             const int slot = kt % kASlots;
-            if (c == 0 || !resident) {
+            if (kind == 1) {
               if (!mbar_wait_or_abort(&bars->a_full[slot], afill[slot] & 1, kErrWaitFull)) {
                 ok = false;
                 break;
               }
               afill[slot]++;
+            } else if (kind == 2) {
+              if (!mbar_wait_or_abort(&bars->a_tma[slot], tfill[slot] & 1, kErrWaitFull)) {
+                ok = false;
+                break;
+              }
+              tfill[slot]++;
             }
             const int st = bidx % kBStages;
             if (!mbar_wait_or_abort(&bars->b_full[st], (bidx / kBStages) & 1, kErrWaitFull)) {
@@ -347,13 +418,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
         ok = false;
       afill[slot]++;
     };
-    auto publish = [&](int slot) {
+    auto publish = [&](int slot, bool cached = false) {
       fence_proxy_async_smem();
+      if (cached) fence_proxy_async_global();  // the cache copy, read back by bulk copies
       mbar_arrive(&bars->a_full[slot]);
     };
     // Warp-per-row slicing of K tile kt of the rows' fp32 source (coalesced loads, all of the
     // warp's rows in flight together) with per-row maxima rmax (shared memory).
-    auto gen_rows = [&](int kt, const float* src, int ld, int K, const float* rmax) {
+    auto gen_rows = [&](int kt, const float* src, int ld, int K, const float* rmax, uint8_t* gA) {
       float4 v[kRowsPerWarp];
       const int e = kt * 128 + 4 * lane;
 #pragma unroll
@@ -364,7 +436,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
 #pragma unroll
       for (int u = 0; u < kRowsPerWarp; ++u) {
         const int rr = warp + kRowWarps * u;
-        put4(sA, rr, e, v[u], row_inv_step(rmax[rr]));
+        if (gA) put4_2(sA, gA, rr, e, v[u], row_inv_step(rmax[rr]));
+        else put4(sA, rr, e, v[u], row_inv_step(rmax[rr]));
       }
     };
     // Runs GEMM g. prefilled: its (resident) A tiles were already published by a fused phase;
@@ -372,16 +445,19 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
     // this thread's row step and weight scale.
     auto run_gemm = [&](int g, bool prefilled, const float* src, int ld, const float* rmax, auto&& epilogue) {
       const GemmSpec& G = a.gemms[g];
-      const bool resident = G.ktiles <= kASlots;
+      const bool cache = use_cache(G);
       const float step = row_step(rmax[r]);
       for (int c = 0; c < G.nchunks; ++c) {
-        if (!prefilled && (c == 0 || !resident)) {
+        const int kind = a_fill_kind(G, c, cache);
+        if (!prefilled && kind == 1) {
           for (int kt = 0; kt < G.ktiles; ++kt) {
             const int slot = kt % kASlots;
             acquire(slot);
-            if (ok) gen_rows(kt, src, ld, G.K, rmax);
-            publish(slot);
+            if (ok) gen_rows(kt, src, ld, G.K, rmax, cache && c == 0 ? acache : nullptr);
+            publish(slot, cache && c == 0);
           }
+        } else if (kind == 2) {
+          for (int kt = 0; kt < G.ktiles; ++kt) afill[kt % kASlots]++;  // filled by the producer
         }
         if (a.trace && a.trace_fine) trace_point(a, tp++);
         const bool got = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&bars->acc_full, chunk_idx & 1, kErrWaitAcc));

@@ -69,6 +69,11 @@ struct BlockArgs {
   unsigned long long* trace;  // optional phase timestamps of CTA 0 (null: off)
   int trace_fine;             // also time every chunk of every GEMM
   int dec_kt;                 // decode kernel: K tiles of its activation-plane region
+  // block kernel: per-SM cache of the digit planes of a GEMM whose K tiles do not all fit in the
+  // A slots ([SM id < a_cache_sms][K tile < a_cache_kt][3 planes x 128 x 128], or null): sliced once
+  // for the GEMM's first chunk, copied back into the slots for the others
+  uint8_t* a_cache;
+  int a_cache_kt, a_cache_sms;
   // decode kernel, final launch with the greedy head fused in (fuse_head): the last GEMM is the
   // tied head; each session's first argmax and probability (argmaxProb) are written as
   // select_kernel would, and the last CTA to finish advances the step counter.

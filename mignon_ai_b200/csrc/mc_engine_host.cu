@@ -249,6 +249,9 @@ int build_dev_model(const HostModel& hm, int device, std::unique_ptr<DevModel>& 
 // ------------------------------------------------------------------------------------------------
 // Session batches on one device
 // ------------------------------------------------------------------------------------------------
+// SM ids the block kernel's plane cache covers (ids above it slice every chunk instead).
+constexpr int kACacheSms = 256;
+
 struct DevBatch {
   DevModel* m = nullptr;
   int S = 0, window = 0, pmax = 0, nsplit = 1, topk = 0;
@@ -258,6 +261,8 @@ struct DevBatch {
   cudaStream_t stream = nullptr;
   std::vector<void*> allocs;
   int32_t* sel_done = nullptr;  // select_kernel's finished-block counter (zero between launches)
+  uint8_t* a_cache = nullptr;    // block kernel: per-SM digit-plane cache of GEMMs wider than the A slots
+  int a_cache_kt = 0;
   int32_t *pos = nullptr, *seglen = nullptr, *tok = nullptr, *next_tok = nullptr, *step = nullptr, *rowmap = nullptr,
           *rowmap_id = nullptr, *target = nullptr;
   float *norm_ring = nullptr, *latch = nullptr, *kv = nullptr;
@@ -325,9 +330,12 @@ static std::mutex g_attr_mu;
 static int ensure_attrs(int device) {
   std::lock_guard<std::mutex> lk(g_attr_mu);
   if (device < 64 && g_attr_done[device]) return kOk;
-  MC_CUDA(cudaFuncSetAttribute(block_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
-  MC_CUDA(cudaFuncSetAttribute(block_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
-  MC_CUDA(cudaFuncSetAttribute(block_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
+  MC_CUDA(cudaFuncSetAttribute(block_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
+  MC_CUDA(cudaFuncSetAttribute(block_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
+  MC_CUDA(cudaFuncSetAttribute(block_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
+  MC_CUDA(cudaFuncSetAttribute(block_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
+  MC_CUDA(cudaFuncSetAttribute(block_kernel<3, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
+  MC_CUDA(cudaFuncSetAttribute(block_kernel<3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlockSmem));
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<1, 32, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<2, 32, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<3, 32, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
@@ -398,6 +406,15 @@ int batch_create(DevModel* m, int S, int window, int pmax, int topk, std::unique
       (st = b->alloc(b->att_rowmax, R * 4)) || (st = b->alloc(b->fnorm, R * D * 4)) || (st = b->alloc(b->fnorm_rowmax, R * 4)))
     return st;
   if (m->n_attn > 0 && (st = b->alloc(b->kvlin, (size_t)S * b->pmax * 2 * D * 4))) return st;
+  {
+    // K tiles of the widest GEMM (K = 3D for W1, H for W2): beyond the A slots, the block kernel
+    // slices its first chunk once and reads the planes back from this per-SM cache
+    const int kt = std::max((3 * D + 127) / 128, (H + 127) / 128);
+    if (kt > kASlots) {
+      b->a_cache_kt = kt;
+      if ((st = b->alloc(b->a_cache, (size_t)kACacheSms * kt * kASlot))) return st;
+    }
+  }
   if ((st = b->alloc(b->part, (size_t)S * b->nsplit * 4 * sizeof(float4)))) return st;
   if (topk > 0 && ((st = b->alloc(b->topv, (size_t)S * b->nsplit * 4 * topk * 4)) ||
                    (st = b->alloc(b->topi, (size_t)S * b->nsplit * 4 * topk * 4))))
@@ -451,6 +468,9 @@ static void fill_common(const DevBatch& b, BlockArgs& a, int P) {
   a.fnorm = b.fnorm;
   a.fnorm_rowmax = b.fnorm_rowmax;
   a.kvlin = P > 1 ? b.kvlin : nullptr;
+  a.a_cache = b.a_cache;
+  a.a_cache_kt = b.a_cache_kt;
+  a.a_cache_sms = kACacheSms;
 }
 
 static GemmSpec spec(const DevGemm& g, int type, int step) {
@@ -587,9 +607,9 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
       kern<<<grid, kDThreads, m.dec_smem, s>>>(a);
     } else {
       switch ((m.D + 127) / 128) {
-        case 1: block_kernel<1><<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
-        case 2: block_kernel<2><<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
-        default: block_kernel<3><<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
+        case 1: (a.a_cache ? block_kernel<1, true> : block_kernel<1, false>)<<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
+        case 2: (a.a_cache ? block_kernel<2, true> : block_kernel<2, false>)<<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
+        default: (a.a_cache ? block_kernel<3, true> : block_kernel<3, false>)<<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
       }
     }
     MC_CUDA(cudaGetLastError());

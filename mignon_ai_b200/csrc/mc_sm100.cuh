@@ -106,6 +106,10 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
 // ---------------------------------------------------------------------------------------------
 // Async-proxy fences and TMA
 // ---------------------------------------------------------------------------------------------
+// Makes this thread's generic-proxy global-memory writes visible to later async-proxy reads
+// (bulk copies) by threads that synchronize with it afterwards.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 // Makes this thread's generic-proxy shared-memory writes visible to the async proxy (TMA, MMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
