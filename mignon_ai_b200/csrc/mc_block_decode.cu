@@ -37,6 +37,9 @@ struct DBars {
   uint64_t w_full[kDMaxWStages], w_empty[kDMaxWStages], s_full[kDSlots], s_empty[kDSlots], b_full;
   uint32_t tmem;
   int valid[kDMaxR], tok[kDMaxR], pos[kDMaxR];
+  // attention blocks: offset in kv of each session's key ring row for its position (value ring
+  // and other heads follow at fixed distances)
+  unsigned long long kvoff[kDMaxR];
   float rstep[kDMaxR];  // step of each session row of the current GEMM's activation planes
   // fused head: per quadrant warp, each session's running (max, sum of exp, first argmax)
   float red_m[4][kDMaxR], red_s[4][kDMaxR];
@@ -282,6 +285,8 @@ __device__ __forceinline__ void decode_block(const BlockArgs& a, const DecodeLay
       const bool v = s < a.n_sess && a.seglen[s] > 0;
       bars->valid[t] = v ? 1 : 0;
       bars->pos[t] = v ? a.pos0[s] : 0;
+      if (a.has_attn && v)
+        bars->kvoff[t] = ((size_t)a.attn_slot * a.n_sess + s) * 2 * (size_t)a.cache * D + (size_t)(a.pos0[s] % a.cache) * a.dh;
       int tok = 0;
       if (v && a.embed_first) {
         tok = a.tokens[s];
@@ -686,20 +691,16 @@ __device__ __forceinline__ void decode_block(const BlockArgs& a, const DecodeLay
         const int part = n / D, e = n - part * D;
         const int hh = part > 0 ? e / dh : 0;
         const float scale = a.gemms[gi - 1].scale;
+        // key/value rings, head-major: [K|V][head][slot][dh]; this channel's place past the
+        // session's key-ring row
+        const size_t cofs = (size_t)(part - 1) * a.cache * D + (size_t)hh * a.cache * dh + (e - hh * dh);
 #pragma unroll
         for (int j = 0; j < kDCols; ++j) {
           const int rr = r0 + j;
           if (!bars->valid[rr]) continue;
-          const int s = s0 + rr;
           const float y = dequant(x1[j], x2[j], x3[j], stp[j], scale);
-          if (part == 0) {
-            a.qbuf[(size_t)s * D + e] = y;
-          } else {
-            // key/value rings, head-major: [K|V][head][slot][dh]
-            float* kvs = a.kv + ((size_t)a.attn_slot * a.n_sess + s) * 2 * (size_t)a.cache * D;
-            const int rslot = bars->pos[rr] % a.cache;
-            kvs[(size_t)(part - 1) * a.cache * D + ((size_t)hh * a.cache + rslot) * dh + (e - hh * dh)] = y;
-          }
+          if (part == 0) a.qbuf[(size_t)(s0 + rr) * D + e] = y;
+          else a.kv[bars->kvoff[rr] + cofs] = y;
         }
       });
     }
