@@ -125,6 +125,15 @@ int mc_append(mc_batch* batch, const int32_t* tokens, float* logits, int32_t* ne
  * vocabulary. Afterwards the sessions continue as after mc_prefill of the same tokens. */
 int mc_score(mc_batch* batch, const int32_t* seqs, const int32_t* lens, int stride, double* out);
 
+/* mc_score with the scored tokens given: out[s*stride + t] = log p(targets[s*stride + t] |
+ * seqs[s][0..t]) for t < lens[s] — the loss terms of nll.score (internal/eval/eval.go:27-43) for
+ * windows whose last target lies past the window itself (Perplexity / PerplexityPerDoc beyond the
+ * context, eval.go:55-60, perdoc.go:16-32); other entries are 0. Same limits as mc_score
+ * (lens[s] <= window and max_prompt; targets inside the vocabulary); afterwards the sessions
+ * continue as after mc_prefill of seqs. */
+int mc_score_targets(mc_batch* batch, const int32_t* seqs, const int32_t* lens, int stride, const int32_t* targets,
+                     double* out);
+
 /* The decode loop of generate.greedyLoop (internal/generate/greedy.go:63-87) without stop tokens,
  * or with temperature > 0 the sampled loop of sampleContinuation (generate/sample.go:196-247)
  * with top-k = the batch's top_k, no repetition penalty, top-p 1: prefill each prompt, then

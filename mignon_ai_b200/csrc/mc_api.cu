@@ -144,6 +144,9 @@ int upload_prompts(mc_batch* b, const int32_t* tokens, const int32_t* lens, int 
     MC_CUDA(cudaMemcpyAsync(sh.seglen, len, sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
     MC_CUDA(cudaMemcpyAsync(sh.pos, zero, sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
     MC_CUDA(cudaMemcpyAsync(sh.rowmap, rowmap, sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    // a one-row segment runs through the decode kernels, which read each session's token from
+    // next_tok
+    if (P == 1) MC_CUDA(cudaMemcpyAsync(sh.next_tok, tok, sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
     MC_CUDA(cudaEventRecord(sh.h_stage_done, sh.stream));
   }
   return kOk;
@@ -186,6 +189,71 @@ int run_decode_steps(DevBatch& sh, int n_new, int mode, double inv_temp, uint32_
   for (int t = 1; t < n_new; ++t) {
     const int st = run_graph_step(sh, mode, inv_temp, session0, false);
     if (st != kOk) return st;
+  }
+  return kOk;
+}
+
+// Per-position log-probabilities of a prefill pass over seqs (the nll.score loop of
+// internal/eval/eval.go:27-43 over every prefix, logProb of eval/suite.go:201-209).
+// targets == null: position t is scored against seqs[t + 1] (t < lens - 1), out is
+// [count x (stride - 1)]; else against targets[t] (t < lens), out is [count x stride].
+int score_impl(mc_batch* b, const int32_t* seqs, const int32_t* lens, int stride, const int32_t* targets, double* out,
+               const char* name) {
+  const std::string fn(name);
+  if (stride < 1) return set_error(kInvalidArgument, fn + ": stride < 1");
+  const int V = b->model->dev[0]->V;
+  auto target_of = [&](int s, int t) -> int32_t {
+    return targets ? targets[(size_t)s * stride + t] : seqs[(size_t)s * stride + t + 1];
+  };
+  auto scored = [&](int s, int t) { return targets ? t < lens[s] : t + 1 < lens[s]; };
+  for (int s = 0; s < b->count; ++s) {
+    if (lens[s] < 0 || lens[s] > stride) return set_error(kInvalidArgument, fn + ": length outside [0, stride]");
+    if (lens[s] > b->window)
+      return set_error(kInvalidArgument, fn + ": sequence " + std::to_string(s) + " is longer than the session window");
+    for (int t = 0; t < lens[s]; ++t)
+      if (scored(s, t) && (target_of(s, t) < 0 || target_of(s, t) >= V))
+        return set_error(kInvalidArgument, fn + ": target token outside the vocabulary");
+  }
+  int P = 1;
+  int st = upload_prompts(b, seqs, lens, stride, &P);
+  if (st != kOk) return st;
+  const int cols = targets ? stride : stride - 1;
+  std::fill(out, out + (size_t)b->count * cols, 0.0);
+  for (size_t g = 0; g < b->shard.size(); ++g) {
+    DevBatch& sh = *b->shard[g];
+    if (sh.S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh.m->device));
+    const int s0 = b->first[g];
+    const size_t rows = (size_t)sh.S * P;
+    if ((st = ensure_score_rows(sh, rows)) != kOk) return st;
+    // row r = i * P + t: the final-normed row of position t of session i
+    const int spt = std::max(1, 128 / P);
+    std::vector<int32_t> rowmap(rows), target(rows, 0), valid(rows, 0), pos(sh.S), seglen(sh.S);
+    for (int i = 0; i < sh.S; ++i) {
+      const int n = lens[s0 + i];
+      for (int t = 0; t < P; ++t) {
+        const size_t r = (size_t)i * P + t;
+        rowmap[r] = (i / spt) * 128 + (i % spt) * P + t;
+        if (t < n && scored(s0 + i, t)) {
+          target[r] = target_of(s0 + i, t);
+          valid[r] = 1;
+        }
+      }
+      pos[i] = n;  // afterwards the sessions continue as after mc_prefill of the same tokens
+      seglen[i] = n > 0 ? 1 : 0;
+    }
+    MC_CUDA(cudaMemcpyAsync(sh.sc_rowmap, rowmap.data(), rows * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.sc_target, target.data(), rows * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.sc_valid, valid.data(), rows * 4, cudaMemcpyHostToDevice, sh.stream));
+    if ((st = enqueue_score(sh, P, rows)) != kOk) return st;
+    std::vector<double> lp(rows);
+    MC_CUDA(cudaMemcpyAsync(lp.data(), sh.sc_logprob, rows * 8, cudaMemcpyDeviceToHost, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.pos, pos.data(), sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.seglen, seglen.data(), sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    if ((st = check_device_error(sh.stream)) != kOk) return st;  // synchronizes the stream
+    for (int i = 0; i < sh.S; ++i)
+      for (int t = 0; t < lens[s0 + i]; ++t)
+        if (scored(s0 + i, t)) out[(size_t)(s0 + i) * cols + t] = lp[(size_t)i * P + t];
   }
   return kOk;
 }
@@ -337,57 +405,14 @@ int mc_prefill(mc_batch* b, const int32_t* tokens, const int32_t* lens, int stri
 int mc_score(mc_batch* b, const int32_t* seqs, const int32_t* lens, int stride, double* out) {
   clear_error();
   if (!b || !seqs || !lens || !out) return set_error(kInvalidArgument, "mc_score: null argument");
-  if (stride < 1) return set_error(kInvalidArgument, "mc_score: stride < 1");
-  const int V = b->model->dev[0]->V;
-  for (int s = 0; s < b->count; ++s) {
-    if (lens[s] < 0 || lens[s] > stride) return set_error(kInvalidArgument, "mc_score: length outside [0, stride]");
-    if (lens[s] > b->window)
-      return set_error(kInvalidArgument, "mc_score: sequence " + std::to_string(s) + " is longer than the session window");
-    for (int t = 1; t < lens[s]; ++t)
-      if (seqs[(size_t)s * stride + t] < 0 || seqs[(size_t)s * stride + t] >= V)
-        return set_error(kInvalidArgument, "mc_score: target token outside the vocabulary");
-  }
-  int P = 1;
-  int st = upload_prompts(b, seqs, lens, stride, &P);
-  if (st != kOk) return st;
-  const int cols = stride - 1;
-  std::fill(out, out + (size_t)b->count * cols, 0.0);
-  for (size_t g = 0; g < b->shard.size(); ++g) {
-    DevBatch& sh = *b->shard[g];
-    if (sh.S == 0) continue;
-    MC_CUDA(cudaSetDevice(sh.m->device));
-    const int s0 = b->first[g];
-    const size_t rows = (size_t)sh.S * P;
-    if ((st = ensure_score_rows(sh, rows)) != kOk) return st;
-    // row r = i * P + t: the final-normed row of position t of session i, target token t + 1
-    const int spt = std::max(1, 128 / P);
-    std::vector<int32_t> rowmap(rows), target(rows, 0), valid(rows, 0), pos(sh.S), seglen(sh.S);
-    for (int i = 0; i < sh.S; ++i) {
-      const int n = lens[s0 + i];
-      for (int t = 0; t < P; ++t) {
-        const size_t r = (size_t)i * P + t;
-        rowmap[r] = (i / spt) * 128 + (i % spt) * P + t;
-        if (t + 1 < n) {
-          target[r] = seqs[(size_t)(s0 + i) * stride + t + 1];
-          valid[r] = 1;
-        }
-      }
-      pos[i] = n;  // afterwards the sessions continue as after mc_prefill of the same tokens
-      seglen[i] = n > 0 ? 1 : 0;
-    }
-    MC_CUDA(cudaMemcpyAsync(sh.sc_rowmap, rowmap.data(), rows * 4, cudaMemcpyHostToDevice, sh.stream));
-    MC_CUDA(cudaMemcpyAsync(sh.sc_target, target.data(), rows * 4, cudaMemcpyHostToDevice, sh.stream));
-    MC_CUDA(cudaMemcpyAsync(sh.sc_valid, valid.data(), rows * 4, cudaMemcpyHostToDevice, sh.stream));
-    if ((st = enqueue_score(sh, P, rows)) != kOk) return st;
-    std::vector<double> lp(rows);
-    MC_CUDA(cudaMemcpyAsync(lp.data(), sh.sc_logprob, rows * 8, cudaMemcpyDeviceToHost, sh.stream));
-    MC_CUDA(cudaMemcpyAsync(sh.pos, pos.data(), sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
-    MC_CUDA(cudaMemcpyAsync(sh.seglen, seglen.data(), sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
-    if ((st = check_device_error(sh.stream)) != kOk) return st;  // synchronizes the stream
-    for (int i = 0; i < sh.S; ++i)
-      for (int t = 0; t + 1 < lens[s0 + i]; ++t) out[(size_t)(s0 + i) * cols + t] = lp[(size_t)i * P + t];
-  }
-  return kOk;
+  return score_impl(b, seqs, lens, stride, nullptr, out, "mc_score");
+}
+
+int mc_score_targets(mc_batch* b, const int32_t* seqs, const int32_t* lens, int stride, const int32_t* targets,
+                     double* out) {
+  clear_error();
+  if (!b || !seqs || !lens || !targets || !out) return set_error(kInvalidArgument, "mc_score_targets: null argument");
+  return score_impl(b, seqs, lens, stride, targets, out, "mc_score_targets");
 }
 
 int mc_append(mc_batch* b, const int32_t* tokens, float* logits, int32_t* next, float* prob) {
@@ -472,7 +497,7 @@ int mc_generate_dev(mc_batch* b, const int32_t* d_prompts, const int32_t* d_lens
   int st;
   if ((st = ensure_step_outputs(sh, false, n_new)) != kOk) return st;
   prepare_prompts_kernel<<<(sh.S + 127) / 128, 128, 0, sh.stream>>>(d_prompts, d_lens, stride, sh.S, P, b->window, sh.tok,
-                                                                      sh.seglen, sh.pos, sh.rowmap, sh.step);
+                                                                      sh.seglen, sh.pos, sh.rowmap, sh.step, sh.next_tok);
   MC_CUDA(cudaGetLastError());
   if ((st = enqueue_forward(sh, P, mode, inv_t, session0, false, true)) != kOk) return st;
   if ((st = run_decode_steps(sh, n_new, mode, inv_t, session0)) != kOk) return st;

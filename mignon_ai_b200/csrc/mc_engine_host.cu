@@ -505,9 +505,12 @@ struct LaunchLog {
 };
 
 // Prepares a prefill from device-resident prompts: trims each prompt to the window, lays the
-// segment out [S][P], resets positions and computes the head's row map.
+// segment out [S][P], resets positions and computes the head's row map. A one-row segment runs
+// through the decode kernels, which read the token of each session from next_tok: P == 1 also
+// writes it there.
 __global__ void prepare_prompts_kernel(const int32_t* prompts, const int32_t* lens, int stride, int S, int P, int window,
-                                       int32_t* tok, int32_t* seglen, int32_t* pos, int32_t* rowmap, int32_t* step) {
+                                       int32_t* tok, int32_t* seglen, int32_t* pos, int32_t* rowmap, int32_t* step,
+                                       int32_t* next_tok) {
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s == 0) *step = 0;
   if (s >= S) return;
@@ -515,6 +518,7 @@ __global__ void prepare_prompts_kernel(const int32_t* prompts, const int32_t* le
   const int n = min(min(L, window), P);
   const int32_t* src = prompts + (size_t)s * stride + (L - n);
   for (int i = 0; i < P; ++i) tok[(size_t)s * P + i] = i < n ? src[i] : 0;
+  if (P == 1) next_tok[s] = n > 0 ? src[0] : 0;
   seglen[s] = n;
   pos[s] = 0;
   const int spt = max(1, 128 / P);

@@ -33,6 +33,7 @@ _lib.register({
     "mc_batch_close": [c_vp],
     "mc_prefill": [c_vp, c_vp, c_vp, _i, c_vp, c_vp, c_vp],
     "mc_score": [c_vp, c_vp, c_vp, _i, c_vp],
+    "mc_score_targets": [c_vp, c_vp, c_vp, _i, c_vp, c_vp],
     "mc_append": [c_vp, c_vp, c_vp, c_vp, c_vp],
     "mc_generate": [c_vp, c_vp, c_vp, _i, _i, ctypes.c_double, ctypes.c_uint32, c_vp, c_vp],
 })
@@ -183,6 +184,21 @@ class SessionBatch:
         _lib.check(_lib.lib().mc_score(self._h, _lib.ptr(q), _lib.ptr(lens), q.shape[1], _lib.ptr(out)))
         return out
 
+    def score_targets(self, seqs, targets, lens=None):
+        """Per-position log-probabilities of given targets: out[s, t] = log p(targets[s, t] |
+        seqs[s, :t+1]) for t < lens[s] (nll.score, internal/eval/eval.go:27-43); other entries 0."""
+        q = np.ascontiguousarray(seqs, np.int32)
+        tg = np.ascontiguousarray(targets, np.int32)
+        if q.ndim == 1:
+            q, tg = q[None, :], tg[None, :]
+        if tg.shape != q.shape:
+            raise ValueError("targets must have the shape of seqs")
+        lens = np.full(self.count, q.shape[1], np.int32) if lens is None else np.ascontiguousarray(lens, np.int32)
+        out = np.zeros((self.count, q.shape[1]), np.float64)
+        _lib.check(_lib.lib().mc_score_targets(self._h, _lib.ptr(q), _lib.ptr(lens), q.shape[1], _lib.ptr(tg),
+                                               _lib.ptr(out)))
+        return out
+
     def generate(self, prompts, lens, n_new: int, temperature: float = 0.0, session0: int = 0):
         p = np.ascontiguousarray(prompts, np.int32)
         lens = np.ascontiguousarray(lens, np.int32)
@@ -252,3 +268,85 @@ def greedy_continuation(sess: Session, context: Sequence[int], max_tokens: int, 
         if len(ids) < max_tokens:
             logits = sess.append(best)
     return ids, probs
+
+
+class HeldOut:
+    """eval.HeldOut (internal/eval/eval.go): mean loss in nats per scored token, perplexity
+    exp(loss), bits per byte (when token byte lengths are given) and the number of tokens."""
+
+    def __init__(self, nats: float = 0.0, tokens: int = 0, nbytes: int = 0, with_bytes: bool = False):
+        self.tokens = tokens
+        self.loss = nats / tokens if tokens else 0.0
+        self.ppl = float(np.exp(self.loss)) if tokens else 0.0
+        self.bpb = (nats / np.log(2.0) / nbytes if nbytes else 0.0) if with_bytes and tokens else None
+
+    def __repr__(self):
+        return f"HeldOut(loss={self.loss:.6f}, ppl={self.ppl:.4f}, bpb={self.bpb}, tokens={self.tokens})"
+
+
+def _nll(model: "Model", streams, context_size: int, token_bytes=None, batch_size: int = 1024) -> HeldOut:
+    """nll.score (internal/eval/eval.go:27-43) over token streams, from position 1 to the end:
+    token t is predicted from window(stream[:t], context_size), the last context_size tokens.
+    Targets t <= context_size share one prefix pass per stream; each later target gets its own
+    window of context_size tokens. The windows run batch_size at a time on the engine."""
+    V = model.vocab
+    ctx = min(int(context_size), model.max_context)
+    jobs = []  # (sequence, targets, positions to read)
+    for T in streams:
+        T = np.asarray(T, np.int64)
+        L = len(T)
+        if L < 2:
+            continue
+        n = min(L - 1, ctx)
+        jobs.append((T[:n], T[1:n + 1], np.arange(n)))
+        for t in range(ctx + 1, L):
+            w = T[t - ctx:t]
+            jobs.append((w, np.concatenate([T[t - ctx + 1:t], T[t:t + 1]]), np.array([ctx - 1])))
+    nats, count, nbytes = 0.0, 0, 0
+    batch = model.new_batch(max(1, min(batch_size, len(jobs))), ctx, ctx)
+    try:
+        for j0 in range(0, len(jobs), batch.count):
+            chunk = jobs[j0:j0 + batch.count]
+            seqs = np.zeros((batch.count, ctx), np.int32)
+            tgts = np.zeros((batch.count, ctx), np.int32)
+            lens = np.zeros(batch.count, np.int32)
+            for i, (q, tg, _) in enumerate(chunk):
+                seqs[i, :len(q)] = q
+                tgts[i, :len(q)] = np.clip(tg, 0, V - 1)  # out-of-range targets are skipped below
+                lens[i] = len(q)
+            lp = batch.score_targets(seqs, tgts, lens)
+            for i, (q, tg, read) in enumerate(chunk):
+                for p in read:
+                    target = int(tg[p])
+                    if 0 <= target < V:  # the reference skips targets outside the logits
+                        nats -= float(lp[i, p])
+                        count += 1
+                        if token_bytes is not None:
+                            nbytes += int(token_bytes[target])
+    finally:
+        batch.close()
+    return HeldOut(nats, count, nbytes, token_bytes is not None)
+
+
+def perplexity(model: "Model", tokens: Sequence[int], context_size: int, max_tokens: int = 0, token_bytes=None,
+               batch_size: int = 1024) -> HeldOut:
+    """eval.Perplexity (internal/eval/eval.go:49-62) on an already tokenized text: one continuous
+    stream, every token after the first predicted from the context_size tokens before it (at most
+    max_tokens of them when > 0). token_bytes[id]: the byte length of each token, for bits per byte."""
+    T = list(tokens)
+    if len(T) < 2:
+        return HeldOut()
+    n = len(T) - 1
+    if max_tokens > 0 and n > max_tokens:
+        n = max_tokens
+    return _nll(model, [T[:n + 1]], context_size, token_bytes, batch_size)
+
+
+def perplexity_per_doc(model: "Model", docs: Sequence[Sequence[int]], context_size: int, eos_id: int,
+                       max_docs: int = 0, token_bytes=None, batch_size: int = 1024) -> HeldOut:
+    """eval.PerplexityPerDoc (internal/eval/perdoc.go:16-32) on already tokenized documents: each
+    document scored on its own, starting from EOS, every token of it (the first included)."""
+    docs = list(docs)
+    if max_docs > 0:
+        docs = docs[:max_docs]
+    return _nll(model, [[eos_id] + list(d) for d in docs], context_size, token_bytes, batch_size)

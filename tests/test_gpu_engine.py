@@ -123,6 +123,34 @@ def test_generate_greedy_matches_oracle(oracle):
     b.close()
 
 
+def test_one_token_prompts_match_oracle(oracle):
+    """A prefill whose longest prompt has one token runs through the decode kernels, which read
+    each session's token from the decode input: the prompt tokens must be the ones there, for
+    mc_prefill (logits after the token), mc_generate and mc_score_targets alike."""
+    spec = small_spec(2, vocab=512)
+    data = synth.build_model_file(spec)
+    om, gm = oracle.Model(data), quant.Model.decode(data)
+    n = 40
+    prompts = synth.prompts_uniform_fast(n, 1, spec.vocab, seed=17)
+    lens = np.ones(n, np.int32)
+    b = gm.new_batch(n, 0, 8)
+    # the decode input holds something else before the prefill
+    b.append(np.full(n, 9, np.int32))
+    logits, _, _ = b.prefill(prompts, lens, want_logits=True)
+    for s in (0, 1, n - 1):
+        check_logits(logits[s], om.call(prompts[s, :1]), f"prefill of one token, session {s}")
+    wt, _, wl = om.generate_greedy(prompts, lens, 6, logits=True)
+    gt, _ = b.generate(prompts, lens, 6)
+    compare_streams(gt, wt, wl)
+    tg = np.full((n, 1), 11, np.int32)
+    lp = b.score_targets(prompts, tg, lens)
+    for s in (0, n - 1):
+        l = np.asarray(om.call(prompts[s, :1]), np.float64)
+        want = l[11] - l.max() - np.log(np.sum(np.exp(l - l.max())))
+        assert abs(lp[s, 0] - want) <= 2e-3 * np.max(np.abs(l))
+    b.close()
+
+
 def test_ragged_prompts_and_idle_sessions(oracle):
     """Prompts of different lengths in one batch; a zero-length prompt leaves its session idle."""
     spec = small_spec(2, vocab=512)
@@ -244,6 +272,45 @@ def test_decode_kernel_matches_block_kernel_bitwise(monkeypatch, cfg, vocab, dec
     for i, name in enumerate(("tokens", "probs", "logits")):
         a, b = got["decode"][i][act], got["block"][i][act]
         assert np.array_equal(a, b), f"{name}: {np.sum(a != b)} entries differ"
+    gm.close()
+
+
+def test_perplexity_matches_reference_loop(oracle):
+    """quant.perplexity / perplexity_per_doc (eval.Perplexity, eval.go:49-62; PerplexityPerDoc,
+    perdoc.go:16-32) against the reference's nll.score loop (eval.go:27-43) restated with the
+    oracle: every target t predicted from a fresh Call of the last context_size tokens before it.
+    Streams longer than the context exercise mc_score_targets' windows past the first pass; batch
+    size 8 splits the windows over several calls. Mean loss within 2e-3 * max|logit| (the
+    per-token log-probability bar), bits per byte with it, token counts exact."""
+    spec = small_spec(2, vocab=512)
+    data = synth.build_model_file(spec)
+    om, gm = oracle.Model(data), quant.Model.decode(data)
+    ctx = 16
+    rng = np.random.default_rng(21)
+    text = rng.integers(5, spec.vocab, size=45)
+    docs = [rng.integers(5, spec.vocab, size=k) for k in (9, 30, 1)]
+    token_bytes = rng.integers(1, 5, size=spec.vocab)
+
+    def ref(streams):
+        nats, count, nbytes, scale = 0.0, 0, 0, 0.0
+        for T in streams:
+            for t in range(1, len(T)):
+                logits = np.asarray(om.call(np.asarray(T[max(0, t - ctx):t], np.int32)), np.float64)
+                m = logits.max()
+                nats -= logits[T[t]] - m - np.log(np.sum(np.exp(logits - m)))
+                count += 1
+                nbytes += int(token_bytes[T[t]])
+                scale = max(scale, float(np.max(np.abs(logits))))
+        return nats / count, nats / (np.log(2.0) * nbytes), count, scale
+
+    for got, streams in ((quant.perplexity(gm, text, ctx, token_bytes=token_bytes, batch_size=8), [list(text)]),
+                         (quant.perplexity_per_doc(gm, docs, ctx, eos_id=4, token_bytes=token_bytes, batch_size=8),
+                          [[4] + list(d) for d in docs])):
+        loss, bpb, count, scale = ref(streams)
+        assert got.tokens == count
+        assert abs(got.loss - loss) <= 2e-3 * scale, (got.loss, loss)
+        assert abs(got.ppl - np.exp(loss)) <= np.exp(loss) * 2e-3 * scale * 1.01
+        assert abs(got.bpb - bpb) <= 2e-3 * scale / np.log(2.0)  # every token covers >= 1 byte
     gm.close()
 
 
