@@ -143,6 +143,14 @@ int mc_score_targets(mc_batch* batch, const int32_t* seqs, const int32_t* lens, 
 int mc_generate(mc_batch* batch, const int32_t* prompts, const int32_t* lens, int stride, int n_new, double temperature,
                 uint32_t session0, int32_t* out_tokens, float* out_probs);
 
+/* mc_generate with stop tokens (greedyLoop's `stops`, internal/generate/greedy.go:63-87): a
+ * session ends before the first token among stops[0..n_stops) it would emit (n_stops <= 8); its
+ * remaining out_tokens entries are -1 (out_probs 0) and out_lens[s] is the number of tokens it
+ * emitted (n_new when no stop came). The session stays after its last emitted token. */
+int mc_generate_stops(mc_batch* batch, const int32_t* prompts, const int32_t* lens, int stride, int n_new,
+                      double temperature, uint32_t session0, const int32_t* stops, int n_stops, int32_t* out_tokens,
+                      float* out_probs, int32_t* out_lens);
+
 /* mc_generate with device-resident inputs and outputs on a single-device batch: enqueues the
  * whole job on the batch's stream (mc_batch_stream) and returns without synchronizing.
  * pmax >= every lens[s]. Check completion and device errors with mc_batch_error. */

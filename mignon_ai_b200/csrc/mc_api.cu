@@ -161,6 +161,8 @@ int run_graph_step(DevBatch& sh, int mode, double inv_temp, uint32_t session0, b
   key.session0 = session0;
   key.out_tok = sh.out_tok;
   key.logits_buf = sh.logits;
+  key.n_stops = sh.n_stops;
+  for (int k = 0; k < sh.n_stops; ++k) key.stops[k] = sh.stops[k];
   if (!sh.graph || !(sh.graph_key == key)) {
     if (sh.graph) {
       cudaGraphExecDestroy(sh.graph);
@@ -257,6 +259,67 @@ int score_impl(mc_batch* b, const int32_t* seqs, const int32_t* lens, int stride
   }
   return kOk;
 }
+
+// The decode loop of mc_generate / mc_generate_stops (greedyLoop, generate/greedy.go:63-87, with
+// stop tokens: a session ends before the first one it would emit; out_lens[s] = tokens emitted,
+// the rest of its row -1).
+int generate_impl(mc_batch* b, const int32_t* prompts, const int32_t* lens, int stride, int n_new, double temperature,
+                  uint32_t session0, const int32_t* stops, int n_stops, int32_t* out_tokens, float* out_probs,
+                  int32_t* out_lens) {
+  if (!b || !prompts || !lens || !out_tokens || n_new <= 0) return set_error(kInvalidArgument, "mc_generate: bad arguments");
+  const int mode = temperature > 0.001 ? 1 : 0;
+  if (mode == 1 && b->topk < 1)
+    return set_error(kUnsupported, "mc_generate: sampling needs a batch opened with top_k in [1, 64]");
+  const double inv_t = temperature > 0.001 ? 1.0 / temperature : 0.0;
+  int P = 1;
+  int st = upload_prompts(b, prompts, lens, stride, &P);
+  if (st != kOk) return st;
+  for (size_t g = 0; g < b->shard.size(); ++g) {
+    DevBatch& sh = *b->shard[g];
+    if (sh.S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh.m->device));
+    if ((st = ensure_step_outputs(sh, false, n_new)) != kOk) return st;
+    MC_CUDA(cudaMemsetAsync(sh.step, 0, 4, sh.stream));
+    sh.n_stops = n_stops;
+    for (int k = 0; k < n_stops; ++k) sh.stops[k] = stops[k];
+    if (n_stops > 0) {  // sessions that end early leave their remaining columns at -1 / 0
+      MC_CUDA(cudaMemsetAsync(sh.out_tok, 0xFF, (size_t)sh.S * sh.out_stride * 4, sh.stream));
+      MC_CUDA(cudaMemsetAsync(sh.out_prob, 0, (size_t)sh.S * sh.out_stride * 4, sh.stream));
+    }
+    const uint32_t s0 = session0 + (uint32_t)b->first[g];
+    st = enqueue_forward(sh, P, mode, inv_t, s0, false, true);
+    if (st == kOk) st = run_decode_steps(sh, n_new, mode, inv_t, s0);
+    sh.n_stops = 0;  // only this job's launches carry the stop tokens
+    if (st != kOk) return st;
+  }
+  for (size_t g = 0; g < b->shard.size(); ++g) {
+    DevBatch& sh = *b->shard[g];
+    if (sh.S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh.m->device));
+    // out columns are laid out with stride sh.out_stride >= n_new: the first n_new of each
+    // session's row go straight to the caller's rows of this shard's sessions
+    const size_t row0 = (size_t)b->first[g] * n_new;
+    MC_CUDA(cudaMemcpy2DAsync(out_tokens + row0, (size_t)n_new * 4, sh.out_tok, (size_t)sh.out_stride * 4,
+                              (size_t)n_new * 4, sh.S, cudaMemcpyDeviceToHost, sh.stream));
+    if (out_probs)
+      MC_CUDA(cudaMemcpy2DAsync(out_probs + row0, (size_t)n_new * 4, sh.out_prob, (size_t)sh.out_stride * 4,
+                                (size_t)n_new * 4, sh.S, cudaMemcpyDeviceToHost, sh.stream));
+  }
+  for (size_t g = 0; g < b->shard.size(); ++g) {
+    DevBatch& sh = *b->shard[g];
+    if (sh.S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh.m->device));
+    if ((st = check_device_error(sh.stream)) != kOk) return st;
+  }
+  if (out_lens)
+    for (int s = 0; s < b->count; ++s) {
+      int n = 0;
+      while (n < n_new && out_tokens[(size_t)s * n_new + n] >= 0) ++n;
+      out_lens[s] = n;
+    }
+  return kOk;
+}
+
 
 }  // namespace
 
@@ -434,44 +497,17 @@ int mc_append(mc_batch* b, const int32_t* tokens, float* logits, int32_t* next, 
 int mc_generate(mc_batch* b, const int32_t* prompts, const int32_t* lens, int stride, int n_new, double temperature,
                 uint32_t session0, int32_t* out_tokens, float* out_probs) {
   clear_error();
-  if (!b || !prompts || !lens || !out_tokens || n_new <= 0) return set_error(kInvalidArgument, "mc_generate: bad arguments");
-  const int mode = temperature > 0.001 ? 1 : 0;
-  if (mode == 1 && b->topk < 1)
-    return set_error(kUnsupported, "mc_generate: sampling needs a batch opened with top_k in [1, 64]");
-  const double inv_t = temperature > 0.001 ? 1.0 / temperature : 0.0;
-  int P = 1;
-  int st = upload_prompts(b, prompts, lens, stride, &P);
-  if (st != kOk) return st;
-  for (size_t g = 0; g < b->shard.size(); ++g) {
-    DevBatch& sh = *b->shard[g];
-    if (sh.S == 0) continue;
-    MC_CUDA(cudaSetDevice(sh.m->device));
-    if ((st = ensure_step_outputs(sh, false, n_new)) != kOk) return st;
-    MC_CUDA(cudaMemsetAsync(sh.step, 0, 4, sh.stream));
-    const uint32_t s0 = session0 + (uint32_t)b->first[g];
-    if ((st = enqueue_forward(sh, P, mode, inv_t, s0, false, true)) != kOk) return st;
-    if ((st = run_decode_steps(sh, n_new, mode, inv_t, s0)) != kOk) return st;
-  }
-  for (size_t g = 0; g < b->shard.size(); ++g) {
-    DevBatch& sh = *b->shard[g];
-    if (sh.S == 0) continue;
-    MC_CUDA(cudaSetDevice(sh.m->device));
-    // out columns are laid out with stride sh.out_stride >= n_new: the first n_new of each
-    // session's row go straight to the caller's rows of this shard's sessions
-    const size_t row0 = (size_t)b->first[g] * n_new;
-    MC_CUDA(cudaMemcpy2DAsync(out_tokens + row0, (size_t)n_new * 4, sh.out_tok, (size_t)sh.out_stride * 4,
-                              (size_t)n_new * 4, sh.S, cudaMemcpyDeviceToHost, sh.stream));
-    if (out_probs)
-      MC_CUDA(cudaMemcpy2DAsync(out_probs + row0, (size_t)n_new * 4, sh.out_prob, (size_t)sh.out_stride * 4,
-                                (size_t)n_new * 4, sh.S, cudaMemcpyDeviceToHost, sh.stream));
-  }
-  for (size_t g = 0; g < b->shard.size(); ++g) {
-    DevBatch& sh = *b->shard[g];
-    if (sh.S == 0) continue;
-    MC_CUDA(cudaSetDevice(sh.m->device));
-    if ((st = check_device_error(sh.stream)) != kOk) return st;
-  }
-  return kOk;
+  return generate_impl(b, prompts, lens, stride, n_new, temperature, session0, nullptr, 0, out_tokens, out_probs, nullptr);
+}
+
+int mc_generate_stops(mc_batch* b, const int32_t* prompts, const int32_t* lens, int stride, int n_new,
+                      double temperature, uint32_t session0, const int32_t* stops, int n_stops, int32_t* out_tokens,
+                      float* out_probs, int32_t* out_lens) {
+  clear_error();
+  if (n_stops < 0 || n_stops > kMaxStops || (n_stops > 0 && !stops))
+    return set_error(kInvalidArgument, "mc_generate_stops: 0 to 8 stop tokens");
+  return generate_impl(b, prompts, lens, stride, n_new, temperature, session0, stops, n_stops, out_tokens, out_probs,
+                       out_lens);
 }
 
 int mc_batch_stream(mc_batch* b, int shard, void** stream) {

@@ -772,10 +772,16 @@ __device__ __forceinline__ void decode_block(const BlockArgs& a, const DecodeLay
         int i = bars->red_i[0][t];
         for (int q = 1; q < 4; ++q) combine(m, sm, i, bars->red_m[q][t], bars->red_s[q][t], bars->red_i[q][t]);
         const int s = s0 + t;
-        a.next_tok[s] = i;
-        if (a.out_tok) a.out_tok[(size_t)s * a.out_stride + step] = i;
-        if (a.out_prob) a.out_prob[(size_t)s * a.out_stride + step] = __fdiv_rn(1.0f, sm);
-        a.pos_w[s] = bars->pos[t] + 1;
+        bool stop = false;
+        for (int k = 0; k < a.n_stops; ++k) stop |= i == a.stops[k];
+        if (stop) {
+          a.seglen_w[s] = 0;  // greedyLoop ends before a stop token (generate/greedy.go:75-77)
+        } else {
+          a.next_tok[s] = i;
+          if (a.out_tok) a.out_tok[(size_t)s * a.out_stride + step] = i;
+          if (a.out_prob) a.out_prob[(size_t)s * a.out_stride + step] = __fdiv_rn(1.0f, sm);
+          a.pos_w[s] = bars->pos[t] + 1;
+        }
       }
       // the last CTA to finish advances the step counter (every CTA has read it by then)
       row_bar_d();

@@ -14,6 +14,7 @@ constexpr int kBStages = 4;                // weight-tile ring
 constexpr int kNC = 128;                   // output columns per chunk (MMA N)
 constexpr int kMaxSteps = 8;
 constexpr int kMaxGemms = 2 + 3 * kMaxSteps;
+constexpr int kMaxStops = 8;               // stop tokens of a generation
 constexpr int kHalfChunk = 64;             // paired chunks: 64 value/delta + 64 gate columns
 
 // Pre-tiled weight image (built at model load): for output chunk c and K tile kt, a 16 KB tile
@@ -86,6 +87,9 @@ struct BlockArgs {
   int32_t* pos_w;       // [S] positions, advanced by one
   int32_t* step;        // device step counter (output column)
   int32_t* done;        // finished-CTA counter (zero between launches)
+  int n_stops;          // a chosen token among stops ends its session (seglen_w = 0, no output)
+  int stops[kMaxStops];
+  int32_t* seglen_w;
 };
 
 // sigmoidClamped (internal/quant/stream.go:128-136): saturated beyond |x| > 15, else 1/(1+e^-x)

@@ -261,6 +261,8 @@ struct DevBatch {
   cudaStream_t stream = nullptr;
   std::vector<void*> allocs;
   int32_t* sel_done = nullptr;  // select_kernel's finished-block counter (zero between launches)
+  int n_stops = 0;              // stop tokens of the generation being enqueued (0: none)
+  int stops[kMaxStops] = {0};
   uint8_t* a_cache = nullptr;    // block kernel: per-SM digit-plane cache of GEMMs wider than the A slots
   int a_cache_kt = 0;
   int32_t *pos = nullptr, *seglen = nullptr, *tok = nullptr, *next_tok = nullptr, *step = nullptr, *rowmap = nullptr,
@@ -295,7 +297,12 @@ struct DevBatch {
     uint32_t session0 = 0;
     const void* out_tok = nullptr;
     const void* logits_buf = nullptr;
+    int n_stops = 0;
+    int stops[kMaxStops] = {0};
     bool operator==(const GraphKey& o) const {
+      if (n_stops != o.n_stops) return false;
+      for (int k = 0; k < n_stops; ++k)
+        if (stops[k] != o.stops[k]) return false;
       return mode == o.mode && logits == o.logits && stride == o.stride && inv_t == o.inv_t && session0 == o.session0 &&
              out_tok == o.out_tok && logits_buf == o.logits_buf;
     }
@@ -576,6 +583,9 @@ static void build_block_args(const DevBatch& b, int P, int bi, bool fuse_head, i
       a.pos_w = b.pos;
       a.step = b.step;
       a.done = b.sel_done;
+      a.n_stops = b.n_stops;
+      for (int k = 0; k < b.n_stops; ++k) a.stops[k] = b.stops[k];
+      a.seglen_w = b.seglen;
     }
   }
   a.ngemms = g;
@@ -741,6 +751,8 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
   sa.seglen = b.seglen;
   sa.advance_from_len = advance_from_len ? 1 : 0;
   sa.done = b.sel_done;  // the last block advances the step counter
+  sa.n_stops = b.n_stops;
+  for (int k = 0; k < b.n_stops; ++k) sa.stops[k] = b.stops[k];
   select_kernel<<<(b.S + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, s>>>(sa);
   MC_CUDA(cudaGetLastError());
   if (log) log->record(s, 4);

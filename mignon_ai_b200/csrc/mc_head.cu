@@ -256,6 +256,8 @@ struct SelectArgs {
   int32_t* seglen;                 // [S] set to 1 for the next decode step when advancing
   int advance_from_len;            // 1: pos = pos0 + seglen (after a prefill); 0: pos += 1
   int32_t* done;                   // finished-block counter (zero between launches); null: no step bump
+  int n_stops;                     // a chosen token among stops[0..n_stops) ends the session: no output,
+  int stops[kMaxStops];            // seglen = 0 (greedyLoop's stop tokens, generate/greedy.go:75-77)
 };
 
 __device__ __forceinline__ void philox4x32_10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0,
@@ -379,7 +381,10 @@ __global__ void __launch_bounds__(kSelectWarps * 32) select_kernel(const SelectA
         }
       }
     }
-    if (lane == 0) {
+    bool stop = false;
+    for (int k = 0; k < a.n_stops; ++k) stop |= tok == a.stops[k];
+    if (lane == 0 && stop) a.seglen[s] = 0;  // the session ends before the stop token
+    if (lane == 0 && !stop) {
       a.next_tok[s] = tok;
       if (a.out_tok) a.out_tok[(size_t)s * a.out_stride + step] = tok;
       if (a.out_prob) a.out_prob[(size_t)s * a.out_stride + step] = (float)(1.0 / S);

@@ -36,6 +36,7 @@ _lib.register({
     "mc_score_targets": [c_vp, c_vp, c_vp, _i, c_vp, c_vp],
     "mc_append": [c_vp, c_vp, c_vp, c_vp, c_vp],
     "mc_generate": [c_vp, c_vp, c_vp, _i, _i, ctypes.c_double, ctypes.c_uint32, c_vp, c_vp],
+    "mc_generate_stops": [c_vp, c_vp, c_vp, _i, _i, ctypes.c_double, ctypes.c_uint32, c_vp, _i, c_vp, c_vp, c_vp],
 })
 
 
@@ -199,14 +200,25 @@ class SessionBatch:
                                                _lib.ptr(out)))
         return out
 
-    def generate(self, prompts, lens, n_new: int, temperature: float = 0.0, session0: int = 0):
+    def generate(self, prompts, lens, n_new: int, temperature: float = 0.0, session0: int = 0, stops=None):
+        """n_new tokens per session after its prompt (greedy, or sampled with temperature > 0):
+        (tokens, probs). With stops (at most 8 token ids): each session ends before the first stop
+        token it would emit, as greedyLoop does (generate/greedy.go:63-87); returns (tokens, probs,
+        lengths) with -1 / 0 past each session's length."""
         p = np.ascontiguousarray(prompts, np.int32)
         lens = np.ascontiguousarray(lens, np.int32)
         toks = np.zeros((self.count, n_new), np.int32)
         probs = np.zeros((self.count, n_new), np.float32)
-        _lib.check(_lib.lib().mc_generate(self._h, _lib.ptr(p), _lib.ptr(lens), p.shape[1], n_new, temperature,
-                                          session0, _lib.ptr(toks), _lib.ptr(probs)))
-        return toks, probs
+        if stops is None:
+            _lib.check(_lib.lib().mc_generate(self._h, _lib.ptr(p), _lib.ptr(lens), p.shape[1], n_new, temperature,
+                                              session0, _lib.ptr(toks), _lib.ptr(probs)))
+            return toks, probs
+        st = np.ascontiguousarray(list(stops), np.int32)
+        out_lens = np.zeros(self.count, np.int32)
+        _lib.check(_lib.lib().mc_generate_stops(self._h, _lib.ptr(p), _lib.ptr(lens), p.shape[1], n_new, temperature,
+                                                session0, _lib.ptr(st) if st.size else None, int(st.size),
+                                                _lib.ptr(toks), _lib.ptr(probs), _lib.ptr(out_lens)))
+        return toks, probs, out_lens
 
 
 class Session:

@@ -151,6 +151,42 @@ def test_one_token_prompts_match_oracle(oracle):
     b.close()
 
 
+def test_generate_stops_end_sessions_before_the_stop_token():
+    """mc_generate_stops: greedyLoop's stop tokens (generate/greedy.go:63-87). A session ends
+    before the first stop token it would emit, in the prefill's selection or in any decode step;
+    the others go on unchanged. Sessions never interact and the stopped ones take no further
+    steps, so every row equals the run without stops up to its first stop token, then -1 / 0, and
+    its length is that position. Stops apply to one call only."""
+    spec = small_spec(2, vocab=512)
+    gm = quant.Model.decode(synth.build_model_file(spec))
+    n, n_new = 200, 24
+    prompts = synth.prompts_uniform_fast(n, 48, spec.vocab, seed=23)
+    lens = synth.prompt_lengths(n, 1, 48, seed=23)
+    lens[3] = 0
+    act = lens > 0
+    b = gm.new_batch(n, 0, 48)
+    t0, p0 = b.generate(prompts, lens, n_new)
+    vals, counts = np.unique(t0[act], return_counts=True)
+    stops = vals[np.argsort(-counts, kind="stable")[:2]]
+    t1, p1, got_len = b.generate(prompts, lens, n_new, stops=stops)
+    stopped = 0
+    for s in range(n):
+        if not act[s]:
+            assert got_len[s] == 0 and np.all(t1[s] == -1)
+            continue
+        hit = np.nonzero(np.isin(t0[s], stops))[0]
+        k = int(hit[0]) if hit.size else n_new
+        stopped += k < n_new
+        assert got_len[s] == k, (s, got_len[s], k)
+        assert np.array_equal(t1[s, :k], t0[s, :k]) and np.all(t1[s, k:] == -1)
+        assert np.array_equal(p1[s, :k], p0[s, :k]) and np.all(p1[s, k:] == 0)
+    assert stopped > 0
+    t2, _ = b.generate(prompts, lens, n_new)
+    assert np.array_equal(t2[act], t0[act])
+    b.close()
+    gm.close()
+
+
 def test_ragged_prompts_and_idle_sessions(oracle):
     """Prompts of different lengths in one batch; a zero-length prompt leaves its session idle."""
     spec = small_spec(2, vocab=512)
