@@ -733,12 +733,14 @@ __device__ __forceinline__ void decode_block(const BlockArgs& a, const DecodeLay
 #pragma unroll
         for (int j = 0; j < kDCols; ++j) {
           const float l = __fadd_rn(dequant(x1[j], x2[j], x3[j], stp[j], scale), pv.x);
+          // the probability's sum of exponentials takes the fast exp (ex2 of x log2 e, a few ulp):
+          // the selection itself is exact, and the probability stays far inside its 1e-4 bar
           if (l > hm[j]) {  // channels arrive in increasing order: ties keep the first index
-            hs[j] = __fmul_rn(hs[j], expf(hm[j] - l));
+            hs[j] = __fmul_rn(hs[j], __expf(hm[j] - l));
             hm[j] = l;
             hi[j] = v;
           }
-          hs[j] = __fadd_rn(hs[j], expf(l - hm[j]));
+          hs[j] = __fadd_rn(hs[j], __expf(l - hm[j]));
         }
       });
       // combine over the 32 channels of the warp, then over the four quadrant warps
