@@ -93,13 +93,14 @@ struct BlockArgs {
 };
 
 // sigmoidClamped (internal/quant/stream.go:128-136): saturated beyond |x| > 15, else 1/(1+e^-x)
-// with float32 add and divide. The reference rounds a float64 exp to float32; here the exp is the
-// fast form (ex2 of x log2 e): for |x| <= 15 within 1e-6 relative of it, far inside the logit
-// tolerance, and a third of expf's instructions in epilogues that are bound by their count.
+// with float32 add and divide. The reference rounds a float64 exp to float32 and divides exactly;
+// here the exp is the fast form (ex2 of x log2 e) and the divide the fast reciprocal: for
+// |x| <= 15 within 2e-6 relative of it, far inside the logit tolerance, and a fraction of the
+// instructions in epilogues that are bound by their count.
 __device__ __forceinline__ float sigmoid_clamped(float x) {
   if (x > 15.0f) return 1.0f;
   if (x < -15.0f) return 0.0f;
-  return __frcp_rn(__fadd_rn(1.0f, __expf(-x)));  // correctly rounded, as 1/x
+  return __fdividef(1.0f, __fadd_rn(1.0f, __expf(-x)));
 }
 
 // Three slice accumulators recombined in float32: a1 + (a2 + a3/254)/254 (two fused steps).
