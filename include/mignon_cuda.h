@@ -151,6 +151,45 @@ int mc_generate_stops(mc_batch* batch, const int32_t* prompts, const int32_t* le
                       double temperature, uint32_t session0, const int32_t* stops, int n_stops, int32_t* out_tokens,
                       float* out_probs, int32_t* out_lens);
 
+/* The knobs of generate.Sampling (internal/generate/chat.go:45-56) for the policy calls below. */
+typedef struct {
+  double temperature; /* <= 0.001: argmax (sample.go:71-82) */
+  double rep_penalty; /* > 1: each distinct token of the window is divided (logit > 0) or multiplied by it */
+  int top_k;          /* <= 0: off */
+  double top_p;       /* in (0, 1): nucleus cutoff; otherwise off */
+  int rep_window;     /* trailing tokens the penalty sees (sampleContinuation: ChatRepetitionWindow = 6,
+                         generate/constants.go:11); <= 0: all */
+  int ban_trigrams;   /* non-zero: sampleContinuation's 3-gram repetition block (sample.go:213-227) */
+} mc_sampling;
+
+/* sampleContinuation (internal/generate/sample.go:196-247) for every session: prefill the prompt,
+ * then up to n_new tokens, each chosen on the device by the whole policy — 3-gram block,
+ * constraint mask, repetition penalty over the last rep_window tokens of (the prompt when
+ * penalize_prompt, chat.go:72; else nothing, chat.go:122) ++ the generated tokens, then
+ * SampleRawLogitsAdvanced (sample.go:33-172) with temperature, top-k, top-p and the draw of
+ * sampleFromCDF (:174-191) from Philox4x32-10 keyed like mc_generate. The constraint
+ * (Constraint.Mask / Advance, chat.go:58-62) is a token automaton: dfa[state * vocab + token] is
+ * the next state, or -1 for a token that is not allowed (its logit becomes -1e300 like
+ * constrain/grammar.go:259); dfa_start[s] is session s's start state (< 0: unconstrained);
+ * dfa == NULL: no constraint. Stop tokens (<= 8) end a session before it would emit one. Writes
+ * out_tokens [count x n_new] (-1 after a session ended), out_probs (the chosen token's
+ * probability in the distribution it was drawn from) and out_lens (tokens emitted) when non-null.
+ * Vocabulary <= 16384. */
+int mc_generate_policy(mc_batch* batch, const int32_t* prompts, const int32_t* lens, int stride, int n_new,
+                       const mc_sampling* sampling, int penalize_prompt, const int32_t* dfa, int n_states,
+                       const int32_t* dfa_start, uint32_t session0, const int32_t* stops, int n_stops,
+                       int32_t* out_tokens, float* out_probs, int32_t* out_lens);
+
+/* SampleRawLogitsAdvanced (internal/generate/sample.go:33-172) over n rows of float32 logits
+ * [n x vocab] on one device. recent (row stride recent_stride, recent_lens[r] tokens; NULL: none)
+ * are row r's recent tokens: the penalty sees their last rep_window, and with ban_trigrams they are
+ * the generated tokens the 3-gram block scans. allowed [n x vocab] (NULL: none) masks token t of
+ * row r when allowed[r * vocab + t] < 0. u [n] are the uniform draws in [0, 1) (NULL: Philox of
+ * (session0 + r, step)). Writes out_tokens [n] and, if non-null, out_probs [n]. Vocabulary <= 16384. */
+int mc_sample_rows(int device, const float* logits, int n, int vocab, const int32_t* recent, const int32_t* recent_lens,
+                   int recent_stride, const int32_t* allowed, const mc_sampling* sampling, const double* u,
+                   uint32_t session0, uint32_t step, int32_t* out_tokens, float* out_probs);
+
 /* mc_generate with device-resident inputs and outputs on a single-device batch: enqueues the
  * whole job on the batch's stream (mc_batch_stream) and returns without synchronizing.
  * pmax >= every lens[s]. Check completion and device errors with mc_batch_error. */

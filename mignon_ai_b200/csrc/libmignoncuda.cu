@@ -7,5 +7,6 @@
 #include "mc_block_decode.cu"
 #include "mc_attn.cu"
 #include "mc_head.cu"
+#include "mc_policy.cu"
 #include "mc_engine_host.cu"
 #include "mc_api.cu"

@@ -1,5 +1,6 @@
 // C-ABI entry points of libmignoncuda (include/mignon_cuda.h).
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -163,6 +164,7 @@ int run_graph_step(DevBatch& sh, int mode, double inv_temp, uint32_t session0, b
   key.logits_buf = sh.logits;
   key.n_stops = sh.n_stops;
   for (int k = 0; k < sh.n_stops; ++k) key.stops[k] = sh.stops[k];
+  key.pol = sh.pol;
   if (!sh.graph || !(sh.graph_key == key)) {
     if (sh.graph) {
       cudaGraphExecDestroy(sh.graph);
@@ -260,36 +262,121 @@ int score_impl(mc_batch* b, const int32_t* seqs, const int32_t* lens, int stride
   return kOk;
 }
 
+// The decode-loop policy of mc_generate_policy as the caller gave it.
+struct PolicyIn {
+  const mc_sampling* sp;
+  int penalize_prompt;
+  const int32_t* dfa;
+  int n_states;
+  const int32_t* dfa_start;
+};
+
+// Checks a policy and uploads what its launches read into one shard: the penalty prefix of each
+// of the shard's sessions (the last tokens of its untrimmed prompt), the automaton and the
+// sessions' start states. The automaton is checked entry by entry: the kernel follows it
+// unchecked.
+int upload_policy(mc_batch* b, size_t g, const PolicyIn& pi, const int32_t* prompts, const int32_t* lens, int stride) {
+  DevBatch& sh = *b->shard[g];
+  const int V = sh.m->V, s0 = b->first[g];
+  const mc_sampling& sp = *pi.sp;
+  int keep = 0;
+  if (pi.penalize_prompt && sp.rep_penalty > 1.0)
+    for (int i = 0; i < sh.S; ++i) {
+      const int n = sp.rep_window > 0 ? std::min(sp.rep_window, lens[s0 + i]) : lens[s0 + i];
+      keep = std::max(keep, n);
+    }
+  int st;
+  if (keep > sh.pol_prefix_cap) {
+    if ((st = sh.alloc(sh.pol_prefix, (size_t)sh.S * keep * 4)) != kOk) return st;
+    sh.pol_prefix_cap = keep;
+  }
+  if (!sh.pol_prefix_len && ((st = sh.alloc(sh.pol_prefix_len, (size_t)sh.S * 4)) != kOk ||
+                             (st = sh.alloc(sh.pol_state, (size_t)sh.S * 4)) != kOk))
+    return st;
+  std::vector<int32_t> plen(sh.S, 0);
+  if (keep > 0) {
+    std::vector<int32_t> pre((size_t)sh.S * sh.pol_prefix_cap, 0);
+    for (int i = 0; i < sh.S; ++i) {
+      const int len = lens[s0 + i], n = std::min(keep, len);
+      const int32_t* src = prompts + (size_t)(s0 + i) * stride + (len - n);
+      std::copy(src, src + n, pre.begin() + (size_t)i * sh.pol_prefix_cap);
+      plen[i] = n;
+    }
+    MC_CUDA(cudaMemcpyAsync(sh.pol_prefix, pre.data(), pre.size() * 4, cudaMemcpyHostToDevice, sh.stream));
+  }
+  MC_CUDA(cudaMemcpyAsync(sh.pol_prefix_len, plen.data(), plen.size() * 4, cudaMemcpyHostToDevice, sh.stream));
+  sh.pol = DevBatch::Policy();
+  sh.pol.temperature = sp.temperature;
+  sh.pol.rep_penalty = sp.rep_penalty;
+  sh.pol.top_p = sp.top_p;
+  sh.pol.top_k = sp.top_k;
+  sh.pol.rep_window = sp.rep_window;
+  sh.pol.ban_trigrams = sp.ban_trigrams ? 1 : 0;
+  if (pi.dfa) {
+    const size_t n = (size_t)pi.n_states * V;
+    if (n > sh.pol_dfa_n) {
+      if ((st = sh.alloc(sh.pol_dfa, n * 4)) != kOk) return st;
+      sh.pol_dfa_n = n;
+    }
+    MC_CUDA(cudaMemcpyAsync(sh.pol_dfa, pi.dfa, n * 4, cudaMemcpyHostToDevice, sh.stream));
+    MC_CUDA(cudaMemcpyAsync(sh.pol_state, pi.dfa_start + s0, (size_t)sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    sh.pol.dfa = sh.pol_dfa;
+  }
+  // pageable sources: the copies above have read them before returning
+  return kOk;
+}
+
+int check_policy(const mc_sampling* sp, const PolicyIn* pi, int V, int count) {
+  if (!sp) return set_error(kInvalidArgument, "sampling policy: null parameters");
+  if (!std::isfinite(sp->temperature) || !std::isfinite(sp->rep_penalty) || !std::isfinite(sp->top_p))
+    return set_error(kInvalidArgument, "sampling policy: non-finite parameter");
+  if (V > kPolicyMaxVocab) return set_error(kUnsupported, "sampling policy: vocabulary above 16384");
+  if (pi && pi->dfa) {
+    if (pi->n_states < 1 || !pi->dfa_start) return set_error(kInvalidArgument, "sampling policy: automaton without states");
+    const size_t n = (size_t)pi->n_states * V;
+    for (size_t i = 0; i < n; ++i)
+      if (pi->dfa[i] < -1 || pi->dfa[i] >= pi->n_states)
+        return set_error(kInvalidArgument, "sampling policy: automaton entry outside [-1, n_states)");
+    for (int s = 0; s < count; ++s)
+      if (pi->dfa_start[s] >= pi->n_states) return set_error(kInvalidArgument, "sampling policy: start state out of range");
+  }
+  return kOk;
+}
+
 // The decode loop of mc_generate / mc_generate_stops (greedyLoop, generate/greedy.go:63-87, with
 // stop tokens: a session ends before the first one it would emit; out_lens[s] = tokens emitted,
-// the rest of its row -1).
+// the rest of its row -1), and with a policy that of mc_generate_policy (sampleContinuation,
+// generate/sample.go:196-247).
 int generate_impl(mc_batch* b, const int32_t* prompts, const int32_t* lens, int stride, int n_new, double temperature,
                   uint32_t session0, const int32_t* stops, int n_stops, int32_t* out_tokens, float* out_probs,
-                  int32_t* out_lens) {
+                  int32_t* out_lens, const PolicyIn* pol = nullptr) {
   if (!b || !prompts || !lens || !out_tokens || n_new <= 0) return set_error(kInvalidArgument, "mc_generate: bad arguments");
-  const int mode = temperature > 0.001 ? 1 : 0;
+  const int mode = pol ? 3 : temperature > 0.001 ? 1 : 0;
   if (mode == 1 && b->topk < 1)
     return set_error(kUnsupported, "mc_generate: sampling needs a batch opened with top_k in [1, 64]");
-  const double inv_t = temperature > 0.001 ? 1.0 / temperature : 0.0;
+  const double inv_t = mode == 1 ? 1.0 / temperature : 0.0;
+  int st;
+  if (pol && (st = check_policy(pol->sp, pol, b->model->dev[0]->V, b->count)) != kOk) return st;
   int P = 1;
-  int st = upload_prompts(b, prompts, lens, stride, &P);
-  if (st != kOk) return st;
+  if ((st = upload_prompts(b, prompts, lens, stride, &P)) != kOk) return st;
   for (size_t g = 0; g < b->shard.size(); ++g) {
     DevBatch& sh = *b->shard[g];
     if (sh.S == 0) continue;
     MC_CUDA(cudaSetDevice(sh.m->device));
-    if ((st = ensure_step_outputs(sh, false, n_new)) != kOk) return st;
+    if ((st = ensure_step_outputs(sh, mode == 3, n_new)) != kOk) return st;
+    if (pol && (st = upload_policy(b, g, *pol, prompts, lens, stride)) != kOk) return st;
     MC_CUDA(cudaMemsetAsync(sh.step, 0, 4, sh.stream));
     sh.n_stops = n_stops;
     for (int k = 0; k < n_stops; ++k) sh.stops[k] = stops[k];
-    if (n_stops > 0) {  // sessions that end early leave their remaining columns at -1 / 0
+    if (n_stops > 0 || mode == 3) {  // sessions that end early leave their remaining columns at -1 / 0
       MC_CUDA(cudaMemsetAsync(sh.out_tok, 0xFF, (size_t)sh.S * sh.out_stride * 4, sh.stream));
       MC_CUDA(cudaMemsetAsync(sh.out_prob, 0, (size_t)sh.S * sh.out_stride * 4, sh.stream));
     }
     const uint32_t s0 = session0 + (uint32_t)b->first[g];
     st = enqueue_forward(sh, P, mode, inv_t, s0, false, true);
     if (st == kOk) st = run_decode_steps(sh, n_new, mode, inv_t, s0);
-    sh.n_stops = 0;  // only this job's launches carry the stop tokens
+    sh.n_stops = 0;  // only this job's launches carry the stop tokens and the policy
+    sh.pol = DevBatch::Policy();
     if (st != kOk) return st;
   }
   for (size_t g = 0; g < b->shard.size(); ++g) {
@@ -508,6 +595,98 @@ int mc_generate_stops(mc_batch* b, const int32_t* prompts, const int32_t* lens, 
     return set_error(kInvalidArgument, "mc_generate_stops: 0 to 8 stop tokens");
   return generate_impl(b, prompts, lens, stride, n_new, temperature, session0, stops, n_stops, out_tokens, out_probs,
                        out_lens);
+}
+
+int mc_generate_policy(mc_batch* b, const int32_t* prompts, const int32_t* lens, int stride, int n_new,
+                       const mc_sampling* sp, int penalize_prompt, const int32_t* dfa, int n_states,
+                       const int32_t* dfa_start, uint32_t session0, const int32_t* stops, int n_stops,
+                       int32_t* out_tokens, float* out_probs, int32_t* out_lens) {
+  clear_error();
+  if (n_stops < 0 || n_stops > kMaxStops || (n_stops > 0 && !stops))
+    return set_error(kInvalidArgument, "mc_generate_policy: 0 to 8 stop tokens");
+  if (!sp) return set_error(kInvalidArgument, "mc_generate_policy: null sampling parameters");
+  const PolicyIn pi{sp, penalize_prompt, dfa, n_states, dfa_start};
+  return generate_impl(b, prompts, lens, stride, n_new, 0.0, session0, stops, n_stops, out_tokens, out_probs, out_lens,
+                       &pi);
+}
+
+int mc_sample_rows(int device, const float* logits, int n, int vocab, const int32_t* recent, const int32_t* recent_lens,
+                   int recent_stride, const int32_t* allowed, const mc_sampling* sp, const double* u, uint32_t session0,
+                   uint32_t step, int32_t* out_tokens, float* out_probs) {
+  clear_error();
+  if (n < 0 || vocab < 1 || !logits || !out_tokens || (recent && (!recent_lens || recent_stride < 0)))
+    return set_error(kInvalidArgument, "mc_sample_rows: bad arguments");
+  int st = check_policy(sp, nullptr, vocab, n);
+  if (st != kOk) return st;
+  if (recent)
+    for (int r = 0; r < n; ++r)
+      if (recent_lens[r] < 0 || recent_lens[r] > recent_stride)
+        return set_error(kInvalidArgument, "mc_sample_rows: recent length outside [0, recent_stride]");
+  if (n == 0) return kOk;
+  MC_CUDA(cudaSetDevice(device));
+  if ((st = ensure_attrs(device)) != kOk) return st;
+  // one allocation: logits | allowed | recent | recent lengths | states | draws | tokens | probs
+  const size_t nl = (size_t)n * vocab, nr = recent ? (size_t)n * std::max(recent_stride, 1) : 0;
+  const size_t bytes = nl * 4 + (allowed ? nl * 4 : 0) + nr * 4 + (size_t)n * (4 + 4 + 8 + 4 + 4) + 64;
+  DevBuf buf;
+  if (cudaMalloc(&buf.p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(kOutOfMemory, "mc_sample_rows: cudaMalloc failed");
+  }
+  char* q = static_cast<char*>(buf.p);
+  auto take = [&](size_t nb) {
+    char* r = q;
+    q += (nb + 15) & ~(size_t)15;
+    return r;
+  };
+  float* d_logits = reinterpret_cast<float*>(take(nl * 4));
+  int32_t* d_allowed = allowed ? reinterpret_cast<int32_t*>(take(nl * 4)) : nullptr;
+  int32_t* d_recent = recent ? reinterpret_cast<int32_t*>(take(nr * 4)) : nullptr;
+  int32_t* d_rlen = reinterpret_cast<int32_t*>(take((size_t)n * 4));
+  int32_t* d_state = reinterpret_cast<int32_t*>(take((size_t)n * 4));
+  double* d_u = reinterpret_cast<double*>(take((size_t)n * 8));
+  int32_t* d_tok = reinterpret_cast<int32_t*>(take((size_t)n * 4));
+  float* d_prob = reinterpret_cast<float*>(take((size_t)n * 4));
+  cudaStream_t s = 0;
+  MC_CUDA(cudaMemcpyAsync(d_logits, logits, nl * 4, cudaMemcpyHostToDevice, s));
+  if (allowed) {
+    // row r's mask is state r of a one-step automaton
+    std::vector<int32_t> iota(n);
+    for (int r = 0; r < n; ++r) iota[r] = r;
+    MC_CUDA(cudaMemcpyAsync(d_allowed, allowed, nl * 4, cudaMemcpyHostToDevice, s));
+    MC_CUDA(cudaMemcpyAsync(d_state, iota.data(), (size_t)n * 4, cudaMemcpyHostToDevice, s));
+  }
+  if (recent) {
+    MC_CUDA(cudaMemcpyAsync(d_recent, recent, nr * 4, cudaMemcpyHostToDevice, s));
+    MC_CUDA(cudaMemcpyAsync(d_rlen, recent_lens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+  }
+  if (u) MC_CUDA(cudaMemcpyAsync(d_u, u, (size_t)n * 8, cudaMemcpyHostToDevice, s));
+  PolicyArgs pa;
+  memset(&pa, 0, sizeof(pa));
+  pa.n_rows = n;
+  pa.V = vocab;
+  pa.logits = d_logits;
+  pa.temperature = sp->temperature;
+  pa.rep_penalty = sp->rep_penalty;
+  pa.top_p = sp->top_p;
+  pa.top_k = sp->top_k;
+  pa.rep_window = sp->rep_window;
+  pa.ban_trigrams = sp->ban_trigrams ? 1 : 0;
+  pa.gen = d_recent;
+  pa.gen_len = d_rlen;
+  pa.gen_stride = recent ? std::max(recent_stride, 1) : 0;
+  pa.dfa = d_allowed;
+  pa.dfa_state = allowed ? d_state : nullptr;
+  pa.u = u ? d_u : nullptr;
+  pa.session0 = session0;
+  pa.step0 = step;
+  pa.out_stride = 1;
+  pa.out_tok = d_tok;
+  pa.out_prob = d_prob;
+  if ((st = launch_policy(pa, s)) != kOk) return st;
+  MC_CUDA(cudaMemcpyAsync(out_tokens, d_tok, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+  if (out_probs) MC_CUDA(cudaMemcpyAsync(out_probs, d_prob, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+  return check_device_error(s);
 }
 
 int mc_batch_stream(mc_batch* b, int shard, void** stream) {

@@ -257,9 +257,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
     asm volatile("mov.u32 %0, %%smid;" : "=r"(id));
     if (a.a_cache && (int)id < a.a_cache_sms) acache = a.a_cache + (size_t)id * a.a_cache_kt * kASlot;
   }
-  // the cache serves GEMM G when it holds all of G's K tiles (instances without CACHE compile none
-  // of its code)
-  auto use_cache = [&](const GemmSpec& G) { return CACHE && acache != nullptr && G.ktiles <= a.a_cache_kt; };
+  // the cache serves GEMM G when it holds all of G's K tiles and G has chunks after the first
+  // (instances without CACHE compile none of its code)
+  auto use_cache = [&](const GemmSpec& G) {
+    return CACHE && acache != nullptr && G.ktiles <= a.a_cache_kt && G.nchunks > 1;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kASlots; ++i) {

@@ -263,6 +263,21 @@ struct DevBatch {
   int32_t* sel_done = nullptr;  // select_kernel's finished-block counter (zero between launches)
   int n_stops = 0;              // stop tokens of the generation being enqueued (0: none)
   int stops[kMaxStops] = {0};
+  // The decode-loop policy of mc_generate_policy (mode 3): the sampling knobs, each session's
+  // penalty prefix (its last pol_prefix_len[s] prompt tokens), and the token automaton with each
+  // session's state.
+  struct Policy {
+    double temperature = 0, rep_penalty = 1, top_p = 1;
+    int top_k = 0, rep_window = 0, ban_trigrams = 0;
+    const int32_t* dfa = nullptr;
+    bool operator==(const Policy& o) const {
+      return temperature == o.temperature && rep_penalty == o.rep_penalty && top_p == o.top_p && top_k == o.top_k &&
+             rep_window == o.rep_window && ban_trigrams == o.ban_trigrams && dfa == o.dfa;
+    }
+  } pol;
+  int32_t *pol_prefix = nullptr, *pol_prefix_len = nullptr, *pol_state = nullptr, *pol_dfa = nullptr;
+  int pol_prefix_cap = 0;  // tokens per session that pol_prefix holds
+  size_t pol_dfa_n = 0;    // entries pol_dfa holds
   uint8_t* a_cache = nullptr;    // block kernel: per-SM digit-plane cache of GEMMs wider than the A slots
   int a_cache_kt = 0;
   int32_t *pos = nullptr, *seglen = nullptr, *tok = nullptr, *next_tok = nullptr, *step = nullptr, *rowmap = nullptr,
@@ -299,8 +314,9 @@ struct DevBatch {
     const void* logits_buf = nullptr;
     int n_stops = 0;
     int stops[kMaxStops] = {0};
+    Policy pol;
     bool operator==(const GraphKey& o) const {
-      if (n_stops != o.n_stops) return false;
+      if (n_stops != o.n_stops || !(pol == o.pol)) return false;
       for (int k = 0; k < n_stops; ++k)
         if (stops[k] != o.stops[k]) return false;
       return mode == o.mode && logits == o.logits && stride == o.stride && inv_t == o.inv_t && session0 == o.session0 &&
@@ -353,6 +369,8 @@ static int ensure_attrs(int device) {
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<2, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<3, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem));
+  MC_CUDA(cudaFuncSetAttribute(policy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)policy_smem(kPolicyMaxVocab)));
   MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
   MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
   MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
@@ -722,7 +740,7 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
   h.head_b = m.head_b;
   h.topk = mode == 1 ? b.topk : 0;
   h.target = mode == 2 ? b.target : nullptr;
-  h.logits_out = want_logits ? b.logits : nullptr;
+  h.logits_out = want_logits || mode == 3 ? b.logits : nullptr;
   h.part = b.part;
   h.topv = b.topv;
   h.topi = b.topi;
@@ -730,6 +748,43 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
   head_kernel<<<hg, kHeadThreads, kHeadSmem, s>>>(h);
   MC_CUDA(cudaGetLastError());
   if (log) log->record(s, 3);
+  if (mode == 3) {
+    // the whole decode-loop policy over the materialised logits; the generated tokens so far are
+    // the first *step columns of out_tok
+    PolicyArgs pa;
+    memset(&pa, 0, sizeof(pa));
+    pa.n_rows = b.S;
+    pa.V = m.V;
+    pa.logits = b.logits;
+    pa.temperature = b.pol.temperature;
+    pa.rep_penalty = b.pol.rep_penalty;
+    pa.top_p = b.pol.top_p;
+    pa.top_k = b.pol.top_k;
+    pa.rep_window = b.pol.rep_window;
+    pa.ban_trigrams = b.pol.ban_trigrams;
+    pa.prefix = b.pol_prefix;
+    pa.prefix_len = b.pol_prefix_len;
+    pa.prefix_stride = b.pol_prefix_cap;
+    pa.gen = b.out_tok;
+    pa.gen_stride = b.out_stride;
+    pa.dfa = b.pol.dfa;
+    pa.dfa_state = b.pol.dfa ? b.pol_state : nullptr;
+    pa.session0 = session0;
+    pa.step = b.step;
+    pa.out_stride = b.out_stride;
+    pa.next_tok = b.next_tok;
+    pa.out_tok = b.out_tok;
+    pa.out_prob = b.out_prob;
+    pa.pos = b.pos;
+    pa.seglen = b.seglen;
+    pa.advance_from_len = advance_from_len ? 1 : 0;
+    pa.done = b.sel_done;
+    pa.n_stops = b.n_stops;
+    for (int k = 0; k < b.n_stops; ++k) pa.stops[k] = b.stops[k];
+    if ((st = launch_policy(pa, s)) != kOk) return st;
+    if (log) log->record(s, 4);
+    return kOk;
+  }
   SelectArgs sa;
   memset(&sa, 0, sizeof(sa));
   sa.n_sess = b.S;

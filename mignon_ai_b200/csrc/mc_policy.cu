@@ -1,0 +1,350 @@
+// Token selection with the whole decode-loop policy of sampleContinuation
+// (internal/generate/sample.go:196-247) over materialised logits, one CTA per row:
+//   1. the 3-gram repetition block (:213-227): a token that followed the trailing pair of the
+//      generated tokens earlier gets -MaxFloat64;
+//   2. Constraint.Mask (:229-231) as a token automaton: dfa[state][token] is the next state, -1
+//      for a token that is not allowed (it gets -1e300, like constrain/grammar.go:259);
+//   3. SampleRawLogitsAdvanced (:33-172): repetition penalty over the distinct tokens of the
+//      trailing window of prefix ++ generated, argmax at T <= 0.001, else temperature, softmax and
+//      either the draw in index order (no truncation) or the sort, top-k, top-p and
+//      sampleFromCDF (:174-191);
+//   4. stop tokens end the session before they are emitted (:233-237); Constraint.Advance (:238).
+// Arithmetic in double like the reference. The running sums are taken in per-thread chunks whose
+// totals are scanned across the block, so they differ from Go's left-to-right sums by rounding
+// only; a draw can change only when it lies within that rounding of a bucket edge.
+#include <cfloat>
+
+#include "mc_engine.cuh"
+
+namespace mc {
+namespace eng {
+
+constexpr int kPolicyThreads = 512;
+constexpr int kPolicyWarps = kPolicyThreads / 32;
+constexpr int kPolicyMaxVocab = 16384;  // the sort keys and indices of a row fill 192 KB of shared memory
+
+struct PolicyArgs {
+  int n_rows, V, vp;                  // vp: V rounded up to a power of two (the sort's size)
+  const float* logits;                // [n_rows][V]
+  double temperature, rep_penalty, top_p;
+  int top_k, rep_window, ban_trigrams;
+  const int32_t* prefix;              // [n_rows][prefix_stride]: penalty prefix, prefix_len[row] tokens (or null)
+  const int32_t* prefix_len;
+  int prefix_stride;
+  const int32_t* gen;                 // [n_rows][gen_stride]: generated tokens, gen_len[row] of them, or
+  const int32_t* gen_len;             // *step of them when gen_len is null; null: none
+  int gen_stride;
+  const int32_t* dfa;                 // [states][V]: next state, -1 = not allowed; null: no constraint
+  int32_t* dfa_state;                 // [n_rows] state of each row (< 0: unconstrained)
+  const double* u;                    // [n_rows] uniform draws, or null: Philox (session0 + row, step)
+  uint32_t session0;
+  int32_t* step;                      // device step counter (output column and draw counter), or null:
+  uint32_t step0;                     // column 0 and draw counter step0
+  int out_stride;
+  int32_t* next_tok;                  // [n_rows] or null
+  int32_t* out_tok;                   // [n_rows][out_stride]
+  float* out_prob;                    // [n_rows][out_stride] or null
+  int32_t* pos;                       // positions advanced like SelectArgs (null: no change)
+  int32_t* seglen;                    // [n_rows]: rows with seglen <= 0 have finished; null: all run
+  int advance_from_len;
+  int32_t* done;                      // finished-block counter; null: no step bump
+  int n_stops;
+  int stops[kMaxStops];
+};
+
+// Token k of the concatenation prefix ++ generated.
+__device__ __forceinline__ int32_t pol_hist(const int32_t* pre, int np, const int32_t* gen, int k) {
+  return k < np ? pre[k] : gen[k - np];
+}
+
+__device__ __forceinline__ bool pol_better(double v, int i, double bv, int bi) { return v > bv || (v == bv && i < bi); }
+
+// Block reductions (every thread gets the result); red_d / red_i hold one entry per warp.
+__device__ __forceinline__ double pol_block_sum(double v, double* red_d) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (lane == 0) red_d[warp] = v;
+  __syncthreads();
+  double s = 0.0;
+#pragma unroll
+  for (int w = 0; w < kPolicyWarps; ++w) s += red_d[w];
+  __syncthreads();
+  return s;
+}
+
+__device__ __forceinline__ double pol_block_max(double v, double* red_d) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (lane == 0) red_d[warp] = v;
+  __syncthreads();
+  double m = red_d[0];
+#pragma unroll
+  for (int w = 1; w < kPolicyWarps; ++w) m = fmax(m, red_d[w]);
+  __syncthreads();
+  return m;
+}
+
+__device__ __forceinline__ int pol_block_min(int v, int* red_i) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (lane == 0) red_i[warp] = v;
+  __syncthreads();
+  int m = red_i[0];
+#pragma unroll
+  for (int w = 1; w < kPolicyWarps; ++w) m = min(m, red_i[w]);
+  __syncthreads();
+  return m;
+}
+
+// First index of the largest value (argmax with the lowest index among equal maxima).
+__device__ __forceinline__ void pol_block_argmax(double& bv, int& bi, double* red_d, int* red_i) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (pol_better(ov, oi, bv, bi)) bv = ov, bi = oi;
+  }
+  if (lane == 0) red_d[warp] = bv, red_i[warp] = bi;
+  __syncthreads();
+  bv = red_d[0];
+  bi = red_i[0];
+#pragma unroll
+  for (int w = 1; w < kPolicyWarps; ++w)
+    if (pol_better(red_d[w], red_i[w], bv, bi)) bv = red_d[w], bi = red_i[w];
+  __syncthreads();
+}
+
+// Running sums of x[0..n): thread t owns the chunk [t*c, min(n, (t+1)*c)), c = ceil(n / threads);
+// returns the sum of the chunks before its own (an exclusive scan of the chunk totals).
+__device__ __forceinline__ double pol_chunk_base(const double* x, int n, int c, double* red_d) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lo = min(n, (int)threadIdx.x * c), hi = min(n, lo + c);
+  double s = 0.0;
+  for (int i = lo; i < hi; ++i) s += x[i];
+  double v = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double y = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += y;
+  }
+  if (lane == 31) red_d[warp] = v;
+  __syncthreads();
+  double base = 0.0;
+  for (int w = 0; w < warp; ++w) base += red_d[w];
+  __syncthreads();
+  return base + v - s;
+}
+
+// Walks this thread's chunk with the running sum from base: the block-wide first index whose
+// running sum is >= t (INT_MAX if none), and the running sum at index k into *at_k (shared).
+__device__ __forceinline__ int pol_first_at_least(const double* x, int n, int c, double base, double t, int k,
+                                                  double* at_k, int* red_i) {
+  const int lo = min(n, (int)threadIdx.x * c), hi = min(n, lo + c);
+  double cum = base;
+  int first = 0x7fffffff;
+  for (int i = lo; i < hi; ++i) {
+    cum += x[i];
+    if (first == 0x7fffffff && cum >= t) first = i;
+    if (i == k) *at_k = cum;
+  }
+  return pol_block_min(first, red_i);
+}
+
+__global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_constant__ PolicyArgs a) {
+  extern __shared__ __align__(16) unsigned char pol_smem[];
+  double* key = reinterpret_cast<double*>(pol_smem);
+  int32_t* idx = reinterpret_cast<int32_t*>(key + a.vp);
+  __shared__ double red_d[kPolicyWarps];
+  __shared__ int red_i[kPolicyWarps];
+  __shared__ double at_k;
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const int V = a.V;
+  const int step = a.step ? *a.step : (int)a.step0;
+  const bool live = !a.seglen || a.seglen[row] > 0;
+  if (live) {
+    const float* lg = a.logits + (size_t)row * V;
+    for (int i = tid; i < V; i += kPolicyThreads) key[i] = (double)lg[i];
+    const int ng = a.gen ? (a.gen_len ? a.gen_len[row] : step) : 0;
+    const int32_t* gen = a.gen ? a.gen + (size_t)row * a.gen_stride : nullptr;
+    const int np = a.prefix ? a.prefix_len[row] : 0;
+    const int32_t* pre = a.prefix ? a.prefix + (size_t)row * a.prefix_stride : nullptr;
+    __syncthreads();
+    // 1. 3-gram block
+    if (a.ban_trigrams && ng >= 2) {
+      const int32_t w1 = gen[ng - 2], w2 = gen[ng - 1];
+      for (int i = tid; i <= ng - 3; i += kPolicyThreads)
+        if (gen[i] == w1 && gen[i + 1] == w2 && gen[i + 2] >= 0 && gen[i + 2] < V) key[gen[i + 2]] = -DBL_MAX;
+    }
+    __syncthreads();
+    // 2. constraint mask
+    const int state = a.dfa && a.dfa_state ? a.dfa_state[row] : -1;
+    if (state >= 0) {
+      const int32_t* tr = a.dfa + (size_t)state * V;
+      for (int i = tid; i < V; i += kPolicyThreads)
+        if (tr[i] < 0) key[i] = -1e300;
+    }
+    __syncthreads();
+    // 3a. repetition penalty: each distinct in-range token of the window once
+    const int total = np + ng;
+    const int w = a.rep_window > 0 && a.rep_window < total ? a.rep_window : total;
+    if (a.rep_penalty > 1.0 && w > 0) {
+      for (int j = tid; j < w; j += kPolicyThreads) {
+        const int32_t tok = pol_hist(pre, np, gen, total - w + j);
+        if (tok < 0 || tok >= V) continue;
+        bool seen = false;
+        for (int k = 0; k < j && !seen; ++k) seen = pol_hist(pre, np, gen, total - w + k) == tok;
+        if (seen) continue;
+        const double v = key[tok];
+        key[tok] = v > 0 ? v / a.rep_penalty : v * a.rep_penalty;
+      }
+    }
+    __syncthreads();
+    int tok = 0;
+    double prob = 0.0;
+    if (a.temperature <= 0.001) {
+      // 3b. argmax; prob = 1 / sum exp(l - max)
+      double bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int i = tid; i < V; i += kPolicyThreads)
+        if (pol_better(key[i], i, bv, bi)) bv = key[i], bi = i;
+      pol_block_argmax(bv, bi, red_d, red_i);
+      double s = 0.0;
+      for (int i = tid; i < V; i += kPolicyThreads) s += exp(key[i] - bv);
+      s = pol_block_sum(s, red_d);
+      tok = bi;
+      prob = 1.0 / s;
+    } else {
+      // 3c. temperature and the shifted exponentials
+      const double inv_t = 1.0 / a.temperature;
+      double m = -DBL_MAX;
+      for (int i = tid; i < V; i += kPolicyThreads) {
+        const double v = key[i] * inv_t;
+        key[i] = v;
+        m = v > m ? v : m;
+      }
+      m = pol_block_max(m, red_d);
+      for (int i = tid; i < V; i += kPolicyThreads) key[i] = exp(key[i] - m);
+      __syncthreads();
+      if (a.top_k <= 0 && a.top_p >= 0.9999) {
+        // 3d. the draw in index order over every token
+        const int c = (V + kPolicyThreads - 1) / kPolicyThreads;
+        const double base = pol_chunk_base(key, V, c, red_d);
+        pol_first_at_least(key, V, c, base, INFINITY, V - 1, &at_k, red_i);
+        const double s = at_k;
+        const double u = a.u ? a.u[row] : sample_uniform(a.session0 + (uint32_t)row, (uint32_t)step);
+        const int k = pol_first_at_least(key, V, c, base, u * s, -1, &at_k, red_i);
+        tok = k == 0x7fffffff ? 0 : k;
+        prob = key[tok] / s;
+      } else {
+        // 3e. probabilities, sorted descending (ties by index)
+        double s = 0.0;
+        for (int i = tid; i < V; i += kPolicyThreads) s += key[i];
+        s = pol_block_sum(s, red_d);
+        const double inv = 1.0 / s;
+        for (int i = tid; i < a.vp; i += kPolicyThreads) {
+          if (i < V) {
+            key[i] *= inv;
+            idx[i] = i;
+          } else {
+            key[i] = -1.0;
+            idx[i] = 0x7fffffff;
+          }
+        }
+        __syncthreads();
+        for (int kk = 2; kk <= a.vp; kk <<= 1) {
+          for (int j = kk >> 1; j > 0; j >>= 1) {
+            for (int p = tid; p < (a.vp >> 1); p += kPolicyThreads) {
+              const int lo = ((p & ~(j - 1)) << 1) | (p & (j - 1)), hi = lo | j;
+              const bool up = (lo & kk) == 0;
+              const double kl = key[lo], kh = key[hi];
+              const int il = idx[lo], ih = idx[hi];
+              if (pol_better(kh, ih, kl, il) == up) {
+                key[lo] = kh;
+                key[hi] = kl;
+                idx[lo] = ih;
+                idx[hi] = il;
+              }
+            }
+            __syncthreads();
+          }
+        }
+        // 3f. top-k, then the shortest prefix whose mass reaches top-p, then the draw
+        int active = a.top_k > 0 && a.top_k < V ? a.top_k : V;
+        const int c = (active + kPolicyThreads - 1) / kPolicyThreads;
+        const double base = pol_chunk_base(key, active, c, red_d);
+        int cut = active;
+        if (a.top_p > 0.0 && a.top_p < 1.0) {
+          const int k = pol_first_at_least(key, active, c, base, a.top_p, -1, &at_k, red_i);
+          if (k != 0x7fffffff) cut = k + 1;
+        }
+        if (cut == 1) {
+          tok = idx[0];
+          prob = 1.0;
+        } else {
+          pol_first_at_least(key, active, c, base, INFINITY, cut - 1, &at_k, red_i);
+          const double sp = at_k;
+          const double u = a.u ? a.u[row] : sample_uniform(a.session0 + (uint32_t)row, (uint32_t)step);
+          int k = pol_first_at_least(key, active, c, base, u * sp, -1, &at_k, red_i);
+          if (k >= cut) k = cut - 1;
+          tok = idx[k];
+          prob = key[k] / sp;
+        }
+      }
+    }
+    // 4. stop tokens, outputs, position, constraint advance
+    if (tid == 0) {
+      bool stop = false;
+      for (int k = 0; k < a.n_stops; ++k) stop |= a.stops[k] >= 0 && tok == a.stops[k];
+      if (stop) {
+        if (a.seglen) a.seglen[row] = 0;
+      } else {
+        const int col = a.step ? step : 0;
+        if (a.next_tok) a.next_tok[row] = tok;
+        a.out_tok[(size_t)row * a.out_stride + col] = tok;
+        if (a.out_prob) a.out_prob[(size_t)row * a.out_stride + col] = (float)prob;
+        if (a.pos) {
+          if (a.advance_from_len) a.pos[row] = a.pos[row] + a.seglen[row];
+          else a.pos[row] = a.pos[row] + 1;
+          a.seglen[row] = 1;
+        }
+        if (state >= 0) a.dfa_state[row] = a.dfa[(size_t)state * V + tok];
+      }
+    }
+  }
+  if (a.done) {
+    // the last block to finish advances the step counter (every block has read it by then)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(a.done, 1) == (int)gridDim.x - 1) {
+        *a.step += 1;
+        *a.done = 0;
+        __threadfence();
+      }
+    }
+  }
+}
+
+inline int policy_vp(int V) {
+  int vp = 1;
+  while (vp < V) vp <<= 1;
+  return vp;
+}
+
+inline size_t policy_smem(int V) { return (size_t)policy_vp(V) * (sizeof(double) + sizeof(int32_t)); }
+
+int launch_policy(PolicyArgs& a, cudaStream_t s) {
+  if (a.V < 1 || a.V > kPolicyMaxVocab) return set_error(kUnsupported, "sampling policy: vocabulary above 16384");
+  a.vp = policy_vp(a.V);
+  const size_t smem = policy_smem(a.V);  // the kernel's shared-memory limit is raised once per device
+  if (a.n_rows > 0) policy_kernel<<<a.n_rows, kPolicyThreads, smem, s>>>(a);
+  MC_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+}  // namespace eng
+}  // namespace mc

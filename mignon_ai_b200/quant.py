@@ -37,7 +37,56 @@ _lib.register({
     "mc_append": [c_vp, c_vp, c_vp, c_vp, c_vp],
     "mc_generate": [c_vp, c_vp, c_vp, _i, _i, ctypes.c_double, ctypes.c_uint32, c_vp, c_vp],
     "mc_generate_stops": [c_vp, c_vp, c_vp, _i, _i, ctypes.c_double, ctypes.c_uint32, c_vp, _i, c_vp, c_vp, c_vp],
+    "mc_generate_policy": [c_vp, c_vp, c_vp, _i, _i, c_vp, _i, c_vp, _i, c_vp, ctypes.c_uint32, c_vp, _i, c_vp, c_vp,
+                           c_vp],
+    "mc_sample_rows": [_i, c_vp, _i, _i, c_vp, c_vp, _i, c_vp, c_vp, c_vp, ctypes.c_uint32, ctypes.c_uint32, c_vp,
+                       c_vp],
 })
+
+# sampleContinuation's repetition window (internal/generate/constants.go:11)
+CHAT_REPETITION_WINDOW = 6
+
+
+class Sampling(ctypes.Structure):
+    """mc_sampling: the knobs of generate.Sampling (internal/generate/chat.go:45-56).
+
+    ``temperature`` <= 0.001 is argmax; ``rep_penalty`` > 1 penalises the distinct tokens of the
+    last ``rep_window`` tokens (all when <= 0); ``top_k`` <= 0 and ``top_p`` outside (0, 1) are off;
+    ``ban_trigrams`` turns on sampleContinuation's 3-gram repetition block."""
+    _fields_ = [("temperature", ctypes.c_double), ("rep_penalty", ctypes.c_double), ("top_k", ctypes.c_int),
+                ("top_p", ctypes.c_double), ("rep_window", ctypes.c_int), ("ban_trigrams", ctypes.c_int)]
+
+    def __init__(self, temperature: float = 0.0, rep_penalty: float = 1.0, top_k: int = 0, top_p: float = 1.0,
+                 rep_window: int = CHAT_REPETITION_WINDOW, ban_trigrams: bool = True):
+        super().__init__(float(temperature), float(rep_penalty), int(top_k), float(top_p), int(rep_window),
+                         int(bool(ban_trigrams)))
+
+
+def sample_rows(logits, sampling: Sampling, recent=None, recent_lens=None, allowed=None, u=None, session0: int = 0,
+                step: int = 0, device: int = 0):
+    """SampleRawLogitsAdvanced (internal/generate/sample.go:33-172) over the rows of a float32
+    [n x vocab] logits array on one GPU: (tokens [n], probs [n]). ``recent`` [n x m] with
+    ``recent_lens`` are each row's recent tokens (the penalty window's source and, with
+    ``ban_trigrams``, the generated tokens of the 3-gram block); ``allowed`` [n x vocab] masks
+    tokens where < 0; ``u`` [n] are the uniform draws (default: Philox of (session0 + r, step))."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    if lg.ndim != 2:
+        raise ValueError("logits must be [n x vocab]")
+    n, V = lg.shape
+    rc = rl = None
+    stride = 0
+    if recent is not None:
+        rc = np.ascontiguousarray(recent, np.int32).reshape(n, -1)
+        stride = rc.shape[1]
+        rl = (np.full(n, stride, np.int32) if recent_lens is None else np.ascontiguousarray(recent_lens, np.int32))
+    al = np.ascontiguousarray(allowed, np.int32).reshape(n, V) if allowed is not None else None
+    uu = np.ascontiguousarray(u, np.float64) if u is not None else None
+    toks = np.zeros(n, np.int32)
+    probs = np.zeros(n, np.float32)
+    _lib.check(_lib.lib().mc_sample_rows(device, _lib.ptr(lg), n, V, _lib.ptr(rc), _lib.ptr(rl), stride,
+                                         _lib.ptr(al), ctypes.byref(sampling), _lib.ptr(uu), session0, step,
+                                         _lib.ptr(toks), _lib.ptr(probs)))
+    return toks, probs
 
 
 class _Options(ctypes.Structure):
@@ -218,6 +267,31 @@ class SessionBatch:
         _lib.check(_lib.lib().mc_generate_stops(self._h, _lib.ptr(p), _lib.ptr(lens), p.shape[1], n_new, temperature,
                                                 session0, _lib.ptr(st) if st.size else None, int(st.size),
                                                 _lib.ptr(toks), _lib.ptr(probs), _lib.ptr(out_lens)))
+        return toks, probs, out_lens
+
+    def generate_policy(self, prompts, lens, n_new: int, sampling: Sampling, penalize_prompt: bool = False,
+                        dfa=None, dfa_start=None, session0: int = 0, stops=()):
+        """sampleContinuation (internal/generate/sample.go:196-247) for every session, the whole
+        policy on the device: (tokens, probs, lengths), -1 / 0 past each session's length.
+        ``penalize_prompt`` makes the prompt the penalty prefix (chat.go:72); ``dfa``
+        [n_states x vocab] (next state, -1 = not allowed) with ``dfa_start`` [count] is the
+        constraint automaton."""
+        p = np.ascontiguousarray(prompts, np.int32)
+        lens = np.ascontiguousarray(lens, np.int32)
+        toks = np.zeros((self.count, n_new), np.int32)
+        probs = np.zeros((self.count, n_new), np.float32)
+        out_lens = np.zeros(self.count, np.int32)
+        st = np.ascontiguousarray(list(stops), np.int32)
+        d = ds = None
+        n_states = 0
+        if dfa is not None:
+            d = np.ascontiguousarray(dfa, np.int32)
+            n_states = d.shape[0]
+            ds = np.ascontiguousarray(dfa_start, np.int32)
+        _lib.check(_lib.lib().mc_generate_policy(self._h, _lib.ptr(p), _lib.ptr(lens), p.shape[1], n_new,
+                                                 ctypes.byref(sampling), int(bool(penalize_prompt)), _lib.ptr(d),
+                                                 n_states, _lib.ptr(ds), session0, _lib.ptr(st) if st.size else None,
+                                                 int(st.size), _lib.ptr(toks), _lib.ptr(probs), _lib.ptr(out_lens)))
         return toks, probs, out_lens
 
 

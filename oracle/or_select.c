@@ -214,3 +214,186 @@ int or_score(const or_model* m, int n_seq, int len, const int32_t* tokens, doubl
     }
     return 0;
 }
+
+/* ---- the full decode-loop policy ---------------------------------------------------------- */
+
+static int is_stop(int tok, const int32_t* stops, int n_stops) {
+    for (int k = 0; k < n_stops; k++)
+        if (stops[k] >= 0 && tok == stops[k]) return 1;
+    return 0;
+}
+
+/* Token k of the concatenation prefix ++ gen. */
+static int32_t hist_at(const int32_t* prefix, int n_prefix, const int32_t* gen, int k) {
+    return k < n_prefix ? prefix[k] : gen[k - n_prefix];
+}
+
+/* Sum of v[0..n) in index order, and the index of the first running sum >= r (or -1). */
+static int first_cum_at_least(const double* v, int n, double r) {
+    double cum = 0.0;
+    for (int i = 0; i < n; i++) {
+        cum += v[i];
+        if (r <= cum) return i;
+    }
+    return -1;
+}
+
+int or_sample_policy(double* logits, int n, const int32_t* prefix, int n_prefix, const int32_t* gen, int n_gen,
+                     const or_sampling* sp, const int32_t* allowed, double u, double* prob) {
+    const double neg_max = -1.7976931348623157e308;
+    if (n <= 0) return 0;
+    /* 3-gram repetition block of sampleContinuation (sample.go:213-227): a token that followed the
+     * trailing pair earlier in the generated tokens gets -MaxFloat64 */
+    if (sp->ban_trigrams && n_gen >= 2) {
+        const int32_t w1 = gen[n_gen - 2], w2 = gen[n_gen - 1];
+        for (int i = 0; i <= n_gen - 3; i++)
+            if (gen[i] == w1 && gen[i + 1] == w2 && gen[i + 2] >= 0 && gen[i + 2] < n) logits[gen[i + 2]] = neg_max;
+    }
+    /* Constraint.Mask (sample.go:229-231): tokens without a transition get -1e300 like the
+     * grammar's negInf (constrain/grammar.go:259) */
+    if (allowed)
+        for (int i = 0; i < n; i++)
+            if (allowed[i] < 0) logits[i] = -1e300;
+    /* repetition penalty over the window's distinct tokens (sample.go:48-69); the window is the
+     * trailing rep_window tokens of prefix ++ generated (sample.go:207-210) */
+    const int total = n_prefix + n_gen;
+    const int w = sp->rep_window > 0 && sp->rep_window < total ? sp->rep_window : total;
+    const int w0 = total - w;
+    if (sp->rep_penalty > 1.0 && w > 0) {
+        for (int i = 0; i < w; i++) {
+            const int32_t tok = hist_at(prefix, n_prefix, gen, w0 + i);
+            if (tok < 0 || tok >= n) continue;
+            int seen = 0;
+            for (int j = 0; j < i && !seen; j++) seen = hist_at(prefix, n_prefix, gen, w0 + j) == tok;
+            if (seen) continue;
+            if (logits[tok] > 0) logits[tok] /= sp->rep_penalty;
+            else logits[tok] *= sp->rep_penalty;
+        }
+    }
+    /* greedy argmax (sample.go:71-82); prob = 1 / sum exp(l - max) as argmaxProb reports it */
+    if (sp->temperature <= 0.001) {
+        int best = 0;
+        for (int i = 1; i < n; i++)
+            if (logits[i] > logits[best]) best = i;
+        if (prob) {
+            double s = 0.0;
+            for (int i = 0; i < n; i++) s += exp(logits[i] - logits[best]);
+            *prob = 1.0 / s;
+        }
+        return best;
+    }
+    const double inv_t = 1.0 / sp->temperature;
+    double mx = neg_max;
+    for (int i = 0; i < n; i++) {
+        logits[i] *= inv_t;
+        if (logits[i] > mx) mx = logits[i];
+    }
+    if (sp->top_k <= 0 && sp->top_p >= 0.9999) {
+        /* pure temperature sampling in index order (sample.go:96-117) */
+        double s = 0.0;
+        for (int i = 0; i < n; i++) {
+            logits[i] = exp(logits[i] - mx);
+            s += logits[i];
+        }
+        int chosen = first_cum_at_least(logits, n, u * s);
+        if (chosen < 0) chosen = 0;
+        if (prob) *prob = logits[chosen] / s;
+        return chosen;
+    }
+    /* truncated sampling (sample.go:119-172): probabilities sorted descending (ties by index),
+     * top-k, then the shortest prefix whose mass reaches top-p, then sampleFromCDF (:174-191) */
+    cand* c = malloc(sizeof(cand) * (size_t)n);
+    double s = 0.0;
+    for (int i = 0; i < n; i++) {
+        c[i].idx = i;
+        c[i].prob = exp(logits[i] - mx);
+        s += c[i].prob;
+    }
+    const double inv = 1.0 / s;
+    for (int i = 0; i < n; i++) c[i].prob *= inv;
+    qsort(c, (size_t)n, sizeof(cand), cand_cmp);
+    int active = n;
+    if (sp->top_k > 0 && sp->top_k < active) active = sp->top_k;
+    if (sp->top_p > 0.0 && sp->top_p < 1.0) {
+        double cum = 0.0;
+        int cut = 0;
+        for (int i = 0; i < active; i++) {
+            cum += c[i].prob;
+            cut = i + 1;
+            if (cum >= sp->top_p) break;
+        }
+        active = cut;
+    }
+    int chosen;
+    double p;
+    if (active == 1) {
+        chosen = c[0].idx;
+        p = 1.0;
+    } else {
+        double sp_sum = 0.0;
+        for (int i = 0; i < active; i++) sp_sum += c[i].prob;
+        const double r = u * sp_sum;
+        double cum = 0.0;
+        int k = active - 1;
+        for (int i = 0; i < active; i++) {
+            cum += c[i].prob;
+            if (r <= cum) {
+                k = i;
+                break;
+            }
+        }
+        chosen = c[k].idx;
+        p = c[k].prob / sp_sum;
+    }
+    if (prob) *prob = p;
+    free(c);
+    return chosen;
+}
+
+int or_generate_policy(const or_model* m, int n_sess, const int32_t* prompts, int stride, const int32_t* lens,
+                       int context_size, int n_new, const or_sampling* sp, int penalize_prompt, const int32_t* dfa,
+                       const int32_t* dfa_start, uint32_t session0, const int32_t* stops, int n_stops,
+                       int32_t* out_tokens, float* out_probs, int32_t* out_lens, float* out_logits, int nthreads) {
+    set_threads(nthreads);
+    const int V = m->vocab;
+#pragma omp parallel
+    {
+        or_session* s = or_session_new(m, context_size);
+        float* logits = malloc(sizeof(float) * (size_t)V);
+        double* work = malloc(sizeof(double) * (size_t)V);
+        int32_t* gen = malloc(sizeof(int32_t) * (size_t)(n_new > 0 ? n_new : 1));
+#pragma omp for schedule(dynamic, 1)
+        for (int i = 0; i < n_sess; i++) {
+            const int32_t* prompt = prompts + (size_t)i * stride;
+            int have = or_session_prefill(s, prompt, lens[i], logits);
+            int n_gen = 0;
+            int state = dfa ? dfa_start[i] : -1;
+            /* sampleContinuation (sample.go:196-247): the penalty prefix is the prompt (chat.go:72)
+             * or nothing (chat.go:122) */
+            for (int t = 0; t < n_new && have; t++) {
+                if (out_logits) memcpy(out_logits + ((size_t)i * n_new + t) * V, logits, sizeof(float) * V);
+                for (int v = 0; v < V; v++) work[v] = (double)logits[v];
+                double p = 0.0;
+                const double u = or_sample_uniform(session0 + (uint32_t)i, (uint32_t)t);
+                const int tok = or_sample_policy(work, V, prompt, penalize_prompt ? lens[i] : 0, gen, n_gen, sp,
+                                                 state >= 0 ? dfa + (size_t)state * V : NULL, u, &p);
+                if (is_stop(tok, stops, n_stops)) break;
+                if (state >= 0) state = dfa[(size_t)state * V + tok];  /* Constraint.Advance */
+                gen[n_gen++] = tok;
+                out_tokens[(size_t)i * n_new + t] = tok;
+                if (out_probs) out_probs[(size_t)i * n_new + t] = (float)p;
+                if (n_gen < n_new) or_session_append(s, tok, logits);
+            }
+            for (int t = n_gen; t < n_new; t++) {
+                out_tokens[(size_t)i * n_new + t] = -1;
+                if (out_probs) out_probs[(size_t)i * n_new + t] = 0.f;
+            }
+            if (out_lens) out_lens[i] = n_gen;
+        }
+        free(gen);
+        free(work);
+        free(logits);
+        or_session_free(s);
+    }
+    return 0;
+}

@@ -87,6 +87,23 @@ double or_sample_uniform(uint32_t session, uint32_t step);
  * topP 1, the uniform draw u supplied by the caller (the reference uses math/rand). */
 int or_sample_topk(const float* logits, int n, double temperature, int topk, double u);
 
+/* Sampling parameters of sampleContinuation / SampleRawLogitsAdvanced (generate/chat.go:45-56). */
+typedef struct {
+    double temperature; /* <= 0.001: argmax */
+    double rep_penalty; /* > 1: the window's distinct tokens are penalised */
+    int top_k;          /* <= 0: off */
+    double top_p;       /* in (0, 1): nucleus cutoff; else off */
+    int rep_window;     /* trailing tokens of prefix ++ generated the penalty sees; <= 0: all */
+    int ban_trigrams;   /* the 3-gram repetition block of sampleContinuation (sample.go:213-227) */
+} or_sampling;
+/* One token of sampleContinuation's loop body (sample.go:206-232) over float64 logits, modified in
+ * place: 3-gram ban over gen, constraint mask (allowed[i] < 0 masks token i; NULL: none),
+ * repetition penalty over the window of prefix ++ gen, then SampleRawLogitsAdvanced
+ * (sample.go:33-172) with the draw u. *prob = the chosen token's probability in the distribution
+ * it was drawn from (argmax: 1 / sum exp(l - max)). */
+int or_sample_policy(double* logits, int n, const int32_t* prefix, int n_prefix, const int32_t* gen, int n_gen,
+                     const or_sampling* sp, const int32_t* allowed, double u, double* prob);
+
 /* ---- batch runners (OpenMP over sessions; one engine state per session) ---- */
 /* Greedy generation (greedyLoop, greedy.go:63-87, no stop tokens): for each session s,
  * prompts[s*stride : s*stride+lens[s]]; writes n_new tokens and probs per session, and if
@@ -98,6 +115,15 @@ int or_generate_greedy(const or_model* m, int n_sess, const int32_t* prompts, in
 int or_generate_sample(const or_model* m, int n_sess, const int32_t* prompts, int stride, const int32_t* lens,
                        int context_size, int n_new, double temperature, int topk, uint32_t session0,
                        int32_t* out_tokens, float* out_logits, int nthreads);
+/* sampleContinuation (generate/sample.go:196-247) per session: the policy of or_sample_policy
+ * with the draw or_sample_uniform(s0 + s, step), the prompt as penalty prefix when
+ * penalize_prompt, a token automaton dfa[n_states][vocab] (next state, -1 = not allowed; NULL:
+ * none) starting in dfa_start[s] (< 0: unconstrained), and stop tokens that end a session before
+ * they are emitted. Unused columns: token -1, prob 0; out_lens[s] = tokens emitted. */
+int or_generate_policy(const or_model* m, int n_sess, const int32_t* prompts, int stride, const int32_t* lens,
+                       int context_size, int n_new, const or_sampling* sp, int penalize_prompt, const int32_t* dfa,
+                       const int32_t* dfa_start, uint32_t session0, const int32_t* stops, int n_stops,
+                       int32_t* out_tokens, float* out_probs, int32_t* out_lens, float* out_logits, int nthreads);
 /* Scoring: for each sequence, the log-prob of tokens[t] given tokens[:t] for t = 1..len-1. */
 int or_score(const or_model* m, int n_seq, int len, const int32_t* tokens, double* out_logprobs, int nthreads);
 

@@ -21,6 +21,16 @@ _f64p = ctypes.POINTER(ctypes.c_double)
 _i8p = ctypes.POINTER(ctypes.c_int8)
 
 
+class Sampling(ctypes.Structure):
+    """or_sampling: the knobs of generate.Sampling (internal/generate/chat.go:45-56)."""
+    _fields_ = [("temperature", ctypes.c_double), ("rep_penalty", ctypes.c_double), ("top_k", ctypes.c_int),
+                ("top_p", ctypes.c_double), ("rep_window", ctypes.c_int), ("ban_trigrams", ctypes.c_int)]
+
+    def __init__(self, temperature=0.0, rep_penalty=1.0, top_k=0, top_p=1.0, rep_window=0, ban_trigrams=0):
+        super().__init__(float(temperature), float(rep_penalty), int(top_k), float(top_p), int(rep_window),
+                         int(ban_trigrams))
+
+
 def build(force: bool = False) -> str:
     """Builds liboracle.so with the committed Makefile (the system gcc)."""
     if force or not os.path.exists(_LIB_PATH) or any(
@@ -88,6 +98,14 @@ def lib():
         L.or_generate_sample.restype = ctypes.c_int
         L.or_generate_sample.argtypes = [ctypes.c_void_p, ctypes.c_int, _i32p, ctypes.c_int, _i32p, ctypes.c_int,
                                          ctypes.c_int, ctypes.c_double, ctypes.c_int, ctypes.c_uint32, _i32p, _f32p,
+                                         ctypes.c_int]
+        L.or_sample_policy.restype = ctypes.c_int
+        L.or_sample_policy.argtypes = [_f64p, ctypes.c_int, _i32p, ctypes.c_int, _i32p, ctypes.c_int,
+                                       ctypes.POINTER(Sampling), _i32p, ctypes.c_double, _f64p]
+        L.or_generate_policy.restype = ctypes.c_int
+        L.or_generate_policy.argtypes = [ctypes.c_void_p, ctypes.c_int, _i32p, ctypes.c_int, _i32p, ctypes.c_int,
+                                         ctypes.c_int, ctypes.POINTER(Sampling), ctypes.c_int, _i32p, _i32p,
+                                         ctypes.c_uint32, _i32p, ctypes.c_int, _i32p, _f32p, _i32p, _f32p,
                                          ctypes.c_int]
         L.or_score.restype = ctypes.c_int
         L.or_score.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, _i32p, _f64p, ctypes.c_int]
@@ -170,6 +188,27 @@ class Model:
                                  _p(lg, _f32p) if lg is not None else None, nthreads)
         return toks, lg
 
+    def generate_policy(self, prompts, lens, n_new, sampling: Sampling, penalize_prompt=False, dfa=None,
+                        dfa_start=None, session0=0, stops=(), context_size=0, logits=False, nthreads=0):
+        """sampleContinuation per session: tokens [n x n_new] (-1 after a session ends), probs,
+        lengths and (logits=True) the float32 logits each token was drawn from."""
+        prompts = i32(prompts)
+        lens = i32(lens)
+        n = prompts.shape[0]
+        toks = np.zeros((n, n_new), dtype=np.int32)
+        probs = np.zeros((n, n_new), dtype=np.float32)
+        out_lens = np.zeros(n, dtype=np.int32)
+        st = i32(list(stops) or [0])
+        d = i32(dfa) if dfa is not None else None
+        ds = i32(dfa_start) if dfa is not None else None
+        lg = np.zeros((n, n_new, self.vocab), dtype=np.float32) if logits else None
+        lib().or_generate_policy(self._h, n, _p(prompts, _i32p), prompts.shape[1], _p(lens, _i32p), context_size,
+                                 n_new, ctypes.byref(sampling), int(penalize_prompt),
+                                 _p(d, _i32p) if d is not None else None, _p(ds, _i32p) if ds is not None else None,
+                                 session0, _p(st, _i32p), len(stops), _p(toks, _i32p), _p(probs, _f32p),
+                                 _p(out_lens, _i32p), _p(lg, _f32p) if lg is not None else None, nthreads)
+        return toks, probs, out_lens, lg
+
     def score(self, seqs, nthreads=0) -> np.ndarray:
         seqs = i32(seqs)
         n, L = seqs.shape
@@ -251,6 +290,19 @@ def log_prob(logits, idx) -> float:
 def sample_topk(logits, temperature, topk, u) -> int:
     l = f32(logits)
     return int(lib().or_sample_topk(_p(l, _f32p), l.size, temperature, topk, u))
+
+
+def sample_policy(logits, sampling: Sampling, prefix=(), gen=(), allowed=None, u=0.5):
+    """One step of sampleContinuation over float64 logits: (token, probability)."""
+    l = np.array(logits, dtype=np.float64)
+    pre = i32(list(prefix) or [0])
+    g = i32(list(gen) or [0])
+    a = i32(allowed) if allowed is not None else None
+    p = ctypes.c_double()
+    t = lib().or_sample_policy(_p(l, _f64p), l.size, _p(pre, _i32p), len(prefix), _p(g, _i32p), len(gen),
+                               ctypes.byref(sampling), _p(a, _i32p) if a is not None else None, float(u),
+                               ctypes.byref(p))
+    return int(t), float(p.value)
 
 
 def philox(ctr, key):
