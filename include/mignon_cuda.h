@@ -190,6 +190,37 @@ int mc_sample_rows(int device, const float* logits, int n, int vocab, const int3
                    int recent_stride, const int32_t* allowed, const mc_sampling* sampling, const double* u,
                    uint32_t session0, uint32_t step, int32_t* out_tokens, float* out_probs);
 
+/* Continuous batching: a scheduler over `slots` sessions of one model (sharded over the
+ * context's devices like mc_batch_open). Requests queue on the host; whenever at least
+ * admit_min slots are free (default slots / 8) or none is running, queued requests are admitted
+ * into the free slots by one prefill pass in which the running slots keep their state, and all
+ * running slots then decode together. Each request runs sampleContinuation
+ * (internal/generate/sample.go:196-247) with the scheduler's sampling knobs, the prompt as
+ * penalty prefix when penalize_prompt (which needs rep_window >= 1), its own token limit and the
+ * scheduler's stop tokens, its draws keyed by its draw_key and its token index (as
+ * mc_generate_policy keys session s by session0 + s), so its tokens do not depend on which slot
+ * it ran in or what ran beside it. Prompts: at most max_prompt tokens after trimming to the
+ * window; token limits: 1 to max_new. */
+typedef struct mc_sched mc_sched;
+int mc_sched_open(mc_model* model, int slots, int context_size, int max_prompt, int max_new,
+                  const mc_sampling* sampling, int penalize_prompt, const int32_t* stops, int n_stops, mc_sched** out);
+int mc_sched_close(mc_sched* sched);
+/* Queues a request; *id = its index (0, 1, 2, ... in submission order). An empty prompt finishes
+ * with no tokens (Prefill of nothing returns no logits). */
+int mc_sched_submit(mc_sched* sched, const int32_t* prompt, int len, int n_new, uint32_t draw_key, int64_t* id);
+/* One round: admission where due, `steps` decode steps, then the finished requests are collected.
+ * *in_flight = requests queued or running afterwards. */
+int mc_sched_step(mc_sched* sched, int steps, int* in_flight);
+/* Rounds of steps_per_poll decode steps until no request is queued or running. */
+int mc_sched_run(mc_sched* sched, int steps_per_poll);
+/* A finished request's tokens (and probabilities, like mc_generate_policy's): *n = its token
+ * count, of which the first `capacity` are copied; *n = -1 while it is queued or running. */
+int mc_sched_result(mc_sched* sched, int64_t id, int32_t* tokens, float* probs, int capacity, int* n);
+/* out[5] = prefill passes, decode steps, tokens emitted, requests finished, requests in flight. */
+int mc_sched_stats(const mc_sched* sched, int64_t* out);
+/* Admit when at least admit_min slots are free (or none is running). */
+int mc_sched_set_admit_min(mc_sched* sched, int admit_min);
+
 /* mc_generate with device-resident inputs and outputs on a single-device batch: enqueues the
  * whole job on the batch's stream (mc_batch_stream) and returns without synchronizing.
  * pmax >= every lens[s]. Check completion and device errors with mc_batch_error. */

@@ -10,3 +10,4 @@
 #include "mc_policy.cu"
 #include "mc_engine_host.cu"
 #include "mc_api.cu"
+#include "mc_sched.cu"

@@ -165,6 +165,7 @@ int run_graph_step(DevBatch& sh, int mode, double inv_temp, uint32_t session0, b
   key.n_stops = sh.n_stops;
   for (int k = 0; k < sh.n_stops; ++k) key.stops[k] = sh.stops[k];
   key.pol = sh.pol;
+  key.per_session = sh.per_session;
   if (!sh.graph || !(sh.graph_key == key)) {
     if (sh.graph) {
       cudaGraphExecDestroy(sh.graph);

@@ -262,6 +262,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
   auto use_cache = [&](const GemmSpec& G) {
     return CACHE && acache != nullptr && G.ktiles <= a.a_cache_kt && G.nchunks > 1;
   };
+  // a tile whose sessions all sit this pass out (seglen 0: idle, finished, or kept out of a
+  // scheduler's admission pass) has nothing to do
+  {
+    const int sess = tile * a.spt + (int)threadIdx.x;
+    const bool live = (int)threadIdx.x < a.spt && sess < a.n_sess && a.seglen[sess] > 0;
+    if (!__syncthreads_or(live)) return;
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kASlots; ++i) {

@@ -278,6 +278,12 @@ struct DevBatch {
   int32_t *pol_prefix = nullptr, *pol_prefix_len = nullptr, *pol_state = nullptr, *pol_dfa = nullptr;
   int pol_prefix_cap = 0;  // tokens per session that pol_prefix holds
   size_t pol_dfa_n = 0;    // entries pol_dfa holds
+  // Per-session generation (the scheduler's slots): tokens emitted, token limit and draw key of
+  // each session, used by mode-3 launches when per_session is set; sched_adm is the scheduler's
+  // admission list.
+  bool per_session = false;
+  int32_t *gen_n = nullptr, *limit = nullptr, *sched_adm = nullptr;
+  uint32_t* key = nullptr;
   uint8_t* a_cache = nullptr;    // block kernel: per-SM digit-plane cache of GEMMs wider than the A slots
   int a_cache_kt = 0;
   int32_t *pos = nullptr, *seglen = nullptr, *tok = nullptr, *next_tok = nullptr, *step = nullptr, *rowmap = nullptr,
@@ -315,8 +321,9 @@ struct DevBatch {
     int n_stops = 0;
     int stops[kMaxStops] = {0};
     Policy pol;
+    bool per_session = false;
     bool operator==(const GraphKey& o) const {
-      if (n_stops != o.n_stops || !(pol == o.pol)) return false;
+      if (n_stops != o.n_stops || !(pol == o.pol) || per_session != o.per_session) return false;
       for (int k = 0; k < n_stops; ++k)
         if (stops[k] != o.stops[k]) return false;
       return mode == o.mode && logits == o.logits && stride == o.stride && inv_t == o.inv_t && session0 == o.session0 &&
@@ -771,6 +778,11 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
     pa.dfa_state = b.pol.dfa ? b.pol_state : nullptr;
     pa.session0 = session0;
     pa.step = b.step;
+    if (b.per_session) {
+      pa.gen_n = b.gen_n;
+      pa.limit = b.limit;
+      pa.key = b.key;
+    }
     pa.out_stride = b.out_stride;
     pa.next_tok = b.next_tok;
     pa.out_tok = b.out_tok;

@@ -36,8 +36,12 @@ struct PolicyArgs {
   int gen_stride;
   const int32_t* dfa;                 // [states][V]: next state, -1 = not allowed; null: no constraint
   int32_t* dfa_state;                 // [n_rows] state of each row (< 0: unconstrained)
-  const double* u;                    // [n_rows] uniform draws, or null: Philox (session0 + row, step)
-  uint32_t session0;
+  const double* u;                    // [n_rows] uniform draws, or null: Philox (key, token index)
+  uint32_t session0;                  // key of row r when key is null: session0 + r
+  const uint32_t* key;                // [n_rows] Philox key of each row's draws, or null
+  int32_t* gen_n;                     // [n_rows] tokens each row has emitted: its output column, draw counter
+                                      // and 3-gram history length, advanced per emitted token; null: *step
+  const int32_t* limit;               // [n_rows] tokens a row may emit (it ends after the last), with gen_n
   int32_t* step;                      // device step counter (output column and draw counter), or null:
   uint32_t step0;                     // column 0 and draw counter step0
   int out_stride;
@@ -166,9 +170,12 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
   const int step = a.step ? *a.step : (int)a.step0;
   const bool live = !a.seglen || a.seglen[row] > 0;
   if (live) {
+    // tokens this row has emitted so far: its output column and the counter of its draw
+    const int cnt = a.gen_n ? a.gen_n[row] : step;
+    const uint32_t dkey = a.key ? a.key[row] : a.session0 + (uint32_t)row;
     const float* lg = a.logits + (size_t)row * V;
     for (int i = tid; i < V; i += kPolicyThreads) key[i] = (double)lg[i];
-    const int ng = a.gen ? (a.gen_len ? a.gen_len[row] : step) : 0;
+    const int ng = a.gen ? (a.gen_len ? a.gen_len[row] : cnt) : 0;
     const int32_t* gen = a.gen ? a.gen + (size_t)row * a.gen_stride : nullptr;
     const int np = a.prefix ? a.prefix_len[row] : 0;
     const int32_t* pre = a.prefix ? a.prefix + (size_t)row * a.prefix_stride : nullptr;
@@ -235,7 +242,7 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
         const double base = pol_chunk_base(key, V, c, red_d);
         pol_first_at_least(key, V, c, base, INFINITY, V - 1, &at_k, red_i);
         const double s = at_k;
-        const double u = a.u ? a.u[row] : sample_uniform(a.session0 + (uint32_t)row, (uint32_t)step);
+        const double u = a.u ? a.u[row] : sample_uniform(dkey, (uint32_t)cnt);
         const int k = pol_first_at_least(key, V, c, base, u * s, -1, &at_k, red_i);
         tok = k == 0x7fffffff ? 0 : k;
         prob = key[tok] / s;
@@ -287,7 +294,7 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
         } else {
           pol_first_at_least(key, active, c, base, INFINITY, cut - 1, &at_k, red_i);
           const double sp = at_k;
-          const double u = a.u ? a.u[row] : sample_uniform(a.session0 + (uint32_t)row, (uint32_t)step);
+          const double u = a.u ? a.u[row] : sample_uniform(dkey, (uint32_t)cnt);
           int k = pol_first_at_least(key, active, c, base, u * sp, -1, &at_k, red_i);
           if (k >= cut) k = cut - 1;
           tok = idx[k];
@@ -302,7 +309,7 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
       if (stop) {
         if (a.seglen) a.seglen[row] = 0;
       } else {
-        const int col = a.step ? step : 0;
+        const int col = a.gen_n || a.step ? cnt : 0;
         if (a.next_tok) a.next_tok[row] = tok;
         a.out_tok[(size_t)row * a.out_stride + col] = tok;
         if (a.out_prob) a.out_prob[(size_t)row * a.out_stride + col] = (float)prob;
@@ -312,6 +319,10 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
           a.seglen[row] = 1;
         }
         if (state >= 0) a.dfa_state[row] = a.dfa[(size_t)state * V + tok];
+        if (a.gen_n) {
+          a.gen_n[row] = cnt + 1;
+          if (a.limit && a.seglen && cnt + 1 >= a.limit[row]) a.seglen[row] = 0;  // its last token
+        }
       }
     }
   }

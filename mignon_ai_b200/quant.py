@@ -41,6 +41,14 @@ _lib.register({
                            c_vp],
     "mc_sample_rows": [_i, c_vp, _i, _i, c_vp, c_vp, _i, c_vp, c_vp, c_vp, ctypes.c_uint32, ctypes.c_uint32, c_vp,
                        c_vp],
+    "mc_sched_open": [c_vp, _i, _i, _i, _i, c_vp, _i, c_vp, _i, ctypes.POINTER(c_vp)],
+    "mc_sched_close": [c_vp],
+    "mc_sched_submit": [c_vp, c_vp, _i, _i, ctypes.c_uint32, ctypes.POINTER(ctypes.c_int64)],
+    "mc_sched_step": [c_vp, _i, ctypes.POINTER(_i)],
+    "mc_sched_run": [c_vp, _i],
+    "mc_sched_result": [c_vp, ctypes.c_int64, c_vp, c_vp, _i, ctypes.POINTER(_i)],
+    "mc_sched_stats": [c_vp, c_vp],
+    "mc_sched_set_admit_min": [c_vp, _i],
 })
 
 # sampleContinuation's repetition window (internal/generate/constants.go:11)
@@ -293,6 +301,75 @@ class SessionBatch:
                                                  n_states, _lib.ptr(ds), session0, _lib.ptr(st) if st.size else None,
                                                  int(st.size), _lib.ptr(toks), _lib.ptr(probs), _lib.ptr(out_lens)))
         return toks, probs, out_lens
+
+
+class Scheduler:
+    """Continuous batching over ``slots`` GPU session slots (mc_sched_*): requests queue on the
+    host, are admitted into free slots by prefill passes while the other slots keep their state,
+    and decode together; each ends at its own ``n_new`` or a stop token. Every request runs
+    sampleContinuation (internal/generate/sample.go:196-247) with ``sampling``; its draws are
+    keyed by ``draw_key`` (default: its id) and its token index, so its tokens do not depend on
+    the slot it ran in or on the other requests."""
+
+    def __init__(self, model: Model, slots: int, sampling: Optional[Sampling] = None, context_size: int = 0,
+                 max_prompt: int = 128, max_new: int = 128, penalize_prompt: bool = False, stops=()):
+        sampling = sampling if sampling is not None else Sampling()
+        st = np.ascontiguousarray(list(stops), np.int32)
+        h = c_vp()
+        _lib.check(_lib.lib().mc_sched_open(model._h, slots, context_size, max_prompt, max_new, ctypes.byref(sampling),
+                                            int(bool(penalize_prompt)), _lib.ptr(st) if st.size else None,
+                                            int(st.size), ctypes.byref(h)))
+        self._h = h
+        self.model = model
+        self.max_new = max_new
+        self._submitted = 0
+
+    def close(self):
+        if self._h:
+            _lib.lib().mc_sched_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def submit(self, prompt: Sequence[int], n_new: int, draw_key: Optional[int] = None) -> int:
+        """Queues a request; returns its id."""
+        p = np.ascontiguousarray(list(prompt), np.int32)
+        rid = ctypes.c_int64()
+        key = self._submitted if draw_key is None else draw_key
+        _lib.check(_lib.lib().mc_sched_submit(self._h, _lib.ptr(p) if p.size else None, int(p.size), int(n_new),
+                                              ctypes.c_uint32(key & 0xFFFFFFFF), ctypes.byref(rid)))
+        self._submitted += 1
+        return int(rid.value)
+
+    def step(self, steps: int = 8) -> int:
+        """One round (admission where due, ``steps`` decode steps, collection); returns the
+        number of requests still queued or running."""
+        left = _i()
+        _lib.check(_lib.lib().mc_sched_step(self._h, steps, ctypes.byref(left)))
+        return int(left.value)
+
+    def run(self, steps_per_poll: int = 8):
+        _lib.check(_lib.lib().mc_sched_run(self._h, steps_per_poll))
+
+    def set_admit_min(self, admit_min: int):
+        _lib.check(_lib.lib().mc_sched_set_admit_min(self._h, admit_min))
+
+    def result(self, rid: int):
+        """(tokens, probs) of a finished request, None while it is queued or running."""
+        n = _i()
+        toks = np.zeros(self.max_new, np.int32)
+        probs = np.zeros(self.max_new, np.float32)
+        _lib.check(_lib.lib().mc_sched_result(self._h, rid, _lib.ptr(toks), _lib.ptr(probs), self.max_new,
+                                              ctypes.byref(n)))
+        if n.value < 0:
+            return None
+        return toks[:n.value].copy(), probs[:n.value].copy()
+
+    def stats(self) -> dict:
+        out = np.zeros(5, np.int64)
+        _lib.check(_lib.lib().mc_sched_stats(self._h, _lib.ptr(out)))
+        return dict(zip(("prefill_passes", "decode_steps", "tokens", "finished", "in_flight"), map(int, out)))
 
 
 class Session:
