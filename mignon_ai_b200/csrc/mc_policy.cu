@@ -19,9 +19,10 @@
 namespace mc {
 namespace eng {
 
-constexpr int kPolicyThreads = 512;
+constexpr int kPolicyThreads = 256;
 constexpr int kPolicyWarps = kPolicyThreads / 32;
 constexpr int kPolicyMaxVocab = 16384;  // the sort keys and indices of a row fill 192 KB of shared memory
+constexpr int kPolicyMaxK = 1024;       // top-k up to this selects its candidates instead of sorting all
 
 struct PolicyArgs {
   int n_rows, V, vp;                  // vp: V rounded up to a power of two (the sort's size)
@@ -158,12 +159,106 @@ __device__ __forceinline__ int pol_first_at_least(const double* x, int n, int c,
   return pol_block_min(first, red_i);
 }
 
+// Exclusive scan of one int per thread in thread order (every thread gets its own prefix).
+__device__ __forceinline__ int pol_block_excl_scan(int v, int* red_i) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) red_i[warp] = x;
+  __syncthreads();
+  int base = 0;
+  for (int w = 0; w < warp; ++w) base += red_i[w];
+  __syncthreads();
+  return base + x - v;
+}
+
+// Bitonic sort of n (a power of two) entries into (value descending, index ascending).
+__device__ __forceinline__ void pol_sort(double* key, int32_t* idx, int n) {
+  for (int kk = 2; kk <= n; kk <<= 1) {
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      for (int p = threadIdx.x; p < (n >> 1); p += kPolicyThreads) {
+        const int lo = ((p & ~(j - 1)) << 1) | (p & (j - 1)), hi = lo | j;
+        const bool up = (lo & kk) == 0;
+        const double kl = key[lo], kh = key[hi];
+        const int il = idx[lo], ih = idx[hi];
+        if (pol_better(kh, ih, kl, il) == up) {
+          key[lo] = kh;
+          key[hi] = kl;
+          idx[lo] = ih;
+          idx[hi] = il;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Radix select over the bit patterns of p[0..n) (non-negative doubles, whose bits order like their
+// values), 8 bits per pass from the top: *tau = the value bits of the k-th entry in (value
+// descending, index ascending) order, *r = how many entries equal to it rank among the first k.
+__device__ __forceinline__ void pol_radix_select(const double* p, int n, int k, unsigned long long* tau, int* r_out,
+                                                 int* hist, int* pick) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  unsigned long long prefix = 0ull, mask = 0ull;
+  int r = k;
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int b = tid; b < 256; b += kPolicyThreads) hist[b] = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += kPolicyThreads) {
+      const unsigned long long kb = (unsigned long long)__double_as_longlong(p[i]);
+      if ((kb & mask) == prefix) atomicAdd(&hist[(int)(kb >> shift) & 255], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // lane l holds the bins 255 - 8l down to 248 - 8l: counts above a bin come from lower lanes
+      int c[8], tot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hist[255 - 8 * lane - j];
+        tot += c[j];
+      }
+      int incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      int acc = incl - tot;
+      if (acc < r && r <= incl) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (acc < r && r <= acc + c[j]) {
+            pick[0] = 255 - 8 * lane - j;
+            pick[1] = acc;
+          }
+          acc += c[j];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= (unsigned long long)pick[0] << shift;
+    mask |= 255ull << shift;
+    r -= pick[1];
+    __syncthreads();
+  }
+  *tau = prefix;
+  *r_out = r;
+}
+
 __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_constant__ PolicyArgs a) {
   extern __shared__ __align__(16) unsigned char pol_smem[];
   double* key = reinterpret_cast<double*>(pol_smem);
   int32_t* idx = reinterpret_cast<int32_t*>(key + a.vp);
+  double* ckey = reinterpret_cast<double*>(idx + a.vp);  // top-k candidates [kPolicyMaxK]
+  int32_t* cidx = reinterpret_cast<int32_t*>(ckey + kPolicyMaxK);
   __shared__ double red_d[kPolicyWarps];
   __shared__ int red_i[kPolicyWarps];
+  __shared__ int hist[256];
+  __shared__ int pick[2];
   __shared__ double at_k;
   const int row = blockIdx.x, tid = threadIdx.x;
   const int V = a.V;
@@ -247,58 +342,81 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
         tok = k == 0x7fffffff ? 0 : k;
         prob = key[tok] / s;
       } else {
-        // 3e. probabilities, sorted descending (ties by index)
+        // 3e. probabilities in (value descending, index ascending) order: with top-k up to
+        //     kPolicyMaxK, a radix select finds the k-th entry and only the k candidates are
+        //     sorted; otherwise the whole row is sorted
         double s = 0.0;
         for (int i = tid; i < V; i += kPolicyThreads) s += key[i];
         s = pol_block_sum(s, red_d);
         const double inv = 1.0 / s;
-        for (int i = tid; i < a.vp; i += kPolicyThreads) {
-          if (i < V) {
-            key[i] *= inv;
-            idx[i] = i;
-          } else {
-            key[i] = -1.0;
-            idx[i] = 0x7fffffff;
-          }
-        }
+        for (int i = tid; i < V; i += kPolicyThreads) key[i] *= inv;
         __syncthreads();
-        for (int kk = 2; kk <= a.vp; kk <<= 1) {
-          for (int j = kk >> 1; j > 0; j >>= 1) {
-            for (int p = tid; p < (a.vp >> 1); p += kPolicyThreads) {
-              const int lo = ((p & ~(j - 1)) << 1) | (p & (j - 1)), hi = lo | j;
-              const bool up = (lo & kk) == 0;
-              const double kl = key[lo], kh = key[hi];
-              const int il = idx[lo], ih = idx[hi];
-              if (pol_better(kh, ih, kl, il) == up) {
-                key[lo] = kh;
-                key[hi] = kl;
-                idx[lo] = ih;
-                idx[hi] = il;
-              }
+        const double* sk;
+        const int32_t* si;
+        int active;
+        if (a.top_k > 0 && a.top_k < V && a.top_k <= kPolicyMaxK) {
+          const int K = a.top_k;
+          unsigned long long tau;
+          int r;
+          pol_radix_select(key, V, K, &tau, &r, hist, pick);
+          // the candidates: entries above tau, and the first r entries equal to it by index
+          const int c = (V + kPolicyThreads - 1) / kPolicyThreads;
+          const int lo = min(V, tid * c), hi = min(V, lo + c);
+          int eq = 0;
+          for (int i = lo; i < hi; ++i) eq += (unsigned long long)__double_as_longlong(key[i]) == tau;
+          int rank = pol_block_excl_scan(eq, red_i);
+          if (tid == 0) pick[0] = 0;
+          __syncthreads();
+          for (int i = lo; i < hi; ++i) {
+            const unsigned long long kb = (unsigned long long)__double_as_longlong(key[i]);
+            const bool take = kb > tau || (kb == tau && rank++ < r);
+            if (take) {
+              const int at = atomicAdd(&pick[0], 1);
+              ckey[at] = key[i];
+              cidx[at] = i;
             }
-            __syncthreads();
           }
+          int kp = 1;
+          while (kp < K) kp <<= 1;
+          for (int j = K + tid; j < kp; j += kPolicyThreads) {
+            ckey[j] = -1.0;
+            cidx[j] = 0x7fffffff;
+          }
+          __syncthreads();
+          pol_sort(ckey, cidx, kp);
+          sk = ckey;
+          si = cidx;
+          active = K;
+        } else {
+          for (int i = tid; i < a.vp; i += kPolicyThreads) {
+            idx[i] = i < V ? i : 0x7fffffff;
+            if (i >= V) key[i] = -1.0;
+          }
+          __syncthreads();
+          pol_sort(key, idx, a.vp);
+          sk = key;
+          si = idx;
+          active = a.top_k > 0 && a.top_k < V ? a.top_k : V;
         }
-        // 3f. top-k, then the shortest prefix whose mass reaches top-p, then the draw
-        int active = a.top_k > 0 && a.top_k < V ? a.top_k : V;
+        // 3f. the shortest prefix whose mass reaches top-p, then the draw
         const int c = (active + kPolicyThreads - 1) / kPolicyThreads;
-        const double base = pol_chunk_base(key, active, c, red_d);
+        const double base = pol_chunk_base(sk, active, c, red_d);
         int cut = active;
         if (a.top_p > 0.0 && a.top_p < 1.0) {
-          const int k = pol_first_at_least(key, active, c, base, a.top_p, -1, &at_k, red_i);
+          const int k = pol_first_at_least(sk, active, c, base, a.top_p, -1, &at_k, red_i);
           if (k != 0x7fffffff) cut = k + 1;
         }
         if (cut == 1) {
-          tok = idx[0];
+          tok = si[0];
           prob = 1.0;
         } else {
-          pol_first_at_least(key, active, c, base, INFINITY, cut - 1, &at_k, red_i);
+          pol_first_at_least(sk, active, c, base, INFINITY, cut - 1, &at_k, red_i);
           const double sp = at_k;
           const double u = a.u ? a.u[row] : sample_uniform(dkey, (uint32_t)cnt);
-          int k = pol_first_at_least(key, active, c, base, u * sp, -1, &at_k, red_i);
+          int k = pol_first_at_least(sk, active, c, base, u * sp, -1, &at_k, red_i);
           if (k >= cut) k = cut - 1;
-          tok = idx[k];
-          prob = key[k] / sp;
+          tok = si[k];
+          prob = sk[k] / sp;
         }
       }
     }
@@ -341,12 +459,14 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
 }
 
 inline int policy_vp(int V) {
-  int vp = 1;
+  int vp = 2;  // even, so the candidate arrays after the row's keys and indices stay 8-byte aligned
   while (vp < V) vp <<= 1;
   return vp;
 }
 
-inline size_t policy_smem(int V) { return (size_t)policy_vp(V) * (sizeof(double) + sizeof(int32_t)); }
+inline size_t policy_smem(int V) {
+  return ((size_t)policy_vp(V) + kPolicyMaxK) * (sizeof(double) + sizeof(int32_t));
+}
 
 int launch_policy(PolicyArgs& a, cudaStream_t s) {
   if (a.V < 1 || a.V > kPolicyMaxVocab) return set_error(kUnsupported, "sampling policy: vocabulary above 16384");

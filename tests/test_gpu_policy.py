@@ -60,6 +60,8 @@ CASES = [
     S(0.7, 1.2, 40, 0.9, 6, True),    # the reference's benchmark knobs (sample_test.go:47-59)
     S(1.3, 2.0, 0, 0.5, 4, True),     # nucleus only
     S(0.5, 1.1, 3, 1.0, 0, False),    # top-k only, whole recent list as the window
+    S(0.9, 1.0, 1000, 0.95, 0, False),  # the largest top-k that selects its candidates
+    S(0.9, 1.0, 1500, 1.0, 0, True),    # a top-k beyond that sorts the whole row
 ]
 
 
