@@ -779,10 +779,15 @@ __device__ __forceinline__ void decode_block(const BlockArgs& a, const DecodeLay
         if (stop) {
           a.seglen_w[s] = 0;  // greedyLoop ends before a stop token (generate/greedy.go:75-77)
         } else {
+          const int col = a.gen_n ? a.gen_n[s] : step;
           a.next_tok[s] = i;
-          if (a.out_tok) a.out_tok[(size_t)s * a.out_stride + step] = i;
-          if (a.out_prob) a.out_prob[(size_t)s * a.out_stride + step] = __fdiv_rn(1.0f, sm);
+          if (a.out_tok) a.out_tok[(size_t)s * a.out_stride + col] = i;
+          if (a.out_prob) a.out_prob[(size_t)s * a.out_stride + col] = __fdiv_rn(1.0f, sm);
           a.pos_w[s] = bars->pos[t] + 1;
+          if (a.gen_n) {  // per-session generation: the session ends after its last token
+            a.gen_n[s] = col + 1;
+            if (a.limit && col + 1 >= a.limit[s]) a.seglen_w[s] = 0;
+          }
         }
       }
       // the last CTA to finish advances the step counter (every CTA has read it by then)

@@ -90,6 +90,8 @@ struct BlockArgs {
   int n_stops;          // a chosen token among stops ends its session (seglen_w = 0, no output)
   int stops[kMaxStops];
   int32_t* seglen_w;
+  int32_t* gen_n;       // [S] tokens each session has emitted (its output column), or null: *step
+  const int32_t* limit; // [S] tokens a session may emit (it ends after the last), with gen_n
 };
 
 // sigmoidClamped (internal/quant/stream.go:128-136): saturated beyond |x| > 15, else 1/(1+e^-x)

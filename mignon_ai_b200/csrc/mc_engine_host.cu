@@ -611,6 +611,10 @@ static void build_block_args(const DevBatch& b, int P, int bi, bool fuse_head, i
       a.n_stops = b.n_stops;
       for (int k = 0; k < b.n_stops; ++k) a.stops[k] = b.stops[k];
       a.seglen_w = b.seglen;
+      if (b.per_session) {
+        a.gen_n = b.gen_n;
+        a.limit = b.limit;
+      }
     }
   }
   a.ngemms = g;
@@ -819,6 +823,10 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
   sa.advance_from_len = advance_from_len ? 1 : 0;
   sa.done = b.sel_done;  // the last block advances the step counter
   sa.n_stops = b.n_stops;
+  if (b.per_session) {
+    sa.gen_n = b.gen_n;
+    sa.limit = b.limit;
+  }
   for (int k = 0; k < b.n_stops; ++k) sa.stops[k] = b.stops[k];
   select_kernel<<<(b.S + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, s>>>(sa);
   MC_CUDA(cudaGetLastError());

@@ -258,6 +258,8 @@ struct SelectArgs {
   int32_t* done;                   // finished-block counter (zero between launches); null: no step bump
   int n_stops;                     // a chosen token among stops[0..n_stops) ends the session: no output,
   int stops[kMaxStops];            // seglen = 0 (greedyLoop's stop tokens, generate/greedy.go:75-77)
+  int32_t* gen_n;                  // [S] tokens each session has emitted (its output column), or null: step
+  const int32_t* limit;            // [S] tokens a session may emit (it ends after the last), with gen_n
 };
 
 __device__ __forceinline__ void philox4x32_10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0,
@@ -385,14 +387,19 @@ __global__ void __launch_bounds__(kSelectWarps * 32) select_kernel(const SelectA
     for (int k = 0; k < a.n_stops; ++k) stop |= tok == a.stops[k];
     if (lane == 0 && stop) a.seglen[s] = 0;  // the session ends before the stop token
     if (lane == 0 && !stop) {
+      const int col = a.gen_n ? a.gen_n[s] : step;
       a.next_tok[s] = tok;
-      if (a.out_tok) a.out_tok[(size_t)s * a.out_stride + step] = tok;
-      if (a.out_prob) a.out_prob[(size_t)s * a.out_stride + step] = (float)(1.0 / S);
-      if (a.out_logprob) a.out_logprob[(size_t)s * a.out_stride + step] = (double)lt - (double)M - log(S);
+      if (a.out_tok) a.out_tok[(size_t)s * a.out_stride + col] = tok;
+      if (a.out_prob) a.out_prob[(size_t)s * a.out_stride + col] = (float)(1.0 / S);
+      if (a.out_logprob) a.out_logprob[(size_t)s * a.out_stride + col] = (double)lt - (double)M - log(S);
       if (a.pos) {
         if (a.advance_from_len) a.pos[s] = a.pos[s] + a.seglen[s];
         else a.pos[s] = a.pos[s] + 1;
         a.seglen[s] = 1;
+      }
+      if (a.gen_n) {  // per-session generation: the session ends after its last token
+        a.gen_n[s] = col + 1;
+        if (a.limit && col + 1 >= a.limit[s]) a.seglen[s] = 0;
       }
     }
   }

@@ -8,7 +8,8 @@
 // token limit or at a stop token. The host harvests finished slots every few steps. Every token
 // is chosen by the decode-loop policy of sampleContinuation (generate/sample.go:196-247) with
 // draws keyed by the request, so a request's tokens do not depend on which slot it ran in or
-// what ran beside it.
+// what ran beside it; plain argmax (no penalty, no 3-gram block) runs on the greedy head fused
+// into the final decode launch, as mc_generate does.
 #include <deque>
 
 namespace mc {
@@ -65,6 +66,7 @@ struct mc_sched {
   mc_batch* batch = nullptr;
   mc_sampling sp{};
   int penalize_prompt = 0, max_new = 0, admit_min = 1;
+  int mode = 3;  // 0: plain greedy (argmax, no penalty, no 3-gram block) on the fused greedy head
   int n_stops = 0;
   int32_t stops[kMaxStops] = {0};
   std::deque<int64_t> queue;
@@ -135,7 +137,7 @@ int sched_admit(mc_sched* q, size_t g) {
   const int thr = 256, blocks = (S + thr - 1) / thr;
   sched_admit_kernel<<<blocks, thr, 0, st>>>(S, P, sh.sched_adm, sh.tok, sh.seglen, sh.pos, sh.gen_n, sh.next_tok);
   MC_CUDA(cudaGetLastError());
-  int rc = enqueue_forward(sh, P, 3, 0.0, 0, false, true);
+  int rc = enqueue_forward(sh, P, q->mode, 0.0, 0, false, true);
   if (rc != kOk) return rc;
   sched_resume_kernel<<<blocks, thr, 0, st>>>(S, sh.sched_adm, sh.seglen);
   MC_CUDA(cudaGetLastError());
@@ -205,6 +207,9 @@ int mc_sched_open(mc_model* model, int slots, int context_size, int max_prompt, 
   if ((st = mc_batch_open(model, slots, context_size, max_prompt, 0, &q->batch)) != kOk) return st;
   q->sp = *sp;
   q->penalize_prompt = penalize ? 1 : 0;
+  // argmax with nothing to change the logits is greedyLoop's selection: the decode steps then
+  // run the greedy head fused into the final block launch
+  q->mode = sp->temperature <= 0.001 && sp->rep_penalty <= 1.0 && !sp->ban_trigrams ? 0 : 3;
   q->max_new = max_new;
   q->admit_min = std::max(1, slots / 8);
   q->n_stops = n_stops;
@@ -221,7 +226,7 @@ int mc_sched_open(mc_model* model, int slots, int context_size, int max_prompt, 
     q->sh.push_back(std::move(ss));
     if (sh.S == 0) continue;
     MC_CUDA(cudaSetDevice(sh.m->device));
-    if ((st = ensure_step_outputs(sh, true, max_new)) != kOk) return st;
+    if ((st = ensure_step_outputs(sh, q->mode == 3, max_new)) != kOk) return st;
     if ((st = sh.alloc(sh.gen_n, (size_t)sh.S * 4)) || (st = sh.alloc(sh.limit, (size_t)sh.S * 4)) ||
         (st = sh.alloc(sh.key, (size_t)sh.S * 4)) || (st = sh.alloc(sh.sched_adm, (size_t)sh.S * 4)) ||
         (st = sh.alloc(sh.pol_prefix_len, (size_t)sh.S * 4)) || (st = sh.alloc(sh.pol_state, (size_t)sh.S * 4)))
@@ -284,7 +289,7 @@ int mc_sched_step(mc_sched* q, int steps, int* in_flight) {
       if ((st = sched_admit(q, g)) != kOk) return st;
     if (ss.busy > 0) {
       for (int k = 0; k < steps; ++k)
-        if ((st = run_graph_step(sh, 3, 0.0, 0, false)) != kOk) return st;
+        if ((st = run_graph_step(sh, q->mode, 0.0, 0, false)) != kOk) return st;
       q->n_steps += steps;
     }
   }

@@ -110,3 +110,25 @@ def test_scheduler_rejects_bad_requests():
     sched.run()
     assert len(sched.result(rid)[0]) == 2
     sched.close()
+
+
+@pytest.mark.parametrize("sp", [S(0.0, 1.0, 0, 1.0, 0, False), S(0.7, 1.0, 8, 1.0, 0, False)])
+def test_scheduler_one_token_prompts(oracle, sp):
+    """Admission passes of one-token prompts run through the decode kernels (the fused greedy head
+    for plain argmax): the per-slot token counts and limits hold there too."""
+    spec = synth.ModelSpec(**{**synth.CONFIGS[2].__dict__, "vocab": 512})
+    data = synth.build_model_file(spec)
+    om, gm = oracle.Model(data), quant.Model.decode(data)
+    n, T, key0 = 12, 9, 50
+    rng = np.random.default_rng(41)
+    prompts = rng.integers(5, spec.vocab, size=(n, 1)).astype(np.int32)
+    lens = np.ones(n, np.int32)
+    n_new = rng.integers(1, T + 1, size=n).astype(np.int32)
+    sched = quant.Scheduler(gm, 4, sp, max_prompt=4, max_new=T)
+    sched.set_admit_min(1)
+    ids = [sched.submit(prompts[i], int(n_new[i]), draw_key=key0 + i) for i in range(n)]
+    sched.run(steps_per_poll=2)
+    got = [sched.result(r)[0] for r in ids]
+    sched.close()
+    assert [len(g) for g in got] == n_new.tolist()
+    _check_against_oracle(oracle, om, sp, prompts, lens, n_new, key0, [], got, False)
