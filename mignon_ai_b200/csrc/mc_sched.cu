@@ -10,6 +10,7 @@
 // draws keyed by the request, so a request's tokens do not depend on which slot it ran in or
 // what ran beside it; plain argmax (no penalty, no 3-gram block) runs on the greedy head fused
 // into the final decode launch, as mc_generate does.
+#include <chrono>
 #include <deque>
 
 namespace mc {
@@ -58,6 +59,14 @@ struct SchedShard {
   std::vector<uint32_t> key;
   std::vector<int32_t> prefix, prefix_len;
   int busy = 0;
+  // pinned host buffers: the admission list's uploads [tok S*P | rowmap | adm | limit | key |
+  // prefix S*cap | prefix_len], and the collection's reads [seglen | gen_n] and output rows
+  cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};  // round start, admission done, decode steps done
+  bool timed = false;                                // this round recorded them
+  int32_t* h_up = nullptr;
+  int32_t* h_state = nullptr;
+  int32_t* h_tok = nullptr;
+  float* h_prob = nullptr;
 };
 
 }  // namespace
@@ -73,7 +82,17 @@ struct mc_sched {
   std::vector<SchedReq> req;
   std::vector<SchedShard> sh;
   int64_t n_prefill = 0, n_steps = 0, n_tokens = 0, n_done = 0;
-  ~mc_sched() { delete batch; }
+  double admit_us = 0, decode_us = 0, host_us = 0;  // device time of admission passes and decode steps;
+                                                    // wall time inside mc_sched_step
+  ~mc_sched() {
+    for (SchedShard& ss : sh) {
+      for (void* p : {(void*)ss.h_up, (void*)ss.h_state, (void*)ss.h_tok, (void*)ss.h_prob})
+        if (p) cudaFreeHost(p);
+      for (cudaEvent_t e : ss.ev)
+        if (e) cudaEventDestroy(e);
+    }
+    delete batch;
+  }
 };
 
 namespace {
@@ -116,24 +135,37 @@ int sched_admit(mc_sched* q, size_t g) {
     ss.prefix_len[s] = k;
   }
   if (n_adm == 0) return kOk;
-  std::vector<int32_t> tok((size_t)S * P, 0), rowmap(S);
+  // staging (the previous admission's copies finished: every round ends with a synchronizing read)
+  int32_t* tok = ss.h_up;
+  int32_t* rowmap = tok + (size_t)S * P;
+  int32_t* hadm = rowmap + S;
+  int32_t* hlim = hadm + S;
+  int32_t* hkey = hlim + S;
+  int32_t* hpre = hkey + S;
+  int32_t* hplen = hpre + (size_t)S * cap;
+  std::fill(tok, tok + (size_t)S * P, 0);
   const int spt = std::max(1, 128 / P);
   for (int s = 0; s < S; ++s) {
     const int n = std::max(adm[s], 0);
     if (n > 0) {
       const std::vector<int32_t>& pr = q->req[ss.slot_req[s]].prompt;
-      std::copy(pr.end() - n, pr.end(), tok.begin() + (size_t)s * P);
+      std::copy(pr.end() - n, pr.end(), tok + (size_t)s * P);
     }
     rowmap[s] = (s / spt) * 128 + (s % spt) * P + std::max(n - 1, 0);
   }
+  std::copy(adm.begin(), adm.end(), hadm);
+  std::copy(ss.limit.begin(), ss.limit.end(), hlim);
+  for (int s = 0; s < S; ++s) hkey[s] = (int32_t)ss.key[s];
+  std::copy(ss.prefix.begin(), ss.prefix.end(), hpre);
+  std::copy(ss.prefix_len.begin(), ss.prefix_len.end(), hplen);
   cudaStream_t st = sh.stream;
-  MC_CUDA(cudaMemcpyAsync(sh.tok, tok.data(), tok.size() * 4, cudaMemcpyHostToDevice, st));
-  MC_CUDA(cudaMemcpyAsync(sh.rowmap, rowmap.data(), (size_t)S * 4, cudaMemcpyHostToDevice, st));
-  MC_CUDA(cudaMemcpyAsync(sh.sched_adm, adm.data(), (size_t)S * 4, cudaMemcpyHostToDevice, st));
-  MC_CUDA(cudaMemcpyAsync(sh.limit, ss.limit.data(), (size_t)S * 4, cudaMemcpyHostToDevice, st));
-  MC_CUDA(cudaMemcpyAsync(sh.key, ss.key.data(), (size_t)S * 4, cudaMemcpyHostToDevice, st));
-  if (cap > 0) MC_CUDA(cudaMemcpyAsync(sh.pol_prefix, ss.prefix.data(), ss.prefix.size() * 4, cudaMemcpyHostToDevice, st));
-  MC_CUDA(cudaMemcpyAsync(sh.pol_prefix_len, ss.prefix_len.data(), (size_t)S * 4, cudaMemcpyHostToDevice, st));
+  MC_CUDA(cudaMemcpyAsync(sh.tok, tok, (size_t)S * P * 4, cudaMemcpyHostToDevice, st));
+  MC_CUDA(cudaMemcpyAsync(sh.rowmap, rowmap, (size_t)S * 4, cudaMemcpyHostToDevice, st));
+  MC_CUDA(cudaMemcpyAsync(sh.sched_adm, hadm, (size_t)S * 4, cudaMemcpyHostToDevice, st));
+  MC_CUDA(cudaMemcpyAsync(sh.limit, hlim, (size_t)S * 4, cudaMemcpyHostToDevice, st));
+  MC_CUDA(cudaMemcpyAsync(sh.key, hkey, (size_t)S * 4, cudaMemcpyHostToDevice, st));
+  if (cap > 0) MC_CUDA(cudaMemcpyAsync(sh.pol_prefix, hpre, (size_t)S * cap * 4, cudaMemcpyHostToDevice, st));
+  MC_CUDA(cudaMemcpyAsync(sh.pol_prefix_len, hplen, (size_t)S * 4, cudaMemcpyHostToDevice, st));
   const int thr = 256, blocks = (S + thr - 1) / thr;
   sched_admit_kernel<<<blocks, thr, 0, st>>>(S, P, sh.sched_adm, sh.tok, sh.seglen, sh.pos, sh.gen_n, sh.next_tok);
   MC_CUDA(cudaGetLastError());
@@ -151,28 +183,35 @@ int sched_harvest(mc_sched* q, size_t g) {
   SchedShard& ss = q->sh[g];
   DevBatch& sh = *q->batch->shard[g];
   const int S = sh.S;
-  std::vector<int32_t> seglen(S), gen_n(S);
-  MC_CUDA(cudaMemcpyAsync(seglen.data(), sh.seglen, (size_t)S * 4, cudaMemcpyDeviceToHost, sh.stream));
-  MC_CUDA(cudaMemcpyAsync(gen_n.data(), sh.gen_n, (size_t)S * 4, cudaMemcpyDeviceToHost, sh.stream));
+  int32_t* seglen = ss.h_state;
+  int32_t* gen_n = seglen + S;
+  MC_CUDA(cudaMemcpyAsync(seglen, sh.seglen, (size_t)S * 4, cudaMemcpyDeviceToHost, sh.stream));
+  MC_CUDA(cudaMemcpyAsync(gen_n, sh.gen_n, (size_t)S * 4, cudaMemcpyDeviceToHost, sh.stream));
   int st = check_device_error(sh.stream);  // synchronizes the stream
   if (st != kOk) return st;
+  if (ss.timed) {
+    float a = 0.f, d = 0.f;
+    MC_CUDA(cudaEventElapsedTime(&a, ss.ev[0], ss.ev[1]));
+    MC_CUDA(cudaEventElapsedTime(&d, ss.ev[1], ss.ev[2]));
+    q->admit_us += 1e3 * a;
+    q->decode_us += 1e3 * d;
+    ss.timed = false;
+  }
   std::vector<int> done;
   for (int s = 0; s < S; ++s)
     if (ss.slot_req[s] >= 0 && seglen[s] <= 0) done.push_back(s);
   if (done.empty()) return kOk;
   const int W = q->max_new;
-  std::vector<int32_t> tok((size_t)S * W);
-  std::vector<float> prob((size_t)S * W);
-  MC_CUDA(cudaMemcpy2DAsync(tok.data(), (size_t)W * 4, sh.out_tok, (size_t)sh.out_stride * 4, (size_t)W * 4, S,
+  MC_CUDA(cudaMemcpy2DAsync(ss.h_tok, (size_t)W * 4, sh.out_tok, (size_t)sh.out_stride * 4, (size_t)W * 4, S,
                             cudaMemcpyDeviceToHost, sh.stream));
-  MC_CUDA(cudaMemcpy2DAsync(prob.data(), (size_t)W * 4, sh.out_prob, (size_t)sh.out_stride * 4, (size_t)W * 4, S,
+  MC_CUDA(cudaMemcpy2DAsync(ss.h_prob, (size_t)W * 4, sh.out_prob, (size_t)sh.out_stride * 4, (size_t)W * 4, S,
                             cudaMemcpyDeviceToHost, sh.stream));
   MC_CUDA(cudaStreamSynchronize(sh.stream));
   for (int s : done) {
     SchedReq& r = q->req[ss.slot_req[s]];
     const int n = std::min(std::max(gen_n[s], 0), r.n_new);
-    r.tokens.assign(tok.begin() + (size_t)s * W, tok.begin() + (size_t)s * W + n);
-    r.probs.assign(prob.begin() + (size_t)s * W, prob.begin() + (size_t)s * W + n);
+    r.tokens.assign(ss.h_tok + (size_t)s * W, ss.h_tok + (size_t)s * W + n);
+    r.probs.assign(ss.h_prob + (size_t)s * W, ss.h_prob + (size_t)s * W + n);
     r.state = 2;
     ss.slot_req[s] = -1;
     --ss.busy;
@@ -226,6 +265,13 @@ int mc_sched_open(mc_model* model, int slots, int context_size, int max_prompt, 
     q->sh.push_back(std::move(ss));
     if (sh.S == 0) continue;
     MC_CUDA(cudaSetDevice(sh.m->device));
+    SchedShard& sp_ = q->sh.back();
+    const size_t up = (size_t)sh.S * (sh.pmax + 5 + cap + 1);
+    MC_CUDA(cudaHostAlloc(&sp_.h_up, up * 4, cudaHostAllocDefault));
+    for (cudaEvent_t& e : sp_.ev) MC_CUDA(cudaEventCreate(&e));
+    MC_CUDA(cudaHostAlloc(&sp_.h_state, (size_t)sh.S * 2 * 4, cudaHostAllocDefault));
+    MC_CUDA(cudaHostAlloc(&sp_.h_tok, (size_t)sh.S * max_new * 4, cudaHostAllocDefault));
+    MC_CUDA(cudaHostAlloc(&sp_.h_prob, (size_t)sh.S * max_new * 4, cudaHostAllocDefault));
     if ((st = ensure_step_outputs(sh, q->mode == 3, max_new)) != kOk) return st;
     if ((st = sh.alloc(sh.gen_n, (size_t)sh.S * 4)) || (st = sh.alloc(sh.limit, (size_t)sh.S * 4)) ||
         (st = sh.alloc(sh.key, (size_t)sh.S * 4)) || (st = sh.alloc(sh.sched_adm, (size_t)sh.S * 4)) ||
@@ -279,19 +325,24 @@ int mc_sched_step(mc_sched* q, int steps, int* in_flight) {
   clear_error();
   if (!q || steps < 1) return set_error(kInvalidArgument, "mc_sched_step: bad arguments");
   int st;
+  const auto t0 = std::chrono::steady_clock::now();
   for (size_t g = 0; g < q->sh.size(); ++g) {
     DevBatch& sh = *q->batch->shard[g];
     SchedShard& ss = q->sh[g];
     if (sh.S == 0) continue;
     MC_CUDA(cudaSetDevice(sh.m->device));
+    MC_CUDA(cudaEventRecord(ss.ev[0], sh.stream));
     const int free_slots = sh.S - ss.busy;
     if (!q->queue.empty() && free_slots > 0 && (free_slots >= q->admit_min || ss.busy == 0))
       if ((st = sched_admit(q, g)) != kOk) return st;
+    MC_CUDA(cudaEventRecord(ss.ev[1], sh.stream));
     if (ss.busy > 0) {
       for (int k = 0; k < steps; ++k)
         if ((st = run_graph_step(sh, q->mode, 0.0, 0, false)) != kOk) return st;
       q->n_steps += steps;
     }
+    MC_CUDA(cudaEventRecord(ss.ev[2], sh.stream));
+    ss.timed = true;
   }
   for (size_t g = 0; g < q->sh.size(); ++g) {
     DevBatch& sh = *q->batch->shard[g];
@@ -299,6 +350,7 @@ int mc_sched_step(mc_sched* q, int steps, int* in_flight) {
     MC_CUDA(cudaSetDevice(sh.m->device));
     if ((st = sched_harvest(q, g)) != kOk) return st;
   }
+  q->host_us += std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
   if (in_flight) *in_flight = sched_in_flight(q);
   return kOk;
 }
@@ -335,6 +387,9 @@ int mc_sched_stats(const mc_sched* q, int64_t* out) {
   out[2] = q->n_tokens;
   out[3] = q->n_done;
   out[4] = sched_in_flight(q);
+  out[5] = (int64_t)q->admit_us;
+  out[6] = (int64_t)q->decode_us;
+  out[7] = (int64_t)q->host_us;
   return kOk;
 }
 
