@@ -90,6 +90,14 @@ int mc_close(mc_ctx* ctx);
  * weights to every device of the context. Replaces quant.Decode (internal/quant/checkpoint.go:162)
  * followed by quant.NewModel (model.go:91). Damaged files fail with MC_BAD_MODEL. */
 int mc_load_model(mc_ctx* ctx, const uint8_t* data, size_t n, mc_model** out);
+/* A full-precision (float32) model file instead of an INT8 one: pkg/model.Decode of a binfmt
+ * kind-1 file (pkg/model/model.go:85-103; checkpoint.Encode, internal/checkpoint/checkpoint.go:86-94)
+ * followed by quant.Quantize (internal/quant/convert.go:8-98), the quantization on the context's
+ * first device: per-matrix max|w| and NewTensorF32's rounding (internal/quant/tensor.go:12-42)
+ * run as kernels over the uploaded weight vector. max_context is Quantize's maxContext (<= 0: the
+ * file's context_size, or 64 when it has none, as pkg/model normalizes it). The result is the
+ * model an INT8 file of the same weights would give. */
+int mc_load_model_full(mc_ctx* ctx, const uint8_t* data, size_t n, int max_context, mc_model** out);
 int mc_model_free(mc_model* model);
 
 /* out[10] = vocab, state, hidden, blocks, max_context, attn_heads, attn_window, total rule steps,

@@ -11,3 +11,4 @@
 #include "mc_engine_host.cu"
 #include "mc_api.cu"
 #include "mc_sched.cu"
+#include "mc_convert.cu"

@@ -27,6 +27,7 @@ _lib.register({
     "mc_open": [c_vp, ctypes.POINTER(c_vp)],
     "mc_close": [c_vp],
     "mc_load_model": [c_vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(c_vp)],
+    "mc_load_model_full": [c_vp, ctypes.c_char_p, ctypes.c_size_t, _i, ctypes.POINTER(c_vp)],
     "mc_model_free": [c_vp],
     "mc_model_info": [c_vp, c_vp],
     "mc_batch_open": [c_vp, _i, _i, _i, _i, ctypes.POINTER(c_vp)],
@@ -153,6 +154,16 @@ class Model:
     def load(cls, path: str, ctx: Optional[Context] = None) -> "Model":
         with open(path, "rb") as f:
             return cls.decode(f.read(), ctx)
+
+    @classmethod
+    def decode_full(cls, data: bytes, max_context: int = 0, ctx: Optional[Context] = None) -> "Model":
+        """A full-precision model file quantized on the GPU: pkg/model.Decode then
+        quant.Quantize (internal/quant/convert.go:8-98) with maxContext = max_context (<= 0: the
+        file's context size)."""
+        ctx = ctx or default_context()
+        h = c_vp()
+        _lib.check(_lib.lib().mc_load_model_full(ctx._h, data, len(data), max_context, ctypes.byref(h)))
+        return cls(h, ctx)
 
     def close(self):
         if getattr(self, "_h", None):

@@ -434,3 +434,138 @@ def encode_model_json(m: QModel, metadata: Optional[dict] = None) -> bytes:
           "head_b": f(m.head_b), "vocab": None, "metadata": meta}
     # float32 values printed with 9 significant digits round-trip exactly.
     return json.dumps(cp, default=float).encode()
+
+
+# ---------------------------------------------------------------------------------------------
+# Full-precision model files (binfmt kind 1: internal/checkpoint/checkpoint.go:86-94) and the
+# flat weight layout of ca.NewLayout (internal/ca/layout.go:103-161)
+# ---------------------------------------------------------------------------------------------
+
+def layout_block_configs(num_blocks: int, steps: int, dilation_base: int) -> List[BlockConfig]:
+    """BuildBlockConfigs as NewLayout stores it: a base <= 1 becomes 2, an initial dilation < 1
+    becomes 1 (internal/ca/layout.go:115-122)."""
+    return [BlockConfig(b.steps, b.dilation_base if b.dilation_base > 1 else 2, max(1, b.initial_dilation))
+            for b in build_block_configs(num_blocks, steps, dilation_base)]
+
+
+@dataclasses.dataclass
+class FModel:
+    """A full-precision model: its flat weight vector in ca.NewLayout order and its shape."""
+    vocab: int
+    state: int
+    hidden: int
+    blocks: int
+    steps: int
+    dilation_base: int
+    tied: bool
+    attn_heads: int
+    attn_window: int
+    context: int
+    weights: np.ndarray  # float32
+
+
+def full_layout(vocab: int, state: int, hidden: int, configs: Sequence[BlockConfig], tied: bool, attn_heads: int):
+    """Offsets of ca.NewLayout: (block offsets [(layer1, layer2, gamma, select, attn)], final norm
+    offset, head offset, total parameters)."""
+    D, H, V = state, hidden, vocab
+    in_dim = 3 * D
+    l1, l2 = 2 * H * (in_dim + 1), 2 * D * (H + 1)
+    cur = V * D
+    blocks = []
+    for _ in configs:
+        sel = cur + l1 + l2 + D
+        extra = sel + D * D
+        attn = -1
+        if attn_heads > 0:
+            attn = extra
+            extra += D + 4 * D * D
+        blocks.append((cur, cur + l1, cur + l1 + l2, sel, attn))
+        cur = extra
+    final_norm = cur
+    cur += D
+    head = cur
+    total = cur + (V if tied else V * (D + 1))
+    return blocks, final_norm, head, total
+
+
+def build_float_model(vocab: int, state: int, hidden: int, blocks: int, steps: int, dilation_base: int = 2,
+                      tied: bool = True, attn_heads: int = 0, attn_window: int = 0, context: int = 64,
+                      seed: int = 11, scale: float = 0.5) -> FModel:
+    """Every parameter uniform in [-scale, scale) from Philox, one stream per parameter slot."""
+    configs = layout_block_configs(blocks, steps, dilation_base)
+    total = full_layout(vocab, state, hidden, configs, tied, attn_heads)[3]
+    w = philox_words(total, seed, 0x46554C4C).astype(np.float64)
+    weights = ((((w + 0.5) * (2.0 ** -32)) * 2.0 - 1.0) * scale).astype(np.float32)
+    return FModel(vocab, state, hidden, blocks, steps, dilation_base, tied, attn_heads, attn_window, context, weights)
+
+
+def float_model_parts(fm: FModel) -> dict:
+    """The parameters quant.Quantize reads from the flat vector (internal/quant/convert.go:8-98):
+    'embed', per block 'w1', 'b1', 'w2', 'b2', 'gamma', 'wsel' (+ 'attn_norm', 'qkv', 'out'),
+    'final_norm', 'head_w' (untied) and 'head_b'; W1 and W2 rows carry their bias after their
+    weights, and so do the rows of an untied head."""
+    D, H, V = fm.state, fm.hidden, fm.vocab
+    w = fm.weights
+    configs = layout_block_configs(fm.blocks, fm.steps, fm.dilation_base)
+    offs, fno, ho, total = full_layout(V, D, H, configs, fm.tied, fm.attn_heads)
+    if w.size != total:
+        raise ValueError("architecture mismatch: %d weights, the model needs %d" % (w.size, total))
+
+    def rows(off, n, width):  # n rows of `width` weights followed by one bias each
+        r = w[off:off + n * (width + 1)].reshape(n, width + 1)
+        return r[:, :width].reshape(-1), r[:, width].copy()
+
+    parts = {"embed": w[:V * D], "configs": configs, "blocks": []}
+    for o1, o2, og, osel, oa in offs:
+        b = {}
+        b["w1"], b["b1"] = rows(o1, 2 * H, 3 * D)
+        b["w2"], b["b2"] = rows(o2, 2 * D, H)
+        b["gamma"], b["wsel"] = w[og:og + D], w[osel:osel + D * D]
+        if oa >= 0:
+            b["attn_norm"] = w[oa:oa + D]
+            b["qkv"] = w[oa + D:oa + D + 3 * D * D]
+            b["out"] = w[oa + D + 3 * D * D:oa + D + 4 * D * D]
+        parts["blocks"].append(b)
+    parts["final_norm"] = w[fno:fno + D]
+    if fm.tied:
+        parts["head_b"] = w[ho:ho + V]
+    else:
+        parts["head_w"], parts["head_b"] = rows(ho, V, D)
+    return parts
+
+
+def quantize_float_model(fm: FModel, max_context: int = 0) -> QModel:
+    """quant.Quantize (internal/quant/convert.go:8-98) of a full-precision model, with the
+    restated NewTensorF32; max_context <= 0 takes the model's context."""
+    p = float_model_parts(fm)
+
+    def qt(a):
+        d, sc = quantize_tensor(np.ascontiguousarray(a, np.float32))
+        return QTensor(d, sc)
+
+    qblocks = []
+    for bc, b in zip(p["configs"], p["blocks"]):
+        qb = QBlock(bc, qt(b["w1"]), b["b1"].copy(), qt(b["w2"]), b["b2"].copy(), b["gamma"].copy(), qt(b["wsel"]))
+        if "qkv" in b:
+            qb.attn_norm, qb.qkv, qb.out = b["attn_norm"].copy(), qt(b["qkv"]), qt(b["out"])
+        qblocks.append(qb)
+    head_w = qt(p["head_w"]) if not fm.tied else QTensor(np.zeros(0, np.int8), np.float32(0.0))
+    return QModel(vocab=fm.vocab, state=fm.state, hidden=fm.hidden, tied=fm.tied, embed=qt(p["embed"]),
+                  blocks=qblocks, final_norm=p["final_norm"].copy(), head_w=head_w, head_b=p["head_b"].copy(),
+                  context=max_context if max_context > 0 else fm.context, attn_heads=fm.attn_heads,
+                  attn_window=fm.attn_window)
+
+
+def encode_full_model(fm: FModel) -> bytes:
+    """The binary full-precision model file (checkpoint.Encode): header
+    ``json.Marshal(File{Vocab, Merges, Metadata})`` with a placeholder vocabulary of the model's
+    size, then one float32 array of all weights."""
+    meta = {"blocks": fm.blocks, "state_size": fm.state, "hidden_size": fm.hidden, "steps": fm.steps,
+            "dilation_base": fm.dilation_base, "context_size": fm.context, "tied_embed": fm.tied,
+            "attn_heads": fm.attn_heads, "attn_window": fm.attn_window, "tokenizer_version": 1}
+    meta_s = "{" + ",".join('"%s":%s' % (k, json.dumps(v)) for k, v in meta.items() if v) + "}"
+    vocab = ["<PAD>", "<UNK>", "<USER>", "<BOT>", "<EOS>"] + ["t%d" % i for i in range(5, fm.vocab)]
+    header = ('{"weights":null,"vocab":%s,"metadata":%s}' % (json.dumps(vocab[:fm.vocab]), meta_s)).encode()
+    w = np.ascontiguousarray(fm.weights, "<f4")
+    return b"".join([b"MGNN", struct.pack("<HBB", 1, 1, 0), struct.pack("<I", len(header)), header,
+                     struct.pack("<I", w.size), w.tobytes()])
