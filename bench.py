@@ -292,6 +292,133 @@ def run_score(args):
     return 0
 
 
+def _policy_knobs():
+    from mignon_ai_b200 import quant
+    # the reference's benchmark knobs for SampleRawLogitsAdvanced (sample_test.go:47-59) with
+    # sampleContinuation's repetition window and 3-gram block
+    return quant.Sampling(0.7, 1.2, 40, 0.9, 6, True)
+
+
+def run_policy(args):
+    """Config-2 generation with the whole decode-loop policy (mc_generate_policy): 4096 sessions,
+    48-token prompts, 80 tokens each, every token chosen by sampleContinuation's policy on the
+    device. Timed with CUDA events around the host API call; the CPU restatement
+    (or_generate_policy) generates a sample beside it."""
+    import torch
+    from mignon_ai_b200 import quant, synth
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle
+    spec = synth.CONFIGS[2]
+    n = args.sessions
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    data = synth.build_model_file(spec)
+    ctx = quant.Context((0,))
+    model = quant.Model.decode(data, ctx)
+    prompts = synth.prompts_uniform_fast(n, PROMPT, spec.vocab, seed=2)
+    lens = np.full(n, PROMPT, np.int32)
+    batch = model.new_batch(n, 0, PROMPT)
+    sp = _policy_knobs()
+    for _ in range(max(1, args.warmup)):
+        batch.generate_policy(prompts, lens, NEW, sp, penalize_prompt=True)
+    steps = max(1, args.steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record()
+    for _ in range(steps):
+        toks, _, out_lens = batch.generate_policy(prompts, lens, NEW, sp, penalize_prompt=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    value = int(out_lens.sum()) / (ms / 1000.0)
+    line = {"metric": "generated tokens/s (config-2 sessions, sampleContinuation policy)", "value": value,
+            "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": max(1, args.warmup), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "f64 selection over f32 logits",
+            "data": "synthetic",
+            "config": {"workload": "config2 model, %d sessions x (%d-token prompt + %d tokens), T 0.7, repetition "
+                                   "penalty 1.2 over the last 6 tokens of prompt ++ generated, top-k 40, top-p 0.9, "
+                                   "3-gram block" % (n, PROMPT, NEW),
+                       "timing": "the host API call (prompts in, tokens out) per step"}}
+    if not args.no_cpu_baseline:
+        cores = os.cpu_count() or 1
+        k = max(cores, 32)
+        om = pyoracle.Model(data)
+        osp = pyoracle.Sampling(sp.temperature, sp.rep_penalty, sp.top_k, sp.top_p, sp.rep_window, sp.ban_trigrams)
+        t0 = time.perf_counter()
+        _, _, ol, _ = om.generate_policy(prompts[:k], lens[:k], NEW, osp, penalize_prompt=True, nthreads=cores)
+        cpu_s = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": int(ol.sum()) / cpu_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+                                "sample": "%d sessions of the workload" % k}
+    print(json.dumps(line))
+    batch.close()
+    model.close()
+    ctx.close()
+    return 0
+
+
+def run_scheduler(args):
+    """Continuous batching (mc_sched_*) on the config-2 model: 2 x slots requests with prompts of
+    16..48 tokens and token limits of 16..80, submitted up front and run to completion through
+    `slots` (= --sessions) session slots; plain greedy, then the benchmark policy knobs. Against
+    two static batches of the same requests (every session of a static batch runs the longest
+    limit). Wall time of mc_sched_run, which returns once every request is done."""
+    from mignon_ai_b200 import quant, synth
+    spec = synth.CONFIGS[2]
+    slots = args.sessions
+    n_req = 2 * slots
+    rng = np.random.default_rng(2)
+    lens = rng.integers(16, PROMPT + 1, size=n_req).astype(np.int32)
+    n_new = rng.integers(16, NEW + 1, size=n_req).astype(np.int32)
+    prompts = synth.prompts_uniform_fast(n_req, PROMPT, spec.vocab, seed=2)
+    ctx = quant.Context((0,))
+    model = quant.Model.decode(synth.build_model_file(spec), ctx)
+    res = {}
+    for name, sp in (("greedy", quant.Sampling(0.0, 1.0, 0, 1.0, 0, False)), ("policy", _policy_knobs())):
+        sched = quant.Scheduler(model, slots, sp, max_prompt=PROMPT, max_new=NEW)
+        for i in range(64):  # warm-up: allocation and graph capture
+            sched.submit(prompts[i, :lens[i]], 4)
+        sched.run(16)
+        base = sched.stats()
+        for i in range(n_req):
+            sched.submit(prompts[i, :lens[i]], int(n_new[i]), draw_key=i)
+        t0 = time.perf_counter()
+        sched.run(16)
+        dt = time.perf_counter() - t0
+        st = sched.stats()
+        sched.close()
+        res[name] = {"tokens_per_s": (st["tokens"] - base["tokens"]) / dt, "ms": dt * 1e3,
+                     "tokens": st["tokens"] - base["tokens"],
+                     "prefill_passes": st["prefill_passes"] - base["prefill_passes"],
+                     "decode_steps": st["decode_steps"] - base["decode_steps"],
+                     "admit_device_ms": (st["admit_us"] - base["admit_us"]) / 1e3,
+                     "decode_device_ms": (st["decode_us"] - base["decode_us"]) / 1e3}
+    batch = model.new_batch(slots, 0, PROMPT)
+    batch.generate(prompts[:slots], lens[:slots], 4)
+    useful = int(n_new.sum())
+    static = {}
+    for name in ("greedy", "policy"):
+        t0 = time.perf_counter()
+        for h in range(2):
+            sl = slice(h * slots, (h + 1) * slots)
+            if name == "greedy":
+                batch.generate(prompts[sl], lens[sl], NEW)
+            else:
+                batch.generate_policy(prompts[sl], lens[sl], NEW, _policy_knobs())
+        dt = time.perf_counter() - t0
+        static[name] = {"requested_tokens_per_s": useful / dt, "ms": dt * 1e3}
+    line = {"metric": "generated tokens/s (continuous batching, config-2 model)",
+            "value": res["greedy"]["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True,
+            "scaling": "none", "vs_baseline": None, "data": "synthetic",
+            "config": {"workload": "%d slots, %d requests: prompts 16..%d tokens, token limits 16..%d (seed 2)" % (
+                slots, n_req, PROMPT, NEW), "timing": "wall time of mc_sched_run (requests submitted before)"},
+            "scheduler": res, "static_batches": static}
+    print(json.dumps(line))
+    batch.close()
+    model.close()
+    ctx.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -302,14 +429,19 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true",
                     help="profiling case: one generation job, no timing, e2e, profile or CPU baseline")
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemm", "score"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemm", "score", "policy", "scheduler"],
                     help="decode: the config-2 generation job (the headline); gemm: the config-5 INT8 GEMM "
-                         "sweep; score: the config-4 scoring pass")
+                         "sweep; score: the config-4 scoring pass; policy: config-2 generation under the whole "
+                         "sampling policy; scheduler: continuous batching of ragged requests")
     args = ap.parse_args()
     if args.workload == "gemm":
         return run_gemm_sweep(args)
     if args.workload == "score":
         return run_score(args)
+    if args.workload == "policy":
+        return run_policy(args)
+    if args.workload == "scheduler":
+        return run_scheduler(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
