@@ -10,6 +10,7 @@
 // draws keyed by the request, so a request's tokens do not depend on which slot it ran in or
 // what ran beside it; plain argmax (no penalty, no 3-gram block) runs on the greedy head fused
 // into the final decode launch, as mc_generate does.
+#include <algorithm>
 #include <chrono>
 #include <deque>
 
@@ -103,24 +104,33 @@ int sched_admit(mc_sched* q, size_t g) {
   DevBatch& sh = *q->batch->shard[g];
   const int S = sh.S, window = q->batch->window, cap = sh.pol_prefix_cap;
   std::vector<int32_t> adm(S, 0);
-  int P = 0, n_adm = 0;
+  std::vector<int> free_slots;
   for (int s = 0; s < S; ++s) {
-    if (ss.slot_req[s] >= 0) {
-      adm[s] = -1;
+    if (ss.slot_req[s] >= 0) adm[s] = -1;
+    else free_slots.push_back(s);
+  }
+  // the requests this pass admits, in queue order (an empty prompt finishes at once: Prefill of
+  // nothing returns no logits, so nothing is generated)
+  std::vector<int64_t> take;
+  while (!q->queue.empty() && take.size() < free_slots.size()) {
+    const int64_t c = q->queue.front();
+    q->queue.pop_front();
+    if (q->req[c].prompt.empty()) {
+      q->req[c].state = 2;
+      ++q->n_done;
       continue;
     }
-    int64_t id = -1;
-    while (!q->queue.empty() && id < 0) {
-      const int64_t c = q->queue.front();
-      q->queue.pop_front();
-      if (q->req[c].prompt.empty()) {  // Prefill of nothing returns no logits: nothing is generated
-        q->req[c].state = 2;
-        ++q->n_done;
-        continue;
-      }
-      id = c;
-    }
-    if (id < 0) continue;
+    take.push_back(c);
+  }
+  // Requests with similar token limits go to neighbouring slots: they tend to finish together, so
+  // later passes find whole prefill tiles free instead of one slot in each. A request's tokens do
+  // not depend on its slot.
+  std::stable_sort(take.begin(), take.end(),
+                   [&](int64_t x, int64_t y) { return q->req[x].n_new < q->req[y].n_new; });
+  int P = 0, n_adm = 0;
+  for (size_t i = 0; i < take.size(); ++i) {
+    const int s = free_slots[i];
+    const int64_t id = take[i];
     SchedReq& r = q->req[id];
     const int n = std::min((int)r.prompt.size(), window);
     r.state = 1;
