@@ -19,13 +19,14 @@
 namespace mc {
 namespace eng {
 
-constexpr int kPolicyThreads = 256;
+constexpr int kPolicyThreads = 128;
 constexpr int kPolicyWarps = kPolicyThreads / 32;
 constexpr int kPolicyMaxVocab = 16384;  // the sort keys and indices of a row fill 192 KB of shared memory
 constexpr int kPolicyMaxK = 1024;       // top-k up to this selects its candidates instead of sorting all
 
 struct PolicyArgs {
   int n_rows, V, vp;                  // vp: V rounded up to a power of two (the sort's size)
+  int kp;                             // top_k rounded up to a power of two (the candidates' sort)
   const float* logits;                // [n_rows][V]
   double temperature, rep_penalty, top_p;
   int top_k, rep_window, ban_trigrams;
@@ -252,9 +253,10 @@ __device__ __forceinline__ void pol_radix_select(const double* p, int n, int k, 
 __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_constant__ PolicyArgs a) {
   extern __shared__ __align__(16) unsigned char pol_smem[];
   double* key = reinterpret_cast<double*>(pol_smem);
+  // after the row's keys: its indices when the whole row is sorted, or the top-k candidates
   int32_t* idx = reinterpret_cast<int32_t*>(key + a.vp);
-  double* ckey = reinterpret_cast<double*>(idx + a.vp);  // top-k candidates [kPolicyMaxK]
-  int32_t* cidx = reinterpret_cast<int32_t*>(ckey + kPolicyMaxK);
+  double* ckey = key + a.vp;
+  int32_t* cidx = reinterpret_cast<int32_t*>(ckey + a.kp);
   __shared__ double red_d[kPolicyWarps];
   __shared__ int red_i[kPolicyWarps];
   __shared__ int hist[256];
@@ -376,8 +378,7 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
               cidx[at] = i;
             }
           }
-          int kp = 1;
-          while (kp < K) kp <<= 1;
+          const int kp = a.kp;
           for (int j = K + tid; j < kp; j += kPolicyThreads) {
             ckey[j] = -1.0;
             cidx[j] = 0x7fffffff;
@@ -464,14 +465,27 @@ inline int policy_vp(int V) {
   return vp;
 }
 
-inline size_t policy_smem(int V) {
-  return ((size_t)policy_vp(V) + kPolicyMaxK) * (sizeof(double) + sizeof(int32_t));
+// The largest launch's shared memory (a whole-row sort at the largest vocabulary).
+inline size_t policy_smem(int V) { return (size_t)policy_vp(V) * (sizeof(double) + sizeof(int32_t)); }
+
+// Shared memory of one launch: the row's keys, then the indices of a whole-row sort or the top-k
+// candidates (keys and indices), by the branch the kernel takes for these knobs.
+inline size_t policy_smem_for(const PolicyArgs& a) {
+  const bool draw = a.temperature > 0.001;
+  const bool truncated = draw && !(a.top_k <= 0 && a.top_p >= 0.9999);
+  const bool select = truncated && a.top_k > 0 && a.top_k < a.V && a.top_k <= kPolicyMaxK;
+  size_t b = (size_t)a.vp * sizeof(double);
+  if (select) b += (size_t)a.kp * (sizeof(double) + sizeof(int32_t));
+  else if (truncated) b += (size_t)a.vp * sizeof(int32_t);
+  return b;
 }
 
 int launch_policy(PolicyArgs& a, cudaStream_t s) {
   if (a.V < 1 || a.V > kPolicyMaxVocab) return set_error(kUnsupported, "sampling policy: vocabulary above 16384");
   a.vp = policy_vp(a.V);
-  const size_t smem = policy_smem(a.V);  // the kernel's shared-memory limit is raised once per device
+  a.kp = 1;
+  while (a.kp < a.top_k && a.kp < kPolicyMaxK) a.kp <<= 1;
+  const size_t smem = policy_smem_for(a);  // within the limit raised once per device (policy_smem)
   if (a.n_rows > 0) policy_kernel<<<a.n_rows, kPolicyThreads, smem, s>>>(a);
   MC_CUDA(cudaGetLastError());
   return kOk;
