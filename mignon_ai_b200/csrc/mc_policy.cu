@@ -27,6 +27,7 @@ constexpr int kPolicyMaxK = 1024;       // top-k up to this selects its candidat
 struct PolicyArgs {
   int n_rows, V, vp;                  // vp: V rounded up to a power of two (the sort's size)
   int kp;                             // top_k rounded up to a power of two (the candidates' sort)
+  int kcap;                           // candidates the shared memory holds (a power of two >= kp)
   const float* logits;                // [n_rows][V]
   double temperature, rep_penalty, top_p;
   int top_k, rep_window, ban_trigrams;
@@ -250,13 +251,61 @@ __device__ __forceinline__ void pol_radix_select(const double* p, int n, int k, 
   *r_out = r;
 }
 
+// The k-th largest of the float keys rz(p[i]) (p rounded toward zero to float32, whose bit
+// patterns order like the values), by the same radix select over 32 bits: four passes.
+__device__ __forceinline__ unsigned int pol_radix_select32(const double* p, int n, int k, int* hist, int* pick) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  unsigned int prefix = 0u, mask = 0u;
+  int r = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = tid; b < 256; b += kPolicyThreads) hist[b] = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += kPolicyThreads) {
+      const unsigned int kb = __float_as_uint(__double2float_rz(p[i]));
+      if ((kb & mask) == prefix) atomicAdd(&hist[(kb >> shift) & 255], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int c[8], tot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hist[255 - 8 * lane - j];
+        tot += c[j];
+      }
+      int incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      int acc = incl - tot;
+      if (acc < r && r <= incl) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (acc < r && r <= acc + c[j]) {
+            pick[0] = 255 - 8 * lane - j;
+            pick[1] = acc;
+          }
+          acc += c[j];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= (unsigned int)pick[0] << shift;
+    mask |= 255u << shift;
+    r -= pick[1];
+    __syncthreads();
+  }
+  return prefix;
+}
+
 __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_constant__ PolicyArgs a) {
   extern __shared__ __align__(16) unsigned char pol_smem[];
   double* key = reinterpret_cast<double*>(pol_smem);
   // after the row's keys: its indices when the whole row is sorted, or the top-k candidates
   int32_t* idx = reinterpret_cast<int32_t*>(key + a.vp);
   double* ckey = key + a.vp;
-  int32_t* cidx = reinterpret_cast<int32_t*>(ckey + a.kp);
+  int32_t* cidx = reinterpret_cast<int32_t*>(ckey + a.kcap);
   __shared__ double red_d[kPolicyWarps];
   __shared__ int red_i[kPolicyWarps];
   __shared__ int hist[256];
@@ -358,30 +407,57 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
         int active;
         if (a.top_k > 0 && a.top_k < V && a.top_k <= kPolicyMaxK) {
           const int K = a.top_k;
-          unsigned long long tau;
-          int r;
-          pol_radix_select(key, V, K, &tau, &r, hist, pick);
-          // the candidates: entries above tau, and the first r entries equal to it by index
           const int c = (V + kPolicyThreads - 1) / kPolicyThreads;
           const int lo = min(V, tid * c), hi = min(V, lo + c);
-          int eq = 0;
-          for (int i = lo; i < hi; ++i) eq += (unsigned long long)__double_as_longlong(key[i]) == tau;
-          int rank = pol_block_excl_scan(eq, red_i);
-          if (tid == 0) pick[0] = 0;
+          // (i) the entries whose float key reaches the k-th largest float key F hold the top k:
+          // an entry below F ranks behind the >= k entries at or above it. Their number C is k
+          // unless float keys tie at F; up to the candidate capacity they are sorted exactly.
+          const unsigned int F = pol_radix_select32(key, V, K, hist, pick);
+          int cnt = 0;
+          for (int i = lo; i < hi; ++i) cnt += __float_as_uint(__double2float_rz(key[i])) >= F;
+          int base = pol_block_excl_scan(cnt, red_i);
+          if (tid == kPolicyThreads - 1) pick[0] = base + cnt;
           __syncthreads();
-          for (int i = lo; i < hi; ++i) {
-            const unsigned long long kb = (unsigned long long)__double_as_longlong(key[i]);
-            const bool take = kb > tau || (kb == tau && rank++ < r);
-            if (take) {
-              const int at = atomicAdd(&pick[0], 1);
-              ckey[at] = key[i];
-              cidx[at] = i;
+          const int C = pick[0];
+          __syncthreads();
+          int kp;
+          if (C <= a.kcap) {
+            for (int i = lo; i < hi; ++i)
+              if (__float_as_uint(__double2float_rz(key[i])) >= F) {
+                ckey[base] = key[i];
+                cidx[base++] = i;
+              }
+            kp = 1;
+            while (kp < C) kp <<= 1;
+            for (int j = C + tid; j < kp; j += kPolicyThreads) {
+              ckey[j] = -1.0;
+              cidx[j] = 0x7fffffff;
             }
-          }
-          const int kp = a.kp;
-          for (int j = K + tid; j < kp; j += kPolicyThreads) {
-            ckey[j] = -1.0;
-            cidx[j] = 0x7fffffff;
+          } else {
+            // (ii) too many float ties: the exact select over the 64-bit patterns, then the
+            // entries above its value tau and the first r entries equal to it by index
+            unsigned long long tau;
+            int r;
+            pol_radix_select(key, V, K, &tau, &r, hist, pick);
+            int eq = 0;
+            for (int i = lo; i < hi; ++i) eq += (unsigned long long)__double_as_longlong(key[i]) == tau;
+            int rank = pol_block_excl_scan(eq, red_i);
+            if (tid == 0) pick[0] = 0;
+            __syncthreads();
+            for (int i = lo; i < hi; ++i) {
+              const unsigned long long kb = (unsigned long long)__double_as_longlong(key[i]);
+              const bool take = kb > tau || (kb == tau && rank++ < r);
+              if (take) {
+                const int at = atomicAdd(&pick[0], 1);
+                ckey[at] = key[i];
+                cidx[at] = i;
+              }
+            }
+            kp = a.kp;
+            for (int j = K + tid; j < kp; j += kPolicyThreads) {
+              ckey[j] = -1.0;
+              cidx[j] = 0x7fffffff;
+            }
           }
           __syncthreads();
           pol_sort(ckey, cidx, kp);
@@ -475,7 +551,7 @@ inline size_t policy_smem_for(const PolicyArgs& a) {
   const bool truncated = draw && !(a.top_k <= 0 && a.top_p >= 0.9999);
   const bool select = truncated && a.top_k > 0 && a.top_k < a.V && a.top_k <= kPolicyMaxK;
   size_t b = (size_t)a.vp * sizeof(double);
-  if (select) b += (size_t)a.kp * (sizeof(double) + sizeof(int32_t));
+  if (select) b += (size_t)a.kcap * (sizeof(double) + sizeof(int32_t));
   else if (truncated) b += (size_t)a.vp * sizeof(int32_t);
   return b;
 }
@@ -485,6 +561,7 @@ int launch_policy(PolicyArgs& a, cudaStream_t s) {
   a.vp = policy_vp(a.V);
   a.kp = 1;
   while (a.kp < a.top_k && a.kp < kPolicyMaxK) a.kp <<= 1;
+  a.kcap = 2 * a.kp;  // room for float-key ties beyond the top k
   const size_t smem = policy_smem_for(a);  // within the limit raised once per device (policy_smem)
   if (a.n_rows > 0) policy_kernel<<<a.n_rows, kPolicyThreads, smem, s>>>(a);
   MC_CUDA(cudaGetLastError());
