@@ -251,9 +251,9 @@ __device__ __forceinline__ void pol_radix_select(const double* p, int n, int k, 
   *r_out = r;
 }
 
-// The k-th largest of the float keys rz(p[i]) (p rounded toward zero to float32, whose bit
-// patterns order like the values), by the same radix select over 32 bits: four passes.
-__device__ __forceinline__ unsigned int pol_radix_select32(const double* p, int n, int k, int* hist, int* pick) {
+// The k-th largest of the float keys fk[i] = bits of rz(p[i]) (p rounded toward zero to float32,
+// whose bit patterns order like the values), by the same radix select over 32 bits: four passes.
+__device__ __forceinline__ unsigned int pol_radix_select32(const unsigned int* fk, int n, int k, int* hist, int* pick) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   unsigned int prefix = 0u, mask = 0u;
   int r = k;
@@ -261,7 +261,7 @@ __device__ __forceinline__ unsigned int pol_radix_select32(const double* p, int 
     for (int b = tid; b < 256; b += kPolicyThreads) hist[b] = 0;
     __syncthreads();
     for (int i = tid; i < n; i += kPolicyThreads) {
-      const unsigned int kb = __float_as_uint(__double2float_rz(p[i]));
+      const unsigned int kb = fk[i];
       if ((kb & mask) == prefix) atomicAdd(&hist[(kb >> shift) & 255], 1);
     }
     __syncthreads();
@@ -306,6 +306,7 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
   int32_t* idx = reinterpret_cast<int32_t*>(key + a.vp);
   double* ckey = key + a.vp;
   int32_t* cidx = reinterpret_cast<int32_t*>(ckey + a.kcap);
+  unsigned int* fkey = reinterpret_cast<unsigned int*>(cidx + a.kcap);  // the candidates' float keys
   __shared__ double red_d[kPolicyWarps];
   __shared__ int red_i[kPolicyWarps];
   __shared__ int hist[256];
@@ -412,9 +413,11 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
           // (i) the entries whose float key reaches the k-th largest float key F hold the top k:
           // an entry below F ranks behind the >= k entries at or above it. Their number C is k
           // unless float keys tie at F; up to the candidate capacity they are sorted exactly.
-          const unsigned int F = pol_radix_select32(key, V, K, hist, pick);
+          for (int i = tid; i < V; i += kPolicyThreads) fkey[i] = __float_as_uint(__double2float_rz(key[i]));
+          __syncthreads();
+          const unsigned int F = pol_radix_select32(fkey, V, K, hist, pick);
           int cnt = 0;
-          for (int i = lo; i < hi; ++i) cnt += __float_as_uint(__double2float_rz(key[i])) >= F;
+          for (int i = lo; i < hi; ++i) cnt += fkey[i] >= F;
           int base = pol_block_excl_scan(cnt, red_i);
           if (tid == kPolicyThreads - 1) pick[0] = base + cnt;
           __syncthreads();
@@ -423,7 +426,7 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
           int kp;
           if (C <= a.kcap) {
             for (int i = lo; i < hi; ++i)
-              if (__float_as_uint(__double2float_rz(key[i])) >= F) {
+              if (fkey[i] >= F) {
                 ckey[base] = key[i];
                 cidx[base++] = i;
               }
@@ -541,8 +544,12 @@ inline int policy_vp(int V) {
   return vp;
 }
 
-// The largest launch's shared memory (a whole-row sort at the largest vocabulary).
-inline size_t policy_smem(int V) { return (size_t)policy_vp(V) * (sizeof(double) + sizeof(int32_t)); }
+// The largest launch's shared memory: the top-k branch at the largest vocabulary and top-k (row
+// keys, 2048 candidates, float keys), above a whole-row sort's.
+inline size_t policy_smem(int V) {
+  const size_t vp = (size_t)policy_vp(V);
+  return vp * (sizeof(double) + sizeof(uint32_t)) + 2 * (size_t)kPolicyMaxK * (sizeof(double) + sizeof(int32_t));
+}
 
 // Shared memory of one launch: the row's keys, then the indices of a whole-row sort or the top-k
 // candidates (keys and indices), by the branch the kernel takes for these knobs.
@@ -551,7 +558,7 @@ inline size_t policy_smem_for(const PolicyArgs& a) {
   const bool truncated = draw && !(a.top_k <= 0 && a.top_p >= 0.9999);
   const bool select = truncated && a.top_k > 0 && a.top_k < a.V && a.top_k <= kPolicyMaxK;
   size_t b = (size_t)a.vp * sizeof(double);
-  if (select) b += (size_t)a.kcap * (sizeof(double) + sizeof(int32_t));
+  if (select) b += (size_t)a.kcap * (sizeof(double) + sizeof(int32_t)) + (size_t)a.vp * sizeof(uint32_t);
   else if (truncated) b += (size_t)a.vp * sizeof(int32_t);
   return b;
 }
