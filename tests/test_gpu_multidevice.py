@@ -1,0 +1,45 @@
+"""Sessions sharded over two GPUs of one process (a context opened on devices 0 and 1): every
+session's tokens must equal those of the same session on one GPU, for greedy generation, the
+sampling policy and the scheduler (sessions never interact, and draws are keyed by the global
+session index or the request). Skipped on a box with one GPU."""
+import numpy as np
+import pytest
+
+from mignon_ai_b200 import quant, synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _two_gpus():
+    import torch
+    return torch.cuda.device_count() >= 2
+
+
+@pytest.mark.skipif("not _two_gpus()")
+def test_two_devices_match_one():
+    spec = synth.ModelSpec(**{**synth.CONFIGS[2].__dict__, "vocab": 512})
+    data = synth.build_model_file(spec)
+    n, P, T = 64, 24, 10
+    prompts = synth.prompts_uniform_fast(n, P, spec.vocab, seed=13)
+    lens = (np.arange(n) % P + 1).astype(np.int32)
+    sp = quant.Sampling(0.8, 1.2, 40, 0.9, 6, True)
+    out = {}
+    for devs in ((0,), (0, 1)):
+        ctx = quant.Context(devs)
+        m = quant.Model.decode(data, ctx)
+        b = m.new_batch(n, 0, P)
+        g = b.generate(prompts, lens, T)[0]
+        pol = b.generate_policy(prompts, lens, T, sp, penalize_prompt=True, session0=5)[0]
+        b.close()
+        sched = quant.Scheduler(m, 16, sp, max_prompt=P, max_new=T)
+        ids = [sched.submit(prompts[i, :lens[i]], T - i % 4, draw_key=100 + i) for i in range(n)]
+        sched.run(4)
+        sc = [sched.result(r)[0].tolist() for r in ids]
+        sched.close()
+        m.close()
+        ctx.close()
+        out[devs] = (g, pol, sc)
+    a, b2 = out[(0,)], out[(0, 1)]
+    np.testing.assert_array_equal(a[0], b2[0])
+    np.testing.assert_array_equal(a[1], b2[1])
+    assert a[2] == b2[2]
