@@ -391,7 +391,9 @@ def run_scheduler(args):
                      "prefill_passes": st["prefill_passes"] - base["prefill_passes"],
                      "decode_steps": st["decode_steps"] - base["decode_steps"],
                      "admit_device_ms": (st["admit_us"] - base["admit_us"]) / 1e3,
-                     "decode_device_ms": (st["decode_us"] - base["decode_us"]) / 1e3}
+                     "decode_device_ms": (st["decode_us"] - base["decode_us"]) / 1e3,
+                     "admit_host_ms": (st["admit_host_us"] - base["admit_host_us"]) / 1e3,
+                     "step_wall_ms": (st["step_us"] - base["step_us"]) / 1e3}
     batch = model.new_batch(slots, 0, PROMPT)
     batch.generate(prompts[:slots], lens[:slots], 4)
     useful = int(n_new.sum())

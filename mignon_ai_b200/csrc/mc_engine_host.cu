@@ -283,6 +283,11 @@ struct DevBatch {
   // admission list.
   bool per_session = false;
   int32_t *gen_n = nullptr, *limit = nullptr, *sched_adm = nullptr;
+  // A prefill pass over some sessions only (the scheduler's admissions): the block kernel runs the
+  // n_pass_tiles tiles of pass_tiles, the prefill attention the n_pass_sess sessions of pass_sess
+  // (0: all). Set for one pass.
+  int32_t *pass_tiles = nullptr, *pass_sess = nullptr;
+  int n_pass_tiles = 0, n_pass_sess = 0;
   uint32_t* key = nullptr;
   uint8_t* a_cache = nullptr;    // block kernel: per-SM digit-plane cache of GEMMs wider than the A slots
   int a_cache_kt = 0;
@@ -649,10 +654,15 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
       else kern = kf == 1 ? block_decode_kernel<1, 16, 3> : kf == 2 ? block_decode_kernel<2, 16, 3> : block_decode_kernel<3, 16, 3>;
       kern<<<grid, kDThreads, m.dec_smem, s>>>(a);
     } else {
+      int grid = a.n_tiles;
+      if (b.n_pass_tiles > 0) {
+        a.tile_list = b.pass_tiles;
+        grid = b.n_pass_tiles;
+      }
       switch ((m.D + 127) / 128) {
-        case 1: (a.a_cache ? block_kernel<1, true> : block_kernel<1, false>)<<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
-        case 2: (a.a_cache ? block_kernel<2, true> : block_kernel<2, false>)<<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
-        default: (a.a_cache ? block_kernel<3, true> : block_kernel<3, false>)<<<a.n_tiles, kBlockThreads, kBlockSmem, s>>>(a); break;
+        case 1: (a.a_cache ? block_kernel<1, true> : block_kernel<1, false>)<<<grid, kBlockThreads, kBlockSmem, s>>>(a); break;
+        case 2: (a.a_cache ? block_kernel<2, true> : block_kernel<2, false>)<<<grid, kBlockThreads, kBlockSmem, s>>>(a); break;
+        default: (a.a_cache ? block_kernel<3, true> : block_kernel<3, false>)<<<grid, kBlockThreads, kBlockSmem, s>>>(a); break;
       }
     }
     MC_CUDA(cudaGetLastError());
@@ -702,20 +712,27 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
           case 64: attn_decode_kernel<64><<<grid, kAttnThreads, 0, s>>>(aa); break;
           default: attn_decode_kernel<0><<<grid, kAttnThreads, 0, s>>>(aa); break;
         }
-      } else if (attn_prefill_fast_ok(aa.dh) && attn_prefill_fast_smem(P, m.D) <= 220 * 1024) {
-        const size_t smem = attn_prefill_fast_smem(P, m.D);
-        switch (aa.dh) {
-          case 4: attn_prefill_fast_kernel<4><<<b.S, kAttnThreads, smem, s>>>(aa); break;
-          case 8: attn_prefill_fast_kernel<8><<<b.S, kAttnThreads, smem, s>>>(aa); break;
-          case 16: attn_prefill_fast_kernel<16><<<b.S, kAttnThreads, smem, s>>>(aa); break;
-          case 32: attn_prefill_fast_kernel<32><<<b.S, kAttnThreads, smem, s>>>(aa); break;
-          case 48: attn_prefill_fast_kernel<48><<<b.S, kAttnThreads, smem, s>>>(aa); break;
-          default: attn_prefill_fast_kernel<64><<<b.S, kAttnThreads, smem, s>>>(aa); break;
-        }
       } else {
-        const size_t smem = (size_t)P * 2 * m.D * 4 + 32 * 4 + 16 + 128;
-        if (smem > 220 * 1024) return set_error(kUnsupported, "prefill segment too long for the attention kernel");
-        attn_prefill_kernel<<<b.S, kAttnThreads, smem, s>>>(aa);
+        int grid = b.S;
+        if (b.n_pass_sess > 0) {
+          aa.sess_list = b.pass_sess;
+          grid = b.n_pass_sess;
+        }
+        if (attn_prefill_fast_ok(aa.dh) && attn_prefill_fast_smem(P, m.D) <= 220 * 1024) {
+          const size_t smem = attn_prefill_fast_smem(P, m.D);
+          switch (aa.dh) {
+            case 4: attn_prefill_fast_kernel<4><<<grid, kAttnThreads, smem, s>>>(aa); break;
+            case 8: attn_prefill_fast_kernel<8><<<grid, kAttnThreads, smem, s>>>(aa); break;
+            case 16: attn_prefill_fast_kernel<16><<<grid, kAttnThreads, smem, s>>>(aa); break;
+            case 32: attn_prefill_fast_kernel<32><<<grid, kAttnThreads, smem, s>>>(aa); break;
+            case 48: attn_prefill_fast_kernel<48><<<grid, kAttnThreads, smem, s>>>(aa); break;
+            default: attn_prefill_fast_kernel<64><<<grid, kAttnThreads, smem, s>>>(aa); break;
+          }
+        } else {
+          const size_t smem = (size_t)P * 2 * m.D * 4 + 32 * 4 + 16 + 128;
+          if (smem > 220 * 1024) return set_error(kUnsupported, "prefill segment too long for the attention kernel");
+          attn_prefill_kernel<<<grid, kAttnThreads, smem, s>>>(aa);
+        }
       }
       MC_CUDA(cudaGetLastError());
       if (log) log->record(s, 1);

@@ -85,6 +85,7 @@ struct mc_sched {
   int64_t n_prefill = 0, n_steps = 0, n_tokens = 0, n_done = 0;
   double admit_us = 0, decode_us = 0, host_us = 0;  // device time of admission passes and decode steps;
                                                     // wall time inside mc_sched_step
+  double admit_host_us = 0;                         // host time choosing and staging admissions
   ~mc_sched() {
     for (SchedShard& ss : sh) {
       for (void* p : {(void*)ss.h_up, (void*)ss.h_state, (void*)ss.h_tok, (void*)ss.h_prob})
@@ -100,6 +101,7 @@ namespace {
 
 // Admits queued requests into the free slots of shard g with one prefill pass.
 int sched_admit(mc_sched* q, size_t g) {
+  const auto t_host = std::chrono::steady_clock::now();
   SchedShard& ss = q->sh[g];
   DevBatch& sh = *q->batch->shard[g];
   const int S = sh.S, window = q->batch->window, cap = sh.pol_prefix_cap;
@@ -153,6 +155,8 @@ int sched_admit(mc_sched* q, size_t g) {
   int32_t* hkey = hlim + S;
   int32_t* hpre = hkey + S;
   int32_t* hplen = hpre + (size_t)S * cap;
+  int32_t* htiles = hplen + S;  // the pass's tiles and sessions: the kernels run only these
+  int32_t* hsess = htiles + S;
   std::fill(tok, tok + (size_t)S * P, 0);
   const int spt = std::max(1, 128 / P);
   for (int s = 0; s < S; ++s) {
@@ -168,7 +172,17 @@ int sched_admit(mc_sched* q, size_t g) {
   for (int s = 0; s < S; ++s) hkey[s] = (int32_t)ss.key[s];
   std::copy(ss.prefix.begin(), ss.prefix.end(), hpre);
   std::copy(ss.prefix_len.begin(), ss.prefix_len.end(), hplen);
+  int n_tiles = 0, n_sess = 0;
+  for (int s = 0; s < S; ++s) {
+    if (adm[s] <= 0) continue;
+    hsess[n_sess++] = s;
+    const int t = s / spt;
+    if (n_tiles == 0 || htiles[n_tiles - 1] != t) htiles[n_tiles++] = t;
+  }
   cudaStream_t st = sh.stream;
+  // the admission's device time starts here, after the host's part
+  MC_CUDA(cudaEventRecord(ss.ev[0], st));
+  q->admit_host_us += std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t_host).count();
   MC_CUDA(cudaMemcpyAsync(sh.tok, tok, (size_t)S * P * 4, cudaMemcpyHostToDevice, st));
   MC_CUDA(cudaMemcpyAsync(sh.rowmap, rowmap, (size_t)S * 4, cudaMemcpyHostToDevice, st));
   MC_CUDA(cudaMemcpyAsync(sh.sched_adm, hadm, (size_t)S * 4, cudaMemcpyHostToDevice, st));
@@ -176,10 +190,15 @@ int sched_admit(mc_sched* q, size_t g) {
   MC_CUDA(cudaMemcpyAsync(sh.key, hkey, (size_t)S * 4, cudaMemcpyHostToDevice, st));
   if (cap > 0) MC_CUDA(cudaMemcpyAsync(sh.pol_prefix, hpre, (size_t)S * cap * 4, cudaMemcpyHostToDevice, st));
   MC_CUDA(cudaMemcpyAsync(sh.pol_prefix_len, hplen, (size_t)S * 4, cudaMemcpyHostToDevice, st));
+  MC_CUDA(cudaMemcpyAsync(sh.pass_tiles, htiles, (size_t)n_tiles * 4, cudaMemcpyHostToDevice, st));
+  MC_CUDA(cudaMemcpyAsync(sh.pass_sess, hsess, (size_t)n_sess * 4, cudaMemcpyHostToDevice, st));
   const int thr = 256, blocks = (S + thr - 1) / thr;
   sched_admit_kernel<<<blocks, thr, 0, st>>>(S, P, sh.sched_adm, sh.tok, sh.seglen, sh.pos, sh.gen_n, sh.next_tok);
   MC_CUDA(cudaGetLastError());
+  sh.n_pass_tiles = n_tiles;
+  sh.n_pass_sess = n_sess;
   int rc = enqueue_forward(sh, P, q->mode, 0.0, 0, false, true);
+  sh.n_pass_tiles = sh.n_pass_sess = 0;
   if (rc != kOk) return rc;
   sched_resume_kernel<<<blocks, thr, 0, st>>>(S, sh.sched_adm, sh.seglen);
   MC_CUDA(cudaGetLastError());
@@ -276,7 +295,7 @@ int mc_sched_open(mc_model* model, int slots, int context_size, int max_prompt, 
     if (sh.S == 0) continue;
     MC_CUDA(cudaSetDevice(sh.m->device));
     SchedShard& sp_ = q->sh.back();
-    const size_t up = (size_t)sh.S * (sh.pmax + 5 + cap + 1);
+    const size_t up = (size_t)sh.S * (sh.pmax + cap + 8);
     MC_CUDA(cudaHostAlloc(&sp_.h_up, up * 4, cudaHostAllocDefault));
     for (cudaEvent_t& e : sp_.ev) MC_CUDA(cudaEventCreate(&e));
     MC_CUDA(cudaHostAlloc(&sp_.h_state, (size_t)sh.S * 2 * 4, cudaHostAllocDefault));
@@ -285,6 +304,7 @@ int mc_sched_open(mc_model* model, int slots, int context_size, int max_prompt, 
     if ((st = ensure_step_outputs(sh, q->mode == 3, max_new)) != kOk) return st;
     if ((st = sh.alloc(sh.gen_n, (size_t)sh.S * 4)) || (st = sh.alloc(sh.limit, (size_t)sh.S * 4)) ||
         (st = sh.alloc(sh.key, (size_t)sh.S * 4)) || (st = sh.alloc(sh.sched_adm, (size_t)sh.S * 4)) ||
+        (st = sh.alloc(sh.pass_tiles, (size_t)sh.S * 4)) || (st = sh.alloc(sh.pass_sess, (size_t)sh.S * 4)) ||
         (st = sh.alloc(sh.pol_prefix_len, (size_t)sh.S * 4)) || (st = sh.alloc(sh.pol_state, (size_t)sh.S * 4)))
       return st;
     if (cap > 0 && (st = sh.alloc(sh.pol_prefix, (size_t)sh.S * cap * 4)) != kOk) return st;
@@ -400,6 +420,7 @@ int mc_sched_stats(const mc_sched* q, int64_t* out) {
   out[5] = (int64_t)q->admit_us;
   out[6] = (int64_t)q->decode_us;
   out[7] = (int64_t)q->host_us;
+  out[8] = (int64_t)q->admit_host_us;
   return kOk;
 }
 
