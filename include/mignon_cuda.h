@@ -237,6 +237,12 @@ int mc_sched_set_admit_min(mc_sched* sched, int admit_min);
 int mc_generate_dev(mc_batch* batch, const int32_t* d_prompts, const int32_t* d_lens, int stride, int pmax, int n_new,
                     double temperature, uint32_t session0, int32_t* d_out_tokens, float* d_out_probs);
 
+/* Exercises the device-error path without a fault (no counterpart in the reference): a kernel
+ * waits on a barrier that nothing completes; its bounded wait gives up after 2 s, records the
+ * device error word and returns. Returns MC_DEVICE_TIMEOUT (any other status means the path is
+ * broken); the device stays usable afterwards. */
+int mc_selftest_wait_timeout(int device);
+
 /* The CUDA stream (cudaStream_t) the batch's work on device shard `shard` runs on. */
 int mc_batch_stream(mc_batch* batch, int shard, void** stream);
 
