@@ -382,7 +382,14 @@ def run_scheduler(args):
         for i in range(n_req):
             sched.submit(prompts[i, :lens[i]], int(n_new[i]), draw_key=i)
         t0 = time.perf_counter()
-        sched.run(16)
+        rounds, prev, left = [], sched.stats(), 1
+        while left:  # rounds of 16 decode steps (mc_sched_run's loop, with the stats of each round)
+            left = sched.step(16)
+            cur = sched.stats()
+            if cur["prefill_passes"] > prev["prefill_passes"]:
+                rounds.append({"admitted": cur["admitted"] - prev["admitted"],
+                               "admit_device_ms": (cur["admit_us"] - prev["admit_us"]) / 1e3})
+            prev = cur
         dt = time.perf_counter() - t0
         st = sched.stats()
         sched.close()
@@ -393,9 +400,14 @@ def run_scheduler(args):
                      "admit_device_ms": (st["admit_us"] - base["admit_us"]) / 1e3,
                      "decode_device_ms": (st["decode_us"] - base["decode_us"]) / 1e3,
                      "admit_host_ms": (st["admit_host_us"] - base["admit_host_us"]) / 1e3,
+                     "admission_passes": rounds,
                      "step_wall_ms": (st["step_us"] - base["step_us"]) / 1e3}
     batch = model.new_batch(slots, 0, PROMPT)
     batch.generate(prompts[:slots], lens[:slots], 4)
+    t0 = time.perf_counter()
+    for _ in range(3):
+        batch.prefill(prompts[:slots], lens[:slots])
+    prefill_ms = (time.perf_counter() - t0) / 3 * 1e3
     useful = int(n_new.sum())
     static = {}
     for name in ("greedy", "policy"):
@@ -413,7 +425,7 @@ def run_scheduler(args):
             "scaling": "none", "vs_baseline": None, "data": "synthetic",
             "config": {"workload": "%d slots, %d requests: prompts 16..%d tokens, token limits 16..%d (seed 2)" % (
                 slots, n_req, PROMPT, NEW), "timing": "wall time of mc_sched_run (requests submitted before)"},
-            "scheduler": res, "static_batches": static}
+            "scheduler": res, "static_batches": static, "static_prefill_ms": prefill_ms}
     print(json.dumps(line))
     batch.close()
     model.close()

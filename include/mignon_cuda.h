@@ -224,9 +224,10 @@ int mc_sched_run(mc_sched* sched, int steps_per_poll);
 /* A finished request's tokens (and probabilities, like mc_generate_policy's): *n = its token
  * count, of which the first `capacity` are copied; *n = -1 while it is queued or running. */
 int mc_sched_result(mc_sched* sched, int64_t id, int32_t* tokens, float* probs, int capacity, int* n);
-/* out[9] = prefill passes, decode steps, tokens emitted, requests finished, requests in flight,
+/* out[10] = prefill passes, decode steps, tokens emitted, requests finished, requests in flight,
  * then microseconds: device time of the admission passes, device time of the decode steps, wall
- * time inside mc_sched_step / mc_sched_run, host time choosing and staging admissions. */
+ * time inside mc_sched_step / mc_sched_run, host time choosing and staging admissions; then the
+ * requests admitted into slots so far. */
 int mc_sched_stats(const mc_sched* sched, int64_t* out);
 /* Admit when at least admit_min slots are free (or none is running). */
 int mc_sched_set_admit_min(mc_sched* sched, int admit_min);

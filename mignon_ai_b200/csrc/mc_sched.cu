@@ -82,7 +82,7 @@ struct mc_sched {
   std::deque<int64_t> queue;
   std::vector<SchedReq> req;
   std::vector<SchedShard> sh;
-  int64_t n_prefill = 0, n_steps = 0, n_tokens = 0, n_done = 0;
+  int64_t n_prefill = 0, n_steps = 0, n_tokens = 0, n_done = 0, n_admitted = 0;
   double admit_us = 0, decode_us = 0, host_us = 0;  // device time of admission passes and decode steps;
                                                     // wall time inside mc_sched_step
   double admit_host_us = 0;                         // host time choosing and staging admissions
@@ -204,6 +204,7 @@ int sched_admit(mc_sched* q, size_t g) {
   MC_CUDA(cudaGetLastError());
   ss.busy += n_adm;
   ++q->n_prefill;
+  q->n_admitted += n_adm;
   return kOk;
 }
 
@@ -421,6 +422,7 @@ int mc_sched_stats(const mc_sched* q, int64_t* out) {
   out[6] = (int64_t)q->decode_us;
   out[7] = (int64_t)q->host_us;
   out[8] = (int64_t)q->admit_host_us;
+  out[9] = q->n_admitted;
   return kOk;
 }
 

@@ -378,10 +378,10 @@ class Scheduler:
         return toks[:n.value].copy(), probs[:n.value].copy()
 
     def stats(self) -> dict:
-        out = np.zeros(9, np.int64)
+        out = np.zeros(10, np.int64)
         _lib.check(_lib.lib().mc_sched_stats(self._h, _lib.ptr(out)))
         return dict(zip(("prefill_passes", "decode_steps", "tokens", "finished", "in_flight", "admit_us", "decode_us",
-                         "step_us", "admit_host_us"), map(int, out)))
+                         "step_us", "admit_host_us", "admitted"), map(int, out)))
 
 
 class Session:
