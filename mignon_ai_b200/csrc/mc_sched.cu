@@ -61,7 +61,8 @@ struct SchedShard {
   std::vector<int32_t> prefix, prefix_len;
   int busy = 0;
   // pinned host buffers: the admission list's uploads [tok S*P | rowmap | adm | limit | key |
-  // prefix S*cap | prefix_len], and the collection's reads [seglen | gen_n] and output rows
+  // prefix S*cap | prefix_len | pass tiles | pass sessions], and the collection's reads
+  // [seglen | gen_n] and output rows
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};  // round start, admission done, decode steps done
   bool timed = false;                                // this round recorded them
   int32_t* h_up = nullptr;
