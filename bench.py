@@ -136,6 +136,33 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+def cpu_model():
+    """The host CPU's model string (the first "model name" of /proc/cpuinfo)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def measure_i8_peak(device=0):
+    """The tensor pipe's int8 rate on this GPU (mc_probe_mma_i8: one CTA per SM issuing back-to-back
+    128 x 256 x 32 kind::i8 MMAs on resident operands), with the SM clock sampled meanwhile."""
+    from mignon_ai_b200 import _lib, quant  # noqa: F401  (quant registers the signatures)
+    L = _lib.lib()
+    tops, ms = ctypes.c_double(), ctypes.c_double()
+    clocks = ClockSampler([device])
+    clocks.start()
+    _lib.check(L.mc_probe_mma_i8(device, 1 << 16, 20, ctypes.byref(tops), ctypes.byref(ms)))
+    clk = clocks.stop()
+    return {"tops": tops.value, "ms_per_launch": ms.value, "clocks": clk,
+            "how": "mc_probe_mma_i8: one CTA per SM, 65536 x 4 back-to-back tcgen05.mma kind::i8 128x256x32 on "
+                   "shared-memory operands (pseudo-random bytes), 20 launches timed with CUDA events"}
+
+
 def run_cpu_reference(steps, warmup, sessions=None, label="reference"):
     """The CPU restatement of the reference engine (oracle/) on all host threads, bounded sample."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -176,14 +203,8 @@ def run_gemm_sweep(args):
     L = _lib.lib()
     gen = torch.Generator(device=dev)
     gen.manual_seed(5)
-    peaks = {}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except OSError:
-        pass
-    # dense int8 tensor rate is twice the bf16 rate on B200; the measured bf16 burst figure is the base
-    i8_peak = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
+    peak = measure_i8_peak(0)
+    i8_peak = peak["tops"]
     rows = []
     steps = max(1, args.steps)
     for M in GEMM_M:
@@ -226,7 +247,7 @@ def run_gemm_sweep(args):
                 "l2": "largest shape: 1 GB of s32 output, far above the 126 MB L2"},
             "roofline": {"bound": "tensor", "achieved": big["tops"], "peak": i8_peak, "unit": "TOPS",
                          "frac": big["tops"] / i8_peak,
-                         "peak_source": "2 x MEASURED_PEAKS.json bf16_tflops (dense int8 runs at twice the bf16 rate)"},
+                         "peak_source": "measured in this run: " + peak["how"], "peak_clocks": peak["clocks"]},
             "all_exact": all(r["exact"] for r in rows), "sweep": rows}
     print(json.dumps(line))
     return 0
@@ -267,6 +288,11 @@ def run_score(args):
     ms = e0.elapsed_time(e1) / steps
     tokens = n * (SCORE_LEN - 1)
     value = tokens / (ms / 1000.0)
+    D, H, V, B, Sx = spec.state, spec.hidden, spec.vocab, spec.blocks, spec.steps
+    spans = [min(p + 1, 64) for p in range(SCORE_LEN - 1)]
+    score_mac = B * Sx * (D * D + 6 * H * D + 2 * D * H) + B * 4 * D * D + V * D + B * 2 * D * float(np.mean(spans))
+    achieved_tops = value * 2 * score_mac / 1e12
+    peak = measure_i8_peak(0)
     # CPU restatement on a sample, all host threads
     cores = os.cpu_count() or 1
     k = max(cores, 32)
@@ -283,7 +309,13 @@ def run_score(args):
                                    "%d sequences x %d tokens (seed 4), every next-token log-probability" % (n, SCORE_LEN),
                        "timing": "the host API call (sequences in, log-probabilities out) per step"},
             "cpu_baseline": {"value": k * (SCORE_LEN - 1) / cpu_s, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": "%d sequences of the workload" % k},
+                             "cpu_model": cpu_model(), "sample": "%d sequences of the workload" % k},
+            "roofline": {"bound": "tensor (int8)", "achieved": achieved_tops, "peak": peak["tops"], "unit": "TOPS",
+                         "frac": achieved_tops / peak["tops"], "peak_source": "mc_probe_mma_i8 on this GPU, this run",
+                         "algorithmic_ops_per_token": 2 * score_mac,
+                         "note": "MACs per scored token: B*S*(D^2 + 6HD + 2DH) + B*(4D^2 + 2*span*D) + V*D, span = "
+                                 "min(pos+1, 64), averaged over positions 0..126; counted once (the three digit "
+                                 "planes are overhead, not work)"},
             "max_abs_dlogprob_vs_cpu": err}
     print(json.dumps(line))
     batch.close()
@@ -433,6 +465,361 @@ def run_scheduler(args):
     return 0
 
 
+PARITY_SESSIONS = 64
+
+
+def headline_parity(model, prompts, tok, prob):
+    """The headline job against the CPU oracle on its first 64 sessions (after the timed region):
+    the job's greedy streams and probabilities against the oracle's, and the logits of every step
+    of the same 64 sessions run through prefill + appends with logits, against the oracle's.
+    Bars: logits within 1e-3 * max |logit|; streams equal except from a step where the oracle's
+    top-2 logit gap is below 1e-4 (excused)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle
+    from mignon_ai_b200 import synth
+    n = PARITY_SESSIONS
+    om = pyoracle.Model(synth.build_model_file(synth.CONFIGS[CONFIG]))
+    lens = np.full(n, PROMPT, np.int32)
+    wt, wp, wl = om.generate_greedy(prompts[:n], lens, NEW, logits=True, nthreads=os.cpu_count() or 1)
+    b = model.new_batch(n, 0, PROMPT)
+    logits, nxt, _ = b.prefill(prompts[:n], lens, want_logits=True)
+    worst = 0.0
+    ok_logits = True
+    gt = [nxt.copy()]
+    for t in range(NEW):
+        # logits of step t while the stream still equals the oracle's (after that they differ by design)
+        for s_ in range(n):
+            if np.array_equal(np.array([g[s_] for g in gt[:t]]), wt[s_, :t]):
+                ref = wl[s_, t].astype(np.float64)
+                rel = float(np.max(np.abs(logits[s_].astype(np.float64) - ref)) / max(1e-30, np.max(np.abs(ref))))
+                worst = max(worst, rel)
+        if t + 1 < NEW:
+            logits, nxt, _ = b.append(nxt, want_logits=True)
+            gt.append(nxt.copy())
+    b.close()
+    ok_logits = worst <= 1e-3
+    equal, excused, bad = 0, 0, 0
+    for s_ in range(n):
+        diff = np.nonzero(tok[s_] != wt[s_])[0]
+        if diff.size == 0:
+            equal += 1
+            continue
+        t = int(diff[0])
+        top2 = np.sort(wl[s_, t].astype(np.float64))[-2:]
+        if top2[1] - top2[0] < 1e-4:
+            excused += 1
+        else:
+            bad += 1
+    same = tok[:n] == wt
+    prob_rel = float(np.max(np.abs(prob[:n][same] - wp[same]) / np.maximum(np.abs(wp[same]), 1e-30), initial=0.0))
+    return {"sessions": n, "oracle": "CPU restatement of the reference engine (oracle/)",
+            "max_rel_dlogit": worst, "logits_within_1e-3": ok_logits, "streams_equal": equal,
+            "excused_near_ties": excused, "unexplained": bad, "max_rel_dprob_equal_streams": prob_rel,
+            "pass": bool(ok_logits and bad == 0)}
+
+
+SAMPLE_SESSIONS = 65536
+SAMPLE_CTX = 128
+SAMPLE_T = 0.8
+SAMPLE_TOPK = 40
+
+
+def run_sample(args):
+    """Config 3: 65,536 sessions split evenly over the ranks (strong scaling; rank g takes the
+    contiguous sessions [g*N/G, (g+1)*N/G)), prompts of 16..64 uniform ids (lengths and ids seed
+    3), each session decoded to the 128-token context (128 - len tokens, a per-session limit),
+    sampled at T 0.8 with top-k 40 from Philox keyed by the global session index.
+
+      value  device-resident prompts, lengths, limits and outputs (mc_generate_limits_dev)
+      e2e    the host API (mc_generate_limits): pinned host prompts in, tokens/probs out
+    One step = the whole job; the max over ranks of the CUDA-event time."""
+    import torch
+    from mignon_ai_b200 import _lib, quant, synth
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", local_rank)
+    spec = synth.CONFIGS[3]
+    N = args.sessions if args.sessions != SESSIONS else SAMPLE_SESSIONS
+    first, end = rank * N // world, (rank + 1) * N // world
+    S = end - first
+    lens_all = synth.prompt_lengths(N, 16, 64, seed=3)
+    prompts = np.ascontiguousarray(synth.prompts_uniform_fast(end, 64, spec.vocab, seed=3)[first:end])
+    lens = np.ascontiguousarray(lens_all[first:end])
+    limits = (SAMPLE_CTX - lens).astype(np.int32)
+    n_max = int(SAMPLE_CTX - 16)
+    data = synth.build_model_file(spec)
+    ctx = quant.Context((local_rank,))
+    model = quant.Model.decode(data, ctx)
+    batch = model.new_batch(S, 0, 64, top_k=SAMPLE_TOPK)
+    L = _lib.lib()
+    sp = ctypes.c_void_p()
+    _lib.check(L.mc_batch_stream(batch._h, 0, ctypes.byref(sp)))
+    stream = torch.cuda.ExternalStream(sp.value, device=dev)
+    d_prompts = torch.from_numpy(prompts).to(dev)
+    d_lens = torch.from_numpy(lens).to(dev)
+    d_lim = torch.from_numpy(limits).to(dev)
+    d_tok = torch.zeros((S, n_max), dtype=torch.int32, device=dev)
+
+    def job():
+        _lib.check(L.mc_generate_limits_dev(batch._h, d_prompts.data_ptr(), d_lens.data_ptr(), 64, 64,
+                                            d_lim.data_ptr(), n_max, SAMPLE_T, first, d_tok.data_ptr(), None))
+
+    for _ in range(args.warmup):
+        job()
+    _lib.check(L.mc_batch_error(batch._h))
+    clocks = ClockSampler([local_rank] if world == 1 else list(range(world))) if rank == 0 else None
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    if clocks:
+        clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        job()
+    e1.record(stream)
+    _lib.check(L.mc_batch_error(batch._h))
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(e0.elapsed_time(e1), dist, dev)
+    clk = clocks.stop() if clocks else None
+    tokens_per_step = int((SAMPLE_CTX - lens_all).sum())  # all ranks
+    value = tokens_per_step * args.steps / (ms / 1000.0)
+    got_dev = d_tok.cpu().numpy()
+
+    # e2e through the host API
+    h_prompts = torch.from_numpy(prompts).pin_memory().numpy()
+    h_lens = torch.from_numpy(lens).pin_memory().numpy()
+    h_lim = torch.from_numpy(limits).pin_memory().numpy()
+    h_tok = torch.zeros((S, n_max), dtype=torch.int32).pin_memory().numpy()
+    h_prob = torch.zeros((S, n_max), dtype=torch.float32).pin_memory().numpy()
+    h_len = torch.zeros(S, dtype=torch.int32).pin_memory().numpy()
+
+    def e2e_job():
+        _lib.check(L.mc_generate_limits(batch._h, h_prompts.ctypes.data, h_lens.ctypes.data, 64, h_lim.ctypes.data,
+                                        n_max, SAMPLE_T, first, h_tok.ctypes.data, h_prob.ctypes.data,
+                                        h_len.ctypes.data))
+
+    e2e_job()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_job()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ems = max_over_ranks(e0.elapsed_time(e1), dist, dev)
+    e2e_value = tokens_per_step * args.steps / (ems / 1000.0)
+    same = bool(np.array_equal(h_tok, got_dev)) and bool(np.array_equal(h_len, limits))
+
+    # decode-step profile with every session attending a full 64-token window: greedy
+    # generation of 2 tokens after 64-token prompts, then one step launch by launch
+    full = np.full(S, 64, np.int32)
+    batch.generate(prompts, full, 2)
+    ms_arr = np.zeros(64, np.float32)
+    kinds = np.zeros(64, np.int32)
+    nl = ctypes.c_int()
+    L.mc_profile_step.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    _lib.check(L.mc_profile_step(batch._h, 64, ms_arr.ctypes.data, kinds.ctypes.data, ctypes.byref(nl)))
+    n = nl.value
+    per_kind = {}
+    for k, t in zip(kinds[:n], ms_arr[:n]):
+        per_kind.setdefault(int(k), []).append(float(t))
+    D = spec.state
+    attn_bytes = S * (2 * 64 * D * 4 + 2 * D * 4 + 4)
+    attn_ms = float(np.mean(per_kind.get(1, [float("nan")])))
+    peaks = _peaks()
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    achieved = attn_bytes / (attn_ms / 1000.0) / 1e9
+    names = {0: "block_decode_kernel", 1: "attn_decode_staged_kernel", 2: "block_decode_kernel(final)",
+             3: "head_kernel", 4: "select_kernel"}
+    step_ms = float(sum(ms_arr[:n]))
+    # whole-step algorithmic bytes (HBM): K/V windows read and the new key/value written per
+    # attention block, the rule state (norm ring read + written, latch read + written) per block
+    state_bytes = S * spec.blocks * (2 * 64 * D * 4 + 2 * D * 4 + 2 * (2 + 1) * D * 4 * 2)
+    out = None
+    if rank == 0:
+        cpu = None
+        parity = None
+        if world == 1 and not args.no_cpu_baseline:
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            import pyoracle
+            cores = os.cpu_count() or 1
+            k = min(S, max(32, 4 * cores))
+            om = pyoracle.Model(data)
+            nn = 32
+            t0 = time.perf_counter()
+            wt, wl = om.generate_sample(prompts[:k], lens[:k], nn, SAMPLE_T, SAMPLE_TOPK, session0=first,
+                                        logits=True, nthreads=cores)
+            cpu_s = time.perf_counter() - t0
+            cpu = {"value": k * nn / cpu_s, "unit": "tokens/s", "cores": cores, "kind": "port", "cpu_model": cpu_model(),
+                   "sample": "%d sessions of the workload (prompts 16..64) x %d sampled tokens each" % (k, nn)}
+            # the same k sessions' first 32 tokens from the timed job (every limit is >= 64)
+            eq, near, bad = 0, 0, 0
+            for s_ in range(k):
+                diff = np.nonzero(got_dev[s_, :nn] != wt[s_])[0]
+                if diff.size == 0:
+                    eq += 1
+                    continue
+                t = int(diff[0])
+                lg = wl[s_, t].astype(np.float64)
+                order = np.lexsort((np.arange(lg.size), -lg))[:SAMPLE_TOPK]
+                v = lg[order] / SAMPLE_T
+                cdf = np.cumsum(np.exp(v - v[0]))
+                u = synth.sample_uniform(first + s_, t)
+                margin = float(np.min(np.abs(cdf - u * cdf[-1])) / cdf[-1])
+                if margin < 5e-3:
+                    near += 1
+                else:
+                    bad += 1
+            parity = {"sessions": k, "tokens_each": nn, "streams_equal": eq, "diverged_at_near_cdf_edge": near,
+                      "unexplained": bad, "pass": bad == 0 and near <= k // 4,
+                      "oracle": "CPU restatement of the reference engine (oracle/), same Philox draws"}
+        out = {"metric": "generated tokens/s (config-3 sampled decode, sessions split over GPUs)", "value": value,
+               "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+               "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+               "dtype": "int8 weights x float32 activations (3 int8 digit planes, s32 accumulate)", "data": "synthetic",
+               "config": {"workload": "config3: D=384 H=1024 8 blocks x 1 step, attn 6 heads (dh 64) window 64, "
+                                      "vocab 4096, ctx 128; %d sessions split over %d GPU(s), prompts U[16,64] (seed 3), "
+                                      "each decoded to the 128-token context, T 0.8, top-k 40, Philox per session"
+                                      % (N, world),
+                          "sessions_total": N, "sessions_per_gpu": S, "tokens_per_step": tokens_per_step,
+                          "l2": "no flush: per-GPU KV rings (%.1f GB) far exceed the 126 MB L2" % (
+                              S * spec.blocks * 2 * 64 * D * 4 / 1e9)},
+               "clocks": clk,
+               "e2e": {"value": e2e_value, "unit": "tokens/s",
+                       "h2d_bytes_per_step": int(world * (prompts.nbytes + lens.nbytes + limits.nbytes)),
+                       "d2h_bytes_per_step": int(world * (h_tok.nbytes + h_prob.nbytes + h_len.nbytes)),
+                       "matches_value_run": same},
+               "roofline": {"bound": "hbm", "kernel": "attn_decode_staged_kernel", "achieved": achieved,
+                            "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                            "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s",
+                            "traffic": None, "traffic_measured": False,
+                            "algorithmic_bytes_per_launch": attn_bytes, "avg_launch_ms": attn_ms,
+                            "note": "one decode step with every session at a full 64-token window"},
+               "decode_step_profile": {"ms_total": step_ms,
+                                       "hbm_frac_whole_step": state_bytes / (step_ms / 1000.0) / 1e9 / hbm_peak,
+                                       "ms_per_kind": {names.get(k, str(k)): float(np.mean(v))
+                                                       for k, v in per_kind.items()}},
+               "cpu_baseline": cpu, "parity": parity,
+               "device": {"rank": rank, "cuda_device": local_rank, "sessions": [first, end]}}
+        print(json.dumps(out, default=lambda o: o.item() if hasattr(o, "item") else str(o)))
+    else:
+        print(json.dumps({"rank": rank, "cuda_device": local_rank, "sessions": [first, end], "ms": ms}),
+              file=sys.stderr)
+    batch.close()
+    model.close()
+    ctx.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_tiny(args):
+    """Config 1 (no attention): 64 sessions, 32-token prompts (seed 1), 64 greedy tokens each.
+    value: device-resident prompts and outputs (mc_generate_dev); e2e: the host API (mc_generate).
+    With 64 sessions a decode step is one tile per launch: the job is bound by the launch chain's
+    latency, which the INT8 fraction shows."""
+    import torch
+    from mignon_ai_b200 import _lib, quant, synth
+    spec = synth.CONFIGS[1]
+    n, plen, new = 64, 32, 64
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    data = synth.build_model_file(spec)
+    ctx = quant.Context((0,))
+    model = quant.Model.decode(data, ctx)
+    batch = model.new_batch(n, 0, plen)
+    L = _lib.lib()
+    sp = ctypes.c_void_p()
+    _lib.check(L.mc_batch_stream(batch._h, 0, ctypes.byref(sp)))
+    stream = torch.cuda.ExternalStream(sp.value, device=dev)
+    prompts = synth.prompts_uniform_fast(n, plen, spec.vocab, seed=1)
+    lens = np.full(n, plen, np.int32)
+    d_p, d_l = torch.from_numpy(prompts).to(dev), torch.from_numpy(lens).to(dev)
+    d_t = torch.zeros((n, new), dtype=torch.int32, device=dev)
+    d_pr = torch.zeros((n, new), dtype=torch.float32, device=dev)
+
+    def job():
+        _lib.check(L.mc_generate_dev(batch._h, d_p.data_ptr(), d_l.data_ptr(), plen, plen, new, 0.0, 0,
+                                     d_t.data_ptr(), d_pr.data_ptr()))
+
+    for _ in range(max(3, args.warmup)):
+        job()
+    _lib.check(L.mc_batch_error(batch._h))
+    steps = max(1, args.steps) * 10
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(steps):
+        job()
+    e1.record(stream)
+    _lib.check(L.mc_batch_error(batch._h))
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    value = n * new / (ms / 1000.0)
+    h_p = torch.from_numpy(prompts).pin_memory().numpy()
+    h_l = torch.from_numpy(lens).pin_memory().numpy()
+    h_t = torch.zeros((n, new), dtype=torch.int32).pin_memory().numpy()
+    h_pr = torch.zeros((n, new), dtype=torch.float32).pin_memory().numpy()
+    L.mc_generate.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 2 + [ctypes.c_double, ctypes.c_uint32] + \
+        [ctypes.c_void_p] * 2
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        _lib.check(L.mc_generate(batch._h, h_p.ctypes.data, h_l.ctypes.data, plen, new, 0.0, 0, h_t.ctypes.data,
+                                 h_pr.ctypes.data))
+    e2e_ms = (time.perf_counter() - t0) * 1000.0 / steps
+    peak = measure_i8_peak(0)
+    mac_per_token = 204800  # B*S*(D^2 + 6HD + 2DH) + V*D (no attention)
+    achieved = value * 2 * mac_per_token / 1e12
+    line = {"metric": "generated tokens/s (config-1 greedy decode)", "value": value, "unit": "tokens/s", "n_gpus": 1,
+            "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "none", "vs_baseline": None, "dtype": "int8 weights x float32 activations", "data": "synthetic",
+            "config": {"workload": "config1: D=64 H=128 2 blocks x 1 step, no attention, vocab 1024; 64 sessions x "
+                                   "(32-token prompt, seed 1, + 64 greedy tokens)"},
+            "e2e": {"value": n * new / (e2e_ms / 1000.0), "unit": "tokens/s", "h2d_bytes_per_step": prompts.nbytes +
+                    lens.nbytes, "d2h_bytes_per_step": h_t.nbytes + h_pr.nbytes, "timing": "host wall clock per call"},
+            "roofline": {"bound": "tensor (int8)", "achieved": achieved, "peak": peak["tops"], "unit": "TOPS",
+                         "frac": achieved / peak["tops"], "peak_source": "mc_probe_mma_i8 on this GPU, this run",
+                         "note": "64 sessions fill one 128-row tile: each decode step is a chain of 3 launches whose "
+                                 "latency, not the tensor pipe, sets the time"},
+            "matches_value_run": bool(np.array_equal(h_t, d_t.cpu().numpy()))}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import pyoracle
+        cores = os.cpu_count() or 1
+        om = pyoracle.Model(data)
+        t0 = time.perf_counter()
+        om.generate_greedy(prompts, lens, new, nthreads=cores)
+        cpu_s = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": n * new / cpu_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+                                "cpu_model": cpu_model(), "sample": "the whole workload"}
+    print(json.dumps(line))
+    batch.close()
+    model.close()
+    ctx.close()
+    return 0
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -441,13 +828,24 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--sessions", type=int, default=SESSIONS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the headline's parity check against the oracle")
     ap.add_argument("--quick", action="store_true",
                     help="profiling case: one generation job, no timing, e2e, profile or CPU baseline")
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemm", "score", "policy", "scheduler"],
-                    help="decode: the config-2 generation job (the headline); gemm: the config-5 INT8 GEMM "
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "sample", "gemm", "score", "policy", "scheduler", "tiny", "i8peak"],
+                    help="decode: the config-2 generation job (the headline); sample: config 3 (65536 sessions "
+                         "split over the ranks, sampled, decoded to the context); gemm: the config-5 INT8 GEMM "
                          "sweep; score: the config-4 scoring pass; policy: config-2 generation under the whole "
-                         "sampling policy; scheduler: continuous batching of ragged requests")
+                         "sampling policy; scheduler: continuous batching of ragged requests; tiny: config 1; "
+                         "i8peak: the tensor pipe's int8 rate")
     args = ap.parse_args()
+    if args.workload == "sample":
+        return run_sample(args)
+    if args.workload == "i8peak":
+        print(json.dumps(measure_i8_peak(0)))
+        return 0
+    if args.workload == "tiny":
+        return run_tiny(args)
     if args.workload == "gemm":
         return run_gemm_sweep(args)
     if args.workload == "score":
@@ -469,7 +867,8 @@ def main():
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1000.0, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32 activations x int8 weights (CPU)",
                 "data": "synthetic", "config": workload_config(args.gpus, args.sessions),
-                "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+                "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
+                                 "cpu_model": cpu_model()},
                 "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                 "note": "the reference is Go; no Go toolchain exists on these machines, so its CPU engine is "
                         "timed as the C restatement in oracle/ (same algorithm and float32 operation order)"}
@@ -564,7 +963,7 @@ def main():
                                  h_tok.ctypes.data, h_prob.ctypes.data))
 
     e2e_job()
-    e_steps = max(1, min(args.steps, 3))
+    e_steps = args.steps
     if dist:
         dist.barrier()
     torch.cuda.synchronize(dev)
@@ -609,12 +1008,17 @@ def main():
     # 4 x (block + attention) and the final block with the greedy head fused in
     launches_per_job = (1 + 2 * 4 + 1 + 2) + (NEW - 1) * (2 * 4 + 1)
 
+    parity = None
+    if rank == 0 and not args.no_parity:
+        parity = headline_parity(model, prompts, h_tok, h_prob)
+
     out = None
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             tps, cores, sample, _ = run_cpu_reference(1, 0)
-            cpu = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+            cpu = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
+                   "cpu_model": cpu_model()}
         out = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -627,13 +1031,16 @@ def main():
             "roofline": {"bound": "hbm", "kernel": "attn_decode_staged_kernel", "achieved": achieved, "peak": hbm_peak,
                          "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s",
-                         "traffic": ATTN_DRAM_BYTES_PER_SESSION * S,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a full-size launch "
-                                           "(profiles/attn_decode_staged_kernel_config2.md)",
+                         "traffic": ATTN_DRAM_BYTES_PER_SESSION * S, "traffic_measured": False,
+                         "traffic_source": "not measured by this run: DRAM bytes per session from an earlier ncu "
+                                           "capture (dram__bytes_read.sum + dram__bytes_write.sum of a full-size "
+                                           "4096-session launch, 273.4 MB) scaled by the sessions",
                          "algorithmic_bytes_per_launch": attn_bytes, "avg_launch_ms": attn_ms},
             "decode_step_profile": {"ms_total": float(step_ms), "share": shares,
                                     "ms_per_kind": {names.get(k, str(k)): float(np.mean(v)) for k, v in per_kind.items()}},
             "cpu_baseline": cpu,
+            "parity": parity,
+            "device": {"rank": rank, "cuda_device": local_rank, "name": torch.cuda.get_device_name(dev)},
         }
         print(json.dumps(out, default=lambda o: o.item() if hasattr(o, "item") else str(o)))
     batch.close()

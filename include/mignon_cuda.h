@@ -56,13 +56,15 @@ int mc_gemm_f32a_dev(const float* x, const int8_t* w, int m, int n, int k, float
                      float* y, int32_t* slices, float* row_max_scratch, void* stream);
 
 /* mc_gemm_f32a_dev without any device allocation, for callers that cannot allocate GPU memory
- * (a host runtime limited to buffers it registered in advance, a fixed memory budget, or work
- * issued during CUDA graph capture, where cudaMalloc is not allowed). It has no counterpart in the
- * reference. Its only scratch, one float per activation row, is a fixed device array of 65536
- * entries (256 KB, held by every GPU that loads the library until exit): m above 65536 fails
- * with MC_INVALID_ARGUMENT. The first call on each device looks up that array's device address
- * (no allocation); make it before any stream capture. All calls share the array; calls that
- * overlap on the GPU race on it and must be serialized by the caller. */
+ * (a host runtime limited to buffers it registered in advance, or a service whose GPU memory is
+ * budgeted once at start-up). It has no counterpart in the reference. Its only scratch, one float
+ * per activation row, is a fixed device array of 65536 entries (256 KB, held by every GPU that
+ * loads the library until exit): m above 65536 fails with MC_INVALID_ARGUMENT, as do the shapes
+ * mc_gemm_f32a_dev rejects, before any CUDA call. The first call on each device looks up that
+ * array's device address and sets the kernels' shared-memory attribute on it (no allocation;
+ * serialized by a lock, so first calls from several host threads are safe); make it before any
+ * stream capture. Device ordinals 0..63. All calls share the array; calls that overlap on the GPU
+ * race on it and must be serialized by the caller. */
 int mc_gemm_f32a_noalloc_dev(const float* x, const int8_t* w, int m, int n, int k, float w_scale, const float* bias,
                              float* y, void* stream);
 
@@ -159,6 +161,16 @@ int mc_generate_stops(mc_batch* batch, const int32_t* prompts, const int32_t* le
                       double temperature, uint32_t session0, const int32_t* stops, int n_stops, int32_t* out_tokens,
                       float* out_probs, int32_t* out_lens);
 
+/* mc_generate with a token limit per session: pkg/infer.Generate with Options.MaxTokens
+ * (pkg/infer/infer.go:64-96) per session, greedy (temperature <= 0.001) or sampled like
+ * mc_generate (top-k = the batch's top_k, Philox keyed by (session0 + s, "SAMP"), counter = the
+ * token index). Session s emits max_tokens[s] tokens (1 <= max_tokens[s] <= n_max); out_tokens
+ * [count x n_max] holds them, then -1; out_lens (if non-null) the counts. A session that has
+ * emitted its tokens sits out the remaining steps (its attention rows are not read). */
+int mc_generate_limits(mc_batch* batch, const int32_t* prompts, const int32_t* lens, int stride,
+                       const int32_t* max_tokens, int n_max, double temperature, uint32_t session0,
+                       int32_t* out_tokens, float* out_probs, int32_t* out_lens);
+
 /* The knobs of generate.Sampling (internal/generate/chat.go:45-56) for the policy calls below. */
 typedef struct {
   double temperature; /* <= 0.001: argmax (sample.go:71-82) */
@@ -237,6 +249,22 @@ int mc_sched_set_admit_min(mc_sched* sched, int admit_min);
  * pmax >= every lens[s]. Check completion and device errors with mc_batch_error. */
 int mc_generate_dev(mc_batch* batch, const int32_t* d_prompts, const int32_t* d_lens, int stride, int pmax, int n_new,
                     double temperature, uint32_t session0, int32_t* d_out_tokens, float* d_out_probs);
+
+/* mc_generate_limits with device-resident prompts, lengths, limits and outputs on a
+ * single-device batch (like mc_generate_dev): enqueues the job and returns without synchronizing.
+ * Limits outside [1, n_max] are not checked on the host: a session emits at least one token and
+ * at most n_max. */
+int mc_generate_limits_dev(mc_batch* batch, const int32_t* d_prompts, const int32_t* d_lens, int stride, int pmax,
+                           const int32_t* d_max_tokens, int n_max, double temperature, uint32_t session0,
+                           int32_t* d_out_tokens, float* d_out_probs);
+
+/* The int8 rate of this device's tensor pipe, the denominator of the INT8 roofline fractions (no
+ * counterpart in the reference: a measurement). One CTA per multiprocessor issues back-to-back
+ * tcgen05.mma kind::i8 instructions of the largest single-CTA shape (M 128, N 256, K 32) on
+ * operands resident in shared memory, with nothing else to do; `launches` launches of `iters`
+ * MMA groups (4 instructions, K 128) each are timed with CUDA events. *tops = int8 tera-ops/s
+ * (2 ops per multiply-add), *ms = milliseconds per launch. iters in [1, 2^22]. */
+int mc_probe_mma_i8(int device, int iters, int launches, double* tops, double* ms);
 
 /* Exercises the device-error path without a fault (no counterpart in the reference): a kernel
  * waits on a barrier that nothing completes; its bounded wait gives up after 2 s, records the

@@ -348,10 +348,29 @@ int check_policy(const mc_sampling* sp, const PolicyIn* pi, int V, int count) {
 // stop tokens: a session ends before the first one it would emit; out_lens[s] = tokens emitted,
 // the rest of its row -1), and with a policy that of mc_generate_policy (sampleContinuation,
 // generate/sample.go:196-247).
+// Per-session token limits (limits[s] tokens for session s, device or host pointer): the sessions
+// generate through the per-session counters (gen_n: output column; limit: it ends after its last
+// token) while the step loop runs n_new steps for all.
+int begin_limits(DevBatch& sh, const int32_t* limits, cudaMemcpyKind kind) {
+  int st;
+  if (!sh.gen_n && (st = sh.alloc(sh.gen_n, (size_t)sh.S * 4)) != kOk) return st;
+  if (!sh.limit && (st = sh.alloc(sh.limit, (size_t)sh.S * 4)) != kOk) return st;
+  MC_CUDA(cudaMemcpyAsync(sh.limit, limits, (size_t)sh.S * 4, kind, sh.stream));
+  MC_CUDA(cudaMemsetAsync(sh.gen_n, 0, (size_t)sh.S * 4, sh.stream));
+  MC_CUDA(cudaMemsetAsync(sh.out_tok, 0xFF, (size_t)sh.S * sh.out_stride * 4, sh.stream));
+  MC_CUDA(cudaMemsetAsync(sh.out_prob, 0, (size_t)sh.S * sh.out_stride * 4, sh.stream));
+  sh.per_session = true;
+  return kOk;
+}
+
 int generate_impl(mc_batch* b, const int32_t* prompts, const int32_t* lens, int stride, int n_new, double temperature,
                   uint32_t session0, const int32_t* stops, int n_stops, int32_t* out_tokens, float* out_probs,
-                  int32_t* out_lens, const PolicyIn* pol = nullptr) {
+                  int32_t* out_lens, const PolicyIn* pol = nullptr, const int32_t* limits = nullptr) {
   if (!b || !prompts || !lens || !out_tokens || n_new <= 0) return set_error(kInvalidArgument, "mc_generate: bad arguments");
+  if (limits)
+    for (int s = 0; s < b->count; ++s)
+      if (limits[s] < 1 || limits[s] > n_new)
+        return set_error(kInvalidArgument, "mc_generate_limits: a session's token limit is outside [1, n_max]");
   const int mode = pol ? 3 : temperature > 0.001 ? 1 : 0;
   if (mode == 1 && b->topk < 1)
     return set_error(kUnsupported, "mc_generate: sampling needs a batch opened with top_k in [1, 64]");
@@ -373,11 +392,13 @@ int generate_impl(mc_batch* b, const int32_t* prompts, const int32_t* lens, int 
       MC_CUDA(cudaMemsetAsync(sh.out_tok, 0xFF, (size_t)sh.S * sh.out_stride * 4, sh.stream));
       MC_CUDA(cudaMemsetAsync(sh.out_prob, 0, (size_t)sh.S * sh.out_stride * 4, sh.stream));
     }
+    if (limits && (st = begin_limits(sh, limits + b->first[g], cudaMemcpyHostToDevice)) != kOk) return st;
     const uint32_t s0 = session0 + (uint32_t)b->first[g];
     st = enqueue_forward(sh, P, mode, inv_t, s0, false, true);
     if (st == kOk) st = run_decode_steps(sh, n_new, mode, inv_t, s0);
-    sh.n_stops = 0;  // only this job's launches carry the stop tokens and the policy
+    sh.n_stops = 0;  // only this job's launches carry the stop tokens, the policy and the limits
     sh.pol = DevBatch::Policy();
+    sh.per_session = false;
     if (st != kOk) return st;
   }
   for (size_t g = 0; g < b->shard.size(); ++g) {
@@ -408,6 +429,72 @@ int generate_impl(mc_batch* b, const int32_t* prompts, const int32_t* lens, int 
   return kOk;
 }
 
+
+// mc_generate_dev / mc_generate_limits_dev: the whole job enqueued on the batch's stream from
+// device-resident prompts (and per-session limits when d_limits is non-null).
+int generate_dev_impl(mc_batch* b, const int32_t* d_prompts, const int32_t* d_lens, int stride, int pmax,
+                      const int32_t* d_limits, int n_new, double temperature, uint32_t session0, int32_t* d_out_tokens,
+                      float* d_out_probs, const char* name) {
+  const std::string fn(name);
+  if (!b || !d_prompts || !d_lens || !d_out_tokens || n_new <= 0 || pmax <= 0)
+    return set_error(kInvalidArgument, fn + ": bad arguments");
+  if (b->shard.size() != 1) return set_error(kUnsupported, fn + ": single-device batches only");
+  DevBatch& sh = *b->shard[0];
+  const int P = std::min(pmax, b->window);
+  if (P > b->pmax) return set_error(kInvalidArgument, fn + ": pmax above the batch's max_prompt");
+  const int mode = temperature > 0.001 ? 1 : 0;
+  if (mode == 1 && b->topk < 1) return set_error(kUnsupported, fn + ": sampling needs top_k >= 1");
+  const double inv_t = mode ? 1.0 / temperature : 0.0;
+  MC_CUDA(cudaSetDevice(sh.m->device));
+  int st;
+  if ((st = ensure_step_outputs(sh, false, n_new)) != kOk) return st;
+  prepare_prompts_kernel<<<(sh.S + 127) / 128, 128, 0, sh.stream>>>(d_prompts, d_lens, stride, sh.S, P, b->window, sh.tok,
+                                                                      sh.seglen, sh.pos, sh.rowmap, sh.step, sh.next_tok);
+  MC_CUDA(cudaGetLastError());
+  if (d_limits && (st = begin_limits(sh, d_limits, cudaMemcpyDeviceToDevice)) != kOk) return st;
+  st = enqueue_forward(sh, P, mode, inv_t, session0, false, true);
+  if (st == kOk) st = run_decode_steps(sh, n_new, mode, inv_t, session0);
+  sh.per_session = false;
+  if (st != kOk) return st;
+  MC_CUDA(cudaMemcpy2DAsync(d_out_tokens, (size_t)n_new * 4, sh.out_tok, (size_t)sh.out_stride * 4, (size_t)n_new * 4, sh.S,
+                            cudaMemcpyDeviceToDevice, sh.stream));
+  if (d_out_probs)
+    MC_CUDA(cudaMemcpy2DAsync(d_out_probs, (size_t)n_new * 4, sh.out_prob, (size_t)sh.out_stride * 4, (size_t)n_new * 4,
+                              sh.S, cudaMemcpyDeviceToDevice, sh.stream));
+  return kOk;
+}
+
+// mc_batch_open; allow_passes: prefills larger than the scratch budget run in passes over
+// contiguous sessions (a scheduler's admission passes over tile lists need every row instead).
+int batch_open(mc_model* m, int count, int context_size, int max_prompt, int top_k, bool allow_passes, mc_batch** out) {
+  if (!m || !out || count <= 0) return set_error(kInvalidArgument, "mc_batch_open: bad arguments");
+  if (top_k < 0 || top_k > kMaxTopK) return set_error(kInvalidArgument, "mc_batch_open: top_k must be in [0, 64]");
+  auto b = std::make_unique<mc_batch>();
+  b->model = m;
+  b->count = count;
+  const DevModel& d0 = *m->dev[0];
+  b->window = d0.max_context;  // NewSession (session.go:20-28)
+  if (context_size > 0 && context_size < b->window) b->window = context_size;
+  b->pmax = std::min(std::max(1, max_prompt > 0 ? std::min(max_prompt, b->window) : b->window), 128);
+  b->topk = top_k;
+  const int ndev = (int)m->dev.size();
+  shard_sizes(count, ndev, b->first);
+  for (int g = 0; g < ndev; ++g) {
+    std::unique_ptr<DevBatch> sh;
+    const int S = b->first[g + 1] - b->first[g];
+    if (S == 0) {
+      b->shard.push_back(std::make_unique<DevBatch>());
+      b->shard.back()->m = m->dev[g].get();
+      continue;
+    }
+    int st = batch_create(m->dev[g].get(), S, b->window, b->pmax, top_k, allow_passes, sh);
+    if (st != kOk) return st;
+    if ((st = ensure_step_outputs(*sh, false, 1)) != kOk) return st;
+    b->shard.push_back(std::move(sh));
+  }
+  *out = b.release();
+  return kOk;
+}
 
 }  // namespace
 
@@ -482,40 +569,13 @@ int mc_model_info(const mc_model* m, int32_t* out) {
 
 int mc_batch_open(mc_model* m, int count, int context_size, int max_prompt, int top_k, mc_batch** out) {
   clear_error();
-  if (!m || !out || count <= 0) return set_error(kInvalidArgument, "mc_batch_open: bad arguments");
-  if (top_k < 0 || top_k > kMaxTopK) return set_error(kInvalidArgument, "mc_batch_open: top_k must be in [0, 64]");
-  auto b = std::make_unique<mc_batch>();
-  b->model = m;
-  b->count = count;
-  const DevModel& d0 = *m->dev[0];
-  b->window = d0.max_context;  // NewSession (session.go:20-28)
-  if (context_size > 0 && context_size < b->window) b->window = context_size;
-  b->pmax = std::min(std::max(1, max_prompt > 0 ? std::min(max_prompt, b->window) : b->window), 128);
-  b->topk = top_k;
-  const int ndev = (int)m->dev.size();
-  shard_sizes(count, ndev, b->first);
-  for (int g = 0; g < ndev; ++g) {
-    std::unique_ptr<DevBatch> sh;
-    const int S = b->first[g + 1] - b->first[g];
-    if (S == 0) {
-      b->shard.push_back(std::make_unique<DevBatch>());
-      b->shard.back()->m = m->dev[g].get();
-      continue;
-    }
-    int st = batch_create(m->dev[g].get(), S, b->window, b->pmax, top_k, sh);
-    if (st != kOk) return st;
-    if ((st = ensure_step_outputs(*sh, false, 1)) != kOk) return st;
-    b->shard.push_back(std::move(sh));
-  }
-  *out = b.release();
-  return kOk;
+  return batch_open(m, count, context_size, max_prompt, top_k, true, out);
 }
 
 int mc_batch_close(mc_batch* b) {
   delete b;
   return kOk;
 }
-
 int mc_prefill(mc_batch* b, const int32_t* tokens, const int32_t* lens, int stride, float* logits, int32_t* next,
                float* prob) {
   clear_error();
@@ -700,29 +760,26 @@ int mc_batch_stream(mc_batch* b, int shard, void** stream) {
 int mc_generate_dev(mc_batch* b, const int32_t* d_prompts, const int32_t* d_lens, int stride, int pmax, int n_new,
                     double temperature, uint32_t session0, int32_t* d_out_tokens, float* d_out_probs) {
   clear_error();
-  if (!b || !d_prompts || !d_lens || !d_out_tokens || n_new <= 0 || pmax <= 0)
-    return set_error(kInvalidArgument, "mc_generate_dev: bad arguments");
-  if (b->shard.size() != 1) return set_error(kUnsupported, "mc_generate_dev: single-device batches only");
-  DevBatch& sh = *b->shard[0];
-  const int P = std::min(pmax, b->window);
-  if (P > b->pmax) return set_error(kInvalidArgument, "mc_generate_dev: pmax above the batch's max_prompt");
-  const int mode = temperature > 0.001 ? 1 : 0;
-  if (mode == 1 && b->topk < 1) return set_error(kUnsupported, "mc_generate_dev: sampling needs top_k >= 1");
-  const double inv_t = mode ? 1.0 / temperature : 0.0;
-  MC_CUDA(cudaSetDevice(sh.m->device));
-  int st;
-  if ((st = ensure_step_outputs(sh, false, n_new)) != kOk) return st;
-  prepare_prompts_kernel<<<(sh.S + 127) / 128, 128, 0, sh.stream>>>(d_prompts, d_lens, stride, sh.S, P, b->window, sh.tok,
-                                                                      sh.seglen, sh.pos, sh.rowmap, sh.step, sh.next_tok);
-  MC_CUDA(cudaGetLastError());
-  if ((st = enqueue_forward(sh, P, mode, inv_t, session0, false, true)) != kOk) return st;
-  if ((st = run_decode_steps(sh, n_new, mode, inv_t, session0)) != kOk) return st;
-  MC_CUDA(cudaMemcpy2DAsync(d_out_tokens, (size_t)n_new * 4, sh.out_tok, (size_t)sh.out_stride * 4, (size_t)n_new * 4, sh.S,
-                            cudaMemcpyDeviceToDevice, sh.stream));
-  if (d_out_probs)
-    MC_CUDA(cudaMemcpy2DAsync(d_out_probs, (size_t)n_new * 4, sh.out_prob, (size_t)sh.out_stride * 4, (size_t)n_new * 4,
-                              sh.S, cudaMemcpyDeviceToDevice, sh.stream));
-  return kOk;
+  return generate_dev_impl(b, d_prompts, d_lens, stride, pmax, nullptr, n_new, temperature, session0, d_out_tokens,
+                           d_out_probs, "mc_generate_dev");
+}
+
+int mc_generate_limits(mc_batch* b, const int32_t* prompts, const int32_t* lens, int stride, const int32_t* max_tokens,
+                       int n_max, double temperature, uint32_t session0, int32_t* out_tokens, float* out_probs,
+                       int32_t* out_lens) {
+  clear_error();
+  if (!max_tokens) return set_error(kInvalidArgument, "mc_generate_limits: null max_tokens");
+  return generate_impl(b, prompts, lens, stride, n_max, temperature, session0, nullptr, 0, out_tokens, out_probs,
+                       out_lens, nullptr, max_tokens);
+}
+
+int mc_generate_limits_dev(mc_batch* b, const int32_t* d_prompts, const int32_t* d_lens, int stride, int pmax,
+                           const int32_t* d_max_tokens, int n_max, double temperature, uint32_t session0,
+                           int32_t* d_out_tokens, float* d_out_probs) {
+  clear_error();
+  if (!d_max_tokens) return set_error(kInvalidArgument, "mc_generate_limits_dev: null max_tokens");
+  return generate_dev_impl(b, d_prompts, d_lens, stride, pmax, d_max_tokens, n_max, temperature, session0,
+                           d_out_tokens, d_out_probs, "mc_generate_limits_dev");
 }
 
 int mc_batch_error(mc_batch* b) {

@@ -25,7 +25,8 @@ struct AttnArgs {
   float* att;
   float* att_rowmax;
   float scale;
-  const int32_t* sess_list;  // prefill: CTA i runs session sess_list[i] (some sessions only), or null: i
+  const int32_t* sess_list;  // prefill: CTA i runs session sess_list[i] (some sessions only), or null: sess0 + i
+  int sess0;                 // prefill: first session of a pass over a contiguous range of sessions
 };
 
 constexpr int kAttnThreads = 256;
@@ -436,7 +437,7 @@ __global__ void __launch_bounds__(kAttnThreads, DH <= 32 ? 4 : 2) attn_prefill_f
   float* sm = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   constexpr int NF = DH / 4;
   constexpr int G = 32 / NF;
-  const int s = a.sess_list ? a.sess_list[blockIdx.x] : (int)blockIdx.x;
+  const int s = a.sess_list ? a.sess_list[blockIdx.x] : a.sess0 + (int)blockIdx.x;
   const int len = a.seglen[s];
   if (len <= 0) return;
   const int D = a.D, heads = a.heads;
@@ -562,7 +563,7 @@ inline size_t attn_prefill_fast_smem(int P, int D) {
 __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const __grid_constant__ AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   float* sm = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  const int s = a.sess_list ? a.sess_list[blockIdx.x] : (int)blockIdx.x;
+  const int s = a.sess_list ? a.sess_list[blockIdx.x] : a.sess0 + (int)blockIdx.x;
   const int len = a.seglen[s];
   if (len <= 0) return;
   const int D = a.D, dh = a.dh;

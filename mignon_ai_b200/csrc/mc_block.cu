@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
   Bars* bars = reinterpret_cast<Bars*>(sB + kSmemB);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int tile = a.tile_list ? a.tile_list[blockIdx.x] : (int)blockIdx.x;
+  const int tile = a.tile_list ? a.tile_list[blockIdx.x] : a.tile0 + (int)blockIdx.x;
   const int D = a.D, H = a.H;
   // this SM's plane cache (one block-kernel CTA per SM at a time: its shared memory)
   uint8_t* acache = nullptr;

@@ -90,7 +90,8 @@ struct BlockArgs {
   int n_stops;          // a chosen token among stops ends its session (seglen_w = 0, no output)
   int stops[kMaxStops];
   int32_t* seglen_w;
-  const int32_t* tile_list;  // CTA i runs tile tile_list[i] (a pass over some tiles only), or null: tile i
+  const int32_t* tile_list;  // CTA i runs tile tile_list[i] (a pass over some tiles only), or null: tile tile0 + i
+  int tile0;                 // first tile of a pass over a contiguous range of tiles (0: from the first)
   int32_t* gen_n;       // [S] tokens each session has emitted (its output column), or null: *step
   const int32_t* limit; // [S] tokens a session may emit (it ends after the last), with gen_n
 };

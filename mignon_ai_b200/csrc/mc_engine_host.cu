@@ -403,7 +403,15 @@ static int ensure_attrs(int device) {
   return kOk;
 }
 
-int batch_create(DevModel* m, int S, int window, int pmax, int topk, std::unique_ptr<DevBatch>& out) {
+// Scratch bytes a batch may hold for prefill rows (MC_PREFILL_SCRATCH_MB, default 8 GiB). A prefill
+// whose rows need more runs as several passes over contiguous ranges of sessions.
+static size_t prefill_scratch_budget() {
+  const char* e = getenv("MC_PREFILL_SCRATCH_MB");
+  const long long mb = e ? atoll(e) : 8192;
+  return (size_t)std::max(mb, 1LL) << 20;
+}
+
+int batch_create(DevModel* m, int S, int window, int pmax, int topk, bool allow_passes, std::unique_ptr<DevBatch>& out) {
   MC_CUDA(cudaSetDevice(m->device));
   int st = ensure_attrs(m->device);
   if (st != kOk) return st;
@@ -420,7 +428,16 @@ int batch_create(DevModel* m, int S, int window, int pmax, int topk, std::unique
   MC_CUDA(cudaDeviceGetAttribute(&b->n_sm, cudaDevAttrMultiProcessorCount, m->device));
   const int D = m->D, H = m->H;
   const int spt_min = std::max(1, 128 / b->pmax);
-  const size_t tiles = std::max((size_t)(S + 127) / 128, (size_t)(S + spt_min - 1) / spt_min);
+  const size_t full_tiles = std::max((size_t)(S + 127) / 128, (size_t)(S + spt_min - 1) / spt_min);
+  // per scratch row: cur, blockin, the 3D neighbourhood, hidden, q, attention output, final norm
+  // (8D + H floats), two row maxima and a prefill row's key and value (2D floats)
+  const size_t row_bytes = (size_t)(10 * D + H + 2) * 4;
+  size_t tiles = full_tiles;
+  if (allow_passes) {
+    // decode needs one row per session; a prefill may run in passes of fewer rows
+    const size_t fit = std::max<size_t>(prefill_scratch_budget() / (row_bytes * 128), 1);
+    tiles = std::max((size_t)(S + 127) / 128, std::min(full_tiles, fit));
+  }
   b->rows = tiles * 128;
   // vocabulary splits: enough CTAs to cover the SMs
   const int mtiles = (S + 127) / 128;
@@ -442,7 +459,9 @@ int batch_create(DevModel* m, int S, int window, int pmax, int topk, std::unique
       (st = b->alloc(b->hbuf, R * H * 4)) || (st = b->alloc(b->qbuf, R * D * 4)) || (st = b->alloc(b->att, R * D * 4)) ||
       (st = b->alloc(b->att_rowmax, R * 4)) || (st = b->alloc(b->fnorm, R * D * 4)) || (st = b->alloc(b->fnorm_rowmax, R * 4)))
     return st;
-  if (m->n_attn > 0 && (st = b->alloc(b->kvlin, (size_t)S * b->pmax * 2 * D * 4))) return st;
+  // a prefill row's key and value: session i's row t of a pass is row (i - first session) * P + t,
+  // below the pass's tiles x 128 scratch rows
+  if (m->n_attn > 0 && (st = b->alloc(b->kvlin, R * 2 * D * 4))) return st;
   {
     // K tiles of the widest GEMM (K = 3D for W1, H for W2): beyond the A slots, the block kernel
     // slices its first chunk once and reads the planes back from this per-SM cache
@@ -635,16 +654,52 @@ static void build_block_args(const DevBatch& b, int P, int bi, bool fuse_head, i
   }
 }
 
+// A prefill pass over the contiguous tiles [t0, t0 + nt) (sessions [s0, s0 + ns)) of a batch
+// whose scratch holds fewer rows than a whole prefill needs. The kernels index scratch rows by
+// the global row (tile * 128 + r) and a segment's keys/values by the session: the pass hands
+// them those bases moved back by its first row and first session, so the rows it touches are
+// the first nt * 128 of the buffers.
+struct PassRange {
+  int t0 = 0, nt = 0, s0 = 0, ns = 0;
+};
+
+template <class T>
+static T* rows_back(T* p, size_t n) {
+  return p ? reinterpret_cast<T*>(reinterpret_cast<uintptr_t>(p) - n * sizeof(T)) : p;
+}
+
+// Tiles of 128 rows a segment of P rows per session takes for the batch's sessions.
+static int segment_tiles(const DevBatch& b, int P) {
+  const int spt = std::max(1, 128 / P);
+  return (b.S + spt - 1) / spt;
+}
+
 // Enqueues the blocks (and attention sublayers) of one segment: P rows per session, P = 1 a decode
-// step; ends with the final RMSNorm of every row.
-static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = false) {
+// step; ends with the final RMSNorm of every row. pr: a prefill pass over some tiles (null: all).
+static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = false, const PassRange* pr = nullptr) {
   const DevModel& m = *b.m;
   cudaStream_t s = b.stream;
   const int nb = (int)m.blocks.size();
+  if (P > 1 && !pr && (size_t)segment_tiles(b, P) * 128 > b.rows)
+    return set_error(kUnsupported, "prefill rows exceed the batch's scratch (a pass over a tile list needs them all)");
+  const size_t row0 = pr ? (size_t)pr->t0 * 128 : 0, kv0 = pr ? (size_t)pr->s0 * P : 0;
   int bs = 0;
   for (int bi = 0; bi <= nb; ++bi) {
     BlockArgs a;
     build_block_args(b, P, bi, fuse_head, &bs, a);
+    if (pr) {
+      a.tile0 = pr->t0;
+      a.cur = rows_back(a.cur, row0 * m.D);
+      a.blockin = rows_back(a.blockin, row0 * m.D);
+      a.xbuf = rows_back(a.xbuf, row0 * 3 * m.D);
+      a.hbuf = rows_back(a.hbuf, row0 * m.H);
+      a.qbuf = rows_back(a.qbuf, row0 * m.D);
+      a.att = rows_back(a.att, row0 * m.D);
+      a.att_rowmax = rows_back(a.att_rowmax, row0);
+      a.fnorm = rows_back(a.fnorm, row0 * m.D);
+      a.fnorm_rowmax = rows_back(a.fnorm_rowmax, row0);
+      a.kvlin = rows_back(a.kvlin, kv0 * 2 * m.D);
+    }
     const bool final_k = bi == nb;
     if (P == 1 && b.decode_kernel) {
       const int grid = (b.S + m.dec_r - 1) / m.dec_r;
@@ -654,7 +709,7 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
       else kern = kf == 1 ? block_decode_kernel<1, 16, 3> : kf == 2 ? block_decode_kernel<2, 16, 3> : block_decode_kernel<3, 16, 3>;
       kern<<<grid, kDThreads, m.dec_smem, s>>>(a);
     } else {
-      int grid = a.n_tiles;
+      int grid = pr ? pr->nt : a.n_tiles;
       if (b.n_pass_tiles > 0) {
         a.tile_list = b.pass_tiles;
         grid = b.n_pass_tiles;
@@ -714,6 +769,14 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
         }
       } else {
         int grid = b.S;
+        if (pr) {
+          aa.sess0 = pr->s0;
+          grid = pr->ns;
+          aa.qbuf = rows_back(aa.qbuf, row0 * m.D);
+          aa.att = rows_back(aa.att, row0 * m.D);
+          aa.att_rowmax = rows_back(aa.att_rowmax, row0);
+          aa.kvlin = rows_back(aa.kvlin, kv0 * 2 * m.D);
+        }
         if (b.n_pass_sess > 0) {
           aa.sess_list = b.pass_sess;
           grid = b.n_pass_sess;
@@ -741,6 +804,77 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
   return kOk;
 }
 
+// The head over the final-normed rows of sessions [s0, s0 + ns) of one pass (its scratch rows
+// start at row0), with the selection partials of those sessions.
+static int enqueue_head(DevBatch& b, int P, int mode, bool want_logits, int s0, int ns, size_t row0, LaunchLog* log) {
+  const DevModel& m = *b.m;
+  HeadArgs h;
+  memset(&h, 0, sizeof(h));
+  h.n_sess = ns;
+  h.D = m.D;
+  h.V = m.V;
+  h.nsplit = b.nsplit;
+  h.nchunks = m.head.nchunks;
+  h.cps = (m.head.nchunks + b.nsplit - 1) / b.nsplit;
+  h.ktiles = m.head.ktiles;
+  h.rowmap = (P == 1 ? b.rowmap_id : b.rowmap) + s0;
+  h.fnorm = rows_back(b.fnorm, row0 * m.D);
+  h.fnorm_rowmax = rows_back(b.fnorm_rowmax, row0);
+  h.tiles = m.head.tiles;
+  h.scale = m.head.scale;
+  h.head_b = m.head_b;
+  h.topk = mode == 1 ? b.topk : 0;
+  h.target = mode == 2 ? b.target + s0 : nullptr;
+  h.logits_out = want_logits || mode == 3 ? b.logits + (size_t)s0 * m.V : nullptr;
+  const size_t np = (size_t)b.nsplit * 4;  // partials per session: splits x column quarters
+  h.part = b.part + (size_t)s0 * np;
+  h.topv = b.topv ? b.topv + (size_t)s0 * np * b.topk : nullptr;
+  h.topi = b.topi ? b.topi + (size_t)s0 * np * b.topk : nullptr;
+  dim3 hg((ns + 127) / 128, b.nsplit);
+  head_kernel<<<hg, kHeadThreads, kHeadSmem, b.stream>>>(h);
+  MC_CUDA(cudaGetLastError());
+  if (log) log->record(b.stream, 3);
+  return kOk;
+}
+
+// The selection of sessions [s0, s0 + ns); bump: this launch advances the step counter (the last
+// selection of a step).
+static int enqueue_select(DevBatch& b, int mode, double inv_temp, uint32_t session0, bool advance_from_len, int s0,
+                          int ns, bool bump, LaunchLog* log) {
+  const size_t np = (size_t)b.nsplit * 4;
+  SelectArgs sa;
+  memset(&sa, 0, sizeof(sa));
+  sa.n_sess = ns;
+  sa.nsplit = (int)np;
+  sa.topk = b.topk;
+  sa.mode = mode;
+  sa.inv_temp = inv_temp;
+  sa.session0 = session0 + (uint32_t)s0;
+  sa.part = b.part + (size_t)s0 * np;
+  sa.topv = b.topv ? b.topv + (size_t)s0 * np * b.topk : nullptr;
+  sa.topi = b.topi ? b.topi + (size_t)s0 * np * b.topk : nullptr;
+  sa.step = b.step;
+  sa.out_stride = b.out_stride;
+  sa.next_tok = b.next_tok + s0;
+  sa.out_tok = b.out_tok ? b.out_tok + (size_t)s0 * b.out_stride : nullptr;
+  sa.out_prob = b.out_prob ? b.out_prob + (size_t)s0 * b.out_stride : nullptr;
+  sa.out_logprob = b.out_logprob ? b.out_logprob + (size_t)s0 * b.out_stride : nullptr;
+  sa.pos = b.pos + s0;
+  sa.seglen = b.seglen + s0;
+  sa.advance_from_len = advance_from_len ? 1 : 0;
+  sa.done = bump ? b.sel_done : nullptr;  // the last block of that launch advances the step counter
+  sa.n_stops = b.n_stops;
+  if (b.per_session) {
+    sa.gen_n = b.gen_n + s0;
+    sa.limit = b.limit ? b.limit + s0 : nullptr;
+  }
+  for (int k = 0; k < b.n_stops; ++k) sa.stops[k] = b.stops[k];
+  select_kernel<<<(ns + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, b.stream>>>(sa);
+  MC_CUDA(cudaGetLastError());
+  if (log) log->record(b.stream, 4);
+  return kOk;
+}
+
 int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t session0, bool want_logits,
                     bool advance_from_len, LaunchLog* log = nullptr) {
   const DevModel& m = *b.m;
@@ -748,105 +882,70 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
   // greedy decode steps without logits: the head and the selection are fused into the final
   // decode launch
   const bool fuse = P == 1 && b.decode_kernel && mode == 0 && !want_logits && !getenv("MC_NO_FUSED_HEAD");
-  int st = enqueue_layers(b, P, log, fuse);
-  if (st != kOk) return st;
-  if (fuse) return kOk;
-  HeadArgs h;
-  memset(&h, 0, sizeof(h));
-  h.n_sess = b.S;
-  h.D = m.D;
-  h.V = m.V;
-  h.nsplit = b.nsplit;
-  h.nchunks = m.head.nchunks;
-  h.cps = (m.head.nchunks + b.nsplit - 1) / b.nsplit;
-  h.ktiles = m.head.ktiles;
-  h.rowmap = P == 1 ? b.rowmap_id : b.rowmap;
-  h.fnorm = b.fnorm;
-  h.fnorm_rowmax = b.fnorm_rowmax;
-  h.tiles = m.head.tiles;
-  h.scale = m.head.scale;
-  h.head_b = m.head_b;
-  h.topk = mode == 1 ? b.topk : 0;
-  h.target = mode == 2 ? b.target : nullptr;
-  h.logits_out = want_logits || mode == 3 ? b.logits : nullptr;
-  h.part = b.part;
-  h.topv = b.topv;
-  h.topi = b.topi;
-  dim3 hg((b.S + 127) / 128, b.nsplit);
-  head_kernel<<<hg, kHeadThreads, kHeadSmem, s>>>(h);
-  MC_CUDA(cudaGetLastError());
-  if (log) log->record(s, 3);
-  if (mode == 3) {
-    // the whole decode-loop policy over the materialised logits; the generated tokens so far are
-    // the first *step columns of out_tok
-    PolicyArgs pa;
-    memset(&pa, 0, sizeof(pa));
-    pa.n_rows = b.S;
-    pa.V = m.V;
-    pa.logits = b.logits;
-    pa.temperature = b.pol.temperature;
-    pa.rep_penalty = b.pol.rep_penalty;
-    pa.top_p = b.pol.top_p;
-    pa.top_k = b.pol.top_k;
-    pa.rep_window = b.pol.rep_window;
-    pa.ban_trigrams = b.pol.ban_trigrams;
-    pa.prefix = b.pol_prefix;
-    pa.prefix_len = b.pol_prefix_len;
-    pa.prefix_stride = b.pol_prefix_cap;
-    pa.gen = b.out_tok;
-    pa.gen_stride = b.out_stride;
-    pa.dfa = b.pol.dfa;
-    pa.dfa_state = b.pol.dfa ? b.pol_state : nullptr;
-    pa.session0 = session0;
-    pa.step = b.step;
-    if (b.per_session) {
-      pa.gen_n = b.gen_n;
-      pa.limit = b.limit;
-      pa.key = b.key;
+  int st;
+  const int total = segment_tiles(b, P);
+  const int per = (int)(b.rows / 128);
+  if (P > 1 && b.n_pass_tiles == 0 && total > per) {
+    // a prefill larger than the scratch: passes over contiguous tiles, each through the head and
+    // the selection of its sessions (the policy runs once, over the logits of all of them)
+    const int spt = std::max(1, 128 / P);
+    for (int t0 = 0; t0 < total; t0 += per) {
+      PassRange pr;
+      pr.t0 = t0;
+      pr.nt = std::min(per, total - t0);
+      pr.s0 = t0 * spt;
+      pr.ns = std::min(b.S, (t0 + pr.nt) * spt) - pr.s0;
+      if ((st = enqueue_layers(b, P, log, false, &pr)) != kOk) return st;
+      if ((st = enqueue_head(b, P, mode, want_logits, pr.s0, pr.ns, (size_t)t0 * 128, log)) != kOk) return st;
+      if (mode != 3 && (st = enqueue_select(b, mode, inv_temp, session0, advance_from_len, pr.s0, pr.ns,
+                                            t0 + pr.nt >= total, log)) != kOk)
+        return st;
     }
-    pa.out_stride = b.out_stride;
-    pa.next_tok = b.next_tok;
-    pa.out_tok = b.out_tok;
-    pa.out_prob = b.out_prob;
-    pa.pos = b.pos;
-    pa.seglen = b.seglen;
-    pa.advance_from_len = advance_from_len ? 1 : 0;
-    pa.done = b.sel_done;
-    pa.n_stops = b.n_stops;
-    for (int k = 0; k < b.n_stops; ++k) pa.stops[k] = b.stops[k];
-    if ((st = launch_policy(pa, s)) != kOk) return st;
-    if (log) log->record(s, 4);
-    return kOk;
+  } else {
+    if ((st = enqueue_layers(b, P, log, fuse)) != kOk) return st;
+    if (fuse) return kOk;
+    if ((st = enqueue_head(b, P, mode, want_logits, 0, b.S, 0, log)) != kOk) return st;
+    if (mode != 3) return enqueue_select(b, mode, inv_temp, session0, advance_from_len, 0, b.S, true, log);
   }
-  SelectArgs sa;
-  memset(&sa, 0, sizeof(sa));
-  sa.n_sess = b.S;
-  sa.nsplit = b.nsplit * 4;  // partials per session: splits x column quarters
-  sa.topk = b.topk;
-  sa.mode = mode;
-  sa.inv_temp = inv_temp;
-  sa.session0 = session0;
-  sa.part = b.part;
-  sa.topv = b.topv;
-  sa.topi = b.topi;
-  sa.step = b.step;
-  sa.out_stride = b.out_stride;
-  sa.next_tok = b.next_tok;
-  sa.out_tok = b.out_tok;
-  sa.out_prob = b.out_prob;
-  sa.out_logprob = b.out_logprob;
-  sa.pos = b.pos;
-  sa.seglen = b.seglen;
-  sa.advance_from_len = advance_from_len ? 1 : 0;
-  sa.done = b.sel_done;  // the last block advances the step counter
-  sa.n_stops = b.n_stops;
+  if (mode != 3) return kOk;
+  // the whole decode-loop policy over the materialised logits; the generated tokens so far are
+  // the first *step columns of out_tok
+  PolicyArgs pa;
+  memset(&pa, 0, sizeof(pa));
+  pa.n_rows = b.S;
+  pa.V = m.V;
+  pa.logits = b.logits;
+  pa.temperature = b.pol.temperature;
+  pa.rep_penalty = b.pol.rep_penalty;
+  pa.top_p = b.pol.top_p;
+  pa.top_k = b.pol.top_k;
+  pa.rep_window = b.pol.rep_window;
+  pa.ban_trigrams = b.pol.ban_trigrams;
+  pa.prefix = b.pol_prefix;
+  pa.prefix_len = b.pol_prefix_len;
+  pa.prefix_stride = b.pol_prefix_cap;
+  pa.gen = b.out_tok;
+  pa.gen_stride = b.out_stride;
+  pa.dfa = b.pol.dfa;
+  pa.dfa_state = b.pol.dfa ? b.pol_state : nullptr;
+  pa.session0 = session0;
+  pa.step = b.step;
   if (b.per_session) {
-    sa.gen_n = b.gen_n;
-    sa.limit = b.limit;
+    pa.gen_n = b.gen_n;
+    pa.limit = b.limit;
+    pa.key = b.key;
   }
-  for (int k = 0; k < b.n_stops; ++k) sa.stops[k] = b.stops[k];
-  select_kernel<<<(b.S + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, s>>>(sa);
-  MC_CUDA(cudaGetLastError());
+  pa.out_stride = b.out_stride;
+  pa.next_tok = b.next_tok;
+  pa.out_tok = b.out_tok;
+  pa.out_prob = b.out_prob;
+  pa.pos = b.pos;
+  pa.seglen = b.seglen;
+  pa.advance_from_len = advance_from_len ? 1 : 0;
+  pa.done = b.sel_done;
+  pa.n_stops = b.n_stops;
+  for (int k = 0; k < b.n_stops; ++k) pa.stops[k] = b.stops[k];
+  if ((st = launch_policy(pa, s)) != kOk) return st;
   if (log) log->record(s, 4);
   return kOk;
 }
@@ -868,44 +967,57 @@ int ensure_score_rows(DevBatch& b, size_t rows) {
 }
 
 // The forward pass of a prompt segment (P rows per session) and the log-probability of every
-// row's target: sc_logprob[r] for the rows r with sc_valid[r] != 0.
+// row's target: sc_logprob[r] for the rows r with sc_valid[r] != 0 (r = session * P + t). A segment
+// larger than the batch's scratch runs in passes over contiguous sessions, each scored at once.
 int enqueue_score(DevBatch& b, int P, size_t rows) {
   const DevModel& m = *b.m;
   cudaStream_t s = b.stream;
-  int st = enqueue_layers(b, P, nullptr);
-  if (st != kOk) return st;
-  HeadArgs h;
-  memset(&h, 0, sizeof(h));
-  h.n_sess = (int)rows;
-  h.D = m.D;
-  h.V = m.V;
-  h.nsplit = b.sc_nsplit;
-  h.nchunks = m.head.nchunks;
-  h.cps = (m.head.nchunks + b.sc_nsplit - 1) / b.sc_nsplit;
-  h.ktiles = m.head.ktiles;
-  h.rowmap = b.sc_rowmap;
-  h.fnorm = b.fnorm;
-  h.fnorm_rowmax = b.fnorm_rowmax;
-  h.tiles = m.head.tiles;
-  h.scale = m.head.scale;
-  h.head_b = m.head_b;
-  h.target = b.sc_target;
-  h.part = b.sc_part;
-  dim3 hg((unsigned)((rows + 127) / 128), b.sc_nsplit);
-  head_kernel<<<hg, kHeadThreads, kHeadSmem, s>>>(h);
-  MC_CUDA(cudaGetLastError());
-  SelectArgs sa;
-  memset(&sa, 0, sizeof(sa));
-  sa.n_sess = (int)rows;
-  sa.nsplit = b.sc_nsplit * 4;
-  sa.mode = 2;
-  sa.part = b.sc_part;
-  sa.out_stride = 1;
-  sa.next_tok = b.sc_next;
-  sa.out_logprob = b.sc_logprob;
-  sa.seglen = b.sc_valid;  // rows without a target are skipped
-  select_kernel<<<(unsigned)((rows + kSelectWarps - 1) / kSelectWarps), kSelectWarps * 32, 0, s>>>(sa);
-  MC_CUDA(cudaGetLastError());
+  const int total = segment_tiles(b, P), per = (int)(b.rows / 128);
+  const int spt = std::max(1, 128 / P);
+  for (int t0 = 0; t0 < total; t0 += per) {
+    PassRange pr;
+    pr.t0 = t0;
+    pr.nt = std::min(per, total - t0);
+    pr.s0 = t0 * spt;
+    pr.ns = std::min(b.S, (t0 + pr.nt) * spt) - pr.s0;
+    const bool whole = pr.nt == total;
+    int st = enqueue_layers(b, P, nullptr, false, whole ? nullptr : &pr);
+    if (st != kOk) return st;
+    const size_t r0 = (size_t)pr.s0 * P, nr = std::min(rows, (size_t)(pr.s0 + pr.ns) * P) - r0;
+    const size_t row0 = whole ? 0 : (size_t)t0 * 128;
+    HeadArgs h;
+    memset(&h, 0, sizeof(h));
+    h.n_sess = (int)nr;
+    h.D = m.D;
+    h.V = m.V;
+    h.nsplit = b.sc_nsplit;
+    h.nchunks = m.head.nchunks;
+    h.cps = (m.head.nchunks + b.sc_nsplit - 1) / b.sc_nsplit;
+    h.ktiles = m.head.ktiles;
+    h.rowmap = b.sc_rowmap + r0;
+    h.fnorm = rows_back(b.fnorm, row0 * m.D);
+    h.fnorm_rowmax = rows_back(b.fnorm_rowmax, row0);
+    h.tiles = m.head.tiles;
+    h.scale = m.head.scale;
+    h.head_b = m.head_b;
+    h.target = b.sc_target + r0;
+    h.part = b.sc_part + r0 * b.sc_nsplit * 4;
+    dim3 hg((unsigned)((nr + 127) / 128), b.sc_nsplit);
+    head_kernel<<<hg, kHeadThreads, kHeadSmem, s>>>(h);
+    MC_CUDA(cudaGetLastError());
+    SelectArgs sa;
+    memset(&sa, 0, sizeof(sa));
+    sa.n_sess = (int)nr;
+    sa.nsplit = b.sc_nsplit * 4;
+    sa.mode = 2;
+    sa.part = b.sc_part + r0 * b.sc_nsplit * 4;
+    sa.out_stride = 1;
+    sa.next_tok = b.sc_next + r0;
+    sa.out_logprob = b.sc_logprob + r0;
+    sa.seglen = b.sc_valid + r0;  // rows without a target are skipped
+    select_kernel<<<(unsigned)((nr + kSelectWarps - 1) / kSelectWarps), kSelectWarps * 32, 0, s>>>(sa);
+    MC_CUDA(cudaGetLastError());
+  }
   return kOk;
 }
 

@@ -12,6 +12,7 @@
 //    activation row is sliced into three int8 digit planes (mc_sm100.cuh: slice3) by the
 //    row-owning warps while the weights stream in by TMA; three MMAs per K step accumulate the
 //    planes into three exact s32 accumulators that the epilogue recombines.
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -376,6 +377,28 @@ __global__ void __launch_bounds__(160, 1)
 // ------------------------------------------------------------------------------------------------
 // Host launchers
 // ------------------------------------------------------------------------------------------------
+// Per-device set-up of the GEMM kernels, done once per device under a lock: the shared-memory
+// size attribute of a kernel is a setting of the device that is current when it is made, and the
+// multiprocessor count (the persistent grid) can differ between devices.
+static int gemm_device_setup(int* n_sm) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static int sms[kMaxDevices] = {0};  // 0: not set up yet
+  int dev = 0;
+  MC_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(kUnsupported, "gemm: device ordinal above 63");
+  std::lock_guard<std::mutex> lk(mu);
+  if (sms[dev] == 0) {
+    MC_CUDA(cudaFuncSetAttribute(gemm::gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kI8Smem));
+    MC_CUDA(cudaFuncSetAttribute(gemm::gemm_f32a_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kFSmem));
+    int n = 0;
+    MC_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    sms[dev] = std::max(n, 1);
+  }
+  *n_sm = sms[dev];
+  return kOk;
+}
+
 int gemm_i8_launch(const int8_t* a, const int8_t* w, int M, int N, int K, const float* row_scale,
                    const float* col_scale, const float* bias, int32_t* c_i32, float* y, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0 || N % gemm::kI8BN != 0 || K % 16 != 0)
@@ -384,18 +407,10 @@ int gemm_i8_launch(const int8_t* a, const int8_t* w, int M, int N, int K, const 
   CUtensorMap ma, mw;
   if (!make_tmap_i8(&ma, a, M, K, K, gemm::kBK, gemm::kBM)) return kCudaError;
   if (!make_tmap_i8(&mw, w, N, K, K, gemm::kBK, gemm::kI8BN)) return kCudaError;
-  static bool attr = false;
-  if (!attr) {
-    MC_CUDA(cudaFuncSetAttribute(gemm::gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kI8Smem));
-    attr = true;
-  }
+  int n_sm = 0;
+  const int st = gemm_device_setup(&n_sm);
+  if (st != kOk) return st;
   gemm::I8Args args{M, N, K, row_scale, col_scale, bias, c_i32, y};
-  static int n_sm = 0;
-  if (!n_sm) {
-    int dev = 0;
-    MC_CUDA(cudaGetDevice(&dev));
-    MC_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
-  }
   const int tiles = (N / gemm::kI8BN) * ((M + gemm::kBM - 1) / gemm::kBM);
   gemm::gemm_i8_kernel<<<std::min(tiles, n_sm), gemm::kI8Threads, gemm::kI8Smem, stream>>>(ma, mw, args);
   MC_CUDA(cudaGetLastError());
@@ -408,11 +423,9 @@ int gemm_f32a_launch(const float* a, const int8_t* w, int M, int N, int K, float
     return set_error(kInvalidArgument, "gemm_f32a: need M,N,K > 0, N % 128 == 0 and K % 16 == 0");
   CUtensorMap mw;
   if (!make_tmap_i8(&mw, w, N, K, K, gemm::kBK, gemm::kFBN)) return kCudaError;
-  static bool attr = false;
-  if (!attr) {
-    MC_CUDA(cudaFuncSetAttribute(gemm::gemm_f32a_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kFSmem));
-    attr = true;
-  }
+  int n_sm = 0;
+  const int st = gemm_device_setup(&n_sm);
+  if (st != kOk) return st;
   gemm::row_absmax_kernel<<<(M + 7) / 8, 256, 0, stream>>>(a, M, K, row_max_scratch);
   gemm::F32Args args{M, N, K, a, row_max_scratch, w_scale, bias, y, slices};
   dim3 grid(N / gemm::kFBN, (M + gemm::kBM - 1) / gemm::kBM);
@@ -425,8 +438,7 @@ int gemm_f32a_launch(const float* a, const int8_t* w, int M, int N, int K, float
 // Allocation-free form of the float32-activation GEMM
 // ------------------------------------------------------------------------------------------------
 // Some callers cannot allocate device memory: a host runtime that may only pass buffers it
-// registered in advance, a service whose GPU memory is budgeted once at start-up, or code issuing
-// work while a CUDA graph is being captured (cudaMalloc is not allowed there). For them, the one
+// registered in advance, or a service whose GPU memory is budgeted once at start-up. For them, the one
 // scratch buffer this GEMM needs, the largest magnitude of every activation row (one float per
 // row), lives in this fixed device array. Every GPU that loads the library holds it (256 KB)
 // until the process exits.
@@ -463,6 +475,9 @@ int gemm_f32a_noalloc_launch(const float* a, const int8_t* w, int M, int N, int 
   if (M > kNoAllocMaxRows)
     return set_error(kInvalidArgument, "gemm_f32a_noalloc: m = " + std::to_string(M) + " is above the fixed maximum of " +
                                            std::to_string(kNoAllocMaxRows) + " rows");
+  // every shape check before the first CUDA call, so a rejected call has no side effects
+  if (M <= 0 || N <= 0 || K <= 0 || N % gemm::kFBN != 0 || K % 16 != 0)
+    return set_error(kInvalidArgument, "gemm_f32a_noalloc: need M,N,K > 0, N % 128 == 0 and K % 16 == 0");
   float* row_max = nullptr;
   const int st = noalloc_row_max(&row_max);
   if (st != kOk) return st;

@@ -274,7 +274,8 @@ int mc_sched_open(mc_model* model, int slots, int context_size, int max_prompt, 
   if (penalize && sp->rep_window <= 0)
     return set_error(kInvalidArgument, "mc_sched_open: a prompt penalty needs rep_window >= 1");
   auto q = std::make_unique<mc_sched>();
-  if ((st = mc_batch_open(model, slots, context_size, max_prompt, 0, &q->batch)) != kOk) return st;
+  // admission passes run over lists of tiles: the batch keeps a scratch row for every prefill row
+  if ((st = batch_open(model, slots, context_size, max_prompt, 0, false, &q->batch)) != kOk) return st;
   q->sp = *sp;
   q->penalize_prompt = penalize ? 1 : 0;
   // argmax with nothing to change the logits is greedyLoop's selection: the decode steps then

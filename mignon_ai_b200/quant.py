@@ -38,6 +38,12 @@ _lib.register({
     "mc_append": [c_vp, c_vp, c_vp, c_vp, c_vp],
     "mc_generate": [c_vp, c_vp, c_vp, _i, _i, ctypes.c_double, ctypes.c_uint32, c_vp, c_vp],
     "mc_generate_stops": [c_vp, c_vp, c_vp, _i, _i, ctypes.c_double, ctypes.c_uint32, c_vp, _i, c_vp, c_vp, c_vp],
+    "mc_generate_limits": [c_vp, c_vp, c_vp, _i, c_vp, _i, ctypes.c_double, ctypes.c_uint32, c_vp, c_vp, c_vp],
+    "mc_generate_limits_dev": [c_vp, c_vp, c_vp, _i, _i, c_vp, _i, ctypes.c_double, ctypes.c_uint32, c_vp, c_vp],
+    "mc_generate_dev": [c_vp, c_vp, c_vp, _i, _i, _i, ctypes.c_double, ctypes.c_uint32, c_vp, c_vp],
+    "mc_batch_stream": [c_vp, _i, ctypes.POINTER(c_vp)],
+    "mc_batch_error": [c_vp],
+    "mc_probe_mma_i8": [_i, _i, _i, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)],
     "mc_generate_policy": [c_vp, c_vp, c_vp, _i, _i, c_vp, _i, c_vp, _i, c_vp, ctypes.c_uint32, c_vp, _i, c_vp, c_vp,
                            c_vp],
     "mc_sample_rows": [_i, c_vp, _i, _i, c_vp, c_vp, _i, c_vp, c_vp, c_vp, ctypes.c_uint32, ctypes.c_uint32, c_vp,
@@ -286,6 +292,22 @@ class SessionBatch:
         _lib.check(_lib.lib().mc_generate_stops(self._h, _lib.ptr(p), _lib.ptr(lens), p.shape[1], n_new, temperature,
                                                 session0, _lib.ptr(st) if st.size else None, int(st.size),
                                                 _lib.ptr(toks), _lib.ptr(probs), _lib.ptr(out_lens)))
+        return toks, probs, out_lens
+
+    def generate_limits(self, prompts, lens, max_tokens, temperature: float = 0.0, session0: int = 0):
+        """max_tokens[s] tokens for session s after its prompt (pkg/infer.Generate's MaxTokens per
+        session; greedy, or sampled with temperature > 0 like ``generate``): (tokens, probs,
+        lengths), tokens [count x max(max_tokens)] with -1 past each session's limit."""
+        p = np.ascontiguousarray(prompts, np.int32)
+        lens = np.ascontiguousarray(lens, np.int32)
+        lim = np.ascontiguousarray(max_tokens, np.int32)
+        n_max = int(lim.max())
+        toks = np.zeros((self.count, n_max), np.int32)
+        probs = np.zeros((self.count, n_max), np.float32)
+        out_lens = np.zeros(self.count, np.int32)
+        _lib.check(_lib.lib().mc_generate_limits(self._h, _lib.ptr(p), _lib.ptr(lens), p.shape[1], _lib.ptr(lim), n_max,
+                                                 temperature, session0, _lib.ptr(toks), _lib.ptr(probs),
+                                                 _lib.ptr(out_lens)))
         return toks, probs, out_lens
 
     def generate_policy(self, prompts, lens, n_new: int, sampling: Sampling, penalize_prompt: bool = False,

@@ -1,8 +1,8 @@
 """The allocation-free GEMM entry point (mc_gemm_f32a_noalloc_dev) against the allocating one.
 
 Some programs that drive this library cannot allocate GPU memory when they call it: a host
-runtime that may only hand over buffers it registered in advance, a service whose GPU memory is
-budgeted once at start-up, or code that issues work while a CUDA graph is being captured. The
+runtime that may only hand over buffers it registered in advance, or a service whose GPU memory is
+budgeted once at start-up. The
 allocation-free entry point serves them by keeping its one scratch buffer (the per-row maxima
 the activation slicing needs) in a fixed device array inside the library. This test checks, on
 two calls in a row with different inputs, that its results equal the allocating entry point's
@@ -63,3 +63,39 @@ def test_noalloc_gemm_rejects_rows_above_its_fixed_maximum():
     torch.cuda.synchronize()
     assert status == 1  # MC_INVALID_ARGUMENT
     assert b"65536" in L.mc_last_error()
+
+
+def test_noalloc_gemm_on_two_devices():
+    """The set-up of the first call (the array's address, the kernels' shared-memory attribute)
+    is per device: a first call on device 0 must not leave device 1 without it."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    L = _declare()
+    rng = np.random.default_rng(12)
+    m, n, k = 256, 256, 512
+    xs = (rng.standard_normal((m, k)) * 2).astype(np.float32)
+    ws = rng.integers(-127, 128, (n, k)).astype(np.int8)
+    for d in (0, 1):
+        dev = torch.device("cuda", d)
+        with torch.cuda.device(d):
+            x, w = torch.from_numpy(xs).to(dev), torch.from_numpy(ws).to(dev)
+            y_ref = torch.zeros((m, n), dtype=torch.float32, device=dev)
+            scratch = torch.zeros(m, dtype=torch.float32, device=dev)
+            _lib.check(L.mc_gemm_f32a_dev(_lib.ptr(x), _lib.ptr(w), m, n, k, 0.5, None, _lib.ptr(y_ref), None,
+                                          _lib.ptr(scratch), None))
+            y = torch.full((m, n), float("nan"), dtype=torch.float32, device=dev)
+            _lib.check(L.mc_gemm_f32a_noalloc_dev(_lib.ptr(x), _lib.ptr(w), m, n, k, 0.5, None, _lib.ptr(y), None))
+            torch.cuda.synchronize(dev)
+            assert torch.equal(y, y_ref), f"device {d}"
+
+
+def test_noalloc_gemm_rejects_bad_shapes_before_any_cuda_call():
+    import torch
+    L = _declare()
+    dev = torch.device("cuda:0")
+    x = torch.zeros((64, 128), dtype=torch.float32, device=dev)
+    w = torch.zeros((100, 128), dtype=torch.int8, device=dev)
+    y = torch.zeros((64, 100), dtype=torch.float32, device=dev)
+    status = L.mc_gemm_f32a_noalloc_dev(_lib.ptr(x), _lib.ptr(w), 64, 100, 128, 1.0, None, _lib.ptr(y), None)
+    assert status == 1  # MC_INVALID_ARGUMENT: N % 128 != 0
