@@ -62,6 +62,23 @@ def session_range(rank, sessions):
     return rank * sessions, (rank + 1) * sessions
 
 
+def strong_range(rank, world, n):
+    """Items [first, end) of a rank when n items are split evenly over the ranks (strong scaling)."""
+    return rank * n // world, (rank + 1) * n // world
+
+
+def sample_inputs(first, end, n_total):
+    """The config-3 workload's sessions [first, end) of n_total: prompts (64 columns), prompt
+    lengths U[16, 64] (seed 3) and token limits (decode to the 128-token context); the Philox rows
+    are the global session ids, so any split over ranks gives the same sessions."""
+    from mignon_ai_b200 import synth
+    lens_all = synth.prompt_lengths(n_total, 16, 64, seed=3)
+    prompts = np.ascontiguousarray(synth.prompts_uniform_fast(end, 64, synth.CONFIGS[3].vocab, seed=3)[first:end])
+    lens = np.ascontiguousarray(lens_all[first:end])
+    limits = (SAMPLE_CTX - lens).astype(np.int32)
+    return prompts, lens, limits, lens_all
+
+
 def max_over_ranks(ms, dist, device):
     """The slowest rank's time (every rank calls this, in the same order)."""
     if dist is None:
@@ -257,70 +274,120 @@ SCORE_SEQS = 16384
 SCORE_LEN = 128
 
 
+def _dist_setup(timeout_s=300):
+    """torchrun ranks (one per GPU, NCCL only for barriers and the max over ranks): (world, rank,
+    local rank, process group module or None, device)."""
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s),
+                                device_id=torch.device("cuda", local_rank))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local_rank, dist, torch.device("cuda", local_rank)
+
+
 def run_score(args):
-    """Config 4: 16384 sequences of 128 uniform token ids (seed 4) scored in one pass through the
-    public host API (mc_score: sequences in from host memory, per-token log-probabilities out),
-    timed with CUDA events around the whole call; the CPU restatement scores a sample beside it."""
+    """Config 4: 16384 sequences of 128 uniform token ids (seed 4), split evenly over the ranks
+    (strong scaling; rank g scores the contiguous sequences [g*N/G, (g+1)*N/G)), each scored in
+    one pass through the public host API (mc_score: sequences in from host memory, per-token
+    log-probabilities out), timed with CUDA events around the call, the max over ranks; the CPU
+    restatement scores a sample beside it (rank 0, one GPU)."""
     import torch
     from mignon_ai_b200 import quant, synth
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import pyoracle
+    world, rank, local_rank, dist, dev = _dist_setup()
     spec = synth.CONFIGS[4]
-    n = SCORE_SEQS if args.sessions == SESSIONS else args.sessions
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
+    N = SCORE_SEQS if args.sessions == SESSIONS else args.sessions
+    first, end = strong_range(rank, world, N)
+    n = end - first
     data = synth.build_model_file(spec)
-    ctx = quant.Context((0,))
+    ctx = quant.Context((local_rank,))
     model = quant.Model.decode(data, ctx)
-    seqs = synth.prompts_uniform_fast(n, SCORE_LEN, spec.vocab, seed=4)
+    seqs = np.ascontiguousarray(synth.prompts_uniform_fast(end, SCORE_LEN, spec.vocab, seed=4)[first:end])
     lens = np.full(n, SCORE_LEN, np.int32)
     batch = model.new_batch(n, 0, SCORE_LEN)
+    if args.quick:  # profiling case: one scoring pass, nothing else
+        out = batch.score(seqs, lens)
+        print(json.dumps({"quick": True, "sequences": n, "sum_logprob": float(out.sum())}))
+        batch.close()
+        model.close()
+        ctx.close()
+        if dist:
+            dist.destroy_process_group()
+        return 0
     for _ in range(max(1, args.warmup)):
         out = batch.score(seqs, lens)
     steps = max(1, args.steps)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler([local_rank] if world == 1 else list(range(world))) if rank == 0 else None
+    if dist:
+        dist.barrier()
     torch.cuda.synchronize(dev)
+    if clocks:
+        clocks.start()
     e0.record()
     for _ in range(steps):
         out = batch.score(seqs, lens)
     e1.record()
     torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1) / steps
-    tokens = n * (SCORE_LEN - 1)
+    ms = max_over_ranks(e0.elapsed_time(e1), dist, dev) / steps
+    clk = clocks.stop() if clocks else None
+    tokens = N * (SCORE_LEN - 1)  # all ranks
     value = tokens / (ms / 1000.0)
     D, H, V, B, Sx = spec.state, spec.hidden, spec.vocab, spec.blocks, spec.steps
     spans = [min(p + 1, 64) for p in range(SCORE_LEN - 1)]
     score_mac = B * Sx * (D * D + 6 * H * D + 2 * D * H) + B * 4 * D * D + V * D + B * 2 * D * float(np.mean(spans))
-    achieved_tops = value * 2 * score_mac / 1e12
-    peak = measure_i8_peak(0)
-    # CPU restatement on a sample, all host threads
-    cores = os.cpu_count() or 1
-    k = max(cores, 32)
-    om = pyoracle.Model(data)
-    t0 = time.perf_counter()
-    want = om.score(seqs[:k], nthreads=cores)
-    cpu_s = time.perf_counter() - t0
-    err = float(np.max(np.abs(out[:k] - want)))
-    line = {"metric": "scored tokens/s (config-4 per-token log-probabilities)", "value": value, "unit": "tokens/s",
-            "n_gpus": 1, "steps": steps, "warmup": max(1, args.warmup), "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "none", "vs_baseline": None, "dtype": "int8 weights x float32 activations (3 int8 digit planes)",
-            "data": "synthetic",
-            "config": {"workload": "config4: D=192 H=512 6 blocks x 2 steps, attn 4 heads window 64, vocab 2048; "
-                                   "%d sequences x %d tokens (seed 4), every next-token log-probability" % (n, SCORE_LEN),
-                       "timing": "the host API call (sequences in, log-probabilities out) per step"},
-            "cpu_baseline": {"value": k * (SCORE_LEN - 1) / cpu_s, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "cpu_model": cpu_model(), "sample": "%d sequences of the workload" % k},
-            "roofline": {"bound": "tensor (int8)", "achieved": achieved_tops, "peak": peak["tops"], "unit": "TOPS",
-                         "frac": achieved_tops / peak["tops"], "peak_source": "mc_probe_mma_i8 on this GPU, this run",
-                         "algorithmic_ops_per_token": 2 * score_mac,
-                         "note": "MACs per scored token: B*S*(D^2 + 6HD + 2DH) + B*(4D^2 + 2*span*D) + V*D, span = "
-                                 "min(pos+1, 64), averaged over positions 0..126; counted once (the three digit "
-                                 "planes are overhead, not work)"},
-            "max_abs_dlogprob_vs_cpu": err}
-    print(json.dumps(line))
+    achieved_tops = value / world * 2 * score_mac / 1e12  # per GPU
+    peak = measure_i8_peak(local_rank) if rank == 0 else None
+    line = None
+    if rank == 0:
+        # CPU restatement on a sample, all host threads (and the parity of that sample)
+        cores = os.cpu_count() or 1
+        k = max(cores, 32) if (not args.no_cpu_baseline and world == 1) else 4
+        om = pyoracle.Model(data)
+        t0 = time.perf_counter()
+        want = om.score(seqs[:k], nthreads=cores)
+        cpu_s = time.perf_counter() - t0
+        err = float(np.max(np.abs(out[:k] - want)))
+        line = {"metric": "scored tokens/s (config-4 per-token log-probabilities)", "value": value, "unit": "tokens/s",
+                "n_gpus": world, "steps": steps, "warmup": max(1, args.warmup), "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "int8 weights x float32 activations (3 int8 digit planes)", "data": "synthetic",
+                "config": {"workload": "config4: D=192 H=512 6 blocks x 2 steps, attn 4 heads window 64, vocab 2048; "
+                                       "%d sequences x %d tokens (seed 4) split over %d GPU(s), every next-token "
+                                       "log-probability" % (N, SCORE_LEN, world),
+                           "timing": "the host API call (sequences in, log-probabilities out) per step, max over ranks",
+                           "l2": "no flush: each pass writes and reads GBs of activation rows, far above the L2"},
+                "clocks": clk,
+                "roofline": {"bound": "tensor (int8)", "achieved": achieved_tops, "peak": peak["tops"], "unit": "TOPS",
+                             "frac": achieved_tops / peak["tops"], "peak_source": "mc_probe_mma_i8 on this GPU, this run",
+                             "algorithmic_ops_per_token": 2 * score_mac,
+                             "note": "per GPU. MACs per scored token: B*S*(D^2 + 6HD + 2DH) + B*(4D^2 + 2*span*D) + "
+                                     "V*D, span = min(pos+1, 64), averaged over positions 0..126; counted once (the "
+                                     "three digit planes are overhead, not work)"},
+                "parity": {"sequences": k, "max_abs_dlogprob_vs_cpu": err,
+                           "oracle": "CPU restatement of the reference engine (oracle/)"},
+                "device": {"rank": rank, "cuda_device": local_rank, "sequences": [first, end]}}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = {"value": k * (SCORE_LEN - 1) / cpu_s, "unit": "tokens/s", "cores": cores,
+                                    "kind": "port", "cpu_model": cpu_model(), "sample": "%d sequences of the workload" % k}
+        print(json.dumps(line))
+    else:
+        print(json.dumps({"rank": rank, "cuda_device": local_rank, "sequences": [first, end]}), file=sys.stderr)
     batch.close()
     model.close()
     ctx.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
 
 
@@ -535,27 +602,12 @@ def run_sample(args):
     One step = the whole job; the max over ranks of the CUDA-event time."""
     import torch
     from mignon_ai_b200 import _lib, quant, synth
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
-    else:
-        torch.cuda.set_device(0)
-    dev = torch.device("cuda", local_rank)
+    world, rank, local_rank, dist, dev = _dist_setup()
     spec = synth.CONFIGS[3]
     N = args.sessions if args.sessions != SESSIONS else SAMPLE_SESSIONS
-    first, end = rank * N // world, (rank + 1) * N // world
+    first, end = strong_range(rank, world, N)
     S = end - first
-    lens_all = synth.prompt_lengths(N, 16, 64, seed=3)
-    prompts = np.ascontiguousarray(synth.prompts_uniform_fast(end, 64, spec.vocab, seed=3)[first:end])
-    lens = np.ascontiguousarray(lens_all[first:end])
-    limits = (SAMPLE_CTX - lens).astype(np.int32)
+    prompts, lens, limits, lens_all = sample_inputs(first, end, N)
     n_max = int(SAMPLE_CTX - 16)
     data = synth.build_model_file(spec)
     ctx = quant.Context((local_rank,))
@@ -574,6 +626,16 @@ def run_sample(args):
         _lib.check(L.mc_generate_limits_dev(batch._h, d_prompts.data_ptr(), d_lens.data_ptr(), 64, 64,
                                             d_lim.data_ptr(), n_max, SAMPLE_T, first, d_tok.data_ptr(), None))
 
+    if args.quick:  # profiling case: one job, nothing else
+        job()
+        _lib.check(L.mc_batch_error(batch._h))
+        print(json.dumps({"quick": True, "sessions": S, "tokens": int((d_tok >= 0).sum().item())}))
+        batch.close()
+        model.close()
+        ctx.close()
+        if dist:
+            dist.destroy_process_group()
+        return 0
     for _ in range(args.warmup):
         job()
     _lib.check(L.mc_batch_error(batch._h))

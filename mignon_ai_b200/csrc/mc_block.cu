@@ -43,6 +43,7 @@ constexpr int kBlockSmem = kSmemA + kSmemB + 1024 /*align*/ + 16384 /*barriers, 
 
 struct Bars {
   uint64_t a_full[kASlots], a_empty[kASlots], a_tma[kASlots], b_full[kBStages], b_empty[kBStages], acc_full, acc_empty;
+  uint64_t a_pre;                      // the row warps wrote a GEMM's planes straight into the plane cache
   uint32_t tmem;
   float rowmax_n[kRows];               // max |norm cell| per row
   float rowmax_part[kTPR][kRows];       // per-thread partial maxima of an epilogue output
@@ -218,11 +219,30 @@ __device__ __forceinline__ void put4_2(uint8_t* sA, uint8_t* gA, int r, int e, f
   *reinterpret_cast<uint32_t*>(gtile + 2 * kTile + off) = p3;
 }
 
+// The three digit planes of four consecutive activations (K indices e..e+3) of tile row r written
+// only to the global copy of the A slots (the per-SM plane cache; K tile kt at gA + kt * kASlot).
+// A warp writing 128 consecutive K values of a row stores one whole 128-byte line per plane.
+__device__ __forceinline__ void put4_g(uint8_t* gA, int r, int e, float4 v, float inv) {
+  const int kt = e >> 7, k = e & 127;
+  uint8_t* gtile = gA + (size_t)kt * kASlot;
+  const uint32_t off = sw128_offset(r, k >> 4) + (k & 15);
+  uint32_t a0, a1, a2, a3, b0, b1, b2, b3, c0, c1, c2, c3;
+  slice3_bits(v.x, inv, a0, b0, c0);
+  slice3_bits(v.y, inv, a1, b1, c1);
+  slice3_bits(v.z, inv, a2, b2, c2);
+  slice3_bits(v.w, inv, a3, b3, c3);
+  *reinterpret_cast<uint32_t*>(gtile + off) = pack_low_bytes(a0, a1, a2, a3);
+  *reinterpret_cast<uint32_t*>(gtile + kTile + off) = pack_low_bytes(b0, b1, b2, b3);
+  *reinterpret_cast<uint32_t*>(gtile + 2 * kTile + off) = pack_low_bytes(c0, c1, c2, c3);
+}
+
 // How the A slots are filled for chunk c of GEMM G: 0 not at all (a resident GEMM's later chunks),
 // 1 by the row warps (sliced, published on a_full), 2 by the producer from the per-SM cache
-// (bulk copies completing on a_tma).
-__device__ __forceinline__ int a_fill_kind(const GemmSpec& G, int c, bool cache) {
+// (bulk copies completing on a_tma). presliced: the row warps wrote every K tile of the planes to
+// the cache before the GEMM (announced on a_pre), so every chunk comes from the cache.
+__device__ __forceinline__ int a_fill_kind(const GemmSpec& G, int c, bool cache, bool presliced) {
   if (G.ktiles <= kASlots) return c == 0 ? 1 : 0;
+  if (presliced) return 2;
   return (c > 0 && cache) ? 2 : 1;
 }
 
@@ -262,6 +282,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
   auto use_cache = [&](const GemmSpec& G) {
     return CACHE && acache != nullptr && G.ktiles <= a.a_cache_kt && G.nchunks > 1;
   };
+  // W1 with more K tiles than A slots: the pass that builds its input rows x = [n | left | latch]
+  // slices them straight into the plane cache (no fp32 copy of x, no slicing pass of its own)
+  auto presliced = [&](const GemmSpec& G) { return G.type == kGW1 && G.ktiles > kASlots && use_cache(G); };
   // a tile whose sessions all sit this pass out (seglen 0: idle, finished, or kept out of a
   // scheduler's admission pass) has nothing to do
   {
@@ -282,6 +305,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
     }
     mbar_init(&bars->acc_full, 1);
     mbar_init(&bars->acc_empty, kRowThreads);
+    mbar_init(&bars->a_pre, kRowThreads);
     fence_barrier_init();
   }
   if (warp == kMmaWarp) tmem_alloc(&bars->tmem, 512);
@@ -296,23 +320,41 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
       uint32_t bidx = 0;
       // fills of each A slot so far (by anyone) and by the row warps, in the consumption order
       uint32_t fills[kASlots] = {0, 0, 0}, rfills[kASlots] = {0, 0, 0};
+      uint32_t npre = 0;  // presliced GEMMs so far (phases of a_pre)
       bool ok = true;
       for (int g = 0; g < a.ngemms && ok; ++g) {
         const GemmSpec& G = a.gemms[g];
         const bool cache = use_cache(G);
+        const bool pre = presliced(G);
         for (int c = 0; c < G.nchunks && ok; ++c) {
-          const int kind = a_fill_kind(G, c, cache);
-          if (kind == 2 && c == 1) {
+          const int kind = a_fill_kind(G, c, cache, pre);
+          if (kind == 2 && c == 1 && !pre) {
             // the first chunk's row fills wrote every K tile to the cache: acquire their writes
             for (int sl = 0; sl < kASlots && ok; ++sl)
               if (rfills[sl] > 0 && !mbar_wait_or_abort(&bars->a_full[sl], (rfills[sl] - 1) & 1, kErrWaitFull)) ok = false;
           }
           for (int kt = 0; kt < G.ktiles && ok; ++kt, ++bidx) {
             const int slot = kt % kASlots;
+            // the weight tile first: it does not depend on the row warps
+            const int st = bidx % kBStages;
+            if (bidx >= kBStages && !mbar_wait_or_abort(&bars->b_empty[st], ((bidx / kBStages) - 1) & 1, kErrWaitEmpty)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&bars->b_full[st], kTile);
+            bulk_load(sB + st * kTile, G.tiles + ((size_t)c * G.ktiles + kt) * kTile, kTile, &bars->b_full[st]);
             if (kind == 1) {
               ++fills[slot];
               ++rfills[slot];
             } else if (kind == 2) {
+              if (pre && c == 0 && kt == 0) {
+                // the row warps' cache writes (each fenced for the async proxy before its arrival)
+                if (!mbar_wait_or_abort(&bars->a_pre, npre & 1, kErrWaitFull)) {
+                  ok = false;
+                  break;
+                }
+                ++npre;
+              }
               if (fills[slot] >= 1 && !mbar_wait_or_abort(&bars->a_empty[slot], (fills[slot] - 1) & 1, kErrWaitEmpty)) {
                 ok = false;
                 break;
@@ -321,13 +363,6 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
               bulk_load(sA + slot * kASlot, acache + (size_t)kt * kASlot, kASlot, &bars->a_tma[slot]);
               ++fills[slot];
             }
-            const int st = bidx % kBStages;
-            if (bidx >= kBStages && !mbar_wait_or_abort(&bars->b_empty[st], ((bidx / kBStages) - 1) & 1, kErrWaitEmpty)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(&bars->b_full[st], kTile);
-            bulk_load(sB + st * kTile, G.tiles + ((size_t)c * G.ktiles + kt) * kTile, kTile, &bars->b_full[st]);
           }
         }
       }
@@ -344,13 +379,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
         const GemmSpec& G = a.gemms[g];
         const bool resident = G.ktiles <= kASlots;
         const bool cache = use_cache(G);
+        const bool pre = presliced(G);
         for (int c = 0; c < G.nchunks && ok; ++c) {
           if (chunk_idx > 0 && !mbar_wait_or_abort(&bars->acc_empty, (chunk_idx - 1) & 1, kErrWaitAccFree)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const int kind = a_fill_kind(G, c, cache);
+          const int kind = a_fill_kind(G, c, cache, pre);
           for (int kt = 0; kt < G.ktiles; ++kt, ++bidx) {
             const int slot = kt % kASlots;
             if (kind == 1) {
@@ -455,9 +491,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
     auto run_gemm = [&](int g, bool prefilled, const float* src, int ld, const float* rmax, auto&& epilogue) {
       const GemmSpec& G = a.gemms[g];
       const bool cache = use_cache(G);
+      const bool pre = presliced(G);
       const float step = row_step(rmax[r]);
       for (int c = 0; c < G.nchunks; ++c) {
-        const int kind = a_fill_kind(G, c, cache);
+        const int kind = a_fill_kind(G, c, cache, pre);
         if (!prefilled && kind == 1) {
           for (int kt = 0; kt < G.ktiles; ++kt) {
             const int slot = kt % kASlots;
@@ -646,7 +683,15 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
       row_bar();
       trace_point(a, tp++);
       const bool w1_resident = a.gemms[g].ktiles <= kASlots;
+      // W1's planes go straight into this SM's plane cache (every chunk then comes from it)
+      const bool w1_pre = !w1_resident && presliced(a.gemms[g]);
       bool w1_prefilled = false;
+      // x's planes written to the cache: each thread fences its writes for the async proxy (the
+      // producer's bulk copies read them) and arrives on a_pre
+      auto announce_pre = [&]() {
+        fence_proxy_async_global();
+        mbar_arrive(&bars->a_pre);
+      };
       if (decode) {
         // ---- decode: latch update, left neighbour, ring write; one warp per row ----
         const bool slice = w1_resident;
@@ -688,7 +733,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
             if (v && f < nf) {
               ls4[f] = l;
               ring4[(size_t)(pos % a.ring) * nf + f] = nv[k];
-              if (!slice) {
+              if (!slice && !w1_pre) {
                 float4* xw = reinterpret_cast<float4*>(a.xbuf + (size_t)gr * 3 * D);
                 xw[nf + f] = lf[k];
                 xw[2 * nf + f] = l;
@@ -698,15 +743,21 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
           }
           m = v ? warp_max(m) : 0.f;
           if (lane == 0) bars->rowmax_a[rr] = m;
-          if (slice) {
+          if (slice || w1_pre) {
             const float is = row_inv_step(m);
 #pragma unroll
             for (int k = 0; k < KF; ++k) {
               const int f = lane + 32 * k;
               if (f < nf) {
-                put4(sA, rr, 4 * f, nv[k], is);
-                put4(sA, rr, D + 4 * f, lf[k], is);
-                put4(sA, rr, 2 * D + 4 * f, lo[k], is);
+                if (slice) {
+                  put4(sA, rr, 4 * f, nv[k], is);
+                  put4(sA, rr, D + 4 * f, lf[k], is);
+                  put4(sA, rr, 2 * D + 4 * f, lo[k], is);
+                } else {
+                  put4_g(acache, rr, 4 * f, nv[k], is);
+                  put4_g(acache, rr, D + 4 * f, lf[k], is);
+                  put4_g(acache, rr, 2 * D + 4 * f, lo[k], is);
+                }
               }
             }
           }
@@ -715,90 +766,210 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
           for (int kt = 0; kt < kts; ++kt) publish(kt % kASlots);
           w1_prefilled = true;
         }
+        if (w1_pre) announce_pre();
         row_bar();
       } else {
         // ---- prefill: latch scan, left neighbours, ring write and row maxima, in passes ----
-        // (1) the latch recurrence over the segment, one thread per (session slot, channel), with
-        //     lambda and n of 8 positions loaded ahead of each run of steps
-        for (int task = t; task < a.spt * D; task += kRowThreads) {
-          const int slot = task / D, d = task - slot * D;
-          const int sess = tile * a.spt + slot;
-          if (sess >= a.n_sess) continue;
-          const int len = a.seglen[sess];
-          if (len <= 0) continue;
-          const int p0 = a.pos0[sess];
-          const size_t st_off = ((size_t)sess * a.total_steps + bs);
-          float l = p0 == 0 ? 0.f : a.latch[st_off * D + d];
-          float* x0 = a.xbuf + (size_t)(tile * kRows + slot * a.P) * 3 * D + d;
-          for (int c0 = 0; c0 < len; c0 += 8) {
-            float lam[8], nv[8];
+        // (1) the latch recurrence over each segment, l_t = lam_t l_{t-1} + (1 - lam_t) n_t
+        //     (updateLatch, stream.go:197-205), one (session slot, channel) at a time
+        constexpr int kLC = 16;  // positions per chunk of the scan
+        if (a.P <= kLC) {
+          // short segments: the recurrence step by step, the loads of each run issued first
+          for (int task = t; task < a.spt * D; task += kRowThreads) {
+            const int slot = task / D, d = task - slot * D;
+            const int sess = tile * a.spt + slot;
+            if (sess >= a.n_sess) continue;
+            const int len = a.seglen[sess];
+            if (len <= 0) continue;
+            const int p0 = a.pos0[sess];
+            const size_t st_off = ((size_t)sess * a.total_steps + bs);
+            float l = p0 == 0 ? 0.f : a.latch[st_off * D + d];
+            float* x0 = a.xbuf + (size_t)(tile * kRows + slot * a.P) * 3 * D + d;
+            for (int c0 = 0; c0 < len; c0 += 8) {
+              float lam[8], nv[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const bool in = c0 + i < len;
-              lam[i] = in ? x0[(size_t)(c0 + i) * 3 * D + 2 * D] : 0.f;
-              nv[i] = in ? x0[(size_t)(c0 + i) * 3 * D] : 0.f;
-            }
+              for (int i = 0; i < 8; ++i) {
+                const bool in = c0 + i < len;
+                lam[i] = in ? x0[(size_t)(c0 + i) * 3 * D + 2 * D] : 0.f;
+                nv[i] = in ? x0[(size_t)(c0 + i) * 3 * D] : 0.f;
+              }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              if (c0 + i < len) {
-                l = __fadd_rn(__fmul_rn(lam[i], l), __fmul_rn(__fsub_rn(1.0f, lam[i]), nv[i]));
-                x0[(size_t)(c0 + i) * 3 * D + 2 * D] = l;
+              for (int i = 0; i < 8; ++i) {
+                if (c0 + i < len) {
+                  l = __fadd_rn(__fmul_rn(lam[i], l), __fmul_rn(__fsub_rn(1.0f, lam[i]), nv[i]));
+                  x0[(size_t)(c0 + i) * 3 * D + 2 * D] = l;
+                }
               }
             }
+            a.latch[st_off * D + d] = l;
           }
-          a.latch[st_off * D + d] = l;
+        } else {
+          // longer segments: a scan in chunks of kLC positions. The recurrence is affine in l, so
+          // a chunk maps its input l to A l + B (A the product of its lambdas, B its output from
+          // l = 0). (a) every chunk's (A, B) at once; (b) the chunks' inputs in order, per
+          // channel; (c) every chunk replays the recurrence from its input, step by step as the
+          // reference writes it. The chunks' (A, B) and inputs live in the free A slots (the
+          // W_select MMAs that read them are complete; W1's planes are not written yet).
+          const int nch = (a.P + kLC - 1) / kLC;
+          float* cA = reinterpret_cast<float*>(sA);       // [spt][nch][D]: A, then the chunk's input
+          float* cB = cA + (size_t)a.spt * nch * D;         // [spt][nch][D]: B
+          const int ntask = a.spt * nch * D;
+          auto chunk_of = [&](int task, int& slot, int& ch, int& d, int& sess, int& len, int& c0) {
+            d = task % D;
+            const int rest = task / D;
+            ch = rest % nch;
+            slot = rest / nch;
+            sess = tile * a.spt + slot;
+            len = sess < a.n_sess ? a.seglen[sess] : 0;
+            c0 = ch * kLC;
+            return c0 < len;
+          };
+          for (int task = t; task < ntask; task += kRowThreads) {
+            int slot, ch, d, sess, len, c0;
+            if (!chunk_of(task, slot, ch, d, sess, len, c0)) continue;
+            const float* x0 = a.xbuf + (size_t)(tile * kRows + slot * a.P + c0) * 3 * D + d;
+            float lam[kLC], nv[kLC];
+#pragma unroll
+            for (int i = 0; i < kLC; ++i) {
+              const bool in = c0 + i < len;
+              lam[i] = in ? x0[(size_t)i * 3 * D + 2 * D] : 1.f;
+              nv[i] = in ? x0[(size_t)i * 3 * D] : 0.f;
+            }
+            float A = 1.f, B = 0.f;
+#pragma unroll
+            for (int i = 0; i < kLC; ++i) {
+              B = __fadd_rn(__fmul_rn(lam[i], B), __fmul_rn(__fsub_rn(1.0f, lam[i]), nv[i]));
+              A = __fmul_rn(A, lam[i]);
+            }
+            cA[task] = A;
+            cB[task] = B;
+          }
+          row_bar();
+          for (int task = t; task < a.spt * D; task += kRowThreads) {
+            const int slot = task / D, d = task - slot * D;
+            const int sess = tile * a.spt + slot;
+            if (sess >= a.n_sess) continue;
+            const int len = a.seglen[sess];
+            if (len <= 0) continue;
+            const size_t st_off = ((size_t)sess * a.total_steps + bs);
+            float l = a.pos0[sess] == 0 ? 0.f : a.latch[st_off * D + d];
+            for (int ch = 0; ch * kLC < len; ++ch) {
+              const size_t i = ((size_t)slot * nch + ch) * D + d;
+              const float A = cA[i];
+              cA[i] = l;
+              l = __fadd_rn(__fmul_rn(A, l), cB[i]);
+            }
+          }
+          row_bar();
+          for (int task = t; task < ntask; task += kRowThreads) {
+            int slot, ch, d, sess, len, c0;
+            if (!chunk_of(task, slot, ch, d, sess, len, c0)) continue;
+            float* x0 = a.xbuf + (size_t)(tile * kRows + slot * a.P + c0) * 3 * D + d;
+            float lam[kLC], nv[kLC];
+#pragma unroll
+            for (int i = 0; i < kLC; ++i) {
+              const bool in = c0 + i < len;
+              lam[i] = in ? x0[(size_t)i * 3 * D + 2 * D] : 0.f;
+              nv[i] = in ? x0[(size_t)i * 3 * D] : 0.f;
+            }
+            float l = cA[task];
+#pragma unroll
+            for (int i = 0; i < kLC; ++i) {
+              if (c0 + i < len) {
+                l = __fadd_rn(__fmul_rn(lam[i], l), __fmul_rn(__fsub_rn(1.0f, lam[i]), nv[i]));
+                x0[(size_t)i * 3 * D + 2 * D] = l;
+              }
+            }
+            if (c0 + kLC >= len) a.latch[((size_t)sess * a.total_steps + bs) * D + d] = l;  // the segment's last
+          }
         }
         if (a.trace && a.trace_fine) trace_point(a, tp++);
-        if (w1_resident) {
+        if (w1_resident || w1_pre) {
           // (2) one warp per row: the left neighbour n(pos - dil) (from the segment, or from the
           //     ring before it), max |x| over x = [n | left | latch], and x sliced straight into
-          //     W1's A slots (no fp32 copy of x goes back to memory). x = one float4 per lane.
+          //     W1's A slots (resident W1) or into this SM's plane cache (no fp32 copy of x goes
+          //     back to memory)
           row_bar();  // the latch scan's rows
           const int kts = a.gemms[g].ktiles;
-          for (int kt = 0; kt < kts; ++kt) acquire(kt % kASlots);
+          if (w1_resident)
+            for (int kt = 0; kt < kts; ++kt) acquire(kt % kASlots);
 #pragma unroll 2
           for (int u = 0; u < kRowsPerWarp; ++u) {
             const int rr = warp + kRowWarps * u;
             const bool v = bars->rvalid[rr] != 0;
             const int tt = rr - (rr / a.P) * a.P;
             const int sess = bars->rsess[rr], lpos = bars->rpos[rr] - dil;
-            const bool in = v && lane < nf;
             const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
             const float4* x4 = reinterpret_cast<const float4*>(a.xbuf + (size_t)(tile * kRows + rr) * 3 * D);
-            float4 nv = z, lt = z, lf = z;
-            if (in) {
-              nv = x4[lane];
-              lt = x4[2 * nf + lane];
-              if (tt >= dil)
-                lf = reinterpret_cast<const float4*>(a.xbuf + (size_t)(tile * kRows + rr - dil) * 3 * D)[lane];
-              else if (lpos >= 0)
-                lf = reinterpret_cast<const float4*>(a.norm_ring + ((size_t)sess * a.total_steps + bs) * a.ring * D +
-                                                     (size_t)(lpos % a.ring) * D)[lane];
+            const float4* left4 =
+                tt >= dil ? reinterpret_cast<const float4*>(a.xbuf + (size_t)(tile * kRows + rr - dil) * 3 * D)
+                          : reinterpret_cast<const float4*>(a.norm_ring + ((size_t)sess * a.total_steps + bs) * a.ring * D +
+                                                            (size_t)((lpos >= 0 ? lpos : 0) % a.ring) * D);
+            const bool has_left = v && (tt >= dil || lpos >= 0);
+            float4 nv[KF], lt[KF], lf[KF];
+#pragma unroll
+            for (int k = 0; k < KF; ++k) {
+              const int f = lane + 32 * k;
+              const bool in = v && f < nf;
+              nv[k] = in ? x4[f] : z;
+              lt[k] = in ? x4[2 * nf + f] : z;
+              lf[k] = (in && has_left) ? left4[f] : z;
             }
-            float m = fmaxf(max4(nv), fmaxf(max4(lf), max4(lt)));
+            float m = 0.f;
+#pragma unroll
+            for (int k = 0; k < KF; ++k) m = fmaxf(m, fmaxf(max4(nv[k]), fmaxf(max4(lf[k]), max4(lt[k]))));
             m = v ? warp_max(m) : 0.f;
             if (lane == 0) bars->rowmax_a[rr] = m;
             const float is = row_inv_step(m);
-            if (lane < nf) {
-              put4(sA, rr, 4 * lane, nv, is);
-              put4(sA, rr, D + 4 * lane, lf, is);
-              put4(sA, rr, 2 * D + 4 * lane, lt, is);
+#pragma unroll
+            for (int k = 0; k < KF; ++k) {
+              const int f = lane + 32 * k;
+              if (f >= nf) continue;
+              if (w1_resident) {
+                put4(sA, rr, 4 * f, nv[k], is);
+                put4(sA, rr, D + 4 * f, lf[k], is);
+                put4(sA, rr, 2 * D + 4 * f, lt[k], is);
+              } else {
+                put4_g(acache, rr, 4 * f, nv[k], is);
+                put4_g(acache, rr, D + 4 * f, lf[k], is);
+                put4_g(acache, rr, 2 * D + 4 * f, lt[k], is);
+              }
             }
           }
-          for (int kt = 0; kt < kts; ++kt) publish(kt % kASlots);
-          w1_prefilled = true;
+          if (w1_resident) {
+            for (int kt = 0; kt < kts; ++kt) publish(kt % kASlots);
+            w1_prefilled = true;
+          } else {
+            announce_pre();
+          }
           row_bar();  // row maxima; the ring reads above come before the ring writes below
           if (a.trace && a.trace_fine) trace_point(a, tp++);
-          // (3) the ring keeps the segment's last norm cells
-          for (int task = t; task < a.spt * D; task += kRowThreads) {
-            const int slot = task / D, d = task - slot * D;
-            const int sess = tile * a.spt + slot;
-            if (sess >= a.n_sess) continue;
-            const int len = a.seglen[sess];
-            const int p0 = a.pos0[sess];
-            float* rg = a.norm_ring + ((size_t)sess * a.total_steps + bs) * a.ring * D + d;
-            for (int tt = max(0, len - a.ring); tt < len; ++tt)
-              rg[(size_t)((p0 + tt) % a.ring) * D] = a.xbuf[(size_t)(tile * kRows + slot * a.P + tt) * 3 * D + d];
+          // (3) the ring keeps the segment's last norm cells: task (slot, j, channel) copies
+          //     position len - 1 - j (j < ring), four tasks' loads in flight before their stores
+          const int rn = min(a.ring, a.P);
+          const int ntask = a.spt * rn * D;
+          for (int t0 = t; t0 < ntask; t0 += 4 * kRowThreads) {
+            float val[4];
+            float* dst[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              dst[q] = nullptr;
+              val[q] = 0.f;
+              const int task = t0 + q * kRowThreads;
+              if (task >= ntask) continue;
+              const int d = task % D, rest = task / D;
+              const int j = rest % rn, slot = rest / rn;
+              const int sess = tile * a.spt + slot;
+              if (sess >= a.n_sess) continue;
+              const int len = a.seglen[sess], tt = len - 1 - j;
+              if (tt < 0) continue;
+              val[q] = a.xbuf[(size_t)(tile * kRows + slot * a.P + tt) * 3 * D + d];
+              dst[q] = a.norm_ring + ((size_t)sess * a.total_steps + bs) * a.ring * D +
+                       (size_t)((a.pos0[sess] + tt) % a.ring) * D + d;
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (dst[q]) *dst[q] = val[q];
           }
           if (a.trace && a.trace_fine) trace_point(a, tp++);
         } else {

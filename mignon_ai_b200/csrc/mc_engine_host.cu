@@ -255,7 +255,7 @@ constexpr int kACacheSms = 256;
 struct DevBatch {
   DevModel* m = nullptr;
   int S = 0, window = 0, pmax = 0, nsplit = 1, topk = 0;
-  bool decode_kernel = true;  // decode steps use block_decode_kernel (MC_DECODE_KERNEL=block: block_kernel)
+  bool decode_kernel = true;  // decode steps use block_decode_kernel, else block_kernel (see batch_create)
   int n_sm = 148;             // multiprocessors of the device (persistent grids)
   size_t rows = 0;  // scratch rows
   cudaStream_t stream = nullptr;
@@ -421,11 +421,18 @@ int batch_create(DevModel* m, int S, int window, int pmax, int topk, bool allow_
   b->window = window;
   b->pmax = std::max(1, std::min(pmax, 128));
   b->topk = topk;
-  {
-    const char* k = getenv("MC_DECODE_KERNEL");
-    b->decode_kernel = m->dec_ok && !(k && strcmp(k, "block") == 0);
-  }
   MC_CUDA(cudaDeviceGetAttribute(&b->n_sm, cudaDevAttrMultiProcessorCount, m->device));
+  {
+    // Decode steps run on block_decode_kernel (weights on the MMA's M side, 16 sessions per CTA)
+    // unless the batch is large and the model wide: from three waves of 128-session tiles on, at
+    // state widths above 128, block_kernel (128 sessions on M, each weight tile read once per 128
+    // sessions instead of once per 16) takes the decode steps too (config 3 at 65,536 sessions:
+    // 2.64 against 3.19 ms per block launch). MC_DECODE_KERNEL=block / decode forces one.
+    const char* k = getenv("MC_DECODE_KERNEL");
+    const bool big_wide = m->D > 128 && (long long)(S + 127) / 128 >= 3LL * b->n_sm;
+    const bool want_block = k ? strcmp(k, "block") == 0 : big_wide;
+    b->decode_kernel = m->dec_ok && !want_block;
+  }
   const int D = m->D, H = m->H;
   const int spt_min = std::max(1, 128 / b->pmax);
   const size_t full_tiles = std::max((size_t)(S + 127) / 128, (size_t)(S + spt_min - 1) / spt_min);

@@ -33,7 +33,11 @@ def _rank_main(rank, world, port, sessions, out_dir):
     ms = bench.max_over_ranks(10.0 + 5.0 * rank, dist, torch.device("cpu"))
     ranges = [None] * world
     dist.all_gather_object(ranges, (first, end))
-    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), prompts=prompts, ms=ms, ranges=np.array(ranges))
+    # the strong-scaling workloads (config 3 sample, config 4 score): 50 sessions split over the ranks
+    sf, se = bench.strong_range(rank, world, 50)
+    sp, sl, slim, _ = bench.sample_inputs(sf, se, 50)
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), prompts=prompts, ms=ms, ranges=np.array(ranges),
+             sp=sp, sl=sl, slim=slim, srange=np.array([sf, se]))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -56,3 +60,10 @@ def test_two_gloo_ranks_shard_sessions_and_take_the_max_time(tmp_path):
     assert np.array_equal(np.concatenate([r["prompts"] for r in res]), whole)
     # a one-rank run of the same global sessions sees the same prompt rows
     assert np.array_equal(bench.prompts_for(0, world * sessions), whole)
+    # strong scaling: the ranks' shards tile the one-rank workload exactly
+    assert [tuple(r["srange"]) for r in res] == [(0, 25), (25, 50)]
+    p1, l1, lim1, _ = bench.sample_inputs(0, 50, 50)
+    assert np.array_equal(np.concatenate([r["sp"] for r in res]), p1)
+    assert np.array_equal(np.concatenate([r["sl"] for r in res]), l1)
+    assert np.array_equal(np.concatenate([r["slim"] for r in res]), lim1)
+    assert np.all(lim1 == 128 - l1) and l1.min() >= 16 and l1.max() <= 64
