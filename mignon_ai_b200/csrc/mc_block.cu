@@ -41,13 +41,16 @@ constexpr int kSmemA = kASlots * kASlot;        // 144 KB
 constexpr int kSmemB = kBStages * kTile;        // 64 KB
 constexpr int kBlockSmem = kSmemA + kSmemB + 1024 /*align*/ + 16384 /*barriers, row data*/;
 
+constexpr int kVecMax = 2048;  // floats of a staged epilogue vector (b1 of hidden widths up to 1024)
+
 struct Bars {
   uint64_t a_full[kASlots], a_empty[kASlots], a_tma[kASlots], b_full[kBStages], b_empty[kBStages], acc_full, acc_empty;
   uint64_t a_pre;                      // the row warps wrote a GEMM's planes straight into the plane cache
   uint32_t tmem;
   float rowmax_n[kRows];               // max |norm cell| per row
   float rowmax_part[kTPR][kRows];       // per-thread partial maxima of an epilogue output
-  float rowmax_warp[kRowWarps][kRows]; // per-warp partial maxima of the prefill scan
+  alignas(16) float vec[kVecMax];      // the per-channel vector of the current GEMM's epilogue
+                                       // (latch base, b1 or b2), staged from global memory
   int rvalid[kRows];                   // row holds a position of an active session
   int rtok[kRows];                     // its token (clamped to the vocabulary)
   int rsess[kRows];                    // its session
@@ -488,7 +491,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
     // Runs GEMM g. prefilled: its (resident) A tiles were already published by a fused phase;
     // otherwise they are sliced from src with the row maxima rmax. The epilogue gets the chunk and
     // this thread's row step and weight scale.
-    auto run_gemm = [&](int g, bool prefilled, const float* src, int ld, const float* rmax, auto&& epilogue) {
+    // prefetch(c) runs before chunk c's accumulator wait: global loads the epilogue needs,
+    // issued so that their latency overlaps the MMAs.
+    auto run_gemm_pre = [&](int g, bool prefilled, const float* src, int ld, const float* rmax, auto&& prefetch,
+                            auto&& epilogue) {
       const GemmSpec& G = a.gemms[g];
       const bool cache = use_cache(G);
       const bool pre = presliced(G);
@@ -506,6 +512,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
           for (int kt = 0; kt < G.ktiles; ++kt) afill[kt % kASlots]++;  // filled by the producer
         }
         if (a.trace && a.trace_fine) trace_point(a, tp++);
+        prefetch(c);
         const bool got = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&bars->acc_full, chunk_idx & 1, kErrWaitAcc));
         if (a.trace && a.trace_fine) trace_point(a, tp++);
         if (!got) ok = false;
@@ -518,6 +525,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
         ++chunk_idx;
         if (a.trace && a.trace_fine) trace_point(a, tp++);
       }
+    };
+    auto run_gemm = [&](int g, bool prefilled, const float* src, int ld, const float* rmax, auto&& epilogue) {
+      run_gemm_pre(g, prefilled, src, ld, rmax, [](int) {}, epilogue);
     };
     // Warp-per-row RMSNorm (nn/rmsnorm.go:14-32) of cur, after the embedding (mode 1) or the
     // inter-block residual (mode 2) when asked: writes out (fp32, row stride out_ld), max |out|
@@ -620,6 +630,17 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
       if (slice)
         for (int kt = 0; kt < kts; ++kt) publish(kt % kASlots);
     };
+    // The per-channel vector src[0..n) of the next GEMM's epilogue, copied into shared memory
+    // (between two row barriers: the previous epilogue's reads of the buffer are done, and every
+    // row thread sees the copy), so the epilogues read it without global-memory latency. Vectors
+    // longer than the buffer stay in global memory.
+    auto stage_vec = [&](const float* src, int n) -> const float* {
+      if (n > kVecMax) return src;
+      row_bar();
+      for (int i = t; i < n; i += kRowThreads) bars->vec[i] = src[i];
+      row_bar();
+      return bars->vec;
+    };
     // max over the four threads of a row (each ran the epilogue on its columns) into rmax
     auto row_max_quad = [&](float mine, float* rmax) {
       bars->rowmax_part[h][r] = mine;
@@ -665,12 +686,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
       trace_point(a, tp++);
       // W_select epilogue: lambda = sigmoid(dot * s_sel + base) into the latch slot of xbuf
       float* xrow = a.xbuf + (size_t)grow * 3 * D;
+      const float* lbase = stage_vec(a.latch_base, D);
       run_gemm(g++, true, nullptr, 0, bars->rowmax_n, [&](int c, float step, float scale) {
         for (int j0 = h * 32; j0 < h * 32 + 32; j0 += 16) {
           const int n0 = c * kNC + j0;
           const bool act = ri.valid && n0 < D;
           float base[16];
-          if (act) ld16(a.latch_base, n0, D, base);
+          if (act) ld16(lbase, n0, D, base);
           uint32_t a1[16], a2[16], a3[16];
           load_acc16(tmem, warp, j0, a1, a2, a3);
           if (!act) continue;
@@ -1020,14 +1042,15 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
       // W1 + GLU -> hidden (fp32 rows in hbuf), per-thread max |hidden|
       float hmax = 0.f;
       float* hrow = a.hbuf + (size_t)grow * H;
+      const float* b1 = stage_vec(a.b1, 2 * H);
       run_gemm(g++, w1_prefilled, a.xbuf, 3 * D, bars->rowmax_a, [&](int c, float step, float scale) {
         for (int j0 = h * 16; j0 < h * 16 + 16; j0 += 8) {  // this thread's 16 of the chunk's 64 hidden units
           const int u0 = c * kHalfChunk + j0;
           const bool act = ri.valid && u0 < H;
           float bv[8], bg[8], hid[8];
           if (act) {
-            ld8(a.b1, u0, H, bv);
-            ld8(a.b1 + H, u0, H, bg);
+            ld8(b1, u0, H, bv);
+            ld8(b1 + H, u0, H, bg);
           }
           uint32_t x1[8], x2[8], x3[8], y1[8], y2[8], y3[8];
           load_acc8x2(tmem, warp, j0, kHalfChunk + j0, x1, x2, x3, y1, y2, y3);  // value and gate columns
@@ -1048,15 +1071,25 @@ __global__ void __launch_bounds__(kBlockThreads, 1) block_kernel(const __grid_co
       trace_point(a, tp++);
       // W2 + highway -> cur
       float* crow = a.cur + (size_t)grow * D;
-      run_gemm(g++, false, a.hbuf, H, bars->rowmax_h, [&](int c, float step, float scale) {
+      const float* b2 = stage_vec(a.b2, 2 * D);
+      float cvp[16];  // this thread's cur values of the chunk, loaded before the accumulator wait
+      auto cur_pre = [&](int c) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int d0 = c * kHalfChunk + h * 16 + 8 * i;
+          if (ri.valid && d0 < D) ld8(crow, d0, D, *reinterpret_cast<float(*)[8]>(cvp + 8 * i));
+        }
+      };
+      run_gemm_pre(g++, false, a.hbuf, H, bars->rowmax_h, cur_pre, [&](int c, float step, float scale) {
         for (int j0 = h * 16; j0 < h * 16 + 16; j0 += 8) {  // this thread's 16 of the chunk's 64 state channels
           const int d0 = c * kHalfChunk + j0;
           const bool act = ri.valid && d0 < D;
           float bd[8], bg[8], cv[8], od[8];
           if (act) {
-            ld8(a.b2, d0, D, bd);
-            ld8(a.b2 + D, d0, D, bg);
-            ld8(crow, d0, D, cv);
+            ld8(b2, d0, D, bd);
+            ld8(b2 + D, d0, D, bg);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cv[j] = cvp[j0 - h * 16 + j];
           }
           uint32_t x1[8], x2[8], x3[8], y1[8], y2[8], y3[8];
           load_acc8x2(tmem, warp, j0, kHalfChunk + j0, x1, x2, x3, y1, y2, y3);  // delta and gate columns
