@@ -506,6 +506,7 @@ int mc_version(void) { return 100; }
 
 int mc_open(const mc_options* opt, mc_ctx** out) {
   clear_error();
+  DeviceRestore restore_device;
   if (!out) return set_error(kInvalidArgument, "mc_open: null output");
   auto c = std::make_unique<mc_ctx>();
   int ndev = 0;
@@ -531,6 +532,7 @@ int mc_close(mc_ctx* ctx) {
 
 int mc_load_model(mc_ctx* ctx, const uint8_t* data, size_t n, mc_model** out) {
   clear_error();
+  DeviceRestore restore_device;
   if (!ctx || !data || !out) return set_error(kInvalidArgument, "mc_load_model: null argument");
   auto m = std::make_unique<mc_model>();
   m->ctx = ctx;
@@ -546,12 +548,14 @@ int mc_load_model(mc_ctx* ctx, const uint8_t* data, size_t n, mc_model** out) {
 }
 
 int mc_model_free(mc_model* m) {
+  DeviceRestore restore_device;  // the destructors switch to the shards' devices
   delete m;
   return kOk;
 }
 
 int mc_model_info(const mc_model* m, int32_t* out) {
   clear_error();
+  DeviceRestore restore_device;
   if (!m || !out) return set_error(kInvalidArgument, "mc_model_info: null argument");
   const DevModel& d = *m->dev[0];
   out[0] = d.V;
@@ -569,16 +573,19 @@ int mc_model_info(const mc_model* m, int32_t* out) {
 
 int mc_batch_open(mc_model* m, int count, int context_size, int max_prompt, int top_k, mc_batch** out) {
   clear_error();
+  DeviceRestore restore_device;
   return batch_open(m, count, context_size, max_prompt, top_k, true, out);
 }
 
 int mc_batch_close(mc_batch* b) {
+  DeviceRestore restore_device;  // the destructors switch to the shards' devices
   delete b;
   return kOk;
 }
 int mc_prefill(mc_batch* b, const int32_t* tokens, const int32_t* lens, int stride, float* logits, int32_t* next,
                float* prob) {
   clear_error();
+  DeviceRestore restore_device;
   if (!b || !tokens || !lens) return set_error(kInvalidArgument, "mc_prefill: null argument");
   int P = 1;
   int st = upload_prompts(b, tokens, lens, stride, &P);
@@ -615,6 +622,7 @@ int mc_prefill(mc_batch* b, const int32_t* tokens, const int32_t* lens, int stri
 
 int mc_score(mc_batch* b, const int32_t* seqs, const int32_t* lens, int stride, double* out) {
   clear_error();
+  DeviceRestore restore_device;
   if (!b || !seqs || !lens || !out) return set_error(kInvalidArgument, "mc_score: null argument");
   return score_impl(b, seqs, lens, stride, nullptr, out, "mc_score");
 }
@@ -622,12 +630,14 @@ int mc_score(mc_batch* b, const int32_t* seqs, const int32_t* lens, int stride, 
 int mc_score_targets(mc_batch* b, const int32_t* seqs, const int32_t* lens, int stride, const int32_t* targets,
                      double* out) {
   clear_error();
+  DeviceRestore restore_device;
   if (!b || !seqs || !lens || !targets || !out) return set_error(kInvalidArgument, "mc_score_targets: null argument");
   return score_impl(b, seqs, lens, stride, targets, out, "mc_score_targets");
 }
 
 int mc_append(mc_batch* b, const int32_t* tokens, float* logits, int32_t* next, float* prob) {
   clear_error();
+  DeviceRestore restore_device;
   if (!b || !tokens) return set_error(kInvalidArgument, "mc_append: null argument");
   int st;
   for (size_t g = 0; g < b->shard.size(); ++g) {
@@ -645,6 +655,7 @@ int mc_append(mc_batch* b, const int32_t* tokens, float* logits, int32_t* next, 
 int mc_generate(mc_batch* b, const int32_t* prompts, const int32_t* lens, int stride, int n_new, double temperature,
                 uint32_t session0, int32_t* out_tokens, float* out_probs) {
   clear_error();
+  DeviceRestore restore_device;
   return generate_impl(b, prompts, lens, stride, n_new, temperature, session0, nullptr, 0, out_tokens, out_probs, nullptr);
 }
 
@@ -652,6 +663,7 @@ int mc_generate_stops(mc_batch* b, const int32_t* prompts, const int32_t* lens, 
                       double temperature, uint32_t session0, const int32_t* stops, int n_stops, int32_t* out_tokens,
                       float* out_probs, int32_t* out_lens) {
   clear_error();
+  DeviceRestore restore_device;
   if (n_stops < 0 || n_stops > kMaxStops || (n_stops > 0 && !stops))
     return set_error(kInvalidArgument, "mc_generate_stops: 0 to 8 stop tokens");
   return generate_impl(b, prompts, lens, stride, n_new, temperature, session0, stops, n_stops, out_tokens, out_probs,
@@ -663,6 +675,7 @@ int mc_generate_policy(mc_batch* b, const int32_t* prompts, const int32_t* lens,
                        const int32_t* dfa_start, uint32_t session0, const int32_t* stops, int n_stops,
                        int32_t* out_tokens, float* out_probs, int32_t* out_lens) {
   clear_error();
+  DeviceRestore restore_device;
   if (n_stops < 0 || n_stops > kMaxStops || (n_stops > 0 && !stops))
     return set_error(kInvalidArgument, "mc_generate_policy: 0 to 8 stop tokens");
   if (!sp) return set_error(kInvalidArgument, "mc_generate_policy: null sampling parameters");
@@ -675,6 +688,7 @@ int mc_sample_rows(int device, const float* logits, int n, int vocab, const int3
                    int recent_stride, const int32_t* allowed, const mc_sampling* sp, const double* u, uint32_t session0,
                    uint32_t step, int32_t* out_tokens, float* out_probs) {
   clear_error();
+  DeviceRestore restore_device;
   if (n < 0 || vocab < 1 || !logits || !out_tokens || (recent && (!recent_lens || recent_stride < 0)))
     return set_error(kInvalidArgument, "mc_sample_rows: bad arguments");
   int st = check_policy(sp, nullptr, vocab, n);
@@ -752,6 +766,7 @@ int mc_sample_rows(int device, const float* logits, int n, int vocab, const int3
 
 int mc_batch_stream(mc_batch* b, int shard, void** stream) {
   clear_error();
+  DeviceRestore restore_device;
   if (!b || !stream || shard < 0 || shard >= (int)b->shard.size()) return set_error(kInvalidArgument, "mc_batch_stream: bad arguments");
   *stream = (void*)b->shard[shard]->stream;
   return kOk;
@@ -760,6 +775,7 @@ int mc_batch_stream(mc_batch* b, int shard, void** stream) {
 int mc_generate_dev(mc_batch* b, const int32_t* d_prompts, const int32_t* d_lens, int stride, int pmax, int n_new,
                     double temperature, uint32_t session0, int32_t* d_out_tokens, float* d_out_probs) {
   clear_error();
+  DeviceRestore restore_device;
   return generate_dev_impl(b, d_prompts, d_lens, stride, pmax, nullptr, n_new, temperature, session0, d_out_tokens,
                            d_out_probs, "mc_generate_dev");
 }
@@ -768,6 +784,7 @@ int mc_generate_limits(mc_batch* b, const int32_t* prompts, const int32_t* lens,
                        int n_max, double temperature, uint32_t session0, int32_t* out_tokens, float* out_probs,
                        int32_t* out_lens) {
   clear_error();
+  DeviceRestore restore_device;
   if (!max_tokens) return set_error(kInvalidArgument, "mc_generate_limits: null max_tokens");
   return generate_impl(b, prompts, lens, stride, n_max, temperature, session0, nullptr, 0, out_tokens, out_probs,
                        out_lens, nullptr, max_tokens);
@@ -777,6 +794,7 @@ int mc_generate_limits_dev(mc_batch* b, const int32_t* d_prompts, const int32_t*
                            const int32_t* d_max_tokens, int n_max, double temperature, uint32_t session0,
                            int32_t* d_out_tokens, float* d_out_probs) {
   clear_error();
+  DeviceRestore restore_device;
   if (!d_max_tokens) return set_error(kInvalidArgument, "mc_generate_limits_dev: null max_tokens");
   return generate_dev_impl(b, d_prompts, d_lens, stride, pmax, d_max_tokens, n_max, temperature, session0,
                            d_out_tokens, d_out_probs, "mc_generate_limits_dev");
@@ -784,12 +802,14 @@ int mc_generate_limits_dev(mc_batch* b, const int32_t* d_prompts, const int32_t*
 
 int mc_batch_error(mc_batch* b) {
   clear_error();
+  DeviceRestore restore_device;
   if (!b) return set_error(kInvalidArgument, "mc_batch_error: null batch");
   return sync_all(b);
 }
 
 int mc_profile_step(mc_batch* b, int max_launches, float* ms, int32_t* kinds, int* n_launches) {
   clear_error();
+  DeviceRestore restore_device;
   if (!b || !ms || !kinds || !n_launches || b->shard.size() != 1)
     return set_error(kInvalidArgument, "mc_profile_step: bad arguments (single-device batches only)");
   DevBatch& sh = *b->shard[0];
@@ -833,6 +853,7 @@ int mc_profile_step(mc_batch* b, int max_launches, float* ms, int32_t* kinds, in
 int mc_gemm_i8_dev(const int8_t* a, const int8_t* w, int m, int n, int k, const float* row_scale,
                    const float* col_scale, const float* bias, int32_t* c_i32, float* y, void* stream) {
   clear_error();
+  DeviceRestore restore_device;
   if (!a || !w) return set_error(kInvalidArgument, "mc_gemm_i8_dev: null operand");
   return gemm_i8_launch(a, w, m, n, k, row_scale, col_scale, bias, c_i32, y, (cudaStream_t)stream);
 }
@@ -840,6 +861,7 @@ int mc_gemm_i8_dev(const int8_t* a, const int8_t* w, int m, int n, int k, const 
 int mc_gemm_f32a_dev(const float* x, const int8_t* w, int m, int n, int k, float w_scale, const float* bias,
                      float* y, int32_t* slices, float* row_max_scratch, void* stream) {
   clear_error();
+  DeviceRestore restore_device;
   if (!x || !w || !y || !row_max_scratch) return set_error(kInvalidArgument, "mc_gemm_f32a_dev: null pointer");
   return gemm_f32a_launch(x, w, m, n, k, w_scale, bias, y, slices, row_max_scratch, (cudaStream_t)stream);
 }
@@ -847,6 +869,7 @@ int mc_gemm_f32a_dev(const float* x, const int8_t* w, int m, int n, int k, float
 int mc_gemm_f32a_noalloc_dev(const float* x, const int8_t* w, int m, int n, int k, float w_scale, const float* bias,
                              float* y, void* stream) {
   clear_error();
+  DeviceRestore restore_device;
   if (!x || !w || !y) return set_error(kInvalidArgument, "mc_gemm_f32a_noalloc_dev: null pointer");
   return gemm_f32a_noalloc_launch(x, w, m, n, k, w_scale, bias, y, (cudaStream_t)stream);
 }
@@ -854,6 +877,7 @@ int mc_gemm_f32a_noalloc_dev(const float* x, const int8_t* w, int m, int n, int 
 int mc_gemm_i8(int device, const int8_t* a, const int8_t* w, int m, int n, int k, const float* row_scale,
                const float* col_scale, const float* bias, int32_t* c_i32, float* y) {
   clear_error();
+  DeviceRestore restore_device;
   if (!a || !w || m <= 0 || n <= 0 || k <= 0) return set_error(kInvalidArgument, "mc_gemm_i8: bad arguments");
   MC_CUDA(cudaSetDevice(device));
   DevBuf da, dw, drs, dcs, db, dc, dy;

@@ -248,6 +248,7 @@ int quantize_full_model(const uint8_t* data, size_t n, int max_context, int devi
 
 extern "C" int mc_load_model_full(mc_ctx* ctx, const uint8_t* data, size_t n, int max_context, mc_model** out) {
   clear_error();
+  DeviceRestore restore_device;
   if (!ctx || !data || !out || ctx->devices.empty()) return set_error(kInvalidArgument, "mc_load_model_full: null argument");
   auto m = std::make_unique<mc_model>();
   m->ctx = ctx;

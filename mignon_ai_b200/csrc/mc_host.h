@@ -41,4 +41,23 @@ bool make_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
 // kDeviceTimeout with a message.
 int check_device_error(cudaStream_t stream);
 
+// Restores the calling thread's current CUDA device when the scope ends. Every entry point holds
+// one: they switch to the devices of their shards, and the caller's own work afterwards (its
+// kernels, or the _dev entry points on the default stream, which run on the current device) must
+// still run on the device the caller chose.
+struct DeviceRestore {
+  int prev = -1;
+  DeviceRestore() {
+    if (cudaGetDevice(&prev) != cudaSuccess) {
+      prev = -1;
+      cudaGetLastError();
+    }
+  }
+  ~DeviceRestore() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+  DeviceRestore(const DeviceRestore&) = delete;
+  DeviceRestore& operator=(const DeviceRestore&) = delete;
+};
+
 }  // namespace mc

@@ -67,6 +67,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_i8_rate_kernel(int iters, uin
 extern "C" int mc_probe_mma_i8(int device, int iters, int launches, double* tops, double* ms) {
   using namespace mc;
   clear_error();
+  DeviceRestore restore_device;
   if (!tops || !ms || iters < 1 || iters > (1 << 22) || launches < 1)
     return set_error(kInvalidArgument, "mc_probe_mma_i8: iters in [1, 2^22], launches >= 1, non-null outputs");
   MC_CUDA(cudaSetDevice(device));

@@ -265,6 +265,7 @@ extern "C" {
 int mc_sched_open(mc_model* model, int slots, int context_size, int max_prompt, int max_new, const mc_sampling* sp,
                   int penalize_prompt, const int32_t* stops, int n_stops, mc_sched** out) {
   clear_error();
+  DeviceRestore restore_device;
   if (!model || !out || slots <= 0 || max_new <= 0 || !sp) return set_error(kInvalidArgument, "mc_sched_open: bad arguments");
   if (n_stops < 0 || n_stops > kMaxStops || (n_stops > 0 && !stops))
     return set_error(kInvalidArgument, "mc_sched_open: 0 to 8 stop tokens");
@@ -334,12 +335,14 @@ int mc_sched_open(mc_model* model, int slots, int context_size, int max_prompt, 
 }
 
 int mc_sched_close(mc_sched* q) {
+  DeviceRestore restore_device;  // the destructors switch to the shards' devices
   delete q;
   return kOk;
 }
 
 int mc_sched_submit(mc_sched* q, const int32_t* prompt, int len, int n_new, uint32_t draw_key, int64_t* id) {
   clear_error();
+  DeviceRestore restore_device;
   if (!q || len < 0 || (len > 0 && !prompt) || n_new <= 0 || n_new > q->max_new)
     return set_error(kInvalidArgument, "mc_sched_submit: bad arguments (n_new in [1, max_new])");
   if (std::min(len, q->batch->window) > q->batch->pmax)
@@ -356,6 +359,7 @@ int mc_sched_submit(mc_sched* q, const int32_t* prompt, int len, int n_new, uint
 
 int mc_sched_step(mc_sched* q, int steps, int* in_flight) {
   clear_error();
+  DeviceRestore restore_device;
   if (!q || steps < 1) return set_error(kInvalidArgument, "mc_sched_step: bad arguments");
   int st;
   const auto t0 = std::chrono::steady_clock::now();
@@ -390,6 +394,7 @@ int mc_sched_step(mc_sched* q, int steps, int* in_flight) {
 
 int mc_sched_run(mc_sched* q, int steps_per_poll) {
   clear_error();
+  DeviceRestore restore_device;
   if (!q) return set_error(kInvalidArgument, "mc_sched_run: null scheduler");
   int left = 1, st;
   while (left > 0)
@@ -399,6 +404,7 @@ int mc_sched_run(mc_sched* q, int steps_per_poll) {
 
 int mc_sched_result(mc_sched* q, int64_t id, int32_t* tokens, float* probs, int capacity, int* n) {
   clear_error();
+  DeviceRestore restore_device;
   if (!q || id < 0 || id >= (int64_t)q->req.size() || !n) return set_error(kInvalidArgument, "mc_sched_result: bad id");
   const SchedReq& r = q->req[id];
   if (r.state != 2) {
@@ -414,6 +420,7 @@ int mc_sched_result(mc_sched* q, int64_t id, int32_t* tokens, float* probs, int 
 
 int mc_sched_stats(const mc_sched* q, int64_t* out) {
   clear_error();
+  DeviceRestore restore_device;
   if (!q || !out) return set_error(kInvalidArgument, "mc_sched_stats: bad arguments");
   out[0] = q->n_prefill;
   out[1] = q->n_steps;
@@ -430,6 +437,7 @@ int mc_sched_stats(const mc_sched* q, int64_t* out) {
 
 int mc_sched_set_admit_min(mc_sched* q, int admit_min) {
   clear_error();
+  DeviceRestore restore_device;
   if (!q || admit_min < 1) return set_error(kInvalidArgument, "mc_sched_set_admit_min: admit_min >= 1");
   q->admit_min = admit_min;
   return kOk;

@@ -18,6 +18,7 @@ __global__ void selftest_wait_kernel(int* gave_up) {
 
 extern "C" int mc_selftest_wait_timeout(int device) {
   clear_error();
+  DeviceRestore restore_device;
   MC_CUDA(cudaSetDevice(device));
   DevBuf flag;
   if (cudaMalloc(&flag.p, sizeof(int)) != cudaSuccess) {

@@ -43,3 +43,33 @@ def test_two_devices_match_one():
     np.testing.assert_array_equal(a[0], b2[0])
     np.testing.assert_array_equal(a[1], b2[1])
     assert a[2] == b2[2]
+
+
+@pytest.mark.skipif("not _two_gpus()")
+def test_entry_points_leave_the_callers_device():
+    """Calls on a context spanning devices 0 and 1 switch to each shard's device and back: the
+    caller's current device is the same after every call (a caller's own kernels, and the _dev
+    entry points on the default stream, run on the current device)."""
+    import torch
+    spec = synth.ModelSpec(**{**synth.CONFIGS[2].__dict__, "vocab": 512})
+    data = synth.build_model_file(spec)
+    n, P = 32, 16
+    prompts = synth.prompts_uniform_fast(n, P, spec.vocab, seed=17)
+    lens = np.full(n, P, np.int32)
+    for cur in (0, 1):
+        torch.cuda.set_device(cur)
+        ctx = quant.Context((0, 1))
+        m = quant.Model.decode(data, ctx)
+        assert torch.cuda.current_device() == cur
+        b = m.new_batch(n, 0, P, top_k=8)
+        b.generate(prompts, lens, 4)
+        assert torch.cuda.current_device() == cur
+        b.generate_limits(prompts, lens, np.full(n, 3, np.int32), temperature=0.7)
+        b.score(prompts, lens)
+        b.prefill(prompts, lens)
+        assert torch.cuda.current_device() == cur
+        b.close()
+        m.close()
+        ctx.close()
+        assert torch.cuda.current_device() == cur
+    torch.cuda.set_device(0)
