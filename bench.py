@@ -1040,6 +1040,18 @@ def main():
     e2e_value = tokens_per_step * e_steps / (ems / 1000.0)
     same = bool(np.array_equal(h_tok, d_tok.cpu().numpy()))
 
+    # ---- the prefill pass of the job alone (device time of one mc_prefill of the same prompts) ----
+    pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pf_ms = []
+    for _ in range(3):
+        torch.cuda.synchronize(dev)
+        pe0.record(stream)
+        batch.prefill(prompts, lens)
+        pe1.record(stream)
+        torch.cuda.synchronize(dev)
+        pf_ms.append(pe0.elapsed_time(pe1))
+    prefill_ms = float(np.median(pf_ms))
+
     # ---- per-launch device times of one decode step (steady state: window full) ----
     ms_arr = np.zeros(64, np.float32)
     kinds = np.zeros(64, np.int32)
@@ -1098,6 +1110,10 @@ def main():
                                            "capture (dram__bytes_read.sum + dram__bytes_write.sum of a full-size "
                                            "4096-session launch, 273.4 MB) scaled by the sessions",
                          "algorithmic_bytes_per_launch": attn_bytes, "avg_launch_ms": attn_ms},
+            "job_breakdown": {"prefill_ms": prefill_ms,
+                              "decode_steps_ms_estimate": float(step_ms) * (NEW - 1),
+                              "note": "prefill: device time of one mc_prefill of the job's prompts (host "
+                                      "staging included); decode: 79 x the step profiled below"},
             "decode_step_profile": {"ms_total": float(step_ms), "share": shares,
                                     "ms_per_kind": {names.get(k, str(k)): float(np.mean(v)) for k, v in per_kind.items()}},
             "cpu_baseline": cpu,
