@@ -13,6 +13,7 @@
 //    row-owning warps while the weights stream in by TMA; three MMAs per K step accumulate the
 //    planes into three exact s32 accumulators that the epilogue recombines.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -372,6 +373,220 @@ __global__ void __launch_bounds__(160, 1)
   if (warp == 4) tmem_dealloc(tmem, 512);
 }
 
+// ------------------------------------------------------------------------------------------------
+// float32 activations with the weights on the MMA's M side (K up to 1536)
+// ------------------------------------------------------------------------------------------------
+// A persistent CTA takes blocks of kWR activation rows. It slices a block's rows once into the
+// three digit planes, which stay in shared memory for the whole block, stacked along the MMA's N
+// (plane p's rows follow plane p-1's: N = 3 kWR), and streams every 128-row tile of W past them
+// (TMA loads through a kWStages ring): D[weight row][plane, activation row] accumulates the three
+// plane products of 128 output columns x kWR rows in one MMA chain, into one of two TMEM
+// accumulators, so one tile's epilogue overlaps the next tile's MMAs. An epilogue thread owns one
+// output column (its TMEM lane); a warp stores 32 consecutive columns of a row at a time. The
+// arithmetic is gemm_f32a_kernel's: the same digits, exact plane accumulators, the same epilogue.
+constexpr int kWR = 32;                  // activation rows per block
+constexpr int kWN = 3 * kWR;             // MMA N: the three planes stacked
+constexpr int kWStages = 4;              // weight-tile ring (deeper rings measured no faster)
+constexpr int kWMaxKT = 12;              // K tiles whose planes stay resident (K <= 1536)
+constexpr int kWPlaneTile = kWN * kBK;   // one K tile of the block's three planes (12 KB)
+constexpr int kWThreads = 192;           // 4 slicing / epilogue warps, the MMA warp, the producer warp
+constexpr size_t kWSmemMax = 1024 + (size_t)kWMaxKT * kWPlaneTile + (size_t)kWStages * kFTile + 256;
+
+inline size_t gemm_f32a_wm_smem(int kt) { return 1024 + (size_t)kt * kWPlaneTile + (size_t)kWStages * kFTile + 256; }
+
+__global__ void __launch_bounds__(kWThreads, 1)
+    gemm_f32a_wm_kernel(const __grid_constant__ CUtensorMap map_w, F32Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ float s_step[kWR];  // the slicing step of each row of the current block
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int KT = (args.K + kBK - 1) / kBK;
+  uint8_t* sP = smem;                                        // [KT][3 kWR rows x 128 B] digit planes
+  uint8_t* sW = smem + (size_t)KT * kWPlaneTile;             // [kWStages][128 x 128 B] weight tiles
+  uint64_t* w_full = reinterpret_cast<uint64_t*>(sW + (size_t)kWStages * kFTile);  // [kWStages]
+  uint64_t* w_empty = w_full + kWStages;
+  uint64_t* acc_full = w_empty + kWStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint64_t* p_full = acc_empty + 2;         // the current block's planes are written
+  uint64_t* p_empty = p_full + 1;           // the current block's MMAs are done with them
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_empty + 1);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nblocks = (args.M + kWR - 1) / kWR, ntiles = args.N / 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWStages; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(p_full, 128);
+    mbar_init(p_empty, 1);
+    fence_barrier_init();
+  }
+  if (warp == 4) tmem_alloc(tmem_slot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 5) {
+    // ---------------- weight tiles by TMA, in the MMA warp's order ----------------
+    if (lane == 0) {
+      uint32_t widx = 0;
+      bool ok = true;
+      for (int b = blockIdx.x; b < nblocks && ok; b += gridDim.x)
+        for (int j = 0; j < ntiles && ok; ++j)
+          for (int kt = 0; kt < KT; ++kt, ++widx) {
+            const int s = widx % kWStages;
+            if (widx >= kWStages && !mbar_wait_or_abort(&w_empty[s], ((widx / kWStages) - 1) & 1, kErrWaitEmpty)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&w_full[s], kFTile);
+            tma_load_2d(sW + (size_t)s * kFTile, &map_w, kt * kBK, j * 128, &w_full[s]);
+          }
+    }
+  } else if (warp == 4) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = idesc_i8(128, kWN);
+      const uint64_t dw0 = smem_desc_sw128(sW), dp0 = smem_desc_sw128(sP);
+      uint32_t widx = 0, tidx = 0, nb = 0;
+      bool ok = true;
+      for (int b = blockIdx.x; b < nblocks && ok; b += gridDim.x, ++nb) {
+        if (!mbar_wait_or_abort(p_full, nb & 1, kErrWaitFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int j = 0; j < ntiles && ok; ++j, ++tidx) {
+          const int slot = tidx & 1;
+          if (tidx >= 2 && !mbar_wait_or_abort(&acc_empty[slot], ((tidx / 2) - 1) & 1, kErrWaitAccFree)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t dt = tmem + (uint32_t)slot * 128;
+          for (int kt = 0; kt < KT; ++kt, ++widx) {
+            const int s = widx % kWStages;
+            if (!mbar_wait_or_abort(&w_full[s], (widx / kWStages) & 1, kErrWaitFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            // descriptors advance by their encoded start address (bytes / 16)
+            const uint64_t da = dw0 + (uint64_t)(s * (kFTile >> 4));
+            const uint64_t db = dp0 + (uint64_t)(kt * (kWPlaneTile >> 4));
+            const int ksteps = min(4, (args.K - kt * kBK + 31) / 32);
+            for (int kk = 0; kk < ksteps; ++kk) mma_i8(dt, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+            mma_commit(&w_empty[s]);
+          }
+          if (!ok) break;
+          mma_commit(&acc_full[slot]);
+        }
+        if (!ok) break;
+        mma_commit(p_empty);  // arrives once every MMA of the block has read its planes
+      }
+    }
+  } else {
+    // ---------------- slicing (per block) and epilogues (per weight tile) ----------------
+    uint32_t tidx = 0, nb = 0;
+    bool ok = true;
+    for (int b = blockIdx.x; b < nblocks; b += gridDim.x, ++nb) {
+      const int m0 = b * kWR;
+      if (nb > 0) ok = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(p_empty, (nb - 1) & 1, kErrWaitEmpty));
+      if (ok) {
+        // warp w slices rows w, w + 4, ...; lane l the K values 4l..4l+3 of every K tile (a warp
+        // reads 512 consecutive bytes of the row per tile, all tiles' loads in flight together)
+        for (int r = warp; r < kWR; r += 4) {
+          const int m = m0 + r;
+          const bool valid = m < args.M;
+          const float rm = valid ? args.row_max[m] : 0.f;
+          const float inv = row_inv_step(rm);
+          if (lane == 0) s_step[r] = row_step(rm);
+          const float* arow = args.a + (size_t)(valid ? m : 0) * args.K;
+          float4 v[kWMaxKT];
+#pragma unroll
+          for (int kt = 0; kt < kWMaxKT; ++kt) {
+            const int k = kt * kBK + 4 * lane;
+            v[kt] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (kt < KT && valid && k < args.K) {
+              if (k + 4 <= args.K) {
+                v[kt] = *reinterpret_cast<const float4*>(arow + k);
+              } else {
+                v[kt].x = arow[k];
+                if (k + 1 < args.K) v[kt].y = arow[k + 1];
+                if (k + 2 < args.K) v[kt].z = arow[k + 2];
+              }
+            }
+          }
+#pragma unroll
+          for (int kt = 0; kt < kWMaxKT; ++kt) {
+            if (kt >= KT) break;
+            const float x[4] = {v[kt].x, v[kt].y, v[kt].z, v[kt].w};
+            Digits3 d[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) d[e] = slice3(x[e], inv);
+            uint8_t* tile = sP + (size_t)kt * kWPlaneTile;
+            const int chunk = lane >> 2, byte = (4 * lane) & 15;
+            *reinterpret_cast<uint32_t*>(tile + sw128_offset(r, chunk) + byte) = pack4(d[0].d1, d[1].d1, d[2].d1, d[3].d1);
+            *reinterpret_cast<uint32_t*>(tile + sw128_offset(kWR + r, chunk) + byte) =
+                pack4(d[0].d2, d[1].d2, d[2].d2, d[3].d2);
+            *reinterpret_cast<uint32_t*>(tile + sw128_offset(2 * kWR + r, chunk) + byte) =
+                pack4(d[0].d3, d[1].d3, d[2].d3, d[3].d3);
+          }
+        }
+        fence_proxy_async_smem();  // the planes, read by the MMAs (async proxy)
+      }
+      mbar_arrive(p_full);
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // s_step of every row of the block
+      for (int j = 0; j < ntiles; ++j, ++tidx) {
+        const int slot = tidx & 1;
+        const bool got = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&acc_full[slot], (tidx / 2) & 1, kErrWaitAcc));
+        if (!got) ok = false;
+        uint32_t r1[32], r2[32], r3[32];
+        if (ok) {
+          tc_fence_after();
+          const uint32_t base = tmem_addr(tmem, 32 * warp, (uint32_t)slot * 128);
+          tmem_ld32(base, r1);
+          tmem_ld32(base + kWR, r2);
+          tmem_ld32(base + 2 * kWR, r3);
+          tmem_wait_ld();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[slot]);
+        if (!ok) continue;
+        const int n = j * 128 + 32 * warp + lane;
+        const float bn = args.bias ? args.bias[n] : 0.f;
+#pragma unroll 4
+        for (int r = 0; r < kWR; ++r) {
+          const int m = m0 + r;
+          if (m >= args.M) break;
+          const double acc = combine3((int)r1[r], (int)r2[r], (int)r3[r]);
+          const float dot = (float)(acc * (double)s_step[r]);
+          // MatVecInt8: y = dot * scale, then y += bias, each rounded (int8.go:37-40).
+          float y = __fmul_rn(dot, args.w_scale);
+          if (args.bias) y = __fadd_rn(y, bn);
+          args.y[(size_t)m * args.N + n] = y;
+          if (args.slices) {
+            const size_t plane = (size_t)args.M * args.N, o = (size_t)m * args.N + n;
+            args.slices[o] = (int)r1[r];
+            args.slices[plane + o] = (int)r2[r];
+            args.slices[2 * plane + o] = (int)r3[r];
+          }
+        }
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // s_step is rewritten by the next block's slicing
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) tmem_dealloc(tmem, 256);
+}
+
 }  // namespace gemm
 
 // ------------------------------------------------------------------------------------------------
@@ -391,6 +606,8 @@ static int gemm_device_setup(int* n_sm) {
   if (sms[dev] == 0) {
     MC_CUDA(cudaFuncSetAttribute(gemm::gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kI8Smem));
     MC_CUDA(cudaFuncSetAttribute(gemm::gemm_f32a_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kFSmem));
+    MC_CUDA(cudaFuncSetAttribute(gemm::gemm_f32a_wm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)gemm::kWSmemMax));
     int n = 0;
     MC_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
     sms[dev] = std::max(n, 1);
@@ -428,8 +645,16 @@ int gemm_f32a_launch(const float* a, const int8_t* w, int M, int N, int K, float
   if (st != kOk) return st;
   gemm::row_absmax_kernel<<<(M + 7) / 8, 256, 0, stream>>>(a, M, K, row_max_scratch);
   gemm::F32Args args{M, N, K, a, row_max_scratch, w_scale, bias, y, slices};
-  dim3 grid(N / gemm::kFBN, (M + gemm::kBM - 1) / gemm::kBM);
-  gemm::gemm_f32a_kernel<<<grid, 160, gemm::kFSmem, stream>>>(mw, args);
+  const int kt = (K + gemm::kBK - 1) / gemm::kBK;
+  const char* old_kernel = getenv("MC_GEMM_F32A_TILED");  // the one-tile-per-CTA kernel, for comparison
+  if (kt <= gemm::kWMaxKT && !old_kernel) {
+    // weights on M: each CTA slices 32 activation rows once and runs every weight tile past them
+    const int nblocks = (M + gemm::kWR - 1) / gemm::kWR;
+    gemm::gemm_f32a_wm_kernel<<<std::min(nblocks, n_sm), gemm::kWThreads, gemm::gemm_f32a_wm_smem(kt), stream>>>(mw, args);
+  } else {
+    dim3 grid(N / gemm::kFBN, (M + gemm::kBM - 1) / gemm::kBM);
+    gemm::gemm_f32a_kernel<<<grid, 160, gemm::kFSmem, stream>>>(mw, args);
+  }
   MC_CUDA(cudaGetLastError());
   return kOk;
 }

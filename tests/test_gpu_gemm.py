@@ -52,7 +52,11 @@ def slice_planes(x):
     return d1.astype(np.int64), d2.astype(np.int64), d3.astype(np.int64), step
 
 
-@pytest.mark.parametrize("m,n,k", [(256, 128, 384), (300, 256, 1152), (128, 512, 192), (256, 2048, 128)])
+# K up to 1536 runs the weights-on-M kernel (32 activation rows sliced once per CTA, every weight
+# tile streamed past them); K = 2048 the one-output-tile-per-CTA kernel. Both must give the exact
+# plane accumulators and the same float32 outputs.
+@pytest.mark.parametrize("m,n,k", [(256, 128, 384), (300, 256, 1152), (128, 512, 192), (256, 2048, 128),
+                                   (45, 384, 1536), (256, 256, 2048)])
 def test_gemm_f32a_slices_exact(m, n, k, oracle):
     import torch
     rng = np.random.default_rng(6)
