@@ -383,7 +383,8 @@ int generate_impl(mc_batch* b, const int32_t* prompts, const int32_t* lens, int 
     DevBatch& sh = *b->shard[g];
     if (sh.S == 0) continue;
     MC_CUDA(cudaSetDevice(sh.m->device));
-    if ((st = ensure_step_outputs(sh, mode == 3, n_new)) != kOk) return st;
+    // the sampler (mode 1) and the policy (mode 3) select from materialised logits
+    if ((st = ensure_step_outputs(sh, mode == 3 || mode == 1, n_new)) != kOk) return st;
     if (pol && (st = upload_policy(b, g, *pol, prompts, lens, stride)) != kOk) return st;
     MC_CUDA(cudaMemsetAsync(sh.step, 0, 4, sh.stream));
     sh.n_stops = n_stops;
@@ -447,7 +448,7 @@ int generate_dev_impl(mc_batch* b, const int32_t* d_prompts, const int32_t* d_le
   const double inv_t = mode ? 1.0 / temperature : 0.0;
   MC_CUDA(cudaSetDevice(sh.m->device));
   int st;
-  if ((st = ensure_step_outputs(sh, false, n_new)) != kOk) return st;
+  if ((st = ensure_step_outputs(sh, mode == 1, n_new)) != kOk) return st;  // the sampler selects from logits
   prepare_prompts_kernel<<<(sh.S + 127) / 128, 128, 0, sh.stream>>>(d_prompts, d_lens, stride, sh.S, P, b->window, sh.tok,
                                                                       sh.seglen, sh.pos, sh.rowmap, sh.step, sh.next_tok);
   MC_CUDA(cudaGetLastError());

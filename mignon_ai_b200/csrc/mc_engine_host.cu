@@ -381,6 +381,8 @@ static int ensure_attrs(int device) {
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<2, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<3, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem));
+  MC_CUDA(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)(kSelectWarps * kLogitsSelectMaxV * sizeof(unsigned int))));
   MC_CUDA(cudaFuncSetAttribute(policy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)policy_smem(kPolicyMaxVocab)));
   MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
@@ -813,8 +815,16 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
 
 // The head over the final-normed rows of sessions [s0, s0 + ns) of one pass (its scratch rows
 // start at row0), with the selection partials of those sessions.
+// Sampling (mode 1) takes its top-k candidates from the materialised logits, selected per row
+// by select_kernel, when the batch holds a logits buffer and the vocabulary fits the select's
+// shared memory (else from the head's per-partial top-k lists).
+static bool select_from_logits(const DevBatch& b, int mode) {
+  return mode == 1 && b.topk > 1 && b.logits != nullptr && b.m->V <= kLogitsSelectMaxV;
+}
+
 static int enqueue_head(DevBatch& b, int P, int mode, bool want_logits, int s0, int ns, size_t row0, LaunchLog* log) {
   const DevModel& m = *b.m;
+  const bool sel_logits = select_from_logits(b, mode);
   HeadArgs h;
   memset(&h, 0, sizeof(h));
   h.n_sess = ns;
@@ -830,9 +840,9 @@ static int enqueue_head(DevBatch& b, int P, int mode, bool want_logits, int s0, 
   h.tiles = m.head.tiles;
   h.scale = m.head.scale;
   h.head_b = m.head_b;
-  h.topk = mode == 1 ? b.topk : 0;
+  h.topk = mode == 1 && !sel_logits ? b.topk : 0;
   h.target = mode == 2 ? b.target + s0 : nullptr;
-  h.logits_out = want_logits || mode == 3 ? b.logits + (size_t)s0 * m.V : nullptr;
+  h.logits_out = want_logits || mode == 3 || sel_logits ? b.logits + (size_t)s0 * m.V : nullptr;
   const size_t np = (size_t)b.nsplit * 4;  // partials per session: splits x column quarters
   h.part = b.part + (size_t)s0 * np;
   h.topv = b.topv ? b.topv + (size_t)s0 * np * b.topk : nullptr;
@@ -876,7 +886,13 @@ static int enqueue_select(DevBatch& b, int mode, double inv_temp, uint32_t sessi
     sa.limit = b.limit ? b.limit + s0 : nullptr;
   }
   for (int k = 0; k < b.n_stops; ++k) sa.stops[k] = b.stops[k];
-  select_kernel<<<(ns + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, b.stream>>>(sa);
+  size_t smem = 0;
+  if (select_from_logits(b, mode)) {
+    sa.logits = b.logits + (size_t)s0 * b.m->V;
+    sa.V = b.m->V;
+    smem = (size_t)kSelectWarps * b.m->V * sizeof(unsigned int);  // each warp's row keys
+  }
+  select_kernel<<<(ns + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, smem, b.stream>>>(sa);
   MC_CUDA(cudaGetLastError());
   if (log) log->record(b.stream, 4);
   return kOk;

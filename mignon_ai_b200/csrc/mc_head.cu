@@ -260,7 +260,71 @@ struct SelectArgs {
   int stops[kMaxStops];            // seglen = 0 (greedyLoop's stop tokens, generate/greedy.go:75-77)
   int32_t* gen_n;                  // [S] tokens each session has emitted (its output column), or null: step
   const int32_t* limit;            // [S] tokens a session may emit (it ends after the last), with gen_n
+  const float* logits;             // [S][V] sampling: the top-k candidates come from the row's logits
+  int V;                           // (null: from the head's per-partial top-k lists)
 };
+
+// Sampling candidates from materialised logits: one warp per row, the row's order-preserving keys
+// staged in shared memory (kLogitsSelectMaxV per warp).
+constexpr int kLogitsSelectMaxV = 8192;
+
+// Order-preserving key of a float: unsigned comparison of keys = float comparison of values.
+__device__ __forceinline__ unsigned int float_key(float v) {
+  const unsigned int u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Warp-level radix select over the keys[0..n) (shared memory), 8 bits per pass from the top: the
+// key of the k-th largest entry, and in *r_out how many entries equal to it rank among the first
+// k. hist: 256 ints of this warp.
+__device__ __forceinline__ unsigned int warp_kth_key(const unsigned int* keys, int n, int k, int* hist, int* r_out) {
+  const int lane = threadIdx.x & 31;
+  unsigned int prefix = 0u, mask = 0u;
+  int r = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = lane; b < 256; b += 32) hist[b] = 0;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+      const unsigned int kb = keys[i];
+      if ((kb & mask) == prefix) atomicAdd(&hist[(kb >> shift) & 255], 1);
+    }
+    __syncwarp();
+    // lane l holds the bins 255 - 8l down to 248 - 8l: counts above a bin come from lower lanes
+    int c[8], tot = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      c[j] = hist[255 - 8 * lane - j];
+      tot += c[j];
+    }
+    int incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int acc = incl - tot, bin = -1, above = 0;
+    if (acc < r && r <= incl) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (bin < 0 && acc < r && r <= acc + c[j]) {
+          bin = 255 - 8 * lane - j;
+          above = acc;
+        }
+        acc += c[j];
+      }
+    }
+    const unsigned int who = __ballot_sync(0xffffffffu, bin >= 0);
+    const int src = __ffs(who) - 1;
+    bin = __shfl_sync(0xffffffffu, bin, src);
+    above = __shfl_sync(0xffffffffu, above, src);
+    prefix |= (unsigned int)bin << shift;
+    mask |= 255u << shift;
+    r -= above;
+    __syncwarp();
+  }
+  *r_out = r;
+  return prefix;
+}
 
 __device__ __forceinline__ void philox4x32_10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0,
                                               uint32_t k1, uint32_t out[4]) {
@@ -299,6 +363,8 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { retur
 __global__ void __launch_bounds__(kSelectWarps * 32) select_kernel(const SelectArgs a) {
   __shared__ float cand_v[kSelectWarps][kMaxTopK];
   __shared__ int cand_i[kSelectWarps][kMaxTopK];
+  __shared__ int sel_hist[kSelectWarps][256];
+  extern __shared__ unsigned int sel_keys[];  // [kSelectWarps][V] with a.logits (sampling)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int s = blockIdx.x * kSelectWarps + warp;
   const int step = a.step ? *a.step : 0;
@@ -327,7 +393,59 @@ __global__ void __launch_bounds__(kSelectWarps * 32) select_kernel(const SelectA
       lt += __shfl_xor_sync(0xffffffffu, lt, o);
     }
     int tok = idx;
-    if (a.mode == 1 && a.topk > 1) {
+    if (a.mode == 1 && a.topk > 1 && a.logits) {
+      // The top-k of the row's logits in (value descending, index ascending) order: the k-th
+      // largest key by radix select, then the entries above it and the first of those equal to it
+      // in index order, ranked exactly.
+      unsigned int* keys = sel_keys + (size_t)warp * a.V;
+      const float* lg = a.logits + (size_t)s * a.V;
+      for (int i = lane; i < a.V; i += 32) keys[i] = float_key(lg[i]);
+      __syncwarp();
+      const int K = min(a.topk, a.V);
+      int r_eq = 0;
+      const unsigned int tau = warp_kth_key(keys, a.V, K, sel_hist[warp], &r_eq);
+      int have = 0, eq_seen = 0;
+      for (int base = 0; base < a.V; base += 32) {
+        const int i = base + lane;
+        const unsigned int kb = i < a.V ? keys[i] : 0u;
+        const bool eq = i < a.V && kb == tau;
+        const unsigned int eqm = __ballot_sync(0xffffffffu, eq);
+        const bool take = (i < a.V && kb > tau) || (eq && eq_seen + __popc(eqm & ((1u << lane) - 1u)) < r_eq);
+        const unsigned int tm = __ballot_sync(0xffffffffu, take);
+        if (take) {
+          const int at = have + __popc(tm & ((1u << lane) - 1u));
+          cand_v[warp][at] = lg[i];
+          cand_i[warp][at] = i;
+        }
+        have += __popc(tm);
+        eq_seen += __popc(eqm);
+      }
+      __syncwarp();
+      // rank of each candidate: those before it in (value descending, index ascending) order
+      float rv[2];
+      int ri[2], rk[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int c = lane + 32 * q;
+        rv[q] = c < K ? cand_v[warp][c] : 0.f;
+        ri[q] = c < K ? cand_i[warp][c] : 0;
+        rk[q] = 0;
+        if (c < K)
+          for (int j = 0; j < K; ++j) rk[q] += better(cand_v[warp][j], cand_i[warp][j], rv[q], ri[q]) ? 1 : 0;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+        if (lane + 32 * q < K) {
+          cand_v[warp][rk[q]] = rv[q];
+          cand_i[warp][rk[q]] = ri[q];
+        }
+      for (int c = K + lane; c < a.topk; c += 32) {  // fewer tokens than k: the rest never drawn
+        cand_v[warp][c] = -INFINITY;
+        cand_i[warp][c] = 0x7fffffff;
+      }
+      __syncwarp();
+    } else if (a.mode == 1 && a.topk > 1) {
       // Merge the partials' top-k lists: repeatedly take the largest remaining value (lowest
       // index on ties); lane k walks lists k and k + 32.
       int h0 = 0, h1 = 0;
@@ -366,6 +484,9 @@ __global__ void __launch_bounds__(kSelectWarps * 32) select_kernel(const SelectA
         if (bl == lane * 2 + 1) ++h1;
       }
       __syncwarp();
+    }
+    if (a.mode == 1 && a.topk > 1) {
+      // the draw over the k candidates (sampleFromCDF over the truncated distribution)
       if (lane == 0) {
         const double mx = (double)cand_v[warp][0] * a.inv_temp;
         double sp = 0.0;
