@@ -274,19 +274,21 @@ __device__ __forceinline__ unsigned int float_key(float v) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Warp-level radix select over the keys[0..n) (shared memory), 8 bits per pass from the top: the
-// key of the k-th largest entry, and in *r_out how many entries equal to it rank among the first
-// k. hist: 256 ints of this warp.
-__device__ __forceinline__ unsigned int warp_kth_key(const unsigned int* keys, int n, int k, int* hist, int* r_out) {
+// Warp-level radix select, 8 bits per pass from the top of BITS-bit keys key(0..n-1) (an
+// order-preserving unsigned view of the values): the key of the k-th largest entry, and in *r_out
+// how many entries equal to it rank among the first k. hist: 256 ints of this warp.
+template <typename K, int BITS, class KeyFn>
+__device__ __forceinline__ K warp_radix_select(KeyFn key, int n, int k, int* hist, int* r_out) {
   const int lane = threadIdx.x & 31;
-  unsigned int prefix = 0u, mask = 0u;
+  K prefix = 0, mask = 0;
   int r = k;
-  for (int shift = 24; shift >= 0; shift -= 8) {
+#pragma unroll 1
+  for (int shift = BITS - 8; shift >= 0; shift -= 8) {
     for (int b = lane; b < 256; b += 32) hist[b] = 0;
     __syncwarp();
     for (int i = lane; i < n; i += 32) {
-      const unsigned int kb = keys[i];
-      if ((kb & mask) == prefix) atomicAdd(&hist[(kb >> shift) & 255], 1);
+      const K kb = key(i);
+      if ((kb & mask) == prefix) atomicAdd(&hist[(int)(kb >> shift) & 255], 1);
     }
     __syncwarp();
     // lane l holds the bins 255 - 8l down to 248 - 8l: counts above a bin come from lower lanes
@@ -317,8 +319,8 @@ __device__ __forceinline__ unsigned int warp_kth_key(const unsigned int* keys, i
     const int src = __ffs(who) - 1;
     bin = __shfl_sync(0xffffffffu, bin, src);
     above = __shfl_sync(0xffffffffu, above, src);
-    prefix |= (unsigned int)bin << shift;
-    mask |= 255u << shift;
+    prefix |= (K)bin << shift;
+    mask |= (K)255 << shift;
     r -= above;
     __syncwarp();
   }
@@ -403,7 +405,8 @@ __global__ void __launch_bounds__(kSelectWarps * 32) select_kernel(const SelectA
       __syncwarp();
       const int K = min(a.topk, a.V);
       int r_eq = 0;
-      const unsigned int tau = warp_kth_key(keys, a.V, K, sel_hist[warp], &r_eq);
+      const unsigned int tau =
+          warp_radix_select<unsigned int, 32>([&](int i) { return keys[i]; }, a.V, K, sel_hist[warp], &r_eq);
       int have = 0, eq_seen = 0;
       for (int base = 0; base < a.V; base += 32) {
         const int i = base + lane;

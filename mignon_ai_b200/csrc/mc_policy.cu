@@ -13,6 +13,7 @@
 // totals are scanned across the block, so they differ from Go's left-to-right sums by rounding
 // only; a draw can change only when it lies within that rounding of a bucket edge.
 #include <cfloat>
+#include <cstdlib>
 
 #include "mc_engine.cuh"
 
@@ -538,6 +539,363 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// The same policy with one warp per row and no per-row array in shared memory, for the knobs
+// whose work needs no whole-row sort: argmax, the draw in index order, and top-k up to
+// kPolRowMaxK. The warp streams its row's logits from global memory (L2-resident after the
+// head) once per pass and recomputes each value the same way every time:
+//   v(t) = logit, then -MaxFloat64 if the 3-gram block bans t, -1e300 if the automaton masks t,
+//   then the repetition penalty if t is in the window (sample.go:48-69, 213-231), with the bans
+//   and the penalty window as two bitmaps of the vocabulary in shared memory.
+// Top-k, exactly: the probabilities p = exp(x - max) / sum are non-decreasing in x = v / T. Pass A
+// takes the max and 128 group maxima of x; the k-th largest group maximum tau bounds the k-th
+// largest x from below, so the entries with x >= tau (pass B, which also sums the exponentials)
+// hold the top k unless an entry below tau has a probability equal to the k-th (rounding or
+// underflow ties). Their exact probabilities are ranked by (p descending, index ascending); if
+// the largest probability below tau is not clearly smaller than the k-th, or more than
+// kPolRowCand entries reach tau, a 64-bit radix select over the probabilities' bit patterns
+// (recomputed per pass) takes exactly the top k instead. Top-p and the draw then run over the k
+// sorted candidates in sequence, like sample.go:152-191.
+constexpr int kPolRowWarps = 4;
+constexpr int kPolRowMaxK = 64;
+constexpr int kPolRowCand = 128;
+constexpr int kPolRowSamples = 128;  // group maxima: 4 per lane
+
+__device__ __forceinline__ double pol_warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double pol_warp_max(double v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Order-preserving 64-bit key of a double (unsigned comparison of keys = comparison of values).
+__device__ __forceinline__ unsigned long long pol_dkey(double v) {
+  const unsigned long long u = (unsigned long long)__double_as_longlong(v);
+  return (u >> 63) ? ~u : (u | 0x8000000000000000ull);
+}
+
+__device__ __forceinline__ double pol_dkey_value(unsigned long long k) {
+  return __longlong_as_double((long long)((k >> 63) ? (k & 0x7fffffffffffffffull) : ~k));
+}
+
+struct PolRowValue {
+  const float* lg;
+  const uint32_t* ban;  // bitmap: the 3-gram block bans the token
+  const uint32_t* pen;  // bitmap: the token is in the repetition window
+  const int32_t* tr;    // the automaton's transitions from the row's state, or null
+  double rep_penalty;
+  __device__ __forceinline__ double operator()(int t) const {
+    double v = (double)lg[t];
+    const uint32_t bit = 1u << (t & 31);
+    if (ban[t >> 5] & bit) v = -DBL_MAX;
+    if (tr && tr[t] < 0) v = -1e300;
+    if (pen[t >> 5] & bit) v = v > 0 ? v / rep_penalty : v * rep_penalty;
+    return v;
+  }
+};
+
+__global__ void __launch_bounds__(kPolRowWarps * 32, 8) policy_row_kernel(const __grid_constant__ PolicyArgs a) {
+  extern __shared__ __align__(16) unsigned char pol_smem[];  // per warp: ban and penalty bitmaps
+  __shared__ double cand_p[kPolRowWarps][kPolRowCand];
+  __shared__ int cand_i[kPolRowWarps][kPolRowCand];
+  __shared__ int whist[kPolRowWarps][256];
+  __shared__ unsigned long long wsamp[kPolRowWarps][kPolRowSamples];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kPolRowWarps + warp;
+  const int V = a.V;
+  const int nw = (V + 31) / 32;  // bitmap words
+  uint32_t* ban = reinterpret_cast<uint32_t*>(pol_smem) + (size_t)warp * 2 * nw;
+  uint32_t* pen = ban + nw;
+  const int step = a.step ? *a.step : (int)a.step0;
+  const bool live = row < a.n_rows && (!a.seglen || a.seglen[row] > 0);
+  if (live) {
+    const int cnt = a.gen_n ? a.gen_n[row] : step;
+    const uint32_t dkey = a.key ? a.key[row] : a.session0 + (uint32_t)row;
+    const int ng = a.gen ? (a.gen_len ? a.gen_len[row] : cnt) : 0;
+    const int32_t* gen = a.gen ? a.gen + (size_t)row * a.gen_stride : nullptr;
+    const int np = a.prefix ? a.prefix_len[row] : 0;
+    const int32_t* pre = a.prefix ? a.prefix + (size_t)row * a.prefix_stride : nullptr;
+    const int state = a.dfa && a.dfa_state ? a.dfa_state[row] : -1;
+    for (int w = lane; w < 2 * nw; w += 32) ban[w] = 0u;
+    __syncwarp();
+    // 1. 3-gram block
+    if (a.ban_trigrams && ng >= 2) {
+      const int32_t w1 = gen[ng - 2], w2 = gen[ng - 1];
+      for (int i = lane; i <= ng - 3; i += 32) {
+        const int32_t t = gen[i + 2];
+        if (gen[i] == w1 && gen[i + 1] == w2 && t >= 0 && t < V) atomicOr(&ban[t >> 5], 1u << (t & 31));
+      }
+    }
+    // 3a. repetition penalty: each distinct in-range token of the window (the bitmap makes it once)
+    const int total = np + ng;
+    const int w = a.rep_window > 0 && a.rep_window < total ? a.rep_window : total;
+    if (a.rep_penalty > 1.0 && w > 0) {
+      for (int j = lane; j < w; j += 32) {
+        const int32_t t = pol_hist(pre, np, gen, total - w + j);
+        if (t >= 0 && t < V) atomicOr(&pen[t >> 5], 1u << (t & 31));
+      }
+    }
+    __syncwarp();
+    // 2. the constraint mask is read from the automaton's row in each pass
+    const PolRowValue val{a.logits + (size_t)row * V, ban, pen, state >= 0 ? a.dfa + (size_t)state * V : nullptr,
+                          a.rep_penalty};
+    int tok = 0;
+    double prob = 0.0;
+    if (a.temperature <= 0.001) {
+      // 3b. argmax; prob = 1 / sum exp(v - max)
+      double bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int t = lane; t < V; t += 32) {
+        const double v = val(t);
+        if (pol_better(v, t, bv, bi)) bv = v, bi = t;
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (pol_better(ov, oi, bv, bi)) bv = ov, bi = oi;
+      }
+      double s = 0.0;
+      for (int t = lane; t < V; t += 32) s += exp(val(t) - bv);
+      s = pol_warp_sum(s);
+      tok = bi;
+      prob = 1.0 / s;
+    } else {
+      const double inv_t = 1.0 / a.temperature;
+      const double u = a.u ? a.u[row] : sample_uniform(dkey, (uint32_t)cnt);
+      if (a.top_k <= 0 && a.top_p >= 0.9999) {
+        // 3d. the draw in index order: lane l owns the chunk [l*c, (l+1)*c); running sums from
+        // the exclusive scan of the chunk totals
+        double m = -DBL_MAX;
+        for (int t = lane; t < V; t += 32) {
+          const double x = val(t) * inv_t;
+          m = x > m ? x : m;
+        }
+        m = pol_warp_max(m);
+        const int c = (V + 31) / 32;
+        const int lo = min(V, lane * c), hi = min(V, lo + c);
+        double cs = 0.0;
+        for (int t = lo; t < hi; ++t) cs += exp(val(t) * inv_t - m);
+        double incl = cs;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const double y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const double base = incl - cs;
+        // the running sum at V - 1 (its owner walks its chunk from the base)
+        double cum = base;
+        for (int t = lo; t < hi; ++t) cum += exp(val(t) * inv_t - m);
+        const double s = __shfl_sync(0xffffffffu, cum, (V - 1) / c);
+        const double thr = u * s;
+        int first = 0x7fffffff;
+        double efirst = 0.0;
+        cum = base;
+        for (int t = lo; t < hi; ++t) {
+          const double e = exp(val(t) * inv_t - m);
+          cum += e;
+          if (cum >= thr) {
+            first = t;
+            efirst = e;
+            break;
+          }
+        }
+        int f = first;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) f = min(f, __shfl_xor_sync(0xffffffffu, f, o));
+        tok = f == 0x7fffffff ? 0 : f;
+        const double e_tok = f == 0x7fffffff ? exp(val(0) * inv_t - m)
+                                             : __shfl_sync(0xffffffffu, efirst, __ffs(__ballot_sync(0xffffffffu, first == f)) - 1);
+        prob = e_tok / s;
+      } else {
+        // 3e. top-k (0 < k < V, k <= kPolRowMaxK)
+        const int K = a.top_k;
+        double* cp = cand_p[warp];
+        int* ci = cand_i[warp];
+        // pass A: the max and the group maxima of x (lane l, group g: the lane's entries with j % 4 == g)
+        double m = -DBL_MAX;
+        double gm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        for (int j0 = 0; j0 * 32 < V; j0 += 4) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int t = (j0 + g) * 32 + lane;
+            if (t < V) {
+              const double x = val(t) * inv_t;
+              m = x > m ? x : m;
+              gm[g] = fmax(gm[g], x);
+            }
+          }
+        }
+        m = pol_warp_max(m);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) wsamp[warp][lane * 4 + g] = pol_dkey(gm[g]);
+        __syncwarp();
+        int r_unused;
+        const double tau = pol_dkey_value(warp_radix_select<unsigned long long, 64>(
+            [&](int i) { return wsamp[warp][i]; }, kPolRowSamples, K, whist[warp], &r_unused));
+        // pass B: the sum of the exponentials; the entries with x >= tau in index order, and the
+        // largest x below tau
+        double s = 0.0, xo = -INFINITY;
+        int C = 0;
+        for (int j = 0; j * 32 < V; ++j) {
+          const int t = j * 32 + lane;
+          const bool in = t < V;
+          const double x = in ? val(t) * inv_t : 0.0;
+          if (in) s += exp(x - m);
+          const bool take = in && x >= tau;
+          if (in && !take) xo = fmax(xo, x);
+          const unsigned int tm = __ballot_sync(0xffffffffu, take);
+          if (take) {
+            const int at = C + __popc(tm & ((1u << lane) - 1u));
+            if (at < kPolRowCand) {
+              cp[at] = x;
+              ci[at] = t;
+            }
+          }
+          C += __popc(tm);
+        }
+        s = pol_warp_sum(s);
+        xo = pol_warp_max(xo);
+        const double inv = 1.0 / s;
+        bool exact = C <= kPolRowCand;
+        if (exact) {
+          __syncwarp();
+          for (int c = lane; c < C; c += 32) cp[c] = exp(cp[c] - m) * inv;
+          __syncwarp();
+        }
+        // rank the candidates: those before each in (p descending, index ascending) order
+        auto rank_in_place = [&](int n) {
+          double rv[kPolRowCand / 32];
+          int ri[kPolRowCand / 32], rk[kPolRowCand / 32];
+#pragma unroll
+          for (int q = 0; q < kPolRowCand / 32; ++q) {
+            const int c = lane + 32 * q;
+            rv[q] = c < n ? cp[c] : 0.0;
+            ri[q] = c < n ? ci[c] : 0;
+            rk[q] = 0;
+            if (c < n)
+              for (int j = 0; j < n; ++j) rk[q] += pol_better(cp[j], ci[j], rv[q], ri[q]) ? 1 : 0;
+          }
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < kPolRowCand / 32; ++q)
+            if (lane + 32 * q < n && rk[q] < K) {
+              cp[rk[q]] = rv[q];
+              ci[rk[q]] = ri[q];
+            }
+          __syncwarp();
+        };
+        if (exact) {
+          rank_in_place(C);
+          // no entry below tau may reach the k-th probability (a margin covers the last bits of exp)
+          const double p_out = xo == -INFINITY ? 0.0 : exp(xo - m) * inv;
+          exact = p_out * (1.0 + 0x1p-40) < cp[K - 1];
+        }
+        if (!exact) {
+          // exactly the top k by the 64-bit patterns of p (>= 0, so they order like p): the entries
+          // above the k-th pattern, then the first r_eq equal to it in index order
+          auto pbits = [&](int t) {
+            return (unsigned long long)__double_as_longlong(exp(val(t) * inv_t - m) * inv);
+          };
+          int r_eq = 0;
+          const unsigned long long kth = warp_radix_select<unsigned long long, 64>(pbits, V, K, whist[warp], &r_eq);
+          int have = 0, eq_seen = 0;
+          for (int j = 0; j * 32 < V; ++j) {
+            const int t = j * 32 + lane;
+            const unsigned long long kb = t < V ? pbits(t) : 0ull;
+            const bool eq = t < V && kb == kth;
+            const unsigned int eqm = __ballot_sync(0xffffffffu, eq);
+            const bool take = (t < V && kb > kth) || (eq && eq_seen + __popc(eqm & ((1u << lane) - 1u)) < r_eq);
+            const unsigned int tm = __ballot_sync(0xffffffffu, take);
+            if (take) {
+              const int at = have + __popc(tm & ((1u << lane) - 1u));
+              cp[at] = __longlong_as_double((long long)kb);
+              ci[at] = t;
+            }
+            have += __popc(tm);
+            eq_seen += __popc(eqm);
+          }
+          __syncwarp();
+          rank_in_place(K);
+        }
+        // 3f. the shortest prefix whose mass reaches top-p, then the draw (in sequence)
+        if (lane == 0) {
+          int active = K;
+          if (a.top_p > 0.0 && a.top_p < 1.0) {
+            double cum = 0.0;
+            int cut = 0;
+            for (int i = 0; i < active; ++i) {
+              cum += cp[i];
+              cut = i + 1;
+              if (cum >= a.top_p) break;
+            }
+            active = cut;
+          }
+          if (active == 1) {
+            tok = ci[0];
+            prob = 1.0;
+          } else {
+            double sp = 0.0;
+            for (int i = 0; i < active; ++i) sp += cp[i];
+            const double r = u * sp;
+            double cum = 0.0;
+            int k = active - 1;
+            for (int i = 0; i < active; ++i) {
+              cum += cp[i];
+              if (r <= cum) {
+                k = i;
+                break;
+              }
+            }
+            tok = ci[k];
+            prob = cp[k] / sp;
+          }
+        }
+      }
+    }
+    // 4. stop tokens, outputs, position, constraint advance
+    if (lane == 0) {
+      bool stop = false;
+      for (int k = 0; k < a.n_stops; ++k) stop |= a.stops[k] >= 0 && tok == a.stops[k];
+      if (stop) {
+        if (a.seglen) a.seglen[row] = 0;
+      } else {
+        const int col = a.gen_n || a.step ? cnt : 0;
+        if (a.next_tok) a.next_tok[row] = tok;
+        a.out_tok[(size_t)row * a.out_stride + col] = tok;
+        if (a.out_prob) a.out_prob[(size_t)row * a.out_stride + col] = (float)prob;
+        if (a.pos) {
+          if (a.advance_from_len) a.pos[row] = a.pos[row] + a.seglen[row];
+          else a.pos[row] = a.pos[row] + 1;
+          a.seglen[row] = 1;
+        }
+        if (state >= 0) a.dfa_state[row] = a.dfa[(size_t)state * V + tok];
+        if (a.gen_n) {
+          a.gen_n[row] = cnt + 1;
+          if (a.limit && a.seglen && cnt + 1 >= a.limit[row]) a.seglen[row] = 0;  // its last token
+        }
+      }
+    }
+  }
+  if (a.done) {
+    // the last block to finish advances the step counter (every block has read it by then)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(a.done, 1) == (int)gridDim.x - 1) {
+        *a.step += 1;
+        *a.done = 0;
+        __threadfence();
+      }
+    }
+  }
+}
+
 inline int policy_vp(int V) {
   int vp = 2;  // even, so the candidate arrays after the row's keys and indices stay 8-byte aligned
   while (vp < V) vp <<= 1;
@@ -569,6 +927,16 @@ int launch_policy(PolicyArgs& a, cudaStream_t s) {
   a.kp = 1;
   while (a.kp < a.top_k && a.kp < kPolicyMaxK) a.kp <<= 1;
   a.kcap = 2 * a.kp;  // room for float-key ties beyond the top k
+  const bool draw = a.temperature > 0.001;
+  const bool index_draw = draw && a.top_k <= 0 && a.top_p >= 0.9999;
+  const bool small_k = draw && !index_draw && a.top_k > 0 && a.top_k < a.V && a.top_k <= kPolRowMaxK;
+  const bool force_block = getenv("MC_POLICY_BLOCK") != nullptr;  // the CTA-per-row kernel for every knob
+  if (!force_block && (!draw || index_draw || small_k)) {
+    const size_t smem = (size_t)kPolRowWarps * 2 * ((a.V + 31) / 32) * sizeof(uint32_t);  // <= 16 KB
+    if (a.n_rows > 0) policy_row_kernel<<<(a.n_rows + kPolRowWarps - 1) / kPolRowWarps, kPolRowWarps * 32, smem, s>>>(a);
+    MC_CUDA(cudaGetLastError());
+    return kOk;
+  }
   const size_t smem = policy_smem_for(a);  // within the limit raised once per device (policy_smem)
   if (a.n_rows > 0) policy_kernel<<<a.n_rows, kPolicyThreads, smem, s>>>(a);
   MC_CUDA(cudaGetLastError());

@@ -65,14 +65,25 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("kernel", ["warp", "block"])
 @pytest.mark.parametrize("V", [16, 257, 2048, 4096, 16384])
-def test_sample_rows_match_oracle(oracle, V):
+def test_sample_rows_match_oracle(oracle, V, kernel, monkeypatch):
+    """Both kernels on the same rows: the warp-per-row kernel takes argmax, the index-order draw
+    and top-k up to 64; MC_POLICY_BLOCK=1 sends every launch to the CTA-per-row kernel. Row 3
+    ties everywhere (one value: the warp kernel's candidate room overflows and its 64-bit select
+    runs), row 5 holds values a few float ulps apart, and the masked rows of the odd cases put
+    -1e300 entries below the group-maximum bound."""
+    if kernel == "block":
+        monkeypatch.setenv("MC_POLICY_BLOCK", "1")
+    else:
+        monkeypatch.delenv("MC_POLICY_BLOCK", raising=False)
     rng = np.random.default_rng(V)
     n = 48 if V <= 4096 else 12
     for ci, sp in enumerate(CASES):
         scale = np.where(np.arange(n) % 2 == 0, 2.0, 0.02)[:, None]
         logits = (rng.standard_normal((n, V)) * scale).astype(np.float32)
         logits[3] = np.round(logits[3])  # ties
+        logits[5] = (1.0 + np.spacing(np.float32(1.0)) * rng.integers(0, 64, V)).astype(np.float32)
         m = 14
         recent = rng.integers(0, min(V, 6), size=(n, m)).astype(np.int32)
         rlen = rng.integers(0, m + 1, size=n).astype(np.int32)
@@ -92,6 +103,38 @@ def test_sample_rows_match_oracle(oracle, V):
                 assert m_edge < 1e-9, f"V={V} case {ci} row {r}: {got_t[r]} != {want_t} ({m_edge:.3g} from an edge)"
                 continue
             assert got_p[r] == pytest.approx(want_p, rel=1e-5), (V, ci, r)
+
+
+@pytest.mark.parametrize("kernel", ["warp", "block"])
+def test_sample_rows_zero_probability_ties(oracle, kernel, monkeypatch):
+    """Rows where fewer than k tokens have a non-zero probability: the automaton allows 10 tokens
+    (the others get -1e300), or the logits spread so far that most exponentials underflow to 0.
+    The k-th probability is then 0 and the top k is completed by the lowest indices among the
+    zeros, which the warp kernel's group-maximum bound cannot see (its exact fallback runs)."""
+    if kernel == "block":
+        monkeypatch.setenv("MC_POLICY_BLOCK", "1")
+    else:
+        monkeypatch.delenv("MC_POLICY_BLOCK", raising=False)
+    rng = np.random.default_rng(77)
+    n, V = 16, 2048
+    logits = rng.standard_normal((n, V)).astype(np.float32)
+    logits[n // 2:] *= 3000.0
+    allowed = np.full((n, V), -1, np.int32)
+    for r in range(n // 2):
+        allowed[r, rng.choice(V, 10, replace=False)] = 0
+    allowed[n // 2:] = 0
+    for ci, sp in enumerate([S(0.8, 1.0, 40, 1.0, 0, False), S(0.8, 1.2, 40, 0.95, 6, True),
+                             S(0.0, 1.0, 0, 1.0, 0, False), S(0.8, 1.0, 0, 1.0, 0, False)]):
+        got_t, got_p = quant.sample_rows(logits, sp, allowed=allowed, session0=3 * ci, step=5)
+        osp = _oracle_sampling(oracle, sp)
+        for r in range(n):
+            u = synth.sample_uniform(3 * ci + r, 5)
+            want_t, want_p = oracle.sample_policy(logits[r].astype(np.float64), osp, (), [], allowed[r], u)
+            if got_t[r] != want_t:
+                m_edge = policy_margin(logits[r], sp, (), [], allowed[r], u)
+                assert m_edge < 1e-9, f"case {ci} row {r}: {got_t[r]} != {want_t} ({m_edge:.3g} from an edge)"
+                continue
+            assert got_p[r] == pytest.approx(want_p, rel=1e-5), (ci, r)
 
 
 def test_sample_rows_python_statement_on_one_row():
