@@ -714,7 +714,7 @@ __device__ __forceinline__ void decode_block(const BlockArgs& a, const DecodeLay
     if (a.final_norm && a.fuse_head) {
       norm_rows(a.final_gain, nullptr, false, nullptr, true);
       publish();
-      const int step = *a.step;  // read before this CTA's arrival below, so before any increment
+      const int step = a.head_logits ? 0 : *a.step;  // read before this CTA's arrival below, so before any increment
       float hm[kDCols], hs[kDCols];
       int hi[kDCols];
 #pragma unroll
@@ -730,6 +730,13 @@ __device__ __forceinline__ void decode_block(const BlockArgs& a, const DecodeLay
         const int v = c * 128 + chl;
         if (v >= a.V) return;
         const float scale = a.gemms[gi - 1].scale;
+        if (a.head_logits) {  // the policy's logits: 32 consecutive channels of a session per warp
+#pragma unroll
+          for (int j = 0; j < kDCols; ++j)
+            if (bars->valid[r0 + j])
+              a.head_logits[(size_t)(s0 + r0 + j) * a.V + v] = __fadd_rn(dequant(x1[j], x2[j], x3[j], stp[j], scale), pv.x);
+          return;
+        }
 #pragma unroll
         for (int j = 0; j < kDCols; ++j) {
           const float l = __fadd_rn(dequant(x1[j], x2[j], x3[j], stp[j], scale), pv.x);
@@ -743,6 +750,8 @@ __device__ __forceinline__ void decode_block(const BlockArgs& a, const DecodeLay
           hs[j] = __fadd_rn(hs[j], __expf(l - hm[j]));
         }
       });
+      if (a.head_logits) goto head_done;
+      {
       // combine over the 32 channels of the warp, then over the four quadrant warps
       auto combine = [](float& m, float& sm, int& i, float m2, float s2, int i2) {
         const float M = fmaxf(m, m2);
@@ -800,6 +809,8 @@ __device__ __forceinline__ void decode_block(const BlockArgs& a, const DecodeLay
           __threadfence();
         }
       }
+      }
+    head_done:;
     }
 
     // ---- the block's output rows for the next kernel ----

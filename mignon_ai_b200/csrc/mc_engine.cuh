@@ -79,6 +79,8 @@ struct BlockArgs {
   // tied head; each session's first argmax and probability (argmaxProb) are written as
   // select_kernel would, and the last CTA to finish advances the step counter.
   int fuse_head;
+  float* head_logits;   // [S][V] or null: the fused head writes each session's logits instead of
+                        // selecting (the decode-loop policy reads them; no step counter advance)
   const float* head_b;  // [V]
   int32_t* next_tok;    // [S]
   int32_t* out_tok;     // [S][out_stride] or null

@@ -592,7 +592,8 @@ __global__ void prepare_prompts_kernel(const int32_t* prompts, const int32_t* le
 
 // The arguments of launch bi of one forward (the CA blocks, then bi = blocks: the final one) for
 // P rows per session; *bs: rule steps of the blocks before bi (advanced past block bi).
-static void build_block_args(const DevBatch& b, int P, int bi, bool fuse_head, int* bs, BlockArgs& a) {
+static void build_block_args(const DevBatch& b, int P, int bi, bool fuse_head, int* bs, BlockArgs& a,
+                             bool head_logits = false) {
   const DevModel& m = *b.m;
   const int nb = (int)m.blocks.size();
   fill_common(b, a, P);
@@ -629,7 +630,13 @@ static void build_block_args(const DevBatch& b, int P, int bi, bool fuse_head, i
     a.block = nb;
     a.embed_first = nb == 0;
     a.final_norm = 1;
-    if (fuse_head) {
+    if (fuse_head && head_logits) {
+      // the head runs inside the final decode launch and writes the logits (the policy selects)
+      a.fuse_head = 1;
+      a.gemms[g++] = spec(m.head, kGHead, 0);
+      a.head_b = m.head_b;
+      a.head_logits = b.logits;
+    } else if (fuse_head) {
       // the greedy head and selection run inside the final decode launch
       a.fuse_head = 1;
       a.gemms[g++] = spec(m.head, kGHead, 0);
@@ -685,7 +692,8 @@ static int segment_tiles(const DevBatch& b, int P) {
 
 // Enqueues the blocks (and attention sublayers) of one segment: P rows per session, P = 1 a decode
 // step; ends with the final RMSNorm of every row. pr: a prefill pass over some tiles (null: all).
-static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = false, const PassRange* pr = nullptr) {
+static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = false, const PassRange* pr = nullptr,
+                          bool head_logits = false) {
   const DevModel& m = *b.m;
   cudaStream_t s = b.stream;
   const int nb = (int)m.blocks.size();
@@ -695,7 +703,7 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
   int bs = 0;
   for (int bi = 0; bi <= nb; ++bi) {
     BlockArgs a;
-    build_block_args(b, P, bi, fuse_head, &bs, a);
+    build_block_args(b, P, bi, fuse_head, &bs, a, head_logits);
     if (pr) {
       a.tile0 = pr->t0;
       a.cur = rows_back(a.cur, row0 * m.D);
@@ -843,6 +851,7 @@ static int enqueue_head(DevBatch& b, int P, int mode, bool want_logits, int s0, 
   h.topk = mode == 1 && !sel_logits ? b.topk : 0;
   h.target = mode == 2 ? b.target + s0 : nullptr;
   h.logits_out = want_logits || mode == 3 || sel_logits ? b.logits + (size_t)s0 * m.V : nullptr;
+  h.logits_only = mode == 3 ? 1 : 0;  // the policy kernel reads the logits, not the partials
   const size_t np = (size_t)b.nsplit * 4;  // partials per session: splits x column quarters
   h.part = b.part + (size_t)s0 * np;
   h.topv = b.topv ? b.topv + (size_t)s0 * np * b.topk : nullptr;
@@ -905,6 +914,8 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
   // greedy decode steps without logits: the head and the selection are fused into the final
   // decode launch
   const bool fuse = P == 1 && b.decode_kernel && mode == 0 && !want_logits && !getenv("MC_NO_FUSED_HEAD");
+  // decode steps under the policy: the head fused into the final decode launch writes the logits
+  const bool fuse_logits = P == 1 && b.decode_kernel && mode == 3 && !getenv("MC_NO_FUSED_HEAD");
   int st;
   const int total = segment_tiles(b, P);
   const int per = (int)(b.rows / 128);
@@ -925,9 +936,9 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
         return st;
     }
   } else {
-    if ((st = enqueue_layers(b, P, log, fuse)) != kOk) return st;
+    if ((st = enqueue_layers(b, P, log, fuse || fuse_logits, nullptr, fuse_logits)) != kOk) return st;
     if (fuse) return kOk;
-    if ((st = enqueue_head(b, P, mode, want_logits, 0, b.S, 0, log)) != kOk) return st;
+    if (!fuse_logits && (st = enqueue_head(b, P, mode, want_logits, 0, b.S, 0, log)) != kOk) return st;
     if (mode != 3) return enqueue_select(b, mode, inv_temp, session0, advance_from_len, 0, b.S, true, log);
   }
   if (mode != 3) return kOk;

@@ -31,6 +31,7 @@ struct HeadArgs {
   int topk;                // 0: no top-k lists
   const int32_t* target;   // [S] or null
   float* logits_out;       // [S][V] or null
+  int logits_only;         // with logits_out: no partials (the policy kernel reads the logits only)
   float4* part;            // [S][nsplit]: max, sum, first argmax (bits), target logit
   float* topv;             // [S][nsplit][topk]
   int32_t* topi;
@@ -194,6 +195,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             l16[j] = __fadd_rn(dequant(a1[j], a2[j], a3[j], step, a.scale), bars->bias[ci * kNC + j0 + j]);
           const int v0 = c * kNC + j0;
           if (a.logits_out) st16(a.logits_out + (size_t)s * a.V, v0, a.V, l16);
+          if (a.logits_only) continue;
           // chunk-local max first, then one rescale of the running sum
           float cm = -INFINITY;
           int ci2 = 0;
@@ -232,7 +234,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
       tc_fence_before();
       mbar_arrive(&bars->acc_empty);
     }
-    if (valid) a.part[(size_t)s * npart + pi] = make_float4(m, sum, __int_as_float(idx), lt);
+    if (valid && !a.logits_only) a.part[(size_t)s * npart + pi] = make_float4(m, sum, __int_as_float(idx), lt);
   }
   tc_fence_before();
   __syncthreads();

@@ -587,20 +587,41 @@ struct PolRowValue {
   const float* lg;
   const uint32_t* ban;  // bitmap: the 3-gram block bans the token
   const uint32_t* pen;  // bitmap: the token is in the repetition window
+  const uint32_t* mod;  // bitmap: ban | pen
   const int32_t* tr;    // the automaton's transitions from the row's state, or null
   double rep_penalty;
-  __device__ __forceinline__ double operator()(int t) const {
-    double v = (double)lg[t];
+  // the token's value differs from its logit (banned, penalised or masked)
+  __device__ __forceinline__ bool modified(int t) const {
+    return ((mod[t >> 5] >> (t & 31)) & 1u) || (tr && tr[t] < 0);
+  }
+  // (not inlined: a predicated copy of the penalty's double division would run for every token)
+  __device__ __noinline__ double full(float f, int t) const {
+    double v = (double)f;
     const uint32_t bit = 1u << (t & 31);
     if (ban[t >> 5] & bit) v = -DBL_MAX;
     if (tr && tr[t] < 0) v = -1e300;
     if (pen[t >> 5] & bit) v = v > 0 ? v / rep_penalty : v * rep_penalty;
     return v;
   }
+  __device__ __forceinline__ double operator()(int t) const {
+    const float f = lg[t];
+    return modified(t) ? full(f, t) : (double)f;
+  }
+  // The value of token t (t < V when in), every lane of the warp calling: the rare modified
+  // tokens take the full path under a warp-uniform branch.
+  __device__ __forceinline__ double warp_value(int t, bool in) const {
+    const float f = in ? lg[t] : 0.f;
+    const bool m = in && modified(t);
+    double v = (double)f;
+    if (__any_sync(0xffffffffu, m)) {
+      if (m) v = full(f, t);
+    }
+    return v;
+  }
 };
 
-__global__ void __launch_bounds__(kPolRowWarps * 32, 8) policy_row_kernel(const __grid_constant__ PolicyArgs a) {
-  extern __shared__ __align__(16) unsigned char pol_smem[];  // per warp: ban and penalty bitmaps
+__global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const __grid_constant__ PolicyArgs a) {
+  extern __shared__ __align__(16) unsigned char pol_smem[];  // per warp: ban, penalty and ban|penalty bitmaps
   __shared__ double cand_p[kPolRowWarps][kPolRowCand];
   __shared__ int cand_i[kPolRowWarps][kPolRowCand];
   __shared__ int whist[kPolRowWarps][256];
@@ -609,8 +630,9 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 8) policy_row_kernel(const 
   const int row = blockIdx.x * kPolRowWarps + warp;
   const int V = a.V;
   const int nw = (V + 31) / 32;  // bitmap words
-  uint32_t* ban = reinterpret_cast<uint32_t*>(pol_smem) + (size_t)warp * 2 * nw;
+  uint32_t* ban = reinterpret_cast<uint32_t*>(pol_smem) + (size_t)warp * 3 * nw;
   uint32_t* pen = ban + nw;
+  uint32_t* mod = pen + nw;
   const int step = a.step ? *a.step : (int)a.step0;
   const bool live = row < a.n_rows && (!a.seglen || a.seglen[row] > 0);
   if (live) {
@@ -621,14 +643,17 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 8) policy_row_kernel(const 
     const int np = a.prefix ? a.prefix_len[row] : 0;
     const int32_t* pre = a.prefix ? a.prefix + (size_t)row * a.prefix_stride : nullptr;
     const int state = a.dfa && a.dfa_state ? a.dfa_state[row] : -1;
-    for (int w = lane; w < 2 * nw; w += 32) ban[w] = 0u;
+    for (int w = lane; w < 3 * nw; w += 32) ban[w] = 0u;
     __syncwarp();
     // 1. 3-gram block
     if (a.ban_trigrams && ng >= 2) {
       const int32_t w1 = gen[ng - 2], w2 = gen[ng - 1];
       for (int i = lane; i <= ng - 3; i += 32) {
         const int32_t t = gen[i + 2];
-        if (gen[i] == w1 && gen[i + 1] == w2 && t >= 0 && t < V) atomicOr(&ban[t >> 5], 1u << (t & 31));
+        if (gen[i] == w1 && gen[i + 1] == w2 && t >= 0 && t < V) {
+          atomicOr(&ban[t >> 5], 1u << (t & 31));
+          atomicOr(&mod[t >> 5], 1u << (t & 31));
+        }
       }
     }
     // 3a. repetition penalty: each distinct in-range token of the window (the bitmap makes it once)
@@ -637,22 +662,26 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 8) policy_row_kernel(const 
     if (a.rep_penalty > 1.0 && w > 0) {
       for (int j = lane; j < w; j += 32) {
         const int32_t t = pol_hist(pre, np, gen, total - w + j);
-        if (t >= 0 && t < V) atomicOr(&pen[t >> 5], 1u << (t & 31));
+        if (t >= 0 && t < V) {
+          atomicOr(&pen[t >> 5], 1u << (t & 31));
+          atomicOr(&mod[t >> 5], 1u << (t & 31));
+        }
       }
     }
     __syncwarp();
     // 2. the constraint mask is read from the automaton's row in each pass
-    const PolRowValue val{a.logits + (size_t)row * V, ban, pen, state >= 0 ? a.dfa + (size_t)state * V : nullptr,
-                          a.rep_penalty};
+    const PolRowValue val{a.logits + (size_t)row * V, ban, pen, mod,
+                          state >= 0 ? a.dfa + (size_t)state * V : nullptr, a.rep_penalty};
     int tok = 0;
     double prob = 0.0;
     if (a.temperature <= 0.001) {
       // 3b. argmax; prob = 1 / sum exp(v - max)
       double bv = -INFINITY;
       int bi = 0x7fffffff;
-      for (int t = lane; t < V; t += 32) {
-        const double v = val(t);
-        if (pol_better(v, t, bv, bi)) bv = v, bi = t;
+      for (int j = 0; j * 32 < V; ++j) {
+        const int t = j * 32 + lane;
+        const double v = val.warp_value(t, t < V);
+        if (t < V && pol_better(v, t, bv, bi)) bv = v, bi = t;
       }
 #pragma unroll
       for (int o = 16; o; o >>= 1) {
@@ -661,7 +690,11 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 8) policy_row_kernel(const 
         if (pol_better(ov, oi, bv, bi)) bv = ov, bi = oi;
       }
       double s = 0.0;
-      for (int t = lane; t < V; t += 32) s += exp(val(t) - bv);
+      for (int j = 0; j * 32 < V; ++j) {
+        const int t = j * 32 + lane;
+        const double v = val.warp_value(t, t < V);
+        if (t < V) s += exp(v - bv);
+      }
       s = pol_warp_sum(s);
       tok = bi;
       prob = 1.0 / s;
@@ -672,9 +705,10 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 8) policy_row_kernel(const 
         // 3d. the draw in index order: lane l owns the chunk [l*c, (l+1)*c); running sums from
         // the exclusive scan of the chunk totals
         double m = -DBL_MAX;
-        for (int t = lane; t < V; t += 32) {
-          const double x = val(t) * inv_t;
-          m = x > m ? x : m;
+        for (int j = 0; j * 32 < V; ++j) {
+          const int t = j * 32 + lane;
+          const double x = val.warp_value(t, t < V) * inv_t;
+          if (t < V) m = x > m ? x : m;
         }
         m = pol_warp_max(m);
         const int c = (V + 31) / 32;
@@ -718,20 +752,35 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 8) policy_row_kernel(const 
         double* cp = cand_p[warp];
         int* ci = cand_i[warp];
         // pass A: the max and the group maxima of x (lane l, group g: the lane's entries with j % 4 == g)
-        double m = -DBL_MAX;
-        double gm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        // (the maxima of x = v / T are the maxima of v times 1/T, since rounding keeps the order;
+        // unmodified values are their float logits, so those maxima are taken in float)
+        float fm = -INFINITY, fg[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        double dm = -INFINITY, dg[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         for (int j0 = 0; j0 * 32 < V; j0 += 4) {
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
             const int t = (j0 + g) * 32 + lane;
-            if (t < V) {
-              const double x = val(t) * inv_t;
-              m = x > m ? x : m;
-              gm[g] = fmax(gm[g], x);
+            const bool in = t < V;
+            const float f = in ? val.lg[t] : 0.f;
+            const bool md = in && val.modified(t);
+            if (__any_sync(0xffffffffu, md)) {
+              if (md) {
+                const double v = val.full(f, t);
+                dm = fmax(dm, v);
+                dg[g] = fmax(dg[g], v);
+              }
+            }
+            if (in && !md) {
+              fm = fmaxf(fm, f);
+              fg[g] = fmaxf(fg[g], f);
             }
           }
         }
-        m = pol_warp_max(m);
+        double m = pol_warp_max(fmax((double)fm, dm)) * inv_t;
+        if (!(m > -DBL_MAX)) m = -DBL_MAX;  // the running maximum starts at -MaxFloat64
+        double gm[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) gm[g] = fmax((double)fg[g], dg[g]) * inv_t;
 #pragma unroll
         for (int g = 0; g < 4; ++g) wsamp[warp][lane * 4 + g] = pol_dkey(gm[g]);
         __syncwarp();
@@ -745,7 +794,7 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 8) policy_row_kernel(const 
         for (int j = 0; j * 32 < V; ++j) {
           const int t = j * 32 + lane;
           const bool in = t < V;
-          const double x = in ? val(t) * inv_t : 0.0;
+          const double x = val.warp_value(t, in) * inv_t;
           if (in) s += exp(x - m);
           const bool take = in && x >= tau;
           if (in && !take) xo = fmax(xo, x);
@@ -932,7 +981,7 @@ int launch_policy(PolicyArgs& a, cudaStream_t s) {
   const bool small_k = draw && !index_draw && a.top_k > 0 && a.top_k < a.V && a.top_k <= kPolRowMaxK;
   const bool force_block = getenv("MC_POLICY_BLOCK") != nullptr;  // the CTA-per-row kernel for every knob
   if (!force_block && (!draw || index_draw || small_k)) {
-    const size_t smem = (size_t)kPolRowWarps * 2 * ((a.V + 31) / 32) * sizeof(uint32_t);  // <= 16 KB
+    const size_t smem = (size_t)kPolRowWarps * 3 * ((a.V + 31) / 32) * sizeof(uint32_t);  // <= 24 KB
     if (a.n_rows > 0) policy_row_kernel<<<(a.n_rows + kPolRowWarps - 1) / kPolRowWarps, kPolRowWarps * 32, smem, s>>>(a);
     MC_CUDA(cudaGetLastError());
     return kOk;
