@@ -573,16 +573,6 @@ __device__ __forceinline__ double pol_warp_max(double v) {
   return v;
 }
 
-// Order-preserving 64-bit key of a double (unsigned comparison of keys = comparison of values).
-__device__ __forceinline__ unsigned long long pol_dkey(double v) {
-  const unsigned long long u = (unsigned long long)__double_as_longlong(v);
-  return (u >> 63) ? ~u : (u | 0x8000000000000000ull);
-}
-
-__device__ __forceinline__ double pol_dkey_value(unsigned long long k) {
-  return __longlong_as_double((long long)((k >> 63) ? (k & 0x7fffffffffffffffull) : ~k));
-}
-
 struct PolRowValue {
   const float* lg;
   const uint32_t* ban;  // bitmap: the 3-gram block bans the token
@@ -625,7 +615,7 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
   __shared__ double cand_p[kPolRowWarps][kPolRowCand];
   __shared__ int cand_i[kPolRowWarps][kPolRowCand];
   __shared__ int whist[kPolRowWarps][256];
-  __shared__ unsigned long long wsamp[kPolRowWarps][kPolRowSamples];
+  __shared__ unsigned int wsamp[kPolRowWarps][kPolRowSamples];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kPolRowWarps + warp;
   const int V = a.V;
@@ -781,12 +771,16 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
         double gm[4];
 #pragma unroll
         for (int g = 0; g < 4; ++g) gm[g] = fmax((double)fg[g], dg[g]) * inv_t;
+        // the bound: the k-th largest of the group maxima rounded down to float (32-bit keys, four
+        // radix passes). At least k entries reach it (each such maximum is an entry >= its
+        // rounded-down value), which is all the candidate set needs.
 #pragma unroll
-        for (int g = 0; g < 4; ++g) wsamp[warp][lane * 4 + g] = pol_dkey(gm[g]);
+        for (int g = 0; g < 4; ++g) wsamp[warp][lane * 4 + g] = float_key(__double2float_rd(gm[g]));
         __syncwarp();
         int r_unused;
-        const double tau = pol_dkey_value(warp_radix_select<unsigned long long, 64>(
-            [&](int i) { return wsamp[warp][i]; }, kPolRowSamples, K, whist[warp], &r_unused));
+        const unsigned int tk = warp_radix_select<unsigned int, 32>([&](int i) { return wsamp[warp][i]; },
+                                                                     kPolRowSamples, K, whist[warp], &r_unused);
+        const double tau = (double)__uint_as_float((tk & 0x80000000u) ? (tk & 0x7fffffffu) : ~tk);
         // pass B: the sum of the exponentials; the entries with x >= tau in index order, and the
         // largest x below tau
         double s = 0.0, xo = -INFINITY;
