@@ -86,7 +86,7 @@ int copy_step_outputs(mc_batch* b, float* logits, int32_t* next, float* prob) {
   return sync_all(b);
 }
 
-int ensure_step_outputs(DevBatch& sh, bool logits, int stride) {
+int ensure_step_outputs(DevBatch& sh, bool logits, int stride, bool gmax = false) {
   int st;
   if (sh.out_stride < stride) {
     if ((st = sh.alloc(sh.out_tok, (size_t)sh.S * stride * 4)) || (st = sh.alloc(sh.out_prob, (size_t)sh.S * stride * 4)))
@@ -94,6 +94,7 @@ int ensure_step_outputs(DevBatch& sh, bool logits, int stride) {
     sh.out_stride = stride;
   }
   if (logits && !sh.logits && (st = sh.alloc(sh.logits, (size_t)sh.S * sh.m->V * 4))) return st;
+  if (gmax && !sh.gmax && (st = sh.alloc(sh.gmax, (size_t)sh.S * kSelSamples * 4))) return st;
   return kOk;
 }
 
@@ -384,7 +385,7 @@ int generate_impl(mc_batch* b, const int32_t* prompts, const int32_t* lens, int 
     if (sh.S == 0) continue;
     MC_CUDA(cudaSetDevice(sh.m->device));
     // the sampler (mode 1) and the policy (mode 3) select from materialised logits
-    if ((st = ensure_step_outputs(sh, mode == 3 || mode == 1, n_new)) != kOk) return st;
+    if ((st = ensure_step_outputs(sh, mode == 3 || mode == 1, n_new, mode == 1)) != kOk) return st;
     if (pol && (st = upload_policy(b, g, *pol, prompts, lens, stride)) != kOk) return st;
     MC_CUDA(cudaMemsetAsync(sh.step, 0, 4, sh.stream));
     sh.n_stops = n_stops;
@@ -448,7 +449,7 @@ int generate_dev_impl(mc_batch* b, const int32_t* d_prompts, const int32_t* d_le
   const double inv_t = mode ? 1.0 / temperature : 0.0;
   MC_CUDA(cudaSetDevice(sh.m->device));
   int st;
-  if ((st = ensure_step_outputs(sh, mode == 1, n_new)) != kOk) return st;  // the sampler selects from logits
+  if ((st = ensure_step_outputs(sh, mode == 1, n_new, mode == 1)) != kOk) return st;  // the sampler selects from logits
   prepare_prompts_kernel<<<(sh.S + 127) / 128, 128, 0, sh.stream>>>(d_prompts, d_lens, stride, sh.S, P, b->window, sh.tok,
                                                                       sh.seglen, sh.pos, sh.rowmap, sh.step, sh.next_tok);
   MC_CUDA(cudaGetLastError());

@@ -297,6 +297,7 @@ struct DevBatch {
   float *cur = nullptr, *blockin = nullptr, *xbuf = nullptr, *hbuf = nullptr, *qbuf = nullptr, *att = nullptr,
         *att_rowmax = nullptr, *fnorm = nullptr, *fnorm_rowmax = nullptr, *kvlin = nullptr, *logits = nullptr;
   float4* part = nullptr;
+  float* gmax = nullptr;  // sampling: [S][128] the head's 32-column group maxima of each row
   float* topv = nullptr;
   int32_t* topi = nullptr;
   unsigned long long* trace = nullptr;  // phase timestamps of CTA 0 per block-kernel launch (debug)
@@ -381,8 +382,6 @@ static int ensure_attrs(int device) {
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<2, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<3, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem));
-  MC_CUDA(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)(kSelectWarps * kLogitsSelectMaxV * sizeof(unsigned int))));
   MC_CUDA(cudaFuncSetAttribute(policy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)policy_smem(kPolicyMaxVocab)));
   MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
@@ -827,7 +826,14 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
 // by select_kernel, when the batch holds a logits buffer and the vocabulary fits the select's
 // shared memory (else from the head's per-partial top-k lists).
 static bool select_from_logits(const DevBatch& b, int mode) {
-  return mode == 1 && b.topk > 1 && b.logits != nullptr && b.m->V <= kLogitsSelectMaxV;
+  return mode == 1 && b.topk > 1 && b.logits != nullptr;
+}
+
+// The head's 32-column group maxima serve the select's bound when there are enough groups for
+// the top-k (4 per 128-column chunk, at most kSelSamples): their count, or 0.
+static int head_groups(const DevBatch& b) {
+  const int g = 4 * b.m->head.nchunks;
+  return b.gmax && g <= kSelSamples && (b.m->V + 31) / 32 > b.topk ? g : 0;
 }
 
 static int enqueue_head(DevBatch& b, int P, int mode, bool want_logits, int s0, int ns, size_t row0, LaunchLog* log) {
@@ -852,6 +858,10 @@ static int enqueue_head(DevBatch& b, int P, int mode, bool want_logits, int s0, 
   h.target = mode == 2 ? b.target + s0 : nullptr;
   h.logits_out = want_logits || mode == 3 || sel_logits ? b.logits + (size_t)s0 * m.V : nullptr;
   h.logits_only = mode == 3 ? 1 : 0;  // the policy kernel reads the logits, not the partials
+  if (sel_logits && head_groups(b) > 0) {
+    h.ngroups = head_groups(b);
+    h.gmax_out = b.gmax + (size_t)s0 * h.ngroups;
+  }
   const size_t np = (size_t)b.nsplit * 4;  // partials per session: splits x column quarters
   h.part = b.part + (size_t)s0 * np;
   h.topv = b.topv ? b.topv + (size_t)s0 * np * b.topk : nullptr;
@@ -895,13 +905,15 @@ static int enqueue_select(DevBatch& b, int mode, double inv_temp, uint32_t sessi
     sa.limit = b.limit ? b.limit + s0 : nullptr;
   }
   for (int k = 0; k < b.n_stops; ++k) sa.stops[k] = b.stops[k];
-  size_t smem = 0;
   if (select_from_logits(b, mode)) {
     sa.logits = b.logits + (size_t)s0 * b.m->V;
     sa.V = b.m->V;
-    smem = (size_t)kSelectWarps * b.m->V * sizeof(unsigned int);  // each warp's row keys
+    if (head_groups(b) > 0) {
+      sa.ngroups = head_groups(b);
+      sa.gmax = b.gmax + (size_t)s0 * sa.ngroups;
+    }
   }
-  select_kernel<<<(ns + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, smem, b.stream>>>(sa);
+  select_kernel<<<(ns + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, b.stream>>>(sa);
   MC_CUDA(cudaGetLastError());
   if (log) log->record(b.stream, 4);
   return kOk;

@@ -32,6 +32,8 @@ struct HeadArgs {
   const int32_t* target;   // [S] or null
   float* logits_out;       // [S][V] or null
   int logits_only;         // with logits_out: no partials (the policy kernel reads the logits only)
+  float* gmax_out;         // [S][ngroups] or null: the row's maximum over each 32-column piece
+  int ngroups;             // (column quarter h of chunk c is group 4c + h)
   float4* part;            // [S][nsplit]: max, sum, first argmax (bits), target logit
   float* topv;             // [S][nsplit][topk]
   int32_t* topi;
@@ -185,6 +187,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
       if (!got) ok = false;
       if (ok) {
         tc_fence_after();
+        float qm = -INFINITY;  // this thread's 32 columns of the chunk: one group maximum
         for (int j0 = h * 32; j0 < h * 32 + 32; j0 += 16) {
           uint32_t a1[16], a2[16], a3[16];
           load_acc16(tmem, warp, j0, a1, a2, a3);
@@ -205,6 +208,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
               cm = l16[j];
               ci2 = v0 + j;
             }
+          qm = fmaxf(qm, cm);
           if (cm > m) {
             sum = __fmul_rn(sum, expf(m - cm));
             m = cm;
@@ -230,6 +234,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             }
           }
         }
+        if (valid && a.gmax_out) a.gmax_out[(size_t)s * a.ngroups + 4 * c + h] = qm;
       }
       tc_fence_before();
       mbar_arrive(&bars->acc_empty);
@@ -264,11 +269,15 @@ struct SelectArgs {
   const int32_t* limit;            // [S] tokens a session may emit (it ends after the last), with gen_n
   const float* logits;             // [S][V] sampling: the top-k candidates come from the row's logits
   int V;                           // (null: from the head's per-partial top-k lists)
+  const float* gmax;               // [S][ngroups] the head's 32-column group maxima, or null
+  int ngroups;
 };
 
-// Sampling candidates from materialised logits: one warp per row, the row's order-preserving keys
-// staged in shared memory (kLogitsSelectMaxV per warp).
-constexpr int kLogitsSelectMaxV = 8192;
+// Sampling candidates from materialised logits, one warp per row (no per-row array in shared
+// memory): the k-th largest of up to 128 group maxima bounds the top k from below, the entries at
+// or above it (at most kSelCand; else an exact radix select over the whole row) are ranked exactly.
+constexpr int kSelCand = 128;
+constexpr int kSelSamples = 128;
 
 // Order-preserving key of a float: unsigned comparison of keys = float comparison of values.
 __device__ __forceinline__ unsigned int float_key(float v) {
@@ -365,10 +374,10 @@ constexpr int kSelectWarps = 4;
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
 __global__ void __launch_bounds__(kSelectWarps * 32) select_kernel(const SelectArgs a) {
-  __shared__ float cand_v[kSelectWarps][kMaxTopK];
-  __shared__ int cand_i[kSelectWarps][kMaxTopK];
+  __shared__ float cand_v[kSelectWarps][kSelCand];
+  __shared__ int cand_i[kSelectWarps][kSelCand];
   __shared__ int sel_hist[kSelectWarps][256];
-  extern __shared__ unsigned int sel_keys[];  // [kSelectWarps][V] with a.logits (sampling)
+  __shared__ unsigned int sel_samp[kSelectWarps][kSelSamples];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int s = blockIdx.x * kSelectWarps + warp;
   const int step = a.step ? *a.step : 0;
@@ -398,50 +407,89 @@ __global__ void __launch_bounds__(kSelectWarps * 32) select_kernel(const SelectA
     }
     int tok = idx;
     if (a.mode == 1 && a.topk > 1 && a.logits) {
-      // The top-k of the row's logits in (value descending, index ascending) order: the k-th
-      // largest key by radix select, then the entries above it and the first of those equal to it
-      // in index order, ranked exactly.
-      unsigned int* keys = sel_keys + (size_t)warp * a.V;
+      // The top-k of the row's logits in (value descending, index ascending) order, compared as
+      // order-preserving keys. The bound: the k-th largest of the group maxima (the head's, or
+      // those of the groups (lane, g) = entries 32j + lane with j % 4 == g); at least k entries
+      // reach it, and an entry below it ranks behind them all.
       const float* lg = a.logits + (size_t)s * a.V;
-      for (int i = lane; i < a.V; i += 32) keys[i] = float_key(lg[i]);
+      const int V = a.V;
+      const int K = min(a.topk, V);
+      unsigned int* samp = sel_samp[warp];
+      int ns = kSelSamples;
+      if (a.gmax) {
+        ns = a.ngroups;
+        for (int i = lane; i < ns; i += 32) samp[i] = float_key(a.gmax[(size_t)s * a.ngroups + i]);
+      } else {
+        float gm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        for (int j0 = 0; j0 * 32 < V; j0 += 4) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int t = (j0 + g) * 32 + lane;
+            if (t < V) gm[g] = fmaxf(gm[g], lg[t]);
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) samp[lane * 4 + g] = float_key(gm[g]);
+      }
       __syncwarp();
-      const int K = min(a.topk, a.V);
       int r_eq = 0;
-      const unsigned int tau =
-          warp_radix_select<unsigned int, 32>([&](int i) { return keys[i]; }, a.V, K, sel_hist[warp], &r_eq);
-      int have = 0, eq_seen = 0;
-      for (int base = 0; base < a.V; base += 32) {
+      unsigned int tk = 0u;  // K >= V: every entry is a candidate
+      if (K < V) tk = warp_radix_select<unsigned int, 32>([&](int i) { return samp[i]; }, ns, K, sel_hist[warp], &r_eq);
+      int C = 0;
+      for (int base = 0; base < V; base += 32) {
         const int i = base + lane;
-        const unsigned int kb = i < a.V ? keys[i] : 0u;
-        const bool eq = i < a.V && kb == tau;
-        const unsigned int eqm = __ballot_sync(0xffffffffu, eq);
-        const bool take = (i < a.V && kb > tau) || (eq && eq_seen + __popc(eqm & ((1u << lane) - 1u)) < r_eq);
+        const float l = i < V ? lg[i] : 0.f;
+        const bool take = i < V && float_key(l) >= tk;
         const unsigned int tm = __ballot_sync(0xffffffffu, take);
         if (take) {
-          const int at = have + __popc(tm & ((1u << lane) - 1u));
-          cand_v[warp][at] = lg[i];
-          cand_i[warp][at] = i;
+          const int at = C + __popc(tm & ((1u << lane) - 1u));
+          if (at < kSelCand) {
+            cand_v[warp][at] = l;
+            cand_i[warp][at] = i;
+          }
         }
-        have += __popc(tm);
-        eq_seen += __popc(eqm);
+        C += __popc(tm);
+      }
+      if (C > kSelCand) {
+        // keys tied at the bound past the room: exactly the top k by a radix select over the row
+        const unsigned int tau = warp_radix_select<unsigned int, 32>([&](int i) { return float_key(lg[i]); }, V, K,
+                                                                     sel_hist[warp], &r_eq);
+        int have = 0, eq_seen = 0;
+        for (int base = 0; base < V; base += 32) {
+          const int i = base + lane;
+          const float l = i < V ? lg[i] : 0.f;
+          const unsigned int kb = i < V ? float_key(l) : 0u;
+          const bool eq = i < V && kb == tau;
+          const unsigned int eqm = __ballot_sync(0xffffffffu, eq);
+          const bool take = (i < V && kb > tau) || (eq && eq_seen + __popc(eqm & ((1u << lane) - 1u)) < r_eq);
+          const unsigned int tm = __ballot_sync(0xffffffffu, take);
+          if (take) {
+            const int at = have + __popc(tm & ((1u << lane) - 1u));
+            cand_v[warp][at] = l;
+            cand_i[warp][at] = i;
+          }
+          have += __popc(tm);
+          eq_seen += __popc(eqm);
+        }
+        C = K;
       }
       __syncwarp();
       // rank of each candidate: those before it in (value descending, index ascending) order
-      float rv[2];
-      int ri[2], rk[2];
+      float rv[kSelCand / 32];
+      int ri[kSelCand / 32], rk[kSelCand / 32];
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+      for (int q = 0; q < kSelCand / 32; ++q) {
         const int c = lane + 32 * q;
-        rv[q] = c < K ? cand_v[warp][c] : 0.f;
-        ri[q] = c < K ? cand_i[warp][c] : 0;
+        rv[q] = c < C ? cand_v[warp][c] : 0.f;
+        ri[q] = c < C ? cand_i[warp][c] : 0;
         rk[q] = 0;
-        if (c < K)
-          for (int j = 0; j < K; ++j) rk[q] += better(cand_v[warp][j], cand_i[warp][j], rv[q], ri[q]) ? 1 : 0;
+        if (c < C)
+          for (int j = 0; j < C; ++j) rk[q] += better(cand_v[warp][j], cand_i[warp][j], rv[q], ri[q]) ? 1 : 0;
       }
       __syncwarp();
 #pragma unroll
-      for (int q = 0; q < 2; ++q)
-        if (lane + 32 * q < K) {
+      for (int q = 0; q < kSelCand / 32; ++q)
+        if (lane + 32 * q < C && rk[q] < K) {
           cand_v[warp][rk[q]] = rv[q];
           cand_i[warp][rk[q]] = ri[q];
         }
