@@ -125,7 +125,10 @@ class Context:
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (AttributeError, TypeError):  # interpreter shutdown: the module globals are gone
+            pass
 
 
 _default_ctx: Optional[Context] = None
@@ -177,7 +180,10 @@ class Model:
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (AttributeError, TypeError):  # interpreter shutdown: the module globals are gone
+            pass
 
     def vocab_size(self) -> int:
         return self.vocab
@@ -226,7 +232,10 @@ class SessionBatch:
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (AttributeError, TypeError):  # interpreter shutdown: the module globals are gone
+            pass
 
     def prefill(self, prompts, lens, want_logits: bool = False):
         p = np.ascontiguousarray(prompts, np.int32)
@@ -363,7 +372,10 @@ class Scheduler:
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (AttributeError, TypeError):  # interpreter shutdown: the module globals are gone
+            pass
 
     def submit(self, prompt: Sequence[int], n_new: int, draw_key: Optional[int] = None) -> int:
         """Queues a request; returns its id."""

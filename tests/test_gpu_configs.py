@@ -74,6 +74,37 @@ def test_config3_sampled_limits_full_vocab(oracle):
     assert diverged <= n // 4, diverged
 
 
+@pytest.mark.parametrize("levels", [5, 1], ids=["five levels", "one level"])
+def test_sampling_ties_at_the_bound(oracle, levels):
+    """Logits that tie in blocks of hundreds: a model whose tied embedding is zero, so every logit
+    is its head bias, here (v mod levels). More than 128 entries then reach the select's bound, so
+    it takes its exact radix select over the whole row. The top 40 are the lowest indices of the
+    top level, and every sampled stream equals the oracle's (T 0.8, vocabulary 4096)."""
+    spec = synth.ModelSpec(vocab=4096, state=128, hidden=256, blocks=1, steps=1, attn_heads=4, attn_window=64)
+    qm = synth.build_model(spec)
+    qm.embed = synth.QTensor(np.zeros_like(qm.embed.data), qm.embed.scale)
+    qm.head_b = (np.arange(spec.vocab) % levels).astype(np.float32)
+    data = synth.encode_model(qm)
+    om, gm = oracle.Model(data), quant.Model.decode(data)
+    n, n_new, T, K = 24, 6, 0.8, 40
+    prompts = synth.prompts_uniform_fast(n, 16, spec.vocab, seed=8)
+    lens = np.full(n, 16, np.int32)
+    wt, wl = om.generate_sample(prompts, lens, n_new, T, K, session0=0, logits=True)
+    b = gm.new_batch(n, 0, 16, top_k=K)
+    gt, _ = b.generate(prompts, lens, n_new, temperature=T)
+    b.close()
+    gm.close()
+    top = levels - 1
+    assert np.all(gt % levels == top), "a token outside the top level"
+    for s in range(n):
+        diff = np.nonzero(gt[s] != wt[s])[0]
+        if diff.size == 0:
+            continue
+        t = int(diff[0])
+        m = _cdf_margin(wl[s, t], T, K, synth.sample_uniform(s, t))
+        assert m < 5e-3, f"session {s} step {t}: {gt[s, t]} != {wt[s, t]} with the draw {m:.3g} from a bucket edge"
+
+
 WINDOWED = [("dh32 window 16", 128, 4, 16), ("dh48 window 24", 192, 4, 24), ("dh64 window 20", 128, 2, 20)]
 
 
