@@ -1142,6 +1142,10 @@ def main():
     achieved = attn_bytes / (attn_ms / 1000.0) / 1e9
     step_ms = sum(ms_arr[:n])
     shares = {names.get(k, str(k)): round(sum(v) / step_ms, 4) for k, v in per_kind.items()}
+    # whole-step algorithmic bytes (HBM), as for the config-3 line: per attention block the K/V
+    # windows read, q and o, the new key/value written, and the rule state (norm ring read and
+    # written, latch read and written); the four blocks of config 2 all carry attention
+    step_bytes = S * 4 * (2 * span * D * 4 + 2 * D * 4 + 2 * (2 + 1) * D * 4 * 2)
 
     # prefill: prompt preparation, 4 x (block + attention), final block, head, select; decode steps:
     # 4 x (block + attention) and the final block with the greedy head fused in
@@ -1179,7 +1183,9 @@ def main():
                               "decode_steps_ms_estimate": float(step_ms) * (NEW - 1),
                               "note": "prefill: device time of one mc_prefill of the job's prompts (host "
                                       "staging included); decode: 79 x the step profiled below"},
-            "decode_step_profile": {"ms_total": float(step_ms), "share": shares,
+            "decode_step_profile": {"ms_total": float(step_ms),
+                                    "hbm_frac_whole_step": step_bytes / (float(step_ms) / 1000.0) / 1e9 / hbm_peak,
+                                    "whole_step_algorithmic_bytes": int(step_bytes), "share": shares,
                                     "ms_per_kind": {names.get(k, str(k)): float(np.mean(v)) for k, v in per_kind.items()}},
             "cpu_baseline": cpu,
             "parity": parity,
