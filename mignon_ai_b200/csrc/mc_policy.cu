@@ -545,15 +545,15 @@ __global__ void __launch_bounds__(kPolicyThreads) policy_kernel(const __grid_con
 // kPolRowMaxK. The warp streams its row's logits from global memory (L2-resident after the
 // head) once per pass and recomputes each value the same way every time:
 //   v(t) = logit, then -MaxFloat64 if the 3-gram block bans t, -1e300 if the automaton masks t,
-//   then the repetition penalty if t is in the window (sample.go:48-69, 213-231), with the bans
-//   and the penalty window as two bitmaps of the vocabulary in shared memory.
+//   then the repetition penalty if t is in the window (sample.go:48-69, 213-231), with the bans,
+//   the penalty window and their union as bitmaps of the vocabulary in shared memory.
 // Top-k, exactly: the probabilities p = exp(x - max) / sum are non-decreasing in x = v / T. Pass A
-// takes the max and 128 group maxima of x; the k-th largest group maximum tau bounds the k-th
-// largest x from below, so the entries with x >= tau (pass B, which also sums the exponentials)
-// hold the top k unless an entry below tau has a probability equal to the k-th (rounding or
-// underflow ties). Their exact probabilities are ranked by (p descending, index ascending); if
-// the largest probability below tau is not clearly smaller than the k-th, or more than
-// kPolRowCand entries reach tau, a 64-bit radix select over the probabilities' bit patterns
+// takes the max and 128 group maxima of x; the k-th largest group maximum rounded down to float,
+// tau, bounds the k-th largest x from below, so the entries with x >= tau (pass B, which also sums
+// the exponentials) hold the top k unless an entry below tau has a probability equal to the k-th
+// (rounding or underflow ties). Their exact probabilities are ranked by (p descending, index
+// ascending); if the largest probability below tau is not clearly smaller than the k-th, or more
+// than kPolRowCand entries reach tau, a 64-bit radix select over the probabilities' bit patterns
 // (recomputed per pass) takes exactly the top k instead. Top-p and the draw then run over the k
 // sorted candidates in sequence, like sample.go:152-191.
 constexpr int kPolRowWarps = 4;
