@@ -131,12 +131,15 @@ def test_sliding_window_attention_matches_oracle(oracle, case):
     gm.close()
 
 
-def test_prefill_passes_match_one_pass(monkeypatch):
+@pytest.mark.parametrize("vocab", [512, 2048])
+def test_prefill_passes_match_one_pass(monkeypatch, vocab):
     """A batch whose prefill needs more scratch than MC_PREFILL_SCRATCH_MB allows runs each prefill
     in passes over contiguous sessions (layers, head and selection per pass). The kernels are the
     same, so greedy and sampled generation, prefill logits and scoring are bit-identical to a
-    batch that holds the whole prefill at once. Ragged and idle sessions included."""
-    spec = synth.ModelSpec(**{**synth.CONFIGS[2].__dict__, "vocab": 512})
+    batch that holds the whole prefill at once. Ragged and idle sessions included. At vocabulary
+    2048 the sampled selection takes its bound from the head's group maxima (64 groups of 32
+    columns), offset per pass like the logits; at 512 it computes them itself."""
+    spec = synth.ModelSpec(**{**synth.CONFIGS[2].__dict__, "vocab": vocab})
     gm = quant.Model.decode(synth.build_model_file(spec))
     n = 300
     prompts = synth.prompts_uniform_fast(n, 48, spec.vocab, seed=41)
