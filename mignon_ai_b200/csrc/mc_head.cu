@@ -436,19 +436,27 @@ __global__ void __launch_bounds__(kSelectWarps * 32) select_kernel(const SelectA
       unsigned int tk = 0u;  // K >= V: every entry is a candidate
       if (K < V) tk = warp_radix_select<unsigned int, 32>([&](int i) { return samp[i]; }, ns, K, sel_hist[warp], &r_eq);
       int C = 0;
-      for (int base = 0; base < V; base += 32) {
-        const int i = base + lane;
-        const float l = i < V ? lg[i] : 0.f;
-        const bool take = i < V && float_key(l) >= tk;
-        const unsigned int tm = __ballot_sync(0xffffffffu, take);
-        if (take) {
-          const int at = C + __popc(tm & ((1u << lane) - 1u));
-          if (at < kSelCand) {
-            cand_v[warp][at] = l;
-            cand_i[warp][at] = i;
-          }
+      for (int b0 = 0; b0 < V; b0 += 256) {
+        float lv[8];  // eight loads in flight before any is used
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = b0 + 32 * u + lane;
+          lv[u] = i < V ? lg[i] : 0.f;
         }
-        C += __popc(tm);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = b0 + 32 * u + lane;
+          const bool take = i < V && float_key(lv[u]) >= tk;
+          const unsigned int tm = __ballot_sync(0xffffffffu, take);
+          if (take) {
+            const int at = C + __popc(tm & ((1u << lane) - 1u));
+            if (at < kSelCand) {
+              cand_v[warp][at] = lv[u];
+              cand_i[warp][at] = i;
+            }
+          }
+          C += __popc(tm);
+        }
       }
       if (C > kSelCand) {
         // keys tied at the bound past the room: exactly the top k by a radix select over the row

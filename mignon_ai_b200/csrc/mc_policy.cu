@@ -785,22 +785,36 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
         // largest x below tau
         double s = 0.0, xo = -INFINITY;
         int C = 0;
-        for (int j = 0; j * 32 < V; ++j) {
-          const int t = j * 32 + lane;
-          const bool in = t < V;
-          const double x = val.warp_value(t, in) * inv_t;
-          if (in) s += exp(x - m);
-          const bool take = in && x >= tau;
-          if (in && !take) xo = fmax(xo, x);
-          const unsigned int tm = __ballot_sync(0xffffffffu, take);
-          if (take) {
-            const int at = C + __popc(tm & ((1u << lane) - 1u));
-            if (at < kPolRowCand) {
-              cp[at] = x;
-              ci[at] = t;
-            }
+        for (int j0 = 0; j0 * 32 < V; j0 += 4) {
+          float f[4];  // four loads in flight before any is used
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int t = (j0 + g) * 32 + lane;
+            f[g] = t < V ? val.lg[t] : 0.f;
           }
-          C += __popc(tm);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int t = (j0 + g) * 32 + lane;
+            const bool in = t < V;
+            const bool md = in && val.modified(t);
+            double v = (double)f[g];
+            if (__any_sync(0xffffffffu, md)) {
+              if (md) v = val.full(f[g], t);
+            }
+            const double x = v * inv_t;
+            if (in) s += exp(x - m);
+            const bool take = in && x >= tau;
+            if (in && !take) xo = fmax(xo, x);
+            const unsigned int tm = __ballot_sync(0xffffffffu, take);
+            if (take) {
+              const int at = C + __popc(tm & ((1u << lane) - 1u));
+              if (at < kPolRowCand) {
+                cp[at] = x;
+                ci[at] = t;
+              }
+            }
+            C += __popc(tm);
+          }
         }
         s = pol_warp_sum(s);
         xo = pol_warp_max(xo);
