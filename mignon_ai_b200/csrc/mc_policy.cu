@@ -597,16 +597,26 @@ struct PolRowValue {
     const float f = lg[t];
     return modified(t) ? full(f, t) : (double)f;
   }
-  // The value of token t (t < V when in), every lane of the warp calling: the rare modified
-  // tokens take the full path under a warp-uniform branch.
-  __device__ __forceinline__ double warp_value(int t, bool in) const {
-    const float f = in ? lg[t] : 0.f;
-    const bool m = in && modified(t);
-    double v = (double)f;
-    if (__any_sync(0xffffffffu, m)) {
-      if (m) v = full(f, t);
+  // The values of tokens 32 (j0 + g) + lane, g < 4 (0 past V), every lane of the warp calling:
+  // the four loads are issued before any is used, and the rare modified tokens take the full
+  // path under a warp-uniform branch.
+  __device__ __forceinline__ void warp_values4(int j0, int V, double (&v)[4]) const {
+    const int lane = threadIdx.x & 31;
+    float f[4];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int t = (j0 + g) * 32 + lane;
+      f[g] = t < V ? lg[t] : 0.f;
     }
-    return v;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int t = (j0 + g) * 32 + lane;
+      const bool m = t < V && modified(t);
+      v[g] = (double)f[g];
+      if (__any_sync(0xffffffffu, m)) {
+        if (m) v[g] = full(f[g], t);
+      }
+    }
   }
 };
 
@@ -668,10 +678,14 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
       // 3b. argmax; prob = 1 / sum exp(v - max)
       double bv = -INFINITY;
       int bi = 0x7fffffff;
-      for (int j = 0; j * 32 < V; ++j) {
-        const int t = j * 32 + lane;
-        const double v = val.warp_value(t, t < V);
-        if (t < V && pol_better(v, t, bv, bi)) bv = v, bi = t;
+      for (int j0 = 0; j0 * 32 < V; j0 += 4) {
+        double v[4];
+        val.warp_values4(j0, V, v);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int t = (j0 + g) * 32 + lane;
+          if (t < V && pol_better(v[g], t, bv, bi)) bv = v[g], bi = t;
+        }
       }
 #pragma unroll
       for (int o = 16; o; o >>= 1) {
@@ -680,10 +694,12 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
         if (pol_better(ov, oi, bv, bi)) bv = ov, bi = oi;
       }
       double s = 0.0;
-      for (int j = 0; j * 32 < V; ++j) {
-        const int t = j * 32 + lane;
-        const double v = val.warp_value(t, t < V);
-        if (t < V) s += exp(v - bv);
+      for (int j0 = 0; j0 * 32 < V; j0 += 4) {
+        double v[4];
+        val.warp_values4(j0, V, v);
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          if ((j0 + g) * 32 + lane < V) s += exp(v[g] - bv);
       }
       s = pol_warp_sum(s);
       tok = bi;
@@ -695,10 +711,14 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
         // 3d. the draw in index order: lane l owns the chunk [l*c, (l+1)*c); running sums from
         // the exclusive scan of the chunk totals
         double m = -DBL_MAX;
-        for (int j = 0; j * 32 < V; ++j) {
-          const int t = j * 32 + lane;
-          const double x = val.warp_value(t, t < V) * inv_t;
-          if (t < V) m = x > m ? x : m;
+        for (int j0 = 0; j0 * 32 < V; j0 += 4) {
+          double v[4];
+          val.warp_values4(j0, V, v);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const double x = v[g] * inv_t;
+            if ((j0 + g) * 32 + lane < V) m = x > m ? x : m;
+          }
         }
         m = pol_warp_max(m);
         const int c = (V + 31) / 32;
@@ -786,22 +806,13 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
         double s = 0.0, xo = -INFINITY;
         int C = 0;
         for (int j0 = 0; j0 * 32 < V; j0 += 4) {
-          float f[4];  // four loads in flight before any is used
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int t = (j0 + g) * 32 + lane;
-            f[g] = t < V ? val.lg[t] : 0.f;
-          }
+          double v[4];
+          val.warp_values4(j0, V, v);
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
             const int t = (j0 + g) * 32 + lane;
             const bool in = t < V;
-            const bool md = in && val.modified(t);
-            double v = (double)f[g];
-            if (__any_sync(0xffffffffu, md)) {
-              if (md) v = val.full(f[g], t);
-            }
-            const double x = v * inv_t;
+            const double x = v[g] * inv_t;
             if (in) s += exp(x - m);
             const bool take = in && x >= tau;
             if (in && !take) xo = fmax(xo, x);
