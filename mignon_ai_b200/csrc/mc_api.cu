@@ -396,8 +396,12 @@ int generate_impl(mc_batch* b, const int32_t* prompts, const int32_t* lens, int 
     }
     if (limits && (st = begin_limits(sh, limits + b->first[g], cudaMemcpyHostToDevice)) != kOk) return st;
     const uint32_t s0 = session0 + (uint32_t)b->first[g];
-    st = enqueue_forward(sh, P, mode, inv_t, s0, false, true);
-    if (st == kOk) st = run_decode_steps(sh, n_new, mode, inv_t, s0);
+    if (tiny_job_ok(sh, mode, n_stops, limits != nullptr, pol != nullptr)) {
+      st = launch_tiny_job(sh, P, n_new);  // the whole job in one launch
+    } else {
+      st = enqueue_forward(sh, P, mode, inv_t, s0, false, true);
+      if (st == kOk) st = run_decode_steps(sh, n_new, mode, inv_t, s0);
+    }
     sh.n_stops = 0;  // only this job's launches carry the stop tokens, the policy and the limits
     sh.pol = DevBatch::Policy();
     sh.per_session = false;
@@ -454,8 +458,12 @@ int generate_dev_impl(mc_batch* b, const int32_t* d_prompts, const int32_t* d_le
                                                                       sh.seglen, sh.pos, sh.rowmap, sh.step, sh.next_tok);
   MC_CUDA(cudaGetLastError());
   if (d_limits && (st = begin_limits(sh, d_limits, cudaMemcpyDeviceToDevice)) != kOk) return st;
-  st = enqueue_forward(sh, P, mode, inv_t, session0, false, true);
-  if (st == kOk) st = run_decode_steps(sh, n_new, mode, inv_t, session0);
+  if (tiny_job_ok(sh, mode, 0, d_limits != nullptr, false)) {
+    st = launch_tiny_job(sh, P, n_new);  // the whole job in one launch
+  } else {
+    st = enqueue_forward(sh, P, mode, inv_t, session0, false, true);
+    if (st == kOk) st = run_decode_steps(sh, n_new, mode, inv_t, session0);
+  }
   sh.per_session = false;
   if (st != kOk) return st;
   MC_CUDA(cudaMemcpy2DAsync(d_out_tokens, (size_t)n_new * 4, sh.out_tok, (size_t)sh.out_stride * 4, (size_t)n_new * 4, sh.S,

@@ -114,6 +114,11 @@ struct DevModel {
   DevGemm head;
   float *head_b = nullptr, *final_gain = nullptr, *latch_base = nullptr;
   std::vector<DevBlock> blocks;
+  // small models without attention: every block's int8 rows for tiny_generate_kernel
+  bool tiny = false;
+  uint32_t* tiny_w = nullptr;
+  int tiny_blk_words = 0;
+  size_t tiny_smem = 0;
   std::vector<void*> allocs;
   ~DevModel() {
     int prev = 0;
@@ -242,6 +247,30 @@ int build_dev_model(const HostModel& hm, int device, std::unique_ptr<DevModel>& 
   m->dec_smem = m->dec_r == 16 ? smem16 : smem32;
   m->dec_ok = m->dec_smem <= kDecodeSmemMax;
   if (nattn > 0 && m->cache > 128) return set_error(kUnsupported, "attention caches above 128 positions");
+  // Small models without attention also keep their blocks' int8 rows for tiny_generate_kernel:
+  // per block W_select, W1 and W2 row-major, each row padded to an odd number of words.
+  const int nb = (int)hm.blocks.size();
+  if (nattn == 0 && m->tied && nb >= 1 && nb <= kTinyMaxBlocks && D <= kTinyMaxD && D % 16 == 0 && H % 4 == 0 &&
+      tiny_smem_bytes(D, H, V, nb, total, m->ring) <= kTinySmemMax) {
+    const int bw = tiny_block_words(D, H);
+    std::vector<uint32_t> img((size_t)nb * bw, 0u);
+    auto put_rows = [&](uint32_t* dst, const std::vector<int8_t>& w, int rows, int k) {
+      const int kw = tiny_stride_words(k);
+      for (int r = 0; r < rows; ++r) memcpy(dst + (size_t)r * kw, w.data() + (size_t)r * k, (size_t)k);
+      return dst + (size_t)rows * kw;
+    };
+    for (int bi = 0; bi < nb; ++bi) {
+      const HostBlock& hb = hm.blocks[bi];
+      uint32_t* p = img.data() + (size_t)bi * bw;
+      p = put_rows(p, hb.wsel.data, D, D);
+      p = put_rows(p, hb.w1.data, 2 * H, 3 * D);
+      put_rows(p, hb.w2.data, 2 * D, H);
+    }
+    if ((st = m->upload(m->tiny_w, img.data(), img.size() * 4)) != kOk) return st;
+    m->tiny_blk_words = bw;
+    m->tiny_smem = tiny_smem_bytes(D, H, V, nb, total, m->ring);
+    m->tiny = true;
+  }
   out = std::move(m);
   return kOk;
 }
@@ -382,6 +411,7 @@ static int ensure_attrs(int device) {
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<2, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(block_decode_kernel<3, 16, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemMax));
   MC_CUDA(cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem));
+  MC_CUDA(cudaFuncSetAttribute(tiny_generate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTinySmemMax));
   MC_CUDA(cudaFuncSetAttribute(policy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)policy_smem(kPolicyMaxVocab)));
   MC_CUDA(cudaFuncSetAttribute(attn_decode_staged_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAsSmemMax));
@@ -916,6 +946,67 @@ static int enqueue_select(DevBatch& b, int mode, double inv_temp, uint32_t sessi
   select_kernel<<<(ns + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, b.stream>>>(sa);
   MC_CUDA(cudaGetLastError());
   if (log) log->record(b.stream, 4);
+  return kOk;
+}
+
+// A greedy job (the prompts of upload_prompts / prepare_prompts_kernel, then n_new tokens) on
+// tiny_generate_kernel, when the batch's model has its tiny weights and the job is plain greedy
+// decoding of a batch of at most two CTAs per multiprocessor (MC_TINY_OFF=1: the batched kernels).
+bool tiny_job_ok(const DevBatch& b, int mode, int n_stops, bool limits, bool policy) {
+  return b.m->tiny && mode == 0 && n_stops == 0 && !limits && !policy && b.S <= 2 * b.n_sm && !getenv("MC_TINY_OFF");
+}
+
+int launch_tiny_job(DevBatch& b, int P, int n_new) {
+  const DevModel& m = *b.m;
+  TinyArgs a;
+  memset(&a, 0, sizeof(a));
+  a.S = b.S;
+  a.D = m.D;
+  a.H = m.H;
+  a.V = m.V;
+  a.nblocks = (int)m.blocks.size();
+  a.total_steps = m.total_steps;
+  a.ring = m.ring;
+  a.P = P;
+  a.n_new = n_new;
+  a.out_stride = b.out_stride;
+  a.kw_sel = tiny_stride_words(m.D);
+  a.kw1 = tiny_stride_words(3 * m.D);
+  a.kw2 = tiny_stride_words(m.H);
+  a.blk_words = m.tiny_blk_words;
+  a.embed = m.embed;
+  a.embed_scale = m.embed_scale;
+  a.head_scale = m.head.scale;
+  a.head_b = m.head_b;
+  a.final_gain = m.final_gain;
+  a.latch_base = m.latch_base;
+  a.tok = b.tok;
+  a.seglen = b.seglen;
+  a.pos = b.pos;
+  a.next_tok = b.next_tok;
+  a.step = b.step;
+  a.latch = b.latch;
+  a.norm_ring = b.norm_ring;
+  a.out_tok = b.out_tok;
+  a.out_prob = b.out_prob;
+  int bs = 0;
+  for (int bi = 0; bi < a.nblocks; ++bi) {
+    const DevBlock& blk = m.blocks[bi];
+    TinyBlock& t = a.blk[bi];
+    t.w = m.tiny_w + (size_t)bi * m.tiny_blk_words;
+    t.s_sel = blk.wsel.scale;
+    t.s1 = blk.w1.scale;
+    t.s2 = blk.w2.scale;
+    t.b1 = blk.b1;
+    t.b2 = blk.b2;
+    t.gamma = blk.gamma;
+    t.steps = blk.steps;
+    t.bs0 = bs;
+    for (int st = 0; st < blk.steps; ++st) t.dil[st] = blk.dil[st];
+    bs += blk.steps;
+  }
+  tiny_generate_kernel<<<b.S, kTinyThreads, m.tiny_smem, b.stream>>>(a);
+  MC_CUDA(cudaGetLastError());
   return kOk;
 }
 
