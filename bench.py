@@ -919,8 +919,9 @@ def run_tiny(args):
                     lens.nbytes, "d2h_bytes_per_step": h_t.nbytes + h_pr.nbytes, "timing": "host wall clock per call"},
             "roofline": {"bound": "tensor (int8)", "achieved": achieved, "peak": peak["tops"], "unit": "TOPS",
                          "frac": achieved / peak["tops"], "peak_source": "mc_probe_mma_i8 on this GPU, this run",
-                         "note": "64 sessions fill one 128-row tile: each decode step is a chain of 3 launches whose "
-                                 "latency, not the tensor pipe, sets the time"},
+                         "note": "algorithmic int8 ops against the tensor-pipe peak; the job runs as one launch of "
+                                 "tiny_generate_kernel (one CTA per session, weights in shared memory, digit-plane dot "
+                                 "products on dp4a), bound by each session's chain of dependent steps"},
             "matches_value_run": bool(np.array_equal(h_t, d_t.cpu().numpy()))}
     if not args.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))

@@ -199,9 +199,10 @@ __global__ void __launch_bounds__(kTinyThreads, 1) tiny_generate_kernel(const __
         norm_slice(B.gamma, sNrm);
         // lambda = sigmoid(W_select n s_sel + base)
         for (int r = tid; r < D; r += kTinyThreads) {
+          const float base_r = a.latch_base[r];
           int x1, x2, x3;
           tiny_dot(wsel + (size_t)r * a.kw_sel, sPl, kwp, D / 4, x1, x2, x3);
-          sLam[r] = sigmoid_clamped(__fadd_rn(dequant(x1, x2, x3, s_step, B.s_sel), a.latch_base[r]));
+          sLam[r] = sigmoid_clamped(__fadd_rn(dequant(x1, x2, x3, s_step, B.s_sel), base_r));
         }
         __syncthreads();
         // latch update, ring write, and x = [n | n(pos - dil) | latch] sliced for W1
@@ -237,11 +238,12 @@ __global__ void __launch_bounds__(kTinyThreads, 1) tiny_generate_kernel(const __
         }
         // hidden = (W1v x s1 + b1v) * sigmoid(W1g x s1 + b1g)
         for (int h = tid; h < H; h += kTinyThreads) {
+          const float bv = B.b1[h], bg = B.b1[H + h];
           int v1, v2, v3, g1, g2, g3;
           tiny_dot(w1 + (size_t)h * a.kw1, sPl, kwp, 3 * D / 4, v1, v2, v3);
           tiny_dot(w1 + (size_t)(H + h) * a.kw1, sPl, kwp, 3 * D / 4, g1, g2, g3);
-          const float hv = __fadd_rn(dequant(v1, v2, v3, s_step, B.s1), B.b1[h]);
-          const float gt = __fadd_rn(dequant(g1, g2, g3, s_step, B.s1), B.b1[H + h]);
+          const float hv = __fadd_rn(dequant(v1, v2, v3, s_step, B.s1), bv);
+          const float gt = __fadd_rn(dequant(g1, g2, g3, s_step, B.s1), bg);
           sHid[h] = __fmul_rn(hv, sigmoid_clamped(gt));
         }
         __syncthreads();
@@ -257,11 +259,12 @@ __global__ void __launch_bounds__(kTinyThreads, 1) tiny_generate_kernel(const __
         __syncthreads();
         // o = W2 hidden s2 + b2; gate = sigmoid(o_gate); cur = (1 - gate) cur + gate o_delta
         for (int d = tid; d < D; d += kTinyThreads) {
+          const float bd = B.b2[d], bg = B.b2[D + d];
           int v1, v2, v3, g1, g2, g3;
           tiny_dot(w2 + (size_t)d * a.kw2, sPl, kwp, H / 4, v1, v2, v3);
           tiny_dot(w2 + (size_t)(D + d) * a.kw2, sPl, kwp, H / 4, g1, g2, g3);
-          const float od = __fadd_rn(dequant(v1, v2, v3, s_step, B.s2), B.b2[d]);
-          const float og = __fadd_rn(dequant(g1, g2, g3, s_step, B.s2), B.b2[D + d]);
+          const float od = __fadd_rn(dequant(v1, v2, v3, s_step, B.s2), bd);
+          const float og = __fadd_rn(dequant(g1, g2, g3, s_step, B.s2), bg);
           const float gate = sigmoid_clamped(og);
           sCur[d] = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, gate), sCur[d]), __fmul_rn(gate, od));
         }
@@ -277,6 +280,7 @@ __global__ void __launch_bounds__(kTinyThreads, 1) tiny_generate_kernel(const __
     float bv = -INFINITY;
     int bi = 0x7fffffff;
     for (int v = tid; v < V; v += kTinyThreads) {
+      const float hb = a.head_b[v];
       const uint32_t* e = reinterpret_cast<const uint32_t*>(a.embed + (size_t)v * D);
       int x1 = 0, x2 = 0, x3 = 0;
       for (int j0 = 0; j0 < D / 4; j0 += 4) {
@@ -289,7 +293,7 @@ __global__ void __launch_bounds__(kTinyThreads, 1) tiny_generate_kernel(const __
           x3 = __dp4a(wv[q], (int)sPl[2 * kwp + j0 + q], x3);
         }
       }
-      const float l = __fadd_rn(dequant(x1, x2, x3, s_step, a.head_scale), a.head_b[v]);
+      const float l = __fadd_rn(dequant(x1, x2, x3, s_step, a.head_scale), hb);
       sLog[v] = l;
       if (l > bv || (l == bv && v < bi)) bv = l, bi = v;
     }
