@@ -46,6 +46,53 @@ struct I8Args {
   float* y;                // [M x N] or null
 };
 
+// The epilogue of one 128-row x 256-column accumulator for one epilogue warp: TMEM lanes
+// quad*32..+31 (output rows r0..r0+31), columns half*128..+127 of the accumulator at column
+// acc_col. 32 columns at a time, each thread (= row) writes its 128-byte row into the warp's
+// staging tile with the 16-byte chunks XOR-swizzled by row (conflict-free), then 8 lanes per row
+// store whole 128-byte lines (4 rows per instruction).
+__device__ __forceinline__ void i8_drain_tile(const I8Args& args, uint32_t tmem, int acc_col, int r0, int n0, int half,
+                                              int lane, uint32_t* st) {
+  const int quad = (r0 / 32) & 3;
+  const int row = r0 + lane;
+  const float rs = (args.row_scale && row < args.M) ? args.row_scale[row] : 1.0f;
+  for (int pass = 0; pass < 2; ++pass) {
+    int32_t* out = pass == 0 ? args.c_i32 : reinterpret_cast<int32_t*>(args.y);
+    if (!out) continue;
+    for (int c = half * 128; c < half * 128 + 128; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tmem_addr(tmem, quad * 32, acc_col + c), r);
+      tmem_wait_ld();
+      const int n = n0 + c;
+      if (pass == 1) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float cs = args.col_scale ? args.col_scale[n + e] : 1.0f;
+          // Separately rounded multiplies and add (never contracted into an FMA).
+          float tv = __fmul_rn((float)(int)r[e], rs);
+          tv = __fmul_rn(tv, cs);
+          if (args.bias) tv = __fadd_rn(tv, args.bias[n + e]);
+          r[e] = __float_as_uint(tv);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<uint4*>(st + lane * 32 + 4 * (j ^ (lane & 7))) =
+            make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int piece = lane + 32 * i;  // 32 rows x 8 chunks of 16 bytes
+        const int rr = piece >> 3, ch = piece & 7;
+        const int grow = r0 + rr;
+        const uint4 v = *reinterpret_cast<const uint4*>(st + rr * 32 + 4 * (ch ^ (rr & 7)));
+        if (grow < args.M) *reinterpret_cast<uint4*>(out + (size_t)grow * args.N + n + 4 * ch) = v;
+      }
+      __syncwarp();
+    }
+  }
+}
+
 // Persistent: one CTA per SM walks the 128 x 256 output tiles (N-tiles fastest, so neighbouring
 // CTAs share the A tile in L2). Warp 0 issues the TMA loads through a 4-stage ring, warp 1 the
 // MMAs into one of two TMEM accumulators (2 x 256 columns), and eight epilogue warps drain the
@@ -144,50 +191,10 @@ __global__ void __launch_bounds__(kI8Threads, 1)
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
       const int b = i & 1;
       const int m0 = (t / ntn) * kBM, n0 = (t % ntn) * kI8BN;
-      const int row = m0 + quad * 32 + lane;
       // TMEM loads are warp-collective: the whole warp takes the same branch.
       if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&acc_full[b], (i / 2) & 1, kErrWaitAcc))) break;
       tc_fence_after();
-      const float rs = (args.row_scale && row < args.M) ? args.row_scale[row] : 1.0f;
-      uint32_t* st = stg + (size_t)(warp - 2) * 32 * 32;
-      // 32 columns at a time: thread = row writes its 128-byte row into the staging tile with the
-      // 16-byte chunks XOR-swizzled by row (conflict-free), then 8 lanes per row store whole
-      // 128-byte lines (4 rows per instruction)
-      for (int pass = 0; pass < 2; ++pass) {
-        int32_t* out = pass == 0 ? args.c_i32 : reinterpret_cast<int32_t*>(args.y);
-        if (!out) continue;
-        for (int c = half * 128; c < half * 128 + 128; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tmem_addr(tmem, quad * 32, b * kI8BN + c), r);
-          tmem_wait_ld();
-          const int n = n0 + c;
-          if (pass == 1) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float cs = args.col_scale ? args.col_scale[n + e] : 1.0f;
-              // Separately rounded multiplies and add (never contracted into an FMA).
-              float tv = __fmul_rn((float)(int)r[e], rs);
-              tv = __fmul_rn(tv, cs);
-              if (args.bias) tv = __fadd_rn(tv, args.bias[n + e]);
-              r[e] = __float_as_uint(tv);
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<uint4*>(st + lane * 32 + 4 * (j ^ (lane & 7))) =
-                make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-          __syncwarp();
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int piece = lane + 32 * i;  // 32 rows x 8 chunks of 16 bytes
-            const int rr = piece >> 3, ch = piece & 7;
-            const int grow = m0 + quad * 32 + rr;
-            const uint4 v = *reinterpret_cast<const uint4*>(st + rr * 32 + 4 * (ch ^ (rr & 7)));
-            if (grow < args.M) *reinterpret_cast<uint4*>(out + (size_t)grow * args.N + n + 4 * ch) = v;
-          }
-          __syncwarp();
-        }
-      }
+      i8_drain_tile(args, tmem, b * kI8BN, m0 + quad * 32, n0, half, lane, stg + (size_t)(warp - 2) * 32 * 32);
       // the accumulator is read: the MMA warp may reuse it
       tc_fence_before();
       __syncwarp();
@@ -197,6 +204,139 @@ __global__ void __launch_bounds__(kI8Threads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// ------------------------------------------------------------------------------------------------
+// int8 x int8 on CTA pairs (cta_group::2)
+// ------------------------------------------------------------------------------------------------
+// The same persistent structure over 256 x 256 output tiles, one per cluster of two CTAs on two
+// SMs. Each CTA loads its own 128 rows of A and its own 128 rows of W (output channels) per K
+// stage; the first CTA's MMA thread issues M = 256, N = 256 MMAs that read both CTAs' stages, and
+// each CTA's TMEM receives its 128 output rows over all 256 columns. Per SM and per 128 x 256
+// output tile that is A 128 x K + W 128 x K bytes through L2 instead of A 128 x K + W 256 x K,
+// the operand traffic the single-CTA kernel waits on.
+//
+// Barriers: both CTAs' loads complete on the first CTA's full[s] (the first CTA expects the
+// pair's bytes); the MMA thread's commits arrive on empty[s] and acc_full[b] in both CTAs; both
+// CTAs' epilogue warps arrive on the first CTA's acc_empty[b]. No load uses cluster multicast.
+constexpr int kPStages = 6;
+constexpr int kPStageA = kBM * kBK;  // 16 KB: this CTA's 128 rows of A
+constexpr int kPStageB = 128 * kBK;  // 16 KB: this CTA's 128 rows of W
+constexpr int kPSmem = kPStages * (kPStageA + kPStageB) + kI8Staging + 1024 + 256;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kI8Threads, 1)
+    gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                        I8Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + kPStages * kPStageA;
+  uint32_t* stg = reinterpret_cast<uint32_t*>(sb + kPStages * kPStageB);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + kPStages * kPStageB + kI8Staging);
+  uint64_t* empty = full + kPStages;
+  uint64_t* acc_full = empty + kPStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();  // 0: issues the MMAs
+  const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
+  const int ktiles = (args.K + kBK - 1) / kBK;
+  const int ntn = args.N / 256, ntm = (args.M + 255) / 256;
+  const int ntiles = ntn * ntm;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * kI8EpiWarps);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers are initialised before any load or commit reaches them
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensormap(&map_a);
+      prefetch_tensormap(&map_w);
+      const uint32_t full0 = cluster_map_shared(full, 0);  // the first CTA's full[0]
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = pair; t < ntiles && ok; t += npairs) {
+        const int m0 = (t / ntn) * 256 + (int)rank * 128, n0 = (t % ntn) * 256 + (int)rank * 128;
+        for (int kt = 0; kt < ktiles; ++kt, ++it) {
+          const int s = it % kPStages;
+          if (it >= kPStages && !mbar_wait_or_abort(&empty[s], ((it / kPStages) - 1) & 1, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (kPStageA + kPStageB));
+          tma_load_2d_pair(sa + s * kPStageA, &map_a, kt * kBK, m0, full0 + 8u * s);
+          tma_load_2d_pair(sb + s * kPStageB, &map_w, kt * kBK, n0, full0 + 8u * s);
+        }
+      }
+      // Until the MMAs have read every stage this CTA filled, the peer's MMA thread still reads
+      // its shared memory: wait for each stage's last release before leaving.
+      if (ok) {
+        for (uint32_t j = it > kPStages ? it - kPStages : 0; j < it; ++j)
+          if (!mbar_wait_or_abort(&empty[j % kPStages], (j / kPStages) & 1, kErrWaitEmpty)) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = idesc_i8(256, 256);
+      uint32_t it = 0, i = 0;
+      bool ok = true;
+      for (int t = pair; t < ntiles && ok; t += npairs, ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !mbar_wait_or_abort(&acc_empty[b], ((i / 2) - 1) & 1, kErrWaitAccFree)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + b * 256;
+        for (int kt = 0; kt < ktiles; ++kt, ++it) {
+          const int s = it % kPStages;
+          if (!mbar_wait_or_abort(&full[s], (it / kPStages) & 1, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_sw128(sa + s * kPStageA);
+          const uint64_t db = smem_desc_sw128(sb + s * kPStageB);
+          const int ksteps = min(4, (args.K - kt * kBK + 31) / 32);
+          for (int kk = 0; kk < ksteps; ++kk)
+            mma_i8_pair(acc, da + 2 * kk, db + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+          mma_commit_pair(&empty[s], 0x3);
+        }
+        if (ok) mma_commit_pair(&acc_full[b], 0x3);
+      }
+    }
+  } else {
+    const int quad = warp % 4, half = (warp - 2) / 4;
+    const uint32_t acc_empty0 = cluster_map_shared(acc_empty, 0);
+    uint32_t i = 0;
+    for (int t = pair; t < ntiles; t += npairs, ++i) {
+      const int b = i & 1;
+      const int m0 = (t / ntn) * 256 + (int)rank * 128, n0 = (t % ntn) * 256;
+      if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&acc_full[b], (i / 2) & 1, kErrWaitAcc))) break;
+      tc_fence_after();
+      i8_drain_tile(args, tmem, b * 256, m0 + quad * 32, n0, half, lane, stg + (size_t)(warp - 2) * 32 * 32);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8u * b);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other may still reach its shared memory or TMEM
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, 512);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -595,16 +735,32 @@ __global__ void __launch_bounds__(kWThreads, 1)
 // Per-device set-up of the GEMM kernels, done once per device under a lock: the shared-memory
 // size attribute of a kernel is a setting of the device that is current when it is made, and the
 // multiprocessor count (the persistent grid) can differ between devices.
-static int gemm_device_setup(int* n_sm) {
+static int gemm_device_setup(int* n_sm, int* n_pairs = nullptr) {
   constexpr int kMaxDevices = 64;
   static std::mutex mu;
-  static int sms[kMaxDevices] = {0};  // 0: not set up yet
+  static int sms[kMaxDevices] = {0};    // 0: not set up yet
+  static int pairs[kMaxDevices] = {0};  // CTA pairs of gemm_i8_pair_kernel resident at once
   int dev = 0;
   MC_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return set_error(kUnsupported, "gemm: device ordinal above 63");
   std::lock_guard<std::mutex> lk(mu);
   if (sms[dev] == 0) {
     MC_CUDA(cudaFuncSetAttribute(gemm::gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kI8Smem));
+    MC_CUDA(cudaFuncSetAttribute(gemm::gemm_i8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 gemm::kPSmem));
+    {
+      // SMs pair up within a GPC, so the resident pairs can be fewer than half the SMs
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2, 1, 1);
+      cfg.blockDim = dim3(gemm::kI8Threads, 1, 1);
+      cfg.dynamicSmemBytes = gemm::kPSmem;
+      int nc = 0;
+      if (cudaOccupancyMaxActiveClusters(&nc, gemm::gemm_i8_pair_kernel, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();  // no pairs: the single-CTA kernel runs
+        nc = 0;
+      }
+      pairs[dev] = nc;
+    }
     MC_CUDA(cudaFuncSetAttribute(gemm::gemm_f32a_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kFSmem));
     MC_CUDA(cudaFuncSetAttribute(gemm::gemm_f32a_wm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)gemm::kWSmemMax));
@@ -613,6 +769,7 @@ static int gemm_device_setup(int* n_sm) {
     sms[dev] = std::max(n, 1);
   }
   *n_sm = sms[dev];
+  if (n_pairs) *n_pairs = pairs[dev];
   return kOk;
 }
 
@@ -621,15 +778,22 @@ int gemm_i8_launch(const int8_t* a, const int8_t* w, int M, int N, int K, const 
   if (M <= 0 || N <= 0 || K <= 0 || N % gemm::kI8BN != 0 || K % 16 != 0)
     return set_error(kInvalidArgument, "gemm_i8: need M,N,K > 0, N % 256 == 0 and K % 16 == 0");
   if (!c_i32 && !y) return set_error(kInvalidArgument, "gemm_i8: no output");
-  CUtensorMap ma, mw;
-  if (!make_tmap_i8(&ma, a, M, K, K, gemm::kBK, gemm::kBM)) return kCudaError;
-  if (!make_tmap_i8(&mw, w, N, K, K, gemm::kBK, gemm::kI8BN)) return kCudaError;
-  int n_sm = 0;
-  const int st = gemm_device_setup(&n_sm);
+  int n_sm = 0, n_pairs = 0;
+  const int st = gemm_device_setup(&n_sm, &n_pairs);
   if (st != kOk) return st;
   gemm::I8Args args{M, N, K, row_scale, col_scale, bias, c_i32, y};
-  const int tiles = (N / gemm::kI8BN) * ((M + gemm::kBM - 1) / gemm::kBM);
-  gemm::gemm_i8_kernel<<<std::min(tiles, n_sm), gemm::kI8Threads, gemm::kI8Smem, stream>>>(ma, mw, args);
+  // CTA pairs (cta_group::2) unless MC_GEMM_I8_SINGLE is set or no pair fits on the device
+  const bool pair = n_pairs > 0 && !getenv("MC_GEMM_I8_SINGLE");
+  CUtensorMap ma, mw;
+  if (!make_tmap_i8(&ma, a, M, K, K, gemm::kBK, gemm::kBM)) return kCudaError;
+  if (!make_tmap_i8(&mw, w, N, K, K, gemm::kBK, pair ? 128 : gemm::kI8BN)) return kCudaError;
+  if (pair) {
+    const int tiles = (N / 256) * ((M + 255) / 256);
+    gemm::gemm_i8_pair_kernel<<<2 * std::min(tiles, n_pairs), gemm::kI8Threads, gemm::kPSmem, stream>>>(ma, mw, args);
+  } else {
+    const int tiles = (N / gemm::kI8BN) * ((M + gemm::kBM - 1) / gemm::kBM);
+    gemm::gemm_i8_kernel<<<std::min(tiles, n_sm), gemm::kI8Threads, gemm::kI8Smem, stream>>>(ma, mw, args);
+  }
   MC_CUDA(cudaGetLastError());
   return kOk;
 }

@@ -157,6 +157,48 @@ __device__ __forceinline__ void bulk_load_hint(void* smem_dst, const void* gmem_
       : "memory");
 }
 
+// ---------------------------------------------------------------------------------------------
+// Clusters of two CTAs (a CTA pair running one cta_group::2 MMA)
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Shared::cluster address of the variable at p in the shared memory of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_map_shared(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// Every thread of every CTA of the cluster; orders prior writes (barrier inits included) before
+// what the other CTAs do after it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrives on an mbarrier given by its shared::cluster address (this CTA's or a peer's), with the
+// default CTA-scope release: it hands over TMEM (ordered by the tcgen05 fences around it), not
+// global memory, so it need not wait for this thread's global stores to become visible to the
+// cluster (a cluster-scope release did, and held each epilogue warp until its stores drained).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// 2-D tiled TMA load (no multicast) into this CTA's shared memory, completing on an mbarrier that
+// may sit in the peer CTA of the pair (shared::cluster address): the pair's operand halves all
+// complete on the barrier of the CTA that issues the MMA.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar_cluster_addr) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -219,6 +261,41 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+// TMEM of a CTA pair: one warp of each CTA (the same warp index in both) allocates the same
+// columns in both CTAs' TMEM; the pair MMA writes rows 0-127 of its M = 256 tile to the first
+// CTA's lanes and rows 128-255 to the second's.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D (+)= A * B^T over a CTA pair, issued by one thread of the pair's first CTA: A's rows 0-127
+// and B's rows 0-127 are read from its shared memory, A's rows 128-255 and B's rows 128-255 from
+// the same addresses in the peer CTA.
+__device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrives on the mbarrier at this address in each CTA of cta_mask once the pair MMAs issued so far
+// by this thread have completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
 }
 
 // 32 consecutive 32-bit TMEM columns of this thread's lane (warp w reads lanes 32*(w%4)..+31).

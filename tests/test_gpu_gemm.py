@@ -17,9 +17,17 @@ def _rng_i8(rng, shape):
     return rng.integers(-127, 128, size=shape, dtype=np.int64).astype(np.int8)
 
 
+# "pair": 256 x 256 tiles on CTA pairs (cta_group::2 MMAs reading both CTAs' operand halves), the
+# default; "single": 128 x 256 tiles, one CTA each (MC_GEMM_I8_SINGLE=1). Row counts that are not a
+# multiple of 256 leave the second CTA of a pair with partly or wholly out-of-range rows.
+@pytest.mark.parametrize("kernel", ["pair", "single"])
 @pytest.mark.parametrize("m,n,k", [(256, 256, 192), (256, 1024, 384), (4096, 256, 1152), (384, 512, 128),
-                                   (200, 256, 384)])
-def test_gemm_i8_exact(m, n, k):
+                                   (200, 256, 384), (100, 512, 96), (4500, 2048, 1152)])
+def test_gemm_i8_exact(m, n, k, kernel, monkeypatch):
+    if kernel == "single":
+        monkeypatch.setenv("MC_GEMM_I8_SINGLE", "1")
+    else:
+        monkeypatch.delenv("MC_GEMM_I8_SINGLE", raising=False)
     rng = np.random.default_rng(5)
     a, w = _rng_i8(rng, (m, k)), _rng_i8(rng, (n, k))
     rs = rng.uniform(0.5, 2, m).astype(np.float32)
@@ -30,7 +38,8 @@ def test_gemm_i8_exact(m, n, k):
     L = _lib.lib()
     _lib.check(L.mc_gemm_i8(0, _lib.ptr(a), _lib.ptr(w), m, n, k, _lib.ptr(rs), _lib.ptr(cs), _lib.ptr(bias),
                             _lib.ptr(c), _lib.ptr(y)))
-    want = a.astype(np.int64) @ w.astype(np.int64).T
+    # float64 products and sums of int8 values stay below 2^53 here: exact
+    want = (a.astype(np.float64) @ w.astype(np.float64).T).astype(np.int64)
     assert np.array_equal(c.astype(np.int64), want)
     yw = ((want.astype(np.float32) * rs[:, None]) * cs[None, :]) + bias[None, :]
     assert np.array_equal(y, yw.astype(np.float32))
