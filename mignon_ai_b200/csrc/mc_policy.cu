@@ -567,6 +567,21 @@ __device__ __forceinline__ double pol_warp_sum(double v) {
   return v;
 }
 
+// exp(y) for y <= 0 (or NaN-free -inf) to within 3e-7 relative, for the softmax denominator only:
+// z = y log2(e) in double, its integer part n exactly, 2^(z - n) (|z - n| <= 1/2, rounded to float:
+// 2^-25 absolute, 2e-8 relative in the result) by exp2f (at most 2 ulp: 2.4e-7 relative), then
+// scaled by 2^n in double (exact). Terms below 2^-126 are dropped: the largest term of the sum is
+// exp(0) = 1, and 2048 such terms stay under 1e-34 of it.
+constexpr double kPolSumRelErr = 3e-7;
+__device__ __forceinline__ double pol_exp_term(double y) {
+  const double z = y * 1.4426950408889634;  // log2(e)
+  if (!(z > -126.0)) return 0.0;
+  const double n = rint(z);
+  const float f = (float)(z - n);
+  const double scale = __longlong_as_double((long long)((int)n + 1023) << 52);
+  return (double)exp2f(f) * scale;
+}
+
 __device__ __forceinline__ double pol_warp_max(double v) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -602,6 +617,7 @@ struct PolRowValue {
   // path under a warp-uniform branch.
   __device__ __forceinline__ void warp_values4(int j0, int V, double (&v)[4]) const {
     const int lane = threadIdx.x & 31;
+    const int nwords = (V + 31) >> 5;
     float f[4];
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
@@ -611,10 +627,16 @@ struct PolRowValue {
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const int t = (j0 + g) * 32 + lane;
-      const bool m = t < V && modified(t);
       v[g] = (double)f[g];
-      if (__any_sync(0xffffffffu, m)) {
-        if (m) v[g] = full(f[g], t);
+      if (tr) {
+        const bool m = t < V && modified(t);
+        if (__any_sync(0xffffffffu, m)) {
+          if (m) v[g] = full(f[g], t);
+        }
+      } else if (j0 + g < nwords) {
+        // the warp's 32 tokens share one bitmap word (bits past V are clear)
+        const uint32_t wd = mod[j0 + g];
+        if (wd != 0u && ((wd >> lane) & 1u)) v[g] = full(f[g], t);
       }
     }
   }
@@ -626,6 +648,7 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
   __shared__ int cand_i[kPolRowWarps][kPolRowCand];
   __shared__ int whist[kPolRowWarps][256];
   __shared__ unsigned int wsamp[kPolRowWarps][kPolRowSamples];
+  __shared__ double csum[kPolRowWarps][kPolRowMaxK];  // running sums of the sorted candidates
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kPolRowWarps + warp;
   const int V = a.V;
@@ -764,25 +787,39 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
         // pass A: the max and the group maxima of x (lane l, group g: the lane's entries with j % 4 == g)
         // (the maxima of x = v / T are the maxima of v times 1/T, since rounding keeps the order;
         // unmodified values are their float logits, so those maxima are taken in float)
+        // 16 loads in flight per lane (the pass waits on L2, not on arithmetic); entry j of the
+        // lane belongs to group j % 4
         float fm = -INFINITY, fg[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         double dm = -INFINITY, dg[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        for (int j0 = 0; j0 * 32 < V; j0 += 4) {
+        for (int j0 = 0; j0 * 32 < V; j0 += 16) {
+          float f[16];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int t = (j0 + g) * 32 + lane;
+          for (int q = 0; q < 16; ++q) {
+            const int t = (j0 + q) * 32 + lane;
+            f[q] = t < V ? val.lg[t] : 0.f;
+          }
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const int g = q & 3;
+            const int t = (j0 + q) * 32 + lane;
             const bool in = t < V;
-            const float f = in ? val.lg[t] : 0.f;
-            const bool md = in && val.modified(t);
+            bool md;
+            if (val.tr) {
+              md = in && val.modified(t);
+            } else {
+              // the warp's 32 tokens share one bitmap word (bits past V are clear)
+              md = (j0 + q) * 32 < V && ((val.mod[j0 + q] >> lane) & 1u);
+            }
             if (__any_sync(0xffffffffu, md)) {
               if (md) {
-                const double v = val.full(f, t);
+                const double v = val.full(f[q], t);
                 dm = fmax(dm, v);
                 dg[g] = fmax(dg[g], v);
               }
             }
             if (in && !md) {
-              fm = fmaxf(fm, f);
-              fg[g] = fmaxf(fg[g], f);
+              fm = fmaxf(fm, f[q]);
+              fg[g] = fmaxf(fg[g], f[q]);
             }
           }
         }
@@ -813,7 +850,7 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
             const int t = (j0 + g) * 32 + lane;
             const bool in = t < V;
             const double x = v[g] * inv_t;
-            if (in) s += exp(x - m);
+            if (in) s += pol_exp_term(x - m);
             const bool take = in && x >= tau;
             if (in && !take) xo = fmax(xo, x);
             const unsigned int tm = __ballot_sync(0xffffffffu, take);
@@ -891,38 +928,70 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
           __syncwarp();
           rank_in_place(K);
         }
-        // 3f. the shortest prefix whose mass reaches top-p, then the draw (in sequence)
-        if (lane == 0) {
-          int active = K;
-          if (a.top_p > 0.0 && a.top_p < 1.0) {
+        // 3f. the shortest prefix whose mass reaches top-p, then the draw, over the running sums of
+        // the sorted candidates in the reference's order (sample.go:141-152, 174-191). Lane 0 forms
+        // them once: the top-p cut is the first that reaches top-p, the draw's total sp is the one
+        // at the cut (the same additions in the same order), and the draw takes the first running
+        // sum at or above u * sp. The candidates' probabilities scale with 1/s, which pass B summed
+        // to within kPolSumRelErr: a top-p comparison closer than that to its threshold is decided
+        // again with the sum of double-precision exponentials (the draw and the reported
+        // probability are ratios of candidate probabilities, so the scale of s cancels in them).
+        const bool use_top_p = a.top_p > 0.0 && a.top_p < 1.0;
+        double* cs = csum[warp];
+        auto running_sums = [&](bool check) {
+          int cut = K;
+          bool near = false;
+          if (lane == 0) {
             double cum = 0.0;
-            int cut = 0;
-            for (int i = 0; i < active; ++i) {
+            for (int i = 0; i < K; ++i) {
               cum += cp[i];
-              cut = i + 1;
-              if (cum >= a.top_p) break;
-            }
-            active = cut;
-          }
-          if (active == 1) {
-            tok = ci[0];
-            prob = 1.0;
-          } else {
-            double sp = 0.0;
-            for (int i = 0; i < active; ++i) sp += cp[i];
-            const double r = u * sp;
-            double cum = 0.0;
-            int k = active - 1;
-            for (int i = 0; i < active; ++i) {
-              cum += cp[i];
-              if (r <= cum) {
-                k = i;
-                break;
+              cs[i] = cum;
+              if (use_top_p) {
+                near |= check && fabs(cum - a.top_p) <= 4.0 * kPolSumRelErr * fmax(cum, a.top_p);
+                if (cum >= a.top_p) {
+                  cut = i + 1;
+                  break;
+                }
               }
             }
-            tok = ci[k];
-            prob = cp[k] / sp;
           }
+          __syncwarp();
+          return make_int2(__shfl_sync(0xffffffffu, cut, 0), __shfl_sync(0xffffffffu, near ? 1 : 0, 0));
+        };
+        int2 cn = running_sums(true);
+        if (cn.y) {
+          double sd = 0.0;
+          for (int j0 = 0; j0 * 32 < V; j0 += 4) {
+            double v[4];
+            val.warp_values4(j0, V, v);
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+              if ((j0 + g) * 32 + lane < V) sd += exp(v[g] * inv_t - m);
+          }
+          sd = pol_warp_sum(sd);
+          const double f = s / sd;  // the candidates' probabilities with the exact sum
+          for (int c = lane; c < K; c += 32) cp[c] *= f;
+          __syncwarp();
+          cn = running_sums(false);
+        }
+        const int active = cn.x;
+        if (active == 1) {
+          tok = ci[0];
+          prob = 1.0;
+        } else {
+          const double sp = cs[active - 1];
+          const double r = u * sp;
+          int k = active - 1;
+          for (int i0 = 0; i0 < active; i0 += 32) {
+            const int i = i0 + lane;
+            const unsigned int hit = __ballot_sync(0xffffffffu, i < active && r <= cs[i]);
+            if (hit) {
+              k = i0 + __ffs(hit) - 1;
+              break;
+            }
+          }
+          tok = ci[k];
+          prob = cp[k] / sp;
         }
       }
     }

@@ -137,6 +137,48 @@ def test_sample_rows_zero_probability_ties(oracle, kernel, monkeypatch):
             assert got_p[r] == pytest.approx(want_p, rel=1e-5), (ci, r)
 
 
+def _oracle_cum(logits, temperature, k):
+    """The running sum after the k most probable entries as the reference computes it
+    (sample.go:119-152): x = logit / T, exponentials of x - max summed in index order, each
+    divided by the sum, sorted descending, summed in that order."""
+    x = logits.astype(np.float64) * (1.0 / temperature)
+    e = np.exp(x - x.max())
+    s = float(np.cumsum(e)[-1])
+    p = e * (1.0 / s)
+    q = p[np.lexsort((np.arange(p.size), -p))]
+    cum = 0.0
+    for i in range(k):
+        cum += float(q[i])
+    return cum
+
+
+@pytest.mark.parametrize("delta", [0.0, 5e-8, -5e-8, 2e-7, -2e-7, 1e-6])
+def test_sample_rows_top_p_at_the_sum_bound(oracle, delta, monkeypatch):
+    """The warp kernel sums the softmax denominator from exponentials good to 3e-7 (relative) and
+    decides a top-p comparison that lies closer than that to its threshold with the exact sum:
+    top-p set within 1e-6 of each row's running sum after its third or fifth candidate must cut
+    where the reference cuts, with the same token and probability (delta 0, the threshold on the
+    sum itself, may go either way and is skipped)."""
+    monkeypatch.delenv("MC_POLICY_BLOCK", raising=False)
+    rng = np.random.default_rng(91)
+    n, V = 6, 2048
+    logits = (rng.standard_normal((n, V)) * 3.0).astype(np.float32)
+    for r in range(n):
+        kc = 3 if r % 2 == 0 else 5
+        top_p = _oracle_cum(logits[r], 0.8, kc) * (1.0 + delta)
+        sp = S(0.8, 1.0, 40, top_p, 0, False)
+        osp = _oracle_sampling(oracle, sp)
+        rows = np.repeat(logits[r:r + 1], 4, axis=0)
+        got_t, got_p = quant.sample_rows(rows, sp, session0=11 * r, step=3)
+        for j in range(4):
+            u = synth.sample_uniform(11 * r + j, 3)
+            want_t, want_p = oracle.sample_policy(rows[j].astype(np.float64), osp, (), [], None, u)
+            if policy_margin(rows[j], sp, (), [], None, u) < 1e-9:
+                continue  # on an edge (delta 0): either cut is the reference's up to rounding
+            assert got_t[j] == want_t, (r, j)
+            assert got_p[j] == pytest.approx(want_p, rel=1e-6), (r, j)
+
+
 def test_sample_rows_python_statement_on_one_row():
     """The device's answer on one row equals the plain-Python statement for every case."""
     rng = np.random.default_rng(5)
