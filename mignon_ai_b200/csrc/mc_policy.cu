@@ -567,19 +567,13 @@ __device__ __forceinline__ double pol_warp_sum(double v) {
   return v;
 }
 
-// exp(y) for y <= 0 (or NaN-free -inf) to within 3e-7 relative, for the softmax denominator only:
-// z = y log2(e) in double, its integer part n exactly, 2^(z - n) (|z - n| <= 1/2, rounded to float:
-// 2^-25 absolute, 2e-8 relative in the result) by exp2f (at most 2 ulp: 2.4e-7 relative), then
-// scaled by 2^n in double (exact). Terms below 2^-126 are dropped: the largest term of the sum is
-// exp(0) = 1, and 2048 such terms stay under 1e-34 of it.
-constexpr double kPolSumRelErr = 3e-7;
-__device__ __forceinline__ double pol_exp_term(double y) {
-  const double z = y * 1.4426950408889634;  // log2(e)
-  if (!(z > -126.0)) return 0.0;
-  const double n = rint(z);
-  const float f = (float)(z - n);
-  const double scale = __longlong_as_double((long long)((int)n + 1023) << 52);
-  return (double)exp2f(f) * scale;
+// 2^z for z <= 0 to within 2e-6 relative, for the softmax denominator only. z is rounded to
+// float: |z| 2^-24 absolute, so at most 30 * 2^-24 * ln 2 < 1.3e-6 relative for every term above
+// 2^-30 (the largest term is 2^0 = 1, and the terms below 2^-30 weigh under 2048 * 2^-30 of the
+// sum); exp2f adds at most 2 ulp (2.4e-7). Terms below 2^-126 are dropped.
+constexpr double kPolSumRelErr = 2e-6;
+__device__ __forceinline__ double pol_exp2_term(double z) {
+  return z > -126.0 ? (double)exp2f((float)z) : 0.0;
 }
 
 __device__ __forceinline__ double pol_warp_max(double v) {
@@ -850,7 +844,7 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
             const int t = (j0 + g) * 32 + lane;
             const bool in = t < V;
             const double x = v[g] * inv_t;
-            if (in) s += pol_exp_term(x - m);
+            if (in) s += pol_exp2_term((x - m) * 1.4426950408889634);  // log2(e)
             const bool take = in && x >= tau;
             if (in && !take) xo = fmax(xo, x);
             const unsigned int tm = __ballot_sync(0xffffffffu, take);
