@@ -248,9 +248,9 @@ int build_dev_model(const HostModel& hm, int device, std::unique_ptr<DevModel>& 
   m->dec_ok = m->dec_smem <= kDecodeSmemMax;
   if (nattn > 0 && m->cache > 128) return set_error(kUnsupported, "attention caches above 128 positions");
   // Small models without attention also keep their blocks' int8 rows for tiny_generate_kernel:
-  // per block W_select, W1 and W2 row-major, each row padded to an odd number of words.
+  // per block W_select, W1 and W2 row-major, each row padded to an odd number of 16-byte quads.
   const int nb = (int)hm.blocks.size();
-  if (nattn == 0 && m->tied && nb >= 1 && nb <= kTinyMaxBlocks && D <= kTinyMaxD && D % 16 == 0 && H % 4 == 0 &&
+  if (nattn == 0 && m->tied && nb >= 1 && nb <= kTinyMaxBlocks && D <= kTinyMaxD && D % 16 == 0 && H % 16 == 0 &&
       tiny_smem_bytes(D, H, V, nb, total, m->ring) <= kTinySmemMax) {
     const int bw = tiny_block_words(D, H);
     std::vector<uint32_t> img((size_t)nb * bw, 0u);

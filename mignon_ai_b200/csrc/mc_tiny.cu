@@ -24,7 +24,7 @@ constexpr int kTinyMaxD = 128;                 // the norms run on one warp, one
 constexpr size_t kTinySmemMax = 200 * 1024;
 
 struct TinyBlock {
-  const uint32_t* w;  // [W_select rows | W1 rows | W2 rows], int8 rows padded to odd word strides
+  const uint32_t* w;  // [W_select rows | W1 rows | W2 rows], int8 rows padded to odd quad strides
   float s_sel, s1, s2;
   const float *b1, *b2, *gamma;
   int steps, bs0;
@@ -33,7 +33,7 @@ struct TinyBlock {
 
 struct TinyArgs {
   int S, D, H, V, nblocks, total_steps, ring, P, n_new, out_stride;
-  int kw_sel, kw1, kw2;  // row strides in 32-bit words: D/4, 3D/4, H/4, each made odd
+  int kw_sel, kw1, kw2;  // row strides in 32-bit words: D/4, 3D/4, H/4, each made an odd number of quads
   int blk_words;         // words per block in w (a multiple of 4)
   const int8_t* embed;   // [V][D]: the embedding and the tied head
   float embed_scale, head_scale;
@@ -46,11 +46,13 @@ struct TinyArgs {
   TinyBlock blk[kTinyMaxBlocks];
 };
 
-// Row strides of the padded weight rows: an odd number of words, so that the 32 rows a warp
-// reads at once fall in 32 different banks.
+// Row strides of the padded weight rows: an odd number of 16-byte quads, so that the eight rows a
+// quarter-warp reads at once with 128-bit loads fall in eight different quad banks. k_bytes is a
+// multiple of 16.
 inline int tiny_stride_words(int k_bytes) {
-  const int w = k_bytes / 4;
-  return (w & 1) ? w : w + 1;
+  int q = k_bytes / 16;
+  if (!(q & 1)) ++q;
+  return 4 * q;
 }
 
 inline int tiny_block_words(int D, int H) {
@@ -58,10 +60,13 @@ inline int tiny_block_words(int D, int H) {
   return (w + 3) & ~3;
 }
 
+// The logits row is padded to whole quads so that the digit planes after it are 16-byte aligned.
+__host__ __device__ inline int tiny_vocab_pad(int V) { return (V + 3) & ~3; }
+
 inline size_t tiny_smem_bytes(int D, int H, int V, int nblocks, int total_steps, int ring) {
   const int kwp = std::max(3 * D, H) / 4;
-  return (size_t)nblocks * tiny_block_words(D, H) * 4 + ((size_t)total_steps * D * (1 + ring) + 4 * (size_t)D + H + V) * 4 +
-         (size_t)3 * kwp * 4;
+  return (size_t)nblocks * tiny_block_words(D, H) * 4 +
+         ((size_t)total_steps * D * (1 + ring) + 4 * (size_t)D + H + tiny_vocab_pad(V)) * 4 + (size_t)3 * kwp * 4;
 }
 
 // The three digit planes of four consecutive values as one word per plane.
@@ -76,16 +81,32 @@ __device__ __forceinline__ void tiny_slice4(float4 v, float is, uint32_t* pl, in
   pl[2 * kwp + word] = pack_low_bytes(c0, c1, c2, c3);
 }
 
-// The three plane dot products of one padded weight row with the planes (nw words of K).
+// Four words of one weight row against the same four words of the three planes.
+__device__ __forceinline__ void tiny_dot4(uint4 x, uint4 y1, uint4 y2, uint4 y3, int& a1, int& a2, int& a3) {
+  a1 = __dp4a((int)x.x, (int)y1.x, a1);
+  a2 = __dp4a((int)x.x, (int)y2.x, a2);
+  a3 = __dp4a((int)x.x, (int)y3.x, a3);
+  a1 = __dp4a((int)x.y, (int)y1.y, a1);
+  a2 = __dp4a((int)x.y, (int)y2.y, a2);
+  a3 = __dp4a((int)x.y, (int)y3.y, a3);
+  a1 = __dp4a((int)x.z, (int)y1.z, a1);
+  a2 = __dp4a((int)x.z, (int)y2.z, a2);
+  a3 = __dp4a((int)x.z, (int)y3.z, a3);
+  a1 = __dp4a((int)x.w, (int)y1.w, a1);
+  a2 = __dp4a((int)x.w, (int)y2.w, a2);
+  a3 = __dp4a((int)x.w, (int)y3.w, a3);
+}
+
+// The three plane dot products of one padded weight row with the planes (nw words of K, a multiple
+// of 4; the row and the planes 16-byte aligned): 128-bit shared-memory loads, four words per load.
 __device__ __forceinline__ void tiny_dot(const uint32_t* w, const uint32_t* pl, int kwp, int nw, int& a1, int& a2, int& a3) {
   a1 = a2 = a3 = 0;
-#pragma unroll 4
-  for (int j = 0; j < nw; ++j) {
-    const int x = (int)w[j];
-    a1 = __dp4a(x, (int)pl[j], a1);
-    a2 = __dp4a(x, (int)pl[kwp + j], a2);
-    a3 = __dp4a(x, (int)pl[2 * kwp + j], a3);
-  }
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+  const uint4* p1 = reinterpret_cast<const uint4*>(pl);
+  const uint4* p2 = reinterpret_cast<const uint4*>(pl + kwp);
+  const uint4* p3 = reinterpret_cast<const uint4*>(pl + 2 * kwp);
+#pragma unroll 2
+  for (int q = 0; q < nw / 4; ++q) tiny_dot4(w4[q], p1[q], p2[q], p3[q], a1, a2, a3);
 }
 
 __device__ __forceinline__ float4 ld4s(const float* p) { return *reinterpret_cast<const float4*>(p); }
@@ -122,8 +143,8 @@ __global__ void __launch_bounds__(kTinyThreads, 1) tiny_generate_kernel(const __
   float* sHid = f;
   f += H;
   float* sLog = f;
-  f += V;
-  uint32_t* sPl = reinterpret_cast<uint32_t*>(f);
+  f += tiny_vocab_pad(V);
+  uint32_t* sPl = reinterpret_cast<uint32_t*>(f);  // 16-byte aligned: every region above is whole quads
 
   {
     const uint4* src = reinterpret_cast<const uint4*>(a.blk[0].w);  // the blocks' weights are one allocation
@@ -283,16 +304,10 @@ __global__ void __launch_bounds__(kTinyThreads, 1) tiny_generate_kernel(const __
       const float hb = a.head_b[v];
       const uint32_t* e = reinterpret_cast<const uint32_t*>(a.embed + (size_t)v * D);
       int x1 = 0, x2 = 0, x3 = 0;
-      for (int j0 = 0; j0 < D / 4; j0 += 4) {
-        const uint4 w4 = *reinterpret_cast<const uint4*>(e + j0);  // D % 16 == 0: whole uint4s
-        const int wv[4] = {(int)w4.x, (int)w4.y, (int)w4.z, (int)w4.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          x1 = __dp4a(wv[q], (int)sPl[j0 + q], x1);
-          x2 = __dp4a(wv[q], (int)sPl[kwp + j0 + q], x2);
-          x3 = __dp4a(wv[q], (int)sPl[2 * kwp + j0 + q], x3);
-        }
-      }
+      for (int j0 = 0; j0 < D / 4; j0 += 4)  // D % 16 == 0: whole uint4s
+        tiny_dot4(*reinterpret_cast<const uint4*>(e + j0), *reinterpret_cast<const uint4*>(sPl + j0),
+                  *reinterpret_cast<const uint4*>(sPl + kwp + j0), *reinterpret_cast<const uint4*>(sPl + 2 * kwp + j0),
+                  x1, x2, x3);
       const float l = __fadd_rn(dequant(x1, x2, x3, s_step, a.head_scale), hb);
       sLog[v] = l;
       if (l > bv || (l == bv && v < bi)) bv = l, bi = v;
