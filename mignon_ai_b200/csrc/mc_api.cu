@@ -645,6 +645,11 @@ int mc_score_targets(mc_batch* b, const int32_t* seqs, const int32_t* lens, int 
   return score_impl(b, seqs, lens, stride, targets, out, "mc_score_targets");
 }
 
+// One append per session is the Go provider's Session.Append for a batch of one, so its fixed cost
+// per call matters as much as the step: the tokens go up and the outputs and the device error word
+// come back through a pinned buffer of the shard (copies to and from the caller's pageable memory
+// would each be staged and synchronous inside the driver), and one stream synchronization per
+// shard ends the call.
 int mc_append(mc_batch* b, const int32_t* tokens, float* logits, int32_t* next, float* prob) {
   clear_error();
   DeviceRestore restore_device;
@@ -655,11 +660,48 @@ int mc_append(mc_batch* b, const int32_t* tokens, float* logits, int32_t* next, 
     if (sh.S == 0) continue;
     MC_CUDA(cudaSetDevice(sh.m->device));
     if ((st = ensure_step_outputs(sh, logits != nullptr, 1)) != kOk) return st;
-    MC_CUDA(cudaMemcpyAsync(sh.next_tok, tokens + b->first[g], sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
+    const size_t S = (size_t)sh.S, need = 3 * S + 4 + (logits ? S * sh.m->V : 0);
+    if (sh.h_step_n < need) {
+      if (sh.h_step) MC_CUDA(cudaFreeHost(sh.h_step));
+      sh.h_step = nullptr;
+      sh.h_step_n = 0;
+      MC_CUDA(cudaHostAlloc(&sh.h_step, need * 4, cudaHostAllocDefault));
+      sh.h_step_n = need;
+    }
+    int32_t* hs = sh.h_step;  // free: the previous call synchronized the stream before returning
+    memcpy(hs, tokens + b->first[g], S * 4);
+    MC_CUDA(cudaMemcpyAsync(sh.next_tok, hs, S * 4, cudaMemcpyHostToDevice, sh.stream));
     MC_CUDA(cudaMemsetAsync(sh.step, 0, 4, sh.stream));
-    if ((st = run_graph_step(sh, 0, 0.0, 0, logits != nullptr)) != kOk) return st;
+    if (tiny_job_ok(sh, 0, 0, false, false))  // small models without attention: one launch
+      st = launch_tiny_job(sh, 1, 1, true, logits ? sh.logits : nullptr);
+    else
+      st = run_graph_step(sh, 0, 0.0, 0, logits != nullptr);
+    if (st != kOk) return st;
+    const size_t pitch = (size_t)sh.out_stride * 4;  // column 0 of the [S x out_stride] outputs
+    if (next) MC_CUDA(cudaMemcpy2DAsync(hs + S, 4, sh.out_tok, pitch, 4, S, cudaMemcpyDeviceToHost, sh.stream));
+    if (prob) MC_CUDA(cudaMemcpy2DAsync(hs + 2 * S, 4, sh.out_prob, pitch, 4, S, cudaMemcpyDeviceToHost, sh.stream));
+    if (logits)
+      MC_CUDA(cudaMemcpyAsync(hs + 3 * S + 4, sh.logits, S * sh.m->V * 4, cudaMemcpyDeviceToHost, sh.stream));
+    MC_CUDA(cudaMemcpyFromSymbolAsync(hs + 3 * S, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, sh.stream));
   }
-  return copy_step_outputs(b, logits, next, prob);
+  st = kOk;
+  for (size_t g = 0; g < b->shard.size(); ++g) {
+    DevBatch& sh = *b->shard[g];
+    if (sh.S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh.m->device));
+    MC_CUDA(cudaStreamSynchronize(sh.stream));
+    const size_t S = (size_t)sh.S, s0 = (size_t)b->first[g];
+    const int32_t* hs = sh.h_step;
+    if (hs[3 * S] != 0) {  // a bounded device wait gave up: clear the word and report it
+      const int e = check_device_error(sh.stream);
+      if (e != kOk && st == kOk) st = e;
+      continue;
+    }
+    if (next) memcpy(next + s0, hs + S, S * 4);
+    if (prob) memcpy(prob + s0, hs + 2 * S, S * 4);
+    if (logits) memcpy(logits + s0 * sh.m->V, hs + 3 * S + 4, S * sh.m->V * 4);
+  }
+  return st;
 }
 
 int mc_generate(mc_batch* b, const int32_t* prompts, const int32_t* lens, int stride, int n_new, double temperature,

@@ -346,6 +346,10 @@ struct DevBatch {
   int32_t* h_stage = nullptr;
   size_t h_stage_n = 0;
   cudaEvent_t h_stage_done = nullptr;
+  // pinned host staging of one append: [tokens S | next S | prob S | device error word, padding 4 |
+  // logits S x V], so its copies are asynchronous and one stream synchronization ends the call
+  int32_t* h_step = nullptr;
+  size_t h_step_n = 0;
   // Everything the captured decode step bakes in; a change forces a new capture.
   struct GraphKey {
     int mode = -1, logits = -1, stride = -1;
@@ -372,6 +376,7 @@ struct DevBatch {
     if (graph) cudaGraphExecDestroy(graph);
     if (h_stage_done) cudaEventSynchronize(h_stage_done), cudaEventDestroy(h_stage_done);
     if (h_stage) cudaFreeHost(h_stage);
+    if (h_step) cudaFreeHost(h_step);
     for (void* p : allocs) cudaFree(p);
     if (stream) cudaStreamDestroy(stream);
     cudaSetDevice(prev);
@@ -956,7 +961,9 @@ bool tiny_job_ok(const DevBatch& b, int mode, int n_stops, bool limits, bool pol
   return b.m->tiny && mode == 0 && n_stops == 0 && !limits && !policy && b.S <= 2 * b.n_sm && !getenv("MC_TINY_OFF");
 }
 
-int launch_tiny_job(DevBatch& b, int P, int n_new) {
+// The whole job (P-token prompt segments, n_new tokens) or, with append, one pending token per
+// session (next_tok at pos, the batched step's state convention) and optionally the logits rows.
+int launch_tiny_job(DevBatch& b, int P, int n_new, bool append = false, float* logits = nullptr) {
   const DevModel& m = *b.m;
   TinyArgs a;
   memset(&a, 0, sizeof(a));
@@ -989,6 +996,8 @@ int launch_tiny_job(DevBatch& b, int P, int n_new) {
   a.norm_ring = b.norm_ring;
   a.out_tok = b.out_tok;
   a.out_prob = b.out_prob;
+  a.append = append ? 1 : 0;
+  a.logits = logits;
   int bs = 0;
   for (int bi = 0; bi < a.nblocks; ++bi) {
     const DevBlock& blk = m.blocks[bi];

@@ -43,6 +43,10 @@ struct TinyArgs {
   float *latch, *norm_ring;  // [S][total_steps][D], [S][total_steps][ring][D]
   int32_t* out_tok;
   float* out_prob;
+  // append: one token per session (next_tok at position pos, the state carried in from global
+  // memory) instead of a whole job; logits: each session's logits row [S][V] when not null
+  int append;
+  float* logits;
   TinyBlock blk[kTinyMaxBlocks];
 };
 
@@ -122,7 +126,7 @@ __global__ void __launch_bounds__(kTinyThreads, 1) tiny_generate_kernel(const __
   const int s = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (s == 0 && tid == 0) *a.step = a.n_new;  // the step counter as the batched job leaves it
   const int n = a.seglen[s];
-  if (n <= 0) return;  // a session without a prompt runs nothing (as in the batched kernels)
+  if (n <= 0) return;  // a session without a prompt (or finished) runs nothing, as in the batched kernels
   const int D = a.D, H = a.H, V = a.V, nf = D / 4;
   const int kwp = max(3 * D, H) / 4;
   // shared memory: the blocks' weights, the session state, the working rows, the digit planes
@@ -154,8 +158,9 @@ __global__ void __launch_bounds__(kTinyThreads, 1) tiny_generate_kernel(const __
     const size_t ring_n = (size_t)a.total_steps * a.ring * D;
     const float* gr = a.norm_ring + (size_t)s * ring_n;
     for (size_t i = tid; i < ring_n; i += kTinyThreads) sRing[i] = gr[i];
-    // prefill resets the latch (quantSeqState.reset, stream.go:116-121)
-    for (int i = tid; i < a.total_steps * D; i += kTinyThreads) sLatch[i] = 0.f;
+    // prefill resets the latch (quantSeqState.reset, stream.go:116-121); an append carries it on
+    const float* gl = a.latch + (size_t)s * a.total_steps * D;
+    for (int i = tid; i < a.total_steps * D; i += kTinyThreads) sLatch[i] = a.append ? gl[i] : 0.f;
   }
   __syncthreads();
 
@@ -310,6 +315,7 @@ __global__ void __launch_bounds__(kTinyThreads, 1) tiny_generate_kernel(const __
                   x1, x2, x3);
       const float l = __fadd_rn(dequant(x1, x2, x3, s_step, a.head_scale), hb);
       sLog[v] = l;
+      if (a.logits) a.logits[(size_t)s * V + v] = l;
       if (l > bv || (l == bv && v < bi)) bv = l, bi = v;
     }
 #pragma unroll
@@ -341,11 +347,17 @@ __global__ void __launch_bounds__(kTinyThreads, 1) tiny_generate_kernel(const __
     __syncthreads();
   };
 
-  for (int i = 0; i < n; ++i) append(a.tok[(size_t)s * a.P + i], i, i == n - 1);
-  head(0);
-  for (int k = 1; k < a.n_new; ++k) {
-    append(s_next, n + k - 1, true);
-    head(k);
+  const int p_app = a.append ? a.pos[s] : 0;  // the pending token's position (read before any write)
+  if (a.append) {
+    append(a.next_tok[s], p_app, true);  // appendPosition of the pending token, then the head
+    head(0);
+  } else {
+    for (int i = 0; i < n; ++i) append(a.tok[(size_t)s * a.P + i], i, i == n - 1);
+    head(0);
+    for (int k = 1; k < a.n_new; ++k) {
+      append(s_next, n + k - 1, true);
+      head(k);
+    }
   }
   // the session continues as after the batched kernels: state, position, pending token
   {
@@ -355,7 +367,7 @@ __global__ void __launch_bounds__(kTinyThreads, 1) tiny_generate_kernel(const __
     float* gl = a.latch + (size_t)s * a.total_steps * D;
     for (int i = tid; i < a.total_steps * D; i += kTinyThreads) gl[i] = sLatch[i];
     if (tid == 0) {
-      a.pos[s] = n + a.n_new - 1;
+      a.pos[s] = a.append ? p_app + 1 : n + a.n_new - 1;
       a.seglen[s] = 1;
       a.next_tok[s] = s_next;
     }
