@@ -68,22 +68,58 @@ int sync_all(mc_batch* b) {
   return st;
 }
 
-// Copies per-session host outputs back after a step that wrote column 0 of out_tok/out_prob.
+// Pinned host staging of a step's transfers (DevBatch::h_step): [tokens S | next S | prob S |
+// device error word, padding 4 | logits S x V]. Sized before a call writes into it, so it is never
+// reallocated while one of its copies is pending (every call synchronizes before returning).
+int ensure_h_step(DevBatch& sh, bool logits) {
+  const size_t S = (size_t)sh.S, need = 3 * S + 4 + (logits ? S * sh.m->V : 0);
+  if (sh.h_step_n < need) {
+    if (sh.h_step) MC_CUDA(cudaFreeHost(sh.h_step));
+    sh.h_step = nullptr;
+    sh.h_step_n = 0;
+    MC_CUDA(cudaHostAlloc(&sh.h_step, need * 4, cudaHostAllocDefault));
+    sh.h_step_n = need;
+  }
+  return kOk;
+}
+
+// Copies per-session host outputs back after a step that wrote column 0 of out_tok/out_prob: the
+// outputs and the device error word go to each shard's pinned staging asynchronously (copies into
+// the caller's pageable memory would each be staged and synchronous inside the driver), then one
+// stream synchronization per shard, then plain host copies out.
 int copy_step_outputs(mc_batch* b, float* logits, int32_t* next, float* prob) {
+  int st;
   for (size_t g = 0; g < b->shard.size(); ++g) {
     DevBatch& sh = *b->shard[g];
     if (sh.S == 0) continue;
     MC_CUDA(cudaSetDevice(sh.m->device));
-    const int s0 = b->first[g];
-    // column 0 of the [S x out_stride] output arrays
-    const size_t pitch = (size_t)sh.out_stride * 4;
-    if (next) MC_CUDA(cudaMemcpy2DAsync(next + s0, 4, sh.out_tok, pitch, 4, sh.S, cudaMemcpyDeviceToHost, sh.stream));
-    if (prob) MC_CUDA(cudaMemcpy2DAsync(prob + s0, 4, sh.out_prob, pitch, 4, sh.S, cudaMemcpyDeviceToHost, sh.stream));
+    if ((st = ensure_h_step(sh, logits != nullptr)) != kOk) return st;
+    const size_t S = (size_t)sh.S, pitch = (size_t)sh.out_stride * 4;  // column 0 of [S x out_stride]
+    int32_t* hs = sh.h_step;
+    if (next) MC_CUDA(cudaMemcpy2DAsync(hs + S, 4, sh.out_tok, pitch, 4, S, cudaMemcpyDeviceToHost, sh.stream));
+    if (prob) MC_CUDA(cudaMemcpy2DAsync(hs + 2 * S, 4, sh.out_prob, pitch, 4, S, cudaMemcpyDeviceToHost, sh.stream));
     if (logits)
-      MC_CUDA(cudaMemcpyAsync(logits + (size_t)s0 * sh.m->V, sh.logits, (size_t)sh.S * sh.m->V * 4, cudaMemcpyDeviceToHost,
-                              sh.stream));
+      MC_CUDA(cudaMemcpyAsync(hs + 3 * S + 4, sh.logits, S * sh.m->V * 4, cudaMemcpyDeviceToHost, sh.stream));
+    MC_CUDA(cudaMemcpyFromSymbolAsync(hs + 3 * S, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, sh.stream));
   }
-  return sync_all(b);
+  st = kOk;
+  for (size_t g = 0; g < b->shard.size(); ++g) {
+    DevBatch& sh = *b->shard[g];
+    if (sh.S == 0) continue;
+    MC_CUDA(cudaSetDevice(sh.m->device));
+    MC_CUDA(cudaStreamSynchronize(sh.stream));
+    const size_t S = (size_t)sh.S, s0 = (size_t)b->first[g];
+    const int32_t* hs = sh.h_step;
+    if (hs[3 * S] != 0) {  // a bounded device wait gave up: clear the word and report it
+      const int e = check_device_error(sh.stream);
+      if (e != kOk && st == kOk) st = e;
+      continue;
+    }
+    if (next) memcpy(next + s0, hs + S, S * 4);
+    if (prob) memcpy(prob + s0, hs + 2 * S, S * 4);
+    if (logits) memcpy(logits + s0 * sh.m->V, hs + 3 * S + 4, S * sh.m->V * 4);
+  }
+  return st;
 }
 
 int ensure_step_outputs(DevBatch& sh, bool logits, int stride, bool gmax = false) {
@@ -646,10 +682,8 @@ int mc_score_targets(mc_batch* b, const int32_t* seqs, const int32_t* lens, int 
 }
 
 // One append per session is the Go provider's Session.Append for a batch of one, so its fixed cost
-// per call matters as much as the step: the tokens go up and the outputs and the device error word
-// come back through a pinned buffer of the shard (copies to and from the caller's pageable memory
-// would each be staged and synchronous inside the driver), and one stream synchronization per
-// shard ends the call.
+// per call matters as much as the step: the tokens go up and the outputs come back through the
+// shard's pinned staging, and one stream synchronization per shard ends the call.
 int mc_append(mc_batch* b, const int32_t* tokens, float* logits, int32_t* next, float* prob) {
   clear_error();
   DeviceRestore restore_device;
@@ -660,48 +694,17 @@ int mc_append(mc_batch* b, const int32_t* tokens, float* logits, int32_t* next, 
     if (sh.S == 0) continue;
     MC_CUDA(cudaSetDevice(sh.m->device));
     if ((st = ensure_step_outputs(sh, logits != nullptr, 1)) != kOk) return st;
-    const size_t S = (size_t)sh.S, need = 3 * S + 4 + (logits ? S * sh.m->V : 0);
-    if (sh.h_step_n < need) {
-      if (sh.h_step) MC_CUDA(cudaFreeHost(sh.h_step));
-      sh.h_step = nullptr;
-      sh.h_step_n = 0;
-      MC_CUDA(cudaHostAlloc(&sh.h_step, need * 4, cudaHostAllocDefault));
-      sh.h_step_n = need;
-    }
-    int32_t* hs = sh.h_step;  // free: the previous call synchronized the stream before returning
-    memcpy(hs, tokens + b->first[g], S * 4);
-    MC_CUDA(cudaMemcpyAsync(sh.next_tok, hs, S * 4, cudaMemcpyHostToDevice, sh.stream));
+    if ((st = ensure_h_step(sh, logits != nullptr)) != kOk) return st;
+    memcpy(sh.h_step, tokens + b->first[g], (size_t)sh.S * 4);  // the tokens up through the pinned staging
+    MC_CUDA(cudaMemcpyAsync(sh.next_tok, sh.h_step, (size_t)sh.S * 4, cudaMemcpyHostToDevice, sh.stream));
     MC_CUDA(cudaMemsetAsync(sh.step, 0, 4, sh.stream));
     if (tiny_job_ok(sh, 0, 0, false, false))  // small models without attention: one launch
       st = launch_tiny_job(sh, 1, 1, true, logits ? sh.logits : nullptr);
     else
       st = run_graph_step(sh, 0, 0.0, 0, logits != nullptr);
     if (st != kOk) return st;
-    const size_t pitch = (size_t)sh.out_stride * 4;  // column 0 of the [S x out_stride] outputs
-    if (next) MC_CUDA(cudaMemcpy2DAsync(hs + S, 4, sh.out_tok, pitch, 4, S, cudaMemcpyDeviceToHost, sh.stream));
-    if (prob) MC_CUDA(cudaMemcpy2DAsync(hs + 2 * S, 4, sh.out_prob, pitch, 4, S, cudaMemcpyDeviceToHost, sh.stream));
-    if (logits)
-      MC_CUDA(cudaMemcpyAsync(hs + 3 * S + 4, sh.logits, S * sh.m->V * 4, cudaMemcpyDeviceToHost, sh.stream));
-    MC_CUDA(cudaMemcpyFromSymbolAsync(hs + 3 * S, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, sh.stream));
   }
-  st = kOk;
-  for (size_t g = 0; g < b->shard.size(); ++g) {
-    DevBatch& sh = *b->shard[g];
-    if (sh.S == 0) continue;
-    MC_CUDA(cudaSetDevice(sh.m->device));
-    MC_CUDA(cudaStreamSynchronize(sh.stream));
-    const size_t S = (size_t)sh.S, s0 = (size_t)b->first[g];
-    const int32_t* hs = sh.h_step;
-    if (hs[3 * S] != 0) {  // a bounded device wait gave up: clear the word and report it
-      const int e = check_device_error(sh.stream);
-      if (e != kOk && st == kOk) st = e;
-      continue;
-    }
-    if (next) memcpy(next + s0, hs + S, S * 4);
-    if (prob) memcpy(prob + s0, hs + 2 * S, S * 4);
-    if (logits) memcpy(logits + s0 * sh.m->V, hs + 3 * S + 4, S * sh.m->V * 4);
-  }
-  return st;
+  return copy_step_outputs(b, logits, next, prob);
 }
 
 int mc_generate(mc_batch* b, const int32_t* prompts, const int32_t* lens, int stride, int n_new, double temperature,
