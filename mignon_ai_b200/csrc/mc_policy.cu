@@ -836,6 +836,9 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
         // largest x below tau
         double s = 0.0, xo = -INFINITY;
         int C = 0;
+        // the exponent of 2 of entry x is (x - m) log2(e) = x log2(e) + zm (one rounding fewer than
+        // the subtraction first; m = -DBL_MAX only when every x is -inf, whose terms stay 0)
+        const double zm = -m * 1.4426950408889634;
         for (int j0 = 0; j0 * 32 < V; j0 += 4) {
           double v[4];
           val.warp_values4(j0, V, v);
@@ -844,7 +847,7 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
             const int t = (j0 + g) * 32 + lane;
             const bool in = t < V;
             const double x = v[g] * inv_t;
-            if (in) s += pol_exp2_term((x - m) * 1.4426950408889634);  // log2(e)
+            if (in) s += pol_exp2_term(fma(x, 1.4426950408889634, zm));  // (x - m) log2(e)
             const bool take = in && x >= tau;
             if (in && !take) xo = fmax(xo, x);
             const unsigned int tm = __ballot_sync(0xffffffffu, take);
@@ -877,8 +880,10 @@ __global__ void __launch_bounds__(kPolRowWarps * 32, 7) policy_row_kernel(const 
             rv[q] = c < n ? cp[c] : 0.0;
             ri[q] = c < n ? ci[c] : 0;
             rk[q] = 0;
-            if (c < n)
+            if (c < n) {
+#pragma unroll 4
               for (int j = 0; j < n; ++j) rk[q] += pol_better(cp[j], ci[j], rv[q], ri[q]) ? 1 : 0;
+            }
           }
           __syncwarp();
 #pragma unroll
