@@ -1,6 +1,6 @@
 """Sessions sharded over two GPUs of one process (a context opened on devices 0 and 1): every
 session's tokens must equal those of the same session on one GPU, for greedy generation, the
-sampling policy and the scheduler (sessions never interact, and draws are keyed by the global
+sampling policy, the scheduler, and prefill and appends with their logits (sessions never interact, and draws are keyed by the global
 session index or the request). Skipped on a box with one GPU."""
 import numpy as np
 import pytest
@@ -30,6 +30,12 @@ def test_two_devices_match_one():
         b = m.new_batch(n, 0, P)
         g = b.generate(prompts, lens, T)[0]
         pol = b.generate_policy(prompts, lens, T, sp, penalize_prompt=True, session0=5)[0]
+        # prefill and appends with logits: each shard's outputs come back through its own staging
+        lg, tok, pr = b.prefill(prompts, lens, want_logits=True)
+        steps = [(lg.copy(), tok.copy(), pr.copy())]
+        for _ in range(3):
+            lg, tok, pr = b.append(tok, want_logits=True)
+            steps.append((lg.copy(), tok.copy(), pr.copy()))
         b.close()
         sched = quant.Scheduler(m, 16, sp, max_prompt=P, max_new=T)
         ids = [sched.submit(prompts[i, :lens[i]], T - i % 4, draw_key=100 + i) for i in range(n)]
@@ -38,11 +44,15 @@ def test_two_devices_match_one():
         sched.close()
         m.close()
         ctx.close()
-        out[devs] = (g, pol, sc)
+        out[devs] = (g, pol, sc, steps)
     a, b2 = out[(0,)], out[(0, 1)]
     np.testing.assert_array_equal(a[0], b2[0])
     np.testing.assert_array_equal(a[1], b2[1])
     assert a[2] == b2[2]
+    for (l1, t1, p1), (l2, t2, p2) in zip(a[3], b2[3]):
+        np.testing.assert_array_equal(t1, t2)
+        np.testing.assert_allclose(p1, p2, rtol=1e-6)
+        np.testing.assert_allclose(l1, l2, rtol=1e-5, atol=1e-6)
 
 
 @pytest.mark.skipif("not _two_gpus()")
