@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Generated tokens/s of batched INT8 sessions on B200 (BASELINE.json metric, config 2).
+"""Generated tokens/s of batched INT8 sessions on B200 (the headline metric, config 2).
 
 One step = one whole generation job on every GPU: 4096 sessions per GPU, each prefilled with a
 48-token prompt (uniform non-special ids, seed 2) and greedily decoded for 80 tokens (filling the

@@ -163,7 +163,7 @@ class ModelSpec:
     tied: bool = True
 
 
-# The BASELINE.json configurations (shapes; prompts are generated by the workload helpers below).
+# The benchmark configurations 1-4 (shapes; prompts are generated by the workload helpers below).
 CONFIGS = {
     1: ModelSpec(vocab=1024, state=64, hidden=128, blocks=2, steps=1, attn_heads=0, attn_window=0),
     2: ModelSpec(vocab=2048, state=128, hidden=256, blocks=4, steps=1, attn_heads=4, attn_window=64),
