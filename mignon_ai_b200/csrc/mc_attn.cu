@@ -27,6 +27,7 @@ struct AttnArgs {
   float scale;
   const int32_t* sess_list;  // prefill: CTA i runs session sess_list[i] (some sessions only), or null: sess0 + i
   int sess0;                 // prefill: first session of a pass over a contiguous range of sessions
+  int last_only;             // prefill: only each segment's last query (its other outputs are unused)
 };
 
 constexpr int kAttnThreads = 256;
@@ -460,8 +461,11 @@ __global__ void __launch_bounds__(kAttnThreads, DH <= 32 ? 4 : 2) attn_prefill_f
   const bool ok = __all_sync(0xffffffffu, mbar_wait_or_abort(bar, 0, kErrWaitFull));
   const int p0 = a.pos0[s];
   if (ok) {
-    for (int item = warp; item < len * heads; item += nw) {
-      const int t = item / heads, h = item - (item / heads) * heads;
+    // last_only: the segment's keys and values are all staged (the last query's window needs them),
+    // but only the last position's queries run
+    const int t_first = a.last_only ? len - 1 : 0;
+    for (int item = warp; item < (len - t_first) * heads; item += nw) {
+      const int t = t_first + item / heads, h = item - (item / heads) * heads;
       const int pos = p0 + t;
       int ws = 0;
       if (a.window > 0 && pos - a.window + 1 > 0) ws = pos - a.window + 1;

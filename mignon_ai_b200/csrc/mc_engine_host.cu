@@ -726,8 +726,11 @@ static int segment_tiles(const DevBatch& b, int P) {
 
 // Enqueues the blocks (and attention sublayers) of one segment: P rows per session, P = 1 a decode
 // step; ends with the final RMSNorm of every row. pr: a prefill pass over some tiles (null: all).
+// last_only: the caller reads each session's last row only (its head); the last block's attention
+// then runs only the last query of each prompt segment when that block is the model's last (every
+// other position's output would only feed rows nothing reads).
 static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = false, const PassRange* pr = nullptr,
-                          bool head_logits = false) {
+                          bool head_logits = false, bool last_only = false) {
   const DevModel& m = *b.m;
   cudaStream_t s = b.stream;
   const int nb = (int)m.blocks.size();
@@ -834,6 +837,7 @@ static int enqueue_layers(DevBatch& b, int P, LaunchLog* log, bool fuse_head = f
         }
         if (attn_prefill_fast_ok(aa.dh) && attn_prefill_fast_smem(P, m.D) <= 220 * 1024) {
           const size_t smem = attn_prefill_fast_smem(P, m.D);
+          aa.last_only = last_only && bi == nb - 1 && !getenv("MC_PREFILL_ALL_QUERIES") ? 1 : 0;
           switch (aa.dh) {
             case 4: attn_prefill_fast_kernel<4><<<grid, kAttnThreads, smem, s>>>(aa); break;
             case 8: attn_prefill_fast_kernel<8><<<grid, kAttnThreads, smem, s>>>(aa); break;
@@ -1041,14 +1045,14 @@ int enqueue_forward(DevBatch& b, int P, int mode, double inv_temp, uint32_t sess
       pr.nt = std::min(per, total - t0);
       pr.s0 = t0 * spt;
       pr.ns = std::min(b.S, (t0 + pr.nt) * spt) - pr.s0;
-      if ((st = enqueue_layers(b, P, log, false, &pr)) != kOk) return st;
+      if ((st = enqueue_layers(b, P, log, false, &pr, false, true)) != kOk) return st;
       if ((st = enqueue_head(b, P, mode, want_logits, pr.s0, pr.ns, (size_t)t0 * 128, log)) != kOk) return st;
       if (mode != 3 && (st = enqueue_select(b, mode, inv_temp, session0, advance_from_len, pr.s0, pr.ns,
                                             t0 + pr.nt >= total, log)) != kOk)
         return st;
     }
   } else {
-    if ((st = enqueue_layers(b, P, log, fuse || fuse_logits, nullptr, fuse_logits)) != kOk) return st;
+    if ((st = enqueue_layers(b, P, log, fuse || fuse_logits, nullptr, fuse_logits, true)) != kOk) return st;
     if (fuse) return kOk;
     if (!fuse_logits && (st = enqueue_head(b, P, mode, want_logits, 0, b.S, 0, log)) != kOk) return st;
     if (mode != 3) return enqueue_select(b, mode, inv_temp, session0, advance_from_len, 0, b.S, true, log);
